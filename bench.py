@@ -1,0 +1,410 @@
+"""Benchmark of the five-value int8 GEMM on B200 (BASELINE.json metric "five-value int8 GEMM TMAC/s").
+
+Workload: every five-value GEMM of one FastConformer block at T = 375 encoder frames
+(a 30 s window): ff1 1024->4096, ff1 4096->1024 (alpha 1/2, beta 1), qkv 1024->3072 (stored fused), pos 1024->1024
+at 2T - 1 = 749 rows, out 1024->1024 (beta 1), pw1 1024->2048, pw2 1024->1024 (beta 1), ff2 as ff1. Weights are
+seeded synthetic five-value planes (P(0) = 1/3, P(+-lo) = P(+-hi) = 1/6, lo ~ U(0.005, 0.02), hi = lo * U(2, 4),
+fp16-rounded); activations fp32 N(0, 1). One step = the nine GEMMs from fp32 activations, each quantised per row
+and multiplied on the tensor cores, as p2_sgemm_fvb does (csrc/blas.c:1481-1499).
+
+Timing: W warm-up steps, then exactly K steps between a barrier + synchronize, CUDA events on the launching stream,
+max over ranks. Steps rotate over enough independent copies of the inputs that they exceed twice the 126 MB L2.
+Each GPU runs its own copy of the workload (windows are independent: weak scaling, no collective on the data path).
+
+--impl reference times phonon-2-c itself (its library compiled from source, exact mode: its int8 path needs AArch64
+dot products) on the host cores, on the same workload and metric.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+import __graft_entry__ as ge  # noqa: E402
+
+T_FRAMES = 375
+METRIC = "five-value int8 GEMM TMAC/s"
+L2_BYTES = 126 * 1024 * 1024
+
+
+def block_gemms(T=T_FRAMES):
+    from phonon2_b200 import synth
+    return [(name, synth.block_rows(rows, T), K, N, alpha, beta)
+            for name, K, N, alpha, beta, rows in synth.BLOCK_SHAPES]
+
+
+def block_macs(T=T_FRAMES) -> int:
+    return sum(M * K * N for _, M, K, N, _, _ in block_gemms(T))
+
+
+def gemm_bytes(M, K, N, beta) -> int:
+    """Algorithmic HBM bytes of one GEMM launch on quantised A: int8 A, the planes (3 bits per weight), lo/hi, the
+    fp32 C store and, when accumulating, the C read."""
+    return M * K + 3 * K * N // 8 + 8 * N + 4 * M * N + (4 * M * N if beta != 0.0 else 0)
+
+
+def load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons, sampled in the background during the timed region."""
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.dev = device_index
+        self.proc = None
+        self.lines = []
+        self.thread = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.dev}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.thread.join(timeout=2)
+
+    def summary(self):
+        rows = []
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                rows.append((float(parts[0]), float(parts[1]), parts[3:]))
+            except ValueError:
+                continue
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"], "samples": 0}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = set()
+        for _, _, r in rows:
+            for name, v in zip(names, r[1:5]):
+                if v.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": max(r[1] for r in rows),
+                "reasons": sorted(reasons), "samples": len(rows)}
+
+
+def dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1 and args.impl == "ours":
+        import datetime
+        import torch.distributed as dist
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        import torch
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda" if dist.get_backend() == "nccl" else "cpu")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---- the reference on the host cores -------------------------------------------------------------------------------
+
+def cpu_reference_step(orc, sets):
+    for (A, w, C, alpha, beta) in sets:
+        orc.ref_sgemm_fvb(A, w, C, alpha=alpha, beta=beta)
+
+
+def build_cpu_sets(T=T_FRAMES):
+    from phonon2_b200 import synth
+    sets = []
+    for i, (name, M, K, N, alpha, beta) in enumerate(block_gemms(T)):
+        w = synth.five_value(K, N, seed=100 + i)
+        A = synth.activations(M, K, seed=200 + i)
+        sets.append((A, w, np.zeros((M, N), np.float32), alpha, beta))
+    return sets
+
+
+def cpu_baseline(seconds=12.0):
+    """phonon-2-c's exact path (its only x86 path) on all host cores, one block's GEMMs at T = 375, repeated for
+    about `seconds`."""
+    orc = ge.load_oracle()
+    if not orc.ref_available():
+        return None
+    sets = build_cpu_sets()
+    cpu_reference_step(orc, sets)   # warm-up (thread pool start, page faults)
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        cpu_reference_step(orc, sets)
+        reps += 1
+        dt = time.perf_counter() - t0
+        if dt >= seconds or reps >= 1000:
+            break
+    value = block_macs() * reps / dt / 1e12
+    return {"value": value, "unit": "TMAC/s", "cores": orc.ref_threads(), "kind": "reference",
+            "sample": f"phonon-2-c p2_sgemm_fvb (exact mode, AVX2) over one block's 9 GEMMs at T={T_FRAMES}, "
+                      f"{reps} repetitions in {dt:.1f} s, P2_THREADS = all host cores"}
+
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return
+    orc = ge.load_oracle()
+    if not orc.ref_available():
+        print(json.dumps({"impl": "reference", "unavailable": "phonon-2-c library not built (oracle/_ref missing)"}))
+        return
+    sets = build_cpu_sets()
+    for _ in range(args.warmup):
+        cpu_reference_step(orc, sets)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        cpu_reference_step(orc, sets)
+    dt = time.perf_counter() - t0
+    value = block_macs() * args.steps / dt / 1e12
+    cores = orc.ref_threads()
+    line = {"metric": METRIC, "value": value, "unit": "TMAC/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "impl": "reference",
+            "config": {"workload": f"one FastConformer block's nine five-value GEMMs at T={T_FRAMES} "
+                                   "(BASELINE configs[1]), exact mode (the reference's only x86 path)",
+                       "mode": "exact", "T": T_FRAMES},
+            "cpu_baseline": {"value": value, "unit": "TMAC/s", "cores": cores, "kind": "reference",
+                             "sample": f"{args.steps} steps of the full workload"},
+            "e2e": {"value": value, "unit": "TMAC/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line))
+
+
+# ---- ours on the GPU ----------------------------------------------------------------------------------------------
+
+class GpuSet:
+    """One independent copy of the workload on the device: weights, fp32 activations, outputs, workspace."""
+
+    def __init__(self, pkg, torch, dev, seed, mode, gemms):
+        from phonon2_b200 import synth
+        from phonon2_b200.device import DeviceFiveValue
+        self.items = []
+        for i, (name, M, K, N, alpha, beta) in enumerate(gemms):
+            w = synth.five_value(K, N, seed=1000 * seed + i)
+            B = DeviceFiveValue(w, dev, codes=False)
+            A = torch.from_numpy(synth.activations(M, K, seed=2000 * seed + i)).to(dev)
+            C = torch.zeros((M, N), dtype=torch.float32, device=dev)
+            ws = torch.empty(max(pkg.workspace_bytes(M, K, mode), 256), dtype=torch.uint8, device=dev)
+            self.items.append((M, K, N, alpha, beta, B, A, C, ws))
+
+    def bytes(self):
+        return sum(B.plane_bytes + A.numel() * 4 + C.numel() * 4 + ws.numel()
+                   for (_, _, _, _, _, B, A, C, ws) in self.items)
+
+    def run(self, pkg, mode, stream):
+        for (M, K, N, alpha, beta, B, A, C, ws) in self.items:
+            pkg.sgemm_fvb(M, N, K, alpha, A.data_ptr(), K, B.struct, mode, beta, C.data_ptr(), N, ws.data_ptr(),
+                          ws.numel(), stream)
+
+    def quantise(self, pkg, stream):
+        for (M, K, N, alpha, beta, B, A, C, ws) in self.items:
+            pkg.quant_rows(A.data_ptr(), M, K, K, ws.data_ptr(), ws.data_ptr() + ((M * K + 255) // 256) * 256,
+                           stream)
+
+    def run_gemm_only(self, pkg, mode, stream):
+        for (M, K, N, alpha, beta, B, A, C, ws) in self.items:
+            q = ws.data_ptr()
+            sc = q + ((M * K + 255) // 256) * 256
+            pkg.sgemm_fvb_q8a(M, N, K, alpha, q, sc, B.struct, mode, beta, C.data_ptr(), N, stream)
+
+
+def run_ours(args, world, rank, local):
+    import torch
+    pkg = ge.load_package()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    mode = pkg.MODES[args.mode]
+    gemms = block_gemms()
+    stream = torch.cuda.Stream(device=dev)
+
+    # Enough independent copies of the inputs that consecutive steps never find their operands in L2.
+    first = GpuSet(pkg, torch, dev, 1 + rank * 100, mode, gemms)
+    nsets = max(2, int(np.ceil(2 * L2_BYTES / first.bytes())))
+    sets = [first] + [GpuSet(pkg, torch, dev, 2 + i + rank * 100, mode, gemms) for i in range(nsets - 1)]
+    torch.cuda.synchronize()
+
+    with torch.cuda.stream(stream):
+        for s in sets:                      # first calls outside capture (kernel attributes, symbol lookups)
+            s.run(pkg, mode, stream)
+        stream.synchronize()
+        pkg.check_device(stream)
+        graphs = []
+        for s in sets:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                s.run(pkg, mode, stream)
+            graphs.append(g)
+        gemm_graphs = []                    # the GEMM kernels alone, on quantised A, for the roofline
+        for s in sets:
+            s.quantise(pkg, stream)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                s.run_gemm_only(pkg, mode, stream)
+            gemm_graphs.append(g)
+    torch.cuda.synchronize()
+
+    for i in range(args.warmup):
+        graphs[i % nsets].replay()
+    torch.cuda.synchronize()
+    barrier(world)
+
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        torch.cuda.synchronize()
+        with torch.cuda.stream(stream):
+            start.record(stream)
+            for i in range(args.steps):
+                graphs[i % nsets].replay()
+            end.record(stream)
+        end.synchronize()
+    torch.cuda.synchronize()
+    barrier(world)
+    ms = start.elapsed_time(end)
+    ms_max = max_over_ranks(ms, world)
+    pkg.check_device(stream)
+
+    macs = block_macs()
+    value = macs * args.steps * world / (ms_max / 1e3) / 1e12
+
+    # Roofline of the dominant kernel (the tcgen05 GEMM): algorithmic bytes of the nine launches / their time.
+    reps = max(50, min(2000, args.steps))
+    g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        g0.record(stream)
+        for i in range(reps):
+            gemm_graphs[i % nsets].replay()
+        g1.record(stream)
+    g1.synchronize()
+    gemm_ms = g0.elapsed_time(g1) / reps
+    algo_bytes = sum(gemm_bytes(M, K, N, beta) for _, M, K, N, _, beta in gemms)
+    peak, peak_kind = load_peaks()
+    achieved = algo_bytes / (gemm_ms / 1e3) / 1e9
+
+    # End to end: fp32 activations from pinned host memory, results back to pinned host memory, every step.
+    e2e = run_e2e(pkg, torch, dev, stream, sets[0], mode, args)
+
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": "TMAC/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "int8" if mode != pkg.EXACT else "f32",
+                "data": "synthetic",
+                "config": {"workload": f"one FastConformer block's nine five-value GEMMs at T={T_FRAMES} "
+                                       "(BASELINE configs[1]): fp32 A quantised per row, then the tcgen05 GEMM",
+                           "mode": args.mode, "T": T_FRAMES, "macs_per_step": macs,
+                           "l2": f"inputs rotate over {nsets} copies ({nsets * first.bytes() / 2**20:.0f} MiB > 2x L2)",
+                           "parallelism": f"replicas x{world} (independent windows)"},
+                "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                             "frac": achieved / peak, "traffic": None, "peak_kind": peak_kind,
+                             "kernel": "fv_gemm_kernel<planes> (nine launches of a step)",
+                             "algo_bytes_per_step": algo_bytes, "gemm_us_per_step": gemm_ms * 1e3},
+                "gpu_launches": args.steps * 2 * len(gemms),
+                "clocks": clocks.summary(),
+                "e2e": e2e}
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline()
+        print(json.dumps(line))
+
+
+def run_e2e(pkg, torch, dev, stream, gset, mode, args):
+    """The same step through the C ABI with host buffers: H2D of the fp32 activations (pinned), the GEMMs, D2H of
+    the outputs (pinned), synchronised every step."""
+    hostA = [torch.empty(A.shape, dtype=torch.float32, pin_memory=True) for (_, _, _, _, _, _, A, _, _) in gset.items]
+    hostC = [torch.empty(C.shape, dtype=torch.float32, pin_memory=True) for (_, _, _, _, _, _, _, C, _) in gset.items]
+    for h, (_, _, _, _, _, _, A, _, _) in zip(hostA, gset.items):
+        h.copy_(A.cpu())
+    h2d = sum(h.numel() * 4 for h in hostA)
+    d2h = sum(h.numel() * 4 for h in hostC)
+    steps = max(10, min(args.steps, 200))
+
+    def step():
+        with torch.cuda.stream(stream):
+            for h, item in zip(hostA, gset.items):
+                item[6].copy_(h, non_blocking=True)
+            gset.run(pkg, mode, stream)
+            for h, item in zip(hostC, gset.items):
+                h.copy_(item[7], non_blocking=True)
+        stream.synchronize()
+
+    for _ in range(3):
+        step()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        step()
+    e1.record(stream)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    return {"value": block_macs() / (ms / 1e3) / 1e12, "unit": "TMAC/s", "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h, "steps": steps, "ms_per_step": ms}
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--mode", choices=["int8w", "int8", "exact"], default="int8w")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    world, rank, local = dist_setup(args)
+    try:
+        if args.impl == "reference":
+            run_reference(args, world, rank)
+        else:
+            run_ours(args, world, rank, local)
+    finally:
+        if world > 1 and args.impl == "ours":
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

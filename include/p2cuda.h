@@ -1,0 +1,98 @@
+/*  p2cuda.h - device-pointer entry points of the B200 five-value GEMM library (libphonon2_b200.so).
+ *
+ *  The reference-facing ABI is blas.h (the same names and arguments as phonon-2-c's csrc/blas.h, host pointers).
+ *  This header is the layer beneath it: every pointer here is device memory, every call is asynchronous on the
+ *  CUDA stream given (a cudaStream_t passed as void *, NULL = the legacy default stream), and nothing here
+ *  allocates: scratch memory is passed in by the caller. All functions return P2CU_OK (0) or a negative P2CU_E*
+ *  code, with a message in p2cu_last_error().
+ *
+ *  Layouts follow the reference's weight format (csrc/blas.h:38-45, csrc/phonon2.h:110-126):
+ *    five-value B [K, N]: signs [K][N/4] (2-bit code sign+1 of column n at bits 2*(n&3)), flags [K][N/8]
+ *                         (bit n&7 set -> |w| = hi[n]), lo / hi [N] fp32 holding fp16 values;
+ *    int8 table B [K, N]: int8 rows of ldb bytes, one fp32 scale per column;
+ *    A, C: fp32 row-major with leading dimensions lda / ldc (in elements).
+ *  Quantised activations are row-major int8 [M][K] (K bytes per row) with one fp32 scale per row.
+ */
+#ifndef P2CUDA_H
+#define P2CUDA_H
+
+#include <stddef.h>
+
+#if defined(__GNUC__)
+#define P2CU_API __attribute__((visibility("default")))
+#else
+#define P2CU_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+    P2CU_OK = 0,
+    P2CU_EINVAL = -1,        /* a contract violation: shapes, alignment, NULL pointers */
+    P2CU_ECUDA = -2,         /* a CUDA runtime / driver error */
+    P2CU_EDEVICE = -3,       /* a kernel gave up waiting (bounded waits) and reported it */
+    P2CU_EUNSUPPORTED = -4   /* a shape this build does not cover */
+};
+
+/* GEMM modes, numbered as the reference's internal enum (csrc/blas.c:1027): int8 = A quantised, two exact weight
+ * planes; exact = fp32 expansion; int8w = A quantised, one int8 code plane. */
+enum { P2CU_INT8 = 0, P2CU_EXACT = 1, P2CU_INT8W = 2 };
+
+/* A five-value weight resident on the device. `codes` optionally points at the weight's int8w codes as a row-major
+ * [K][N] int8 plane (p2cu_fv_pack_codes); with it the int8w GEMM streams the codes instead of expanding planes. */
+typedef struct {
+    const unsigned char *signs;
+    const unsigned char *flags;
+    const float         *lo;
+    const float         *hi;
+    const signed char   *codes;
+    int                  K, N;
+} P2cuFiveValue;
+
+/* The message of the last failed call on this host thread ("" when none). */
+P2CU_API const char *p2cu_last_error(void);
+
+/* Synchronise `stream`, then read and clear the device's error word: P2CU_EDEVICE when a kernel reported a wait that
+ * ran out, P2CU_ECUDA on a CUDA error, else P2CU_OK. */
+P2CU_API int p2cu_check_device(void *stream);
+
+/* Per-row int8 quantisation (csrc/blas.c:1114-1144): q [M][K] int8, scales [M]. */
+P2CU_API int p2cu_quant_rows(const float *A, int M, int K, int lda, signed char *q, float *scales, void *stream);
+
+/* C = alpha * A * B + beta * C on quantised A (csrc/blas.c:1430-1437). mode P2CU_INT8 or P2CU_INT8W.
+ * N % 128 == 0, K % 16 == 0. beta: 0 stores, 1 accumulates, other values scale C first. */
+P2CU_API int p2cu_sgemm_fvb_q8a(int M, int N, int K, float alpha, const signed char *q, const float *a_scales,
+                       const P2cuFiveValue *B, int mode, float beta, float *C, int ldc, void *stream);
+
+/* The same with an int8 table B [K, N] (row stride ldb bytes) and one scale per column (csrc/blas.c:1439-1446). */
+P2CU_API int p2cu_sgemm_q8b_q8a(int M, int N, int K, float alpha, const signed char *q, const float *a_scales,
+                       const signed char *B, const float *scales, int ldb, float beta, float *C, int ldc,
+                       void *stream);
+
+/* Workspace bytes p2cu_sgemm_fvb / p2cu_sgemm_q8b need for M x K activations in the int8 modes (0 in exact mode). */
+P2CU_API size_t p2cu_gemm_workspace_bytes(int M, int K, int mode);
+
+/* C = alpha * A * B + beta * C from fp32 A (csrc/blas.c:1481-1499 / 1462-1479): in the int8 modes A is quantised
+ * into `workspace` first; in P2CU_EXACT the weights are expanded to fp32 and every output is the reference's FMA
+ * chain, bit for bit. */
+P2CU_API int p2cu_sgemm_fvb(int M, int N, int K, float alpha, const float *A, int lda, const P2cuFiveValue *B, int mode,
+                   float beta, float *C, int ldc, void *workspace, size_t workspace_bytes, void *stream);
+P2CU_API int p2cu_sgemm_q8b(int M, int N, int K, float alpha, const float *A, int lda, const signed char *B,
+                   const float *scales, int ldb, int mode, float beta, float *C, int ldc, void *workspace,
+                   size_t workspace_bytes, void *stream);
+
+/* fp32 C = alpha * op(A) * op(B) + beta * C (csrc/blas.c:748-763); trans flags 0 / 1. NN is the reference's FMA chain
+ * bit for bit; the transposed forms run one sequential chain per output. */
+P2CU_API int p2cu_sgemm(int transA, int transB, int M, int N, int K, float alpha, const float *A, int lda, const float *B,
+               int ldb, float beta, float *C, int ldc, void *stream);
+
+/* The int8w codes of B as a row-major [K][N] int8 plane (csrc/blas.c:1391-1400 values): codes has K * N bytes. */
+P2CU_API int p2cu_fv_pack_codes(const P2cuFiveValue *B, signed char *codes, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* P2CUDA_H */

@@ -1,0 +1,193 @@
+"""ctypes access to the CPU checkers. TEST INFRASTRUCTURE ONLY.
+
+Two libraries, both built by oracle/Makefile (``__graft_entry__.build()`` runs it):
+  * ``liboracle.so``          - fv_oracle.c, the C restatement of the reference's GEMM arithmetic;
+  * ``_ref/libphonon2_ref.so`` - phonon-2-c's own library compiled from its sources (exact mode on x86).
+
+Only tests/, ``__graft_entry__.smoke()`` and bench.py's CPU legs import this module; the product never does.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+ORACLE_SO = HERE / "liboracle.so"
+REF_SO = HERE / "_ref" / "libphonon2_ref.so"
+
+MODE_INT8, MODE_INT8W, MODE_Q8B = 0, 2, 8
+_MODES = {"int8": MODE_INT8, "int8w": MODE_INT8W}
+
+_f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
+_i8p = np.ctypeslib.ndpointer(np.int8, flags="C_CONTIGUOUS")
+_u8p = np.ctypeslib.ndpointer(np.uint8, flags="C_CONTIGUOUS")
+_i32p = np.ctypeslib.ndpointer(np.int32, flags="C_CONTIGUOUS")
+
+_lib = None
+_ref = None
+
+
+def lib() -> C.CDLL:
+    global _lib
+    if _lib is None:
+        if not ORACLE_SO.exists():
+            raise RuntimeError(f"{ORACLE_SO} is not built (run __graft_entry__.build())")
+        L = C.CDLL(str(ORACLE_SO))
+        L.orc_quant_rows.argtypes = [_f32p, C.c_int, C.c_int, C.c_int, _i8p, _f32p]
+        L.orc_clo.argtypes = [C.c_float, C.c_float]
+        L.orc_clo.restype = C.c_int
+        L.orc_fv_codes.argtypes = [_u8p, _u8p, _f32p, _f32p, C.c_int, C.c_int, _i8p]
+        L.orc_acc_blocks.argtypes = [C.c_int, C.c_int, C.c_int, _i8p, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
+                                     C.c_void_p, C.c_void_p, C.c_int, _i32p, C.c_void_p]
+        common = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_float,
+                  _f32p, C.c_int]
+        L.orc_gemm_i8.argtypes = [C.c_int, C.c_int, C.c_int, C.c_float, _i8p, _f32p, C.c_int] + common
+        L.orc_gemm_exact.argtypes = [C.c_int, C.c_int, C.c_int, C.c_float, _f32p, C.c_int] + common
+        L.orc_sgemm_i8.argtypes = [C.c_int, C.c_int, C.c_int, C.c_float, _f32p, C.c_int, C.c_int] + common
+        _lib = L
+    return _lib
+
+
+def _ptr(a):
+    return None if a is None else a.ctypes.data_as(C.c_void_p)
+
+
+def _fv_args(w):
+    if w is None:
+        return [None] * 4
+    return [_ptr(w["signs"]), _ptr(w["flags"]), _ptr(w["lo"]), _ptr(w["hi"])]
+
+
+def quant_rows(A: np.ndarray):
+    M, K = A.shape
+    q = np.empty((M, K), np.int8)
+    s = np.empty(M, np.float32)
+    lib().orc_quant_rows(np.ascontiguousarray(A, np.float32), M, K, K, q, s)
+    return q, s
+
+
+def clo(lo: float, hi: float) -> int:
+    return lib().orc_clo(lo, hi)
+
+
+def fv_codes(w) -> np.ndarray:
+    K, N = w["K"], w["N"]
+    out = np.empty((K, N), np.int8)
+    lib().orc_fv_codes(w["signs"], w["flags"], w["lo"], w["hi"], K, N, out)
+    return out
+
+
+def acc_blocks(q: np.ndarray, mode: str, w=None, q8=None):
+    """int32 accumulators per 1024-row K block: (accS, accT) as [nblk, M, N] (accT None unless mode 'int8')."""
+    M, K = q.shape
+    N = w["N"] if w is not None else q8["N"]
+    nblk = (K + 1023) // 1024
+    accS = np.empty((nblk, M, N), np.int32)
+    accT = np.empty((nblk, M, N), np.int32) if mode == "int8" else None
+    m = MODE_Q8B if mode == "q8b" else _MODES[mode]
+    lib().orc_acc_blocks(M, N, K, np.ascontiguousarray(q), m, *_fv_args(w),
+                         _ptr(q8["q8"]) if q8 else None, N, accS, _ptr(accT))
+    return accS, accT
+
+
+def gemm_i8(q, a_scales, mode, out, w=None, q8=None, alpha=1.0, beta=0.0):
+    """In place on out [M, N]: the int8 GEMM on pre-quantised rows with the reference epilogue."""
+    M, K = q.shape
+    N = out.shape[1]
+    m = MODE_Q8B if mode == "q8b" else _MODES[mode]
+    lib().orc_gemm_i8(M, N, K, alpha, np.ascontiguousarray(q), np.ascontiguousarray(a_scales), m, *_fv_args(w),
+                      _ptr(q8["q8"]) if q8 else None, _ptr(q8["scales"]) if q8 else None, N, beta, out, N)
+    return out
+
+
+def sgemm_i8(A, mode, out, w=None, q8=None, alpha=1.0, beta=0.0):
+    """In place on out: quantise fp32 A per row, then the int8 GEMM (p2_sgemm_fvb / p2_sgemm_q8b in int8 modes)."""
+    M, K = A.shape
+    N = out.shape[1]
+    m = MODE_Q8B if mode == "q8b" else _MODES[mode]
+    lib().orc_sgemm_i8(M, N, K, alpha, np.ascontiguousarray(A, np.float32), K, m, *_fv_args(w),
+                       _ptr(q8["q8"]) if q8 else None, _ptr(q8["scales"]) if q8 else None, N, beta, out, N)
+    return out
+
+
+def gemm_exact(A, out, w=None, q8=None, alpha=1.0, beta=0.0):
+    """In place on out: the exact path, one FMA chain per output (p2_sgemm_fvb / p2_sgemm_q8b in exact mode)."""
+    M, K = A.shape
+    N = out.shape[1]
+    lib().orc_gemm_exact(M, N, K, alpha, np.ascontiguousarray(A, np.float32), K, *_fv_args(w),
+                         _ptr(q8["q8"]) if q8 else None, _ptr(q8["scales"]) if q8 else None, N, beta, out, N)
+    return out
+
+
+# ---- the reference library ---------------------------------------------------------------------------------------
+
+class FiveValueB(C.Structure):
+    """The reference's FiveValueB (csrc/blas.h:38-45)."""
+    _fields_ = [("signs", C.c_void_p), ("flags", C.c_void_p), ("lo", C.c_void_p), ("hi", C.c_void_p),
+                ("codes", C.c_void_p)]
+
+
+def ref_available() -> bool:
+    return REF_SO.exists()
+
+
+def ref() -> C.CDLL:
+    """phonon-2-c compiled from source. Exact mode on x86 (its int8 paths need AArch64 dot products)."""
+    global _ref
+    if _ref is None:
+        if not REF_SO.exists():
+            raise RuntimeError(f"{REF_SO} is not built (needs the reference sources; run __graft_entry__.build())")
+        L = C.CDLL(str(REF_SO))
+        L.p2_sgemm_fvb.argtypes = [C.c_int, C.c_int, C.c_int, C.c_float, _f32p, C.c_int, C.POINTER(FiveValueB),
+                                   C.c_float, _f32p, C.c_int]
+        L.p2_sgemm_q8b.argtypes = [C.c_int, C.c_int, C.c_int, C.c_float, _f32p, C.c_int, _i8p, _f32p, C.c_int,
+                                   C.c_float, _f32p, C.c_int]
+        L.p2_sgemm.argtypes = [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_float, _f32p, C.c_int, _f32p,
+                               C.c_int, C.c_float, _f32p, C.c_int]
+        L.p2_gemm_mode.restype = C.c_char_p
+        L.p2_gemm_exact.restype = C.c_int
+        L.p2_pool.restype = C.c_void_p
+        L.p2_pool_nthreads.argtypes = [C.c_void_p]
+        L.p2_pool_nthreads.restype = C.c_int
+        _ref = L
+    return _ref
+
+
+def ref_threads() -> int:
+    L = ref()
+    return L.p2_pool_nthreads(L.p2_pool())
+
+
+def ref_sgemm_fvb(A, w, out, alpha=1.0, beta=0.0):
+    """The reference's p2_sgemm_fvb on host arrays, in place on C."""
+    M, K = A.shape
+    N = out.shape[1]
+    b = FiveValueB(_ptr(w["signs"]).value, _ptr(w["flags"]).value, _ptr(w["lo"]).value, _ptr(w["hi"]).value, None)
+    ref().p2_sgemm_fvb(M, N, K, alpha, np.ascontiguousarray(A, np.float32), K, C.byref(b), beta, out, N)
+    return out
+
+
+def ref_sgemm_q8b(A, q8, out, alpha=1.0, beta=0.0):
+    M, K = A.shape
+    N = out.shape[1]
+    ref().p2_sgemm_q8b(M, N, K, alpha, np.ascontiguousarray(A, np.float32), K, q8["q8"], q8["scales"], N, beta, out, N)
+    return out
+
+
+def ref_sgemm(transA, transB, A, B, out, alpha=1.0, beta=0.0):
+    """The reference's fp32 p2_sgemm (P2Trans 111 = no transpose, 112 = transpose), in place on out."""
+    M, N = out.shape
+    K = A.shape[0] if transA else A.shape[1]
+    ref().p2_sgemm(112 if transA else 111, 112 if transB else 111, M, N, K, alpha, np.ascontiguousarray(A), A.shape[1],
+                   np.ascontiguousarray(B), B.shape[1], beta, out, N)
+    return out
+
+
+def cpu_cores() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1

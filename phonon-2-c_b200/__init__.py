@@ -1,0 +1,138 @@
+"""phonon2_b200 - Python access to libphonon2_b200.so, the B200 build of phonon-2-c's five-value GEMM.
+
+The library is C: ``include/blas.h`` (the reference's host-pointer GEMM ABI) and ``include/p2cuda.h`` (device
+pointers, explicit streams and workspaces). This module binds both with ctypes for tests, the benchmark and Python
+callers; it adds no arithmetic of its own. Loading fails loudly when the library has not been built: there is no
+CPU fallback.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from pathlib import Path
+
+HERE = Path(__file__).resolve().parent
+LIB_PATH = HERE / "libphonon2_b200.so"
+
+# GEMM modes (include/p2cuda.h), numbered as the reference's internal enum (csrc/blas.c:1027).
+INT8, EXACT, INT8W = 0, 1, 2
+MODES = {"int8": INT8, "exact": EXACT, "int8w": INT8W}
+
+P2CU_OK, P2CU_EINVAL, P2CU_ECUDA, P2CU_EDEVICE, P2CU_EUNSUPPORTED = 0, -1, -2, -3, -4
+
+
+class Error(RuntimeError):
+    """A P2CU_E* return code, with the library's message."""
+
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"p2cu error {code}: {msg}")
+        self.code = code
+
+
+class P2cuFiveValue(C.Structure):
+    """include/p2cuda.h P2cuFiveValue: a five-value weight resident on the device."""
+    _fields_ = [("signs", C.c_void_p), ("flags", C.c_void_p), ("lo", C.c_void_p), ("hi", C.c_void_p),
+                ("codes", C.c_void_p), ("K", C.c_int), ("N", C.c_int)]
+
+
+class FiveValueB(C.Structure):
+    """include/blas.h FiveValueB (the reference's csrc/blas.h:38-45): host pointers."""
+    _fields_ = [("signs", C.c_void_p), ("flags", C.c_void_p), ("lo", C.c_void_p), ("hi", C.c_void_p),
+                ("codes", C.c_void_p)]
+
+
+class QuantA(C.Structure):
+    """include/phonon2.h QuantA (the reference's csrc/phonon2.h:432-436)."""
+    _fields_ = [("q", C.c_void_p), ("scales", C.c_void_p), ("M", C.c_int), ("K", C.c_int)]
+
+
+_lib = None
+_vp, _i, _f, _sz = C.c_void_p, C.c_int, C.c_float, C.c_size_t
+
+# (name, restype, argtypes) of every exported function, in the order of include/p2cuda.h then include/blas.h.
+SIGNATURES = {
+    "p2cu_last_error": (C.c_char_p, []),
+    "p2cu_check_device": (_i, [_vp]),
+    "p2cu_quant_rows": (_i, [_vp, _i, _i, _i, _vp, _vp, _vp]),
+    "p2cu_sgemm_fvb_q8a": (_i, [_i, _i, _i, _f, _vp, _vp, C.POINTER(P2cuFiveValue), _i, _f, _vp, _i, _vp]),
+    "p2cu_sgemm_q8b_q8a": (_i, [_i, _i, _i, _f, _vp, _vp, _vp, _vp, _i, _f, _vp, _i, _vp]),
+    "p2cu_gemm_workspace_bytes": (_sz, [_i, _i, _i]),
+    "p2cu_sgemm_fvb": (_i, [_i, _i, _i, _f, _vp, _i, C.POINTER(P2cuFiveValue), _i, _f, _vp, _i, _vp, _sz, _vp]),
+    "p2cu_sgemm_q8b": (_i, [_i, _i, _i, _f, _vp, _i, _vp, _vp, _i, _i, _f, _vp, _i, _vp, _sz, _vp]),
+    "p2cu_sgemm": (_i, [_i, _i, _i, _i, _i, _f, _vp, _i, _vp, _i, _f, _vp, _i, _vp]),
+    "p2cu_fv_pack_codes": (_i, [C.POINTER(P2cuFiveValue), _vp, _vp]),
+}
+
+
+def lib() -> C.CDLL:
+    """The loaded library (raises when it is missing: build it with __graft_entry__.build())."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise RuntimeError(f"{LIB_PATH} is not built; run __graft_entry__.build() (no CPU fallback exists)")
+        L = C.CDLL(str(LIB_PATH))
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def last_error() -> str:
+    return lib().p2cu_last_error().decode()
+
+
+def check(rc: int) -> None:
+    if rc != P2CU_OK:
+        raise Error(rc, last_error())
+
+
+def five_value_struct(signs: int, flags: int, lo: int, hi: int, K: int, N: int, codes: int | None = None):
+    """A P2cuFiveValue from device addresses."""
+    return P2cuFiveValue(signs, flags, lo, hi, codes, K, N)
+
+
+def workspace_bytes(M: int, K: int, mode: int) -> int:
+    return int(lib().p2cu_gemm_workspace_bytes(M, K, mode))
+
+
+def stream_ptr(stream) -> int | None:
+    """A cudaStream_t value from a torch stream (or None for the legacy default stream)."""
+    return None if stream is None else int(stream.cuda_stream)
+
+
+# ---- device-pointer calls (addresses are ints, e.g. torch's data_ptr()) ----------------------------------------------
+
+def quant_rows(A: int, M: int, K: int, lda: int, q: int, scales: int, stream=None) -> None:
+    check(lib().p2cu_quant_rows(A, M, K, lda, q, scales, stream_ptr(stream)))
+
+
+def sgemm_fvb(M, N, K, alpha, A, lda, B: P2cuFiveValue, mode, beta, Cp, ldc, workspace, ws_bytes, stream=None):
+    check(lib().p2cu_sgemm_fvb(M, N, K, alpha, A, lda, C.byref(B), mode, beta, Cp, ldc, workspace, ws_bytes,
+                               stream_ptr(stream)))
+
+
+def sgemm_fvb_q8a(M, N, K, alpha, q, a_scales, B: P2cuFiveValue, mode, beta, Cp, ldc, stream=None):
+    check(lib().p2cu_sgemm_fvb_q8a(M, N, K, alpha, q, a_scales, C.byref(B), mode, beta, Cp, ldc, stream_ptr(stream)))
+
+
+def sgemm_q8b(M, N, K, alpha, A, lda, B, scales, ldb, mode, beta, Cp, ldc, workspace, ws_bytes, stream=None):
+    check(lib().p2cu_sgemm_q8b(M, N, K, alpha, A, lda, B, scales, ldb, mode, beta, Cp, ldc, workspace, ws_bytes,
+                               stream_ptr(stream)))
+
+
+def sgemm_q8b_q8a(M, N, K, alpha, q, a_scales, B, scales, ldb, beta, Cp, ldc, stream=None):
+    check(lib().p2cu_sgemm_q8b_q8a(M, N, K, alpha, q, a_scales, B, scales, ldb, beta, Cp, ldc, stream_ptr(stream)))
+
+
+def sgemm(transA, transB, M, N, K, alpha, A, lda, B, ldb, beta, Cp, ldc, stream=None):
+    check(lib().p2cu_sgemm(int(transA), int(transB), M, N, K, alpha, A, lda, B, ldb, beta, Cp, ldc,
+                           stream_ptr(stream)))
+
+
+def fv_pack_codes(B: P2cuFiveValue, codes: int, stream=None) -> None:
+    check(lib().p2cu_fv_pack_codes(C.byref(B), codes, stream_ptr(stream)))
+
+
+def check_device(stream=None) -> None:
+    check(lib().p2cu_check_device(stream_ptr(stream)))

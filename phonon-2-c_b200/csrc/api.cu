@@ -1,0 +1,319 @@
+// api.cu - the device-pointer C ABI (include/p2cuda.h): argument checks, TMA descriptors, kernel selection.
+#include <cstdarg>
+#include <cstdint>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include "p2cuda.h"
+#include "fv_gemm.h"
+#include "kernels.h"
+
+namespace {
+
+thread_local char g_msg[512] = "";
+
+int fail(int code, const char* fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_msg, sizeof(g_msg), fmt, ap);
+    va_end(ap);
+    return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+    return fail(P2CU_ECUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+// The device error word the kernels report bounded-wait timeouts in; one per device (a __device__ variable exists
+// once per device the module is loaded on), its address looked up per device.
+__device__ uint32_t g_dev_err;
+
+uint32_t* dev_err_ptr() {
+    static uint32_t* ptrs[64] = {};
+    static std::mutex mu;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return nullptr;
+    std::lock_guard<std::mutex> lock(mu);
+    if (!ptrs[dev]) {
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_dev_err) != cudaSuccess) return nullptr;
+        ptrs[dev] = static_cast<uint32_t*>(p);
+    }
+    return ptrs[dev];
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link-time dependency on libcuda).
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
+                cudaSuccess && q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    return fn;
+}
+
+// A 2-D uint8 tensor map: `inner` bytes per row, `outer` rows, rows `stride` bytes apart, boxes box_in x box_out.
+int make_map(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t stride, uint32_t box_in,
+             uint32_t box_out, bool swizzle128, const char* what) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return fail(P2CU_ECUDA, "cuTensorMapEncodeTiled is not available from the driver");
+    if (reinterpret_cast<uintptr_t>(base) % 16) return fail(P2CU_EINVAL, "%s: base address not 16-byte aligned", what);
+    if (stride % 16) return fail(P2CU_EINVAL, "%s: row stride %llu not a multiple of 16 bytes", what,
+                                 static_cast<unsigned long long>(stride));
+    const cuuint64_t dims[2] = {inner, outer};
+    const cuuint64_t strides[1] = {stride};
+    const cuuint32_t box[2] = {box_in, box_out};
+    const cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE,
+                     swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(P2CU_ECUDA, "%s: cuTensorMapEncodeTiled failed (%d)", what, static_cast<int>(r));
+    return P2CU_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+size_t round256(size_t x) { return (x + 255) & ~size_t(255); }
+
+__global__ void scale_c_kernel(float* C, int M, int N, int ldc, float beta) {
+    const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= static_cast<size_t>(M) * N) return;
+    const int m = static_cast<int>(i / N), n = static_cast<int>(i % N);
+    float* c = C + static_cast<size_t>(m) * ldc + n;
+    *c = beta == 0.f ? 0.f : __fmul_rn(*c, beta);
+}
+
+// C = beta * C as the reference's scale_c (csrc/blas.c:60-70): nothing for beta == 1, zeros for beta == 0.
+int scale_c(float* C, int M, int N, int ldc, float beta, cudaStream_t s) {
+    if (beta == 1.f || M == 0 || N == 0) return P2CU_OK;
+    const size_t total = static_cast<size_t>(M) * N;
+    scale_c_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, s>>>(C, M, N, ldc, beta);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? P2CU_OK : cuda_fail(e, "scale_c");
+}
+
+int check_gemm_common(int M, int N, int K, const void* C, int ldc, const char* who) {
+    if (M < 0 || N < 0 || K < 0) return fail(P2CU_EINVAL, "%s: negative shape M=%d N=%d K=%d", who, M, N, K);
+    if (!C && M && N) return fail(P2CU_EINVAL, "%s: C is NULL", who);
+    if (ldc < N) return fail(P2CU_EINVAL, "%s: ldc=%d < N=%d", who, ldc, N);
+    return P2CU_OK;
+}
+
+// The tcgen05 GEMM on quantised rows. `B` five-value (planes or cached codes) or `q8`/`scales` an int8 table.
+int run_i8(int M, int N, int K, float alpha, const int8_t* q, const float* a_scales, const P2cuFiveValue* B,
+           const int8_t* q8, const float* scales, int ldb, int mode, float beta, float* C, int ldc, cudaStream_t s,
+           const char* who) {
+    int rc = check_gemm_common(M, N, K, C, ldc, who);
+    if (rc) return rc;
+    if (N % 16) return fail(P2CU_EINVAL, "%s: N = %d is not a multiple of 16", who, N);
+    if (M == 0 || N == 0) return P2CU_OK;
+    if (alpha == 0.f || K == 0) return scale_c(C, M, N, ldc, beta, s);   // no products: C = beta * C
+    if (N % 128) return fail(P2CU_EUNSUPPORTED, "%s: N = %d: the tensor-core path needs N %% 128 == 0", who, N);
+    if (K % 16) return fail(P2CU_EUNSUPPORTED, "%s: K = %d: the tensor-core path needs K %% 16 == 0", who, K);
+    if (!q || !a_scales) return fail(P2CU_EINVAL, "%s: quantised A is NULL", who);
+    if (!aligned16(C) || ldc % 4) return fail(P2CU_EINVAL, "%s: C must be 16-byte aligned with ldc %% 4 == 0", who);
+    if (beta != 0.f && beta != 1.f) {
+        if ((rc = scale_c(C, M, N, ldc, beta, s))) return rc;
+        beta = 1.f;
+    }
+    p2cu::FvGemmParams p{};
+    p.M = M; p.N = N; p.K = K; p.alpha = alpha; p.beta_zero = beta == 0.f;
+    p.a_scales = a_scales; p.C = C; p.ldc = ldc; p.err = dev_err_ptr();
+    CUtensorMap ta, tb0, tb1;
+    if ((rc = make_map(&ta, q, static_cast<uint64_t>(K), static_cast<uint64_t>(M), static_cast<uint64_t>(K), 128, 128,
+                       true, "A")))
+        return rc;
+    cudaError_t e;
+    if (B) {
+        if (!B->lo || !B->hi) return fail(P2CU_EINVAL, "%s: lo / hi are NULL", who);
+        if (B->K != K || B->N != N) return fail(P2CU_EINVAL, "%s: weight is [%d, %d], GEMM wants [%d, %d]", who, B->K,
+                                                B->N, K, N);
+        p.lo = B->lo; p.hi = B->hi;
+        if (mode == P2CU_INT8W && B->codes) {
+            p.cmode = p2cu::CM_INT8W;   // one plane of codes, f = (float)acc * (hi / 127)
+            if ((rc = make_map(&tb0, B->codes, static_cast<uint64_t>(N), static_cast<uint64_t>(K),
+                               static_cast<uint64_t>(N), 128, 128, true, "codes")))
+                return rc;
+            e = p2cu::fv_gemm_launch_table(ta, tb0, p, s);
+        } else {
+            if (!B->signs || !B->flags) return fail(P2CU_EINVAL, "%s: planes are NULL", who);
+            p.cmode = mode == P2CU_INT8W ? p2cu::CM_INT8W : p2cu::CM_INT8;
+            if ((rc = make_map(&tb0, B->signs, static_cast<uint64_t>(N / 4), static_cast<uint64_t>(K),
+                               static_cast<uint64_t>(N / 4), 32, 128, false, "signs")))
+                return rc;
+            if ((rc = make_map(&tb1, B->flags, static_cast<uint64_t>(N / 8), static_cast<uint64_t>(K),
+                               static_cast<uint64_t>(N / 8), 16, 128, false, "flags")))
+                return rc;
+            e = p2cu::fv_gemm_launch_planes(ta, tb0, tb1, p, s);
+        }
+    } else {
+        if (!q8 || !scales) return fail(P2CU_EINVAL, "%s: int8 table is NULL", who);
+        if (ldb < N) return fail(P2CU_EINVAL, "%s: ldb=%d < N=%d", who, ldb, N);
+        p.cmode = p2cu::CM_Q8B;
+        p.scales = scales;
+        if ((rc = make_map(&tb0, q8, static_cast<uint64_t>(N), static_cast<uint64_t>(K), static_cast<uint64_t>(ldb),
+                           128, 128, true, "B")))
+            return rc;
+        e = p2cu::fv_gemm_launch_table(ta, tb0, p, s);
+    }
+    return e == cudaSuccess ? P2CU_OK : cuda_fail(e, who);
+}
+
+int run_exact(int M, int N, int K, float alpha, const float* A, int lda, int transA, const P2cuFiveValue* B,
+              const int8_t* q8, const float* scales, const float* Bf, int ldb, int transB, float beta, float* C,
+              int ldc, cudaStream_t s, const char* who) {
+    int rc = check_gemm_common(M, N, K, C, ldc, who);
+    if (rc) return rc;
+    if (M == 0 || N == 0) return P2CU_OK;
+    if (alpha == 0.f) return scale_c(C, M, N, ldc, beta, s);
+    if (!A) return fail(P2CU_EINVAL, "%s: A is NULL", who);
+    p2cu::ExactParams p{};
+    p.M = M; p.N = N; p.K = K; p.alpha = alpha; p.beta = beta;
+    p.A = A; p.lda = lda; p.transA = transA; p.ldb = ldb; p.transB = transB; p.C = C; p.ldc = ldc;
+    p.vec_store = (N % 4 == 0) && (ldc % 4 == 0) && aligned16(C);
+    if (B) {
+        if (N % 16) return fail(P2CU_EINVAL, "%s: N = %d is not a multiple of 16", who, N);
+        if (B->K != K || B->N != N) return fail(P2CU_EINVAL, "%s: weight is [%d, %d], GEMM wants [%d, %d]", who, B->K,
+                                                B->N, K, N);
+        if (!B->signs || !B->flags || !B->lo || !B->hi) return fail(P2CU_EINVAL, "%s: planes are NULL", who);
+        p.bkind = p2cu::BK_FIVE;
+        p.signs = B->signs; p.flags = B->flags; p.lo = B->lo; p.hi = B->hi;
+    } else if (q8) {
+        if (N % 16) return fail(P2CU_EINVAL, "%s: N = %d is not a multiple of 16", who, N);
+        if (!scales) return fail(P2CU_EINVAL, "%s: scales are NULL", who);
+        p.bkind = p2cu::BK_TABLE;
+        p.q8 = q8; p.scales = scales;
+    } else {
+        if (!Bf) return fail(P2CU_EINVAL, "%s: B is NULL", who);
+        p.bkind = p2cu::BK_F32;
+        p.Bf = Bf;
+    }
+    cudaError_t e = p2cu::exact_gemm_launch(p, s);
+    return e == cudaSuccess ? P2CU_OK : cuda_fail(e, who);
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* p2cu_last_error(void) { return g_msg; }
+
+int p2cu_check_device(void* stream) {
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaError_t e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return cuda_fail(e, "stream");
+    uint32_t v = 0, zero = 0;
+    if ((e = cudaMemcpyFromSymbol(&v, g_dev_err, sizeof(v))) != cudaSuccess) return cuda_fail(e, "error word");
+    if (v) {
+        cudaMemcpyToSymbol(g_dev_err, &zero, sizeof(zero));
+        return fail(P2CU_EDEVICE, "a kernel stopped waiting on a barrier (code %u)", v);
+    }
+    return P2CU_OK;
+}
+
+int p2cu_quant_rows(const float* A, int M, int K, int lda, signed char* q, float* scales, void* stream) {
+    if (M < 0 || K < 0 || lda < K) return fail(P2CU_EINVAL, "p2cu_quant_rows: bad shape M=%d K=%d lda=%d", M, K, lda);
+    if (M == 0 || K == 0) return P2CU_OK;
+    if (!A || !q || !scales) return fail(P2CU_EINVAL, "p2cu_quant_rows: NULL pointer");
+    cudaError_t e = p2cu::quant_rows_launch(A, M, K, lda, reinterpret_cast<int8_t*>(q), scales,
+                                            static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? P2CU_OK : cuda_fail(e, "p2cu_quant_rows");
+}
+
+int p2cu_sgemm_fvb_q8a(int M, int N, int K, float alpha, const signed char* q, const float* a_scales,
+                       const P2cuFiveValue* B, int mode, float beta, float* C, int ldc, void* stream) {
+    if (!B) return fail(P2CU_EINVAL, "p2cu_sgemm_fvb_q8a: B is NULL");
+    if (mode != P2CU_INT8 && mode != P2CU_INT8W) return fail(P2CU_EINVAL, "p2cu_sgemm_fvb_q8a: mode %d", mode);
+    return run_i8(M, N, K, alpha, reinterpret_cast<const int8_t*>(q), a_scales, B, nullptr, nullptr, 0, mode, beta,
+                  C, ldc, static_cast<cudaStream_t>(stream), "p2cu_sgemm_fvb_q8a");
+}
+
+int p2cu_sgemm_q8b_q8a(int M, int N, int K, float alpha, const signed char* q, const float* a_scales,
+                       const signed char* B, const float* scales, int ldb, float beta, float* C, int ldc,
+                       void* stream) {
+    return run_i8(M, N, K, alpha, reinterpret_cast<const int8_t*>(q), a_scales, nullptr,
+                  reinterpret_cast<const int8_t*>(B), scales, ldb, P2CU_INT8, beta, C, ldc,
+                  static_cast<cudaStream_t>(stream), "p2cu_sgemm_q8b_q8a");
+}
+
+size_t p2cu_gemm_workspace_bytes(int M, int K, int mode) {
+    if (mode == P2CU_EXACT || M <= 0 || K <= 0) return 0;
+    return round256(static_cast<size_t>(M) * K) + round256(static_cast<size_t>(M) * sizeof(float));
+}
+
+static int quantise_into(const float* A, int M, int K, int lda, void* ws, size_t ws_bytes, int8_t** q, float** sc,
+                         cudaStream_t s, const char* who) {
+    const size_t need = p2cu_gemm_workspace_bytes(M, K, P2CU_INT8);
+    if (!ws || ws_bytes < need) return fail(P2CU_EINVAL, "%s: workspace of %zu bytes, %zu needed", who, ws_bytes, need);
+    if (!aligned16(ws)) return fail(P2CU_EINVAL, "%s: workspace not 16-byte aligned", who);
+    if (!A) return fail(P2CU_EINVAL, "%s: A is NULL", who);
+    *q = static_cast<int8_t*>(ws);
+    *sc = reinterpret_cast<float*>(static_cast<char*>(ws) + round256(static_cast<size_t>(M) * K));
+    cudaError_t e = p2cu::quant_rows_launch(A, M, K, lda, *q, *sc, s);
+    return e == cudaSuccess ? P2CU_OK : cuda_fail(e, who);
+}
+
+int p2cu_sgemm_fvb(int M, int N, int K, float alpha, const float* A, int lda, const P2cuFiveValue* B, int mode,
+                   float beta, float* C, int ldc, void* workspace, size_t workspace_bytes, void* stream) {
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (!B) return fail(P2CU_EINVAL, "p2cu_sgemm_fvb: B is NULL");
+    if (mode == P2CU_EXACT)
+        return run_exact(M, N, K, alpha, A, lda, 0, B, nullptr, nullptr, nullptr, 0, 0, beta, C, ldc, s,
+                         "p2cu_sgemm_fvb");
+    if (mode != P2CU_INT8 && mode != P2CU_INT8W) return fail(P2CU_EINVAL, "p2cu_sgemm_fvb: mode %d", mode);
+    int rc = check_gemm_common(M, N, K, C, ldc, "p2cu_sgemm_fvb");
+    if (rc) return rc;
+    if (M == 0 || N == 0) return P2CU_OK;
+    if (alpha == 0.f) return scale_c(C, M, N, ldc, beta, s);
+    int8_t* q;
+    float* sc;
+    if ((rc = quantise_into(A, M, K, lda, workspace, workspace_bytes, &q, &sc, s, "p2cu_sgemm_fvb"))) return rc;
+    return run_i8(M, N, K, alpha, q, sc, B, nullptr, nullptr, 0, mode, beta, C, ldc, s, "p2cu_sgemm_fvb");
+}
+
+int p2cu_sgemm_q8b(int M, int N, int K, float alpha, const float* A, int lda, const signed char* B,
+                   const float* scales, int ldb, int mode, float beta, float* C, int ldc, void* workspace,
+                   size_t workspace_bytes, void* stream) {
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (mode == P2CU_EXACT)
+        return run_exact(M, N, K, alpha, A, lda, 0, nullptr, reinterpret_cast<const int8_t*>(B), scales, nullptr, ldb,
+                         0, beta, C, ldc, s, "p2cu_sgemm_q8b");
+    int rc = check_gemm_common(M, N, K, C, ldc, "p2cu_sgemm_q8b");
+    if (rc) return rc;
+    if (M == 0 || N == 0) return P2CU_OK;
+    if (alpha == 0.f) return scale_c(C, M, N, ldc, beta, s);
+    int8_t* q;
+    float* sc;
+    if ((rc = quantise_into(A, M, K, lda, workspace, workspace_bytes, &q, &sc, s, "p2cu_sgemm_q8b"))) return rc;
+    return run_i8(M, N, K, alpha, q, sc, nullptr, reinterpret_cast<const int8_t*>(B), scales, ldb, P2CU_INT8, beta, C,
+                  ldc, s, "p2cu_sgemm_q8b");
+}
+
+int p2cu_sgemm(int transA, int transB, int M, int N, int K, float alpha, const float* A, int lda, const float* B,
+               int ldb, float beta, float* C, int ldc, void* stream) {
+    return run_exact(M, N, K, alpha, A, lda, transA ? 1 : 0, nullptr, nullptr, nullptr, B, ldb, transB ? 1 : 0, beta,
+                     C, ldc, static_cast<cudaStream_t>(stream), "p2cu_sgemm");
+}
+
+int p2cu_fv_pack_codes(const P2cuFiveValue* B, signed char* codes, void* stream) {
+    if (!B || !codes || !B->signs || !B->flags || !B->lo || !B->hi)
+        return fail(P2CU_EINVAL, "p2cu_fv_pack_codes: NULL pointer");
+    if (B->K <= 0 || B->N <= 0 || B->N % 16) return fail(P2CU_EINVAL, "p2cu_fv_pack_codes: shape [%d, %d]", B->K, B->N);
+    cudaError_t e = p2cu::fv_codes_launch(B->signs, B->flags, B->lo, B->hi, B->K, B->N,
+                                          reinterpret_cast<int8_t*>(codes), static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? P2CU_OK : cuda_fail(e, "p2cu_fv_pack_codes");
+}
+
+}  // extern "C"

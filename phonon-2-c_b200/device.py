@@ -1,0 +1,39 @@
+"""Device-memory plumbing for Python callers of libphonon2_b200.so: torch allocates and moves bytes, the library
+computes. Nothing here does arithmetic on the data."""
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+from . import P2cuFiveValue, five_value_struct
+
+
+class DeviceFiveValue:
+    """A five-value weight (synth.five_value layout) copied to the device once, with its P2cuFiveValue view."""
+
+    def __init__(self, w: dict, device="cuda", codes: bool = False, stream=None):
+        self.K, self.N = int(w["K"]), int(w["N"])
+        self.signs = torch.from_numpy(np.ascontiguousarray(w["signs"])).to(device)
+        self.flags = torch.from_numpy(np.ascontiguousarray(w["flags"])).to(device)
+        self.lo = torch.from_numpy(np.ascontiguousarray(w["lo"])).to(device)
+        self.hi = torch.from_numpy(np.ascontiguousarray(w["hi"])).to(device)
+        self.codes = None
+        self.struct = five_value_struct(self.signs.data_ptr(), self.flags.data_ptr(), self.lo.data_ptr(),
+                                        self.hi.data_ptr(), self.K, self.N)
+        if codes:
+            self.pack_codes(stream)
+
+    def pack_codes(self, stream=None) -> None:
+        from . import fv_pack_codes
+        self.codes = torch.empty((self.K, self.N), dtype=torch.int8, device=self.signs.device)
+        fv_pack_codes(self.struct, self.codes.data_ptr(), stream)
+        self.struct.codes = self.codes.data_ptr()
+
+    def without_codes(self) -> P2cuFiveValue:
+        s = P2cuFiveValue.from_buffer_copy(self.struct)
+        s.codes = None
+        return s
+
+    @property
+    def plane_bytes(self) -> int:
+        return self.signs.numel() + self.flags.numel() + 4 * (self.lo.numel() + self.hi.numel())
