@@ -47,10 +47,11 @@ def block_macs(T=T_FRAMES) -> int:
     return sum(M * K * N for _, M, K, N, _, _ in block_gemms(T))
 
 
-def gemm_bytes(M, K, N, beta) -> int:
-    """Algorithmic HBM bytes of one GEMM launch on quantised A: int8 A, the planes (3 bits per weight), lo/hi, the
-    fp32 C store and, when accumulating, the C read."""
-    return M * K + 3 * K * N // 8 + 8 * N + 4 * M * N + (4 * M * N if beta != 0.0 else 0)
+def gemm_bytes(M, K, N, beta, codes=False) -> int:
+    """Algorithmic HBM bytes of one GEMM launch on quantised A: int8 A, the weight (the planes at 3 bits per weight,
+    or the cached int8w codes at 8), lo/hi, the fp32 C store and, when accumulating, the C read."""
+    w = K * N if codes else 3 * K * N // 8
+    return M * K + w + 8 * N + 4 * M * N + (4 * M * N if beta != 0.0 else 0)
 
 
 def load_peaks():
@@ -221,21 +222,21 @@ def run_reference(args, world, rank):
 class GpuSet:
     """One independent copy of the workload on the device: weights, fp32 activations, outputs, workspace."""
 
-    def __init__(self, pkg, torch, dev, seed, mode, gemms):
+    def __init__(self, pkg, torch, dev, seed, mode, gemms, codes=False):
         from phonon2_b200 import synth
         from phonon2_b200.device import DeviceFiveValue
         self.items = []
         for i, (name, M, K, N, alpha, beta) in enumerate(gemms):
             w = synth.five_value(K, N, seed=1000 * seed + i)
-            B = DeviceFiveValue(w, dev, codes=False)
+            B = DeviceFiveValue(w, dev, codes=codes)
             A = torch.from_numpy(synth.activations(M, K, seed=2000 * seed + i)).to(dev)
             C = torch.zeros((M, N), dtype=torch.float32, device=dev)
-            ws = torch.empty(max(pkg.workspace_bytes(M, K, mode), 256), dtype=torch.uint8, device=dev)
+            ws = torch.empty(max(pkg.workspace_bytes(M, N, K, mode), 256), dtype=torch.uint8, device=dev)
             self.items.append((M, K, N, alpha, beta, B, A, C, ws))
 
     def bytes(self):
-        return sum(B.plane_bytes + A.numel() * 4 + C.numel() * 4 + ws.numel()
-                   for (_, _, _, _, _, B, A, C, ws) in self.items)
+        return sum(B.plane_bytes + (B.codes.numel() if B.codes is not None else 0) + A.numel() * 4 + C.numel() * 4
+                   + ws.numel() for (_, _, _, _, _, B, A, C, ws) in self.items)
 
     def run(self, pkg, mode, stream):
         for (M, K, N, alpha, beta, B, A, C, ws) in self.items:
@@ -251,7 +252,9 @@ class GpuSet:
         for (M, K, N, alpha, beta, B, A, C, ws) in self.items:
             q = ws.data_ptr()
             sc = q + ((M * K + 255) // 256) * 256
-            pkg.sgemm_fvb_q8a(M, N, K, alpha, q, sc, B.struct, mode, beta, C.data_ptr(), N, stream)
+            rest = sc + ((M * 4 + 255) // 256) * 256
+            pkg.sgemm_fvb_q8a(M, N, K, alpha, q, sc, B.struct, mode, beta, C.data_ptr(), N, rest,
+                              ws.numel() - (rest - q), stream)
 
 
 def run_ours(args, world, rank, local):
@@ -264,9 +267,10 @@ def run_ours(args, world, rank, local):
     stream = torch.cuda.Stream(device=dev)
 
     # Enough independent copies of the inputs that consecutive steps never find their operands in L2.
-    first = GpuSet(pkg, torch, dev, 1 + rank * 100, mode, gemms)
+    codes = args.weights == "codes"
+    first = GpuSet(pkg, torch, dev, 1 + rank * 100, mode, gemms, codes)
     nsets = max(2, int(np.ceil(2 * L2_BYTES / first.bytes())))
-    sets = [first] + [GpuSet(pkg, torch, dev, 2 + i + rank * 100, mode, gemms) for i in range(nsets - 1)]
+    sets = [first] + [GpuSet(pkg, torch, dev, 2 + i + rank * 100, mode, gemms, codes) for i in range(nsets - 1)]
     torch.cuda.synchronize()
 
     with torch.cuda.stream(stream):
@@ -322,7 +326,7 @@ def run_ours(args, world, rank, local):
         g1.record(stream)
     g1.synchronize()
     gemm_ms = g0.elapsed_time(g1) / reps
-    algo_bytes = sum(gemm_bytes(M, K, N, beta) for _, M, K, N, _, beta in gemms)
+    algo_bytes = sum(gemm_bytes(M, K, N, beta, codes) for _, M, K, N, _, beta in gemms)
     peak, peak_kind = load_peaks()
     achieved = algo_bytes / (gemm_ms / 1e3) / 1e9
 
@@ -336,12 +340,12 @@ def run_ours(args, world, rank, local):
                 "data": "synthetic",
                 "config": {"workload": f"one FastConformer block's nine five-value GEMMs at T={T_FRAMES} "
                                        "(BASELINE configs[1]): fp32 A quantised per row, then the tcgen05 GEMM",
-                           "mode": args.mode, "T": T_FRAMES, "macs_per_step": macs,
+                           "mode": args.mode, "weights": args.weights, "T": T_FRAMES, "macs_per_step": macs,
                            "l2": f"inputs rotate over {nsets} copies ({nsets * first.bytes() / 2**20:.0f} MiB > 2x L2)",
                            "parallelism": f"replicas x{world} (independent windows)"},
                 "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                              "frac": achieved / peak, "traffic": None, "peak_kind": peak_kind,
-                             "kernel": "fv_gemm_kernel<planes> (nine launches of a step)",
+                             "kernel": f"fv_gemm_kernel ({args.weights}; nine launches of a step)",
                              "algo_bytes_per_step": algo_bytes, "gemm_us_per_step": gemm_ms * 1e3},
                 "gpu_launches": args.steps * 2 * len(gemms),
                 "clocks": clocks.summary(),
@@ -391,6 +395,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--mode", choices=["int8w", "int8", "exact"], default="int8w")
+    ap.add_argument("--weights", choices=["planes", "codes"], default="planes",
+                    help="planes: expand the sign/magnitude planes in every GEMM (the reference's default); codes: "
+                         "the int8w code cache (the reference's P2_CACHE_CODES), int8w only")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)

@@ -62,17 +62,24 @@ P2CU_API int p2cu_check_device(void *stream);
 P2CU_API int p2cu_quant_rows(const float *A, int M, int K, int lda, signed char *q, float *scales, void *stream);
 
 /* C = alpha * A * B + beta * C on quantised A (csrc/blas.c:1430-1437). mode P2CU_INT8 or P2CU_INT8W.
- * N % 128 == 0, K % 16 == 0. beta: 0 stores, 1 accumulates, other values scale C first. */
+ * N % 128 == 0, K % 16 == 0. beta: 0 stores, 1 accumulates, other values scale C first. When K > 1024 the GEMM
+ * keeps one fp32 value per output and 1024-row block of K in `workspace` (p2cu_q8a_workspace_bytes; 0 otherwise)
+ * and folds them into C in block order, as the reference's blockwise epilogue does. */
 P2CU_API int p2cu_sgemm_fvb_q8a(int M, int N, int K, float alpha, const signed char *q, const float *a_scales,
-                       const P2cuFiveValue *B, int mode, float beta, float *C, int ldc, void *stream);
+                                const P2cuFiveValue *B, int mode, float beta, float *C, int ldc, void *workspace,
+                                size_t workspace_bytes, void *stream);
 
 /* The same with an int8 table B [K, N] (row stride ldb bytes) and one scale per column (csrc/blas.c:1439-1446). */
 P2CU_API int p2cu_sgemm_q8b_q8a(int M, int N, int K, float alpha, const signed char *q, const float *a_scales,
-                       const signed char *B, const float *scales, int ldb, float beta, float *C, int ldc,
-                       void *stream);
+                                const signed char *B, const float *scales, int ldb, float beta, float *C, int ldc,
+                                void *workspace, size_t workspace_bytes, void *stream);
 
-/* Workspace bytes p2cu_sgemm_fvb / p2cu_sgemm_q8b need for M x K activations in the int8 modes (0 in exact mode). */
-P2CU_API size_t p2cu_gemm_workspace_bytes(int M, int K, int mode);
+/* Workspace bytes of the q8a GEMMs (K-block slices when K > 1024, else 0). */
+P2CU_API size_t p2cu_q8a_workspace_bytes(int M, int N, int K);
+
+/* Workspace bytes of p2cu_sgemm_fvb / p2cu_sgemm_q8b: the quantised activations plus the K-block slices
+ * (0 in exact mode). */
+P2CU_API size_t p2cu_gemm_workspace_bytes(int M, int N, int K, int mode);
 
 /* C = alpha * A * B + beta * C from fp32 A (csrc/blas.c:1481-1499 / 1462-1479): in the int8 modes A is quantised
  * into `workspace` first; in P2CU_EXACT the weights are expanded to fp32 and every output is the reference's FMA

@@ -1,0 +1,155 @@
+/*  phonon2.h - the phonon-2-c types and constants this library's ABI uses, laid out exactly as phonon-2-c's own
+ *  csrc/phonon2.h lays them out (v0.1.0), so that objects compiled against either header interoperate.
+ *
+ *  Only declarations this library implements live here (the weight and model structs, QuantA, the model
+ *  constants). phonon-2-c's engine, audio front end, decoder and tokenizer keep their own header and sources; a
+ *  build that links them with libphonon2_b200.so gets the GEMM layer and the encoder from the GPU.
+ *  Each type cites the reference declaration it mirrors (csrc/phonon2.h line numbers).
+ */
+#ifndef PHONON2_H
+#define PHONON2_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define P2_API __attribute__((visibility("default")))
+#else
+#define P2_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* The model's dimensions (csrc/phonon2.h:73-105). */
+#define P2_D_MODEL      1024
+#define P2_N_HEADS      8
+#define P2_HEAD_DIM     128
+#define P2_FF_DIM       4096
+#define P2_N_BLOCKS     24
+#define P2_CONV_KERNEL  9
+#define P2_N_MELS       128
+#define P2_SUB_CHANNELS 256
+#define P2_SUB_FACTOR   8
+#define P2_LSTM_HIDDEN  640
+#define P2_LSTM_LAYERS  2
+#define P2_EMBED_DIM    640
+#define P2_JOINT_DIM    640
+#define P2_VOCAB        8193
+#define P2_BLANK        8192
+#define P2_N_DURATIONS  5
+#define P2_N_LOGITS     (P2_VOCAB + P2_N_DURATIONS)
+
+/* A GEMM weight op(B) = [K, N] in one of three storage kinds (csrc/phonon2.h:109-126). */
+typedef enum {
+    P2_W_F32 = 0,   /* fp32 [K, N] */
+    P2_W_I8  = 8,   /* int8 [K, N], one fp32 scale per column */
+    P2_W_FV  = 5    /* five-value: per column n the values {0, +-lo[n], +-hi[n]} as sign and magnitude planes */
+} P2WeightKind;
+
+typedef struct {
+    P2WeightKind kind;
+    int K, N;
+    const float         *f32;
+    const signed char   *q8;
+    const float         *scales;
+    const unsigned char *signs;    /* [K][N/4], the 2-bit code (sign + 1) of column n at bits 2*(n & 3) */
+    const unsigned char *flags;    /* [K][N/8], bit (n & 7) set when |w| = hi[n] */
+    const float         *lo, *hi;  /* [N] */
+    signed char         *codes;    /* optional pre-expanded int8w codes (p2_fv_pack_codes), else NULL */
+} Weight;
+
+/* csrc/phonon2.h:128-137: the 8x convolutional subsampling. */
+typedef struct {
+    const float *conv0_w, *conv0_b;   /* Conv2d 1 -> 256, 3x3, stride 2 */
+    const float *conv2_w, *conv2_b;   /* depthwise 3x3, stride 2 */
+    const float *conv3_w, *conv3_b;   /* pointwise 256 -> 256 */
+    const float *conv5_w, *conv5_b;   /* depthwise 3x3, stride 2 */
+    const float *conv6_w, *conv6_b;   /* pointwise 256 -> 256 */
+    Weight       linear_w;            /* [4096, 1024] int8 table */
+    const float *linear_b;
+} SubsamplingWeights;
+
+/* csrc/phonon2.h:139-142 */
+typedef struct {
+    Weight linear1_w;   /* [1024, 4096] */
+    Weight linear2_w;   /* [4096, 1024] */
+} FFWeights;
+
+/* csrc/phonon2.h:144-150 */
+typedef struct {
+    Weight       qkv_w;    /* [1024, 3072]: Q | K | V */
+    Weight       pos_w;    /* [1024, 1024] */
+    Weight       out_w;    /* [1024, 1024] */
+    const float *bias_u;   /* [8 x 128] */
+    const float *bias_v;
+} MHAWeights;
+
+/* csrc/phonon2.h:152-157 */
+typedef struct {
+    Weight       pw1_w;    /* [1024, 2048], followed by a GLU */
+    const float *dw_w;     /* [1024 x 9] depthwise, BatchNorm folded in */
+    const float *dw_b;     /* [1024] */
+    Weight       pw2_w;    /* [1024, 1024] */
+} ConvModWeights;
+
+/* csrc/phonon2.h:159-169 */
+typedef struct {
+    const float *norm_ff1_w, *norm_ff1_b;
+    FFWeights    ff1;
+    const float *norm_sa_w, *norm_sa_b;
+    MHAWeights   mha;
+    const float *norm_conv_w, *norm_conv_b;
+    ConvModWeights conv;
+    const float *norm_ff2_w, *norm_ff2_b;
+    FFWeights    ff2;
+    const float *norm_out_w, *norm_out_b;
+} ConformerBlock;
+
+/* csrc/phonon2.h:177-182 */
+typedef struct {
+    SubsamplingWeights subsampling;
+    ConformerBlock     blocks[P2_N_BLOCKS];
+    Weight             projector_w;   /* [1024, 640] int8 table */
+    const float       *projector_b;
+} EncoderWeights;
+
+#define P2_DEC_OWNED 8
+
+/* csrc/phonon2.h:189-199 */
+typedef struct {
+    const float *embed_w;
+    const float *lstm_w_ih[P2_LSTM_LAYERS];
+    const float *lstm_w_hh[P2_LSTM_LAYERS];
+    const float *lstm_b_ih[P2_LSTM_LAYERS];
+    const float *lstm_b_hh[P2_LSTM_LAYERS];
+    const float *proj_w, *proj_b;
+    const float *head_w, *head_b;
+    float       *owned[P2_DEC_OWNED];
+    int          n_owned;
+} DecoderWeights;
+
+/* csrc/phonon2.h:201-206 */
+typedef struct {
+    EncoderWeights enc;
+    DecoderWeights dec;
+    void          *map;
+    size_t         map_len;
+} P2Model;
+
+/* Activations prepared for the int8 GEMMs (csrc/phonon2.h:432-436). In this build the rows given to p2_quant_row
+ * are kept as fp32 in `q` (a buffer of the calling thread) and quantised on the GPU inside the GEMM, with the
+ * reference's rounding; `scales` is NULL. Callers that only pass a QuantA from prepare to the GEMM see no
+ * difference. */
+typedef struct {
+    signed char *q;
+    float       *scales;
+    int          M, K;
+} QuantA;
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PHONON2_H */

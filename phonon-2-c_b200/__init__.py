@@ -53,14 +53,32 @@ SIGNATURES = {
     "p2cu_last_error": (C.c_char_p, []),
     "p2cu_check_device": (_i, [_vp]),
     "p2cu_quant_rows": (_i, [_vp, _i, _i, _i, _vp, _vp, _vp]),
-    "p2cu_sgemm_fvb_q8a": (_i, [_i, _i, _i, _f, _vp, _vp, C.POINTER(P2cuFiveValue), _i, _f, _vp, _i, _vp]),
-    "p2cu_sgemm_q8b_q8a": (_i, [_i, _i, _i, _f, _vp, _vp, _vp, _vp, _i, _f, _vp, _i, _vp]),
-    "p2cu_gemm_workspace_bytes": (_sz, [_i, _i, _i]),
+    "p2cu_sgemm_fvb_q8a": (_i, [_i, _i, _i, _f, _vp, _vp, C.POINTER(P2cuFiveValue), _i, _f, _vp, _i, _vp, _sz,
+                                _vp]),
+    "p2cu_sgemm_q8b_q8a": (_i, [_i, _i, _i, _f, _vp, _vp, _vp, _vp, _i, _f, _vp, _i, _vp, _sz, _vp]),
+    "p2cu_q8a_workspace_bytes": (_sz, [_i, _i, _i]),
+    "p2cu_gemm_workspace_bytes": (_sz, [_i, _i, _i, _i]),
     "p2cu_sgemm_fvb": (_i, [_i, _i, _i, _f, _vp, _i, C.POINTER(P2cuFiveValue), _i, _f, _vp, _i, _vp, _sz, _vp]),
     "p2cu_sgemm_q8b": (_i, [_i, _i, _i, _f, _vp, _i, _vp, _vp, _i, _i, _f, _vp, _i, _vp, _sz, _vp]),
     "p2cu_sgemm": (_i, [_i, _i, _i, _i, _i, _f, _vp, _i, _vp, _i, _f, _vp, _i, _vp]),
     "p2cu_fv_pack_codes": (_i, [C.POINTER(P2cuFiveValue), _vp, _vp]),
+    # include/blas.h: the reference's host-pointer ABI
+    "p2_sgemm": (None, [_i, _i, _i, _i, _i, _f, _vp, _i, _vp, _i, _f, _vp, _i]),
+    "p2_sgemm_st": (None, [_i, _i, _i, _i, _i, _f, _vp, _i, _vp, _i, _f, _vp, _i]),
+    "p2_fv_pack_codes": (_vp, [C.POINTER(FiveValueB), _i, _i]),
+    "p2_sgemm_q8b": (None, [_i, _i, _i, _f, _vp, _i, _vp, _vp, _i, _f, _vp, _i]),
+    "p2_sgemm_fvb": (None, [_i, _i, _i, _f, _vp, _i, C.POINTER(FiveValueB), _f, _vp, _i]),
+    "p2_gemm_mode": (C.c_char_p, []),
+    "p2_gemm_exact": (_i, []),
+    "p2_quant_prepare": (_i, [C.POINTER(QuantA), _i, _i]),
+    "p2_quant_row": (None, [C.POINTER(QuantA), _i, _vp]),
+    "p2_sgemm_fvb_q8a": (None, [_i, _i, _i, _f, C.POINTER(QuantA), C.POINTER(FiveValueB), _f, _vp, _i]),
+    "p2_sgemm_q8b_q8a": (None, [_i, _i, _i, _f, C.POINTER(QuantA), _vp, _vp, _i, _f, _vp, _i]),
+    "p2_b200_set_device": (_i, [_i]),
+    "p2_b200_release_weights": (None, []),
 }
+
+P2_NO_TRANS, P2_TRANS = 111, 112
 
 
 def lib() -> C.CDLL:
@@ -92,8 +110,14 @@ def five_value_struct(signs: int, flags: int, lo: int, hi: int, K: int, N: int, 
     return P2cuFiveValue(signs, flags, lo, hi, codes, K, N)
 
 
-def workspace_bytes(M: int, K: int, mode: int) -> int:
-    return int(lib().p2cu_gemm_workspace_bytes(M, K, mode))
+def workspace_bytes(M: int, N: int, K: int, mode: int) -> int:
+    """Workspace of sgemm_fvb / sgemm_q8b (quantised activations plus K-block slices)."""
+    return int(lib().p2cu_gemm_workspace_bytes(M, N, K, mode))
+
+
+def q8a_workspace_bytes(M: int, N: int, K: int) -> int:
+    """Workspace of sgemm_fvb_q8a / sgemm_q8b_q8a (K-block slices when K > 1024)."""
+    return int(lib().p2cu_q8a_workspace_bytes(M, N, K))
 
 
 def stream_ptr(stream) -> int | None:
@@ -112,8 +136,10 @@ def sgemm_fvb(M, N, K, alpha, A, lda, B: P2cuFiveValue, mode, beta, Cp, ldc, wor
                                stream_ptr(stream)))
 
 
-def sgemm_fvb_q8a(M, N, K, alpha, q, a_scales, B: P2cuFiveValue, mode, beta, Cp, ldc, stream=None):
-    check(lib().p2cu_sgemm_fvb_q8a(M, N, K, alpha, q, a_scales, C.byref(B), mode, beta, Cp, ldc, stream_ptr(stream)))
+def sgemm_fvb_q8a(M, N, K, alpha, q, a_scales, B: P2cuFiveValue, mode, beta, Cp, ldc, workspace=None, ws_bytes=0,
+                  stream=None):
+    check(lib().p2cu_sgemm_fvb_q8a(M, N, K, alpha, q, a_scales, C.byref(B), mode, beta, Cp, ldc, workspace, ws_bytes,
+                                   stream_ptr(stream)))
 
 
 def sgemm_q8b(M, N, K, alpha, A, lda, B, scales, ldb, mode, beta, Cp, ldc, workspace, ws_bytes, stream=None):
@@ -121,8 +147,10 @@ def sgemm_q8b(M, N, K, alpha, A, lda, B, scales, ldb, mode, beta, Cp, ldc, works
                                stream_ptr(stream)))
 
 
-def sgemm_q8b_q8a(M, N, K, alpha, q, a_scales, B, scales, ldb, beta, Cp, ldc, stream=None):
-    check(lib().p2cu_sgemm_q8b_q8a(M, N, K, alpha, q, a_scales, B, scales, ldb, beta, Cp, ldc, stream_ptr(stream)))
+def sgemm_q8b_q8a(M, N, K, alpha, q, a_scales, B, scales, ldb, beta, Cp, ldc, workspace=None, ws_bytes=0,
+                  stream=None):
+    check(lib().p2cu_sgemm_q8b_q8a(M, N, K, alpha, q, a_scales, B, scales, ldb, beta, Cp, ldc, workspace, ws_bytes,
+                                   stream_ptr(stream)))
 
 
 def sgemm(transA, transB, M, N, K, alpha, A, lda, B, ldb, beta, Cp, ldc, stream=None):
@@ -136,3 +164,39 @@ def fv_pack_codes(B: P2cuFiveValue, codes: int, stream=None) -> None:
 
 def check_device(stream=None) -> None:
     check(lib().p2cu_check_device(stream_ptr(stream)))
+
+
+# ---- the reference's host-pointer ABI (include/blas.h), on numpy arrays -------------------------------------------
+
+def _addr(a) -> int:
+    return a.ctypes.data
+
+
+def host_five_value(w: dict, codes: int | None = None) -> FiveValueB:
+    """A FiveValueB over host arrays in synth.five_value layout (the arrays must outlive every call using it)."""
+    return FiveValueB(_addr(w["signs"]), _addr(w["flags"]), _addr(w["lo"]), _addr(w["hi"]), codes)
+
+
+def host_sgemm_fvb(A, w: dict, out, alpha=1.0, beta=0.0, fvb: FiveValueB | None = None):
+    """p2_sgemm_fvb on host arrays, in place on `out` (float32 [M, N])."""
+    M, K = A.shape
+    N = out.shape[1]
+    b = fvb if fvb is not None else host_five_value(w)
+    lib().p2_sgemm_fvb(M, N, K, alpha, _addr(A), A.strides[0] // 4, C.byref(b), beta, _addr(out), out.strides[0] // 4)
+    return out
+
+
+def host_sgemm_q8b(A, t: dict, out, alpha=1.0, beta=0.0):
+    M, K = A.shape
+    N = out.shape[1]
+    lib().p2_sgemm_q8b(M, N, K, alpha, _addr(A), A.strides[0] // 4, _addr(t["q8"]), _addr(t["scales"]),
+                       t["q8"].strides[0], beta, _addr(out), out.strides[0] // 4)
+    return out
+
+
+def host_sgemm(transA, transB, A, B, out, alpha=1.0, beta=0.0):
+    M, N = out.shape
+    K = A.shape[0] if transA else A.shape[1]
+    lib().p2_sgemm(P2_TRANS if transA else P2_NO_TRANS, P2_TRANS if transB else P2_NO_TRANS, M, N, K, alpha,
+                   _addr(A), A.strides[0] // 4, _addr(B), B.strides[0] // 4, beta, _addr(out), out.strides[0] // 4)
+    return out

@@ -3,6 +3,7 @@
 #include <cstdint>
 #include <cstdio>
 #include <cstring>
+#include <cstdlib>
 #include <mutex>
 #include <cuda.h>
 #include <cuda_runtime.h>
@@ -45,6 +46,16 @@ uint32_t* dev_err_ptr() {
     return ptrs[dev];
 }
 
+#ifdef P2CU_TRACE
+// Diagnostic builds: pipeline timestamps of one CTA per GEMM launch (see fv_gemm.cu).
+__device__ long long g_trace[512];
+long long* trace_ptr() {
+    void* p = nullptr;
+    cudaGetSymbolAddress(&p, g_trace);
+    return static_cast<long long*>(p);
+}
+#endif
+
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no link-time dependency on libcuda).
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -63,9 +74,10 @@ EncodeTiledFn encode_fn() {
     return fn;
 }
 
-// A 2-D uint8 tensor map: `inner` bytes per row, `outer` rows, rows `stride` bytes apart, boxes box_in x box_out.
-int make_map(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t stride, uint32_t box_in,
-             uint32_t box_out, bool swizzle128, const char* what) {
+// A 2-D tensor map: `inner` elements per row of `esize` bytes, `outer` rows `stride` bytes apart, boxes box_in x
+// box_out elements, swizzle 0 / 64 / 128 (bytes).
+int make_map(CUtensorMap* map, const void* base, int esize, uint64_t inner, uint64_t outer, uint64_t stride,
+             uint32_t box_in, uint32_t box_out, int swizzle, const char* what) {
     EncodeTiledFn enc = encode_fn();
     if (!enc) return fail(P2CU_ECUDA, "cuTensorMapEncodeTiled is not available from the driver");
     if (reinterpret_cast<uintptr_t>(base) % 16) return fail(P2CU_EINVAL, "%s: base address not 16-byte aligned", what);
@@ -75,9 +87,10 @@ int make_map(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
     const cuuint64_t strides[1] = {stride};
     const cuuint32_t box[2] = {box_in, box_out};
     const cuuint32_t estr[2] = {1, 1};
-    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
-                     CU_TENSOR_MAP_INTERLEAVE_NONE,
-                     swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+    const CUtensorMapSwizzle sw = swizzle == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                                : swizzle == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_NONE;
+    CUresult r = enc(map, esize == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_UINT8, 2,
+                     const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(P2CU_ECUDA, "%s: cuTensorMapEncodeTiled failed (%d)", what, static_cast<int>(r));
     return P2CU_OK;
@@ -111,10 +124,35 @@ int check_gemm_common(int M, int N, int K, const void* C, int ldc, const char* w
     return P2CU_OK;
 }
 
+// Tile width for the tensor-core GEMM: the widest tile (128 for the two int8-mode planes, else 256) that still gives
+// about half the SMs a CTA, else 64. P2CU_TILE_N=64|128|256 forces one (where the operand kind allows it).
+int choose_bn(int M, int N, int nblk, int kind) {
+    static int forced = -1;
+    if (forced < 0) {
+        const char* e = getenv("P2CU_TILE_N");
+        const int v = e ? atoi(e) : 0;
+        forced = (v == 64 || v == 128 || v == 256) ? v : 0;
+    }
+    const int widest = kind == p2cu::KIND_ST ? 128 : 256;
+    if (forced) return forced > widest ? widest : forced;
+    const long mt = (M + 127) / 128;
+    for (int bn = widest; bn > 64; bn /= 2)
+        if (N % bn == 0 && static_cast<long>(N / bn) * mt * nblk >= 74) return bn;
+    return 64;
+}
+
+size_t split_bytes(int M, int N, int K) {
+    const int nblk = (K + 1023) / 1024;
+    if (nblk <= 1) return 0;
+    const size_t m_pad = (static_cast<size_t>(M) + 127) / 128 * 128;
+    return round256(static_cast<size_t>(nblk) * m_pad * N * sizeof(float));
+}
+
 // The tcgen05 GEMM on quantised rows. `B` five-value (planes or cached codes) or `q8`/`scales` an int8 table.
+// `ws` holds the per-block slices when K > 1024 (split_bytes).
 int run_i8(int M, int N, int K, float alpha, const int8_t* q, const float* a_scales, const P2cuFiveValue* B,
-           const int8_t* q8, const float* scales, int ldb, int mode, float beta, float* C, int ldc, cudaStream_t s,
-           const char* who) {
+           const int8_t* q8, const float* scales, int ldb, int mode, float beta, float* C, int ldc, void* ws,
+           size_t ws_bytes, cudaStream_t s, const char* who) {
     int rc = check_gemm_common(M, N, K, C, ldc, who);
     if (rc) return rc;
     if (N % 16) return fail(P2CU_EINVAL, "%s: N = %d is not a multiple of 16", who, N);
@@ -124,6 +162,11 @@ int run_i8(int M, int N, int K, float alpha, const int8_t* q, const float* a_sca
     if (K % 16) return fail(P2CU_EUNSUPPORTED, "%s: K = %d: the tensor-core path needs K %% 16 == 0", who, K);
     if (!q || !a_scales) return fail(P2CU_EINVAL, "%s: quantised A is NULL", who);
     if (!aligned16(C) || ldc % 4) return fail(P2CU_EINVAL, "%s: C must be 16-byte aligned with ldc %% 4 == 0", who);
+    const int nblk = (K + 1023) / 1024;
+    const size_t need = split_bytes(M, N, K);
+    if (need && (!ws || ws_bytes < need || !aligned16(ws)))
+        return fail(P2CU_EINVAL, "%s: K = %d needs %zu bytes of 16-byte aligned workspace, %zu given", who, K, need,
+                    ws ? ws_bytes : 0);
     if (beta != 0.f && beta != 1.f) {
         if ((rc = scale_c(C, M, N, ldc, beta, s))) return rc;
         beta = 1.f;
@@ -131,43 +174,50 @@ int run_i8(int M, int N, int K, float alpha, const int8_t* q, const float* a_sca
     p2cu::FvGemmParams p{};
     p.M = M; p.N = N; p.K = K; p.alpha = alpha; p.beta_zero = beta == 0.f;
     p.a_scales = a_scales; p.C = C; p.ldc = ldc; p.err = dev_err_ptr();
-    CUtensorMap ta, tb0, tb1;
-    if ((rc = make_map(&ta, q, static_cast<uint64_t>(K), static_cast<uint64_t>(M), static_cast<uint64_t>(K), 128, 128,
-                       true, "A")))
-        return rc;
-    cudaError_t e;
+    p.ksplit = nblk;
+    p.m_pad = (M + 127) / 128 * 128;
+#ifdef P2CU_TRACE
+    p.trace = trace_ptr();
+#endif
+    const bool planes = B && !(mode == P2CU_INT8W && B->codes);
+    const int kind = !planes ? p2cu::KIND_TABLE : mode == P2CU_INT8W ? p2cu::KIND_CODES : p2cu::KIND_ST;
+    const int bn = choose_bn(M, N, nblk, kind);
+    const int atom = bn > 128 ? 128 : bn;   // an int8 table is loaded in boxes one swizzle atom wide
+    CUtensorMap ta, tb0, tb1, tout;
+    if ((rc = make_map(&ta, q, 1, K, M, K, 128, 128, 128, "A"))) return rc;
+    if (nblk > 1)
+        rc = make_map(&tout, ws, 4, N, static_cast<uint64_t>(nblk) * p.m_pad, static_cast<uint64_t>(N) * 4, 32, 128,
+                      128, "workspace");
+    else
+        rc = make_map(&tout, C, 4, N, M, static_cast<uint64_t>(ldc) * 4, 32, 128, 128, "C");
+    if (rc) return rc;
     if (B) {
         if (!B->lo || !B->hi) return fail(P2CU_EINVAL, "%s: lo / hi are NULL", who);
         if (B->K != K || B->N != N) return fail(P2CU_EINVAL, "%s: weight is [%d, %d], GEMM wants [%d, %d]", who, B->K,
                                                 B->N, K, N);
         p.lo = B->lo; p.hi = B->hi;
-        if (mode == P2CU_INT8W && B->codes) {
-            p.cmode = p2cu::CM_INT8W;   // one plane of codes, f = (float)acc * (hi / 127)
-            if ((rc = make_map(&tb0, B->codes, static_cast<uint64_t>(N), static_cast<uint64_t>(K),
-                               static_cast<uint64_t>(N), 128, 128, true, "codes")))
-                return rc;
-            e = p2cu::fv_gemm_launch_table(ta, tb0, p, s);
+        p.cmode = mode == P2CU_INT8W ? p2cu::CM_INT8W : p2cu::CM_INT8;
+        if (!planes) {   // int8w from the cached codes: one plane, f = (float)acc * (hi / 127)
+            if ((rc = make_map(&tb0, B->codes, 1, N, K, N, atom, 128, atom, "codes"))) return rc;
+            tb1 = tb0;
         } else {
             if (!B->signs || !B->flags) return fail(P2CU_EINVAL, "%s: planes are NULL", who);
-            p.cmode = mode == P2CU_INT8W ? p2cu::CM_INT8W : p2cu::CM_INT8;
-            if ((rc = make_map(&tb0, B->signs, static_cast<uint64_t>(N / 4), static_cast<uint64_t>(K),
-                               static_cast<uint64_t>(N / 4), 32, 128, false, "signs")))
+            if ((rc = make_map(&tb0, B->signs, 1, N / 4, K, N / 4, bn / 4, 128, 0, "signs"))) return rc;
+            if ((rc = make_map(&tb1, B->flags, 1, N / 8, K, N / 8, bn / 8 < 16 ? 16 : bn / 8, 128, 0, "flags")))
                 return rc;
-            if ((rc = make_map(&tb1, B->flags, static_cast<uint64_t>(N / 8), static_cast<uint64_t>(K),
-                               static_cast<uint64_t>(N / 8), 16, 128, false, "flags")))
-                return rc;
-            e = p2cu::fv_gemm_launch_planes(ta, tb0, tb1, p, s);
         }
     } else {
         if (!q8 || !scales) return fail(P2CU_EINVAL, "%s: int8 table is NULL", who);
         if (ldb < N) return fail(P2CU_EINVAL, "%s: ldb=%d < N=%d", who, ldb, N);
         p.cmode = p2cu::CM_Q8B;
         p.scales = scales;
-        if ((rc = make_map(&tb0, q8, static_cast<uint64_t>(N), static_cast<uint64_t>(K), static_cast<uint64_t>(ldb),
-                           128, 128, true, "B")))
-            return rc;
-        e = p2cu::fv_gemm_launch_table(ta, tb0, p, s);
+        if ((rc = make_map(&tb0, q8, 1, N, K, ldb, atom, 128, atom, "B"))) return rc;
+        tb1 = tb0;
     }
+    cudaError_t e = p2cu::fv_gemm_launch(bn, kind, ta, tb0, tb1, tout, p, s);
+    if (e == cudaSuccess && nblk > 1)
+        e = p2cu::fv_combine_launch(static_cast<const float*>(ws), p.m_pad, nblk, a_scales, alpha, p.beta_zero, C, M,
+                                    N, ldc, s);
     return e == cudaSuccess ? P2CU_OK : cuda_fail(e, who);
 }
 
@@ -208,6 +258,12 @@ int run_exact(int M, int N, int K, float alpha, const float* A, int lda, int tra
 
 extern "C" {
 
+#ifdef P2CU_TRACE
+__attribute__((visibility("default"))) int p2cu_debug_trace(long long* out, int n) {
+    return cudaMemcpyFromSymbol(out, g_trace, sizeof(long long) * (n < 512 ? n : 512)) == cudaSuccess ? 0 : -1;
+}
+#endif
+
 const char* p2cu_last_error(void) { return g_msg; }
 
 int p2cu_check_device(void* stream) {
@@ -233,34 +289,45 @@ int p2cu_quant_rows(const float* A, int M, int K, int lda, signed char* q, float
 }
 
 int p2cu_sgemm_fvb_q8a(int M, int N, int K, float alpha, const signed char* q, const float* a_scales,
-                       const P2cuFiveValue* B, int mode, float beta, float* C, int ldc, void* stream) {
+                       const P2cuFiveValue* B, int mode, float beta, float* C, int ldc, void* workspace,
+                       size_t workspace_bytes, void* stream) {
     if (!B) return fail(P2CU_EINVAL, "p2cu_sgemm_fvb_q8a: B is NULL");
     if (mode != P2CU_INT8 && mode != P2CU_INT8W) return fail(P2CU_EINVAL, "p2cu_sgemm_fvb_q8a: mode %d", mode);
     return run_i8(M, N, K, alpha, reinterpret_cast<const int8_t*>(q), a_scales, B, nullptr, nullptr, 0, mode, beta,
-                  C, ldc, static_cast<cudaStream_t>(stream), "p2cu_sgemm_fvb_q8a");
+                  C, ldc, workspace, workspace_bytes, static_cast<cudaStream_t>(stream), "p2cu_sgemm_fvb_q8a");
 }
 
 int p2cu_sgemm_q8b_q8a(int M, int N, int K, float alpha, const signed char* q, const float* a_scales,
                        const signed char* B, const float* scales, int ldb, float beta, float* C, int ldc,
-                       void* stream) {
+                       void* workspace, size_t workspace_bytes, void* stream) {
     return run_i8(M, N, K, alpha, reinterpret_cast<const int8_t*>(q), a_scales, nullptr,
-                  reinterpret_cast<const int8_t*>(B), scales, ldb, P2CU_INT8, beta, C, ldc,
-                  static_cast<cudaStream_t>(stream), "p2cu_sgemm_q8b_q8a");
+                  reinterpret_cast<const int8_t*>(B), scales, ldb, P2CU_INT8, beta, C, ldc, workspace,
+                  workspace_bytes, static_cast<cudaStream_t>(stream), "p2cu_sgemm_q8b_q8a");
 }
 
-size_t p2cu_gemm_workspace_bytes(int M, int K, int mode) {
-    if (mode == P2CU_EXACT || M <= 0 || K <= 0) return 0;
-    return round256(static_cast<size_t>(M) * K) + round256(static_cast<size_t>(M) * sizeof(float));
+size_t p2cu_q8a_workspace_bytes(int M, int N, int K) {
+    if (M <= 0 || N <= 0 || K <= 0) return 0;
+    return split_bytes(M, N, K);
 }
 
-static int quantise_into(const float* A, int M, int K, int lda, void* ws, size_t ws_bytes, int8_t** q, float** sc,
-                         cudaStream_t s, const char* who) {
-    const size_t need = p2cu_gemm_workspace_bytes(M, K, P2CU_INT8);
+size_t p2cu_gemm_workspace_bytes(int M, int N, int K, int mode) {
+    if (mode == P2CU_EXACT || M <= 0 || K <= 0 || N <= 0) return 0;
+    return round256(static_cast<size_t>(M) * K) + round256(static_cast<size_t>(M) * sizeof(float)) +
+           split_bytes(M, N, K);
+}
+
+// Quantise A into the head of the workspace; the rest (if any) is handed to the GEMM for its K-block slices.
+static int quantise_into(const float* A, int M, int N, int K, int lda, void* ws, size_t ws_bytes, int8_t** q,
+                         float** sc, void** rest, size_t* rest_bytes, cudaStream_t s, const char* who) {
+    const size_t need = p2cu_gemm_workspace_bytes(M, N, K, P2CU_INT8);
     if (!ws || ws_bytes < need) return fail(P2CU_EINVAL, "%s: workspace of %zu bytes, %zu needed", who, ws_bytes, need);
     if (!aligned16(ws)) return fail(P2CU_EINVAL, "%s: workspace not 16-byte aligned", who);
     if (!A) return fail(P2CU_EINVAL, "%s: A is NULL", who);
+    const size_t head = round256(static_cast<size_t>(M) * K) + round256(static_cast<size_t>(M) * sizeof(float));
     *q = static_cast<int8_t*>(ws);
     *sc = reinterpret_cast<float*>(static_cast<char*>(ws) + round256(static_cast<size_t>(M) * K));
+    *rest = static_cast<char*>(ws) + head;
+    *rest_bytes = ws_bytes - head;
     cudaError_t e = p2cu::quant_rows_launch(A, M, K, lda, *q, *sc, s);
     return e == cudaSuccess ? P2CU_OK : cuda_fail(e, who);
 }
@@ -276,11 +343,16 @@ int p2cu_sgemm_fvb(int M, int N, int K, float alpha, const float* A, int lda, co
     int rc = check_gemm_common(M, N, K, C, ldc, "p2cu_sgemm_fvb");
     if (rc) return rc;
     if (M == 0 || N == 0) return P2CU_OK;
-    if (alpha == 0.f) return scale_c(C, M, N, ldc, beta, s);
+    if (alpha == 0.f || K == 0) return scale_c(C, M, N, ldc, beta, s);
     int8_t* q;
     float* sc;
-    if ((rc = quantise_into(A, M, K, lda, workspace, workspace_bytes, &q, &sc, s, "p2cu_sgemm_fvb"))) return rc;
-    return run_i8(M, N, K, alpha, q, sc, B, nullptr, nullptr, 0, mode, beta, C, ldc, s, "p2cu_sgemm_fvb");
+    void* rest;
+    size_t rest_bytes;
+    if ((rc = quantise_into(A, M, N, K, lda, workspace, workspace_bytes, &q, &sc, &rest, &rest_bytes, s,
+                            "p2cu_sgemm_fvb")))
+        return rc;
+    return run_i8(M, N, K, alpha, q, sc, B, nullptr, nullptr, 0, mode, beta, C, ldc, rest, rest_bytes, s,
+                  "p2cu_sgemm_fvb");
 }
 
 int p2cu_sgemm_q8b(int M, int N, int K, float alpha, const float* A, int lda, const signed char* B,
@@ -293,12 +365,16 @@ int p2cu_sgemm_q8b(int M, int N, int K, float alpha, const float* A, int lda, co
     int rc = check_gemm_common(M, N, K, C, ldc, "p2cu_sgemm_q8b");
     if (rc) return rc;
     if (M == 0 || N == 0) return P2CU_OK;
-    if (alpha == 0.f) return scale_c(C, M, N, ldc, beta, s);
+    if (alpha == 0.f || K == 0) return scale_c(C, M, N, ldc, beta, s);
     int8_t* q;
     float* sc;
-    if ((rc = quantise_into(A, M, K, lda, workspace, workspace_bytes, &q, &sc, s, "p2cu_sgemm_q8b"))) return rc;
+    void* rest;
+    size_t rest_bytes;
+    if ((rc = quantise_into(A, M, N, K, lda, workspace, workspace_bytes, &q, &sc, &rest, &rest_bytes, s,
+                            "p2cu_sgemm_q8b")))
+        return rc;
     return run_i8(M, N, K, alpha, q, sc, nullptr, reinterpret_cast<const int8_t*>(B), scales, ldb, P2CU_INT8, beta, C,
-                  ldc, s, "p2cu_sgemm_q8b");
+                  ldc, rest, rest_bytes, s, "p2cu_sgemm_q8b");
 }
 
 int p2cu_sgemm(int transA, int transB, int M, int N, int K, float alpha, const float* A, int lda, const float* B,

@@ -1,26 +1,32 @@
-// fv_gemm.cu - the five-value int8 GEMM on sm_100a tensor cores (tcgen05, TMEM accumulators, TMA operand loads).
+// fv_gemm.cu - the five-value int8 GEMM on sm_100a tensor cores (tcgen05, TMEM accumulators, TMA operand loads and
+// result stores).
 //
-// C[M, N] = alpha * A * B + beta * C with A int8 [M, K] (one fp32 scale per row, produced by a quantising kernel)
-// and B one of
-//   * a five-value weight as stored by phonon-2-c: 2-bit sign plane [K, N/4] + 1-bit magnitude plane [K, N/8] and
-//     per-column lo / hi (csrc/blas.h:38-45). The planes are streamed by TMA into shared memory and expanded there
-//     into two int8 planes, S = sign and T = sign * flag, which feed two MMAs into two TMEM accumulators.
-//       int8  mode (csrc/blas.c:1329-1333, 1362): f = fma((float)accT, hi - lo, (float)accS * lo)
-//       int8w mode (csrc/blas.c:1319-1328, 1222-1240): the reference multiplies by the one code plane
-//         code = sign * (flag ? 127 : clo), clo = round(127 lo / hi); its int32 sum equals, exactly,
-//         clo * accS + (127 - clo) * accT, which is what the epilogue forms before f = (float)acc * (hi / 127).
-//   * a plain int8 table [K, N] with one fp32 scale per column (the int8-table weights, csrc/blas.c:1243-1254, and
-//     the pre-expanded int8w codes of the code cache): loaded by TMA straight into the MMA layout, one MMA.
-// The int32 sums restart every 1024 rows of K, and the fp32 epilogue runs per 1024-row block in the reference order
+// C[M, N] = alpha * A * B + beta * C with A int8 [M, K] (one fp32 scale per row, from a quantising kernel) and B one
+// of three operand kinds:
+//   KIND_CODES  five-value planes as phonon-2-c stores them (2-bit sign plane [K, N/4], 1-bit magnitude plane
+//               [K, N/8], per-column lo / hi; csrc/blas.h:38-45), streamed by TMA and expanded in shared memory into
+//               the int8w code plane sign * (flag ? 127 : clo), clo = round(127 lo / hi) (csrc/blas.c:1222-1240,
+//               1316-1328); f = (float)acc * (hi * (1 / 127)).
+//   KIND_ST     the same planes expanded into the two int8 planes of the int8 mode, S = sign and T = sign * flag,
+//               multiplied by one MMA over [S | T] into adjacent TMEM columns (csrc/blas.c:1190-1220, 1329-1362):
+//               f = fma((float)accT, hi - lo, (float)accS * lo).
+//   KIND_TABLE  an int8 table [K, N] with one fp32 scale per column (the int8-table weights, csrc/blas.c:1243-1254,
+//               and the cached int8w codes), loaded by TMA straight into the operand layout.
+// The reference restarts its int32 sums every 1024 rows of K and rescales per block into C in block order
 // (csrc/blas.c:1339-1366): C = (beta == 0 && first block) ? f * as : fma(f, as, C), as = a_scale[m] * alpha.
+// Here one CTA owns exactly one 1024-row block of one 128 x BN output tile:
+//   * K <= 1024: the CTA finishes the tile: C = f * as or fma(f, as, C_old);
+//   * K > 1024: CTA z writes its block's f to a workspace slice, and fv_combine_kernel folds the slices into C in
+//     block order afterwards, which is the reference's arithmetic bit for bit.
+// Output chunks (128 rows x 32 columns) are staged in shared memory (128-byte swizzle) and written by TMA stores as
+// soon as each is ready; C_old comes in by TMA.
 //
-// Tile: 128 rows (one TMEM lane per row) x 128 columns per CTA, K staged 128 at a time. Roles:
-//   warps 0-3  epilogue (TMEM -> registers -> rescale -> C), one row per thread
-//   warps 4-7  expand the sign / flag planes into the S and T operand tiles (planes mode only)
-//   warp  8    TMA producer
-//   warp  9    TMEM allocation and MMA issue (one elected lane)
-// Accumulators are double-buffered in TMEM so that the epilogue of one 1024-row block overlaps the next block's MMAs.
+// Roles (warps): epilogue groups of four warps (one TMEM lane quarter each); with planes, groups 1 and 2 expand the
+// planes during the main loop; then the TMA producer and the MMA issuer (one elected lane, also the TMEM owner).
+// Launched with programmatic dependent launch: the set-up overlaps the previous kernel's tail, and nothing that
+// kernel writes is read before griddepcontrol.wait.
 #include <cstdint>
+#include <utility>
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include "ptx.cuh"
@@ -28,53 +34,149 @@
 
 namespace p2cu {
 
-constexpr int BM = 128, BN = 128, BK = 128, KBLK = 1024;
-constexpr int NTHREADS = 320;
-constexpr uint32_t A_BYTES = BM * BK;            // int8 A tile, K-major, 128-byte swizzle
-constexpr uint32_t B_BYTES = BK * BN;            // int8 B tile, MN-major, 128-byte swizzle
-constexpr uint32_t SG_BYTES = BK * (BN / 4);     // sign-plane tile
-constexpr uint32_t FL_BYTES = BK * (BN / 8);     // flag-plane tile
+// Diagnostic builds (-DP2CU_TRACE) record clock64() at pipeline events of CTA (0, 0, 0) into p.trace[slot].
+#ifdef P2CU_TRACE
+#define TRACE(slot) do { if (p.trace && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0) \
+                             p.trace[(slot)] = clock64(); } while (0)
+#else
+#define TRACE(slot) do { } while (0)
+#endif
+// Trace slots: 0 start, 1 after set-up, 8+kb producer issue, 80+kb MMA ready, 160+kb expansion done (first
+// expander thread), 240 accumulator ready, 241 first chunk staged, 242 all chunks staged, 250 stores read, 260 end.
 
-template <bool PLANES> struct Cfg {
-    static constexpr int STAGES = PLANES ? 3 : 4;
-    static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES * (PLANES ? 2 : 1) + (PLANES ? SG_BYTES + FL_BYTES : 0);
+constexpr int BM = 128, BK = 128, KBLK = 1024;
+
+template <int BN_, int KIND_> struct Cfg {
+    static constexpr int BN = BN_;                                 // output columns per CTA
+    static constexpr int KIND = KIND_;
+    static constexpr bool PLANES = KIND != KIND_TABLE;             // B arrives as sign / magnitude planes
+    static constexpr bool ST = KIND == KIND_ST;
+    // B operand of the single MMA per K step: [S | T] (2 BN columns) or one plane of BN columns, MN-major, in atom
+    // columns ATOM_W bytes wide (an atom = 8 K rows of ATOM_W bytes, swizzled).
+    static constexpr int MMA_N = ST ? 2 * BN : BN;
+    static constexpr int ATOM_W = ST ? BN : (BN < 128 ? BN : 128);
+    static constexpr int N_ATOMS = MMA_N / ATOM_W;
+    static constexpr uint32_t REGION = BK * ATOM_W;               // bytes of one atom column = the leading offset
+    static constexpr uint32_t B_SWZ = ATOM_W == 128 ? SWZ_128B : SWZ_64B;
+    static constexpr uint32_t SBO = 8 * ATOM_W;                    // 8-row K groups
+    static constexpr int EPI_GROUPS = PLANES ? 3 : 2;
+    static constexpr int NEXP = PLANES ? 8 : 0;                    // expander warps (= epilogue groups 1 and 2)
+    static constexpr int PROD = 4 * EPI_GROUPS, MMAW = PROD + 1;
+    static constexpr int NTHREADS = (MMAW + 1) * 32;
+    static constexpr uint32_t A_BYTES = BM * BK;                   // int8 A tile, K-major, 128-byte swizzle
+    static constexpr uint32_t B_BYTES = BK * MMA_N;                // the MMA's B operand
+    static constexpr uint32_t SG_BYTES = BK * (BN / 4);            // sign-plane tile
+    static constexpr uint32_t FL_ROW = BN / 8 < 16 ? 16 : BN / 8;  // a TMA box row is at least 16 bytes
+    static constexpr uint32_t FL_BYTES = BK * FL_ROW;              // flag-plane tile
+    static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES + (PLANES ? SG_BYTES + FL_BYTES : 0);
     static constexpr uint32_t TX_BYTES = A_BYTES + (PLANES ? SG_BYTES + FL_BYTES : B_BYTES);
-    static constexpr uint32_t ACC_COLS = PLANES ? 2 * BN : BN;   // S | T, or the single plane
-    static constexpr uint32_t TMEM_COLS = 2 * ACC_COLS;          // two accumulator buffers
-    static constexpr uint32_t BAR_BYTES = 1024;                  // barriers, flags, per-column constants
-    static constexpr uint32_t CONST_BYTES = 3 * BN * 4;
-    static constexpr uint32_t SMEM_BYTES = 1024 /*alignment slack*/ + STAGES * STAGE_BYTES + BAR_BYTES + CONST_BYTES;
+    static constexpr int STAGES = (200 * 1024) / STAGE_BYTES > 6 ? 6 : (200 * 1024) / STAGE_BYTES;
+    static constexpr uint32_t TMEM_COLS = MMA_N <= 32 ? 32 : MMA_N <= 64 ? 64 : MMA_N <= 128 ? 128 : 256;
+    static constexpr int CHUNKS = BN / 32;                         // 32-column output chunks
+    static constexpr uint32_t OUT_BYTES = BM * BN * 4;             // fp32 output tile, aliases the stage buffers
+    static constexpr uint32_t BAR_BYTES = 512;
+    static constexpr uint32_t CONST_BYTES = 2 * BN * 4;
+    static constexpr uint32_t SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + BAR_BYTES + CONST_BYTES;
+    static_assert(MMA_N <= 256 && MMA_N % 16 == 0, "MMA N");
+    static_assert(ATOM_W == 64 || ATOM_W == 128, "atom width");
+    static_assert(STAGES >= 2, "pipeline depth");
+    static_assert(OUT_BYTES <= STAGES * STAGE_BYTES, "the output tile must fit in the stage buffers");
 };
 
-// Expand 32 columns of one K row: x0, x1 = the 8 sign bytes of the columns, fw = their 32 flag bits.
-// Output word j holds, at byte p, the operand for column 8p + j of the group (a 4 x 8 transpose of the natural order
-// that keeps the expansion to shifts and masks); the epilogue undoes it with compile-time register indexing.
-__device__ __forceinline__ void expand32(uint32_t x0, uint32_t x1, uint32_t fw, uint32_t (&S)[8], uint32_t (&T)[8]) {
-    const uint32_t u = __byte_perm(x0, x1, 0x6420);   // sign bytes of columns 0-3, 8-11, 16-19, 24-27
-    const uint32_t v = __byte_perm(x0, x1, 0x7531);   // sign bytes of columns 4-7, 12-15, 20-23, 28-31
+// Byte masks from bits: byte p of the result is 0xFF when bit 7 of byte p of x is set. PTX prmt with the selector's
+// sign bit set replicates the selected byte's top bit (the __byte_perm intrinsic only uses the low three bits).
+__device__ __forceinline__ uint32_t msb_mask(uint32_t x) {
+    uint32_t r;
+    asm("prmt.b32 %0, %1, 0, 0xBA98;" : "=r"(r) : "r"(x));
+    return r;
+}
+
+// The planes of 32 columns of one K row in "column-transposed" words: word j holds, at byte p, column 8p + j of the
+// group. x0, x1 are the 8 sign bytes of the columns and fw their 32 flag bits; u / v gather the sign bytes of
+// columns 0-3, 8-11, 16-19, 24-27 / 4-7, 12-15, 20-23, 28-31, so for word j the 2-bit code of each column sits at
+// bits 2 (j mod 4), 2 (j mod 4) + 1 of its byte and its flag at bit j of its byte of fw. The epilogue undoes the
+// transposition with compile-time register indexing.
+struct Planes32 {
+    uint32_t u, v, fw;
+    __device__ __forceinline__ void load(uint32_t x0, uint32_t x1, uint32_t f) {
+        u = __byte_perm(x0, x1, 0x6420);
+        v = __byte_perm(x0, x1, 0x7531);
+        fw = f;
+    }
+    // Byte masks of word j: code 2 (+1), code 1 (0), and the magnitude flag.
+    __device__ __forceinline__ void masks(int j, uint32_t& pos, uint32_t& zero, uint32_t& hi) const {
+        const uint32_t src = j < 4 ? u : v;
+        const int b = 2 * (j & 3);
+        pos = msb_mask(src << (6 - b));    // bit b + 1 -> bit 7
+        zero = msb_mask(src << (7 - b));   // bit b -> bit 7
+        hi = msb_mask(fw << (7 - j));      // bit j -> bit 7
+    }
+};
+
+// S = sign (+1 / 0 / -1) and T = sign * flag as int8 bytes.
+__device__ __forceinline__ void expand_st(const Planes32& pl, uint32_t (&S)[8], uint32_t (&T)[8]) {
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-        const uint32_t src = j < 4 ? u : v;
-        const uint32_t code = (src >> (2 * (j & 3))) & 0x03030303u;     // 2-bit codes 0, 1, 2 per byte
-        const uint32_t s = (code + 0x7F7F7F7Fu) ^ 0x80808080u;            // code - 1 per byte: -1, 0, +1
-        const uint32_t f = (fw >> j) & 0x01010101u;                        // magnitude flag per byte
+        uint32_t pos, zero, hi;
+        pl.masks(j, pos, zero, hi);
+        // +1 = 0x01 (pos), 0 = 0x00 (zero), -1 = 0xFF (neither)
+        const uint32_t s = (pos & 0x01010101u) | (~pos & ~zero);
         S[j] = s;
-        T[j] = s & (f * 0xFFu);
+        T[j] = s & hi;
     }
 }
 
-// Byte offset of (row k, 16-byte chunk c) inside an MN-major, 128-byte-swizzled 128 x 128 int8 tile.
-__device__ __forceinline__ uint32_t mn_sw128_offset(int k, int c) {
-    return static_cast<uint32_t>((k >> 3) * 1024 + (k & 7) * 128 + ((c ^ (k & 7)) << 4));
+// The int8w codes sign * (flag ? 127 : clo) with this thread's per-column clo bytes (same word layout).
+__device__ __forceinline__ void expand_codes(const Planes32& pl, const uint32_t (&clo)[8], const uint32_t (&nclo)[8],
+                                             uint32_t (&W)[8]) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        uint32_t pos, zero, hi;
+        pl.masks(j, pos, zero, hi);
+        const uint32_t mag = (hi & 0x7F7F7F7Fu) | (~hi & clo[j]);     // 127 or clo
+        const uint32_t nmag = (hi & 0x81818181u) | (~hi & nclo[j]);   // -127 or -clo
+        W[j] = (mag & pos) | (nmag & ~zero & ~pos);
+    }
 }
 
-template <bool PLANES>
-__global__ void __launch_bounds__(NTHREADS, 1)
+// clo = clamp(rint(127 * lo / hi), 0, 127), 0 when hi <= 0 (csrc/blas.c:1319-1324, IEEE division).
+__device__ __forceinline__ int clo_of(float lo, float hi) {
+    const int c = hi > 0.f ? __float2int_rn(__fdiv_rn(__fmul_rn(127.0f, lo), hi)) : 0;
+    return c < 0 ? 0 : c > 127 ? 127 : c;
+}
+
+// Byte offset of (row k, 16-byte chunk c) in an MN-major atom column W bytes wide, 8-row swizzle atoms
+// (128-byte mode: chunk ^= k mod 8; 64-byte mode: chunk ^= (k / 2) mod 4 - the address bits 7-8 of the row).
+template <int W>
+__device__ __forceinline__ uint32_t b_offset(int k, int c) {
+    const int swz = W == 128 ? (k & 7) : ((k >> 1) & 3);
+    return static_cast<uint32_t>((k >> 3) * (8 * W) + (k & 7) * W + ((c ^ swz) << 4));
+}
+
+// Byte offset of (row r, float4 chunk j) in a 128-row x 32-float staging tile with 128-byte swizzle.
+__device__ __forceinline__ uint32_t out_offset(int r, int j) {
+    return static_cast<uint32_t>(r * 128 + ((j ^ (r & 7)) << 4));
+}
+
+// Wait for a barrier phase with one polling lane per warp; every lane then acquires the completed phase.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, uint32_t code, uint32_t* err,
+                                          volatile int* abort_flag) {
+    int ok = 1;
+    if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, code, err, abort_flag) ? 1 : 0;
+    ok = __shfl_sync(0xffffffffu, ok, 0);
+    if (ok) mbar_try_wait(smem_u32(bar), parity);   // already complete: acquire for this lane
+    return ok != 0;
+}
+
+template <int BN, int KIND>
+__global__ void __launch_bounds__(Cfg<BN, KIND>::NTHREADS, 1)
 fv_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB0,
-               const __grid_constant__ CUtensorMap tmB1, const FvGemmParams p) {
-    using G = Cfg<PLANES>;
+               const __grid_constant__ CUtensorMap tmB1, const __grid_constant__ CUtensorMap tmOut,
+               const FvGemmParams p) {
+    using G = Cfg<BN, KIND>;
     constexpr int STAGES = G::STAGES;
-    constexpr uint32_t IDESC = idesc_i8(BM, BN, /*A K-major*/ false, /*B MN-major*/ true);
+    constexpr bool PLANES = G::PLANES;
+    constexpr uint32_t IDESC = idesc_i8(BM, G::MMA_N, /*A MN-major*/ false, /*B MN-major*/ true);
 
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -83,76 +185,58 @@ fv_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     uint64_t* bready = full + STAGES;
     uint64_t* empty = bready + STAGES;
     uint64_t* accfull = empty + STAGES;
-    uint64_t* accempty = accfull + 2;
-    uint64_t* drain = accempty + 2;
+    uint64_t* cfull = accfull + 1;
+    uint64_t* drain = cfull + 1;
     uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
     float* cc1 = reinterpret_cast<float*>(bar_region + G::BAR_BYTES);
     float* cc2 = cc1 + BN;
-    int* cclo = reinterpret_cast<int*>(cc2 + BN);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM;
-    const int nk = (p.K + BK - 1) / BK;
-    const int nblk = (p.K + KBLK - 1) / KBLK;
+    const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM, z = blockIdx.z;
+    const int k_begin = z * KBLK;
+    const int k_len = p.K - k_begin < KBLK ? p.K - k_begin : KBLK;
+    const int nk = (k_len + BK - 1) / BK;
+    const bool partial = p.ksplit > 1;   // this CTA writes f for its block to the workspace slice z
 
     auto stage_ptr = [&](int s) { return smem + s * G::STAGE_BYTES; };
     auto a_tile = [&](int s) { return stage_ptr(s); };
-    auto b0_tile = [&](int s) { return stage_ptr(s) + A_BYTES; };
-    auto b1_tile = [&](int s) { return stage_ptr(s) + A_BYTES + B_BYTES; };
-    auto sg_tile = [&](int s) { return stage_ptr(s) + A_BYTES + 2 * B_BYTES; };
-    auto fl_tile = [&](int s) { return stage_ptr(s) + A_BYTES + 2 * B_BYTES + SG_BYTES; };
+    auto b_tile = [&](int s) { return stage_ptr(s) + G::A_BYTES; };
+    auto sg_tile = [&](int s) { return stage_ptr(s) + G::A_BYTES + G::B_BYTES; };
+    auto fl_tile = [&](int s) { return stage_ptr(s) + G::A_BYTES + G::B_BYTES + G::SG_BYTES; };
 
     if (threadIdx.x == 0) {
+        TRACE(0);
         for (int s = 0; s < STAGES; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&bready[s], 128);
+            mbar_init(&bready[s], G::NEXP > 0 ? G::NEXP * 32 : 1);
             mbar_init(&empty[s], 1);
         }
-        for (int b = 0; b < 2; ++b) {
-            mbar_init(&accfull[b], 1);
-            mbar_init(&accempty[b], 128);
-        }
+        mbar_init(accfull, 1);
+        mbar_init(cfull, 1);
         mbar_init(drain, 1);
         *abort_flag = 0;
         fence_barrier_init();
     }
-    if (warp == 8 && lane == 0) {
+    if (warp == G::PROD && lane == 0) {
         tma_prefetch_desc(&tmA);
         tma_prefetch_desc(&tmB0);
         if (PLANES) tma_prefetch_desc(&tmB1);
+        tma_prefetch_desc(&tmOut);
     }
-    if (warp == 9) {
+    if (warp == G::MMAW) {
         tmem_alloc(tmem_holder, G::TMEM_COLS);
         tmem_relinquish();
-    }
-    if (threadIdx.x < BN) {   // per-column epilogue constants
-        const int n = n0 + threadIdx.x;
-        float c1 = 0.f, c2 = 0.f;
-        int clo = 0;
-        if (n < p.N) {
-            if (p.cmode == CM_Q8B) {
-                c1 = p.scales[n];
-            } else if (p.cmode == CM_INT8) {
-                c1 = p.lo[n];
-                c2 = __fsub_rn(p.hi[n], p.lo[n]);
-            } else {   // int8w: c1 = hi * (1 / 127); clo = clamp(rint(127 * lo / hi), 0, 127)
-                const float lo = p.lo[n], hi = p.hi[n];
-                c1 = __fmul_rn(hi, 1.0f / 127.0f);
-                const int c = hi > 0.f ? __float2int_rn(__fdiv_rn(__fmul_rn(127.0f, lo), hi)) : 0;
-                clo = c < 0 ? 0 : c > 127 ? 127 : c;
-            }
-        }
-        cc1[threadIdx.x] = c1;
-        cc2[threadIdx.x] = c2;
-        cclo[threadIdx.x] = clo;
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_holder;
+    if (threadIdx.x == 0) TRACE(1);
+    griddep_launch_dependents();   // the next kernel in the stream may start its set-up
+    griddep_wait();                // everything the previous kernels wrote is visible from here on
 
-    if (warp == 8) {
+    if (warp == G::PROD) {
         // ---------------- TMA producer ----------------
         if (lane == 0) {
             int issued = 0;
@@ -160,167 +244,317 @@ fv_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 const int s = kb % STAGES, r = kb / STAGES;
                 if (!mbar_wait(&empty[s], (r & 1) ^ 1, DEV_TIMEOUT_EMPTY, p.err, abort_flag)) break;
                 issued = kb + 1;
+                TRACE(8 + kb);
                 mbar_arrive_expect_tx(&full[s], G::TX_BYTES);
-                tma_load_2d(a_tile(s), &tmA, &full[s], kb * BK, m0);
+                const int kx = k_begin + kb * BK;
+                tma_load_2d(a_tile(s), &tmA, &full[s], kx, m0);
                 if (PLANES) {
-                    tma_load_2d(sg_tile(s), &tmB0, &full[s], n0 / 4, kb * BK);
-                    tma_load_2d(fl_tile(s), &tmB1, &full[s], n0 / 8, kb * BK);
+                    tma_load_2d(sg_tile(s), &tmB0, &full[s], n0 / 4, kx);
+                    tma_load_2d(fl_tile(s), &tmB1, &full[s], (n0 / 8) & ~15, kx);   // 16-byte aligned box
                 } else {
-                    tma_load_2d(b0_tile(s), &tmB0, &full[s], n0, kb * BK);
+#pragma unroll
+                    for (int a = 0; a < G::N_ATOMS; ++a)
+                        tma_load_2d(b_tile(s) + a * G::REGION, &tmB0, &full[s], n0 + a * G::ATOM_W, kx);
                 }
             }
-            // No copy may still be landing in shared memory when the CTA exits (matters on the abort path only):
-            // wait, bounded, for the last round issued on every stage.
+            // No copy may still be landing in shared memory when the CTA exits (matters on the abort path only).
             for (int kb = issued - STAGES < 0 ? 0 : issued - STAGES; kb < issued; ++kb) {
                 const int s = kb % STAGES, r = kb / STAGES;
                 for (uint32_t i = 0; i < WAIT_LIMIT && !mbar_try_wait(smem_u32(&full[s]), r & 1); ++i) {}
             }
         }
-    } else if (warp == 9) {
+    } else if (warp == G::MMAW) {
         // ---------------- MMA issue ----------------
         if (lane == 0) {
             for (int kb = 0; kb < nk; ++kb) {
                 const int s = kb % STAGES, r = kb / STAGES;
-                const int b = (kb * BK) / KBLK, ab = b & 1;
-                const bool first = (kb * BK) % KBLK == 0;
-                const bool last = ((kb + 1) * BK) % KBLK == 0 || kb == nk - 1;
-                if (first && !mbar_wait(&accempty[ab], ((b >> 1) & 1) ^ 1, DEV_TIMEOUT_ACC, p.err, abort_flag)) break;
                 if (!mbar_wait(PLANES ? &bready[s] : &full[s], r & 1, DEV_TIMEOUT_READY, p.err, abort_flag)) break;
                 tc_fence_after();
+                TRACE(80 + kb);
                 const uint32_t a_base = smem_u32(a_tile(s));
-                const uint32_t b0_base = smem_u32(b0_tile(s)), b1_base = smem_u32(b1_tile(s));
-                const uint32_t d = tmem + ab * G::ACC_COLS;
+                const uint32_t b_base = smem_u32(b_tile(s));
 #pragma unroll
                 for (int ks = 0; ks < BK / 32; ++ks) {
-                    // A: K-major rows of 128 bytes, 8-row groups 1024 bytes apart; a K step of 32 advances 32 bytes
-                    // inside the swizzle atom. B: MN-major, 8-row K groups 1024 bytes apart, one 128-column atom
-                    // (its leading offset is never used; it is set to the group stride so that no reading of the
-                    // descriptor reaches past the tile).
+                    // A: K-major 128-byte rows, 8-row groups 1024 bytes apart; a K step of 32 moves 32 bytes inside
+                    // the swizzle atom. B: MN-major atom columns ATOM_W bytes wide, REGION bytes apart (the leading
+                    // offset; with a single atom column it is never used and is set to SBO so that no reading of it
+                    // leaves the tile), 8-row K groups SBO bytes apart; a K step of 32 rows moves 4 groups.
                     const uint64_t adesc = smem_desc(a_base + ks * 32, 16, 1024, SWZ_128B);
-                    const uint32_t acc = (!first || ks > 0) ? 1u : 0u;
-                    mma_i8(d, adesc, smem_desc(b0_base + ks * 4096, 1024, 1024, SWZ_128B), IDESC, acc);
-                    if (PLANES)
-                        mma_i8(d + BN, adesc, smem_desc(b1_base + ks * 4096, 1024, 1024, SWZ_128B), IDESC, acc);
+                    const uint64_t bdesc = smem_desc(b_base + ks * 4 * G::SBO, G::N_ATOMS > 1 ? G::REGION : G::SBO,
+                                                     G::SBO, G::B_SWZ);
+                    mma_i8(tmem, adesc, bdesc, IDESC, (kb > 0 || ks > 0) ? 1u : 0u);
                 }
                 mma_commit(&empty[s]);
-                if (last) mma_commit(&accfull[ab]);
             }
-            // Every MMA this thread issued has completed once `drain` flips (bounded: also on the abort path).
+            mma_commit(accfull);
+            // Every MMA issued has completed once `drain` flips (bounded: also on the abort path).
             mma_commit(drain);
             mbar_wait(drain, 0, DEV_TIMEOUT_DRAIN, p.err, abort_flag);
         }
         __syncwarp();
-    } else if (warp >= 4) {
-        // ---------------- plane expansion (planes mode) ----------------
-        if (PLANES) {
-            const int et = threadIdx.x - 128, h = et & 3;
+    } else {
+        if (PLANES && warp >= 4) {
+            // ---------------- plane expansion: warps 4-11 during the main loop ----------------
+            const int et = threadIdx.x - 128;            // 0 .. 255
+            constexpr int GROUPS = BN / 32;              // 32-column groups per K row
+            constexpr int ITEMS = BK * GROUPS / 256;     // (row, group) items per expander thread per stage
+            const int h = et % GROUPS;                   // this thread's 32-column group, the same in every item
+            const int fl_off = (n0 / 8) & 15;            // this tile's flags inside the 16-byte box rows
+            uint32_t clo[8], nclo[8];                    // codes: clo and -clo of the group's columns, word layout
+            if (KIND == KIND_CODES) {
+                // one column per expander thread into shared memory, then each thread packs its group's bytes
+                uint8_t* clo_s = reinterpret_cast<uint8_t*>(cc2);   // cc2 is free in the int8w mode
+                for (int nl = et; nl < BN; nl += 256) {
+                    const int n = n0 + nl;
+                    clo_s[nl] = n < p.N ? static_cast<uint8_t>(clo_of(p.lo[n], p.hi[n])) : 0;
+                }
+                named_barrier_sync(5, 256);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    uint32_t c = 0, nc = 0;
+#pragma unroll
+                    for (int pb = 0; pb < 4; ++pb) {
+                        const uint32_t v = clo_s[32 * h + 8 * pb + j];
+                        c |= v << (8 * pb);
+                        nc |= ((0x100u - v) & 0xFFu) << (8 * pb);
+                    }
+                    clo[j] = c;
+                    nclo[j] = nc;
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) clo[j] = nclo[j] = 0;
+            }
+            // where this thread's 32 columns sit in the operand: atom column and 16-byte chunk within its rows
+            const uint32_t atom = static_cast<uint32_t>((32 * h) / G::ATOM_W) * G::REGION;
+            const int cc = ((32 * h) % G::ATOM_W) / 16;
             for (int kb = 0; kb < nk; ++kb) {
                 const int s = kb % STAGES, r = kb / STAGES;
-                if (!mbar_wait(&full[s], r & 1, DEV_TIMEOUT_FULL, p.err, abort_flag)) break;
+                if (!warp_wait(&full[s], r & 1, DEV_TIMEOUT_FULL, p.err, abort_flag)) break;
                 const uint8_t* sg = sg_tile(s);
                 const uint8_t* fl = fl_tile(s);
-                uint8_t* bS = b0_tile(s);
-                uint8_t* bT = b1_tile(s);
+                uint8_t* bt = b_tile(s);
 #pragma unroll
-                for (int it = 0; it < BK / 32; ++it) {
-                    const int k = it * 32 + (et >> 2);
+                for (int it = 0; it < ITEMS; ++it) {
+                    const int k = (it * 256 + et) / GROUPS;
                     const uint2 x = *reinterpret_cast<const uint2*>(sg + k * (BN / 4) + 8 * h);
-                    const uint32_t fw = *reinterpret_cast<const uint32_t*>(fl + k * (BN / 8) + 4 * h);
-                    uint32_t S[8], T[8];
-                    expand32(x.x, x.y, fw, S, T);
-                    const uint32_t o0 = mn_sw128_offset(k, 2 * h), o1 = mn_sw128_offset(k, 2 * h + 1);
-                    *reinterpret_cast<uint4*>(bS + o0) = make_uint4(S[0], S[1], S[2], S[3]);
-                    *reinterpret_cast<uint4*>(bS + o1) = make_uint4(S[4], S[5], S[6], S[7]);
-                    *reinterpret_cast<uint4*>(bT + o0) = make_uint4(T[0], T[1], T[2], T[3]);
-                    *reinterpret_cast<uint4*>(bT + o1) = make_uint4(T[4], T[5], T[6], T[7]);
+                    const uint32_t fw = *reinterpret_cast<const uint32_t*>(fl + k * G::FL_ROW + fl_off + 4 * h);
+                    Planes32 pl;
+                    pl.load(x.x, x.y, fw);
+                    const uint32_t q0 = atom + b_offset<G::ATOM_W>(k, cc), q1 = atom + b_offset<G::ATOM_W>(k, cc + 1);
+                    if (KIND == KIND_ST) {   // S in the first atom column, T in the second
+                        uint32_t S[8], T[8];
+                        expand_st(pl, S, T);
+                        *reinterpret_cast<uint4*>(bt + q0) = make_uint4(S[0], S[1], S[2], S[3]);
+                        *reinterpret_cast<uint4*>(bt + q1) = make_uint4(S[4], S[5], S[6], S[7]);
+                        *reinterpret_cast<uint4*>(bt + G::REGION + q0) = make_uint4(T[0], T[1], T[2], T[3]);
+                        *reinterpret_cast<uint4*>(bt + G::REGION + q1) = make_uint4(T[4], T[5], T[6], T[7]);
+                    } else {
+                        uint32_t W[8];
+                        expand_codes(pl, clo, nclo, W);
+                        *reinterpret_cast<uint4*>(bt + q0) = make_uint4(W[0], W[1], W[2], W[3]);
+                        *reinterpret_cast<uint4*>(bt + q1) = make_uint4(W[4], W[5], W[6], W[7]);
+                    }
                 }
                 fence_proxy_async_smem();
+                if (et == 0) TRACE(160 + kb);
                 mbar_arrive(&bready[s]);
             }
         }
-    } else {
-        // ---------------- epilogue: warps 0-3, TMEM lanes 32w .. 32w + 31 ----------------
-        const int row = m0 + warp * 32 + lane;
+        // ---------------- epilogue: all groups; warp w reads TMEM lanes 32 (w % 4) .. + 31 ----------------
+        constexpr int NEPI = 128 * G::EPI_GROUPS;
+        const int grp = warp >> 2, quarter = warp & 3;
+        const int rloc = quarter * 32 + lane, row = m0 + rloc;
         const bool live = row < p.M;
-        const float as = live ? __fmul_rn(p.a_scales[row], p.alpha) : 0.f;
-        float* crow = p.C + static_cast<size_t>(live ? row : 0) * p.ldc + n0;
-        const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
-        for (int b = 0; b < nblk; ++b) {
-            const int ab = b & 1;
-            if (!mbar_wait(&accfull[ab], (b >> 1) & 1, DEV_TIMEOUT_ACC, p.err, abort_flag)) break;
-            tc_fence_after();
-            const bool store = p.beta_zero && b == 0;
-#pragma unroll 1
-            for (int c = 0; c < BN / 32; ++c) {
-                uint32_t rS[32], rT[32];
-                tmem_ld_32x32b_x32(tmem + lane_base + ab * G::ACC_COLS + 32 * c, rS);
-                if (PLANES) tmem_ld_32x32b_x32(tmem + lane_base + ab * G::ACC_COLS + BN + 32 * c, rT);
-                tmem_wait_ld();
-                if (live && n0 + 32 * c < p.N) {
-#pragma unroll
-                    for (int t4 = 0; t4 < 8; ++t4) {
-                        float4 old = make_float4(0.f, 0.f, 0.f, 0.f);
-                        if (!store) old = *reinterpret_cast<const float4*>(crow + 32 * c + 4 * t4);
-                        float o[4] = {old.x, old.y, old.z, old.w};
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            const int t = 4 * t4 + e;                              // column within the group
-                            const int ph = PLANES ? 4 * (t & 7) + (t >> 3) : t;    // its TMEM column
-                            const int nl = 32 * c + t;
-                            float f;
-                            if (PLANES && p.cmode == CM_INT8W) {
-                                const int clo = cclo[nl];
-                                const int acc = clo * static_cast<int>(rS[ph]) + (127 - clo) * static_cast<int>(rT[ph]);
-                                f = __fmul_rn(__int2float_rn(acc), cc1[nl]);
-                            } else if (PLANES) {
-                                f = __fmaf_rn(__int2float_rn(static_cast<int>(rT[ph])), cc2[nl],
-                                              __fmul_rn(__int2float_rn(static_cast<int>(rS[ph])), cc1[nl]));
-                            } else {
-                                f = __fmul_rn(__int2float_rn(static_cast<int>(rS[ph])), cc1[nl]);
-                            }
-                            o[e] = store ? __fmul_rn(f, as) : __fmaf_rn(f, as, o[e]);
-                        }
-                        *reinterpret_cast<float4*>(crow + 32 * c + 4 * t4) = make_float4(o[0], o[1], o[2], o[3]);
+        if (grp == 0) {   // per-column constants, while the main loop runs
+            for (int nl = rloc; nl < BN; nl += 128) {
+                const int n = n0 + nl;
+                float c1 = 0.f, c2 = 0.f;
+                if (n < p.N) {
+                    if (p.cmode == CM_Q8B) {
+                        c1 = p.scales[n];
+                    } else if (p.cmode == CM_INT8) {
+                        c1 = p.lo[n];
+                        c2 = __fsub_rn(p.hi[n], p.lo[n]);
+                    } else {   // int8w: c1 = hi * (1 / 127)
+                        c1 = __fmul_rn(p.hi[n], 1.0f / 127.0f);
                     }
                 }
+                cc1[nl] = c1;
+                if (G::ST) cc2[nl] = c2;   // in the int8w mode the expanders keep their clo table there
             }
-            tc_fence_before();
-            mbar_arrive(&accempty[ab]);
+        }
+        const float as = live ? __fmul_rn(p.a_scales[row], p.alpha) : 0.f;
+        named_barrier_sync(1, NEPI);   // constants visible; the expanders are done with the stage buffers
+        const bool ok = warp_wait(accfull, 0, DEV_TIMEOUT_ACC, p.err, abort_flag);
+        tc_fence_after();
+        if (threadIdx.x == 0) TRACE(240);
+        const bool load_old = !partial && !p.beta_zero;
+        bool have_old = ok && load_old;
+        if (have_old && threadIdx.x == 0) {   // C_old into the staging tiles (the stage buffers are free now)
+            mbar_arrive_expect_tx(cfull, G::OUT_BYTES);
+            for (int c = 0; c < G::CHUNKS; ++c) tma_load_2d(smem + c * (BM * 128), &tmOut, cfull, n0 + 32 * c, m0);
+        }
+        if (have_old) have_old = warp_wait(cfull, 0, DEV_TIMEOUT_ACC, p.err, abort_flag);
+        const bool go = ok && (!load_old || have_old);
+        const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+        const int out_row = partial ? z * p.m_pad + m0 : m0;   // the workspace slice of block z, or C
+        if (go) {
+#pragma unroll 1
+            for (int c = grp; c < G::CHUNKS; c += G::EPI_GROUPS) {
+                uint8_t* tile = smem + c * (BM * 128);
+                // Two halves of 16 TMEM columns. With planes the columns are column-transposed (TMEM column
+                // 16 h + 4 e + i holds output column 8 i + 4 h + e), so half h covers the float4 groups 2 i + h.
+#pragma unroll 1
+                for (int half = 0; half < 2; ++half) {
+                    uint32_t rS[16], rT[16];
+                    tmem_ld_32x32b_x16(tmem + lane_base + 32 * c + 16 * half, rS);
+                    if (G::ST) tmem_ld_32x32b_x16(tmem + lane_base + BN + 32 * c + 16 * half, rT);
+                    // the constants of these 16 output columns, while the TMEM loads are in flight
+                    float c1a[16], c2a[16];
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const int t4 = PLANES ? 2 * i + half : 4 * half + i;   // float4 group of output columns
+                        const float4 a = *reinterpret_cast<const float4*>(cc1 + 32 * c + 4 * t4);
+                        c1a[4 * i] = a.x; c1a[4 * i + 1] = a.y; c1a[4 * i + 2] = a.z; c1a[4 * i + 3] = a.w;
+                        if (G::ST) {
+                            const float4 b = *reinterpret_cast<const float4*>(cc2 + 32 * c + 4 * t4);
+                            c2a[4 * i] = b.x; c2a[4 * i + 1] = b.y; c2a[4 * i + 2] = b.z; c2a[4 * i + 3] = b.w;
+                        }
+                    }
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const int t4 = PLANES ? 2 * i + half : 4 * half + i;
+                        float4 old = make_float4(0.f, 0.f, 0.f, 0.f);
+                        if (load_old) old = *reinterpret_cast<const float4*>(tile + out_offset(rloc, t4));
+                        const float ov[4] = {old.x, old.y, old.z, old.w};
+                        float o[4];
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const int ph = PLANES ? 4 * e + i : 4 * i + e;   // its register among the 16
+                            float f;
+                            if (G::ST) {
+                                f = __fmaf_rn(__int2float_rn(static_cast<int>(rT[ph])), c2a[4 * i + e],
+                                              __fmul_rn(__int2float_rn(static_cast<int>(rS[ph])), c1a[4 * i + e]));
+                            } else {
+                                f = __fmul_rn(__int2float_rn(static_cast<int>(rS[ph])), c1a[4 * i + e]);
+                            }
+                            o[e] = partial ? f : (load_old ? __fmaf_rn(f, as, ov[e]) : __fmul_rn(f, as));
+                        }
+                        *reinterpret_cast<float4*>(tile + out_offset(rloc, t4)) = make_float4(o[0], o[1], o[2], o[3]);
+                    }
+                }
+                // the chunk is staged: the group's first thread stores it while the group moves on
+                fence_proxy_async_smem();
+                named_barrier_sync(2 + grp, 128);
+                if (quarter == 0 && lane == 0) {
+                    tma_store_2d(&tmOut, tile, n0 + 32 * c, out_row);
+                    tma_store_commit();
+                    if (c == 0) TRACE(241);
+                }
+            }
+        }
+        if (threadIdx.x == 0) TRACE(242);
+        if (go && quarter == 0 && lane == 0) {
+            tma_store_wait_read();   // the staging tiles must stay valid until the stores have read them
+            if (threadIdx.x == 0) TRACE(250);
         }
     }
 
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    if (warp == 9) tmem_dealloc(tmem, G::TMEM_COLS);
+    if (warp == G::MMAW) tmem_dealloc(tmem, G::TMEM_COLS);
+    if (threadIdx.x == 0) TRACE(260);
 }
 
-template <bool PLANES>
+// K > 1024: fold the per-block values f_b of the workspace slices into C in block order, as the reference's
+// epilogue does block after block (csrc/blas.c:1354-1366). One thread per four consecutive columns.
+__global__ void __launch_bounds__(256) fv_combine_kernel(const float* __restrict__ f, int m_pad, int nblk,
+                                                         const float* __restrict__ a_scales, float alpha,
+                                                         int beta_zero, float* __restrict__ C, int M, int N,
+                                                         int ldc) {
+    griddep_launch_dependents();
+    griddep_wait();
+    const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const int groups = N / 4;
+    if (i >= static_cast<size_t>(M) * groups) return;
+    const int m = static_cast<int>(i / groups), n = static_cast<int>(i % groups) * 4;
+    const float as = __fmul_rn(a_scales[m], alpha);
+    float4 c = beta_zero ? make_float4(0.f, 0.f, 0.f, 0.f)
+                         : *reinterpret_cast<const float4*>(C + static_cast<size_t>(m) * ldc + n);
+    for (int b = 0; b < nblk; ++b) {
+        const float4 v = *reinterpret_cast<const float4*>(f + (static_cast<size_t>(b) * m_pad + m) * N + n);
+        if (b == 0 && beta_zero) {
+            c = make_float4(__fmul_rn(v.x, as), __fmul_rn(v.y, as), __fmul_rn(v.z, as), __fmul_rn(v.w, as));
+        } else {
+            c = make_float4(__fmaf_rn(v.x, as, c.x), __fmaf_rn(v.y, as, c.y), __fmaf_rn(v.z, as, c.z),
+                            __fmaf_rn(v.w, as, c.w));
+        }
+    }
+    *reinterpret_cast<float4*>(C + static_cast<size_t>(m) * ldc + n) = c;
+}
+
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                              Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+template <int BN, int KIND>
 static cudaError_t launch(const CUtensorMap& a, const CUtensorMap& b0, const CUtensorMap& b1,
-                          const FvGemmParams& p, cudaStream_t stream) {
-    using G = Cfg<PLANES>;
+                          const CUtensorMap& out, const FvGemmParams& p, cudaStream_t stream) {
+    using G = Cfg<BN, KIND>;
     static bool configured[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 64 && !configured[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(fv_gemm_kernel<PLANES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        cudaError_t e = cudaFuncSetAttribute(fv_gemm_kernel<BN, KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              static_cast<int>(G::SMEM_BYTES));
         if (e != cudaSuccess) return e;
         configured[dev] = true;
     }
-    dim3 grid((p.N + BN - 1) / BN, (p.M + BM - 1) / BM);
-    fv_gemm_kernel<PLANES><<<grid, NTHREADS, G::SMEM_BYTES, stream>>>(a, b0, b1, p);
-    return cudaGetLastError();
+    dim3 grid((p.N + BN - 1) / BN, (p.M + BM - 1) / BM, p.ksplit);
+    return launch_pdl(fv_gemm_kernel<BN, KIND>, grid, dim3(G::NTHREADS), G::SMEM_BYTES, stream, a, b0, b1, out, p);
 }
 
-cudaError_t fv_gemm_launch_planes(const CUtensorMap& a, const CUtensorMap& signs, const CUtensorMap& flags,
-                                  const FvGemmParams& p, cudaStream_t stream) {
-    return launch<true>(a, signs, flags, p, stream);
+cudaError_t fv_gemm_launch(int bn, int kind, const CUtensorMap& a, const CUtensorMap& b0, const CUtensorMap& b1,
+                           const CUtensorMap& out, const FvGemmParams& p, cudaStream_t stream) {
+    switch (kind) {
+    case KIND_ST:
+        if (bn == 64) return launch<64, KIND_ST>(a, b0, b1, out, p, stream);
+        if (bn == 128) return launch<128, KIND_ST>(a, b0, b1, out, p, stream);
+        break;
+    case KIND_CODES:
+        if (bn == 64) return launch<64, KIND_CODES>(a, b0, b1, out, p, stream);
+        if (bn == 128) return launch<128, KIND_CODES>(a, b0, b1, out, p, stream);
+        if (bn == 256) return launch<256, KIND_CODES>(a, b0, b1, out, p, stream);
+        break;
+    default:
+        if (bn == 64) return launch<64, KIND_TABLE>(a, b0, b1, out, p, stream);
+        if (bn == 128) return launch<128, KIND_TABLE>(a, b0, b1, out, p, stream);
+        if (bn == 256) return launch<256, KIND_TABLE>(a, b0, b1, out, p, stream);
+        break;
+    }
+    return cudaErrorInvalidValue;
 }
 
-cudaError_t fv_gemm_launch_table(const CUtensorMap& a, const CUtensorMap& table, const FvGemmParams& p,
-                                 cudaStream_t stream) {
-    return launch<false>(a, table, table, p, stream);
+cudaError_t fv_combine_launch(const float* f, int m_pad, int nblk, const float* a_scales, float alpha, int beta_zero,
+                              float* C, int M, int N, int ldc, cudaStream_t stream) {
+    const size_t threads = static_cast<size_t>(M) * (N / 4);
+    return launch_pdl(fv_combine_kernel, dim3(static_cast<unsigned>((threads + 255) / 256)), dim3(256), 0, stream, f,
+                      m_pad, nblk, a_scales, alpha, beta_zero, C, M, N, ldc);
 }
 
 }  // namespace p2cu

@@ -9,6 +9,9 @@ namespace p2cu {
 // How the epilogue turns int32 sums into fp32 (the reference's GEMM modes, csrc/blas.c:1316-1336).
 enum : int { CM_INT8 = 0, CM_INT8W = 2, CM_Q8B = 8 };
 
+// The B operand: five-value planes expanded to int8w codes, to the two int8-mode planes S and T, or an int8 table.
+enum : int { KIND_TABLE = 0, KIND_ST = 1, KIND_CODES = 2 };
+
 struct FvGemmParams {
     int M, N, K;
     float alpha;
@@ -20,16 +23,22 @@ struct FvGemmParams {
     const float* scales;      // [N] int8-table column scales (CM_Q8B)
     float* C;
     int ldc;
+    int ksplit;               // CTAs along K, one per 1024-row block; > 1 writes per-block f to the workspace slices
+    int m_pad;                // rows per workspace slice (M rounded up to 128)
     uint32_t* err;            // device error word (timeouts), first error wins
+    long long* trace;         // diagnostic builds only (-DP2CU_TRACE): event timestamps of CTA (0, 0), or null
 };
 
-// Five-value planes: A [M, K] int8 (128 x 128 boxes, 128-byte swizzle), signs [K, N/4] (32 x 128 boxes) and
-// flags [K, N/8] (16 x 128 boxes). Requires N % 128 == 0 and K % 16 == 0.
-cudaError_t fv_gemm_launch_planes(const CUtensorMap& a, const CUtensorMap& signs, const CUtensorMap& flags,
-                                  const FvGemmParams& p, cudaStream_t stream);
+// One launch of the GEMM kernel: tile width bn (64, 128, or 256 for KIND_CODES / KIND_TABLE); for the planes kinds
+// b0 = signs [K, N/4] in bn/4 x 128 boxes and b1 = flags [K, N/8] in max(16, bn/8) x 128 boxes, for KIND_TABLE
+// b0 = [K, N] in min(bn, 128) x 128 boxes with that many bytes of swizzle. a = int8 A [M, K] in 128 x 128 boxes,
+// 128-byte swizzle. out = fp32 C [M, N] (ksplit == 1) or the workspace slices [ksplit * m_pad, N] (ksplit > 1),
+// 32 x 128 boxes, 128-byte swizzle.
+cudaError_t fv_gemm_launch(int bn, int kind, const CUtensorMap& a, const CUtensorMap& b0, const CUtensorMap& b1,
+                           const CUtensorMap& out, const FvGemmParams& p, cudaStream_t stream);
 
-// int8 table [K, N] (128 x 128 boxes, 128-byte swizzle): the int8-table weights, or cached int8w codes.
-cudaError_t fv_gemm_launch_table(const CUtensorMap& a, const CUtensorMap& table, const FvGemmParams& p,
-                                 cudaStream_t stream);
+// C = fold of the workspace slices (fp32 f per 1024-row block) in block order, with the row scales.
+cudaError_t fv_combine_launch(const float* f, int m_pad, int nblk, const float* a_scales, float alpha, int beta_zero,
+                              float* C, int M, int N, int ldc, cudaStream_t stream);
 
 }  // namespace p2cu

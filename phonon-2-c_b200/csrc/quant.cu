@@ -5,6 +5,7 @@
 #include <cstdint>
 #include <cuda_runtime.h>
 #include "kernels.h"
+#include "ptx.cuh"
 
 namespace p2cu {
 
@@ -15,8 +16,10 @@ __device__ __forceinline__ int8_t quant_one(float x, float inv) {
 }
 
 // One warp per row; K % 4 == 0 and 16-byte aligned rows (lda % 4 == 0) take the vector path.
-__global__ void __launch_bounds__(256) quant_rows_kernel(const float* __restrict__ A, int M, int K, int lda,
+__global__ void __launch_bounds__(128) quant_rows_kernel(const float* __restrict__ A, int M, int K, int lda,
                                                          int8_t* __restrict__ q, float* __restrict__ scales) {
+    griddep_launch_dependents();
+    griddep_wait();   // A may come from the previous kernel in the stream
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (warp >= M) return;
     const float* row = A + static_cast<size_t>(warp) * lda;
@@ -49,10 +52,17 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(const float* __restrict
 }
 
 cudaError_t quant_rows_launch(const float* A, int M, int K, int lda, int8_t* q, float* scales, cudaStream_t stream) {
-    const int rows_per_block = 8;
-    quant_rows_kernel<<<(M + rows_per_block - 1) / rows_per_block, 32 * rows_per_block, 0, stream>>>(A, M, K, lda, q,
-                                                                                                    scales);
-    return cudaGetLastError();
+    const int rows_per_block = 4;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((M + rows_per_block - 1) / rows_per_block);
+    cfg.blockDim = dim3(32 * rows_per_block);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;   // set-up overlaps the previous kernel
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, quant_rows_kernel, A, M, K, lda, q, scales);
 }
 
 // The int8w codes of a whole five-value weight as a row-major [K, N] int8 plane:

@@ -33,7 +33,7 @@ def _run_fvb(pkg, torch, cuda, w, A, mode, alpha, beta, C0, codes=False):
     B = DeviceFiveValue(w, cuda, codes=codes)
     A_d = torch.from_numpy(A).to(cuda)
     C_d = torch.from_numpy(C0.copy()).to(cuda)
-    nws = max(pkg.workspace_bytes(M, K, mode), 16)
+    nws = max(pkg.workspace_bytes(M, N, K, mode), 16)
     ws = torch.empty(nws, dtype=torch.uint8, device=cuda)
     pkg.sgemm_fvb(M, N, K, alpha, A_d.data_ptr(), K, B.struct, mode, beta, C_d.data_ptr(), N, ws.data_ptr(), nws)
     pkg.check_device()
@@ -91,7 +91,10 @@ def test_int32_accumulators_bitwise(pkg, orc, synth, cuda, K):
         ww = dict(w, lo=np.full(N, lo, np.float32), hi=np.full(N, hi, np.float32))
         B = DeviceFiveValue(ww, cuda)
         C_d = torch.zeros((M, N), dtype=torch.float32, device=cuda)
-        pkg.sgemm_fvb_q8a(M, N, K, 1.0, q_d.data_ptr(), ones.data_ptr(), B.struct, pkg.INT8, 0.0, C_d.data_ptr(), N)
+        nws = max(pkg.q8a_workspace_bytes(M, N, K), 16)
+        ws = torch.empty(nws, dtype=torch.uint8, device=cuda)
+        pkg.sgemm_fvb_q8a(M, N, K, 1.0, q_d.data_ptr(), ones.data_ptr(), B.struct, pkg.INT8, 0.0, C_d.data_ptr(), N,
+                          ws.data_ptr(), nws)
         pkg.check_device()
         got = C_d.cpu().numpy().astype(np.int64)
         want = want_blocks.astype(np.int64).sum(axis=0)   # blocks summed in fp32 exactly (integers below 2^24)
@@ -125,7 +128,7 @@ def test_int8_table_bitwise(pkg, orc, synth, cuda, mode, M, K, N):
     s_d = torch.from_numpy(t["scales"]).to(cuda)
     C_d = torch.zeros((M, N), dtype=torch.float32, device=cuda)
     m = pkg.MODES[mode]
-    nws = max(pkg.workspace_bytes(M, K, m), 16)
+    nws = max(pkg.workspace_bytes(M, N, K, m), 16)
     ws = torch.empty(nws, dtype=torch.uint8, device=cuda)
     pkg.sgemm_q8b(M, N, K, 1.0, A_d.data_ptr(), K, B_d.data_ptr(), s_d.data_ptr(), N, m, 0.0, C_d.data_ptr(), N,
                   ws.data_ptr(), nws)
@@ -198,3 +201,49 @@ def test_contract_errors(pkg, synth, cuda):
                       ws.data_ptr(), ws.numel())
     assert e.value.code == pkg.P2CU_EINVAL
     pkg.check_device()
+
+
+TILE_CHILD = r"""
+import json, sys
+import numpy as np
+sys.path.insert(0, {root!r})
+import __graft_entry__ as ge
+import torch
+pkg, orc = ge.load_package(), ge.load_oracle()
+from phonon2_b200 import synth
+from phonon2_b200.device import DeviceFiveValue
+dev = torch.device("cuda:0")
+res = []
+for (M, K, N, mode, beta, codes) in [(375, 1024, 1024, "int8w", 1.0, False), (300, 2048, 512, "int8", 0.0, False),
+                                     (130, 1024, 768, "int8w", 0.0, True), (375, 1024, 512, "int8", 1.0, False)]:
+    w = synth.five_value(K, N, seed=M + N)
+    A = synth.activations(M, K, seed=K)
+    C0 = np.random.default_rng(1).standard_normal((M, N)).astype(np.float32)
+    B = DeviceFiveValue(w, dev, codes=codes)
+    A_d, C_d = torch.from_numpy(A).to(dev), torch.from_numpy(C0.copy()).to(dev)
+    m = pkg.MODES[mode]
+    nws = max(pkg.workspace_bytes(M, N, K, m), 16)
+    ws = torch.empty(nws, dtype=torch.uint8, device=dev)
+    pkg.sgemm_fvb(M, N, K, 1.0, A_d.data_ptr(), K, B.struct, m, beta, C_d.data_ptr(), N, ws.data_ptr(), nws)
+    pkg.check_device()
+    got = C_d.cpu().numpy()
+    want = orc.sgemm_i8(A, mode, C0.copy(), w=w, beta=beta)
+    res.append(bool(np.array_equal(got.view(np.uint32), want.view(np.uint32))))
+print(json.dumps(res))
+"""
+
+
+@pytest.mark.parametrize("tile", ["64", "128", "256"])
+def test_every_tile_width_bitwise(cuda, tile):
+    """The same GEMMs with each tile width forced (P2CU_TILE_N, read once per process: a child each)."""
+    import json
+    import os
+    import subprocess
+    import sys
+    from pathlib import Path
+    root = str(Path(__file__).resolve().parents[1])
+    env = dict(os.environ, P2CU_TILE_N=tile)
+    out = subprocess.run([sys.executable, "-c", TILE_CHILD.format(root=root)], env=env, capture_output=True, text=True,
+                         timeout=300)
+    assert out.returncode == 0, out.stderr[-3000:]
+    assert json.loads(out.stdout.strip().splitlines()[-1]) == [True] * 4
