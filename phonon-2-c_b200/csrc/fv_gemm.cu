@@ -403,47 +403,68 @@ fv_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 #pragma unroll 1
             for (int c = grp; c < G::CHUNKS; c += G::EPI_GROUPS) {
                 uint8_t* tile = smem + c * (BM * 128);
-                // Two halves of 16 TMEM columns. With planes the columns are column-transposed (TMEM column
-                // 16 h + 4 e + i holds output column 8 i + 4 h + e), so half h covers the float4 groups 2 i + h.
-#pragma unroll 1
-                for (int half = 0; half < 2; ++half) {
-                    uint32_t rS[16], rT[16];
-                    tmem_ld_32x32b_x16(tmem + lane_base + 32 * c + 16 * half, rS);
-                    if (G::ST) tmem_ld_32x32b_x16(tmem + lane_base + BN + 32 * c + 16 * half, rT);
-                    // the constants of these 16 output columns, while the TMEM loads are in flight
-                    float c1a[16], c2a[16];
+                if (!G::ST) {
+                    // one plane: the chunk's 32 TMEM columns in one load, its constants loaded meanwhile
+                    uint32_t r32[32];
+                    tmem_ld_32x32b_x32(tmem + lane_base + 32 * c, r32);
+                    float c1a[32];
 #pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        const int t4 = PLANES ? 2 * i + half : 4 * half + i;   // float4 group of output columns
+                    for (int t4 = 0; t4 < 8; ++t4) {
                         const float4 a = *reinterpret_cast<const float4*>(cc1 + 32 * c + 4 * t4);
-                        c1a[4 * i] = a.x; c1a[4 * i + 1] = a.y; c1a[4 * i + 2] = a.z; c1a[4 * i + 3] = a.w;
-                        if (G::ST) {
-                            const float4 b = *reinterpret_cast<const float4*>(cc2 + 32 * c + 4 * t4);
-                            c2a[4 * i] = b.x; c2a[4 * i + 1] = b.y; c2a[4 * i + 2] = b.z; c2a[4 * i + 3] = b.w;
-                        }
+                        c1a[4 * t4] = a.x; c1a[4 * t4 + 1] = a.y; c1a[4 * t4 + 2] = a.z; c1a[4 * t4 + 3] = a.w;
                     }
                     tmem_wait_ld();
 #pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        const int t4 = PLANES ? 2 * i + half : 4 * half + i;
+                    for (int t4 = 0; t4 < 8; ++t4) {
                         float4 old = make_float4(0.f, 0.f, 0.f, 0.f);
                         if (load_old) old = *reinterpret_cast<const float4*>(tile + out_offset(rloc, t4));
                         const float ov[4] = {old.x, old.y, old.z, old.w};
                         float o[4];
 #pragma unroll
                         for (int e = 0; e < 4; ++e) {
-                            const int ph = PLANES ? 4 * e + i : 4 * i + e;   // its register among the 16
-                            float f;
-                            if (G::ST) {
-                                f = __fmaf_rn(__int2float_rn(static_cast<int>(rT[ph])), c2a[4 * i + e],
-                                              __fmul_rn(__int2float_rn(static_cast<int>(rS[ph])), c1a[4 * i + e]));
-                            } else {
-                                f = __fmul_rn(__int2float_rn(static_cast<int>(rS[ph])), c1a[4 * i + e]);
-                            }
+                            const int t = 4 * t4 + e;
+                            const int ph = PLANES ? 4 * (t & 7) + (t >> 3) : t;   // column-transposed with planes
+                            const float f = __fmul_rn(__int2float_rn(static_cast<int>(r32[ph])), c1a[t]);
                             o[e] = partial ? f : (load_old ? __fmaf_rn(f, as, ov[e]) : __fmul_rn(f, as));
                         }
                         *reinterpret_cast<float4*>(tile + out_offset(rloc, t4)) = make_float4(o[0], o[1], o[2], o[3]);
                     }
+                } else {
+                // S and T: two halves of 16 TMEM columns each. The columns are column-transposed (TMEM column
+                // 16 h + 4 e + i holds output column 8 i + 4 h + e), so half h covers the float4 groups 2 i + h.
+#pragma unroll 1
+                for (int half = 0; half < 2; ++half) {
+                    uint32_t rS[16], rT[16];
+                    tmem_ld_32x32b_x16(tmem + lane_base + 32 * c + 16 * half, rS);
+                    tmem_ld_32x32b_x16(tmem + lane_base + BN + 32 * c + 16 * half, rT);
+                    // the constants of these 16 output columns, while the TMEM loads are in flight
+                    float c1a[16], c2a[16];
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const int t4 = 2 * i + half;   // float4 group of output columns
+                        const float4 a = *reinterpret_cast<const float4*>(cc1 + 32 * c + 4 * t4);
+                        c1a[4 * i] = a.x; c1a[4 * i + 1] = a.y; c1a[4 * i + 2] = a.z; c1a[4 * i + 3] = a.w;
+                        const float4 b = *reinterpret_cast<const float4*>(cc2 + 32 * c + 4 * t4);
+                        c2a[4 * i] = b.x; c2a[4 * i + 1] = b.y; c2a[4 * i + 2] = b.z; c2a[4 * i + 3] = b.w;
+                    }
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const int t4 = 2 * i + half;
+                        float4 old = make_float4(0.f, 0.f, 0.f, 0.f);
+                        if (load_old) old = *reinterpret_cast<const float4*>(tile + out_offset(rloc, t4));
+                        const float ov[4] = {old.x, old.y, old.z, old.w};
+                        float o[4];
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const int ph = 4 * e + i;   // its register among the 16
+                            const float f = __fmaf_rn(__int2float_rn(static_cast<int>(rT[ph])), c2a[4 * i + e],
+                                                      __fmul_rn(__int2float_rn(static_cast<int>(rS[ph])), c1a[4 * i + e]));
+                            o[e] = partial ? f : (load_old ? __fmaf_rn(f, as, ov[e]) : __fmul_rn(f, as));
+                        }
+                        *reinterpret_cast<float4*>(tile + out_offset(rloc, t4)) = make_float4(o[0], o[1], o[2], o[3]);
+                    }
+                }
                 }
                 // the chunk is staged: the group's first thread stores it while the group moves on
                 fence_proxy_async_smem();

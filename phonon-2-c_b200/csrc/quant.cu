@@ -15,47 +15,68 @@ __device__ __forceinline__ int8_t quant_one(float x, float inv) {
     return static_cast<int8_t>(v);
 }
 
-// One warp per row; K % 4 == 0 and 16-byte aligned rows (lda % 4 == 0) take the vector path.
-__global__ void __launch_bounds__(128) quant_rows_kernel(const float* __restrict__ A, int M, int K, int lda,
-                                                         int8_t* __restrict__ q, float* __restrict__ scales) {
+// One CTA of 128 threads per row. Rows up to 4096 wide with K % 4 == 0 and 16-byte aligned rows stay in registers
+// (one read of A); other shapes take a strided two-pass path.
+constexpr int QT = 128;            // threads per row
+constexpr int QV = 4096 / (4 * QT);   // float4 per thread when the row is held in registers
+
+__device__ __forceinline__ float block_max(float v, float* red) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    v = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+    return v;
+}
+
+__global__ void __launch_bounds__(QT) quant_rows_kernel(const float* __restrict__ A, int M, int K, int lda,
+                                                        int8_t* __restrict__ q, float* __restrict__ scales) {
     griddep_launch_dependents();
     griddep_wait();   // A may come from the previous kernel in the stream
-    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-    if (warp >= M) return;
-    const float* row = A + static_cast<size_t>(warp) * lda;
-    int8_t* qrow = q + static_cast<size_t>(warp) * K;
-    float amax = 0.f;
-    const bool vec = (K % 4 == 0) && (lda % 4 == 0) && ((reinterpret_cast<uintptr_t>(A) & 15) == 0);
+    __shared__ float red[QT / 32];
+    const int m = blockIdx.x;
+    const float* row = A + static_cast<size_t>(m) * lda;
+    int8_t* qrow = q + static_cast<size_t>(m) * K;
+    const bool vec = (K % 4 == 0) && (K <= 4 * QT * QV) && (lda % 4 == 0) &&
+                     ((reinterpret_cast<uintptr_t>(A) & 15) == 0);
     if (vec) {
-        for (int k = 4 * lane; k < K; k += 128) {
-            const float4 v = *reinterpret_cast<const float4*>(row + k);
-            amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
-        }
-    } else {
-        for (int k = lane; k < K; k += 32) amax = fmaxf(amax, fabsf(row[k]));
-    }
+        float4 v[QV];
+        float amax = 0.f;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        for (int i = 0; i < QV; ++i) {
+            const int k = 4 * (threadIdx.x + i * QT);
+            v[i] = k < K ? *reinterpret_cast<const float4*>(row + k) : make_float4(0.f, 0.f, 0.f, 0.f);
+            amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[i].x), fabsf(v[i].y)), fmaxf(fabsf(v[i].z), fabsf(v[i].w))));
+        }
+        amax = block_max(amax, red);
+        const float scale = amax > 0.f ? __fdiv_rn(amax, 127.0f) : 1.0f;
+        const float inv = __fdiv_rn(1.0f, scale);
+#pragma unroll
+        for (int i = 0; i < QV; ++i) {
+            const int k = 4 * (threadIdx.x + i * QT);
+            if (k < K) {
+                char4 o;
+                o.x = quant_one(v[i].x, inv); o.y = quant_one(v[i].y, inv);
+                o.z = quant_one(v[i].z, inv); o.w = quant_one(v[i].w, inv);
+                *reinterpret_cast<char4*>(qrow + k) = o;
+            }
+        }
+        if (threadIdx.x == 0) scales[m] = scale;
+        return;
+    }
+    float amax = 0.f;
+    for (int k = threadIdx.x; k < K; k += QT) amax = fmaxf(amax, fabsf(row[k]));
+    amax = block_max(amax, red);
     const float scale = amax > 0.f ? __fdiv_rn(amax, 127.0f) : 1.0f;
     const float inv = __fdiv_rn(1.0f, scale);
-    if (vec) {
-        for (int k = 4 * lane; k < K; k += 128) {
-            const float4 v = *reinterpret_cast<const float4*>(row + k);
-            char4 o;
-            o.x = quant_one(v.x, inv); o.y = quant_one(v.y, inv); o.z = quant_one(v.z, inv); o.w = quant_one(v.w, inv);
-            *reinterpret_cast<char4*>(qrow + k) = o;
-        }
-    } else {
-        for (int k = lane; k < K; k += 32) qrow[k] = quant_one(row[k], inv);
-    }
-    if (lane == 0) scales[warp] = scale;
+    for (int k = threadIdx.x; k < K; k += QT) qrow[k] = quant_one(row[k], inv);
+    if (threadIdx.x == 0) scales[m] = scale;
 }
 
 cudaError_t quant_rows_launch(const float* A, int M, int K, int lda, int8_t* q, float* scales, cudaStream_t stream) {
-    const int rows_per_block = 4;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((M + rows_per_block - 1) / rows_per_block);
-    cfg.blockDim = dim3(32 * rows_per_block);
+    cfg.gridDim = dim3(M);
+    cfg.blockDim = dim3(QT);
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;   // set-up overlaps the previous kernel
