@@ -98,6 +98,23 @@ P2CU_API int p2cu_sgemm(int transA, int transB, int M, int N, int K, float alpha
 /* The int8w codes of B as a row-major [K][N] int8 plane (csrc/blas.c:1391-1400 values): codes has K * N bytes. */
 P2CU_API int p2cu_fv_pack_codes(const P2cuFiveValue *B, signed char *codes, void *stream);
 
+/* Bytes of the fixed device array behind p2cu_sgemm_fvb_noalloc (16 MiB), held on every device that loads the
+ * library until the process exits. */
+#define P2CU_NOALLOC_SCRATCH_BYTES (16u << 20)
+
+/* p2cu_sgemm_fvb without a workspace argument, for callers that cannot allocate device memory: a real-time thread
+ * (cudaMalloc may block and synchronise the device), a host that grants a fixed memory budget, code running while a
+ * stream is captured into a CUDA graph. No counterpart in the reference (its GEMMs use per-thread host buffers).
+ * The scratch - quantised activations and, for K > 1024, the per-block partials; p2cu_gemm_workspace_bytes(M, N, K,
+ * mode) bytes - lives in one fixed array of P2CU_NOALLOC_SCRATCH_BYTES per device; larger shapes are refused with
+ * P2CU_EINVAL and a message. This function calls no cudaMalloc, cudaFree or other allocating routine. Its first call
+ * on a device looks up the array's device address (cudaGetSymbolAddress, that device current): make that first call
+ * before any stream capture. Every call on a device shares the array, so calls whose kernels overlap on the GPU (on
+ * different streams, or from different threads) race on it and must be serialised by the caller; nothing in it
+ * needs to start at zero. */
+P2CU_API int p2cu_sgemm_fvb_noalloc(int M, int N, int K, float alpha, const float *A, int lda, const P2cuFiveValue *B,
+                                    int mode, float beta, float *C, int ldc, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -62,6 +62,7 @@ SIGNATURES = {
     "p2cu_sgemm_q8b": (_i, [_i, _i, _i, _f, _vp, _i, _vp, _vp, _i, _i, _f, _vp, _i, _vp, _sz, _vp]),
     "p2cu_sgemm": (_i, [_i, _i, _i, _i, _i, _f, _vp, _i, _vp, _i, _f, _vp, _i, _vp]),
     "p2cu_fv_pack_codes": (_i, [C.POINTER(P2cuFiveValue), _vp, _vp]),
+    "p2cu_sgemm_fvb_noalloc": (_i, [_i, _i, _i, _f, _vp, _i, C.POINTER(P2cuFiveValue), _i, _f, _vp, _i, _vp]),
     # include/blas.h: the reference's host-pointer ABI
     "p2_sgemm": (None, [_i, _i, _i, _i, _i, _f, _vp, _i, _vp, _i, _f, _vp, _i]),
     "p2_sgemm_st": (None, [_i, _i, _i, _i, _i, _f, _vp, _i, _vp, _i, _f, _vp, _i]),
@@ -134,6 +135,14 @@ def quant_rows(A: int, M: int, K: int, lda: int, q: int, scales: int, stream=Non
 def sgemm_fvb(M, N, K, alpha, A, lda, B: P2cuFiveValue, mode, beta, Cp, ldc, workspace, ws_bytes, stream=None):
     check(lib().p2cu_sgemm_fvb(M, N, K, alpha, A, lda, C.byref(B), mode, beta, Cp, ldc, workspace, ws_bytes,
                                stream_ptr(stream)))
+
+
+def sgemm_fvb_noalloc(M, N, K, alpha, A, lda, B: P2cuFiveValue, mode, beta, Cp, ldc, stream=None):
+    """p2cu_sgemm_fvb with its scratch in the library's fixed device array (no workspace, no allocation)."""
+    check(lib().p2cu_sgemm_fvb_noalloc(M, N, K, alpha, A, lda, C.byref(B), mode, beta, Cp, ldc, stream_ptr(stream)))
+
+
+NOALLOC_SCRATCH_BYTES = 16 << 20   # P2CU_NOALLOC_SCRATCH_BYTES in include/p2cuda.h
 
 
 def sgemm_fvb_q8a(M, N, K, alpha, q, a_scales, B: P2cuFiveValue, mode, beta, Cp, ldc, workspace=None, ws_bytes=0,

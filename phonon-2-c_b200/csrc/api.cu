@@ -256,6 +256,11 @@ int run_exact(int M, int N, int K, float alpha, const float* A, int lda, int tra
 
 }  // namespace
 
+namespace p2cu {
+// For the library's other translation units: set the text p2cu_last_error() returns on this thread.
+void set_error_message(int code, const char* msg) { fail(code, "%s", msg); }
+}  // namespace p2cu
+
 extern "C" {
 
 #ifdef P2CU_TRACE
