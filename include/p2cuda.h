@@ -17,6 +17,7 @@
 #define P2CUDA_H
 
 #include <stddef.h>
+#include "phonon2.h"
 
 #if defined(__GNUC__)
 #define P2CU_API __attribute__((visibility("default")))
@@ -114,6 +115,56 @@ P2CU_API int p2cu_fv_pack_codes(const P2cuFiveValue *B, signed char *codes, void
  * needs to start at zero. */
 P2CU_API int p2cu_sgemm_fvb_noalloc(int M, int N, int K, float alpha, const float *A, int lda, const P2cuFiveValue *B,
                                     int mode, float beta, float *C, int ldc, void *stream);
+
+/* ---- The encoder's row ops on device rows (the reference's ops ABI, csrc/phonon2.h:424-465) ----------------------
+ * Every array is row-major fp32 [rows][features] in device memory; quantised rows are int8 [rows][features] with one
+ * fp32 scale per row, as p2cu_quant_rows writes them. */
+
+/* LayerNorm, eps 1e-5 (p2_layer_norm_rows, csrc/tensor_ops.c:204-303); out may be x (p2_layer_norm_rows_inplace). */
+P2CU_API int p2cu_layer_norm_rows(const float *x, const float *gamma, const float *beta, float *out, int n_rows, int D,
+                                  void *stream);
+/* LayerNorm straight into quantised rows (p2_layer_norm_quant_rows, csrc/tensor_ops.c:329-350). */
+P2CU_API int p2cu_layer_norm_quant_rows(const float *x, const float *gamma, const float *beta, signed char *q,
+                                        float *scales, int n_rows, int D, void *stream);
+/* x * sigmoid(x) in place (p2_swish, csrc/tensor_ops.c:436-490). */
+P2CU_API int p2cu_swish(float *x, size_t n, void *stream);
+/* SiLU of each row straight into quantised rows (p2_swish_quant_rows, csrc/tensor_ops.c:492-511). */
+P2CU_API int p2cu_swish_quant_rows(const float *h, signed char *q, float *scales, int n_rows, int len, void *stream);
+/* Softmax of each row in place (p2_softmax_rows, csrc/tensor_ops.c:354-428). */
+P2CU_API int p2cu_softmax_rows(float *x, int n_rows, int len, void *stream);
+/* Depthwise convolution over time with kernel 9 and padding 4 (p2_depthwise_conv1d with K = 9, csrc/tensor_ops.c:
+ * 559-649), on time-major rows: x and out are [T][C], w is [C][9], b is [C] or NULL. */
+P2CU_API int p2cu_depthwise_conv1d_rows(const float *x, const float *w, const float *b, float *out, int C, int T,
+                                        void *stream);
+
+/* ---- The encoder on the device (csrc/encoder.c) ------------------------------------------------------------------
+ * Unlike the calls above these allocate device memory, once: p2cu_model_upload copies a model's weights to the
+ * current device, p2cu_encoder_create makes a plan with every buffer of one batch of windows and captures its forward
+ * pass in a CUDA graph; p2cu_encoder_run then launches that graph and allocates nothing. */
+typedef struct P2cuModel P2cuModel;
+typedef struct P2cuEncoder P2cuEncoder;
+
+/* Copy the encoder weights of `m` (host pointers, as phonon-2-c's loader maps them) into one allocation on the current
+ * device. codes != 0 also builds the int8w code plane of every five-value weight there (the reference's
+ * P2_CACHE_CODES, K * N bytes each), which the int8w GEMMs then stream instead of expanding the planes. */
+P2CU_API int p2cu_model_upload(const P2Model *m, int codes, P2cuModel **out);
+P2CU_API void p2cu_model_free(P2cuModel *m);
+P2CU_API size_t p2cu_model_bytes(const P2cuModel *m);
+
+/* A plan for `n_windows` windows of n_frames[w] mel frames each, in mode P2CU_INT8, P2CU_INT8W or P2CU_EXACT, on the
+ * model's device. chunk_frames > 0 encodes each window's frames in chunks of that many frames with chunk_overlap
+ * frames of context on each side (p2_encoder_chunked); 0 encodes every window in one pass. */
+P2CU_API int p2cu_encoder_create(const P2cuModel *m, const int *n_frames, int n_windows, int mode, int chunk_frames,
+                                 int chunk_overlap, P2cuEncoder **out);
+P2CU_API void p2cu_encoder_destroy(P2cuEncoder *e);
+/* Encoder frames of window w (three stride-2 halvings of its mel frames), or of all windows together for w < 0. */
+P2CU_API int p2cu_encoder_frames(const P2cuEncoder *e, int window);
+/* The plan's input: the windows' mel frames stacked, [sum n_frames][128] fp32, written by the caller before a run. */
+P2CU_API float *p2cu_encoder_mel(P2cuEncoder *e);
+/* The plan's output: the windows' encoder frames stacked, [sum frames][640] fp32, valid after a run completes. */
+P2CU_API float *p2cu_encoder_out(P2cuEncoder *e);
+/* One forward pass over the plan's input on `stream` (one graph launch). Runs on one plan must not overlap. */
+P2CU_API int p2cu_encoder_run(P2cuEncoder *e, void *stream);
 
 #ifdef __cplusplus
 }

@@ -2,8 +2,9 @@
  *  csrc/phonon2.h lays them out (v0.1.0), so that objects compiled against either header interoperate.
  *
  *  Only declarations this library implements live here (the weight and model structs, QuantA, the model
- *  constants). phonon-2-c's engine, audio front end, decoder and tokenizer keep their own header and sources; a
- *  build that links them with libphonon2_b200.so gets the GEMM layer and the encoder from the GPU.
+ *  constants, the encoder entry points). phonon-2-c's engine, audio front end, decoder and tokenizer keep their own
+ *  header and sources; a build that links them with libphonon2_b200.so gets the GEMM layer and the encoder from the
+ *  GPU.
  *  Each type cites the reference declaration it mirrors (csrc/phonon2.h line numbers).
  */
 #ifndef PHONON2_H
@@ -147,6 +148,21 @@ typedef struct {
     float       *scales;
     int          M, K;
 } QuantA;
+
+/* Encoder progress on stderr in the reference (csrc/phonon2.h:224); this build prints nothing per block but keeps
+ * the variable, which the reference's engine and CLI set. */
+P2_API extern int p2_verbose;
+
+/* The encoder, mel [n_frames x 128] -> projected frames [T' x 640], T' = three stride-2 halvings of n_frames; the
+ * caller frees *out (csrc/phonon2.h:394-395). Runs on the GPU of the calling thread (p2_b200_set_device): the
+ * model's weights are uploaded there on first use (found again by the P2Model's address) and the whole forward pass
+ * runs as one CUDA graph. The mode is the GEMM layer's (P2_GEMM / P2_EXACT); beyond 500 frames of T' (or as P2_CHUNK
+ * says) the sequence is encoded in chunks of P2_CHUNK_SIZE (400) frames with P2_CHUNK_OVERLAP (8) frames of context,
+ * as the reference does. Returns 0, or -1 with a message on stderr. */
+P2_API int p2_encoder(const P2Model *m, const float *mel, int n_frames, float **out, int *out_len);
+
+/* The chunked encoder regardless of length (csrc/phonon2.h:397-398). Same contract. */
+P2_API int p2_encoder_chunked(const P2Model *m, const float *mel, int n_frames, float **out, int *out_len);
 
 #ifdef __cplusplus
 }

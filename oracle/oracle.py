@@ -1,8 +1,10 @@
 """ctypes access to the CPU checkers. TEST INFRASTRUCTURE ONLY.
 
-Two libraries, both built by oracle/Makefile (``__graft_entry__.build()`` runs it):
-  * ``liboracle.so``          - fv_oracle.c, the C restatement of the reference's GEMM arithmetic;
-  * ``_ref/libphonon2_ref.so`` - phonon-2-c's own library compiled from its sources (exact mode on x86).
+Three libraries, all built by oracle/Makefile (``__graft_entry__.build()`` runs it):
+  * ``liboracle.so``             - fv_oracle.c, the C restatement of the reference's GEMM arithmetic;
+  * ``_ref/libphonon2_ref.so``    - phonon-2-c's own library compiled from its sources (exact mode on x86);
+  * ``_ref/libphonon2_ref_i8.so`` - the same, with its int8 GEMM entry points supplied by ref_int8_blas.c (the
+    restatement), so that the reference's own encoder runs its int8 control flow on x86.
 
 Only tests/, ``__graft_entry__.smoke()`` and bench.py's CPU legs import this module; the product never does.
 """
@@ -17,6 +19,7 @@ import numpy as np
 HERE = Path(__file__).resolve().parent
 ORACLE_SO = HERE / "liboracle.so"
 REF_SO = HERE / "_ref" / "libphonon2_ref.so"
+REF_I8_SO = HERE / "_ref" / "libphonon2_ref_i8.so"
 
 MODE_INT8, MODE_INT8W, MODE_Q8B = 0, 2, 8
 _MODES = {"int8": MODE_INT8, "int8w": MODE_INT8W}
@@ -28,6 +31,7 @@ _i32p = np.ctypeslib.ndpointer(np.int32, flags="C_CONTIGUOUS")
 
 _lib = None
 _ref = None
+_ref_i8 = None
 
 
 def lib() -> C.CDLL:
@@ -184,6 +188,139 @@ def ref_sgemm(transA, transB, A, B, out, alpha=1.0, beta=0.0):
     ref().p2_sgemm(112 if transA else 111, 112 if transB else 111, M, N, K, alpha, np.ascontiguousarray(A), A.shape[1],
                    np.ascontiguousarray(B), B.shape[1], beta, out, N)
     return out
+
+
+def _encoder_lib(path):
+    L = C.CDLL(str(path))
+    L.p2_encoder.argtypes = [C.c_void_p, _f32p, C.c_int, C.POINTER(C.c_void_p), C.POINTER(C.c_int)]
+    L.p2_encoder.restype = C.c_int
+    L.p2_encoder_chunked.argtypes = L.p2_encoder.argtypes
+    L.p2_encoder_chunked.restype = C.c_int
+    C.c_int.in_dll(L, "p2_verbose").value = 0
+    return L
+
+
+def ref_i8() -> C.CDLL:
+    """The reference's encoder with the restated int8 GEMMs (see ref_int8_blas.c)."""
+    global _ref_i8
+    if _ref_i8 is None:
+        if not REF_I8_SO.exists():
+            raise RuntimeError(f"{REF_I8_SO} is not built (needs the reference sources; run __graft_entry__.build())")
+        L = _encoder_lib(REF_I8_SO)
+        L.orc_shim_set_mode.argtypes = [C.c_int]
+        _ref_i8 = L
+    return _ref_i8
+
+
+_libc = C.CDLL(None)
+_libc.free.argtypes = [C.c_void_p]
+
+
+def ref_encoder(model_struct, mel: np.ndarray, mode: str = "exact", chunked: bool = False) -> np.ndarray:
+    """phonon-2-c's p2_encoder (csrc/encoder.c:753-761) on a P2Model (ctypes struct) and mel [n, 128]: [T', 640].
+
+    mode "exact" runs the reference library as built (its x86 path is exact); "int8" / "int8w" run its encoder with
+    the restated int8 GEMMs (libphonon2_ref_i8.so)."""
+    if mode == "exact":
+        L = ref()
+        if not hasattr(L, "_enc_ready"):
+            L.p2_encoder.argtypes = [C.c_void_p, _f32p, C.c_int, C.POINTER(C.c_void_p), C.POINTER(C.c_int)]
+            L.p2_encoder.restype = C.c_int
+            L.p2_encoder_chunked.argtypes = L.p2_encoder.argtypes
+            L.p2_encoder_chunked.restype = C.c_int
+            C.c_int.in_dll(L, "p2_verbose").value = 0
+            L._enc_ready = True
+    else:
+        L = ref_i8()
+        L.orc_shim_set_mode({"int8": 0, "int8w": 2}[mode])
+    mel = np.ascontiguousarray(mel, np.float32)
+    out, n = C.c_void_p(), C.c_int()
+    fn = L.p2_encoder_chunked if chunked else L.p2_encoder
+    rc = fn(C.addressof(model_struct), mel, mel.shape[0], C.byref(out), C.byref(n))
+    if rc != 0:
+        raise RuntimeError(f"reference p2_encoder returned {rc}")
+    try:
+        return np.ctypeslib.as_array(C.cast(out, C.POINTER(C.c_float)), shape=(n.value, 640)).copy()
+    finally:
+        _libc.free(out)
+
+
+class _QuantA(C.Structure):   # csrc/phonon2.h:432-436
+    _fields_ = [("q", C.c_void_p), ("scales", C.c_void_p), ("M", C.c_int), ("K", C.c_int)]
+
+
+def _rows_fn(L, name, argtypes):
+    fn = getattr(L, name)
+    fn.argtypes = argtypes
+    fn.restype = None
+    return fn
+
+
+def ref_layer_norm_rows(x, gamma, beta):
+    """The reference's p2_layer_norm_rows (csrc/tensor_ops.c:298-303)."""
+    x = np.ascontiguousarray(x, np.float32)
+    out = np.empty_like(x)
+    _rows_fn(ref(), "p2_layer_norm_rows", [_f32p, _f32p, _f32p, _f32p, C.c_int, C.c_int])(
+        x, np.ascontiguousarray(gamma, np.float32), np.ascontiguousarray(beta, np.float32), out, x.shape[0],
+        x.shape[1])
+    return out
+
+
+def ref_softmax_rows(x):
+    """The reference's p2_softmax_rows (csrc/tensor_ops.c:424-428), on a copy."""
+    x = np.array(x, np.float32, order="C")
+    _rows_fn(ref(), "p2_softmax_rows", [_f32p, C.c_int, C.c_int])(x, x.shape[0], x.shape[1])
+    return x
+
+
+def ref_swish(x):
+    """The reference's p2_swish (csrc/tensor_ops.c:481-490), on a copy."""
+    x = np.array(x, np.float32, order="C")
+    _rows_fn(ref(), "p2_swish", [_f32p, C.c_int])(x, x.size)
+    return x
+
+
+def ref_depthwise_conv1d(x_ct, w, b):
+    """The reference's p2_depthwise_conv1d with kernel 9 (csrc/tensor_ops.c:644-649) on channel-major x [C, T]."""
+    x_ct = np.ascontiguousarray(x_ct, np.float32)
+    Cn, T = x_ct.shape
+    out = np.empty_like(x_ct)
+    _rows_fn(ref(), "p2_depthwise_conv1d", [_f32p, _f32p, C.c_void_p, _f32p, C.c_int, C.c_int, C.c_int])(
+        x_ct, np.ascontiguousarray(w, np.float32), None if b is None else np.ascontiguousarray(b, np.float32).ctypes.data,
+        out, Cn, T, 9)
+    return out
+
+
+def _ref_quant_rows(name, x, *extra):
+    L = ref_i8()
+    L.orc_shim_set_mode(2)
+    x = np.ascontiguousarray(x, np.float32)
+    M, K = x.shape
+    qa = _QuantA()
+    L.p2_quant_prepare.argtypes = [C.POINTER(_QuantA), C.c_int, C.c_int]
+    if L.p2_quant_prepare(C.byref(qa), M, K) != 0:
+        raise RuntimeError("p2_quant_prepare declined")
+    fn = getattr(L, name)
+    fn.restype = None
+    if extra:
+        fn.argtypes = [_f32p, _f32p, _f32p, C.POINTER(_QuantA), C.c_int, C.c_int]
+        fn(x, np.ascontiguousarray(extra[0], np.float32), np.ascontiguousarray(extra[1], np.float32), C.byref(qa), M, K)
+    else:
+        fn.argtypes = [_f32p, C.POINTER(_QuantA), C.c_int, C.c_int]
+        fn(x, C.byref(qa), M, K)
+    q = np.ctypeslib.as_array(C.cast(qa.q, C.POINTER(C.c_int8)), shape=(M, K)).copy()
+    sc = np.ctypeslib.as_array(C.cast(qa.scales, C.POINTER(C.c_float)), shape=(M,)).copy()
+    return q, sc
+
+
+def ref_layer_norm_quant_rows(x, gamma, beta):
+    """The reference's p2_layer_norm_quant_rows (csrc/tensor_ops.c:329-350), quantiser restated."""
+    return _ref_quant_rows("p2_layer_norm_quant_rows", x, gamma, beta)
+
+
+def ref_swish_quant_rows(h):
+    """The reference's p2_swish_quant_rows (csrc/tensor_ops.c:492-511), quantiser restated."""
+    return _ref_quant_rows("p2_swish_quant_rows", h)
 
 
 def cpu_cores() -> int:

@@ -63,6 +63,24 @@ SIGNATURES = {
     "p2cu_sgemm": (_i, [_i, _i, _i, _i, _i, _f, _vp, _i, _vp, _i, _f, _vp, _i, _vp]),
     "p2cu_fv_pack_codes": (_i, [C.POINTER(P2cuFiveValue), _vp, _vp]),
     "p2cu_sgemm_fvb_noalloc": (_i, [_i, _i, _i, _f, _vp, _i, C.POINTER(P2cuFiveValue), _i, _f, _vp, _i, _vp]),
+    "p2cu_layer_norm_rows": (_i, [_vp, _vp, _vp, _vp, _i, _i, _vp]),
+    "p2cu_layer_norm_quant_rows": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _vp]),
+    "p2cu_swish": (_i, [_vp, _sz, _vp]),
+    "p2cu_swish_quant_rows": (_i, [_vp, _vp, _vp, _i, _i, _vp]),
+    "p2cu_softmax_rows": (_i, [_vp, _i, _i, _vp]),
+    "p2cu_depthwise_conv1d_rows": (_i, [_vp, _vp, _vp, _vp, _i, _i, _vp]),
+    "p2cu_model_upload": (_i, [_vp, _i, C.POINTER(_vp)]),
+    "p2cu_model_free": (None, [_vp]),
+    "p2cu_model_bytes": (_sz, [_vp]),
+    "p2cu_encoder_create": (_i, [_vp, C.POINTER(_i), _i, _i, _i, _i, C.POINTER(_vp)]),
+    "p2cu_encoder_destroy": (None, [_vp]),
+    "p2cu_encoder_frames": (_i, [_vp, _i]),
+    "p2cu_encoder_mel": (_vp, [_vp]),
+    "p2cu_encoder_out": (_vp, [_vp]),
+    "p2cu_encoder_run": (_i, [_vp, _vp]),
+    # include/phonon2.h: the reference's encoder entry points
+    "p2_encoder": (_i, [_vp, _vp, _i, C.POINTER(_vp), C.POINTER(_i)]),
+    "p2_encoder_chunked": (_i, [_vp, _vp, _i, C.POINTER(_vp), C.POINTER(_i)]),
     # include/blas.h: the reference's host-pointer ABI
     "p2_sgemm": (None, [_i, _i, _i, _i, _i, _f, _vp, _i, _vp, _i, _f, _vp, _i]),
     "p2_sgemm_st": (None, [_i, _i, _i, _i, _i, _f, _vp, _i, _vp, _i, _f, _vp, _i]),
@@ -209,3 +227,75 @@ def host_sgemm(transA, transB, A, B, out, alpha=1.0, beta=0.0):
     lib().p2_sgemm(P2_TRANS if transA else P2_NO_TRANS, P2_TRANS if transB else P2_NO_TRANS, M, N, K, alpha,
                    _addr(A), A.strides[0] // 4, _addr(B), B.strides[0] // 4, beta, _addr(out), out.strides[0] // 4)
     return out
+
+
+# ---- the encoder (include/p2cuda.h device plans, include/phonon2.h host entry) --------------------------------------
+
+class DeviceModel:
+    """p2cu_model_upload: a P2Model's encoder weights on the current device."""
+
+    def __init__(self, model_struct, codes: bool = False):
+        self.ptr = C.c_void_p()
+        check(lib().p2cu_model_upload(C.addressof(model_struct), 1 if codes else 0, C.byref(self.ptr)))
+
+    @property
+    def nbytes(self) -> int:
+        return lib().p2cu_model_bytes(self.ptr)
+
+    def close(self) -> None:
+        if self.ptr:
+            lib().p2cu_model_free(self.ptr)
+            self.ptr = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class Encoder:
+    """p2cu_encoder_create: a plan (buffers + captured graph) for a batch of windows of n_frames mel frames each."""
+
+    def __init__(self, model: DeviceModel, n_frames, mode: int = INT8W, chunk: int = 0, overlap: int = 8):
+        self.model = model   # keeps the weights alive
+        self.n_frames = [int(n) for n in n_frames]
+        arr = (C.c_int * len(self.n_frames))(*self.n_frames)
+        self.ptr = C.c_void_p()
+        check(lib().p2cu_encoder_create(model.ptr, arr, len(self.n_frames), mode, chunk, overlap, C.byref(self.ptr)))
+        L = lib()
+        self.frames = [L.p2cu_encoder_frames(self.ptr, w) for w in range(len(self.n_frames))]
+        self.total_frames = L.p2cu_encoder_frames(self.ptr, -1)
+        self.mel_ptr = L.p2cu_encoder_mel(self.ptr)
+        self.out_ptr = L.p2cu_encoder_out(self.ptr)
+
+    def run(self, stream=None) -> None:
+        check(lib().p2cu_encoder_run(self.ptr, stream_ptr(stream)))
+
+    def close(self) -> None:
+        if self.ptr:
+            lib().p2cu_encoder_destroy(self.ptr)
+            self.ptr = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def host_encoder(model_struct, mel, chunked: bool = False):
+    """p2_encoder (or p2_encoder_chunked) on a host mel array [n_frames, 128]: the [T', 640] frames as numpy."""
+    import numpy as _np
+    mel = _np.ascontiguousarray(mel, dtype=_np.float32)
+    out = C.c_void_p()
+    n = C.c_int()
+    fn = lib().p2_encoder_chunked if chunked else lib().p2_encoder
+    rc = fn(C.addressof(model_struct), mel.ctypes.data, mel.shape[0], C.byref(out), C.byref(n))
+    if rc != 0:
+        raise Error(rc, "p2_encoder failed (see stderr)")
+    try:
+        res = _np.ctypeslib.as_array(C.cast(out, C.POINTER(C.c_float)), shape=(n.value, 640)).copy()
+    finally:
+        C.CDLL(None).free(out)
+    return res

@@ -10,6 +10,7 @@
 #include "p2cuda.h"
 #include "fv_gemm.h"
 #include "kernels.h"
+#include "gemm.h"
 
 namespace {
 
@@ -223,7 +224,7 @@ int run_i8(int M, int N, int K, float alpha, const int8_t* q, const float* a_sca
 
 int run_exact(int M, int N, int K, float alpha, const float* A, int lda, int transA, const P2cuFiveValue* B,
               const int8_t* q8, const float* scales, const float* Bf, int ldb, int transB, float beta, float* C,
-              int ldc, cudaStream_t s, const char* who) {
+              int ldc, cudaStream_t s, const char* who, const p2cu::Epilogue* epi = nullptr) {
     int rc = check_gemm_common(M, N, K, C, ldc, who);
     if (rc) return rc;
     if (M == 0 || N == 0) return P2CU_OK;
@@ -233,6 +234,11 @@ int run_exact(int M, int N, int K, float alpha, const float* A, int lda, int tra
     p.M = M; p.N = N; p.K = K; p.alpha = alpha; p.beta = beta;
     p.A = A; p.lda = lda; p.transA = transA; p.ldb = ldb; p.transB = transB; p.C = C; p.ldc = ldc;
     p.vec_store = (N % 4 == 0) && (ldc % 4 == 0) && aligned16(C);
+    if (epi) {
+        if (epi->residual && beta != 0.f) return fail(P2CU_EINVAL, "%s: a residual epilogue needs beta == 0", who);
+        if (epi->residual && alpha == 0.f) return fail(P2CU_EINVAL, "%s: a residual epilogue needs alpha != 0", who);
+        p.bias = epi->bias; p.relu = epi->relu; p.residual = epi->residual; p.res_alpha = epi->res_alpha;
+    }
     if (B) {
         if (N % 16) return fail(P2CU_EINVAL, "%s: N = %d is not a multiple of 16", who, N);
         if (B->K != K || B->N != N) return fail(P2CU_EINVAL, "%s: weight is [%d, %d], GEMM wants [%d, %d]", who, B->K,
@@ -259,6 +265,32 @@ int run_exact(int M, int N, int K, float alpha, const float* A, int lda, int tra
 namespace p2cu {
 // For the library's other translation units: set the text p2cu_last_error() returns on this thread.
 void set_error_message(int code, const char* msg) { fail(code, "%s", msg); }
+
+int fail_fmt(int code, const char* fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_msg, sizeof(g_msg), fmt, ap);
+    va_end(ap);
+    return code;
+}
+
+int cuda_error(cudaError_t e, const char* what) { return cuda_fail(e, what); }
+
+uint32_t* device_error_word() { return dev_err_ptr(); }
+
+size_t gemm_split_bytes(int M, int N, int K) { return split_bytes(M, N, K); }
+
+int gemm_i8(int M, int N, int K, float alpha, const int8_t* q, const float* a_scales, const P2cuFiveValue* B,
+            const int8_t* q8, const float* scales, int ldb, int mode, float beta, float* C, int ldc, void* ws,
+            size_t ws_bytes, cudaStream_t s, const char* who) {
+    return run_i8(M, N, K, alpha, q, a_scales, B, q8, scales, ldb, mode, beta, C, ldc, ws, ws_bytes, s, who);
+}
+
+int gemm_exact(int M, int N, int K, float alpha, const float* A, int lda, int transA, const P2cuFiveValue* B,
+               const int8_t* q8, const float* scales, const float* Bf, int ldb, int transB, float beta, float* C,
+               int ldc, const Epilogue* epi, cudaStream_t s, const char* who) {
+    return run_exact(M, N, K, alpha, A, lda, transA, B, q8, scales, Bf, ldb, transB, beta, C, ldc, s, who, epi);
+}
 }  // namespace p2cu
 
 extern "C" {

@@ -74,6 +74,9 @@ const char *p2_gemm_mode(void)
 
 int p2_gemm_exact(void) { return gemm_mode() == P2CU_EXACT; }
 
+/* For the library's encoder entry points (encoder_host.cu): the mode in P2CU_* numbering. Not exported. */
+int p2b_gemm_mode(void) { return gemm_mode(); }
+
 /* ---- per-thread context ---- */
 
 typedef struct {
@@ -140,6 +143,14 @@ static void *grow(void **p, size_t *cap, size_t need, const char *who)
     check_cuda(cudaMalloc(p, n), who);
     *cap = n;
     return *p;
+}
+
+/* The GPU the calling thread's calls run on (p2_b200_set_device, else the current device). Not exported. */
+int p2b_thread_device(void)
+{
+    int d = t_device;
+    if (d < 0 && cudaGetDevice(&d) != cudaSuccess) d = 0;
+    return d;
 }
 
 int p2_b200_set_device(int device)
@@ -277,8 +288,11 @@ static Entry *table_entry(const signed char *B, const float *scales, int K, int 
     return e;
 }
 
+void p2b_release_encoder_models(void);   /* encoder_host.cu */
+
 void p2_b200_release_weights(void)
 {
+    p2b_release_encoder_models();
     pthread_mutex_lock(&g_reg_mu);
     int prev = 0;
     cudaGetDevice(&prev);

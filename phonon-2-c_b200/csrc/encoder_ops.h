@@ -1,0 +1,76 @@
+// encoder_ops.h - launch interfaces of the FastConformer encoder's memory-bound ops (encoder_ops.cu). Internal to
+// the library. Activations are row-major [rows][features]; a batch of windows is stacked along the rows and every
+// op that looks across rows (convolutions over time, attention) stops at window edges, found through prefix tables
+// of row offsets in device memory.
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace p2cu {
+
+// LayerNorm (eps 1e-5) of each row; into `out` (fp32, may alias x) or, with q != nullptr, quantised per row into
+// int8 q [rows][D] with one scale per row (the reference's quantiser).
+cudaError_t ln_rows_launch(const float* x, int ldx, const float* gamma, const float* beta, float* out, int ldo,
+                           int8_t* q, float* qscale, int rows, int D, cudaStream_t s);
+
+// SiLU of each row, into `out` (fp32, may alias h) or quantised into q / qscale.
+cudaError_t swish_rows_launch(const float* h, int ldh, float* out, int ldo, int8_t* q, float* qscale, int rows,
+                              int len, cudaStream_t s);
+
+// Elementwise SiLU of n values in place (p2_swish).
+cudaError_t swish_launch(float* x, size_t n, cudaStream_t s);
+
+// Plain softmax of each row in place (p2_softmax_rows).
+cudaError_t softmax_rows_launch(float* x, int rows, int len, cudaStream_t s);
+
+// GLU over the channel axis: gated[r][d] = pw1[r][d] * sigmoid(pw1[r][D + d]).
+cudaError_t glu_rows_launch(const float* pw1, float* gated, int rows, int D, cudaStream_t s);
+
+// Depthwise conv over time (kernel 9, padding 4 inside each window) + bias, then SiLU when `swish`; into fp32 `out`
+// or quantised into q / qscale. row_off: n_win + 1 prefix offsets of the windows' rows (NULL: all rows are one
+// window). b may be NULL (no bias).
+cudaError_t dwconv_swish_launch(const float* gated, const float* w, const float* b, const int* row_off, int n_win,
+                                float* out, int8_t* q, float* qscale, int rows, int D, cudaStream_t s,
+                                bool swish = true);
+
+// dst[r] = src[map[r]] for rows of `cols` floats.
+cudaError_t gather_rows_launch(float* dst, const float* src, const int* map, int rows, int cols, cudaStream_t s);
+
+// Subsampling, stage 1: Conv2d(1 -> C, 3x3, stride 2, pad 1) + ReLU over each window's [n_mel x 128] mel plane.
+// mel_off / h1_off: prefix offsets (mel rows, output rows) per window. Output [rows1][W1][C].
+cudaError_t sub_conv0_launch(const float* mel, const int* mel_off, const int* h1_off, int n_win, const float* w,
+                             const float* b, float* out, int rows1, int W_in, int C, cudaStream_t s);
+
+// Subsampling, depthwise Conv2d(C, 3x3, stride 2, pad 1) + bias over each window: [rows_in][W_in][C] ->
+// [rows_out][W_out][C].
+cudaError_t sub_dwconv_launch(const float* in, const int* in_off, const int* out_off, int n_win, const float* w,
+                              const float* b, float* out, int rows_out, int W_in, int C, cudaStream_t s);
+
+// [rows][W][C] -> [rows][C * W] (channel-major within a frame).
+cudaError_t sub_flatten_launch(const float* in, float* out, int rows, int W, int C, cudaStream_t s);
+
+// x[r][n] += b[n].
+cudaError_t bias_rows_launch(float* x, const float* b, int rows, int N, cudaStream_t s);
+
+// One SIMT fp32 GEMM problem of a group launch: C[m][n] = sum_k (A[m][k] + a_bias[k]) * B[k][n], one FMA chain
+// per output in k order (the reference's fp32 sgemm). Offsets are in elements from the launch's base pointers.
+struct GemmGroup {
+    int M, N, K, tile0;
+    long long a_off, b_off, c_off;
+    int lda, ldb, ldc;
+    int bias_off;   // offset into the launch's a_bias vector, or -1
+};
+
+// All groups in one launch; B is [k][n] (transB == 0) or [n][k] (transB == 1).
+cudaError_t group_gemm_launch(const GemmGroup* groups, int n_groups, int total_tiles, const float* A, const float* B,
+                              float* C, const float* a_bias, int transB, cudaStream_t s);
+int group_gemm_tiles(int M, int N);
+
+// Attention scores of every (window, head, query) row, in place in S_ac: x_j = (ac[i][j] + bd[i][T-1-i+j]) * scale,
+// then softmax over j. srow_off: prefix offsets of the H*T rows per window; s_off / b_off: element offsets of each
+// window's S_ac / S_bd blocks; Tw: frames per window.
+cudaError_t attn_softmax_launch(float* s_ac, const float* s_bd, const int* srow_off, const long long* s_off,
+                                const long long* b_off, const int* Tw, int n_win, int H, int rows, float scale,
+                                cudaStream_t s);
+
+}  // namespace p2cu

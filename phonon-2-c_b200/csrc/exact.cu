@@ -129,6 +129,18 @@ __global__ void __launch_bounds__(256) exact_gemm_kernel(ExactParams p) {
         if (m >= p.M) continue;
         float* crow = p.C + static_cast<size_t>(m) * p.ldc;
         const int na = n0 + 4 * tx, nb = n0 + 64 + 4 * tx;
+        if (p.bias || p.relu || p.residual) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int n = j < 4 ? na + j : nb + j - 4;
+                if (n >= p.N) continue;
+                float v = acc[i][j];
+                if (p.bias) v = __fadd_rn(v, p.bias[n]);
+                if (p.relu) v = v > 0.f ? v : 0.f;
+                if (p.residual) v = __fmaf_rn(v, p.res_alpha, crow[n]);
+                acc[i][j] = v;
+            }
+        }
         if (p.vec_store) {   // N % 4 == 0, ldc % 4 == 0 and C 16-byte aligned
             if (na < p.N) *reinterpret_cast<float4*>(crow + na) = make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
             if (nb < p.N) *reinterpret_cast<float4*>(crow + nb) = make_float4(acc[i][4], acc[i][5], acc[i][6], acc[i][7]);

@@ -1,0 +1,38 @@
+// gemm.h - the GEMM entry points and error helpers api.cu offers the library's other translation units.
+#pragma once
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+#include "p2cuda.h"
+
+namespace p2cu {
+
+// Optional epilogue of the exact (fp32) GEMM: + bias[n], then ReLU, then C = fma(result, res_alpha, C).
+struct Epilogue {
+    const float* bias = nullptr;
+    int relu = 0;
+    int residual = 0;
+    float res_alpha = 1.0f;
+};
+
+// Set p2cu_last_error()'s text for this thread and return `code`.
+int fail_fmt(int code, const char* fmt, ...);
+int cuda_error(cudaError_t e, const char* what);
+void set_error_message(int code, const char* msg);
+uint32_t* device_error_word();
+
+// Bytes of K-block slices the tensor-core GEMM needs for K > 1024 (0 otherwise).
+size_t gemm_split_bytes(int M, int N, int K);
+
+// The tensor-core GEMM on quantised rows q / a_scales; B five-value (planes or cached codes) or q8 / scales an int8
+// table. mode P2CU_INT8 or P2CU_INT8W for five-value weights.
+int gemm_i8(int M, int N, int K, float alpha, const int8_t* q, const float* a_scales, const P2cuFiveValue* B,
+            const int8_t* q8, const float* scales, int ldb, int mode, float beta, float* C, int ldc, void* ws,
+            size_t ws_bytes, cudaStream_t s, const char* who);
+
+// The exact fp32 GEMM (one FMA chain per output) on B five-value, an int8 table or an fp32 matrix.
+int gemm_exact(int M, int N, int K, float alpha, const float* A, int lda, int transA, const P2cuFiveValue* B,
+               const int8_t* q8, const float* scales, const float* Bf, int ldb, int transB, float beta, float* C,
+               int ldc, const Epilogue* epi, cudaStream_t s, const char* who);
+
+}  // namespace p2cu

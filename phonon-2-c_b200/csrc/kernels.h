@@ -19,6 +19,12 @@ struct ExactParams {
     int ldb;
     float* C; int ldc;
     int vec_store;
+    // Epilogue, in this order: + bias[n] (a separate rounded add, as the reference's bias loops), ReLU, then
+    // C = fma(result, res_alpha, C) (the reference's residual axpy, csrc/encoder.c:252-275); beta must be 0 with it.
+    const float* bias;
+    int relu;
+    int residual;
+    float res_alpha;
 };
 
 cudaError_t quant_rows_launch(const float* A, int M, int K, int lda, int8_t* q, float* scales, cudaStream_t stream);

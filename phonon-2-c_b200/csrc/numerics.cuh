@@ -1,0 +1,73 @@
+// numerics.cuh - device helpers shared by the kernels that restate the reference's fp32 arithmetic.
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace p2cu {
+
+// One value of the reference's per-row int8 quantisation (csrc/blas.c:1123-1131): saturate(round_half_even(x * inv)).
+__device__ __forceinline__ int8_t quant_one(float x, float inv) {
+    int v = __float2int_rn(__fmul_rn(x, inv));
+    v = v > 127 ? 127 : (v < -128 ? -128 : v);
+    return static_cast<int8_t>(v);
+}
+
+// The reference's scale for a row with maximum magnitude amax: amax / 127, or 1 for an all-zero row.
+__device__ __forceinline__ float quant_scale(float amax) { return amax > 0.f ? __fdiv_rn(amax, 127.0f) : 1.0f; }
+
+// exp(x) as the reference's AVX2 path evaluates it (csrc/tensor_ops.c:154-172): clamp to [-87, 87], k = round(x *
+// log2 e), r = x - k * ln 2, a degree-5 Taylor polynomial in r by Horner's rule, times 2^k built in the exponent
+// bits. The compiled reference fuses r into one fused multiply-subtract, as here.
+__device__ __forceinline__ float exp_poly(float x) {
+    x = fminf(fmaxf(x, -87.0f), 87.0f);
+    const float kf = rintf(__fmul_rn(x, 1.44269504088896341f));
+    const int ki = static_cast<int>(kf);
+    const float r = __fmaf_rn(-kf, 0.69314718055994529f, x);
+    float y = 1.0f / 120.0f;
+    y = __fmaf_rn(y, r, 1.0f / 24.0f);
+    y = __fmaf_rn(y, r, 1.0f / 6.0f);
+    y = __fmaf_rn(y, r, 0.5f);
+    y = __fmaf_rn(y, r, 1.0f);
+    y = __fmaf_rn(y, r, 1.0f);
+    return __fmul_rn(y, __int_as_float((ki + 127) << 23));
+}
+
+// SiLU as the reference's vector loop computes it (csrc/tensor_ops.c:450-458): v * (1 / (1 + exp(0 - v))).
+__device__ __forceinline__ float swish1(float v) {
+    const float e = exp_poly(__fsub_rn(0.0f, v));
+    return __fmul_rn(v, __fdiv_rn(1.0f, __fadd_rn(1.0f, e)));
+}
+
+// Sum of the eight lanes of an 8-lane group in the order of the reference's AVX2 horizontal sum
+// (csrc/tensor_ops.c:182-190): ((v0 + v4) + (v2 + v6)) + ((v1 + v5) + (v3 + v7)); every lane of the group gets it.
+__device__ __forceinline__ float hsum8(float v) {
+    v = __fadd_rn(v, __shfl_down_sync(0xffffffffu, v, 4, 8));
+    v = __fadd_rn(v, __shfl_down_sync(0xffffffffu, v, 2, 8));
+    v = __fadd_rn(v, __shfl_down_sync(0xffffffffu, v, 1, 8));
+    return __shfl_sync(0xffffffffu, v, 0, 8);
+}
+
+__device__ __forceinline__ float max8(float v) {
+    v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 4, 8));
+    v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 2, 8));
+    v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 1, 8));
+    return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// The window that row r belongs to: the largest w with off[w] <= r (off holds n + 1 prefix offsets).
+__device__ __forceinline__ int find_window(const int* __restrict__ off, int n, int r) {
+    int lo = 0, hi = n - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (off[mid] <= r) lo = mid; else hi = mid - 1;
+    }
+    return lo;
+}
+
+}  // namespace p2cu

@@ -5,15 +5,10 @@
 #include <cstdint>
 #include <cuda_runtime.h>
 #include "kernels.h"
+#include "numerics.cuh"
 #include "ptx.cuh"
 
 namespace p2cu {
-
-__device__ __forceinline__ int8_t quant_one(float x, float inv) {
-    int v = __float2int_rn(__fmul_rn(x, inv));
-    v = v > 127 ? 127 : (v < -128 ? -128 : v);
-    return static_cast<int8_t>(v);
-}
 
 // One CTA of 128 threads per row. Rows up to 4096 wide with K % 4 == 0 and 16-byte aligned rows stay in registers
 // (one read of A); other shapes take a strided two-pass path.

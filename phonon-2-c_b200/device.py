@@ -37,3 +37,17 @@ class DeviceFiveValue:
     @property
     def plane_bytes(self) -> int:
         return self.signs.numel() + self.flags.numel() + 4 * (self.lo.numel() + self.hi.numel())
+
+
+class _CudaArray:
+    """A raw device pointer presented through __cuda_array_interface__ (no copy, no ownership)."""
+
+    def __init__(self, ptr: int, shape, typestr: str):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr, "data": (int(ptr), False),
+                                         "version": 3, "strides": None}
+
+
+def device_view(ptr: int, shape, dtype=torch.float32, device="cuda"):
+    """A torch tensor over device memory the library owns (a plan's input or output buffer); valid while it lives."""
+    typestr = {torch.float32: "<f4", torch.int8: "|i1", torch.uint8: "|u1", torch.int32: "<i4"}[dtype]
+    return torch.as_tensor(_CudaArray(ptr, shape, typestr), device=device)

@@ -1,0 +1,210 @@
+"""The encoder on the device against phonon-2-c's own encoder, through the C ABI.
+
+Oracles: exact mode is phonon-2-c's p2_encoder compiled from its sources (oracle/_ref/libphonon2_ref.so, whose x86
+build is the exact path); the int8 modes are the same encoder sources with the int8 GEMM entry points restated
+(oracle/_ref/libphonon2_ref_i8.so), so the reference's int8 control flow - rows quantised as they are produced,
+residuals added in the GEMM epilogues - runs on x86.
+
+Tolerances. The five-value GEMMs are bit-exact (tests/test_gemm_gpu.py); the encoder as a whole cannot be, because the
+compiled reference's LayerNorm takes 1/sqrt from an approximate reciprocal square root refined by one Newton step and
+some of its exps from a vectorised libm, both host-CPU specific. So:
+  * exact mode: max |device - reference| <= 1e-4 * max |reference| over the [T', 640] output (the north star's 1e-4);
+  * int8 modes: statistical (see the test's docstring): an ulp-level difference before a quantiser can move one int8
+    value by a whole step, which the following layers carry and multiply;
+  * the row ops: allclose at a few fp32 ulp, quantised rows equal except for rare one-step differences.
+Batched windows are compared bit for bit with the same windows run one at a time (every GEMM is row-independent and
+every cross-row op stops at window edges).
+"""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+EXACT_TOL = 1e-4
+
+
+@pytest.fixture(scope="module")
+def model(pkg):
+    from phonon2_b200 import model as M
+    return M.SyntheticModel(seed=7)
+
+
+@pytest.fixture(scope="module")
+def dev_model(pkg, cuda, model):
+    d = pkg.DeviceModel(model.struct)
+    yield d
+    d.close()
+
+
+def _run(pkg, torch, dev_model, mels, mode, chunk=0, overlap=8):
+    """One plan over the windows `mels`: the per-window [T', 640] outputs."""
+    from phonon2_b200.device import device_view
+    enc = pkg.Encoder(dev_model, [m.shape[0] for m in mels], mode, chunk, overlap)
+    stacked = np.ascontiguousarray(np.concatenate(mels), np.float32)
+    device_view(enc.mel_ptr, stacked.shape).copy_(torch.from_numpy(stacked))
+    enc.run()
+    pkg.check_device()
+    out = device_view(enc.out_ptr, (enc.total_frames, 640)).cpu().numpy()
+    offs = np.cumsum([0] + enc.frames)
+    res = [out[offs[i]:offs[i + 1]] for i in range(len(mels))]
+    enc.close()
+    return res
+
+
+def _rel(got, ref):
+    return float(np.abs(got - ref).max() / np.abs(ref).max())
+
+
+# ---- the row ops against the reference's own functions -------------------------------------------------------------
+
+def test_layer_norm_rows(pkg, orc, cuda):
+    import torch
+    rng = np.random.default_rng(1)
+    x = (rng.standard_normal((300, 1024)) * 3 + 0.5).astype(np.float32)
+    g = (1 + 0.02 * rng.standard_normal(1024)).astype(np.float32)
+    b = (0.02 * rng.standard_normal(1024)).astype(np.float32)
+    xd, gd, bd = (torch.from_numpy(a).to(cuda) for a in (x, g, b))
+    out = torch.empty_like(xd)
+    pkg.check(pkg.lib().p2cu_layer_norm_rows(xd.data_ptr(), gd.data_ptr(), bd.data_ptr(), out.data_ptr(), 300, 1024,
+                                             None))
+    ref = orc.ref_layer_norm_rows(x, g, b)
+    np.testing.assert_allclose(out.cpu().numpy(), ref, rtol=2e-6, atol=2e-6)
+    # in place (p2_layer_norm_rows_inplace)
+    pkg.check(pkg.lib().p2cu_layer_norm_rows(xd.data_ptr(), gd.data_ptr(), bd.data_ptr(), xd.data_ptr(), 300, 1024,
+                                             None))
+    assert np.array_equal(xd.cpu().numpy(), out.cpu().numpy())
+
+
+def _quant_close(q, s, rq, rs):
+    np.testing.assert_allclose(s, rs, rtol=2e-6)
+    d = np.abs(q.astype(np.int32) - rq.astype(np.int32))
+    assert d.max() <= 1 and (d != 0).mean() < 1e-3, (d.max(), (d != 0).mean())
+
+
+def test_layer_norm_quant_rows(pkg, orc, cuda):
+    import torch
+    rng = np.random.default_rng(2)
+    x = (rng.standard_normal((200, 1024)) * 2).astype(np.float32)
+    g = (1 + 0.02 * rng.standard_normal(1024)).astype(np.float32)
+    b = (0.02 * rng.standard_normal(1024)).astype(np.float32)
+    xd, gd, bd = (torch.from_numpy(a).to(cuda) for a in (x, g, b))
+    q = torch.empty((200, 1024), dtype=torch.int8, device=cuda)
+    s = torch.empty(200, dtype=torch.float32, device=cuda)
+    pkg.check(pkg.lib().p2cu_layer_norm_quant_rows(xd.data_ptr(), gd.data_ptr(), bd.data_ptr(), q.data_ptr(),
+                                                   s.data_ptr(), 200, 1024, None))
+    rq, rs = orc.ref_layer_norm_quant_rows(x, g, b)
+    _quant_close(q.cpu().numpy(), s.cpu().numpy(), rq, rs)
+
+
+def test_swish_and_swish_quant(pkg, orc, cuda):
+    import torch
+    rng = np.random.default_rng(3)
+    h = (rng.standard_normal((64, 4096)) * 4).astype(np.float32)
+    hd = torch.from_numpy(h.copy()).to(cuda)
+    pkg.check(pkg.lib().p2cu_swish(hd.data_ptr(), h.size, None))
+    np.testing.assert_allclose(hd.cpu().numpy(), orc.ref_swish(h), rtol=1e-6, atol=1e-7)
+    hd = torch.from_numpy(h).to(cuda)
+    q = torch.empty((64, 4096), dtype=torch.int8, device=cuda)
+    s = torch.empty(64, dtype=torch.float32, device=cuda)
+    pkg.check(pkg.lib().p2cu_swish_quant_rows(hd.data_ptr(), q.data_ptr(), s.data_ptr(), 64, 4096, None))
+    rq, rs = orc.ref_swish_quant_rows(h)
+    _quant_close(q.cpu().numpy(), s.cpu().numpy(), rq, rs)
+
+
+@pytest.mark.parametrize("length", [375, 38, 64, 7])
+def test_softmax_rows(pkg, orc, cuda, length):
+    import torch
+    x = (np.random.default_rng(length).standard_normal((96, length)) * 4).astype(np.float32)
+    xd = torch.from_numpy(x.copy()).to(cuda)
+    pkg.check(pkg.lib().p2cu_softmax_rows(xd.data_ptr(), 96, length, None))
+    np.testing.assert_allclose(xd.cpu().numpy(), orc.ref_softmax_rows(x), rtol=2e-6, atol=1e-8)
+
+
+@pytest.mark.parametrize("T", [375, 38, 7, 13, 1])
+def test_depthwise_conv1d(pkg, orc, cuda, T):
+    import torch
+    rng = np.random.default_rng(T)
+    Cn = 1024
+    x = rng.standard_normal((T, Cn)).astype(np.float32)   # time-major
+    w = (rng.standard_normal((Cn, 9)) / 3).astype(np.float32)
+    b = (0.02 * rng.standard_normal(Cn)).astype(np.float32)
+    xd, wd, bd = (torch.from_numpy(a).to(cuda) for a in (x, w, b))
+    out = torch.empty_like(xd)
+    pkg.check(pkg.lib().p2cu_depthwise_conv1d_rows(xd.data_ptr(), wd.data_ptr(), bd.data_ptr(), out.data_ptr(), Cn,
+                                                   T, None))
+    ref = orc.ref_depthwise_conv1d(x.T, w, b).T
+    np.testing.assert_allclose(out.cpu().numpy(), ref, rtol=1e-6, atol=1e-6)
+
+
+# ---- the encoder ---------------------------------------------------------------------------------------------------
+
+@pytest.mark.parametrize("n_mel", [300, 3000])   # config 4 (T' = 38) and config 2 (T' = 375)
+def test_encoder_exact_matches_reference(pkg, orc, cuda, model, dev_model, n_mel):
+    import torch
+    from phonon2_b200 import model as M
+    mel = M.mel(n_mel, seed=n_mel)
+    got, = _run(pkg, torch, dev_model, [mel], pkg.EXACT)
+    ref = orc.ref_encoder(model.struct, mel, "exact")
+    assert got.shape == ref.shape == (M.frames_after_subsampling(n_mel), 640)
+    assert _rel(got, ref) <= EXACT_TOL, _rel(got, ref)
+
+
+@pytest.mark.parametrize("mode", ["int8w", "int8"])
+def test_encoder_int8_matches_reference_control_flow(pkg, orc, cuda, model, dev_model, mode):
+    """Statistical parity: quantisation makes the int8 encoder sensitive to ulp-level differences before a quantiser
+    (one flipped rounding moves an activation by a whole step, and 24 blocks carry and multiply such steps), so two
+    valid int8 encoders - the reference built on two different CPUs, for one - agree only to about the size of the
+    quantisation noise itself. The device's int8 output must sit within that envelope of the reference's int8 output
+    (the distance between the reference's int8 and exact outputs), and correlate with it almost perfectly."""
+    import torch
+    from phonon2_b200 import model as M
+    mel = M.mel(300, seed=11)
+    got, = _run(pkg, torch, dev_model, [mel], pkg.MODES[mode])
+    ref = orc.ref_encoder(model.struct, mel, mode)
+    exact = orc.ref_encoder(model.struct, mel, "exact")
+    noise = _rel(ref, exact)
+    print(f"{mode}: device vs reference {_rel(got, ref):.3e}, device vs exact {_rel(got, exact):.3e}, "
+          f"reference int8 vs exact {noise:.3e}, corr {np.corrcoef(got.ravel(), ref.ravel())[0, 1]:.6f}")
+    assert noise < 0.1
+    assert _rel(got, ref) <= 2 * noise and _rel(got, exact) <= 2 * noise
+    assert np.corrcoef(got.ravel(), ref.ravel())[0, 1] > 0.999
+
+
+@pytest.mark.parametrize("mode", ["int8w", "exact"])
+def test_windows_batched_equal_windows_alone(pkg, cuda, dev_model, mode):
+    import torch
+    from phonon2_b200 import model as M
+    mels = [M.mel(n, seed=n) for n in (300, 251, 333, 17)]
+    together = _run(pkg, torch, dev_model, mels, pkg.MODES[mode])
+    for mel, got in zip(mels, together):
+        alone, = _run(pkg, torch, dev_model, [mel], pkg.MODES[mode])
+        assert np.array_equal(got.view(np.uint32), alone.view(np.uint32))
+
+
+def test_chunked_encoder_matches_reference(pkg, orc, cuda, model, dev_model):
+    import torch
+    from phonon2_b200 import model as M
+    mel = M.mel(4500, seed=3)   # T' = 563 > 500: the reference chunks (400 frames + 8 of context each side)
+    ref = orc.ref_encoder(model.struct, mel, "exact")
+    got, = _run(pkg, torch, dev_model, [mel], pkg.EXACT, chunk=400, overlap=8)
+    assert _rel(got, ref) <= EXACT_TOL, _rel(got, ref)
+    full, = _run(pkg, torch, dev_model, [mel], pkg.EXACT)
+    assert _rel(full, ref) > 10 * EXACT_TOL   # the chunk boundaries do change the result
+
+
+def test_host_entry_point_matches_plan(pkg, cuda, model, dev_model):
+    """p2_encoder (host pointers, the reference's signature) gives the plan's output bit for bit."""
+    import torch
+    from phonon2_b200 import model as M
+    mel = M.mel(300, seed=21)
+    got = pkg.host_encoder(model.struct, mel)
+    mode = pkg.MODES["int8w"]   # the host entry's default mode (P2_GEMM unset)
+    plan, = _run(pkg, torch, dev_model, [mel], mode)
+    assert np.array_equal(got.view(np.uint32), plan.view(np.uint32))
+
+
+def test_encoder_argument_errors(pkg, cuda, dev_model):
+    with pytest.raises(pkg.Error):
+        pkg.Encoder(dev_model, [0], pkg.INT8W)
+    with pytest.raises(pkg.Error):
+        pkg.Encoder(dev_model, [300], 7)
