@@ -232,6 +232,8 @@ struct P2cuEncoder {
     long long *d_s_off, *d_b_off;
     p2cu::GemmGroup *g_ac, *g_bd, *g_av;
     int ng = 0, t_ac = 0, t_bd = 0, t_av = 0;
+    int2* att_tiles = nullptr;   // fused attention (every window <= ATT_MAXT frames): (window, first query) per tile
+    int n_att_tiles = 0;
 
     cudaStream_t stream = nullptr;
     cudaGraph_t graph = nullptr;
@@ -324,12 +326,18 @@ int self_attention(P2cuEncoder& e, const DBlock& b, cudaStream_t s) {
         TRY(wmatmul(e, e.lnbuf, e.R, b.qkv, e.big, 1.f, 0.f, nullptr, s, "qkv"));
         TRY(wmatmul(e, e.pe, e.L, b.pos, e.P, 1.f, 0.f, nullptr, s, "pos"));
     }
-    TRYC(p2cu::group_gemm_launch(e.g_ac, e.ng, e.t_ac, e.big, e.big, e.s_ac, b.bias_u, 1, s), "attention ac");
-    TRYC(p2cu::group_gemm_launch(e.g_bd, e.ng, e.t_bd, e.big, e.P, e.s_bd, b.bias_v, 1, s), "attention bd");
-    TRYC(p2cu::attn_softmax_launch(e.s_ac, e.s_bd, e.d_srow_off, e.d_s_off, e.d_b_off, e.d_T, e.n_win, H, e.srows,
-                                   e.scale, s),
-         "attention softmax");
-    TRYC(p2cu::group_gemm_launch(e.g_av, e.ng, e.t_av, e.s_ac, e.big, e.attn, nullptr, 0, s), "attention av");
+    if (e.n_att_tiles) {
+        TRYC(p2cu::attn_fused_launch(e.big, e.P, b.bias_u, b.bias_v, e.d_row_off, e.att_tiles, e.n_att_tiles, e.Tmax,
+                                     e.scale, e.attn, s),
+             "attention");
+    } else {   // windows longer than the fused kernel holds: the products as grouped GEMMs, scores in HBM
+        TRYC(p2cu::group_gemm_launch(e.g_ac, e.ng, e.t_ac, e.big, e.big, e.s_ac, b.bias_u, 1, s), "attention ac");
+        TRYC(p2cu::group_gemm_launch(e.g_bd, e.ng, e.t_bd, e.big, e.P, e.s_bd, b.bias_v, 1, s), "attention bd");
+        TRYC(p2cu::attn_softmax_launch(e.s_ac, e.s_bd, e.d_srow_off, e.d_s_off, e.d_b_off, e.d_T, e.n_win, H,
+                                       e.srows, e.scale, s),
+             "attention softmax");
+        TRYC(p2cu::group_gemm_launch(e.g_av, e.ng, e.t_av, e.s_ac, e.big, e.attn, nullptr, 0, s), "attention av");
+    }
     if (i8) {
         TRYC(p2cu::quant_rows_launch(e.attn, e.R, D, D, e.q, e.qs, s), "attention quant");
         return wmatmul_q8a(e, e.R, b.out, e.x, 1.f, 1.f, s, "out");   // x += attn @ W_o
@@ -511,6 +519,14 @@ int create_plan(const P2cuModel* m, const int* n_frames, int n_mel_win, int mode
         srow_off.push_back(srow_off.back() + H * t);
     }
     e->srows = srow_off.back();
+    const bool fused = e->Tmax <= p2cu::ATT_MAXT;
+    std::vector<int2> att_tiles;
+    if (fused) {
+        for (int w = 0; w < n_win; ++w)
+            for (int q0 = 0; q0 < e->T[w]; q0 += 32) att_tiles.push_back(make_int2(w, q0));
+        e->n_att_tiles = static_cast<int>(att_tiles.size());
+        e->s_total = e->b_total = 0;   // no score matrices in HBM
+    }
     e->ng = static_cast<int>(gac.size());
     e->t_ac = tac; e->t_bd = tbd; e->t_av = tav;
 
@@ -559,6 +575,7 @@ int create_plan(const P2cuModel* m, const int* n_frames, int n_mel_win, int mode
         {reinterpret_cast<void**>(&e->g_ac), gac.size() * sizeof(p2cu::GemmGroup)},
         {reinterpret_cast<void**>(&e->g_bd), gbd.size() * sizeof(p2cu::GemmGroup)},
         {reinterpret_cast<void**>(&e->g_av), gav.size() * sizeof(p2cu::GemmGroup)},
+        {reinterpret_cast<void**>(&e->att_tiles), att_tiles.size() * sizeof(int2)},
     };
     size_t total = 0;
     for (const Slot& sl : slots) total += al256(sl.bytes ? sl.bytes : 1);
@@ -594,9 +611,10 @@ int create_plan(const P2cuModel* m, const int* n_frames, int n_mel_win, int mode
         {e->g_ac, gac.data(), gac.size() * sizeof(p2cu::GemmGroup)},
         {e->g_bd, gbd.data(), gbd.size() * sizeof(p2cu::GemmGroup)},
         {e->g_av, gav.data(), gav.size() * sizeof(p2cu::GemmGroup)},
+        {e->att_tiles, att_tiles.data(), att_tiles.size() * sizeof(int2)},
     };
     for (const Copy& c : copies)
-        if ((ce = cudaMemcpy(c.dst, c.src, c.bytes, cudaMemcpyHostToDevice)) != cudaSuccess) break;
+        if (c.bytes && (ce = cudaMemcpy(c.dst, c.src, c.bytes, cudaMemcpyHostToDevice)) != cudaSuccess) break;
     if (ce == cudaSuccess) ce = cudaMemset(e->mel, 0, static_cast<size_t>(e->mel_rows) * NMEL * f);
     if (ce == cudaSuccess) ce = cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking);
     if (ce == cudaSuccess && mode != P2CU_EXACT)

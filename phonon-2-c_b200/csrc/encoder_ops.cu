@@ -1,11 +1,12 @@
 // encoder_ops.cu - the FastConformer encoder's memory-bound ops on the device.
 //
 // Each kernel restates one of the reference's CPU loops (csrc/encoder.c, csrc/tensor_ops.c) in fp32 with the same
-// order of operations where that order is fixed by the source: LayerNorm's 8-lane sums and horizontal-sum tree, the
-// polynomial exp of the vector loops, the FMA chains of the convolutions in tap order. Where the compiled reference
-// depends on the host CPU (its -ffast-math build computes 1/sqrt with an approximate reciprocal square root refined
-// by one Newton step, and calls a vectorised expf for short tails) these kernels use IEEE operations instead, so
-// they agree with the reference to a few ulp, not bit for bit.
+// operations in the same order where the result depends on it and the order can be reproduced: the polynomial exp of
+// the vector loops, the FMA chains of the convolutions in tap order, the attention products as one FMA chain per
+// output. Sums over a row (LayerNorm, softmax) are tree-ordered: the compiled reference's own results there depend on
+// the host CPU (its -ffast-math build computes 1/sqrt with an approximate reciprocal square root refined by one Newton
+// step, and calls a vectorised expf for short tails), so no order reproduces it bit for bit; these kernels agree with
+// it to an ulp or two.
 //
 // Layout: activations are row-major [rows][features] and a batch of windows is stacked along the rows. Ops that
 // look across rows (convolutions over time, attention) find a row's window in prefix tables of row offsets.
@@ -21,64 +22,135 @@ namespace {
 
 constexpr unsigned FULL = 0xffffffffu;
 
-// ---- LayerNorm (csrc/tensor_ops.c:204-281, AVX2 branch): 8 lanes per row -----------------------------------------
+// ---- LayerNorm (csrc/tensor_ops.c:204-281): mean, variance, y = fma((x - mean) * inv_std, gamma, beta) ---------
 //
-// sum: per lane l, x[l] + x[l + 8] + ... in order, then the horizontal-sum tree, then the D % 8 tail in order;
-// mean = sum / D; var = (same shape over fma(d, d, .)) / D; y = fma((x - mean) * inv_std, gamma, beta).
+// One warp per row with the row held in registers (one read of x, one write of y). The sums are tree-ordered; the
+// reference sums in 8 lanes and takes 1/sqrt from an approximate reciprocal square root plus a Newton step, so the
+// two agree to an ulp or two, not bit for bit, whatever order is used here.
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+__device__ __forceinline__ float4 ln_apply(float4 v, float mean, float inv, float4 g, float4 b) {
+    return make_float4(__fmaf_rn(__fmul_rn(__fsub_rn(v.x, mean), inv), g.x, b.x),
+                       __fmaf_rn(__fmul_rn(__fsub_rn(v.y, mean), inv), g.y, b.y),
+                       __fmaf_rn(__fmul_rn(__fsub_rn(v.z, mean), inv), g.z, b.z),
+                       __fmaf_rn(__fmul_rn(__fsub_rn(v.w, mean), inv), g.w, b.w));
+}
+
+__device__ __forceinline__ float amax4(float4 v) {
+    return fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+}
+
+__device__ __forceinline__ char4 quant4(float4 v, float inv) {
+    char4 c;
+    c.x = quant_one(v.x, inv); c.y = quant_one(v.y, inv); c.z = quant_one(v.z, inv); c.w = quant_one(v.w, inv);
+    return c;
+}
+
+// D = 128 V; 8 rows per 256-thread block.
+template <int V, bool QUANT>
+__global__ void __launch_bounds__(256) ln_warp_kernel(const float* __restrict__ x, int ldx,
+                                                      const float* __restrict__ gamma, const float* __restrict__ beta,
+                                                      float* out, int ldo, int8_t* __restrict__ q,
+                                                      float* __restrict__ qscale, int rows) {
+    constexpr int D = 128 * V;
+    const int lane = threadIdx.x & 31;
+    const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (row >= rows) return;
+    const float4* xr = reinterpret_cast<const float4*>(x + static_cast<size_t>(row) * ldx);
+    float4 v[V];
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+        v[i] = xr[lane + 32 * i];
+        s = __fadd_rn(s, __fadd_rn(__fadd_rn(v[i].x, v[i].y), __fadd_rn(v[i].z, v[i].w)));
+    }
+    const float mean = __fdiv_rn(warp_sum(s), static_cast<float>(D));
+    float var = 0.f;
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+        const float a = __fsub_rn(v[i].x, mean), b = __fsub_rn(v[i].y, mean);
+        const float c = __fsub_rn(v[i].z, mean), d = __fsub_rn(v[i].w, mean);
+        var = __fmaf_rn(a, a, var); var = __fmaf_rn(b, b, var);
+        var = __fmaf_rn(c, c, var); var = __fmaf_rn(d, d, var);
+    }
+    var = __fdiv_rn(warp_sum(var), static_cast<float>(D));
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, 1e-5f)));
+    const float4* g4 = reinterpret_cast<const float4*>(gamma);
+    const float4* b4 = reinterpret_cast<const float4*>(beta);
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+        v[i] = ln_apply(v[i], mean, inv, g4[lane + 32 * i], b4[lane + 32 * i]);
+        amax = fmaxf(amax, amax4(v[i]));
+    }
+    if (!QUANT) {
+        float4* orow = reinterpret_cast<float4*>(out + static_cast<size_t>(row) * ldo);
+#pragma unroll
+        for (int i = 0; i < V; ++i) orow[lane + 32 * i] = v[i];
+        return;
+    }
+    const float scale = quant_scale(warp_max(amax));
+    const float qinv = __fdiv_rn(1.0f, scale);
+    char4* qrow = reinterpret_cast<char4*>(q + static_cast<size_t>(row) * D);
+#pragma unroll
+    for (int i = 0; i < V; ++i) qrow[lane + 32 * i] = quant4(v[i], qinv);
+    if (lane == 0) qscale[row] = scale;
+}
+
+// Any D and alignment: one 256-thread block per row, the row re-read from L1/L2 in each pass.
 template <bool QUANT>
 __global__ void __launch_bounds__(256) ln_rows_kernel(const float* __restrict__ x, int ldx,
                                                       const float* __restrict__ gamma, const float* __restrict__ beta,
                                                       float* out, int ldo, int8_t* __restrict__ q,
-                                                      float* __restrict__ qscale, int rows, int D) {
-    const int vl = threadIdx.x & 7;
-    const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 3;
-    const bool active = row < rows;
-    const float* xr = x + static_cast<size_t>(active ? row : 0) * ldx;
-    const int nv = D & ~7;
-
+                                                      float* __restrict__ qscale, int D) {
+    __shared__ float red[8];
+    const int row = blockIdx.x;
+    const float* xr = x + static_cast<size_t>(row) * ldx;
+    auto block_sum = [&](float v) {
+        v = warp_sum(v);
+        __syncthreads();
+        if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+        __syncthreads();
+        float t = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) t = __fadd_rn(t, red[i]);
+        return t;
+    };
     float s = 0.f;
-    if (active)
-        for (int i = vl; i < nv; i += 8) s = __fadd_rn(s, xr[i]);
-    s = hsum8(s);
-    if (active)
-        for (int i = nv; i < D; ++i) s = __fadd_rn(s, xr[i]);
-    const float mean = __fdiv_rn(s, static_cast<float>(D));
-
-    float v = 0.f;
-    if (active)
-        for (int i = vl; i < nv; i += 8) {
-            const float d = __fsub_rn(xr[i], mean);
-            v = __fmaf_rn(d, d, v);
-        }
-    v = hsum8(v);
-    if (active)
-        for (int i = nv; i < D; ++i) {
-            const float d = __fsub_rn(xr[i], mean);
-            v = __fmaf_rn(d, d, v);
-        }
-    const float var = __fdiv_rn(v, static_cast<float>(D));
+    for (int i = threadIdx.x; i < D; i += 256) s = __fadd_rn(s, xr[i]);
+    const float mean = __fdiv_rn(block_sum(s), static_cast<float>(D));
+    float var = 0.f;
+    for (int i = threadIdx.x; i < D; i += 256) {
+        const float d = __fsub_rn(xr[i], mean);
+        var = __fmaf_rn(d, d, var);
+    }
+    var = __fdiv_rn(block_sum(var), static_cast<float>(D));
     const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, 1e-5f)));
-
+    auto y = [&](int i) { return __fmaf_rn(__fmul_rn(__fsub_rn(xr[i], mean), inv), gamma[i], beta[i]); };
     if (!QUANT) {
-        if (!active) return;
         float* orow = out + static_cast<size_t>(row) * ldo;
-        for (int i = vl; i < D; i += 8)
-            orow[i] = __fmaf_rn(__fmul_rn(__fsub_rn(xr[i], mean), inv), gamma[i], beta[i]);
+        for (int i = threadIdx.x; i < D; i += 256) orow[i] = y(i);
         return;
     }
-    // Quantised output: the normalised row is computed twice (once for its maximum, once to quantise), never stored.
     float amax = 0.f;
-    if (active)
-        for (int i = vl; i < D; i += 8)
-            amax = fmaxf(amax, fabsf(__fmaf_rn(__fmul_rn(__fsub_rn(xr[i], mean), inv), gamma[i], beta[i])));
-    amax = max8(amax);
-    if (!active) return;
-    const float scale = quant_scale(amax);
+    for (int i = threadIdx.x; i < D; i += 256) amax = fmaxf(amax, fabsf(y(i)));
+    amax = warp_max(amax);
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
+    __syncthreads();
+    float m = red[0];
+#pragma unroll
+    for (int i = 1; i < 8; ++i) m = fmaxf(m, red[i]);
+    const float scale = quant_scale(m);
     const float qinv = __fdiv_rn(1.0f, scale);
     int8_t* qrow = q + static_cast<size_t>(row) * D;
-    for (int i = vl; i < D; i += 8)
-        qrow[i] = quant_one(__fmaf_rn(__fmul_rn(__fsub_rn(xr[i], mean), inv), gamma[i], beta[i]), qinv);
-    if (vl == 0) qscale[row] = scale;
+    for (int i = threadIdx.x; i < D; i += 256) qrow[i] = quant_one(y(i), qinv);
+    if (threadIdx.x == 0) qscale[row] = scale;
 }
 
 // ---- SiLU (csrc/tensor_ops.c:436-511) ------------------------------------------------------------------------------
@@ -111,6 +183,37 @@ __global__ void __launch_bounds__(256) swish_rows_kernel(const float* __restrict
     const float qinv = __fdiv_rn(1.0f, scale);
     int8_t* qrow = q + static_cast<size_t>(r) * len;
     for (int i = threadIdx.x; i < len; i += 256) qrow[i] = quant_one(swish1(hr[i]), qinv);
+    if (threadIdx.x == 0) qscale[r] = scale;
+}
+
+// len = 1024 V, one 256-thread block per row, the row in registers.
+template <int V, bool QUANT>
+__global__ void __launch_bounds__(256) swish_vec_kernel(const float* __restrict__ h, int ldh, float* out, int ldo,
+                                                        int8_t* __restrict__ q, float* __restrict__ qscale) {
+    __shared__ float red[8];
+    constexpr int len = 1024 * V;
+    const int r = blockIdx.x;
+    const float4* hr = reinterpret_cast<const float4*>(h + static_cast<size_t>(r) * ldh);
+    float4 v[V];
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+        const float4 a = hr[threadIdx.x + 256 * i];
+        v[i] = make_float4(swish1(a.x), swish1(a.y), swish1(a.z), swish1(a.w));
+        amax = fmaxf(amax, amax4(v[i]));
+    }
+    if (!QUANT) {
+        float4* orow = reinterpret_cast<float4*>(out + static_cast<size_t>(r) * ldo);
+#pragma unroll
+        for (int i = 0; i < V; ++i) orow[threadIdx.x + 256 * i] = v[i];
+        return;
+    }
+    amax = block_max256(amax, red);
+    const float scale = quant_scale(amax);
+    const float qinv = __fdiv_rn(1.0f, scale);
+    char4* qrow = reinterpret_cast<char4*>(q + static_cast<size_t>(r) * len);
+#pragma unroll
+    for (int i = 0; i < V; ++i) qrow[threadIdx.x + 256 * i] = quant4(v[i], qinv);
     if (threadIdx.x == 0) qscale[r] = scale;
 }
 
@@ -245,64 +348,85 @@ __global__ void __launch_bounds__(256) dwconv_swish_kernel(const float* __restri
 
 __device__ __forceinline__ int conv_out(int n) { return (n + 2 - 3) / 2 + 1; }
 
-// Conv2d(1 -> C, 3x3, stride 2, pad 1) + ReLU; out [rows1][W1][C], C fastest.
-__global__ void sub_conv0_kernel(const float* __restrict__ mel, const int* __restrict__ mel_off,
-                                 const int* __restrict__ h1_off, int n_win, const float* __restrict__ w,
-                                 const float* __restrict__ b, float* __restrict__ out, int rows1, int W_in, int C) {
+// Conv2d(1 -> C, 3x3, stride 2, pad 1) + ReLU; out [rows1][W1][C], C fastest. One block per output row and 16
+// output columns, one thread per channel with its 9 taps in registers; the three input rows are staged in shared
+// memory. Per output: bias, then the in-range taps in (kh, kw) order as one FMA chain.
+constexpr int SUB_OW = 16;
+
+__global__ void __launch_bounds__(256) sub_conv0_kernel(const float* __restrict__ mel, const int* __restrict__ mel_off,
+                                                        const int* __restrict__ h1_off, int n_win,
+                                                        const float* __restrict__ w, const float* __restrict__ b,
+                                                        float* __restrict__ out, int W_in, int C) {
+    __shared__ float xs[3][2 * SUB_OW + 1];
     const int W1 = conv_out(W_in);
-    const size_t idx = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (idx >= static_cast<size_t>(rows1) * W1 * C) return;
-    const int c = static_cast<int>(idx % C);
-    const size_t rest = idx / C;
-    const int ow = static_cast<int>(rest % W1), r1 = static_cast<int>(rest / W1);
+    const int r1 = blockIdx.x, ow0 = blockIdx.y * SUB_OW;
     const int win = find_window(h1_off, n_win, r1);
     const int oh = r1 - h1_off[win];
     const int H = mel_off[win + 1] - mel_off[win];
     const float* x = mel + static_cast<size_t>(mel_off[win]) * W_in;
-    const float* wc = w + c * 9;
-    float acc = b[c];
+    const int iw0 = 2 * ow0 - 1;
+    for (int e = threadIdx.x; e < 3 * (2 * SUB_OW + 1); e += blockDim.x) {
+        const int kh = e / (2 * SUB_OW + 1), col = e % (2 * SUB_OW + 1);
+        const int ih = 2 * oh - 1 + kh, iw = iw0 + col;
+        xs[kh][col] = (ih >= 0 && ih < H && iw >= 0 && iw < W_in) ? x[static_cast<size_t>(ih) * W_in + iw] : 0.f;
+    }
+    __syncthreads();
+    for (int c = threadIdx.x; c < C; c += blockDim.x) {
+        float wc[9];
 #pragma unroll
-    for (int kh = 0; kh < 3; ++kh) {
-        const int ih = 2 * oh - 1 + kh;
-        if (ih < 0 || ih >= H) continue;
+        for (int k = 0; k < 9; ++k) wc[k] = w[c * 9 + k];
+        const float bc = b[c];
+        for (int ow = ow0; ow < ow0 + SUB_OW && ow < W1; ++ow) {
+            float acc = bc;
 #pragma unroll
-        for (int kw = 0; kw < 3; ++kw) {
-            const int iw = 2 * ow - 1 + kw;
-            if (iw >= 0 && iw < W_in) acc = __fmaf_rn(x[static_cast<size_t>(ih) * W_in + iw], wc[kh * 3 + kw], acc);
+            for (int kh = 0; kh < 3; ++kh) {
+                const int ih = 2 * oh - 1 + kh;
+                if (ih < 0 || ih >= H) continue;
+#pragma unroll
+                for (int kw = 0; kw < 3; ++kw) {
+                    const int iw = 2 * ow - 1 + kw;
+                    if (iw >= 0 && iw < W_in) acc = __fmaf_rn(xs[kh][iw - iw0], wc[kh * 3 + kw], acc);
+                }
+            }
+            out[(static_cast<size_t>(r1) * W1 + ow) * C + c] = acc > 0.f ? acc : 0.f;
         }
     }
-    out[idx] = acc > 0.f ? acc : 0.f;
 }
 
-// Depthwise Conv2d(C, 3x3, stride 2, pad 1) + bias (no activation), per window.
-__global__ void sub_dwconv_kernel(const float* __restrict__ in, const int* __restrict__ in_off,
-                                  const int* __restrict__ out_off, int n_win, const float* __restrict__ w,
-                                  const float* __restrict__ b, float* __restrict__ out, int rows_out, int W_in,
-                                  int C) {
+// Depthwise Conv2d(C, 3x3, stride 2, pad 1) + bias (no activation), per window: [rows_in][W_in][C] ->
+// [rows_out][W_out][C]. One block per output row and 16 output columns, one thread per channel (loads coalesced
+// across channels).
+__global__ void __launch_bounds__(256) sub_dwconv_kernel(const float* __restrict__ in, const int* __restrict__ in_off,
+                                                         const int* __restrict__ out_off, int n_win,
+                                                         const float* __restrict__ w, const float* __restrict__ b,
+                                                         float* __restrict__ out, int W_in, int C) {
     const int W_out = conv_out(W_in);
-    const size_t idx = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (idx >= static_cast<size_t>(rows_out) * W_out * C) return;
-    const int c = static_cast<int>(idx % C);
-    const size_t rest = idx / C;
-    const int ow = static_cast<int>(rest % W_out), ro = static_cast<int>(rest / W_out);
+    const int ro = blockIdx.x, ow0 = blockIdx.y * SUB_OW;
     const int win = find_window(out_off, n_win, ro);
     const int oh = ro - out_off[win];
     const int H = in_off[win + 1] - in_off[win];
-    const float* x = in + static_cast<size_t>(in_off[win]) * W_in * C + c;
-    const float* wc = w + c * 9;
-    float acc = b[c];
+    const float* x = in + static_cast<size_t>(in_off[win]) * W_in * C;
+    for (int c = threadIdx.x; c < C; c += blockDim.x) {
+        float wc[9];
 #pragma unroll
-    for (int kh = 0; kh < 3; ++kh) {
-        const int ih = 2 * oh - 1 + kh;
-        if (ih < 0 || ih >= H) continue;
+        for (int k = 0; k < 9; ++k) wc[k] = w[c * 9 + k];
+        const float bc = b[c];
+        for (int ow = ow0; ow < ow0 + SUB_OW && ow < W_out; ++ow) {
+            float acc = bc;
 #pragma unroll
-        for (int kw = 0; kw < 3; ++kw) {
-            const int iw = 2 * ow - 1 + kw;
-            if (iw >= 0 && iw < W_in)
-                acc = __fmaf_rn(x[(static_cast<size_t>(ih) * W_in + iw) * C], wc[kh * 3 + kw], acc);
+            for (int kh = 0; kh < 3; ++kh) {
+                const int ih = 2 * oh - 1 + kh;
+                if (ih < 0 || ih >= H) continue;
+#pragma unroll
+                for (int kw = 0; kw < 3; ++kw) {
+                    const int iw = 2 * ow - 1 + kw;
+                    if (iw >= 0 && iw < W_in)
+                        acc = __fmaf_rn(x[(static_cast<size_t>(ih) * W_in + iw) * C + c], wc[kh * 3 + kw], acc);
+                }
+            }
+            out[(static_cast<size_t>(ro) * W_out + ow) * C + c] = acc;
         }
     }
-    out[idx] = acc;
 }
 
 __global__ void sub_flatten_kernel(const float* __restrict__ in, float* __restrict__ out, int rows, int W, int C) {
@@ -431,22 +555,206 @@ __global__ void __launch_bounds__(256) group_gemm_kernel(const GemmGroup* __rest
     }
 }
 
+// ---- fused relative-position attention for windows of up to ATT_MAXT frames (csrc/encoder.c:470-528) -----------
+//
+// One CTA per (32 queries of one window, head). Phase 1 computes the score rows
+//     s[i][j] = ((Q_i + bias_u) . K_j + (Q_i + bias_v) . P_{T-1-i+j}) * scale
+// each dot product one FMA chain over d = 0..127 in order, added after both chains as the reference adds ac and
+// the shifted bd; only the band of positions a query tile needs is loaded (the reference computes all 2T - 1).
+// Phase 2 is the softmax of each row in shared memory, phase 3 the context rows sum_j s[i][j] V_j, one FMA chain
+// over j in order per output, written straight into the concatenated-heads layout [row][h * 128 + d].
+constexpr int AQ = 32, AK = 64, AD = 32, AP = 96;
+
+__global__ void __launch_bounds__(128) attn_fused_kernel(const float* __restrict__ qkv, const float* __restrict__ P,
+                                                         const float* __restrict__ bias_u,
+                                                         const float* __restrict__ bias_v,
+                                                         const int* __restrict__ row_off,
+                                                         const int2* __restrict__ tiles, int Tmax, int SS,
+                                                         float scale, float* __restrict__ attn) {
+    extern __shared__ __align__(16) float smem[];
+    float* S = smem;                   // [AQ][SS] score rows
+    float* buf = smem + AQ * SS;       // phase 1: Qu [AD][AQ], Qv [AD][AQ], K [AD][AK], P [AD][AP]; phase 3: V [32][128]
+    float* Qu_s = buf;
+    float* Qv_s = Qu_s + AD * AQ;
+    float* K_s = Qv_s + AD * AQ;
+    float* P_s = K_s + AD * AK;
+    const int2 tile = tiles[blockIdx.x];
+    const int w = tile.x, q0 = tile.y, h = blockIdx.y;
+    const int r0 = row_off[w], T = row_off[w + 1] - r0;
+    const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+    const float* Qb = qkv + static_cast<size_t>(r0) * 3 * 1024 + h * 128;
+    const float* Kb = Qb + 1024;
+    const float* Vb = Qb + 2048;
+    const float* bu = bias_u + h * 128;
+    const float* bv = bias_v + h * 128;
+    const float* Pw = P + static_cast<size_t>(Tmax - T) * 1024 + h * 128;   // row p = this window's position p
+
+    for (int j0 = 0; j0 < T; j0 += AK) {
+        float ac[4][4], bd[4][4];
+#pragma unroll
+        for (int a = 0; a < 4; ++a)
+#pragma unroll
+            for (int b = 0; b < 4; ++b) ac[a][b] = bd[a][b] = 0.f;
+        const int pbase = T - 1 - q0 - (AQ - 1) + j0;   // the position at band index 0
+        for (int dc = 0; dc < 128; dc += AD) {
+            __syncthreads();
+            for (int e = tid; e < AQ * AD; e += 128) {
+                const int qi = e / AD, dd = e % AD, i = q0 + qi;
+                float u = 0.f, v = 0.f;
+                if (i < T) {
+                    const float qv = Qb[static_cast<size_t>(i) * 3072 + dc + dd];
+                    u = __fadd_rn(qv, bu[dc + dd]);
+                    v = __fadd_rn(qv, bv[dc + dd]);
+                }
+                Qu_s[dd * AQ + qi] = u;
+                Qv_s[dd * AQ + qi] = v;
+            }
+            for (int e = tid; e < AK * AD; e += 128) {
+                const int jj = e / AD, dd = e % AD, j = j0 + jj;
+                K_s[dd * AK + jj] = j < T ? Kb[static_cast<size_t>(j) * 3072 + dc + dd] : 0.f;
+            }
+            for (int e = tid; e < AP * AD; e += 128) {
+                const int pl = e / AD, dd = e % AD, p = pbase + pl;
+                P_s[dd * AP + pl] = (p >= 0 && p < 2 * T - 1) ? Pw[static_cast<size_t>(p) * 1024 + dc + dd] : 0.f;
+            }
+            __syncthreads();
+            const int pl0 = (AQ - 4) - 4 * ty + 4 * tx;   // band index of (row 4ty + 3, column 4tx)
+#pragma unroll 8
+            for (int dd = 0; dd < AD; ++dd) {
+                const float4 qu = *reinterpret_cast<const float4*>(&Qu_s[dd * AQ + 4 * ty]);
+                const float4 qv = *reinterpret_cast<const float4*>(&Qv_s[dd * AQ + 4 * ty]);
+                const float4 k = *reinterpret_cast<const float4*>(&K_s[dd * AK + 4 * tx]);
+                const float4 p0 = *reinterpret_cast<const float4*>(&P_s[dd * AP + pl0]);
+                const float4 p1 = *reinterpret_cast<const float4*>(&P_s[dd * AP + pl0 + 4]);
+                const float uq[4] = {qu.x, qu.y, qu.z, qu.w}, vq[4] = {qv.x, qv.y, qv.z, qv.w};
+                const float kk[4] = {k.x, k.y, k.z, k.w};
+                const float pp[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+#pragma unroll
+                for (int a = 0; a < 4; ++a)
+#pragma unroll
+                    for (int b = 0; b < 4; ++b) {
+                        ac[a][b] = __fmaf_rn(uq[a], kk[b], ac[a][b]);
+                        bd[a][b] = __fmaf_rn(vq[a], pp[3 - a + b], bd[a][b]);
+                    }
+            }
+        }
+#pragma unroll
+        for (int a = 0; a < 4; ++a)
+#pragma unroll
+            for (int b = 0; b < 4; ++b) {
+                const int j = j0 + 4 * tx + b;
+                if (j < T) S[(4 * ty + a) * SS + j] = __fmul_rn(__fadd_rn(ac[a][b], bd[a][b]), scale);
+            }
+    }
+    __syncthreads();
+
+    // phase 2: softmax of each valid row (max; the polynomial exp on the first 8 * floor(T / 8), expf on the tail,
+    // as the reference's vector loop and scalar tail; e * (1 / sum))
+    const int lane = tid & 31, warp = tid >> 5;
+    const int nv = T & ~7;
+    for (int r = warp; r < AQ; r += 4) {
+        if (q0 + r >= T) break;
+        float* Sr = S + r * SS;
+        float mx = -FLT_MAX;
+        for (int j = lane; j < T; j += 32) mx = fmaxf(mx, Sr[j]);
+        mx = warp_max(mx);
+        float sum = 0.f;
+        for (int j = lane; j < T; j += 32) {
+            const float d = __fsub_rn(Sr[j], mx);
+            const float e = j < nv ? exp_poly(d) : expf(d);
+            Sr[j] = e;
+            sum = __fadd_rn(sum, e);
+        }
+        const float inv = __fdiv_rn(1.0f, warp_sum(sum));
+        for (int j = lane; j < T; j += 32) Sr[j] = __fmul_rn(Sr[j], inv);
+    }
+
+    // phase 3: context rows; thread (ty, tx) owns rows 4ty..4ty+3 and columns 4tx..+3, 64+4tx..+3
+    float o[4][8];
+#pragma unroll
+    for (int a = 0; a < 4; ++a)
+#pragma unroll
+        for (int b = 0; b < 8; ++b) o[a][b] = 0.f;
+    float* V_s = buf;   // [32 keys][128]
+    for (int k0 = 0; k0 < T; k0 += 32) {
+        __syncthreads();
+        for (int e = tid; e < 32 * 32; e += 128) {
+            const int jj = e >> 5, c4 = e & 31, j = k0 + jj;
+            const float4 v = j < T ? *reinterpret_cast<const float4*>(Vb + static_cast<size_t>(j) * 3072 + 4 * c4)
+                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+            *reinterpret_cast<float4*>(&V_s[jj * 128 + 4 * c4]) = v;
+        }
+        __syncthreads();
+        const int kend = T - k0 < 32 ? T - k0 : 32;
+        for (int jj = 0; jj < kend; ++jj) {
+            const float4 v0 = *reinterpret_cast<const float4*>(&V_s[jj * 128 + 4 * tx]);
+            const float4 v1 = *reinterpret_cast<const float4*>(&V_s[jj * 128 + 64 + 4 * tx]);
+            const float vv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+#pragma unroll
+            for (int a = 0; a < 4; ++a) {
+                const float sa = S[(4 * ty + a) * SS + k0 + jj];
+#pragma unroll
+                for (int b = 0; b < 8; ++b) o[a][b] = __fmaf_rn(sa, vv[b], o[a][b]);
+            }
+        }
+    }
+#pragma unroll
+    for (int a = 0; a < 4; ++a) {
+        const int i = q0 + 4 * ty + a;
+        if (i >= T) continue;
+        float* dst = attn + static_cast<size_t>(r0 + i) * 1024 + h * 128;
+        *reinterpret_cast<float4*>(dst + 4 * tx) = make_float4(o[a][0], o[a][1], o[a][2], o[a][3]);
+        *reinterpret_cast<float4*>(dst + 64 + 4 * tx) = make_float4(o[a][4], o[a][5], o[a][6], o[a][7]);
+    }
+}
+
 unsigned blocks_for(size_t n, int threads) { return static_cast<unsigned>((n + threads - 1) / threads); }
 
 }  // namespace
 
+static bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
 cudaError_t ln_rows_launch(const float* x, int ldx, const float* gamma, const float* beta, float* out, int ldo,
                            int8_t* q, float* qscale, int rows, int D, cudaStream_t s) {
     if (rows <= 0) return cudaSuccess;
-    const unsigned grid = blocks_for(static_cast<size_t>(rows) * 8, 256);
-    if (q) ln_rows_kernel<true><<<grid, 256, 0, s>>>(x, ldx, gamma, beta, out, ldo, q, qscale, rows, D);
-    else ln_rows_kernel<false><<<grid, 256, 0, s>>>(x, ldx, gamma, beta, out, ldo, q, qscale, rows, D);
+    const bool vec = (D == 1024 || D == 512 || D == 256 || D == 128) && ldx % 4 == 0 && al16(x) && al16(gamma) &&
+                     al16(beta) && (q ? al16(q) : (ldo % 4 == 0 && al16(out)));
+    if (vec) {
+        const unsigned grid = static_cast<unsigned>((rows + 7) / 8);
+#define P2CU_LN(V)                                                                                                   \
+        if (q) ln_warp_kernel<V, true><<<grid, 256, 0, s>>>(x, ldx, gamma, beta, out, ldo, q, qscale, rows);         \
+        else ln_warp_kernel<V, false><<<grid, 256, 0, s>>>(x, ldx, gamma, beta, out, ldo, q, qscale, rows);
+        switch (D) {
+        case 1024: P2CU_LN(8) break;
+        case 512: P2CU_LN(4) break;
+        case 256: P2CU_LN(2) break;
+        default: P2CU_LN(1) break;
+        }
+#undef P2CU_LN
+        return cudaGetLastError();
+    }
+    if (q) ln_rows_kernel<true><<<rows, 256, 0, s>>>(x, ldx, gamma, beta, out, ldo, q, qscale, D);
+    else ln_rows_kernel<false><<<rows, 256, 0, s>>>(x, ldx, gamma, beta, out, ldo, q, qscale, D);
     return cudaGetLastError();
 }
 
 cudaError_t swish_rows_launch(const float* h, int ldh, float* out, int ldo, int8_t* q, float* qscale, int rows,
                               int len, cudaStream_t s) {
     if (rows <= 0) return cudaSuccess;
+    const bool vec = (len == 4096 || len == 2048 || len == 1024) && ldh % 4 == 0 && al16(h) &&
+                     (q ? al16(q) : (ldo % 4 == 0 && al16(out)));
+    if (vec) {
+#define P2CU_SW(V)                                                                                                   \
+        if (q) swish_vec_kernel<V, true><<<rows, 256, 0, s>>>(h, ldh, out, ldo, q, qscale);                          \
+        else swish_vec_kernel<V, false><<<rows, 256, 0, s>>>(h, ldh, out, ldo, q, qscale);
+        switch (len) {
+        case 4096: P2CU_SW(4) break;
+        case 2048: P2CU_SW(2) break;
+        default: P2CU_SW(1) break;
+        }
+#undef P2CU_SW
+        return cudaGetLastError();
+    }
     if (q) swish_rows_kernel<true><<<rows, 256, 0, s>>>(h, ldh, out, ldo, q, qscale, len);
     else swish_rows_kernel<false><<<rows, 256, 0, s>>>(h, ldh, out, ldo, q, qscale, len);
     return cudaGetLastError();
@@ -490,17 +798,19 @@ cudaError_t gather_rows_launch(float* dst, const float* src, const int* map, int
 
 cudaError_t sub_conv0_launch(const float* mel, const int* mel_off, const int* h1_off, int n_win, const float* w,
                              const float* b, float* out, int rows1, int W_in, int C, cudaStream_t s) {
-    const size_t n = static_cast<size_t>(rows1) * ((W_in - 1) / 2 + 1) * C;
-    if (!n) return cudaSuccess;
-    sub_conv0_kernel<<<blocks_for(n, 256), 256, 0, s>>>(mel, mel_off, h1_off, n_win, w, b, out, rows1, W_in, C);
+    const int W1 = (W_in - 1) / 2 + 1;
+    if (rows1 <= 0 || W1 <= 0) return cudaSuccess;
+    sub_conv0_kernel<<<dim3(rows1, (W1 + SUB_OW - 1) / SUB_OW), 256, 0, s>>>(mel, mel_off, h1_off, n_win, w, b, out,
+                                                                            W_in, C);
     return cudaGetLastError();
 }
 
 cudaError_t sub_dwconv_launch(const float* in, const int* in_off, const int* out_off, int n_win, const float* w,
                               const float* b, float* out, int rows_out, int W_in, int C, cudaStream_t s) {
-    const size_t n = static_cast<size_t>(rows_out) * ((W_in - 1) / 2 + 1) * C;
-    if (!n) return cudaSuccess;
-    sub_dwconv_kernel<<<blocks_for(n, 256), 256, 0, s>>>(in, in_off, out_off, n_win, w, b, out, rows_out, W_in, C);
+    const int W_out = (W_in - 1) / 2 + 1;
+    if (rows_out <= 0 || W_out <= 0) return cudaSuccess;
+    sub_dwconv_kernel<<<dim3(rows_out, (W_out + SUB_OW - 1) / SUB_OW), 256, 0, s>>>(in, in_off, out_off, n_win, w, b,
+                                                                                   out, W_in, C);
     return cudaGetLastError();
 }
 
@@ -534,6 +844,32 @@ cudaError_t attn_softmax_launch(float* s_ac, const float* s_bd, const int* srow_
     if (rows <= 0) return cudaSuccess;
     attn_softmax_kernel<<<blocks_for(static_cast<size_t>(rows) * 32, 256), 256, 0, s>>>(s_ac, s_bd, srow_off, s_off,
                                                                                        b_off, Tw, n_win, rows, scale);
+    return cudaGetLastError();
+}
+
+}  // namespace p2cu
+
+namespace p2cu {
+
+int attn_fused_smem_bytes(int Tmax) {
+    const int SS = (Tmax + 3) / 4 * 4 + 4;
+    const int buf = (2 * AD * AQ + AD * AK + AD * AP) > 32 * 128 ? (2 * AD * AQ + AD * AK + AD * AP) : 32 * 128;
+    return static_cast<int>((AQ * SS + buf) * sizeof(float));
+}
+
+cudaError_t attn_fused_launch(const float* qkv, const float* P, const float* bias_u, const float* bias_v,
+                              const int* row_off, const int2* tiles, int n_tiles, int Tmax, float scale, float* attn,
+                              cudaStream_t s) {
+    if (n_tiles <= 0) return cudaSuccess;
+    if (Tmax > ATT_MAXT) return cudaErrorInvalidValue;
+    const int bytes = attn_fused_smem_bytes(Tmax);
+    if (bytes > 48 * 1024) {   // a per-device attribute: set on every launch that needs it (cheap, host only)
+        cudaError_t e = cudaFuncSetAttribute(attn_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+        if (e != cudaSuccess) return e;
+    }
+    const int SS = (Tmax + 3) / 4 * 4 + 4;
+    attn_fused_kernel<<<dim3(n_tiles, 8), 128, bytes, s>>>(qkv, P, bias_u, bias_v, row_off, tiles, Tmax, SS, scale,
+                                                           attn);
     return cudaGetLastError();
 }
 

@@ -73,4 +73,14 @@ cudaError_t attn_softmax_launch(float* s_ac, const float* s_bd, const int* srow_
                                 const long long* b_off, const int* Tw, int n_win, int H, int rows, float scale,
                                 cudaStream_t s);
 
+// Fused relative-position attention for windows of at most ATT_MAXT frames: scores (content + shifted positional
+// band), softmax and context in one kernel, output in the concatenated-heads layout attn [rows][1024]. qkv [rows][3072]
+// (Q | K | V), P [2 Tmax - 1][1024] the projected positions of the longest window (a window of T frames uses rows
+// Tmax - T .. Tmax + T - 2), tiles: (window, first query) of every 32-query tile.
+constexpr int ATT_MAXT = 512;
+int attn_fused_smem_bytes(int Tmax);
+cudaError_t attn_fused_launch(const float* qkv, const float* P, const float* bias_u, const float* bias_v,
+                              const int* row_off, const int2* tiles, int n_tiles, int Tmax, float scale, float* attn,
+                              cudaStream_t s);
+
 }  // namespace p2cu

@@ -23,8 +23,9 @@
 //
 // Roles (warps): epilogue groups of four warps (one TMEM lane quarter each); with planes, groups 1 and 2 expand the
 // planes during the main loop; then the TMA producer and the MMA issuer (one elected lane, also the TMEM owner).
-// Launched with programmatic dependent launch: the set-up overlaps the previous kernel's tail, and nothing that
-// kernel writes is read before griddepcontrol.wait.
+// Launched with programmatic dependent launch: the set-up, the weight loads and the plane expansion overlap the
+// previous kernel's tail; A, its scales and C (everything a previous kernel may write) are touched only after
+// griddepcontrol.wait. The weights must therefore not be written by a kernel that triggers dependent launches early.
 #include <cstdint>
 #include <utility>
 #include <cuda.h>
@@ -69,7 +70,8 @@ template <int BN_, int KIND_> struct Cfg {
     static constexpr uint32_t FL_ROW = BN / 8 < 16 ? 16 : BN / 8;  // a TMA box row is at least 16 bytes
     static constexpr uint32_t FL_BYTES = BK * FL_ROW;              // flag-plane tile
     static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES + (PLANES ? SG_BYTES + FL_BYTES : 0);
-    static constexpr uint32_t TX_BYTES = A_BYTES + (PLANES ? SG_BYTES + FL_BYTES : B_BYTES);
+    static constexpr uint32_t B_TX_BYTES = PLANES ? SG_BYTES + FL_BYTES : B_BYTES;   // bytes TMA brings per stage
+                                                                                      // besides the A tile
     static constexpr int STAGES = (200 * 1024) / STAGE_BYTES > 6 ? 6 : (200 * 1024) / STAGE_BYTES;
     static constexpr uint32_t TMEM_COLS = MMA_N <= 32 ? 32 : MMA_N <= 64 ? 64 : MMA_N <= 128 ? 128 : 256;
     static constexpr int CHUNKS = BN / 32;                         // 32-column output chunks
@@ -187,7 +189,8 @@ fv_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     uint64_t* accfull = empty + STAGES;
     uint64_t* cfull = accfull + 1;
     uint64_t* drain = cfull + 1;
-    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
+    uint64_t* afull = drain + 1;   // the A tile of a stage has landed (full[] covers the weights)
+    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(afull + STAGES);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
     float* cc1 = reinterpret_cast<float*>(bar_region + G::BAR_BYTES);
     float* cc2 = cc1 + BN;
@@ -209,6 +212,7 @@ fv_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         TRACE(0);
         for (int s = 0; s < STAGES; ++s) {
             mbar_init(&full[s], 1);
+            mbar_init(&afull[s], 1);
             mbar_init(&bready[s], G::NEXP > 0 ? G::NEXP * 32 : 1);
             mbar_init(&empty[s], 1);
         }
@@ -234,20 +238,17 @@ fv_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     const uint32_t tmem = *tmem_holder;
     if (threadIdx.x == 0) TRACE(1);
     griddep_launch_dependents();   // the next kernel in the stream may start its set-up
-    griddep_wait();                // everything the previous kernels wrote is visible from here on
+    // Only what the previous kernels write (A, its scales, C_old, and C itself) waits for them (griddepcontrol.wait,
+    // below, in the producer before the first A load and in the epilogue before the first read): the weights are
+    // constant, so their loads and expansion overlap the previous kernel's tail.
 
     if (warp == G::PROD) {
         // ---------------- TMA producer ----------------
         if (lane == 0) {
-            int issued = 0;
-            for (int kb = 0; kb < nk; ++kb) {
-                const int s = kb % STAGES, r = kb / STAGES;
-                if (!mbar_wait(&empty[s], (r & 1) ^ 1, DEV_TIMEOUT_EMPTY, p.err, abort_flag)) break;
-                issued = kb + 1;
-                TRACE(8 + kb);
-                mbar_arrive_expect_tx(&full[s], G::TX_BYTES);
+            auto load_b = [&](int kb) {
+                const int s = kb % STAGES;
                 const int kx = k_begin + kb * BK;
-                tma_load_2d(a_tile(s), &tmA, &full[s], kx, m0);
+                mbar_arrive_expect_tx(&full[s], G::B_TX_BYTES);
                 if (PLANES) {
                     tma_load_2d(sg_tile(s), &tmB0, &full[s], n0 / 4, kx);
                     tma_load_2d(fl_tile(s), &tmB1, &full[s], (n0 / 8) & ~15, kx);   // 16-byte aligned box
@@ -256,11 +257,27 @@ fv_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                     for (int a = 0; a < G::N_ATOMS; ++a)
                         tma_load_2d(b_tile(s) + a * G::REGION, &tmB0, &full[s], n0 + a * G::ATOM_W, kx);
                 }
+            };
+            const int pre = nk < STAGES ? nk : STAGES;
+            for (int kb = 0; kb < pre; ++kb) load_b(kb);   // the stages are empty at the start
+            griddep_wait();
+            int issued = 0;
+            for (int kb = 0; kb < nk; ++kb) {
+                const int s = kb % STAGES, r = kb / STAGES;
+                if (kb >= pre) {
+                    if (!mbar_wait(&empty[s], (r & 1) ^ 1, DEV_TIMEOUT_EMPTY, p.err, abort_flag)) break;
+                    load_b(kb);
+                }
+                issued = kb + 1;
+                TRACE(8 + kb);
+                mbar_arrive_expect_tx(&afull[s], G::A_BYTES);
+                tma_load_2d(a_tile(s), &tmA, &afull[s], k_begin + kb * BK, m0);
             }
             // No copy may still be landing in shared memory when the CTA exits (matters on the abort path only).
             for (int kb = issued - STAGES < 0 ? 0 : issued - STAGES; kb < issued; ++kb) {
                 const int s = kb % STAGES, r = kb / STAGES;
                 for (uint32_t i = 0; i < WAIT_LIMIT && !mbar_try_wait(smem_u32(&full[s]), r & 1); ++i) {}
+                for (uint32_t i = 0; i < WAIT_LIMIT && !mbar_try_wait(smem_u32(&afull[s]), r & 1); ++i) {}
             }
         }
     } else if (warp == G::MMAW) {
@@ -269,6 +286,7 @@ fv_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             for (int kb = 0; kb < nk; ++kb) {
                 const int s = kb % STAGES, r = kb / STAGES;
                 if (!mbar_wait(PLANES ? &bready[s] : &full[s], r & 1, DEV_TIMEOUT_READY, p.err, abort_flag)) break;
+                if (!mbar_wait(&afull[s], r & 1, DEV_TIMEOUT_READY, p.err, abort_flag)) break;
                 tc_fence_after();
                 TRACE(80 + kb);
                 const uint32_t a_base = smem_u32(a_tile(s));
@@ -384,6 +402,7 @@ fv_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 if (G::ST) cc2[nl] = c2;   // in the int8w mode the expanders keep their clo table there
             }
         }
+        griddep_wait();   // a_scales, C_old and C belong to the previous kernels until here
         const float as = live ? __fmul_rn(p.a_scales[row], p.alpha) : 0.f;
         named_barrier_sync(1, NEPI);   // constants visible; the expanders are done with the stage buffers
         const bool ok = warp_wait(accfull, 0, DEV_TIMEOUT_ACC, p.err, abort_flag);

@@ -182,3 +182,10 @@ def frames_after_subsampling(n_mel: int) -> int:
 def mel(n_frames: int, seed: int) -> np.ndarray:
     """Synthetic log-mel features [n_frames, 128], N(0, 1) per feature (the BASELINE configs 2-4)."""
     return np.random.default_rng(seed).standard_normal((n_frames, NMEL), dtype=np.float32)
+
+
+def long_audio_windows(seed: int = 0, n: int = 64, lo_s: float = 25.0, hi_s: float = 35.0) -> list[int]:
+    """Mel frame counts of the long-audio batch: n windows of U(lo_s, hi_s) seconds of a
+    synthetic stream, 100 mel frames per second."""
+    rng = np.random.default_rng(seed)
+    return [int(round(s * 100)) for s in rng.uniform(lo_s, hi_s, n)]
