@@ -214,6 +214,14 @@ def run_reference(args, world, rank):
             "cpu_baseline": {"value": value, "unit": "TMAC/s", "cores": cores, "kind": "reference",
                              "sample": f"{args.steps} steps of the full workload"},
             "e2e": {"value": value, "unit": "TMAC/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    if not args.no_encoder:
+        enc = encoder_reference()
+        if enc is not None:
+            line["encoder"] = {"metric": "encoder audio-sec/sec", "value": enc["value"], "unit": "audio-s/s",
+                               "workload": encoder_workload("long-audio")[1], "mode": "exact",
+                               "cpu_baseline": enc,
+                               "e2e": {"value": enc["value"], "unit": "audio-s/s", "h2d_bytes_per_step": 0,
+                                       "d2h_bytes_per_step": 0}}
     print(json.dumps(line))
 
 
@@ -333,6 +341,7 @@ def run_ours(args, world, rank, local):
     # End to end: fp32 activations from pinned host memory, results back to pinned host memory, every step.
     e2e = run_e2e(pkg, torch, dev, stream, sets[0], mode, args)
 
+    line = None
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": "TMAC/s", "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
@@ -350,9 +359,124 @@ def run_ours(args, world, rank, local):
                 "gpu_launches": args.steps * 2 * len(gemms),
                 "clocks": clocks.summary(),
                 "e2e": e2e}
+    if not args.no_encoder:
+        enc = encoder_ours(args, world, rank, local, torch, pkg)
+        if rank == 0:
+            line["encoder"] = enc
+    if rank == 0:
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline()
+            if not args.no_encoder:
+                line["encoder"]["cpu_baseline"] = encoder_reference()
         print(json.dumps(line))
+
+
+# ---- the encoder: audio seconds per second --------------------------------------------------
+
+ENC_SECONDS_PER_FRAME = 0.01   # 100 mel frames per second of audio
+
+
+def shard_windows(frames, world):
+    """Windows to ranks as p2_b200_encode_windows assigns them to GPUs: longest first, to the least-loaded rank."""
+    order = sorted(range(len(frames)), key=lambda w: -frames[w])
+    load, out = [0] * world, [[] for _ in range(world)]
+    for w in order:
+        r = min(range(world), key=lambda i: load[i])
+        out[r].append(w)
+        load[r] += frames[w]
+    return [sorted(v) for v in out]
+
+
+def encoder_workload(name):
+    from phonon2_b200 import model as M
+    if name == "long-audio":
+        return M.long_audio_windows(0), ("BASELINE configs[3]: a 32-minute synthetic log-mel stream as 64 windows "
+                                         "of U(25, 35) s (seeded), sharded over the GPUs longest-first")
+    if name == "window":
+        return [3000], "BASELINE configs[2]: one 30 s window (mel [3000 x 128], T' = 375)"
+    return [300], "BASELINE configs[4]: one 3 s utterance (mel [300 x 128], T' = 38)"
+
+
+def encoder_ours(args, world, rank, local, torch, pkg, workload="long-audio", steps=5):
+    """The encoder on this rank's share of the windows: device-timed graph launches (mel resident), then end to end
+    through p2_b200_encode_windows (host mel in, host frames out, this rank's GPU)."""
+    from phonon2_b200 import model as M
+    from phonon2_b200.device import device_view
+    frames, desc = encoder_workload(workload)
+    mine = shard_windows(frames, world)[rank]
+    sm = M.SyntheticModel(seed=1)
+    dm = pkg.DeviceModel(sm.struct, codes=args.weights == "codes")
+    mode = pkg.MODES[args.mode]
+    mels = [M.mel(frames[w], seed=w) for w in mine]
+    enc = pkg.Encoder(dm, [frames[w] for w in mine], mode) if mine else None
+    stream = torch.cuda.Stream()
+    ms = 0.0
+    if enc is not None:
+        stacked = np.ascontiguousarray(np.concatenate(mels), np.float32)
+        device_view(enc.mel_ptr, stacked.shape).copy_(torch.from_numpy(stacked))
+        torch.cuda.synchronize()
+        for _ in range(2):
+            enc.run(stream)
+        stream.synchronize()
+    barrier(world)
+    if enc is not None:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            enc.run(stream)
+        e1.record(stream)
+        e1.synchronize()
+        pkg.check_device(stream)
+        ms = e0.elapsed_time(e1) / steps
+    barrier(world)
+    ms_max = max_over_ranks(ms, world)
+    audio_s = sum(frames) * ENC_SECONDS_PER_FRAME
+    # end to end through the public host API, on this rank's GPU
+    e2e_ms = 0.0
+    if mine:
+        pkg.host_encode_windows(sm.struct, mels, devices=[local])   # plan creation outside the timed region
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            pkg.host_encode_windows(sm.struct, mels, devices=[local])
+        e2e_ms = (time.perf_counter() - t0) / steps * 1e3
+    barrier(world)
+    e2e_max = max_over_ranks(e2e_ms, world)
+    n_out = sum(M.frames_after_subsampling(frames[w]) for w in mine)
+    res = {"metric": "encoder audio-sec/sec", "value": audio_s / (ms_max / 1e3), "unit": "audio-s/s",
+           "ms_per_step": ms_max, "steps": steps, "workload": desc, "windows": len(frames),
+           "audio_seconds": audio_s, "rows_per_gpu": enc.total_frames if enc else 0, "mode": args.mode,
+           "weights": args.weights, "timing": "CUDA events around graph launches, mel resident, max over ranks",
+           "gpu_launches_per_step": None,
+           "e2e": {"value": audio_s / (e2e_max / 1e3), "unit": "audio-s/s", "ms_per_step": e2e_max,
+                   "h2d_bytes_per_step": sum(m.nbytes for m in mels), "d2h_bytes_per_step": n_out * 640 * 4,
+                   "api": "p2_b200_encode_windows (host mel in, host frames out), wall clock, max over ranks"}}
+    if enc is not None:
+        enc.close()
+    dm.close()
+    return res
+
+
+def encoder_reference(seconds=15.0, workload="long-audio"):
+    """phonon-2-c's own p2_encoder (exact, its only x86 path) on the host cores, on the first windows of the
+    workload for about `seconds`."""
+    orc = ge.load_oracle()
+    if not orc.ref_available():
+        return None
+    from phonon2_b200 import model as M
+    frames, desc = encoder_workload(workload)
+    sm = M.SyntheticModel(seed=1)
+    done, t0, n = 0.0, time.perf_counter(), 0
+    while True:
+        w = n % len(frames)
+        orc.ref_encoder(sm.struct, M.mel(frames[w], seed=w), "exact")
+        done += frames[w] * ENC_SECONDS_PER_FRAME
+        n += 1
+        dt = time.perf_counter() - t0
+        if dt >= seconds:
+            break
+    return {"value": done / dt, "unit": "audio-s/s", "cores": orc.ref_threads(), "kind": "reference",
+            "sample": f"phonon-2-c p2_encoder (exact, AVX2) on {n} window(s) of the workload ({done:.0f} s of audio) "
+                      f"in {dt:.1f} s, P2_THREADS = all host cores"}
 
 
 def run_e2e(pkg, torch, dev, stream, gset, mode, args):
@@ -399,6 +523,7 @@ def main():
                     help="planes: expand the sign/magnitude planes in every GEMM (the reference's default); codes: "
                          "the int8w code cache (the reference's P2_CACHE_CODES), int8w only")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-encoder", action="store_true", help="skip the encoder (config 3) part of the line")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     world, rank, local = dist_setup(args)

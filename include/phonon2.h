@@ -164,6 +164,16 @@ P2_API int p2_encoder(const P2Model *m, const float *mel, int n_frames, float **
 /* The chunked encoder regardless of length (csrc/phonon2.h:397-398). Same contract. */
 P2_API int p2_encoder_chunked(const P2Model *m, const float *mel, int n_frames, float **out, int *out_len);
 
+/* The encoder over a batch of windows spread across GPUs. No counterpart in the reference, whose engine encodes the
+ * windows of long audio one after another (csrc/engine.c:311-357). Window w has n_frames[w] mel frames; `mel` holds
+ * the windows' frames one after another ([sum n_frames][128]) and `out` receives their encoder frames the same way
+ * ([sum T'_w][640], T'_w three stride-2 halvings of n_frames[w]). The windows go to the `n_devices` GPUs listed
+ * (all visible GPUs when n_devices is 0), longest first to the GPU with the fewest frames so far; each GPU encodes
+ * its share as one batch from one host thread, with no collective. Results equal p2_encoder's window by window.
+ * Each GPU keeps its last two plans (window sets) for reuse. Returns 0, or -1 with a message on stderr. */
+P2_API int p2_b200_encode_windows(const P2Model *m, const float *mel, const int *n_frames, int n_windows,
+                                  const int *devices, int n_devices, float *out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -81,6 +81,7 @@ SIGNATURES = {
     # include/phonon2.h: the reference's encoder entry points
     "p2_encoder": (_i, [_vp, _vp, _i, C.POINTER(_vp), C.POINTER(_i)]),
     "p2_encoder_chunked": (_i, [_vp, _vp, _i, C.POINTER(_vp), C.POINTER(_i)]),
+    "p2_b200_encode_windows": (_i, [_vp, _vp, C.POINTER(_i), _i, C.POINTER(_i), _i, _vp]),
     # include/blas.h: the reference's host-pointer ABI
     "p2_sgemm": (None, [_i, _i, _i, _i, _i, _f, _vp, _i, _vp, _i, _f, _vp, _i]),
     "p2_sgemm_st": (None, [_i, _i, _i, _i, _i, _f, _vp, _i, _vp, _i, _f, _vp, _i]),
@@ -299,3 +300,22 @@ def host_encoder(model_struct, mel, chunked: bool = False):
     finally:
         C.CDLL(None).free(out)
     return res
+
+
+def host_encode_windows(model_struct, mels, devices=None):
+    """p2_b200_encode_windows: a list of host mel arrays [n_i, 128] -> their [T'_i, 640] frames, spread over
+    `devices` (all visible GPUs when None)."""
+    import numpy as _np
+    from .model import frames_after_subsampling
+    frames = [int(m.shape[0]) for m in mels]
+    stacked = _np.ascontiguousarray(_np.concatenate(mels), dtype=_np.float32)
+    T = [frames_after_subsampling(n) for n in frames]
+    out = _np.empty((sum(T), 640), _np.float32)
+    fr = (C.c_int * len(frames))(*frames)
+    devs = None if not devices else (C.c_int * len(devices))(*devices)
+    rc = lib().p2_b200_encode_windows(C.addressof(model_struct), stacked.ctypes.data, fr, len(frames), devs,
+                                      len(devices) if devices else 0, out.ctypes.data)
+    if rc != 0:
+        raise Error(rc, "p2_b200_encode_windows failed (see stderr)")
+    offs = _np.cumsum([0] + T)
+    return [out[offs[i]:offs[i + 1]] for i in range(len(mels))]

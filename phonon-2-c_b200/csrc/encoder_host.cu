@@ -6,11 +6,15 @@
 // frames go up, one graph launch runs the whole encoder, the frames come back. Each host thread keeps its last plan
 // (buffers and captured graph for one length and mode) and a stream of its own, so concurrent callers on one model
 // do not share buffers (the reference allows concurrent p2_transcribe calls on one engine, csrc/phonon2.h:277-279).
+#include <algorithm>
 #include <cstdint>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <numeric>
+#include <string>
+#include <thread>
 #include <vector>
 #include <cuda_runtime.h>
 #include "p2cuda.h"
@@ -176,9 +180,183 @@ int encode(const P2Model* m, const float* mel, int n_frames, bool force_chunk, f
     return 0;
 }
 
+int conv3(int n) {   // encoder frames of n mel frames: three stride-2 convolutions
+    for (int i = 0; i < 3; ++i) n = (n - 1) / 2 + 1;
+    return n;
+}
+
+// Windows to GPUs: longest first, each to the GPU with the fewest frames so far; each GPU keeps its windows in their
+// original order.
+std::vector<std::vector<int>> shard_windows(const int* n_frames, int n, int n_dev) {
+    std::vector<int> order(n);
+    std::iota(order.begin(), order.end(), 0);
+    std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return n_frames[a] > n_frames[b]; });
+    std::vector<long long> load(n_dev, 0);
+    std::vector<std::vector<int>> out(n_dev);
+    for (int w : order) {
+        const int d = static_cast<int>(std::min_element(load.begin(), load.end()) - load.begin());
+        out[d].push_back(w);
+        load[d] += n_frames[w];
+    }
+    for (auto& v : out) std::sort(v.begin(), v.end());
+    return out;
+}
+
+// One GPU's share of p2_b200_encode_windows: its cached plans (one per distinct window set and chunking) and stream.
+struct DeviceSlot {
+    std::mutex mu;
+    cudaStream_t stream = nullptr;
+    struct Cached {
+        const P2cuModel* model;
+        std::vector<int> frames;
+        int mode, chunk, overlap;
+        P2cuEncoder* plan;
+    };
+    std::vector<Cached> plans;   // the two most recent
+
+    P2cuEncoder* plan_for(const P2cuModel* dm, const std::vector<int>& frames, int mode, int chunk, int overlap) {
+        for (Cached& c : plans)
+            if (c.model == dm && c.frames == frames && c.mode == mode && c.chunk == chunk && c.overlap == overlap)
+                return c.plan;
+        P2cuEncoder* e = nullptr;
+        if (p2cu_encoder_create(dm, frames.data(), static_cast<int>(frames.size()), mode, chunk, overlap, &e) !=
+            P2CU_OK)
+            return nullptr;
+        if (plans.size() >= 2) {
+            p2cu_encoder_destroy(plans.front().plan);
+            plans.erase(plans.begin());
+        }
+        plans.push_back({dm, frames, mode, chunk, overlap, e});
+        return e;
+    }
+};
+
+DeviceSlot g_slots[64];
+
+// Encode `wins` (indices into the caller's windows) on `device` with one plan; mel / out are the caller's host
+// arrays with per-window row offsets.
+int encode_on_device(const P2Model* m, int device, const std::vector<int>& wins, const float* mel,
+                     const std::vector<long long>& mel_off, const int* n_frames, const std::vector<long long>& out_off,
+                     float* out, int chunk, int overlap, std::string* err) {
+    if (wins.empty()) return 0;
+    if (cudaSetDevice(device) != cudaSuccess) {
+        *err = "cannot use GPU " + std::to_string(device);
+        return -1;
+    }
+    DeviceSlot& slot = g_slots[device];
+    std::lock_guard<std::mutex> lock(slot.mu);
+    if (!slot.stream && cudaStreamCreateWithFlags(&slot.stream, cudaStreamNonBlocking) != cudaSuccess) {
+        *err = "cannot create a CUDA stream";
+        return -1;
+    }
+    const P2cuModel* dm = model_on(m, device);
+    if (!dm) {
+        *err = p2cu_last_error();
+        return -1;
+    }
+    std::vector<int> frames;
+    for (int w : wins) frames.push_back(n_frames[w]);
+    P2cuEncoder* e = slot.plan_for(dm, frames, p2b_gemm_mode(), chunk, overlap);
+    if (!e) {
+        *err = p2cu_last_error();
+        return -1;
+    }
+    float* dmel = p2cu_encoder_mel(e);
+    float* dout = p2cu_encoder_out(e);
+    cudaError_t ce = cudaSuccess;
+    size_t row = 0;
+    for (int w : wins) {
+        ce = cudaMemcpyAsync(dmel + row * P2_N_MELS, mel + mel_off[w] * P2_N_MELS,
+                             static_cast<size_t>(n_frames[w]) * P2_N_MELS * sizeof(float), cudaMemcpyHostToDevice,
+                             slot.stream);
+        if (ce != cudaSuccess) break;
+        row += n_frames[w];
+    }
+    int rc = ce == cudaSuccess ? p2cu_encoder_run(e, slot.stream) : P2CU_ECUDA;
+    row = 0;
+    for (size_t i = 0; rc == P2CU_OK && ce == cudaSuccess && i < wins.size(); ++i) {
+        const int w = wins[i];
+        const int t = p2cu_encoder_frames(e, static_cast<int>(i));
+        ce = cudaMemcpyAsync(out + out_off[w] * P2_JOINT_DIM, dout + row * P2_JOINT_DIM,
+                             static_cast<size_t>(t) * P2_JOINT_DIM * sizeof(float), cudaMemcpyDeviceToHost,
+                             slot.stream);
+        row += t;
+    }
+    if (rc == P2CU_OK && ce == cudaSuccess) rc = p2cu_check_device(slot.stream);
+    if (rc != P2CU_OK || ce != cudaSuccess) {
+        *err = ce != cudaSuccess ? cudaGetErrorString(ce) : p2cu_last_error();
+        return -1;
+    }
+    return 0;
+}
+
 }  // namespace
 
 extern "C" {
+
+// No counterpart in the reference, whose engine encodes the windows of long audio one after another on its thread
+// pool (csrc/engine.c:311-357): here they are spread over GPUs, one batch per GPU, with no collective.
+__attribute__((visibility("default"))) int p2_b200_encode_windows(const P2Model* m, const float* mel,
+                                                                  const int* n_frames, int n_windows,
+                                                                  const int* devices, int n_devices, float* out) {
+    if (!m || !mel || !n_frames || n_windows <= 0 || !out || n_devices < 0 || (n_devices > 0 && !devices)) {
+        fprintf(stderr, "p2_b200_encode_windows: bad arguments\n");
+        return -1;
+    }
+    std::vector<int> devs;
+    if (n_devices == 0) {
+        int n = 0;
+        if (cudaGetDeviceCount(&n) != cudaSuccess || n <= 0) {
+            fprintf(stderr, "p2_b200_encode_windows: no CUDA device\n");
+            return -1;
+        }
+        for (int i = 0; i < n; ++i) devs.push_back(i);
+    } else {
+        devs.assign(devices, devices + n_devices);
+    }
+    for (int d : devs)
+        if (d < 0 || d >= 64) {
+            fprintf(stderr, "p2_b200_encode_windows: device %d out of range\n", d);
+            return -1;
+        }
+    std::vector<long long> mel_off(n_windows + 1, 0), out_off(n_windows + 1, 0);
+    for (int w = 0; w < n_windows; ++w) {
+        if (n_frames[w] < 1) {
+            fprintf(stderr, "p2_b200_encode_windows: window %d has %d frames\n", w, n_frames[w]);
+            return -1;
+        }
+        mel_off[w + 1] = mel_off[w] + n_frames[w];
+        out_off[w + 1] = out_off[w] + conv3(n_frames[w]);
+    }
+    // The reference's chunking rule per window (csrc/encoder.c:715-723): windows it would chunk go in a plan of
+    // their own on the same GPU.
+    const int chunk = env_int("P2_CHUNK_SIZE", 400), overlap = env_int("P2_CHUNK_OVERLAP", 8);
+    int prev = 0;
+    cudaGetDevice(&prev);
+    const auto shards = shard_windows(n_frames, n_windows, static_cast<int>(devs.size()));
+    // The same GPU may appear twice in `devices`: its shares then run one after the other (the slot's mutex).
+    std::vector<std::string> errs(devs.size());
+    std::vector<int> rcs(devs.size(), 0);
+    std::vector<std::thread> threads;
+    for (size_t i = 0; i < devs.size(); ++i) {
+        threads.emplace_back([&, i] {
+            std::vector<int> plain, chunked;
+            for (int w : shards[i]) (should_chunk(conv3(n_frames[w])) ? chunked : plain).push_back(w);
+            rcs[i] = encode_on_device(m, devs[i], plain, mel, mel_off, n_frames, out_off, out, 0, 0, &errs[i]);
+            if (rcs[i] == 0)
+                rcs[i] = encode_on_device(m, devs[i], chunked, mel, mel_off, n_frames, out_off, out, chunk, overlap,
+                                          &errs[i]);
+        });
+    }
+    for (auto& t : threads) t.join();
+    cudaSetDevice(prev);
+    for (size_t i = 0; i < devs.size(); ++i)
+        if (rcs[i]) {
+            fprintf(stderr, "p2_b200_encode_windows: GPU %d: %s\n", devs[i], errs[i].c_str());
+            return -1;
+        }
+    return 0;
+}
 
 __attribute__((visibility("default"))) int p2_encoder(const P2Model* m, const float* mel, int n_frames, float** out,
                                                       int* out_len) {
@@ -193,6 +371,14 @@ __attribute__((visibility("default"))) int p2_encoder_chunked(const P2Model* m, 
 // Called by p2_b200_release_weights: drop the calling thread's plan and every uploaded encoder model.
 void p2b_release_encoder_models(void) {
     t_ctx.drop_plan();
+    for (int d = 0; d < 64; ++d) {
+        DeviceSlot& slot = g_slots[d];
+        std::lock_guard<std::mutex> lock(slot.mu);
+        if (slot.plans.empty()) continue;
+        cudaSetDevice(d);
+        for (auto& c : slot.plans) p2cu_encoder_destroy(c.plan);
+        slot.plans.clear();
+    }
     std::lock_guard<std::mutex> lock(g_mu);
     int prev = 0;
     cudaGetDevice(&prev);

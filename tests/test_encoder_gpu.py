@@ -208,3 +208,16 @@ def test_encoder_argument_errors(pkg, cuda, dev_model):
         pkg.Encoder(dev_model, [0], pkg.INT8W)
     with pytest.raises(pkg.Error):
         pkg.Encoder(dev_model, [300], 7)
+
+
+def test_encode_windows_spread_over_devices(pkg, cuda, model):
+    """p2_b200_encode_windows gives every window exactly what p2_encoder gives it. The device list names GPU 0 twice,
+    so the sharding, the per-GPU threads and the per-GPU plan cache run on a one-GPU box too."""
+    from phonon2_b200 import model as M
+    mels = [M.mel(n, seed=n) for n in (300, 251, 333, 17, 290)]
+    got = pkg.host_encode_windows(model.struct, mels, devices=[0, 0])
+    again = pkg.host_encode_windows(model.struct, mels, devices=[0, 0])   # from the cached plans
+    for mel, g, a in zip(mels, got, again):
+        one = pkg.host_encoder(model.struct, mel)
+        assert np.array_equal(g.view(np.uint32), one.view(np.uint32))
+        assert np.array_equal(a.view(np.uint32), one.view(np.uint32))
