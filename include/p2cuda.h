@@ -137,6 +137,14 @@ P2CU_API int p2cu_softmax_rows(float *x, int n_rows, int len, void *stream);
 P2CU_API int p2cu_depthwise_conv1d_rows(const float *x, const float *w, const float *b, float *out, int C, int T,
                                         void *stream);
 
+/* C = A op(B) in fp32 on the tensor cores: A [M][K] (rows lda apart), op(B) = B^T with B [N][K] (transB != 0) or
+ * B [K][N] (rows ldb apart), C [M][N] (rows ldc apart), overwritten. Each operand value is split into two tf32 parts
+ * and three tcgen05 products are summed (hi*hi + hi*lo + lo*hi), which keeps fp32 accuracy (relative error about
+ * 2^-21 per product); the summation order is the tensor core's, not one FMA chain. No counterpart in the reference,
+ * which runs its fp32 attention products on the CPU (csrc/encoder.c:282-316); the encoder uses this kernel for them. */
+P2CU_API int p2cu_sgemm_tf32x3(int transB, int M, int N, int K, const float *A, int lda, const float *B, int ldb,
+                               float *C, int ldc, void *stream);
+
 /* ---- The encoder on the device (csrc/encoder.c) ------------------------------------------------------------------
  * Unlike the calls above these allocate device memory, once: p2cu_model_upload copies a model's weights to the
  * current device, p2cu_encoder_create makes a plan with every buffer of one batch of windows and captures its forward

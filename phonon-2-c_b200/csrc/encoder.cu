@@ -22,6 +22,7 @@
 #include "p2cuda.h"
 #include "gemm.h"
 #include "encoder_ops.h"
+#include "attn_tc.h"
 #include "kernels.h"
 
 namespace {
@@ -234,6 +235,11 @@ struct P2cuEncoder {
     int ng = 0, t_ac = 0, t_bd = 0, t_av = 0;
     int2* att_tiles = nullptr;   // fused attention (every window <= ATT_MAXT frames): (window, first query) per tile
     int n_att_tiles = 0;
+    // Attention path: 0 = tensor cores (products as split-tf32 tcgen05 GEMMs, scores in HBM), 1 = SIMT grouped GEMMs,
+    // 2 = SIMT fused kernel (short windows). P2CU_ATTN=tc|simt|fused chooses; tc is the default.
+    int attn_path = 0;
+    p2cu::TcGroup *tc_scores = nullptr, *tc_context = nullptr;
+    int n_tc = 0, t_tc_scores = 0, t_tc_context = 0;
 
     cudaStream_t stream = nullptr;
     cudaGraph_t graph = nullptr;
@@ -326,7 +332,22 @@ int self_attention(P2cuEncoder& e, const DBlock& b, cudaStream_t s) {
         TRY(wmatmul(e, e.lnbuf, e.R, b.qkv, e.big, 1.f, 0.f, nullptr, s, "qkv"));
         TRY(wmatmul(e, e.pe, e.L, b.pos, e.P, 1.f, 0.f, nullptr, s, "pos"));
     }
-    if (e.n_att_tiles) {
+    if (e.attn_path == 0) {   // tensor cores: AC and BD in one launch, softmax, then the context
+        p2cu::TcArgs a{};
+        a.src[0] = e.big; a.src[1] = e.P;
+        a.dst[0] = e.s_ac; a.dst[1] = e.s_bd;
+        a.bias[0] = b.bias_u; a.bias[1] = b.bias_v;
+        a.err = p2cu::device_error_word();
+        TRYC(p2cu::attn_tc_launch(e.tc_scores, 2 * e.n_tc, e.t_tc_scores, a, false, s), "attention scores");
+        TRYC(p2cu::attn_softmax_launch(e.s_ac, e.s_bd, e.d_srow_off, e.d_s_off, e.d_b_off, e.d_T, e.n_win, H,
+                                       e.srows, e.scale, s),
+             "attention softmax");
+        p2cu::TcArgs c{};
+        c.src[0] = e.s_ac; c.src[1] = e.big;
+        c.dst[0] = e.attn; c.dst[1] = e.attn;
+        c.err = a.err;
+        TRYC(p2cu::attn_tc_launch(e.tc_context, e.n_tc, e.t_tc_context, c, true, s), "attention context");
+    } else if (e.n_att_tiles) {
         TRYC(p2cu::attn_fused_launch(e.big, e.P, b.bias_u, b.bias_v, e.d_row_off, e.att_tiles, e.n_att_tiles, e.Tmax,
                                      e.scale, e.attn, s),
              "attention");
@@ -519,7 +540,53 @@ int create_plan(const P2cuModel* m, const int* n_frames, int n_mel_win, int mode
         srow_off.push_back(srow_off.back() + H * t);
     }
     e->srows = srow_off.back();
-    const bool fused = e->Tmax <= p2cu::ATT_MAXT;
+    {
+        const char* ap = getenv("P2CU_ATTN");
+        e->attn_path = ap && strcmp(ap, "simt") == 0 ? 1 : ap && strcmp(ap, "fused") == 0 ? 2 : 0;
+    }
+    // tensor-core groups: scores (AC then BD groups, one launch) and context (one launch)
+    std::vector<p2cu::TcGroup> tcs, tcc;
+    {
+        int ts = 0, tc = 0;
+        for (int pass = 0; pass < 2; ++pass)
+            for (int w = 0; w < n_win; ++w) {
+                const int t = e->T[w], Lw = 2 * t - 1, r0 = e->row_off[w];
+                for (int h = 0; h < H; ++h) {
+                    p2cu::TcGroup g{};
+                    g.M = t; g.K = DH; g.tile0 = ts;
+                    g.a_off = static_cast<long long>(r0) * 3 * D + h * DH; g.lda = 3 * D;
+                    g.a_src = 0;
+                    g.bias_off = h * DH;
+                    if (pass == 0) {   // AC = (Q + bias_u) K^T
+                        g.N = t;
+                        g.b_src = 0; g.b_off = static_cast<long long>(r0) * 3 * D + D + h * DH; g.ldb = 3 * D;
+                        g.c_dst = 0; g.c_off = gac[w * H + h].c_off; g.ldc = t;
+                        g.bias_sel = 0;
+                    } else {           // BD = (Q + bias_v) P^T over the window's 2T - 1 positions
+                        g.N = Lw;
+                        g.b_src = 1; g.b_off = static_cast<long long>(e->Tmax - t) * D + h * DH; g.ldb = D;
+                        g.c_dst = 1; g.c_off = gbd[w * H + h].c_off; g.ldc = Lw;
+                        g.bias_sel = 1;
+                    }
+                    tcs.push_back(g);
+                    ts += p2cu::tc_gemm_tiles(g.M, g.N);
+                    if (pass == 0) {   // context = S V into the concatenated heads
+                        p2cu::TcGroup c{};
+                        c.M = t; c.N = DH; c.K = t; c.tile0 = tc;
+                        c.a_src = 0; c.a_off = gac[w * H + h].c_off; c.lda = t;
+                        c.b_src = 1; c.b_off = static_cast<long long>(r0) * 3 * D + 2 * D + h * DH; c.ldb = 3 * D;
+                        c.c_dst = 0; c.c_off = static_cast<long long>(r0) * D + h * DH; c.ldc = D;
+                        c.bias_sel = -1;
+                        tcc.push_back(c);
+                        tc += p2cu::tc_gemm_tiles(c.M, c.N);
+                    }
+                }
+            }
+        e->n_tc = static_cast<int>(tcc.size());
+        e->t_tc_scores = ts;
+        e->t_tc_context = tc;
+    }
+    const bool fused = e->attn_path == 2 && e->Tmax <= p2cu::ATT_MAXT;
     std::vector<int2> att_tiles;
     if (fused) {
         for (int w = 0; w < n_win; ++w)
@@ -576,6 +643,8 @@ int create_plan(const P2cuModel* m, const int* n_frames, int n_mel_win, int mode
         {reinterpret_cast<void**>(&e->g_bd), gbd.size() * sizeof(p2cu::GemmGroup)},
         {reinterpret_cast<void**>(&e->g_av), gav.size() * sizeof(p2cu::GemmGroup)},
         {reinterpret_cast<void**>(&e->att_tiles), att_tiles.size() * sizeof(int2)},
+        {reinterpret_cast<void**>(&e->tc_scores), tcs.size() * sizeof(p2cu::TcGroup)},
+        {reinterpret_cast<void**>(&e->tc_context), tcc.size() * sizeof(p2cu::TcGroup)},
     };
     size_t total = 0;
     for (const Slot& sl : slots) total += al256(sl.bytes ? sl.bytes : 1);
@@ -612,6 +681,8 @@ int create_plan(const P2cuModel* m, const int* n_frames, int n_mel_win, int mode
         {e->g_bd, gbd.data(), gbd.size() * sizeof(p2cu::GemmGroup)},
         {e->g_av, gav.data(), gav.size() * sizeof(p2cu::GemmGroup)},
         {e->att_tiles, att_tiles.data(), att_tiles.size() * sizeof(int2)},
+        {e->tc_scores, tcs.data(), tcs.size() * sizeof(p2cu::TcGroup)},
+        {e->tc_context, tcc.data(), tcc.size() * sizeof(p2cu::TcGroup)},
     };
     for (const Copy& c : copies)
         if (c.bytes && (ce = cudaMemcpy(c.dst, c.src, c.bytes, cudaMemcpyHostToDevice)) != cudaSuccess) break;

@@ -160,16 +160,6 @@ __device__ __forceinline__ uint32_t out_offset(int r, int j) {
     return static_cast<uint32_t>(r * 128 + ((j ^ (r & 7)) << 4));
 }
 
-// Wait for a barrier phase with one polling lane per warp; every lane then acquires the completed phase.
-__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, uint32_t code, uint32_t* err,
-                                          volatile int* abort_flag) {
-    int ok = 1;
-    if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, code, err, abort_flag) ? 1 : 0;
-    ok = __shfl_sync(0xffffffffu, ok, 0);
-    if (ok) mbar_try_wait(smem_u32(bar), parity);   // already complete: acquire for this lane
-    return ok != 0;
-}
-
 template <int BN, int KIND>
 __global__ void __launch_bounds__(Cfg<BN, KIND>::NTHREADS, 1)
 fv_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB0,

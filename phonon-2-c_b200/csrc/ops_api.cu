@@ -4,6 +4,7 @@
 #include "p2cuda.h"
 #include "gemm.h"
 #include "encoder_ops.h"
+#include "attn_tc.h"
 
 namespace {
 
@@ -66,6 +67,26 @@ int p2cu_depthwise_conv1d_rows(const float* x, const float* w, const float* b, f
     return done(p2cu::dwconv_swish_launch(x, w, b, nullptr, 1, out, nullptr, nullptr, T, C,
                                           static_cast<cudaStream_t>(stream), false),
                 "p2cu_depthwise_conv1d_rows");
+}
+
+int p2cu_sgemm_tf32x3(int transB, int M, int N, int K, const float* A, int lda, const float* B, int ldb, float* C,
+                      int ldc, void* stream) {
+    if (M < 0 || N < 0 || K < 0) return p2cu::fail_fmt(P2CU_EINVAL, "p2cu_sgemm_tf32x3: shape M=%d N=%d K=%d", M, N, K);
+    if (M == 0 || N == 0) return P2CU_OK;
+    if (K == 0) return p2cu::fail_fmt(P2CU_EUNSUPPORTED, "p2cu_sgemm_tf32x3: K = 0");
+    if (!A || !B || !C) return p2cu::fail_fmt(P2CU_EINVAL, "p2cu_sgemm_tf32x3: NULL pointer");
+    if (lda < K || ldc < N || ldb < (transB ? K : N))
+        return p2cu::fail_fmt(P2CU_EINVAL, "p2cu_sgemm_tf32x3: leading dimensions lda=%d ldb=%d ldc=%d", lda, ldb, ldc);
+    p2cu::TcArgs a{};
+    a.src[0] = A; a.src[1] = B;
+    a.dst[0] = C; a.dst[1] = C;
+    a.err = p2cu::device_error_word();
+    p2cu::TcGroup& g = a.single;
+    g.M = M; g.N = N; g.K = K; g.tile0 = 0;
+    g.a_src = 0; g.b_src = 1; g.c_dst = 0; g.lda = lda; g.ldb = ldb; g.ldc = ldc; g.bias_sel = -1;
+    return done(p2cu::attn_tc_launch(nullptr, 0, p2cu::tc_gemm_tiles(M, N), a, !transB,
+                                     static_cast<cudaStream_t>(stream)),
+                "p2cu_sgemm_tf32x3");
 }
 
 }  // extern "C"

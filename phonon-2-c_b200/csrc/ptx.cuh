@@ -62,6 +62,17 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32
     return false;
 }
 
+// Wait for a barrier phase with one polling lane per warp; every lane then acquires the completed phase. The whole
+// warp must call it; every lane gets the same result.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, uint32_t code, uint32_t* err,
+                                          volatile int* abort_flag) {
+    int ok = 1;
+    if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, code, err, abort_flag) ? 1 : 0;
+    ok = __shfl_sync(0xffffffffu, ok, 0);
+    if (ok) mbar_try_wait(smem_u32(bar), parity);   // already complete: acquire for this lane
+    return ok != 0;
+}
+
 // ---- TMA ---------------------------------------------------------------------------------------------------------
 
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
@@ -140,6 +151,15 @@ __device__ __forceinline__ void mma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t
                  :: "r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate) : "memory");
 }
 
+// D[tmem] (+)= A[smem] * B[smem], tf32 x tf32 -> fp32 (the low 13 mantissa bits of each operand are ignored).
+__device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accumulate) {
+    asm volatile("{\n\t.reg .pred p;\n\t"
+                 "setp.ne.b32 p, %4, 0;\n\t"
+                 "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}"
+                 :: "r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate) : "memory");
+}
+
 // Arrive on `bar` once every tcgen05 operation this thread issued so far has completed.
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
@@ -194,6 +214,16 @@ __host__ __device__ constexpr uint32_t idesc_i8(int M, int N, bool a_mn, bool b_
          | (1u << 7)                                  // A: signed 8-bit
          | (1u << 10)                                 // B: signed 8-bit
          | ((a_mn ? 1u : 0u) << 15)
+         | ((b_mn ? 1u : 0u) << 16)
+         | (static_cast<uint32_t>(N >> 3) << 17)
+         | (static_cast<uint32_t>(M >> 4) << 24);
+}
+
+// Instruction descriptor for kind::tf32 with fp32 accumulators; A K-major, B K-major or (b_mn) MN-major.
+__host__ __device__ constexpr uint32_t idesc_tf32(int M, int N, bool b_mn) {
+    return (1u << 4)                                  // D format: f32
+         | (2u << 7)                                  // A: tf32
+         | (2u << 10)                                 // B: tf32
          | ((b_mn ? 1u : 0u) << 16)
          | (static_cast<uint32_t>(N >> 3) << 17)
          | (static_cast<uint32_t>(M >> 4) << 24);

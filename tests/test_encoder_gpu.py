@@ -221,3 +221,16 @@ def test_encode_windows_spread_over_devices(pkg, cuda, model):
         one = pkg.host_encoder(model.struct, mel)
         assert np.array_equal(g.view(np.uint32), one.view(np.uint32))
         assert np.array_equal(a.view(np.uint32), one.view(np.uint32))
+
+
+@pytest.mark.parametrize("path", ["tc", "simt", "fused"])
+def test_attention_paths_match_reference(pkg, orc, cuda, model, dev_model, path, monkeypatch):
+    """Each attention implementation (tensor cores with split-tf32 operands, SIMT grouped GEMMs, the fused SIMT
+    kernel) gives the exact-mode encoder within 1e-4 of the reference (P2CU_ATTN chooses; the plan reads it)."""
+    import torch
+    from phonon2_b200 import model as M
+    monkeypatch.setenv("P2CU_ATTN", path)
+    mel = M.mel(1000, seed=9)   # T' = 125
+    got, = _run(pkg, torch, dev_model, [mel], pkg.EXACT)
+    ref = orc.ref_encoder(model.struct, mel, "exact")
+    assert _rel(got, ref) <= EXACT_TOL, _rel(got, ref)
