@@ -114,6 +114,7 @@ __global__ void __launch_bounds__(NTHREADS, 3) attn_tc_kernel(const TcGroup* __r
         const int t = threadIdx.x;   // 0 .. 127
         const bool avec = (g.lda & 3) == 0 && (reinterpret_cast<uintptr_t>(A) & 15) == 0;
         const bool bvec = !B_KN && (g.ldb & 3) == 0 && (reinterpret_cast<uintptr_t>(B) & 15) == 0;
+        const bool biasvec = (reinterpret_cast<uintptr_t>(bias) & 15) == 0;
         float4 ra[PER], rb[PER];
         auto fetch = [&](int kb) {
             const int k0 = kb * TK;
@@ -124,10 +125,11 @@ __global__ void __launch_bounds__(NTHREADS, 3) attn_tc_kernel(const TcGroup* __r
                     const int r = e >> 2, c = e & 3, m = m0 + r, k = k0 + 4 * c;
                     ra[i] = m < g.M ? load4(A + static_cast<size_t>(m) * g.lda, k, g.K, avec) : make_float4(0, 0, 0, 0);
                     if (bias && m < g.M) {
-                        ra[i].x = k < g.K ? __fadd_rn(ra[i].x, bias[k]) : 0.f;
-                        ra[i].y = k + 1 < g.K ? __fadd_rn(ra[i].y, bias[k + 1]) : 0.f;
-                        ra[i].z = k + 2 < g.K ? __fadd_rn(ra[i].z, bias[k + 2]) : 0.f;
-                        ra[i].w = k + 3 < g.K ? __fadd_rn(ra[i].w, bias[k + 3]) : 0.f;
+                        const float4 b4 = load4(bias, k, g.K, biasvec);
+                        ra[i].x = k < g.K ? __fadd_rn(ra[i].x, b4.x) : 0.f;
+                        ra[i].y = k + 1 < g.K ? __fadd_rn(ra[i].y, b4.y) : 0.f;
+                        ra[i].z = k + 2 < g.K ? __fadd_rn(ra[i].z, b4.z) : 0.f;
+                        ra[i].w = k + 3 < g.K ? __fadd_rn(ra[i].w, b4.w) : 0.f;
                     }
                 }
                 if (!B_KN) {   // B [n][k]: like A

@@ -217,20 +217,20 @@ struct P2cuEncoder {
     std::vector<int> T, row_off;
     bool chunked = false;
     int mel_rows = 0, rows1 = 0, rows2 = 0, R_sub = 0, R = 0, Tmax = 0, L = 0;
-    long long s_total = 0, b_total = 0;
+    long long s_total = 0, b_total = 0, vt_total = 0;
     int srows = 0;
     float scale = 0.f;
 
     char* arena = nullptr;
     // device buffers
     float *mel, *s1, *s2dw, *s2, *s3dw, *s3, *flat, *x_sub, *x, *big, *lnbuf, *gated, *attn, *pe, *P, *s_ac, *s_bd,
-        *out;
+        *vt, *out;
     int8_t *q, *pe_q;
     float *qs, *pe_s;
     void* ws = nullptr;
     size_t ws_bytes = 0;
     int *d_mel_off, *d_h1_off, *d_h2_off, *d_sub_off, *d_row_off, *d_srow_off, *d_T, *d_gather, *d_scatter;
-    long long *d_s_off, *d_b_off;
+    long long *d_s_off, *d_b_off, *d_vt_off;
     p2cu::GemmGroup *g_ac, *g_bd, *g_av;
     int ng = 0, t_ac = 0, t_bd = 0, t_av = 0;
     int2* att_tiles = nullptr;   // fused attention (every window <= ATT_MAXT frames): (window, first query) per tile
@@ -342,11 +342,12 @@ int self_attention(P2cuEncoder& e, const DBlock& b, cudaStream_t s) {
         TRYC(p2cu::attn_softmax_launch(e.s_ac, e.s_bd, e.d_srow_off, e.d_s_off, e.d_b_off, e.d_T, e.n_win, H,
                                        e.srows, e.scale, s),
              "attention softmax");
+        TRYC(p2cu::v_transpose_launch(e.big, e.vt, e.d_row_off, e.d_vt_off, e.n_win, e.R, s), "attention v^T");
         p2cu::TcArgs c{};
-        c.src[0] = e.s_ac; c.src[1] = e.big;
+        c.src[0] = e.s_ac; c.src[1] = e.vt;
         c.dst[0] = e.attn; c.dst[1] = e.attn;
         c.err = a.err;
-        TRYC(p2cu::attn_tc_launch(e.tc_context, e.n_tc, e.t_tc_context, c, true, s), "attention context");
+        TRYC(p2cu::attn_tc_launch(e.tc_context, e.n_tc, e.t_tc_context, c, false, s), "attention context");
     } else if (e.n_att_tiles) {
         TRYC(p2cu::attn_fused_launch(e.big, e.P, b.bias_u, b.bias_v, e.d_row_off, e.att_tiles, e.n_att_tiles, e.Tmax,
                                      e.scale, e.attn, s),
@@ -505,38 +506,41 @@ int create_plan(const P2cuModel* m, const int* n_frames, int n_mel_win, int mode
 
     // attention tables and GEMM groups (one group per window and head)
     std::vector<int> srow_off{0};
-    std::vector<long long> s_off, b_off;
+    std::vector<long long> s_off, b_off, vt_off;
     std::vector<p2cu::GemmGroup> gac, gbd, gav;
     int tac = 0, tbd = 0, tav = 0;
     for (int w = 0; w < n_win; ++w) {
         const int t = e->T[w], Lw = 2 * t - 1, r0 = e->row_off[w];
         s_off.push_back(e->s_total);
         b_off.push_back(e->b_total);
+        const int ldS = (t + 3) & ~3, ldB = (Lw + 3) & ~3;   // 16-byte aligned score rows
         for (int h = 0; h < H; ++h) {
-            const long long sac = e->s_total + static_cast<long long>(h) * t * t;
-            const long long sbd = e->b_total + static_cast<long long>(h) * t * Lw;
+            const long long sac = e->s_total + static_cast<long long>(h) * t * ldS;
+            const long long sbd = e->b_total + static_cast<long long>(h) * t * ldB;
             p2cu::GemmGroup g{};
             // AC = (Q + bias_u) K^T: A = Q columns of QKV, B = K columns (transposed), C = S_ac
             g.M = t; g.N = t; g.K = DH; g.tile0 = tac;
             g.a_off = static_cast<long long>(r0) * 3 * D + h * DH; g.lda = 3 * D;
             g.b_off = static_cast<long long>(r0) * 3 * D + D + h * DH; g.ldb = 3 * D;
-            g.c_off = sac; g.ldc = t; g.bias_off = h * DH;
+            g.c_off = sac; g.ldc = ldS; g.bias_off = h * DH;
             gac.push_back(g); tac += p2cu::group_gemm_tiles(g.M, g.N);
             // BD = (Q + bias_v) P^T over this window's 2T-1 positions, rows Tmax-T .. Tmax+T-2 of P (the positions
             // T-1 .. -(T-1) of a window of T frames)
             g.N = Lw; g.tile0 = tbd;
             g.b_off = static_cast<long long>(e->Tmax - t) * D + h * DH; g.ldb = D;
-            g.c_off = sbd; g.ldc = Lw;
+            g.c_off = sbd; g.ldc = ldB;
             gbd.push_back(g); tbd += p2cu::group_gemm_tiles(g.M, g.N);
             // AV = S V into the concatenated heads [R][D]
             g.M = t; g.N = DH; g.K = t; g.tile0 = tav;
-            g.a_off = sac; g.lda = t;
+            g.a_off = sac; g.lda = ldS;
             g.b_off = static_cast<long long>(r0) * 3 * D + 2 * D + h * DH; g.ldb = 3 * D;
             g.c_off = static_cast<long long>(r0) * D + h * DH; g.ldc = D; g.bias_off = -1;
             gav.push_back(g); tav += p2cu::group_gemm_tiles(g.M, g.N);
         }
-        e->s_total += static_cast<long long>(H) * t * t;
-        e->b_total += static_cast<long long>(H) * t * Lw;
+        vt_off.push_back(e->vt_total);
+        e->vt_total += static_cast<long long>(H) * DH * ldS;
+        e->s_total += static_cast<long long>(H) * t * ldS;
+        e->b_total += static_cast<long long>(H) * t * ldB;
         srow_off.push_back(srow_off.back() + H * t);
     }
     e->srows = srow_off.back();
@@ -560,21 +564,22 @@ int create_plan(const P2cuModel* m, const int* n_frames, int n_mel_win, int mode
                     if (pass == 0) {   // AC = (Q + bias_u) K^T
                         g.N = t;
                         g.b_src = 0; g.b_off = static_cast<long long>(r0) * 3 * D + D + h * DH; g.ldb = 3 * D;
-                        g.c_dst = 0; g.c_off = gac[w * H + h].c_off; g.ldc = t;
+                        g.c_dst = 0; g.c_off = gac[w * H + h].c_off; g.ldc = gac[w * H + h].ldc;
                         g.bias_sel = 0;
                     } else {           // BD = (Q + bias_v) P^T over the window's 2T - 1 positions
                         g.N = Lw;
                         g.b_src = 1; g.b_off = static_cast<long long>(e->Tmax - t) * D + h * DH; g.ldb = D;
-                        g.c_dst = 1; g.c_off = gbd[w * H + h].c_off; g.ldc = Lw;
+                        g.c_dst = 1; g.c_off = gbd[w * H + h].c_off; g.ldc = gbd[w * H + h].ldc;
                         g.bias_sel = 1;
                     }
                     tcs.push_back(g);
                     ts += p2cu::tc_gemm_tiles(g.M, g.N);
-                    if (pass == 0) {   // context = S V into the concatenated heads
+                    if (pass == 0) {   // context = S V into the concatenated heads, V^T (K-major) from vt
                         p2cu::TcGroup c{};
+                        const int ldS = gac[w * H + h].ldc;
                         c.M = t; c.N = DH; c.K = t; c.tile0 = tc;
-                        c.a_src = 0; c.a_off = gac[w * H + h].c_off; c.lda = t;
-                        c.b_src = 1; c.b_off = static_cast<long long>(r0) * 3 * D + 2 * D + h * DH; c.ldb = 3 * D;
+                        c.a_src = 0; c.a_off = gac[w * H + h].c_off; c.lda = ldS;
+                        c.b_src = 1; c.b_off = vt_off[w] + static_cast<long long>(h) * DH * ldS; c.ldb = ldS;
                         c.c_dst = 0; c.c_off = static_cast<long long>(r0) * D + h * DH; c.ldc = D;
                         c.bias_sel = -1;
                         tcc.push_back(c);
@@ -626,6 +631,8 @@ int create_plan(const P2cuModel* m, const int* n_frames, int n_mel_win, int mode
         {reinterpret_cast<void**>(&e->P), static_cast<size_t>(L) * D * f},
         {reinterpret_cast<void**>(&e->s_ac), static_cast<size_t>(e->s_total) * f},
         {reinterpret_cast<void**>(&e->s_bd), static_cast<size_t>(e->b_total) * f},
+        {reinterpret_cast<void**>(&e->vt), e->attn_path == 0 ? static_cast<size_t>(e->vt_total) * f : 0},
+        {reinterpret_cast<void**>(&e->d_vt_off), n_win * sizeof(long long)},
         {reinterpret_cast<void**>(&e->out), static_cast<size_t>(Rs) * P2_JOINT_DIM * f},
         {&e->ws, e->ws_bytes},
         {reinterpret_cast<void**>(&e->d_mel_off), (n_mel_win + 1) * sizeof(int)},
@@ -677,6 +684,7 @@ int create_plan(const P2cuModel* m, const int* n_frames, int n_mel_win, int mode
         {e->d_T, Tw.data(), n_win * sizeof(int)},
         {e->d_s_off, s_off.data(), n_win * sizeof(long long)},
         {e->d_b_off, b_off.data(), n_win * sizeof(long long)},
+        {e->d_vt_off, vt_off.data(), n_win * sizeof(long long)},
         {e->g_ac, gac.data(), gac.size() * sizeof(p2cu::GemmGroup)},
         {e->g_bd, gbd.data(), gbd.size() * sizeof(p2cu::GemmGroup)},
         {e->g_av, gav.data(), gav.size() * sizeof(p2cu::GemmGroup)},
@@ -687,6 +695,8 @@ int create_plan(const P2cuModel* m, const int* n_frames, int n_mel_win, int mode
     for (const Copy& c : copies)
         if (c.bytes && (ce = cudaMemcpy(c.dst, c.src, c.bytes, cudaMemcpyHostToDevice)) != cudaSuccess) break;
     if (ce == cudaSuccess) ce = cudaMemset(e->mel, 0, static_cast<size_t>(e->mel_rows) * NMEL * f);
+    if (ce == cudaSuccess && e->attn_path == 0)   // V^T's padding columns stay zero
+        ce = cudaMemset(e->vt, 0, static_cast<size_t>(e->vt_total) * f);
     if (ce == cudaSuccess) ce = cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking);
     if (ce == cudaSuccess && mode != P2CU_EXACT)
         ce = p2cu::quant_rows_launch(e->pe, L, D, D, e->pe_q, e->pe_s, e->stream);

@@ -269,8 +269,9 @@ __global__ void __launch_bounds__(256) attn_softmax_kernel(float* s_ac, const fl
     const int local = row - srow_off[w];
     const int T = Tw[w], L = 2 * T - 1;
     const int i = local % T;
-    float* a = s_ac + s_off[w] + static_cast<long long>(local) * T;
-    const float* b = s_bd + b_off[w] + static_cast<long long>(local) * L + (T - 1 - i);
+    // score rows are stored with their lengths rounded up to a multiple of 4 floats (16-byte aligned rows)
+    float* a = s_ac + s_off[w] + static_cast<long long>(local) * ((T + 3) & ~3);
+    const float* b = s_bd + b_off[w] + static_cast<long long>(local) * ((L + 3) & ~3) + (T - 1 - i);
     float mx = -FLT_MAX;
     for (int j = threadIdx.x & 31; j < T; j += 32) {
         const float v = __fmul_rn(__fadd_rn(a[j], b[j]), scale);
@@ -444,6 +445,27 @@ __global__ void gather_rows_kernel(float* __restrict__ dst, const float* __restr
     if (i >= static_cast<size_t>(rows) * cols) return;
     const size_t r = i / cols, c = i % cols;
     dst[i] = src[static_cast<size_t>(map[r]) * cols + c];
+}
+
+// V of every (window, head) transposed: vt[block + d * ldT + j] = qkv[(r0 + j) * 3072 + 2048 + h * 128 + d], ldT = T
+// rounded up to a multiple of 4; block = vt_off[w] + h * 128 * ldT. One block per 32 rows x 32 columns of one head.
+__global__ void __launch_bounds__(256) v_transpose_kernel(const float* __restrict__ qkv, float* __restrict__ vt,
+                                                          const int* __restrict__ row_off,
+                                                          const long long* __restrict__ vt_off, int n_win, int rows) {
+    __shared__ float tile[32][33];
+    const int r0 = blockIdx.x * 32, h = blockIdx.y >> 2, d0 = (blockIdx.y & 3) * 32;
+    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;   // 32 x 8
+    for (int j = ty; j < 32; j += 8) {
+        const int r = r0 + j;
+        tile[j][tx] = r < rows ? qkv[static_cast<size_t>(r) * 3072 + 2048 + h * 128 + d0 + tx] : 0.f;
+    }
+    __syncthreads();
+    const int r = r0 + tx;
+    if (r >= rows) return;
+    const int w = find_window(row_off, n_win, r);
+    const int T = row_off[w + 1] - row_off[w], ldT = (T + 3) & ~3, j = r - row_off[w];
+    float* blk = vt + vt_off[w] + static_cast<long long>(h) * 128 * ldT;
+    for (int d = ty; d < 32; d += 8) blk[static_cast<size_t>(d0 + d) * ldT + j] = tile[tx][d];
 }
 
 __global__ void bias_rows_kernel(float* x, const float* __restrict__ b, size_t total, int N) {
@@ -818,6 +840,13 @@ cudaError_t sub_flatten_launch(const float* in, float* out, int rows, int W, int
     const size_t n = static_cast<size_t>(rows) * W * C;
     if (!n) return cudaSuccess;
     sub_flatten_kernel<<<blocks_for(n, 256), 256, 0, s>>>(in, out, rows, W, C);
+    return cudaGetLastError();
+}
+
+cudaError_t v_transpose_launch(const float* qkv, float* vt, const int* row_off, const long long* vt_off, int n_win,
+                               int rows, cudaStream_t s) {
+    if (rows <= 0) return cudaSuccess;
+    v_transpose_kernel<<<dim3((rows + 31) / 32, 32), 256, 0, s>>>(qkv, vt, row_off, vt_off, n_win, rows);
     return cudaGetLastError();
 }
 

@@ -49,6 +49,11 @@ cudaError_t sub_dwconv_launch(const float* in, const int* in_off, const int* out
 // [rows][W][C] -> [rows][C * W] (channel-major within a frame).
 cudaError_t sub_flatten_launch(const float* in, float* out, int rows, int W, int C, cudaStream_t s);
 
+// V (columns 2048 + 128 h .. of qkv [rows][3072]) of every window and head transposed into vt: the block of (window
+// w, head h) starts at vt_off[w] + h * 128 * ldT and holds [128][ldT], ldT = T rounded up to a multiple of 4.
+cudaError_t v_transpose_launch(const float* qkv, float* vt, const int* row_off, const long long* vt_off, int n_win,
+                               int rows, cudaStream_t s);
+
 // x[r][n] += b[n].
 cudaError_t bias_rows_launch(float* x, const float* b, int rows, int N, cudaStream_t s);
 
@@ -68,7 +73,8 @@ int group_gemm_tiles(int M, int N);
 
 // Attention scores of every (window, head, query) row, in place in S_ac: x_j = (ac[i][j] + bd[i][T-1-i+j]) * scale,
 // then softmax over j. srow_off: prefix offsets of the H*T rows per window; s_off / b_off: element offsets of each
-// window's S_ac / S_bd blocks; Tw: frames per window.
+// window's S_ac / S_bd blocks, whose rows are T and 2T - 1 floats rounded up to a multiple of 4 apart; Tw: frames per
+// window.
 cudaError_t attn_softmax_launch(float* s_ac, const float* s_bd, const int* srow_off, const long long* s_off,
                                 const long long* b_off, const int* Tw, int n_win, int H, int rows, float scale,
                                 cudaStream_t s);
