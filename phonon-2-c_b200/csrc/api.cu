@@ -215,7 +215,20 @@ int run_i8(int M, int N, int K, float alpha, const int8_t* q, const float* a_sca
         if ((rc = make_map(&tb0, q8, 1, N, K, ldb, atom, 128, atom, "B"))) return rc;
         tb1 = tb0;
     }
-    cudaError_t e = p2cu::fv_gemm_launch(bn, kind, ta, tb0, tb1, tout, p, s);
+    // Many tiles (large M): the persistent kernel, where it measured faster - expanded planes, or more than one
+    // 1024-row K block (with one K block from an int8 table or the code cache the one-tile-per-CTA kernel streams as
+    // fast). P2CU_PERSIST=1 forces it, 0 forbids it. Its epilogue reads the per-column constants as 16-byte vectors.
+    static int persist_env = -2;
+    if (persist_env == -2) {
+        const char* pe = getenv("P2CU_PERSIST");
+        persist_env = pe && pe[0] == '1' ? 1 : pe && pe[0] == '0' ? 0 : -1;
+    }
+    const bool vec_ok = aligned16(p.lo) && aligned16(p.hi) && aligned16(p.scales);
+    const bool many = p2cu::fv_gemm_p_tiles(M, N, bn, nblk) > p2cu::fv_gemm_p_min_tiles();
+    const bool persist = vec_ok && (persist_env == 1 ||
+                                    (persist_env == -1 && many && (kind != p2cu::KIND_TABLE || nblk > 1)));
+    cudaError_t e = persist ? p2cu::fv_gemm_p_launch(bn, kind, ta, tb0, tb1, tout, p, s)
+                            : p2cu::fv_gemm_launch(bn, kind, ta, tb0, tb1, tout, p, s);
     if (e == cudaSuccess && nblk > 1)
         e = p2cu::fv_combine_launch(static_cast<const float*>(ws), p.m_pad, nblk, a_scales, alpha, p.beta_zero, C, M,
                                     N, ldc, s);

@@ -37,6 +37,13 @@ struct FvGemmParams {
 cudaError_t fv_gemm_launch(int bn, int kind, const CUtensorMap& a, const CUtensorMap& b0, const CUtensorMap& b1,
                            const CUtensorMap& out, const FvGemmParams& p, cudaStream_t stream);
 
+// The persistent form of the same GEMM (fv_gemm_p.cu) for launches with many output tiles: same arguments and
+// results, one CTA per SM walking the tiles with the epilogue of one tile overlapping the MMAs of the next.
+cudaError_t fv_gemm_p_launch(int bn, int kind, const CUtensorMap& a, const CUtensorMap& b0, const CUtensorMap& b1,
+                             const CUtensorMap& out, const FvGemmParams& p, cudaStream_t stream);
+int fv_gemm_p_tiles(int M, int N, int bn, int ksplit);
+int fv_gemm_p_min_tiles();   // the SM count: below it every tile has an SM of its own anyway
+
 // C = fold of the workspace slices (fp32 f per 1024-row block) in block order, with the row scales.
 cudaError_t fv_combine_launch(const float* f, int m_pad, int nblk, const float* a_scales, float alpha, int beta_zero,
                               float* C, int M, int N, int ldc, cudaStream_t stream);

@@ -104,6 +104,10 @@ __device__ __forceinline__ void tma_store_wait_all() {
 __device__ __forceinline__ void tma_store_wait_read() {
     asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
 }
+// The same for all but the most recently committed store.
+__device__ __forceinline__ void tma_store_wait_read_1() {
+    asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+}
 
 // Programmatic dependent launch: let the next kernel in the stream begin, and wait for the previous ones' writes.
 __device__ __forceinline__ void griddep_launch_dependents() {

@@ -247,3 +247,72 @@ def test_every_tile_width_bitwise(cuda, tile):
                          timeout=300)
     assert out.returncode == 0, out.stderr[-3000:]
     assert json.loads(out.stdout.strip().splitlines()[-1]) == [True] * 4
+
+
+PERSIST_CHILD = r"""
+import json, sys
+import numpy as np
+sys.path.insert(0, {root!r})
+import __graft_entry__ as ge
+import torch
+pkg, orc = ge.load_package(), ge.load_oracle()
+from phonon2_b200 import synth
+from phonon2_b200.device import DeviceFiveValue
+dev = torch.device("cuda:0")
+res = []
+cases = [(2500, 1024, 4096, "int8w", 1.0, 0.0, False), (2500, 4096, 1024, "int8w", 0.5, 1.0, False),
+         (1300, 1024, 2048, "int8", 1.0, 1.0, False), (2500, 1024, 3072, "int8w", 1.0, 0.0, True),
+         (640, 2048, 1024, "int8", 1.0, 0.0, False), (375, 1024, 1024, "int8w", 1.0, 1.0, False)]
+for (M, K, N, mode, alpha, beta, codes) in cases:
+    w = synth.five_value(K, N, seed=M + N)
+    A = synth.activations(M, K, seed=K)
+    C0 = np.random.default_rng(1).standard_normal((M, N)).astype(np.float32)
+    B = DeviceFiveValue(w, dev, codes=codes)
+    A_d, C_d = torch.from_numpy(A).to(dev), torch.from_numpy(C0.copy()).to(dev)
+    m = pkg.MODES[mode]
+    nws = max(pkg.workspace_bytes(M, N, K, m), 16)
+    ws = torch.empty(nws, dtype=torch.uint8, device=dev)
+    pkg.sgemm_fvb(M, N, K, alpha, A_d.data_ptr(), K, B.struct, m, beta, C_d.data_ptr(), N, ws.data_ptr(), nws)
+    pkg.check_device()
+    want = orc.sgemm_i8(A, mode, C0.copy(), w=w, alpha=alpha, beta=beta)
+    res.append(bool(np.array_equal(C_d.cpu().numpy().view(np.uint32), want.view(np.uint32))))
+# an int8 table (q8b) through the same kernel
+M, K, N = 2000, 4096, 1024
+t = synth.int8_table(K, N, seed=3)
+A = synth.activations(M, K, seed=4)
+A_d = torch.from_numpy(A).to(dev)
+C_d = torch.zeros((M, N), dtype=torch.float32, device=dev)
+q8, sc = torch.from_numpy(t["q8"]).to(dev), torch.from_numpy(t["scales"]).to(dev)
+nws = pkg.workspace_bytes(M, N, K, pkg.INT8)
+ws = torch.empty(nws, dtype=torch.uint8, device=dev)
+pkg.sgemm_q8b(M, N, K, 1.0, A_d.data_ptr(), K, q8.data_ptr(), sc.data_ptr(), N, pkg.INT8, 0.0, C_d.data_ptr(), N,
+              ws.data_ptr(), nws)
+pkg.check_device()
+want = orc.sgemm_i8(A, "q8b", np.zeros((M, N), np.float32), q8=t)
+res.append(bool(np.array_equal(C_d.cpu().numpy().view(np.uint32), want.view(np.uint32))))
+print(json.dumps(res))
+"""
+
+
+@pytest.mark.parametrize("persist,tile", [("1", "128"), ("1", "256"), ("1", "64"), ("", "")])
+def test_persistent_kernel_bitwise(cuda, persist, tile):
+    """The persistent GEMM (many tiles; forced with P2CU_PERSIST=1 for every shape, including few-tile ones, or chosen
+    by tile count) against the restatement, bit for bit: every mode, beta 0 / 1 / alpha 1/2, K > 1024 through the
+    workspace slices, the code cache and an int8 table."""
+    import json
+    import os
+    import subprocess
+    import sys
+    from pathlib import Path
+    root = str(Path(__file__).resolve().parents[1])
+    env = dict(os.environ)
+    env.pop("P2CU_PERSIST", None)
+    env.pop("P2CU_TILE_N", None)
+    if persist:
+        env["P2CU_PERSIST"] = persist
+    if tile:
+        env["P2CU_TILE_N"] = tile
+    out = subprocess.run([sys.executable, "-c", PERSIST_CHILD.format(root=root)], env=env, capture_output=True,
+                         text=True, timeout=600)
+    assert out.returncode == 0, out.stderr[-3000:]
+    assert json.loads(out.stdout.strip().splitlines()[-1]) == [True] * 7
