@@ -387,22 +387,26 @@ def shard_windows(frames, world):
     return [sorted(v) for v in out]
 
 
-def encoder_workload(name):
+def encoder_workload(name, windows=0):
     from phonon2_b200 import model as M
     if name == "long-audio":
-        return M.long_audio_windows(0), ("BASELINE configs[3]: a 32-minute synthetic log-mel stream as 64 windows "
-                                         "of U(25, 35) s (seeded), sharded over the GPUs longest-first")
+        frames = M.long_audio_windows(0)
+        if windows:
+            frames = frames[:windows]
+        return frames, ("BASELINE configs[3]: a 32-minute synthetic log-mel stream as 64 windows of U(25, 35) s "
+                        "(seeded), sharded over the GPUs longest-first" + (f"; the first {windows} windows" if windows
+                                                                           else ""))
     if name == "window":
         return [3000], "BASELINE configs[2]: one 30 s window (mel [3000 x 128], T' = 375)"
     return [300], "BASELINE configs[4]: one 3 s utterance (mel [300 x 128], T' = 38)"
 
 
-def encoder_ours(args, world, rank, local, torch, pkg, workload="long-audio", steps=5):
+def encoder_ours(args, world, rank, local, torch, pkg, workload="long-audio", steps=5, windows=0):
     """The encoder on this rank's share of the windows: device-timed graph launches (mel resident), then end to end
     through p2_b200_encode_windows (host mel in, host frames out, this rank's GPU)."""
     from phonon2_b200 import model as M
     from phonon2_b200.device import device_view
-    frames, desc = encoder_workload(workload)
+    frames, desc = encoder_workload(workload, windows)
     mine = shard_windows(frames, world)[rank]
     sm = M.SyntheticModel(seed=1)
     dm = pkg.DeviceModel(sm.struct, codes=args.weights == "codes")
@@ -456,14 +460,87 @@ def encoder_ours(args, world, rank, local, torch, pkg, workload="long-audio", st
     return res
 
 
-def encoder_reference(seconds=15.0, workload="long-audio"):
+def run_encoder_only(args, world, rank, local):
+    """--workload encoder: the encoder alone, as its own line (the metric's "encoder audio-sec/sec")."""
+    import torch
+    pkg = ge.load_package()
+    torch.cuda.set_device(local)
+    enc = encoder_ours(args, world, rank, local, torch, pkg, workload=args.encoder_config, steps=args.steps,
+                       windows=args.windows)
+    if rank != 0:
+        return
+    line = {"metric": "encoder audio-sec/sec", "value": enc["value"], "unit": "audio-s/s", "n_gpus": world,
+            "steps": args.steps, "warmup": 2, "ms_per_step": enc["ms_per_step"], "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "int8" if args.mode != "exact" else "f32",
+            "data": "synthetic", "config": {"workload": enc["workload"], "mode": args.mode, "weights": args.weights,
+                                            "rows_per_gpu": enc["rows_per_gpu"]},
+            "e2e": enc["e2e"]}
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = encoder_reference(workload=args.encoder_config, windows=args.windows)
+    print(json.dumps(line))
+
+
+def run_gemm_sweep(args):
+    """--workload gemm-sweep: the five-value GEMM alone (quantised A resident) at growing M, K = 1024, N = 4096 (the
+    north star's large-M shape) and K = 4096, N = 1024; planes and the code cache. One JSON line per case."""
+    import torch
+    pkg = ge.load_package()
+    from phonon2_b200 import synth
+    from phonon2_b200.device import DeviceFiveValue
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    s = torch.cuda.Stream()
+    for (M, K, N) in [(375, 1024, 4096), (4096, 1024, 4096), (8192, 1024, 4096), (24000, 1024, 4096),
+                      (8192, 4096, 1024)]:
+        w = synth.five_value(K, N, seed=1)
+        for codes in (False, True):
+            B = DeviceFiveValue(w, dev, codes=codes)
+            A = torch.from_numpy(synth.activations(M, K, seed=2)).to(dev)
+            q = torch.empty((M, K), dtype=torch.int8, device=dev)
+            sc = torch.empty(M, dtype=torch.float32, device=dev)
+            pkg.quant_rows(A.data_ptr(), M, K, K, q.data_ptr(), sc.data_ptr())
+            C = torch.zeros((M, N), dtype=torch.float32, device=dev)
+            nws = max(pkg.q8a_workspace_bytes(M, N, K), 256)
+            ws = torch.empty(nws, dtype=torch.uint8, device=dev)
+            mode = pkg.MODES[args.mode if args.mode != "exact" else "int8w"]
+
+            def run():
+                pkg.sgemm_fvb_q8a(M, N, K, 1.0, q.data_ptr(), sc.data_ptr(), B.struct, mode, 0.0, C.data_ptr(), N,
+                                  ws.data_ptr(), nws, s)
+            with torch.cuda.stream(s):
+                for _ in range(args.warmup):
+                    run()
+                s.synchronize()
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=s):
+                    for _ in range(10):
+                        run()
+                g.replay()
+                s.synchronize()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                reps = max(1, args.steps // 10)
+                e0.record(s)
+                for _ in range(reps):
+                    g.replay()
+                e1.record(s)
+                e1.synchronize()
+            pkg.check_device(s)
+            us = e0.elapsed_time(e1) / (10 * reps) * 1e3
+            tmacs = M * K * N / (us / 1e6) / 1e12
+            print(json.dumps({"metric": "five-value int8 GEMM TMAC/s", "M": M, "K": K, "N": N, "mode": args.mode,
+                              "weights": "codes" if codes else "planes", "us": us, "value": tmacs, "unit": "TMAC/s",
+                              "frac_of_nominal_int8": tmacs / 2250.0,
+                              "hbm_bound_us": (M * K + (K * N if codes else 3 * K * N // 8) + 4 * M * N) / 6534.8e3}))
+
+
+def encoder_reference(seconds=15.0, workload="long-audio", windows=0):
     """phonon-2-c's own p2_encoder (exact, its only x86 path) on the host cores, on the first windows of the
     workload for about `seconds`."""
     orc = ge.load_oracle()
     if not orc.ref_available():
         return None
     from phonon2_b200 import model as M
-    frames, desc = encoder_workload(workload)
+    frames, desc = encoder_workload(workload, windows)
     sm = M.SyntheticModel(seed=1)
     done, t0, n = 0.0, time.perf_counter(), 0
     while True:
@@ -524,12 +601,23 @@ def main():
                          "the int8w code cache (the reference's P2_CACHE_CODES), int8w only")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-encoder", action="store_true", help="skip the encoder (config 3) part of the line")
+    ap.add_argument("--workload", choices=["block-gemms", "encoder", "gemm-sweep"], default="block-gemms",
+                    help="block-gemms: configs[1] with the encoder object (default); encoder: the encoder alone; "
+                         "gemm-sweep: the GEMM alone at growing M (one line per case)")
+    ap.add_argument("--encoder-config", choices=["long-audio", "window", "short"], default="long-audio",
+                    help="--workload encoder: configs[3] (64 windows), [2] (one 30 s window) or [4] (3 s)")
+    ap.add_argument("--windows", type=int, default=0, help="--workload encoder long-audio: only the first N windows")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     world, rank, local = dist_setup(args)
     try:
         if args.impl == "reference":
             run_reference(args, world, rank)
+        elif args.workload == "encoder":
+            run_encoder_only(args, world, rank, local)
+        elif args.workload == "gemm-sweep":
+            if rank == 0:
+                run_gemm_sweep(args)
         else:
             run_ours(args, world, rank, local)
     finally:
