@@ -153,7 +153,7 @@ typedef struct P2cuModel P2cuModel;
 typedef struct P2cuEncoder P2cuEncoder;
 
 /* Copy the encoder weights of `m` (host pointers, as phonon-2-c's loader maps them) into one allocation on the current
- * device. codes != 0 also builds the int8w code plane of every five-value weight there (the reference's
+ * device, and the decoder's fp32 tables too when m->dec.embed_w is set. codes != 0 also builds the int8w code plane of every five-value weight there (the reference's
  * P2_CACHE_CODES, K * N bytes each), which the int8w GEMMs then stream instead of expanding the planes. */
 P2CU_API int p2cu_model_upload(const P2Model *m, int codes, P2cuModel **out);
 P2CU_API void p2cu_model_free(P2cuModel *m);
@@ -173,6 +173,29 @@ P2CU_API float *p2cu_encoder_mel(P2cuEncoder *e);
 P2CU_API float *p2cu_encoder_out(P2cuEncoder *e);
 /* One forward pass over the plan's input on `stream` (one graph launch). Runs on one plan must not overlap. */
 P2CU_API int p2cu_encoder_run(P2cuEncoder *e, void *stream);
+
+/* ---- The greedy TDT decoder on the device (csrc/decoder.c) ------------------------------------------------------
+ * p2cu_decoder_create allocates the state and token buffers of up to max_windows windows (at most 1024) of up to
+ * max_frames encoder frames together; the calls after it allocate nothing. The model must have been uploaded with its
+ * decoder tables. The decoder's kernel is one cooperative launch with one CTA on each SM. */
+typedef struct P2cuDecoder P2cuDecoder;
+P2CU_API int p2cu_decoder_create(const P2cuModel *m, int max_windows, int max_frames, P2cuDecoder **out);
+P2CU_API void p2cu_decoder_destroy(P2cuDecoder *d);
+/* Greedy decoding (csrc/decoder.c:100-141) of n_windows windows whose encoder frames are stacked in `enc` (device,
+ * [sum n_frames][640], 16-byte aligned); n_frames is a host array. Asynchronous on `stream`. */
+P2CU_API int p2cu_decode(P2cuDecoder *d, const float *enc, const int *n_frames, int n_windows, void *stream);
+/* After p2cu_decode: synchronises `stream`, writes offsets[0..n_windows] (window w's tokens are
+ * [offsets[w], offsets[w + 1]) of the decode's list) and copies the first min(cap, total) tokens into `tokens`.
+ * Returns the total token count, or a negative P2CU_E* code. */
+P2CU_API int p2cu_decoder_read(P2cuDecoder *d, int *offsets, P2Token *tokens, int cap, void *stream);
+/* The same lists on the device: tokens as [total][3] ints (id, frame, duration), offsets [n_windows + 1]. */
+P2CU_API const int *p2cu_decoder_tokens(const P2cuDecoder *d);
+P2CU_API const int *p2cu_decoder_offsets(const P2cuDecoder *d);
+/* One prediction-network step (csrc/decoder.c:62-74) on device pointers: state is an LSTMState (h[2][640] then
+ * c[2][640]) updated in place, dec_out [640]. Asynchronous on `stream`. */
+P2CU_API int p2cu_decoder_step(P2cuDecoder *d, int token_id, float *state, float *dec_out, void *stream);
+/* The joint network (csrc/decoder.c:78-88) on device pointers: logits [8198]. Asynchronous on `stream`. */
+P2CU_API int p2cu_joint(P2cuDecoder *d, const float *enc_t, const float *dec_out, float *logits, void *stream);
 
 #ifdef __cplusplus
 }

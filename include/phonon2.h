@@ -139,6 +139,18 @@ typedef struct {
     size_t         map_len;
 } P2Model;
 
+/* csrc/phonon2.h:210-220 */
+typedef struct {
+    float h[P2_LSTM_LAYERS][P2_LSTM_HIDDEN];
+    float c[P2_LSTM_LAYERS][P2_LSTM_HIDDEN];
+} LSTMState;
+
+typedef struct {
+    int id;        /* token id, never blank */
+    int frame;     /* encoder frame it was emitted at */
+    int duration;  /* frames the decoder then advanced, 0..4 */
+} P2Token;
+
 /* Activations prepared for the int8 GEMMs (csrc/phonon2.h:432-436). In this build the rows given to p2_quant_row
  * are kept as fp32 in `q` (a buffer of the calling thread) and quantised on the GPU inside the GEMM, with the
  * reference's rounding; `scales` is NULL. Callers that only pass a QuantA from prepare to the GEMM see no
@@ -173,6 +185,28 @@ P2_API int p2_encoder_chunked(const P2Model *m, const float *mel, int n_frames, 
  * Each GPU keeps its last two plans (window sets) for reuse. Returns 0, or -1 with a message on stderr. */
 P2_API int p2_b200_encode_windows(const P2Model *m, const float *mel, const int *n_frames, int n_windows,
                                   const int *devices, int n_devices, float *out);
+
+/* The prediction network's step (csrc/phonon2.h:400-401, csrc/decoder.c:62-74): embedding row of token_id, two LSTM
+ * layers updating *state, decoder projector into dec_out [640]. Host pointers; runs on the calling thread's GPU with
+ * the model's decoder tables uploaded there on first use. */
+P2_API void p2_decoder_step(const P2Model *m, int token_id, LSTMState *state, float *dec_out);
+
+/* The joint network (csrc/phonon2.h:403-404, csrc/decoder.c:78-88): logits [8198] = head . relu(enc_t + dec_out) +
+ * bias, 8193 token logits then 5 duration logits. Host pointers, calling thread's GPU. */
+P2_API void p2_joint(const P2Model *m, const float *enc_t, const float *dec_out, float *logits);
+
+/* Greedy TDT decoding of T encoder frames [T x 640] (csrc/phonon2.h:406-407, csrc/decoder.c:100-141): the whole
+ * loop runs as one launch on the calling thread's GPU. *out_tokens is malloc'd (the caller frees it) and the token
+ * count returned, or -1 with a message on stderr. */
+P2_API int p2_greedy_decode(const P2Model *m, const float *enc_out, int T, P2Token **out_tokens);
+
+/* Encoder and greedy decoder over a batch of windows spread across GPUs, the encoder frames staying on the device. No
+ * counterpart in the reference, whose engine runs p2_encoder then p2_greedy_decode window after window
+ * (csrc/engine.c:100-125, 311-357). Windows, mel layout and GPU placement as p2_b200_encode_windows. tokens[w] receives
+ * a malloc'd array of window w's tokens (NULL when it has none; the caller frees each) and n_tokens[w] their count.
+ * Returns 0, or -1 with a message on stderr. */
+P2_API int p2_b200_transcribe_windows(const P2Model *m, const float *mel, const int *n_frames, int n_windows,
+                                      const int *devices, int n_devices, P2Token **tokens, int *n_tokens);
 
 #ifdef __cplusplus
 }

@@ -245,6 +245,46 @@ def ref_encoder(model_struct, mel: np.ndarray, mode: str = "exact", chunked: boo
         _libc.free(out)
 
 
+def _ref_decoder():
+    L = ref()
+    if not hasattr(L, "_dec_ready"):
+        L.p2_greedy_decode.argtypes = [C.c_void_p, _f32p, C.c_int, C.POINTER(C.c_void_p)]
+        L.p2_greedy_decode.restype = C.c_int
+        L.p2_decoder_step.argtypes = [C.c_void_p, C.c_int, _f32p, _f32p]
+        L.p2_decoder_step.restype = None
+        L.p2_joint.argtypes = [C.c_void_p, _f32p, _f32p, _f32p]
+        L.p2_joint.restype = None
+        L._dec_ready = True
+    return L
+
+
+def ref_greedy_decode(model_struct, enc: np.ndarray) -> np.ndarray:
+    """phonon-2-c's p2_greedy_decode (csrc/decoder.c:100-141) on frames [T, 640]: int32 [n, 3] (id, frame, duration)."""
+    L = _ref_decoder()
+    enc = np.ascontiguousarray(enc, np.float32)
+    out = C.c_void_p()
+    n = L.p2_greedy_decode(C.addressof(model_struct), enc, enc.shape[0], C.byref(out))
+    try:
+        if n <= 0:
+            return np.zeros((0, 3), np.int32)
+        return np.ctypeslib.as_array(C.cast(out, C.POINTER(C.c_int)), shape=(n, 3)).copy()
+    finally:
+        _libc.free(out)
+
+
+def ref_decoder_step(model_struct, token: int, state: np.ndarray, dec_out: np.ndarray) -> None:
+    """phonon-2-c's p2_decoder_step (csrc/decoder.c:62-74): state float32 [2, 2, 640] (h, c) in place, dec_out [640]."""
+    _ref_decoder().p2_decoder_step(C.addressof(model_struct), token, state, dec_out)
+
+
+def ref_joint(model_struct, enc_t: np.ndarray, dec_out: np.ndarray) -> np.ndarray:
+    """phonon-2-c's p2_joint (csrc/decoder.c:78-88): logits float32 [8198]."""
+    logits = np.zeros(8198, np.float32)
+    _ref_decoder().p2_joint(C.addressof(model_struct), np.ascontiguousarray(enc_t, np.float32),
+                            np.ascontiguousarray(dec_out, np.float32), logits)
+    return logits
+
+
 class _QuantA(C.Structure):   # csrc/phonon2.h:432-436
     _fields_ = [("q", C.c_void_p), ("scales", C.c_void_p), ("M", C.c_int), ("K", C.c_int)]
 

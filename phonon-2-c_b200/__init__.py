@@ -79,10 +79,23 @@ SIGNATURES = {
     "p2cu_encoder_mel": (_vp, [_vp]),
     "p2cu_encoder_out": (_vp, [_vp]),
     "p2cu_encoder_run": (_i, [_vp, _vp]),
-    # include/phonon2.h: the reference's encoder entry points
+    "p2cu_decoder_create": (_i, [_vp, _i, _i, C.POINTER(_vp)]),
+    "p2cu_decoder_destroy": (None, [_vp]),
+    "p2cu_decode": (_i, [_vp, _vp, C.POINTER(_i), _i, _vp]),
+    "p2cu_decoder_read": (_i, [_vp, C.POINTER(_i), _vp, _i, _vp]),
+    "p2cu_decoder_tokens": (_vp, [_vp]),
+    "p2cu_decoder_offsets": (_vp, [_vp]),
+    "p2cu_decoder_step": (_i, [_vp, _i, _vp, _vp, _vp]),
+    "p2cu_joint": (_i, [_vp, _vp, _vp, _vp, _vp]),
+    # include/phonon2.h: the reference's encoder and decoder entry points
     "p2_encoder": (_i, [_vp, _vp, _i, C.POINTER(_vp), C.POINTER(_i)]),
     "p2_encoder_chunked": (_i, [_vp, _vp, _i, C.POINTER(_vp), C.POINTER(_i)]),
     "p2_b200_encode_windows": (_i, [_vp, _vp, C.POINTER(_i), _i, C.POINTER(_i), _i, _vp]),
+    "p2_decoder_step": (None, [_vp, _i, _vp, _vp]),
+    "p2_joint": (None, [_vp, _vp, _vp, _vp]),
+    "p2_greedy_decode": (_i, [_vp, _vp, _i, C.POINTER(_vp)]),
+    "p2_b200_transcribe_windows": (_i, [_vp, _vp, C.POINTER(_i), _i, C.POINTER(_i), _i, C.POINTER(_vp),
+                                        C.POINTER(_i)]),
     # include/blas.h: the reference's host-pointer ABI
     "p2_sgemm": (None, [_i, _i, _i, _i, _i, _f, _vp, _i, _vp, _i, _f, _vp, _i]),
     "p2_sgemm_st": (None, [_i, _i, _i, _i, _i, _f, _vp, _i, _vp, _i, _f, _vp, _i]),
@@ -234,7 +247,7 @@ def host_sgemm(transA, transB, A, B, out, alpha=1.0, beta=0.0):
 # ---- the encoder (include/p2cuda.h device plans, include/phonon2.h host entry) --------------------------------------
 
 class DeviceModel:
-    """p2cu_model_upload: a P2Model's encoder weights on the current device."""
+    """p2cu_model_upload: a P2Model's encoder weights (and decoder tables, when it has them) on the current device."""
 
     def __init__(self, model_struct, codes: bool = False):
         self.ptr = C.c_void_p()
@@ -320,3 +333,106 @@ def host_encode_windows(model_struct, mels, devices=None):
         raise Error(rc, "p2_b200_encode_windows failed (see stderr)")
     offs = _np.cumsum([0] + T)
     return [out[offs[i]:offs[i + 1]] for i in range(len(mels))]
+
+
+# ---- the greedy TDT decoder (include/p2cuda.h device plans, include/phonon2.h host entry) ----------------------------
+
+def _tokens_array(ptr, n: int):
+    """n P2Tokens at ptr as an int32 [n, 3] array (id, frame, duration), copied."""
+    import numpy as _np
+    if n <= 0:
+        return _np.zeros((0, 3), _np.int32)
+    return _np.ctypeslib.as_array(C.cast(ptr, C.POINTER(C.c_int)), shape=(n, 3)).copy()
+
+
+class Decoder:
+    """p2cu_decoder_create: state and token buffers for up to max_windows windows of max_frames frames together."""
+
+    def __init__(self, model: DeviceModel, max_windows: int, max_frames: int):
+        self.model = model
+        self.ptr = C.c_void_p()
+        check(lib().p2cu_decoder_create(model.ptr, max_windows, max_frames, C.byref(self.ptr)))
+        self.n_windows = 0
+
+    def decode(self, enc_ptr: int, n_frames, stream=None) -> None:
+        """p2cu_decode over device frames at enc_ptr ([sum n_frames, 640]), asynchronous on `stream`."""
+        fr = [int(n) for n in n_frames]
+        arr = (C.c_int * len(fr))(*fr)
+        check(lib().p2cu_decode(self.ptr, enc_ptr, arr, len(fr), stream_ptr(stream)))
+        self.n_windows = len(fr)
+
+    def read(self, stream=None):
+        """p2cu_decoder_read: per-window int32 [n_i, 3] token arrays (id, frame, duration)."""
+        import numpy as _np
+        offs = (C.c_int * (self.n_windows + 1))()
+        total = lib().p2cu_decoder_read(self.ptr, offs, None, 0, stream_ptr(stream))
+        check(min(total, 0))
+        toks = _np.zeros((max(total, 1), 3), _np.int32)
+        if total > 0:
+            got = lib().p2cu_decoder_read(self.ptr, offs, toks.ctypes.data, total, stream_ptr(stream))
+            check(min(got, 0))
+        return [toks[offs[i]:offs[i + 1]].copy() for i in range(self.n_windows)]
+
+    def step(self, token: int, state_ptr: int, dec_ptr: int, stream=None) -> None:
+        check(lib().p2cu_decoder_step(self.ptr, token, state_ptr, dec_ptr, stream_ptr(stream)))
+
+    def joint(self, enc_ptr: int, dec_ptr: int, logits_ptr: int, stream=None) -> None:
+        check(lib().p2cu_joint(self.ptr, enc_ptr, dec_ptr, logits_ptr, stream_ptr(stream)))
+
+    def close(self) -> None:
+        if self.ptr:
+            lib().p2cu_decoder_destroy(self.ptr)
+            self.ptr = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def host_greedy_decode(model_struct, enc):
+    """p2_greedy_decode on host frames [T, 640]: int32 [n, 3] tokens (id, frame, duration)."""
+    import numpy as _np
+    enc = _np.ascontiguousarray(enc, dtype=_np.float32)
+    out = C.c_void_p()
+    n = lib().p2_greedy_decode(C.addressof(model_struct), enc.ctypes.data, enc.shape[0], C.byref(out))
+    if n < 0:
+        raise Error(n, "p2_greedy_decode failed (see stderr)")
+    try:
+        return _tokens_array(out, n)
+    finally:
+        C.CDLL(None).free(out)
+
+
+def host_decoder_step(model_struct, token: int, state, dec_out) -> None:
+    """p2_decoder_step on host arrays: state float32 [2, 2, 640] (h then c) updated in place, dec_out [640]."""
+    lib().p2_decoder_step(C.addressof(model_struct), token, state.ctypes.data, dec_out.ctypes.data)
+
+
+def host_joint(model_struct, enc_t, dec_out, logits) -> None:
+    """p2_joint on host arrays: logits float32 [8198]."""
+    lib().p2_joint(C.addressof(model_struct), enc_t.ctypes.data, dec_out.ctypes.data, logits.ctypes.data)
+
+
+def host_transcribe_windows(model_struct, mels, devices=None):
+    """p2_b200_transcribe_windows: a list of host mel arrays [n_i, 128] -> per-window int32 [k, 3] tokens, encoder
+    and decoder on the device, windows spread over `devices` (all visible GPUs when None)."""
+    import numpy as _np
+    frames = [int(m.shape[0]) for m in mels]
+    stacked = _np.ascontiguousarray(_np.concatenate(mels), dtype=_np.float32)
+    fr = (C.c_int * len(frames))(*frames)
+    devs = None if not devices else (C.c_int * len(devices))(*devices)
+    toks = (C.c_void_p * len(frames))()
+    counts = (C.c_int * len(frames))()
+    rc = lib().p2_b200_transcribe_windows(C.addressof(model_struct), stacked.ctypes.data, fr, len(frames), devs,
+                                          len(devices) if devices else 0, toks, counts)
+    if rc != 0:
+        raise Error(rc, "p2_b200_transcribe_windows failed (see stderr)")
+    res = []
+    libc = C.CDLL(None)
+    for i in range(len(frames)):
+        res.append(_tokens_array(toks[i], counts[i]))
+        if toks[i]:
+            libc.free(C.c_void_p(toks[i]))
+    return res

@@ -324,7 +324,7 @@ int p2cu_check_device(void* stream) {
     if ((e = cudaMemcpyFromSymbol(&v, g_dev_err, sizeof(v))) != cudaSuccess) return cuda_fail(e, "error word");
     if (v) {
         cudaMemcpyToSymbol(g_dev_err, &zero, sizeof(zero));
-        return fail(P2CU_EDEVICE, "a kernel stopped waiting on a barrier (code %u)", v);
+        return fail(P2CU_EDEVICE, "a kernel stopped early and reported device error code %u", v);
     }
     return P2CU_OK;
 }

@@ -74,7 +74,7 @@ const char *p2_gemm_mode(void)
 
 int p2_gemm_exact(void) { return gemm_mode() == P2CU_EXACT; }
 
-/* For the library's encoder entry points (encoder_host.cu): the mode in P2CU_* numbering. Not exported. */
+/* For the library's encoder entry points (host_entry.cu): the mode in P2CU_* numbering. Not exported. */
 int p2b_gemm_mode(void) { return gemm_mode(); }
 
 /* ---- per-thread context ---- */
@@ -288,7 +288,7 @@ static Entry *table_entry(const signed char *B, const float *scales, int K, int 
     return e;
 }
 
-void p2b_release_encoder_models(void);   /* encoder_host.cu */
+void p2b_release_encoder_models(void);   /* host_entry.cu */
 
 void p2_b200_release_weights(void)
 {

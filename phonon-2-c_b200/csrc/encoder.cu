@@ -24,6 +24,7 @@
 #include "encoder_ops.h"
 #include "attn_tc.h"
 #include "kernels.h"
+#include "model.h"
 
 namespace {
 
@@ -34,33 +35,10 @@ constexpr int SUBC = P2_SUB_CHANNELS, NMEL = P2_N_MELS;
 
 int conv_out(int n) { return (n + 2 - 3) / 2 + 1; }   // csrc/encoder.c:174
 
-// A GEMM weight on the device.
-struct DWeight {
-    int kind = -1;   // P2_W_FV, P2_W_I8, P2_W_F32
-    int K = 0, N = 0;
-    P2cuFiveValue fv{};
-    const int8_t* q8 = nullptr;
-    const float* scales = nullptr;
-    const float* f32 = nullptr;
-};
-
-struct DBlock {
-    const float *n_ff1_w, *n_ff1_b, *n_sa_w, *n_sa_b, *n_conv_w, *n_conv_b, *n_ff2_w, *n_ff2_b, *n_out_w, *n_out_b;
-    const float *bias_u, *bias_v, *dw_w, *dw_b;
-    DWeight ff1a, ff1b, qkv, pos, out, pw1, pw2, ff2a, ff2b;
-};
+using p2cu::DWeight;
+using p2cu::DBlock;
 
 }  // namespace
-
-struct P2cuModel {
-    int device = 0;
-    char* arena = nullptr;
-    size_t bytes = 0;
-    int codes = 0;
-    const float *c0w, *c0b, *c2w, *c2b, *c3w, *c3b, *c5w, *c5b, *c6w, *c6b, *lin_b, *proj_b;
-    DWeight lin, proj;
-    DBlock blk[NB];
-};
 
 namespace {
 
@@ -154,6 +132,22 @@ int upload_model(const P2Model* m, int codes, P2cuModel** out) {
     }
     u.weight(m->enc.projector_w, D, P2_JOINT_DIM, &d->proj, "encoder_projector.weight");
     u.f32(m->enc.projector_b, P2_JOINT_DIM, &d->proj_b, "encoder_projector.bias");
+    const DecoderWeights& dw = m->dec;
+    if (dw.embed_w) {   // a model without decoder tables uploads the encoder alone
+        constexpr size_t HID = P2_LSTM_HIDDEN, G4 = 4 * HID;
+        d->has_dec = 1;
+        u.f32(dw.embed_w, static_cast<size_t>(P2_VOCAB) * P2_EMBED_DIM, &d->embed, "decoder.embedding");
+        for (int l = 0; l < 2; ++l) {
+            u.f32(dw.lstm_w_ih[l], G4 * (l ? HID : P2_EMBED_DIM), &d->wih[l], "decoder.lstm.weight_ih");
+            u.f32(dw.lstm_w_hh[l], G4 * HID, &d->whh[l], "decoder.lstm.weight_hh");
+            u.f32(dw.lstm_b_ih[l], G4, &d->bih[l], "decoder.lstm.bias_ih");
+            u.f32(dw.lstm_b_hh[l], G4, &d->bhh[l], "decoder.lstm.bias_hh");
+        }
+        u.f32(dw.proj_w, static_cast<size_t>(P2_JOINT_DIM) * HID, &d->dproj, "decoder_projector.weight");
+        u.f32(dw.proj_b, P2_JOINT_DIM, &d->dproj_b, "decoder_projector.bias");
+        u.f32(dw.head_w, static_cast<size_t>(P2_N_LOGITS) * P2_JOINT_DIM, &d->head, "joint.head.weight");
+        u.f32(dw.head_b, P2_N_LOGITS, &d->head_b, "joint.head.bias");
+    }
     if (u.bad) {
         delete d;
         return fail_fmt(P2CU_EINVAL, "p2cu_model_upload: %s", u.what);

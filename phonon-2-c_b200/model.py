@@ -3,7 +3,8 @@ seeded synthetic encoder in them.
 
 A ``SyntheticModel`` owns numpy arrays for every encoder tensor and a ``P2Model`` whose pointers point into them, the
 way phonon-2-c's loader points a P2Model into its weights.bin mapping. Anything that takes a ``const P2Model *`` can
-take ``ctypes.byref(model.struct)``. The decoder tables are left NULL: the encoder never reads them.
+take ``ctypes.byref(model.struct)``. The decoder tables are fp32 as the loader expands them (``decoder=False`` leaves
+them NULL: the encoder never reads them).
 
 Distributions (the BASELINE configs 2-4): five-value weights as ``synth.five_value`` (P(0) = 1/3, lo ~ U(0.005, 0.02),
 hi = lo * U(2, 4), fp16 values); fp32 norms and biases N(0, 0.02); LayerNorm gains ``1 + N(0, 0.02)`` by default
@@ -22,6 +23,9 @@ from . import synth
 D, H, DH, FF, NB, KC = 1024, 8, 128, 4096, 24, 9
 SUBC, NMEL, JOINT = 256, 128, 640
 LSTM_LAYERS, DEC_OWNED = 2, 8
+HID, EMB, VOCAB, BLANK, N_DUR = 640, 640, 8193, 8192, 5
+MAX_SYMBOLS = 10   # tokens at one frame before the decoder moves on (csrc/phonon2.h:92)
+LOGITS = VOCAB + N_DUR
 W_F32, W_I8, W_FV = 0, 8, 5
 
 
@@ -83,7 +87,7 @@ def _seed(base: int, name: str) -> int:
 class SyntheticModel:
     """A seeded random encoder laid out as phonon-2-c's P2Model (``struct``), arrays kept alive by this object."""
 
-    def __init__(self, seed: int = 0, gamma: str = "unit"):
+    def __init__(self, seed: int = 0, gamma: str = "unit", decoder: bool = True):
         if gamma not in ("unit", "small"):
             raise ValueError("gamma is 'unit' or 'small'")
         self.seed, self.gamma = seed, gamma
@@ -126,6 +130,40 @@ class SyntheticModel:
             b.norm_out_w, b.norm_out_b = self._norm(p + "norm_out")
         self._table(e.projector_w, "encoder_projector.weight", D, JOINT)
         e.projector_b = self._normal("encoder_projector.bias", JOINT, 0.02)
+        if decoder:
+            self._decoder()
+
+    def _decoder(self) -> None:
+        """The TDT prediction and joint networks as the loader leaves them (csrc/weights.c:498-512): fp32 tables.
+        PyTorch-style uniform(+-1/sqrt(640)) LSTM and projector weights, a zero blank embedding row, and a joint head
+        whose blank logit is biased up so that blanks and tokens alternate as in speech."""
+        d = self.struct.dec
+        H = HID
+        bound = 1.0 / np.sqrt(H)
+
+        def uniform(name, shape):
+            rng = np.random.default_rng(_seed(self.seed, name))
+            return self._keep(name, rng.uniform(-bound, bound, shape).astype(np.float32))
+
+        rng = np.random.default_rng(_seed(self.seed, "decoder.embedding.weight"))
+        emb = rng.standard_normal((VOCAB, EMB)).astype(np.float32)
+        emb[BLANK] = 0.0
+        d.embed_w = self._keep("decoder.embedding.weight", emb)
+        for l in range(LSTM_LAYERS):
+            d.lstm_w_ih[l] = uniform(f"decoder.lstm.weight_ih_l{l}", (4 * H, EMB if l == 0 else H))
+            d.lstm_w_hh[l] = uniform(f"decoder.lstm.weight_hh_l{l}", (4 * H, H))
+            d.lstm_b_ih[l] = uniform(f"decoder.lstm.bias_ih_l{l}", (4 * H,))
+            d.lstm_b_hh[l] = uniform(f"decoder.lstm.bias_hh_l{l}", (4 * H,))
+        d.proj_w = uniform("decoder.decoder_projector.weight", (JOINT, H))
+        d.proj_b = uniform("decoder.decoder_projector.bias", (JOINT,))
+        rng = np.random.default_rng(_seed(self.seed, "joint.head.weight"))
+        d.head_w = self._keep("joint.head.weight", (rng.standard_normal((LOGITS, JOINT)) / np.sqrt(JOINT)).astype(
+            np.float32))
+        rng = np.random.default_rng(_seed(self.seed, "joint.head.bias"))
+        hb = (rng.standard_normal(LOGITS) * 0.02).astype(np.float32)
+        hb[BLANK] += 2.5
+        d.head_b = self._keep("joint.head.bias", hb)
+        d.n_owned = 0
 
     # -- array makers: each stores its array and returns the address for the struct
     def _keep(self, name: str, a: np.ndarray) -> int:
