@@ -363,11 +363,20 @@ def run_ours(args, world, rank, local):
         enc = encoder_ours(args, world, rank, local, torch, pkg)
         if rank == 0:
             line["encoder"] = enc
+    if not args.no_decoder:
+        dec = decoder_ours(args, world, rank, local, torch, pkg)
+        if rank == 0:
+            line["decoder"] = dec
+            line["transcribe"] = transcribe_ours(pkg, local)
     if rank == 0:
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline()
             if not args.no_encoder:
                 line["encoder"]["cpu_baseline"] = encoder_reference()
+            if not args.no_decoder:
+                line["decoder"]["cpu_baseline"] = decoder_reference()
+                for cfg in line["transcribe"]:
+                    cfg["cpu_baseline"] = transcribe_reference(cfg["mel_frames"])
         print(json.dumps(line))
 
 
@@ -458,6 +467,134 @@ def encoder_ours(args, world, rank, local, torch, pkg, workload="long-audio", st
         enc.close()
     dm.close()
     return res
+
+
+# ---- the greedy TDT decoder and the whole transcription (encoder + decoder) ------------------------------------------
+
+def decoder_frames(T, seed):
+    """Joint-network input frames for the decoder workload: N(0, 1) [T, 640]. The synthetic encoder's own output
+    varies too little from frame to frame to make the decoder emit tokens; on N(0, 1) frames it emits about one
+    token every two frames, as speech does, so the decoder does the LSTM steps a real transcript costs."""
+    return np.random.default_rng(seed).standard_normal((T, 640), dtype=np.float32)
+
+
+def decoder_ours(args, world, rank, local, torch, pkg, steps=5):
+    """Greedy TDT decoding of this rank's share of the config-3 windows (T'_i encoder frames each) in one launch per
+    step, frames resident; then end to end through p2_greedy_decode window by window (host frames in, host tokens
+    out), as the reference's engine calls it."""
+    from phonon2_b200 import model as M
+    frames, desc = encoder_workload("long-audio")
+    T = [M.frames_after_subsampling(n) for n in frames]
+    mine = shard_windows(frames, world)[rank]
+    sm = M.SyntheticModel(seed=1)
+    dm = pkg.DeviceModel(sm.struct)
+    encs = [decoder_frames(T[w], seed=1000 + w) for w in mine]
+    stream = torch.cuda.Stream()
+    ms, n_tok = 0.0, 0
+    dec = None
+    if mine:
+        x = torch.from_numpy(np.concatenate(encs)).to(f"cuda:{local}")
+        dec = pkg.Decoder(dm, len(mine), sum(T[w] for w in mine))
+        for _ in range(2):
+            dec.decode(x.data_ptr(), [T[w] for w in mine], stream)
+        n_tok = sum(len(t) for t in dec.read(stream))
+    barrier(world)
+    if dec is not None:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            dec.decode(x.data_ptr(), [T[w] for w in mine], stream)
+        e1.record(stream)
+        e1.synchronize()
+        pkg.check_device(stream)
+        ms = e0.elapsed_time(e1) / steps
+    barrier(world)
+    ms_max = max_over_ranks(ms, world)
+    audio_s = sum(frames) * ENC_SECONDS_PER_FRAME
+    e2e_ms = 0.0
+    if mine:
+        for e in encs[:1]:
+            pkg.host_greedy_decode(sm.struct, e)   # plan creation outside the timed region
+        t0 = time.perf_counter()
+        for e in encs:
+            pkg.host_greedy_decode(sm.struct, e)
+        e2e_ms = (time.perf_counter() - t0) * 1e3
+    barrier(world)
+    e2e_max = max_over_ranks(e2e_ms, world)
+    res = {"metric": "decoder audio-sec/sec", "value": audio_s / (ms_max / 1e3), "unit": "audio-s/s",
+           "ms_per_step": ms_max, "steps": steps,
+           "workload": desc + "; decoder input: N(0, 1) joint frames of each window's T' (seeded)",
+           "frames": sum(T), "tokens_rank0": n_tok,
+           "timing": "CUDA events around one cooperative decode launch over the rank's windows, max over ranks",
+           "gpu_launches_per_step": 1,
+           "e2e": {"value": audio_s / (e2e_max / 1e3), "unit": "audio-s/s", "ms_per_step": e2e_max,
+                   "h2d_bytes_per_step": sum(e.nbytes for e in encs), "d2h_bytes_per_step": 12 * n_tok,
+                   "api": "p2_greedy_decode window by window (host frames in, host tokens out), wall clock, "
+                          "max over ranks"}}
+    if dec is not None:
+        dec.close()
+    dm.close()
+    return res
+
+
+def decoder_reference(seconds=10.0):
+    """phonon-2-c's own p2_greedy_decode on the host cores, on the decoder workload's windows for about `seconds`."""
+    orc = ge.load_oracle()
+    if not orc.ref_available():
+        return None
+    from phonon2_b200 import model as M
+    frames, _ = encoder_workload("long-audio")
+    sm = M.SyntheticModel(seed=1)
+    done, t0, n = 0, time.perf_counter(), 0
+    while True:
+        w = n % len(frames)
+        orc.ref_greedy_decode(sm.struct, decoder_frames(M.frames_after_subsampling(frames[w]), seed=1000 + w))
+        done += frames[w]
+        n += 1
+        dt = time.perf_counter() - t0
+        if dt >= seconds:
+            break
+    return {"value": done * ENC_SECONDS_PER_FRAME / dt, "unit": "audio-s/s", "cores": orc.ref_threads(),
+            "kind": "reference",
+            "sample": f"phonon-2-c p2_greedy_decode on {n} window(s) of the decoder workload in {dt:.1f} s, "
+                      "P2_THREADS = all host cores"}
+
+
+def transcribe_ours(pkg, local, steps=5):
+    """Configs 2 and 4 end to end: host mel in, host tokens out, through p2_b200_transcribe_windows (the encoder in
+    the library's mode, then the decoder on the encoder's frames without leaving the device)."""
+    from phonon2_b200 import model as M
+    sm = M.SyntheticModel(seed=1)
+    out = []
+    for name, n in (("window", 3000), ("short", 300)):
+        mel = M.mel(n, seed=n)
+        toks = pkg.host_transcribe_windows(sm.struct, [mel], devices=[local])   # plans outside the timed region
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            pkg.host_transcribe_windows(sm.struct, [mel], devices=[local])
+        ms = (time.perf_counter() - t0) / steps * 1e3
+        out.append({"config": name, "workload": encoder_workload(name)[1], "mel_frames": n,
+                    "value": ms, "unit": "ms", "higher_is_better": False, "steps": steps,
+                    "tokens": int(len(toks[0])), "h2d_bytes": mel.nbytes, "d2h_bytes": 12 * int(len(toks[0])),
+                    "api": "p2_b200_transcribe_windows, wall clock (mel host -> tokens host)"})
+    return out
+
+
+def transcribe_reference(n_mel, reps=2):
+    """phonon-2-c's p2_encoder (exact) then p2_greedy_decode on the host cores for one window of n_mel frames."""
+    orc = ge.load_oracle()
+    if not orc.ref_available():
+        return None
+    from phonon2_b200 import model as M
+    sm = M.SyntheticModel(seed=1)
+    mel = M.mel(n_mel, seed=n_mel)
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        orc.ref_greedy_decode(sm.struct, orc.ref_encoder(sm.struct, mel, "exact"))
+    ms = (time.perf_counter() - t0) / reps * 1e3
+    return {"value": ms, "unit": "ms", "cores": orc.ref_threads(), "kind": "reference",
+            "sample": f"phonon-2-c p2_encoder (exact, AVX2) + p2_greedy_decode, {reps} runs, P2_THREADS = all host "
+                      "cores"}
 
 
 def run_encoder_only(args, world, rank, local):
@@ -601,6 +738,8 @@ def main():
                          "the int8w code cache (the reference's P2_CACHE_CODES), int8w only")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-encoder", action="store_true", help="skip the encoder (config 3) part of the line")
+    ap.add_argument("--no-decoder", action="store_true",
+                    help="skip the decoder (config 3 windows) and transcription (configs 2, 4) parts of the line")
     ap.add_argument("--workload", choices=["block-gemms", "encoder", "gemm-sweep"], default="block-gemms",
                     help="block-gemms: configs[1] with the encoder object (default); encoder: the encoder alone; "
                          "gemm-sweep: the GEMM alone at growing M (one line per case)")

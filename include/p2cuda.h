@@ -175,7 +175,7 @@ P2CU_API float *p2cu_encoder_out(P2cuEncoder *e);
 P2CU_API int p2cu_encoder_run(P2cuEncoder *e, void *stream);
 
 /* ---- The greedy TDT decoder on the device (csrc/decoder.c) ------------------------------------------------------
- * p2cu_decoder_create allocates the state and token buffers of up to max_windows windows (at most 1024) of up to
+ * p2cu_decoder_create allocates the state and token buffers of up to max_windows windows (at most 512) of up to
  * max_frames encoder frames together; the calls after it allocate nothing. The model must have been uploaded with its
  * decoder tables. The decoder's kernel is one cooperative launch with one CTA on each SM. */
 typedef struct P2cuDecoder P2cuDecoder;

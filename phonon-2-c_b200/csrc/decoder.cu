@@ -34,11 +34,15 @@ constexpr int HDP = 656;              // padded shared-memory row: the two 16-la
 constexpr int NLOG = 8198;            // 8193 tokens + 5 durations
 constexpr int NVOCAB = 8193, BLANK = 8192, NDUR = 5;
 constexpr int THREADS = 512, WARPS = THREADS / 32, GROUPS = THREADS / 16;
-constexpr int WG = 16;                // windows whose joint input is staged at a time
+constexpr int WG = 16;                // windows whose joint input (or projector input) is staged at a time
 constexpr int WL = 8;                 // windows whose LSTM input (x and h rows) is staged at a time
-constexpr int MAXW = 1024;            // windows per launch
+constexpr int XTS = 20;               // staged inputs are transposed, [640][XTS]: 16 windows and 4 floats of padding,
+                                      // so 8 lanes' 16-byte loads of 8 consecutive rows hit disjoint banks
+constexpr int MAXW = 512;             // windows per launch
 constexpr int MAXU = GROUPS / 4;      // hidden units a CTA can own: four gate rows each, one group per row
 constexpr int NO_ROW = 0x7fffffff;
+constexpr int STAGE_BATCH = 2;        // float4 loads per thread in flight while staging
+constexpr int CAND_PER_LANE = 5;      // candidate loads a lane has in flight (148 CTAs: one round)
 constexpr uint32_t DEC_TIMEOUT_BARRIER = 20, DEC_TOKEN_OVERFLOW = 21, DEC_ITER_LIMIT = 22;
 constexpr unsigned long long BARRIER_NS = 2000000000ull;   // two seconds
 
@@ -48,33 +52,156 @@ __device__ __forceinline__ unsigned long long global_ns() {
     return t;
 }
 
-// Dot products of one 640-row w with nw (<= NW) vectors xs[s * xstride], by one group of 16 lanes (one half of a
-// warp) in the reference's order: lane j runs the FMA chain over i = j, j + 16, ...; lanes j and j + 8 are added;
-// then the horizontal-sum tree of csrc/tensor_ops.c:182-190. Every lane of the group gets the results. The shuffles
-// name only the group's lanes: the two halves of a warp may be on different rows (or one of them on none).
-template <int NW>
-__device__ __forceinline__ void dot_rows(const float* __restrict__ w, const float* __restrict__ xs, int xstride,
-                                         int nw, int j, float (&out)[NW]) {
-    const unsigned mask = (threadIdx.x & 16) ? 0xFFFF0000u : 0x0000FFFFu;
-    float acc[NW];
+// The reduction of csrc/tensor_ops.c:182-190 (acc0 + acc1, then the horizontal-sum tree) for N dot products at once
+// over the 16 lanes of a group (one half of a warp), lane j holding the FMA chain over i = j, j + 16, ... of each.
+// The tree adds lanes (j, j + 8), then (j, j + 4), (j, j + 2), (j, j + 1); here each step pairs the same lanes, and
+// while a lane holds two or more values it keeps one half of them and sends the other to its partner, so N sums take
+// N/2 + N/4 + ... shuffles instead of 4 N. The sums are those of the tree, addition being commutative. On return
+// lane j holds max(N / 16, 1) results in v[0..): those of dot products tree16_base<N>(j) + a. The shuffles name only
+// the group's lanes: the two halves of a warp may be on different rows (or one of them on none).
+template <int M, int N, int O>
+__device__ __forceinline__ void tree16(float (&v)[M], unsigned mask, int j) {
+    if constexpr (N >= 2) {
+        const bool up = (j & O) != 0;
 #pragma unroll
-    for (int s = 0; s < NW; ++s) acc[s] = 0.f;
+        for (int a = 0; a < N / 2; ++a) {
+            const float send = up ? v[a] : v[a + N / 2];
+            const float keep = up ? v[a + N / 2] : v[a];
+            v[a] = __fadd_rn(keep, __shfl_xor_sync(mask, send, O, 16));
+        }
+        if constexpr (O > 1) tree16<M, N / 2, O / 2>(v, mask, j);
+    } else {
+        v[0] = __fadd_rn(v[0], __shfl_xor_sync(mask, v[0], O, 16));
+        if constexpr (O > 1) tree16<M, 1, O / 2>(v, mask, j);
+    }
+}
+
+template <int N>
+__device__ __forceinline__ int tree16_base(int j) {
+    int b = 0, n = N;
+#pragma unroll
+    for (int o = 8; o >= 1; o >>= 1)
+        if (n >= 2) {
+            if (j & o) b += n / 2;
+            n /= 2;
+        }
+    return b;
+}
+
+__device__ __forceinline__ unsigned group_mask() { return (threadIdx.x & 16) ? 0xFFFF0000u : 0x0000FFFFu; }
+
+// Joint logits for the CTA's head rows (shared memory, rows HDP apart) and up to 4 NQ windows staged transposed in
+// xt: group g takes rows g and g + GROUPS (then g + 2 GROUPS, ...), each lane the chains over i = j + 16 k of both
+// rows for every window, one 16-byte load per 4 windows. out[row * ostride + s] = dot + bias[row].
+template <int NQ>
+__device__ __forceinline__ void joint_rows(const float* head_s, const float* xt, int nrows, int nw, int grp, int j,
+                                           const float* bias, float* out, int ostride) {
+    constexpr int NW = 4 * NQ, NA = 2 * NW;
+    const unsigned mask = group_mask();
+    for (int r = grp; r < nrows; r += 2 * GROUPS) {
+        const int r2 = r + GROUPS;
+        const float* ha = head_s + r * HDP;
+        const float* hb = head_s + (r2 < nrows ? r2 : r) * HDP;
+        float acc[NA];
+#pragma unroll
+        for (int a = 0; a < NA; ++a) acc[a] = 0.f;
 #pragma unroll 4
-    for (int i = j; i < HD; i += 16) {
-        const float wv = w[i];
+        for (int i = j; i < HD; i += 16) {
+            const float a0 = ha[i], a1 = hb[i];
+            const float4* x = reinterpret_cast<const float4*>(xt + i * XTS);
 #pragma unroll
-        for (int s = 0; s < NW; ++s)
-            if (s < nw) acc[s] = __fmaf_rn(wv, xs[s * xstride + i], acc[s]);
-    }
+            for (int q = 0; q < NQ; ++q) {
+                const float4 xv = x[q];
+                acc[4 * q + 0] = __fmaf_rn(a0, xv.x, acc[4 * q + 0]);
+                acc[4 * q + 1] = __fmaf_rn(a0, xv.y, acc[4 * q + 1]);
+                acc[4 * q + 2] = __fmaf_rn(a0, xv.z, acc[4 * q + 2]);
+                acc[4 * q + 3] = __fmaf_rn(a0, xv.w, acc[4 * q + 3]);
+                acc[NW + 4 * q + 0] = __fmaf_rn(a1, xv.x, acc[NW + 4 * q + 0]);
+                acc[NW + 4 * q + 1] = __fmaf_rn(a1, xv.y, acc[NW + 4 * q + 1]);
+                acc[NW + 4 * q + 2] = __fmaf_rn(a1, xv.z, acc[NW + 4 * q + 2]);
+                acc[NW + 4 * q + 3] = __fmaf_rn(a1, xv.w, acc[NW + 4 * q + 3]);
+            }
+        }
+        tree16<NA, NA, 8>(acc, mask, j);
+        constexpr int R = NA >= 16 ? NA / 16 : 1;
+        if (NA >= 16 || (j & (16 / NA - 1)) == 0) {
+            const int base = tree16_base<NA>(j);
 #pragma unroll
-    for (int s = 0; s < NW; ++s) {
-        float a = acc[s];
-        a = __fadd_rn(a, __shfl_down_sync(mask, a, 8, 16));   // acc0 + acc1
-        a = __fadd_rn(a, __shfl_down_sync(mask, a, 4, 16));
-        a = __fadd_rn(a, __shfl_down_sync(mask, a, 2, 16));
-        a = __fadd_rn(a, __shfl_down_sync(mask, a, 1, 16));
-        out[s] = __shfl_sync(mask, a, 0, 16);
+            for (int a = 0; a < R; ++a) {
+                const int idx = base + a, row = idx < NW ? r : r2, s = idx % NW;
+                if (row < nrows && s < nw) out[row * ostride + s] = __fadd_rn(acc[a], bias[row]);
+            }
+        }
     }
+}
+
+// The dot products of one 640-float global row w with 16 vectors staged transposed in xt (columns 0-15), by one group:
+// lane j returns the dot product with column j. The row is read 20 floats per lane at a time, all loads in flight.
+__device__ __forceinline__ float row_dot16(const float* __restrict__ w, const float* xt, int j) {
+    float acc[16];
+#pragma unroll
+    for (int a = 0; a < 16; ++a) acc[a] = 0.f;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        float wv[20];
+#pragma unroll
+        for (int k = 0; k < 20; ++k) wv[k] = w[j + 16 * (20 * h + k)];
+#pragma unroll
+        for (int k = 0; k < 20; ++k) {
+            const float4* x = reinterpret_cast<const float4*>(xt + (j + 16 * (20 * h + k)) * XTS);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const float4 xv = x[q];
+                acc[4 * q + 0] = __fmaf_rn(wv[k], xv.x, acc[4 * q + 0]);
+                acc[4 * q + 1] = __fmaf_rn(wv[k], xv.y, acc[4 * q + 1]);
+                acc[4 * q + 2] = __fmaf_rn(wv[k], xv.z, acc[4 * q + 2]);
+                acc[4 * q + 3] = __fmaf_rn(wv[k], xv.w, acc[4 * q + 3]);
+            }
+        }
+    }
+    tree16<16, 16, 8>(acc, group_mask(), j);
+    return acc[0];
+}
+
+// The same for two rows at once against 8 vectors each: lane j < 8 returns wa . column j, lane j >= 8 returns
+// wb . column j (columns 8-15 hold the vectors of wb).
+__device__ __forceinline__ float row_pair_dot8(const float* __restrict__ wa, const float* __restrict__ wb,
+                                               const float* xt, int j) {
+    float acc[16];
+#pragma unroll
+    for (int a = 0; a < 16; ++a) acc[a] = 0.f;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        float va[20], vb[20];
+#pragma unroll
+        for (int k = 0; k < 20; ++k) {
+            va[k] = wa[j + 16 * (20 * h + k)];
+            vb[k] = wb[j + 16 * (20 * h + k)];
+        }
+#pragma unroll
+        for (int k = 0; k < 20; ++k) {
+            const float4* x = reinterpret_cast<const float4*>(xt + (j + 16 * (20 * h + k)) * XTS);
+            const float4 x0 = x[0], x1 = x[1], y0 = x[2], y1 = x[3];
+            acc[0] = __fmaf_rn(va[k], x0.x, acc[0]);
+            acc[1] = __fmaf_rn(va[k], x0.y, acc[1]);
+            acc[2] = __fmaf_rn(va[k], x0.z, acc[2]);
+            acc[3] = __fmaf_rn(va[k], x0.w, acc[3]);
+            acc[4] = __fmaf_rn(va[k], x1.x, acc[4]);
+            acc[5] = __fmaf_rn(va[k], x1.y, acc[5]);
+            acc[6] = __fmaf_rn(va[k], x1.z, acc[6]);
+            acc[7] = __fmaf_rn(va[k], x1.w, acc[7]);
+            acc[8] = __fmaf_rn(vb[k], y0.x, acc[8]);
+            acc[9] = __fmaf_rn(vb[k], y0.y, acc[9]);
+            acc[10] = __fmaf_rn(vb[k], y0.z, acc[10]);
+            acc[11] = __fmaf_rn(vb[k], y0.w, acc[11]);
+            acc[12] = __fmaf_rn(vb[k], y1.x, acc[12]);
+            acc[13] = __fmaf_rn(vb[k], y1.y, acc[13]);
+            acc[14] = __fmaf_rn(vb[k], y1.z, acc[14]);
+            acc[15] = __fmaf_rn(vb[k], y1.w, acc[15]);
+        }
+    }
+    tree16<16, 16, 8>(acc, group_mask(), j);
+    return acc[0];
 }
 
 __device__ __forceinline__ float relu_ref(float v) { return v > 0.f ? v : 0.f; }   // csrc/decoder.c:81-84
@@ -117,6 +244,22 @@ struct Cand {
     int i;
 };
 
+// Diagnostic builds (-DP2CU_TRACE) add up the globaltimer time thread 0 of CTA 0 spends in each phase (slots below)
+// and count the iterations; p2cu_decoder_trace reads and clears the sums.
+#ifdef P2CU_TRACE
+enum { TR_SETUP, TR_J, TR_JBAR, TR_A, TR_L0, TR_L0BAR, TR_L1, TR_L1BAR, TR_P, TR_PBAR, TR_ITERS, TR_TOKITERS,
+       TR_TAIL, TR_N = 16 };
+__device__ unsigned long long g_dec_trace[TR_N];
+#define DTRACE_START() unsigned long long tr_t = (blockIdx.x == 0 && threadIdx.x == 0) ? global_ns() : 0
+#define DTRACE(slot) do { if (blockIdx.x == 0 && threadIdx.x == 0) { const unsigned long long n_ = global_ns(); \
+                              g_dec_trace[slot] += n_ - tr_t; tr_t = n_; } } while (0)
+#define DCOUNT(slot) do { if (blockIdx.x == 0 && threadIdx.x == 0) g_dec_trace[slot] += 1; } while (0)
+#else
+#define DTRACE_START() do { } while (0)
+#define DTRACE(slot) do { } while (0)
+#define DCOUNT(slot) do { } while (0)
+#endif
+
 // true when candidate (v, i) beats (bv, bi): the larger logit, and among equal logits the lower row - the first
 // maximum in row order, as the reference's argmax (csrc/decoder.c:90-96) finds it.
 __device__ __forceinline__ bool beats(float v, int i, float bv, int bi) {
@@ -144,10 +287,13 @@ __global__ void __launch_bounds__(THREADS, 1) tdt_decode_kernel(DecParams p) {
     const int u0 = cta * HD / G, nu = (cta + 1) * HD / G - u0;
 
     float* head_s = smem;                                          // [rows_max][HDP]
-    float* xs_s = head_s + static_cast<size_t>(rows_max) * HDP;    // [WG][HDP] joint inputs / LSTM x, h rows
-    float* logit_s = xs_s + WG * HDP;                              // [rows_max][WG]
+    float* xt = head_s + static_cast<size_t>(rows_max) * HDP;      // [640][XTS] staged inputs, transposed
+    float* logit_s = xt + HD * XTS;                                // [rows_max][WG]
     float* gate_s = logit_s + rows_max * WG;                       // [WL][GROUPS]
-    int* step_tok = reinterpret_cast<int*>(gate_s + WL * GROUPS);  // [MAXW] token of the window's next LSTM step
+    float* headb_s = gate_s + WL * GROUPS;                         // [rows_max] the head bias of the CTA's rows
+    int* Ts = reinterpret_cast<int*>(headb_s + rows_max);          // [MAXW] frames of each window
+    int* off_s = Ts + MAXW;                                        // [MAXW] first frame of each window
+    int* step_tok = off_s + MAXW;                                  // [MAXW] token of the window's next LSTM step
     int* hp = step_tok + MAXW;                                     // [MAXW] current ping-pong side of h
     int* t_s = hp + MAXW;                                          // [MAXW] frame pointer
     int* sym_s = t_s + MAXW;                                       // [MAXW] tokens emitted at the current frame
@@ -157,8 +303,9 @@ __global__ void __launch_bounds__(THREADS, 1) tdt_decode_kernel(DecParams p) {
     int* misc = live + MAXW;                                       // s_ok, n_act, n_live
     int* s_ok = misc;
 
+    DTRACE_START();
     const int B = p.B;
-    auto T_of = [&](int b) { return p.win_off[b + 1] - p.win_off[b]; };
+    auto T_of = [&](int b) { return Ts[b]; };
     auto hrow = [&](int side, int layer, int b) { return p.h + ((static_cast<size_t>(side) * 2 + layer) * B + b) * HD; };
 
     if (p.mode != DEC_STEP) {
@@ -168,7 +315,11 @@ __global__ void __launch_bounds__(THREADS, 1) tdt_decode_kernel(DecParams p) {
             *reinterpret_cast<float4*>(head_s + r * HDP + 4 * k) = src[i];
         }
     }
+    for (int r = tid; r < nrows; r += THREADS) headb_s[r] = p.headb[r0 + r];
     for (int b = tid; b < B; b += THREADS) {
+        const int o = p.win_off[b];
+        off_s[b] = o;
+        Ts[b] = p.win_off[b + 1] - o;
         hp[b] = 0;
         step_tok[b] = p.first_token;   // a decode starts with one step on the blank token (zero embedding row)
         t_s[b] = 0;
@@ -190,36 +341,55 @@ __global__ void __launch_bounds__(THREADS, 1) tdt_decode_kernel(DecParams p) {
         for (int w0 = 0; w0 < n_act; w0 += WL) {
             const int nw = n_act - w0 < WL ? n_act - w0 : WL;
             __syncthreads();
-            for (int i = tid; i < nw * 2 * (HD / 4); i += THREADS) {   // row 2s: x, row 2s + 1: h
-                const int s = i / (2 * (HD / 4)), rem = i % (2 * (HD / 4)), which = rem / (HD / 4), k = rem % (HD / 4);
-                const int b = act[w0 + s], cur = hp[b];
-                const float* src = which ? hrow(cur, layer, b)
-                                         : (layer ? hrow(1 - cur, 0, b) : p.embed + static_cast<size_t>(step_tok[b]) * HD);
-                *reinterpret_cast<float4*>(xs_s + (2 * s + which) * HDP + 4 * k) =
-                    reinterpret_cast<const float4*>(src)[k];
+            // column s: x, column 8 + s: h; each thread's loads of a batch are in flight together
+            for (int i0 = 0; i0 < nw * 2 * (HD / 4); i0 += STAGE_BATCH * THREADS) {
+                float4 v[STAGE_BATCH];
+#pragma unroll
+                for (int u = 0; u < STAGE_BATCH; ++u) {
+                    const int i = i0 + tid + u * THREADS;
+                    if (i < nw * 2 * (HD / 4)) {
+                        const int k = i % (HD / 4), which = (i / (HD / 4)) & 1, s = i / (2 * (HD / 4));
+                        const int b = act[w0 + s], cur = hp[b];
+                        const float* src = which ? hrow(cur, layer, b)
+                                                 : (layer ? hrow(1 - cur, 0, b)
+                                                          : p.embed + static_cast<size_t>(step_tok[b]) * HD);
+                        v[u] = reinterpret_cast<const float4*>(src)[k];
+                    }
+                }
+#pragma unroll
+                for (int u = 0; u < STAGE_BATCH; ++u) {
+                    const int i = i0 + tid + u * THREADS;
+                    if (i < nw * 2 * (HD / 4)) {
+                        const int k = i % (HD / 4), which = (i / (HD / 4)) & 1, s = i / (2 * (HD / 4));
+                        float* d = xt + 4 * k * XTS + 8 * which + s;
+                        d[0] = v[u].x;
+                        d[XTS] = v[u].y;
+                        d[2 * XTS] = v[u].z;
+                        d[3 * XTS] = v[u].w;
+                    }
+                }
+            }
+            // the cells' c, read while the gate rows are computed
+            float c_old = 0.f;
+            if (tid < nw * nu) {
+                const int b = act[w0 + tid / nu];
+                c_old = p.c[(static_cast<size_t>(layer) * B + b) * HD + u0 + tid % nu];
             }
             __syncthreads();
             if (grp < 4 * nu) {   // group -> gate row (gate order i, f, g, o) of one of the CTA's units
                 const int r = (grp / nu) * HD + u0 + grp % nu;
-                float d1[WL], d2[WL];
-                dot_rows<WL>(Wih + static_cast<size_t>(r) * HD, xs_s, 2 * HDP, nw, j, d1);
-                dot_rows<WL>(Whh + static_cast<size_t>(r) * HD, xs_s + HDP, 2 * HDP, nw, j, d2);
-                if (j == 0) {
-                    const float bi = bih[r], bh = bhh[r];
-#pragma unroll
-                    for (int s = 0; s < WL; ++s)
-                        if (s < nw) gate_s[s * GROUPS + grp] = __fadd_rn(__fadd_rn(__fadd_rn(d1[s], d2[s]), bi), bh);
-                }
+                const float d = row_pair_dot8(Wih + static_cast<size_t>(r) * HD, Whh + static_cast<size_t>(r) * HD, xt, j);
+                const float dh = __shfl_down_sync(group_mask(), d, 8, 16);   // lane s: W_ih x_s, lane 8 + s: W_hh h_s
+                if (j < nw) gate_s[j * GROUPS + grp] = __fadd_rn(__fadd_rn(__fadd_rn(d, dh), bih[r]), bhh[r]);
             }
             __syncthreads();
-            for (int i = tid; i < nw * nu; i += THREADS) {
-                const int s = i / nu, k = i % nu, u = u0 + k, b = act[w0 + s], cur = hp[b];
+            if (tid < nw * nu) {   // nw * nu <= WL * MAXU <= THREADS: one cell per thread
+                const int s = tid / nu, k = tid % nu, u = u0 + k, b = act[w0 + s], cur = hp[b];
                 const float* g = gate_s + s * GROUPS;
                 const float gi = sigmoid_ref(g[k]), gf = sigmoid_ref(g[nu + k]);
                 const float gg = tanhf(g[2 * nu + k]), go = sigmoid_ref(g[3 * nu + k]);
-                float* c = p.c + (static_cast<size_t>(layer) * B + b) * HD + u;
-                const float cn = __fadd_rn(__fmul_rn(gf, *c), __fmul_rn(gi, gg));
-                *c = cn;
+                const float cn = __fadd_rn(__fmul_rn(gf, c_old), __fmul_rn(gi, gg));
+                p.c[(static_cast<size_t>(layer) * B + b) * HD + u] = cn;
                 hrow(1 - cur, layer, b)[u] = __fmul_rn(go, tanhf(cn));
             }
         }
@@ -228,25 +398,36 @@ __global__ void __launch_bounds__(THREADS, 1) tdt_decode_kernel(DecParams p) {
     // dec = proj_w h1 + proj_b (csrc/decoder.c:72-73) for the CTA's rows and the windows in act
     auto projector = [&]() {
         const int n_act = misc[1];
-        for (int w0 = 0; w0 < n_act; w0 += WL) {
-            const int nw = n_act - w0 < WL ? n_act - w0 : WL;
+        for (int w0 = 0; w0 < n_act; w0 += WG) {
+            const int nw = n_act - w0 < WG ? n_act - w0 : WG;
             __syncthreads();
-            for (int i = tid; i < nw * (HD / 4); i += THREADS) {
-                const int s = i / (HD / 4), k = i % (HD / 4), b = act[w0 + s];
-                *reinterpret_cast<float4*>(xs_s + s * HDP + 4 * k) =
-                    reinterpret_cast<const float4*>(hrow(1 - hp[b], 1, b))[k];
+            for (int i0 = 0; i0 < nw * (HD / 4); i0 += STAGE_BATCH * THREADS) {
+                float4 v[STAGE_BATCH];
+#pragma unroll
+                for (int u = 0; u < STAGE_BATCH; ++u) {
+                    const int i = i0 + tid + u * THREADS;
+                    if (i < nw * (HD / 4)) {
+                        const int b = act[w0 + i / (HD / 4)];
+                        v[u] = reinterpret_cast<const float4*>(hrow(1 - hp[b], 1, b))[i % (HD / 4)];
+                    }
+                }
+#pragma unroll
+                for (int u = 0; u < STAGE_BATCH; ++u) {
+                    const int i = i0 + tid + u * THREADS;
+                    if (i < nw * (HD / 4)) {
+                        float* d = xt + 4 * (i % (HD / 4)) * XTS + i / (HD / 4);
+                        d[0] = v[u].x;
+                        d[XTS] = v[u].y;
+                        d[2 * XTS] = v[u].z;
+                        d[3 * XTS] = v[u].w;
+                    }
+                }
             }
             __syncthreads();
             if (grp < nu) {
                 const int r = u0 + grp;
-                float d[WL];
-                dot_rows<WL>(p.proj + static_cast<size_t>(r) * HD, xs_s, HDP, nw, j, d);
-                if (j == 0) {
-                    const float pb = p.projb[r];
-#pragma unroll
-                    for (int s = 0; s < WL; ++s)
-                        if (s < nw) p.dec[static_cast<size_t>(act[w0 + s]) * HD + r] = __fadd_rn(d[s], pb);
-                }
+                const float d = row_dot16(p.proj + static_cast<size_t>(r) * HD, xt, j);
+                if (j < nw) p.dec[static_cast<size_t>(act[w0 + j]) * HD + r] = __fadd_rn(d, p.projb[r]);
             }
         }
         __syncthreads();
@@ -255,15 +436,12 @@ __global__ void __launch_bounds__(THREADS, 1) tdt_decode_kernel(DecParams p) {
     };
 
     if (p.mode == DEC_JOINT) {   // p2_joint (csrc/decoder.c:78-88): logits of enc[0] with dec[0], every row out
-        for (int i = tid; i < HD; i += THREADS) {
-            xs_s[i] = relu_ref(__fadd_rn(p.enc[i], p.dec[i]));
+        for (int i = tid; i < HD * XTS; i += THREADS) {
+            const int k = i / XTS, c = i % XTS;
+            xt[i] = c == 0 ? relu_ref(__fadd_rn(p.enc[k], p.dec[k])) : 0.f;
         }
         __syncthreads();
-        for (int r = grp; r < nrows; r += GROUPS) {
-            float v[1];
-            dot_rows<1>(head_s + r * HDP, xs_s, HDP, 1, j, v);
-            if (j == 0) p.logits[r0 + r] = __fadd_rn(v[0], p.headb[r0 + r]);
-        }
+        joint_rows<1>(head_s, xt, nrows, 1, grp, j, p.headb + r0, p.logits + r0, 1);
         return;
     }
 
@@ -280,6 +458,7 @@ __global__ void __launch_bounds__(THREADS, 1) tdt_decode_kernel(DecParams p) {
         if (lane == 0) misc[2] = n;
     }
     if (!grid_sync(p.bar_count, p.bar_gen, G, p.err, s_ok)) return;
+    DTRACE(TR_SETUP);
 
     int iter = 0;
     for (; iter < p.max_iters && misc[2] > 0; ++iter) {
@@ -291,55 +470,81 @@ __global__ void __launch_bounds__(THREADS, 1) tdt_decode_kernel(DecParams p) {
         for (int w0 = 0; w0 < n_live; w0 += WG) {
             const int nw = n_live - w0 < WG ? n_live - w0 : WG;
             __syncthreads();
-            for (int i = tid; i < nw * (HD / 4); i += THREADS) {
-                const int s = i / (HD / 4), k = i % (HD / 4), b = live[w0 + s];
-                const float4 e = reinterpret_cast<const float4*>(
-                    p.enc + (static_cast<size_t>(p.win_off[b]) + t_s[b]) * HD)[k];
-                const float4 d = reinterpret_cast<const float4*>(p.dec + static_cast<size_t>(b) * HD)[k];
-                float4 v;   // v > 0 ? v : 0, as the reference writes it (a -0 sum becomes +0)
-                v.x = relu_ref(__fadd_rn(e.x, d.x));
-                v.y = relu_ref(__fadd_rn(e.y, d.y));
-                v.z = relu_ref(__fadd_rn(e.z, d.z));
-                v.w = relu_ref(__fadd_rn(e.w, d.w));
-                *reinterpret_cast<float4*>(xs_s + s * HDP + 4 * k) = v;
-            }
-            __syncthreads();
-            for (int r = grp; r < nrows; r += GROUPS) {
-                float v[WG];
-                dot_rows<WG>(head_s + r * HDP, xs_s, HDP, nw, j, v);
-                if (j == 0) {
-                    const float hb = p.headb[r0 + r];
+            // relu(enc[t] + dec): v > 0 ? v : 0, as the reference writes it (a -0 sum becomes +0)
+            for (int i0 = 0; i0 < nw * (HD / 4); i0 += STAGE_BATCH * THREADS) {
+                float4 e[STAGE_BATCH], d[STAGE_BATCH];
 #pragma unroll
-                    for (int s = 0; s < WG; ++s)
-                        if (s < nw) logit_s[r * WG + s] = __fadd_rn(v[s], hb);
+                for (int u = 0; u < STAGE_BATCH; ++u) {
+                    const int i = i0 + tid + u * THREADS;
+                    if (i < nw * (HD / 4)) {
+                        const int b = live[w0 + i / (HD / 4)], k = i % (HD / 4);
+                        e[u] = reinterpret_cast<const float4*>(p.enc + (static_cast<size_t>(off_s[b]) + t_s[b]) * HD)[k];
+                        d[u] = reinterpret_cast<const float4*>(p.dec + static_cast<size_t>(b) * HD)[k];
+                    }
+                }
+#pragma unroll
+                for (int u = 0; u < STAGE_BATCH; ++u) {
+                    const int i = i0 + tid + u * THREADS;
+                    if (i < nw * (HD / 4)) {
+                        float* o = xt + 4 * (i % (HD / 4)) * XTS + i / (HD / 4);
+                        o[0] = relu_ref(__fadd_rn(e[u].x, d[u].x));
+                        o[XTS] = relu_ref(__fadd_rn(e[u].y, d[u].y));
+                        o[2 * XTS] = relu_ref(__fadd_rn(e[u].z, d[u].z));
+                        o[3 * XTS] = relu_ref(__fadd_rn(e[u].w, d[u].w));
+                    }
                 }
             }
             __syncthreads();
-            for (int s = tid; s < nw; s += THREADS) {   // the CTA's first maximum; the duration rows it owns
+            if (nw <= 4)
+                joint_rows<1>(head_s, xt, nrows, nw, grp, j, headb_s, logit_s, WG);
+            else if (nw <= 8)
+                joint_rows<2>(head_s, xt, nrows, nw, grp, j, headb_s, logit_s, WG);
+            else
+                joint_rows<4>(head_s, xt, nrows, nw, grp, j, headb_s, logit_s, WG);
+            __syncthreads();
+            for (int s = warp; s < nw; s += WARPS) {   // a warp per window: the CTA's first maximum
                 const int b = live[w0 + s];
-                Cand best{-INFINITY, NO_ROW};
-                for (int r = 0; r < nrows; ++r) {
+                float bv = -INFINITY;
+                int bi = NO_ROW;
+                for (int r = lane; r < nrows; r += 32) {
                     const int row = r0 + r;
                     const float v = logit_s[r * WG + s];
                     if (row < NVOCAB) {
-                        if (best.i == NO_ROW || v > best.v) best = Cand{v, row};
+                        if (beats(v, row, bv, bi)) { bv = v; bi = row; }
                     } else {
-                        dur[static_cast<size_t>(b) * NDUR + (row - NVOCAB)] = v;
+                        dur[static_cast<size_t>(b) * NDUR + (row - NVOCAB)] = v;   // the duration rows it owns
                     }
                 }
-                cand[static_cast<size_t>(cta) * B + b] = best;
+#pragma unroll
+                for (int off = 16; off; off >>= 1) {
+                    const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+                    const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+                    if (beats(ov, oi, bv, bi)) { bv = ov; bi = oi; }
+                }
+                if (lane == 0) cand[static_cast<size_t>(cta) * B + b] = Cand{bv, bi};
             }
         }
+        DTRACE(TR_J);
         if (!grid_sync(p.bar_count, p.bar_gen, G, p.err, s_ok)) return;
+        DTRACE(TR_JBAR);
+        DCOUNT(TR_ITERS);
 
         // ---- A: the decisions of csrc/decoder.c:115-140, the same in every CTA; a warp per window ----
         for (int k = warp; k < n_live; k += WARPS) {
             const int b = live[k];
             float bv = -INFINITY;
             int bi = NO_ROW;
-            for (int c = lane; c < G; c += 32) {
-                const Cand x = cand[static_cast<size_t>(c) * B + b];
-                if (beats(x.v, x.i, bv, bi)) { bv = x.v; bi = x.i; }
+            const float dv = lane < NDUR ? dur[static_cast<size_t>(b) * NDUR + lane] : 0.f;
+            for (int c0 = 0; c0 < G; c0 += CAND_PER_LANE * 32) {   // every load of the lane in flight at once
+                Cand x[CAND_PER_LANE];
+#pragma unroll
+                for (int u = 0; u < CAND_PER_LANE; ++u) {
+                    const int c = c0 + lane + 32 * u;
+                    x[u] = c < G ? cand[static_cast<size_t>(c) * B + b] : Cand{-INFINITY, NO_ROW};
+                }
+#pragma unroll
+                for (int u = 0; u < CAND_PER_LANE; ++u)
+                    if (beats(x[u].v, x[u].i, bv, bi)) { bv = x[u].v; bi = x[u].i; }
             }
 #pragma unroll
             for (int off = 16; off; off >>= 1) {
@@ -347,9 +552,12 @@ __global__ void __launch_bounds__(THREADS, 1) tdt_decode_kernel(DecParams p) {
                 const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
                 if (beats(ov, oi, bv, bi)) { bv = ov; bi = oi; }
             }
+            float dl[NDUR];
+#pragma unroll
+            for (int q = 0; q < NDUR; ++q) dl[q] = __shfl_sync(0xffffffffu, dv, q);
             if (lane == 0) {
-                const float* dl = dur + static_cast<size_t>(b) * NDUR;
                 int duration = 0;   // the durations are {0, 1, 2, 3, 4}: the argmax index itself
+#pragma unroll
                 for (int q = 1; q < NDUR; ++q)
                     if (dl[q] > dl[duration]) duration = q;
                 const int t = t_s[b];
@@ -360,7 +568,7 @@ __global__ void __launch_bounds__(THREADS, 1) tdt_decode_kernel(DecParams p) {
                     const int n = cnt_s[b];
                     if (cta == 0) {
                         if (n < P2CU_DEC_MAX_SYMBOLS * T_of(b)) {
-                            int* o = p.tokens + (static_cast<size_t>(P2CU_DEC_MAX_SYMBOLS) * p.win_off[b] + n) * 3;
+                            int* o = p.tokens + (static_cast<size_t>(P2CU_DEC_MAX_SYMBOLS) * off_s[b] + n) * 3;
                             o[0] = bi;
                             o[1] = t;
                             o[2] = duration;
@@ -399,13 +607,21 @@ __global__ void __launch_bounds__(THREADS, 1) tdt_decode_kernel(DecParams p) {
             }
         }
         __syncthreads();
+        DTRACE(TR_A);
         if (misc[1] > 0) {
+            DCOUNT(TR_TOKITERS);
             lstm_layer(0);
+            DTRACE(TR_L0);
             if (!grid_sync(p.bar_count, p.bar_gen, G, p.err, s_ok)) return;
+            DTRACE(TR_L0BAR);
             lstm_layer(1);
+            DTRACE(TR_L1);
             if (!grid_sync(p.bar_count, p.bar_gen, G, p.err, s_ok)) return;
+            DTRACE(TR_L1BAR);
             projector();
+            DTRACE(TR_P);
             if (!grid_sync(p.bar_count, p.bar_gen, G, p.err, s_ok)) return;
+            DTRACE(TR_PBAR);
         }
     }
     if (cta != 0) return;
@@ -436,16 +652,17 @@ __global__ void __launch_bounds__(THREADS, 1) tdt_decode_kernel(DecParams p) {
     __syncthreads();
     for (int b = warp; b < B; b += WARPS) {
         const int o = p.tok_off[b], n = p.tok_off[b + 1] - o;
-        const int* src = p.tokens + static_cast<size_t>(P2CU_DEC_MAX_SYMBOLS) * p.win_off[b] * 3;
+        const int* src = p.tokens + static_cast<size_t>(P2CU_DEC_MAX_SYMBOLS) * off_s[b] * 3;
         for (int i = lane; i < 3 * n; i += 32) p.tok_out[static_cast<size_t>(o) * 3 + i] = src[i];
     }
+    DTRACE(TR_TAIL);
 }
 
 }  // namespace
 
 int decoder_smem_bytes(int grid) {
     const int rows_max = (NLOG + grid - 1) / grid;
-    return (rows_max * HDP + WG * HDP + rows_max * WG + WL * GROUPS) * 4 + (7 * MAXW + 4) * 4;
+    return (rows_max * HDP + HD * XTS + rows_max * WG + WL * GROUPS + rows_max) * 4 + (9 * MAXW + 4) * 4;
 }
 
 int decoder_max_windows() { return MAXW; }
@@ -474,3 +691,11 @@ int decoder_max_grid(int device) {
 }
 
 }  // namespace p2cu
+
+#ifdef P2CU_TRACE
+extern "C" __attribute__((visibility("default"))) int p2cu_decoder_trace(unsigned long long* out) {
+    const unsigned long long zero[p2cu::TR_N] = {};
+    if (cudaMemcpyFromSymbol(out, p2cu::g_dec_trace, sizeof(zero)) != cudaSuccess) return -1;
+    return cudaMemcpyToSymbol(p2cu::g_dec_trace, zero, sizeof(zero)) == cudaSuccess ? 0 : -1;
+}
+#endif

@@ -478,33 +478,38 @@ __attribute__((visibility("default"))) int p2_b200_transcribe_windows(const P2Mo
     auto decode = [&](P2cuEncoder* e, cudaStream_t s, DeviceSlot& slot, const P2cuModel* dm,
                       const std::vector<int>& wins, std::string* err) {
         const int nw = static_cast<int>(wins.size());
-        if (nw > 1024) {
-            *err = "more than 1024 windows on one GPU";
-            return -1;
-        }
         std::vector<int> T(nw);
         for (int i = 0; i < nw; ++i) T[i] = p2cu_encoder_frames(e, i);
-        P2cuDecoder* d = slot.decoder_for(dm, nw, p2cu_encoder_frames(e, -1));
-        std::vector<int> offs(nw + 1);
-        int total = -1;
-        if (d && p2cu_decode(d, p2cu_encoder_out(e), T.data(), nw, s) == P2CU_OK)
-            total = p2cu_decoder_read(d, offs.data(), nullptr, 0, s);
-        std::vector<P2Token> all(std::max(total, 1));
-        if (total > 0 && p2cu_decoder_read(d, offs.data(), all.data(), total, s) != total) total = -1;
-        if (total < 0) {
-            *err = p2cu_last_error();
-            return -1;
-        }
-        for (int i = 0; i < nw; ++i) {
-            const int n = offs[i + 1] - offs[i], w = wins[i];
-            n_tokens[w] = n;
-            if (n == 0) continue;
-            tokens[w] = static_cast<P2Token*>(malloc(static_cast<size_t>(n) * sizeof(P2Token)));
-            if (!tokens[w]) {
-                *err = "out of host memory";
+        // one decoder launch per group of at most kDecodeWindows windows
+        constexpr int kDecodeWindows = 512;
+        const float* enc = p2cu_encoder_out(e);
+        for (int g0 = 0; g0 < nw; g0 += kDecodeWindows) {
+            const int gn = std::min(kDecodeWindows, nw - g0);
+            long long frames = 0;
+            for (int i = 0; i < gn; ++i) frames += T[g0 + i];
+            P2cuDecoder* d = slot.decoder_for(dm, gn, static_cast<int>(std::max(frames, 1LL)));
+            std::vector<int> offs(gn + 1);
+            int total = -1;
+            if (d && p2cu_decode(d, enc, T.data() + g0, gn, s) == P2CU_OK)
+                total = p2cu_decoder_read(d, offs.data(), nullptr, 0, s);
+            std::vector<P2Token> all(std::max(total, 1));
+            if (total > 0 && p2cu_decoder_read(d, offs.data(), all.data(), total, s) != total) total = -1;
+            if (total < 0) {
+                *err = p2cu_last_error();
                 return -1;
             }
-            memcpy(tokens[w], all.data() + offs[i], static_cast<size_t>(n) * sizeof(P2Token));
+            for (int i = 0; i < gn; ++i) {
+                const int n = offs[i + 1] - offs[i], w = wins[g0 + i];
+                n_tokens[w] = n;
+                if (n == 0) continue;
+                tokens[w] = static_cast<P2Token*>(malloc(static_cast<size_t>(n) * sizeof(P2Token)));
+                if (!tokens[w]) {
+                    *err = "out of host memory";
+                    return -1;
+                }
+                memcpy(tokens[w], all.data() + offs[i], static_cast<size_t>(n) * sizeof(P2Token));
+            }
+            enc += frames * P2_JOINT_DIM;
         }
         return 0;
     };

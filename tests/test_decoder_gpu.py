@@ -150,7 +150,7 @@ def test_decoder_argument_errors(pkg, cuda, model, dev_model):
         pkg.Decoder(dm, 1, 10)   # uploaded without decoder tables
     dm.close()
     with pytest.raises(pkg.Error):
-        pkg.Decoder(dev_model, 1025, 10)
+        pkg.Decoder(dev_model, 513, 10)
     dec = pkg.Decoder(dev_model, 2, 100)
     with pytest.raises(pkg.Error):
         dec.decode(0, [50, 60])          # NULL frames
