@@ -182,15 +182,29 @@ int run_i8(int M, int N, int K, float alpha, const int8_t* q, const float* a_sca
 #endif
     const bool planes = B && !(mode == P2CU_INT8W && B->codes);
     const int kind = !planes ? p2cu::KIND_TABLE : mode == P2CU_INT8W ? p2cu::KIND_CODES : p2cu::KIND_ST;
-    const int bn = choose_bn(M, N, nblk, kind);
+    // CTA pairs (256 x 256 tiles, fv_gemm_2sm.cu) for int8w / int8-table products with at least as many pair tiles
+    // as the GPU has SM pairs (large M: batched windows); P2CU_PAIR=1 forces them where they apply, 0 forbids them.
+    static int pair_env = -2;
+    if (pair_env == -2) {
+        const char* pe = getenv("P2CU_PAIR");
+        pair_env = pe && pe[0] == '1' ? 1 : pe && pe[0] == '0' ? 0 : -1;
+    }
+    const bool vec_ok = aligned16(B ? B->lo : nullptr) && aligned16(B ? B->hi : nullptr) && aligned16(scales);
+    const bool pair_ok = vec_ok && kind != p2cu::KIND_ST && N % 256 == 0;
+    const bool use_pair = pair_ok && (pair_env == 1 ||
+                                      (pair_env == -1 &&
+                                       2 * p2cu::fv_gemm_2sm_tiles(M, N, nblk) >= p2cu::fv_gemm_p_min_tiles()));
+    const int bn = use_pair ? 128 : choose_bn(M, N, nblk, kind);
     const int atom = bn > 128 ? 128 : bn;   // an int8 table is loaded in boxes one swizzle atom wide
     CUtensorMap ta, tb0, tb1, tout;
     if ((rc = make_map(&ta, q, 1, K, M, K, 128, 128, 128, "A"))) return rc;
+    // output box: 32 columns x 128 rows (one CTA's chunk), or x 32 rows for the pair kernel (one warp's block)
+    const uint32_t out_rows = use_pair ? 32 : 128;
     if (nblk > 1)
-        rc = make_map(&tout, ws, 4, N, static_cast<uint64_t>(nblk) * p.m_pad, static_cast<uint64_t>(N) * 4, 32, 128,
-                      128, "workspace");
+        rc = make_map(&tout, ws, 4, N, static_cast<uint64_t>(nblk) * p.m_pad, static_cast<uint64_t>(N) * 4, 32,
+                      out_rows, 128, "workspace");
     else
-        rc = make_map(&tout, C, 4, N, M, static_cast<uint64_t>(ldc) * 4, 32, 128, 128, "C");
+        rc = make_map(&tout, C, 4, N, M, static_cast<uint64_t>(ldc) * 4, 32, out_rows, 128, "C");
     if (rc) return rc;
     if (B) {
         if (!B->lo || !B->hi) return fail(P2CU_EINVAL, "%s: lo / hi are NULL", who);
@@ -223,12 +237,12 @@ int run_i8(int M, int N, int K, float alpha, const int8_t* q, const float* a_sca
         const char* pe = getenv("P2CU_PERSIST");
         persist_env = pe && pe[0] == '1' ? 1 : pe && pe[0] == '0' ? 0 : -1;
     }
-    const bool vec_ok = aligned16(p.lo) && aligned16(p.hi) && aligned16(p.scales);
     const bool many = p2cu::fv_gemm_p_tiles(M, N, bn, nblk) > p2cu::fv_gemm_p_min_tiles();
     const bool persist = vec_ok && (persist_env == 1 ||
                                     (persist_env == -1 && many && (kind != p2cu::KIND_TABLE || nblk > 1)));
-    cudaError_t e = persist ? p2cu::fv_gemm_p_launch(bn, kind, ta, tb0, tb1, tout, p, s)
-                            : p2cu::fv_gemm_launch(bn, kind, ta, tb0, tb1, tout, p, s);
+    cudaError_t e = use_pair  ? p2cu::fv_gemm_2sm_launch(kind, ta, tb0, tb1, tout, p, s)
+                    : persist ? p2cu::fv_gemm_p_launch(bn, kind, ta, tb0, tb1, tout, p, s)
+                              : p2cu::fv_gemm_launch(bn, kind, ta, tb0, tb1, tout, p, s);
     if (e == cudaSuccess && nblk > 1)
         e = p2cu::fv_combine_launch(static_cast<const float*>(ws), p.m_pad, nblk, a_scales, alpha, p.beta_zero, C, M,
                                     N, ldc, s);

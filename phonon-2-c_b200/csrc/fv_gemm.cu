@@ -63,8 +63,6 @@ template <int BN_, int KIND_> struct Cfg {
     static constexpr uint32_t SBO = 8 * ATOM_W;                    // 8-row K groups
     static constexpr int EPI_GROUPS = PLANES ? 3 : 2;
     static constexpr int NEXP = PLANES ? 8 : 0;                    // expander warps (= epilogue groups 1 and 2)
-    static constexpr int PROD = 4 * EPI_GROUPS, MMAW = PROD + 1;
-    static constexpr int NTHREADS = (MMAW + 1) * 32;
     static constexpr uint32_t A_BYTES = BM * BK;                   // int8 A tile, K-major, 128-byte swizzle
     static constexpr uint32_t B_BYTES = BK * MMA_N;                // the MMA's B operand
     static constexpr uint32_t SG_BYTES = BK * (BN / 4);            // sign-plane tile
@@ -74,6 +72,13 @@ template <int BN_, int KIND_> struct Cfg {
     static constexpr uint32_t B_TX_BYTES = PLANES ? SG_BYTES + FL_BYTES : B_BYTES;   // bytes TMA brings per stage
                                                                                       // besides the A tile
     static constexpr int STAGES = (200 * 1024) / STAGE_BYTES > 6 ? 6 : (200 * 1024) / STAGE_BYTES;
+    // TMA producer warps: one warp's tile loads complete one after another (about 0.4 us each on B200, whatever the
+    // box size), so warp PROD + w issues the loads of the K steps kb with kb % NPROD == w. NPROD <= STAGES: a warp's
+    // wait for round r of a stage (by phase parity) is unambiguous only if round r - 2 is known to be complete, which
+    // its own previous wait (for step kb - NPROD) guarantees exactly when NPROD <= STAGES.
+    static constexpr int NPROD = STAGES < 4 ? STAGES : 4;
+    static constexpr int PROD = 4 * EPI_GROUPS, MMAW = PROD + NPROD;
+    static constexpr int NTHREADS = (MMAW + 1) * 32;
     static constexpr uint32_t TMEM_COLS = MMA_N <= 32 ? 32 : MMA_N <= 64 ? 64 : MMA_N <= 128 ? 128 : 256;
     static constexpr int CHUNKS = BN / 32;                         // 32-column output chunks
     static constexpr uint32_t OUT_BYTES = BM * BN * 4;             // fp32 output tile, aliases the stage buffers
@@ -83,6 +88,7 @@ template <int BN_, int KIND_> struct Cfg {
     static_assert(MMA_N <= 256 && MMA_N % 16 == 0, "MMA N");
     static_assert(ATOM_W == 64 || ATOM_W == 128, "atom width");
     static_assert(STAGES >= 2, "pipeline depth");
+    static_assert(NPROD <= STAGES, "producer warps and stage phases");
     static_assert(OUT_BYTES <= STAGES * STAGE_BYTES, "the output tile must fit in the stage buffers");
 };
 
@@ -158,8 +164,9 @@ fv_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     // below, in the producer before the first A load and in the epilogue before the first read): the weights are
     // constant, so their loads and expansion overlap the previous kernel's tail.
 
-    if (warp == G::PROD) {
-        // ---------------- TMA producer ----------------
+    if (warp >= G::PROD && warp < G::PROD + G::NPROD) {
+        // ---------------- TMA producers ----------------
+        const int pw = warp - G::PROD;
         if (lane == 0) {
             auto load_b = [&](int kb) {
                 const int s = kb % STAGES;
@@ -175,10 +182,10 @@ fv_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 }
             };
             const int pre = nk < STAGES ? nk : STAGES;
-            for (int kb = 0; kb < pre; ++kb) load_b(kb);   // the stages are empty at the start
+            for (int kb = pw; kb < pre; kb += G::NPROD) load_b(kb);   // the stages are empty at the start
             griddep_wait();
             int issued = 0;
-            for (int kb = 0; kb < nk; ++kb) {
+            for (int kb = pw; kb < nk; kb += G::NPROD) {
                 const int s = kb % STAGES, r = kb / STAGES;
                 if (kb >= pre) {
                     if (!mbar_wait(&empty[s], (r & 1) ^ 1, DEV_TIMEOUT_EMPTY, p.err, abort_flag)) break;
@@ -189,8 +196,10 @@ fv_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 mbar_arrive_expect_tx(&afull[s], G::A_BYTES);
                 tma_load_2d(a_tile(s), &tmA, &afull[s], k_begin + kb * BK, m0);
             }
-            // No copy may still be landing in shared memory when the CTA exits (matters on the abort path only).
+            // No copy this warp issued may still be landing in shared memory when the CTA exits (matters on the abort
+            // path only).
             for (int kb = issued - STAGES < 0 ? 0 : issued - STAGES; kb < issued; ++kb) {
+                if (kb % G::NPROD != pw) continue;
                 const int s = kb % STAGES, r = kb / STAGES;
                 for (uint32_t i = 0; i < WAIT_LIMIT && !mbar_try_wait(smem_u32(&full[s]), r & 1); ++i) {}
                 for (uint32_t i = 0; i < WAIT_LIMIT && !mbar_try_wait(smem_u32(&afull[s]), r & 1); ++i) {}

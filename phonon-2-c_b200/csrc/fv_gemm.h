@@ -42,6 +42,13 @@ cudaError_t fv_gemm_launch(int bn, int kind, const CUtensorMap& a, const CUtenso
 cudaError_t fv_gemm_p_launch(int bn, int kind, const CUtensorMap& a, const CUtensorMap& b0, const CUtensorMap& b1,
                              const CUtensorMap& out, const FvGemmParams& p, cudaStream_t stream);
 int fv_gemm_p_tiles(int M, int N, int bn, int ksplit);
+
+// The CTA-pair form (fv_gemm_2sm.cu): 256 x 256 output tiles on clusters of two CTAs (tcgen05 cta_group::2), for
+// KIND_TABLE and KIND_CODES with N % 256 == 0. The A and B maps are those of bn = 128 (each CTA loads a 128-column
+// half of B); the output map's box is 32 x 32 (each epilogue warp stores its own 32-row blocks).
+cudaError_t fv_gemm_2sm_launch(int kind, const CUtensorMap& a, const CUtensorMap& b0, const CUtensorMap& b1,
+                               const CUtensorMap& out, const FvGemmParams& p, cudaStream_t stream);
+int fv_gemm_2sm_tiles(int M, int N, int ksplit);
 int fv_gemm_p_min_tiles();   // the SM count: below it every tile has an SM of its own anyway
 
 // C = fold of the workspace slices (fp32 f per 1024-row block) in block order, with the row scales.

@@ -39,8 +39,7 @@ template <int BN_, int KIND_> struct PCfg {
     static constexpr uint32_t SBO = 8 * ATOM_W;
     static constexpr int NEXP = PLANES ? 8 : 0;                 // expander warps 0 .. NEXP - 1
     static constexpr int EPI0 = NEXP;                           // epilogue warps EPI0 .. EPI0 + 3
-    static constexpr int PROD = EPI0 + 4, MMAW = PROD + 1;
-    static constexpr int NTHREADS = (MMAW + 1) * 32;
+
     static constexpr uint32_t A_BYTES = PBM * PBK;
     static constexpr uint32_t B_BYTES = PBK * MMA_N;
     static constexpr uint32_t SG_BYTES = PBK * (BN / 4);
@@ -52,10 +51,17 @@ template <int BN_, int KIND_> struct PCfg {
     static constexpr uint32_t BAR_BYTES = 512;
     static constexpr uint32_t FIXED = 1024 + 2 * STG_BYTES + BAR_BYTES;
     static constexpr int STAGES = (220 * 1024 - FIXED) / STAGE_BYTES > 4 ? 4 : (220 * 1024 - FIXED) / STAGE_BYTES;
+    // TMA producer warps: one warp's tile loads complete one after another (about 0.4 us each on B200, whatever the
+    // box size), so warp PROD + w issues the loads of the K steps g with g % NPROD == w. NPROD <= STAGES keeps each
+    // warp's parity wait on a stage unambiguous (its own previous wait proves the round before last complete).
+    static constexpr int NPROD = STAGES < 4 ? STAGES : 4;
+    static constexpr int PROD = EPI0 + 4, MMAW = PROD + NPROD;
+    static constexpr int NTHREADS = (MMAW + 1) * 32;
     static constexpr uint32_t SMEM_BYTES = FIXED + STAGES * STAGE_BYTES;
     static constexpr uint32_t TMEM_COLS = 2 * MMA_N <= 128 ? 128 : 2 * MMA_N <= 256 ? 256 : 512;
     static constexpr int CHUNKS = BN / 32;
     static_assert(STAGES >= 2, "pipeline depth");
+    static_assert(NPROD <= STAGES, "producer warps and stage phases");
     static_assert(2 * MMA_N <= 512, "two accumulators must fit in TMEM");
 };
 
@@ -148,8 +154,9 @@ fv_gemm_p_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
     const uint32_t tmem = *tmem_holder;
     griddep_launch_dependents();
 
-    if (warp == G::PROD) {
-        // ---------------- TMA producer: one ring of stages across all of this CTA's tiles ----------------
+    if (warp >= G::PROD && warp < G::PROD + G::NPROD) {
+        // ---------------- TMA producers: one ring of stages across all of this CTA's tiles ----------------
+        const int pw = warp - G::PROD;
         if (lane == 0) {
             auto load_b = [&](int s, int n0, int kx) {
                 mbar_arrive_expect_tx(&full[s], G::B_TX_BYTES);
@@ -167,7 +174,7 @@ fv_gemm_p_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
             if (static_cast<int>(blockIdx.x) < total) {
                 const TileDesc d = tile_of(blockIdx.x, m_tiles, n_tiles, BN, p.K);
                 pre = d.nk < STAGES ? d.nk : STAGES;
-                for (int kb = 0; kb < pre; ++kb) load_b(kb, d.n0, d.k_begin + kb * PBK);
+                for (int kb = pw; kb < pre; kb += G::NPROD) load_b(kb, d.n0, d.k_begin + kb * PBK);
             }
             griddep_wait();
             int g = 0;
@@ -175,6 +182,7 @@ fv_gemm_p_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
             for (int t = blockIdx.x; ok && t < total; t += gridDim.x) {
                 const TileDesc d = tile_of(t, m_tiles, n_tiles, BN, p.K);
                 for (int kb = 0; kb < d.nk; ++kb, ++g) {
+                    if (g % G::NPROD != pw) continue;
                     const int s = g % STAGES, r = g / STAGES;
                     if (g >= pre) {
                         if (!mbar_wait(&empty[s], (r & 1) ^ 1, DEV_TIMEOUT_EMPTY, p.err, abort_flag)) { ok = false; break; }
@@ -184,8 +192,9 @@ fv_gemm_p_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                     tma_load_2d(a_tile(s), &tmA, &afull[s], d.k_begin + kb * PBK, d.m0);
                 }
             }
-            // No copy may still be landing in shared memory when the CTA exits.
+            // No copy this warp issued may still be landing in shared memory when the CTA exits.
             for (int k = g - STAGES < 0 ? 0 : g - STAGES; k < g; ++k) {
+                if (k % G::NPROD != pw) continue;
                 const int s = k % STAGES, r = k / STAGES;
                 for (uint32_t i = 0; i < WAIT_LIMIT && !mbar_try_wait(smem_u32(&full[s]), r & 1); ++i) {}
                 for (uint32_t i = 0; i < WAIT_LIMIT && !mbar_try_wait(smem_u32(&afull[s]), r & 1); ++i) {}

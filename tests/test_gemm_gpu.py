@@ -294,11 +294,13 @@ print(json.dumps(res))
 """
 
 
-@pytest.mark.parametrize("persist,tile", [("1", "128"), ("1", "256"), ("1", "64"), ("", "")])
-def test_persistent_kernel_bitwise(cuda, persist, tile):
+@pytest.mark.parametrize("persist,tile,pair", [("1", "128", ""), ("1", "256", ""), ("1", "64", ""), ("", "", ""),
+                                               ("", "", "1")])
+def test_persistent_kernel_bitwise(cuda, persist, tile, pair):
     """The persistent GEMM (many tiles; forced with P2CU_PERSIST=1 for every shape, including few-tile ones, or chosen
-    by tile count) against the restatement, bit for bit: every mode, beta 0 / 1 / alpha 1/2, K > 1024 through the
-    workspace slices, the code cache and an int8 table."""
+    by tile count) and the CTA-pair GEMM (P2CU_PAIR=1: every int8w / int8-table shape with N % 256 == 0, including
+    M = 375, whose last pair tile has no rows in its odd CTA) against the restatement, bit for bit: every mode,
+    beta 0 / 1 / alpha 1/2, K > 1024 through the workspace slices, the code cache and an int8 table."""
     import json
     import os
     import subprocess
@@ -308,6 +310,9 @@ def test_persistent_kernel_bitwise(cuda, persist, tile):
     env = dict(os.environ)
     env.pop("P2CU_PERSIST", None)
     env.pop("P2CU_TILE_N", None)
+    env.pop("P2CU_PAIR", None)
+    if pair:
+        env["P2CU_PAIR"] = pair
     if persist:
         env["P2CU_PERSIST"] = persist
     if tile:
