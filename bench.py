@@ -617,6 +617,38 @@ def run_encoder_only(args, world, rank, local):
     print(json.dumps(line))
 
 
+def measured_int8_peak(pkg, pair=False) -> float:
+    """The tcgen05 int8 MMA rate measured on this GPU (p2cu_probe_int8_mma), in TMAC/s."""
+    import ctypes as C
+    v = C.c_double()
+    pkg.check(pkg.lib().p2cu_probe_int8_mma(1 if pair else 0, 4000, C.byref(v)))
+    return v.value / 1e12
+
+
+def run_probes(args):
+    """--workload probes: the hardware rates the GEMM design rests on, one JSON line each: the int8 MMA peak (one CTA
+    per SM, and CTA pairs) and tiled TMA load throughput per SM by issuing warps and box size."""
+    import ctypes as C
+    import torch
+    pkg = ge.load_package()
+    torch.cuda.set_device(0)
+    for pair in (False, True):
+        print(json.dumps({"probe": "int8_mma", "cta_pairs": pair, "value": measured_int8_peak(pkg, pair),
+                          "unit": "TMAC/s", "nominal": 2250.0,
+                          "what": "tcgen05 kind::i8 MMAs from shared memory, M=%d N=256 K=32, all SMs" %
+                                  (256 if pair else 128)}))
+    v = C.c_double()
+    for box_rows in (32, 128, 256):
+        for warps in (1, 2, 4):
+            if 2 * warps * 128 * box_rows > 196608:
+                continue
+            pkg.check(pkg.lib().p2cu_probe_tma_load(warps, box_rows, C.byref(v)))
+            print(json.dumps({"probe": "tma_load", "issuing_warps": warps, "box_bytes": 128 * box_rows,
+                              "value": v.value / 1e9, "unit": "GB/s per SM",
+                              "what": "tiled TMA loads of 128-byte rows from an L2-resident int8 matrix, two boxes "
+                                      "in flight per issuing warp"}))
+
+
 def run_gemm_sweep(args):
     """--workload gemm-sweep: the five-value GEMM alone (quantised A resident) at growing M, K = 1024, N = 4096 (the
     north star's large-M shape) and K = 4096, N = 1024; planes and the code cache. One JSON line per case."""
@@ -627,8 +659,9 @@ def run_gemm_sweep(args):
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     s = torch.cuda.Stream()
-    for (M, K, N) in [(375, 1024, 4096), (4096, 1024, 4096), (8192, 1024, 4096), (24000, 1024, 4096),
-                      (8192, 4096, 1024)]:
+    peak = measured_int8_peak(pkg)
+    for (M, K, N) in [(375, 1024, 4096), (1500, 1024, 4096), (4096, 1024, 4096), (8192, 1024, 4096),
+                      (24000, 1024, 4096), (8192, 4096, 1024)]:
         w = synth.five_value(K, N, seed=1)
         for codes in (False, True):
             B = DeviceFiveValue(w, dev, codes=codes)
@@ -666,7 +699,8 @@ def run_gemm_sweep(args):
             tmacs = M * K * N / (us / 1e6) / 1e12
             print(json.dumps({"metric": "five-value int8 GEMM TMAC/s", "M": M, "K": K, "N": N, "mode": args.mode,
                               "weights": "codes" if codes else "planes", "us": us, "value": tmacs, "unit": "TMAC/s",
-                              "frac_of_nominal_int8": tmacs / 2250.0,
+                              "frac_of_nominal_int8": tmacs / 2250.0, "measured_int8_peak": peak,
+                              "frac_of_measured_int8": tmacs / peak,
                               "hbm_bound_us": (M * K + (K * N if codes else 3 * K * N // 8) + 4 * M * N) / 6534.8e3}))
 
 
@@ -740,7 +774,7 @@ def main():
     ap.add_argument("--no-encoder", action="store_true", help="skip the encoder (config 3) part of the line")
     ap.add_argument("--no-decoder", action="store_true",
                     help="skip the decoder (config 3 windows) and transcription (configs 2, 4) parts of the line")
-    ap.add_argument("--workload", choices=["block-gemms", "encoder", "gemm-sweep"], default="block-gemms",
+    ap.add_argument("--workload", choices=["block-gemms", "encoder", "gemm-sweep", "probes"], default="block-gemms",
                     help="block-gemms: configs[1] with the encoder object (default); encoder: the encoder alone; "
                          "gemm-sweep: the GEMM alone at growing M (one line per case)")
     ap.add_argument("--encoder-config", choices=["long-audio", "window", "short"], default="long-audio",
@@ -757,6 +791,9 @@ def main():
         elif args.workload == "gemm-sweep":
             if rank == 0:
                 run_gemm_sweep(args)
+        elif args.workload == "probes":
+            if rank == 0:
+                run_probes(args)
         else:
             run_ours(args, world, rank, local)
     finally:

@@ -197,6 +197,14 @@ P2CU_API int p2cu_decoder_step(P2cuDecoder *d, int token_id, float *state, float
 /* The joint network (csrc/decoder.c:78-88) on device pointers: logits [8198]. Asynchronous on `stream`. */
 P2CU_API int p2cu_joint(P2cuDecoder *d, const float *enc_t, const float *dec_out, float *logits, void *stream);
 
+/* ---- Measurements of the hardware the kernels are built around (allocate their own buffers; a few launches) ----
+ * p2cu_probe_int8_mma: the tcgen05 int8 MMA rate in MACs per second over all SMs, from shared-memory operands, one
+ * CTA per SM (pair = 0, M = 128 per MMA) or on CTA pairs (pair != 0, M = 256); iters K = 128 steps per SM.
+ * p2cu_probe_tma_load: tiled TMA load bytes per second per SM from an L2-resident matrix, boxes of box_rows 128-byte
+ * rows (8-256) issued by `warps` warps (1-4) of each CTA, two boxes in flight per warp. */
+P2CU_API int p2cu_probe_int8_mma(int pair, int iters, double *macs_per_s);
+P2CU_API int p2cu_probe_tma_load(int warps, int box_rows, double *bytes_per_s_per_sm);
+
 #ifdef __cplusplus
 }
 #endif

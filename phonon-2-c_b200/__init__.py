@@ -87,6 +87,8 @@ SIGNATURES = {
     "p2cu_decoder_offsets": (_vp, [_vp]),
     "p2cu_decoder_step": (_i, [_vp, _i, _vp, _vp, _vp]),
     "p2cu_joint": (_i, [_vp, _vp, _vp, _vp, _vp]),
+    "p2cu_probe_int8_mma": (_i, [_i, _i, C.POINTER(C.c_double)]),
+    "p2cu_probe_tma_load": (_i, [_i, _i, C.POINTER(C.c_double)]),
     # include/phonon2.h: the reference's encoder and decoder entry points
     "p2_encoder": (_i, [_vp, _vp, _i, C.POINTER(_vp), C.POINTER(_i)]),
     "p2_encoder_chunked": (_i, [_vp, _vp, _i, C.POINTER(_vp), C.POINTER(_i)]),

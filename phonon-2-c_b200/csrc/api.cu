@@ -307,6 +307,11 @@ uint32_t* device_error_word() { return dev_err_ptr(); }
 
 size_t gemm_split_bytes(int M, int N, int K) { return split_bytes(M, N, K); }
 
+int make_tile_map(CUtensorMap* map, const void* base, int esize, uint64_t inner, uint64_t outer, uint64_t stride,
+                  uint32_t box_in, uint32_t box_out, int swizzle, const char* what) {
+    return make_map(map, base, esize, inner, outer, stride, box_in, box_out, swizzle, what);
+}
+
 int gemm_i8(int M, int N, int K, float alpha, const int8_t* q, const float* a_scales, const P2cuFiveValue* B,
             const int8_t* q8, const float* scales, int ldb, int mode, float beta, float* C, int ldc, void* ws,
             size_t ws_bytes, cudaStream_t s, const char* who) {

@@ -2,10 +2,16 @@
 #pragma once
 #include <cstddef>
 #include <cstdint>
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include "p2cuda.h"
 
 namespace p2cu {
+
+// A 2-D tiled tensor map over `base` ([outer][inner] elements of `esize` bytes, rows `stride` bytes apart), boxes
+// box_in x box_out, swizzle 128 / 64 / 32 bytes or 0; P2CU_EINVAL with a message when the driver refuses it.
+int make_tile_map(CUtensorMap* map, const void* base, int esize, uint64_t inner, uint64_t outer, uint64_t stride,
+                  uint32_t box_in, uint32_t box_out, int swizzle, const char* what);
 
 // Optional epilogue of the exact (fp32) GEMM: + bias[n], then ReLU, then C = fma(result, res_alpha, C).
 struct Epilogue {

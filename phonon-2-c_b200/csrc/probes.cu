@@ -1,0 +1,245 @@
+// probes.cu - measurements of the B200 features the GEMM kernels are built around, for the roofline and the design:
+//   * p2cu_probe_int8_mma: the tcgen05 kind::i8 MMA rate with shared-memory operands (M = 128, N = 256, K = 32 per
+//     instruction, one CTA per SM; or M = 256 on CTA pairs), i.e. the measured int8 dense peak;
+//   * p2cu_probe_tma_load: tiled TMA load throughput per SM from an L2-resident int8 matrix, with the loads issued
+//     by 1-4 warps of a CTA - one warp's loads complete one after another, which is why the GEMM kernels spread their
+//     K steps over several producer warps.
+// Both allocate their own buffers, run a few launches, and report through out-parameters. Every wait is bounded.
+#include <cstdint>
+#include <cstdio>
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include "p2cuda.h"
+#include "gemm.h"
+#include "ptx.cuh"
+
+using p2cu::fail_fmt;
+
+namespace p2cu {
+namespace {
+
+constexpr int PROBE_THREADS = 128;
+constexpr uint32_t PROBE_TIMEOUT = 30;
+
+// One CTA per SM: `iters` K = 128 steps of four MMAs on zero operands (128 x 128 A, 256-column B, MN-major).
+__global__ void __launch_bounds__(PROBE_THREADS, 1) mma_probe_kernel(int iters, uint32_t* err) {
+    extern __shared__ uint8_t raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* a = smem;                 // 16 KB
+    uint8_t* b = smem + 16384;         // 32 KB
+    uint64_t* bar = reinterpret_cast<uint64_t*>(smem + 16384 + 32768);
+    uint32_t* holder = reinterpret_cast<uint32_t*>(bar + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(holder + 1);
+    for (int i = threadIdx.x; i < (16384 + 32768) / 16; i += blockDim.x)
+        reinterpret_cast<uint4*>(smem)[i] = make_uint4(0, 0, 0, 0);
+    if (threadIdx.x == 0) {
+        mbar_init(bar, 1);
+        *abort_flag = 0;
+        fence_barrier_init();
+    }
+    fence_proxy_async_smem();
+    if (threadIdx.x < 32) {
+        tmem_alloc(holder, 256);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *holder;
+    if (threadIdx.x == 0) {
+        constexpr uint32_t IDESC = idesc_i8(128, 256, false, true);
+        const uint32_t ab = smem_u32(a), bb = smem_u32(b);
+        for (int it = 0; it < iters; ++it)
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks)
+                mma_i8(tmem, smem_desc(ab + ks * 32, 16, 1024, SWZ_128B),
+                       smem_desc(bb + ks * 4 * 1024, 16384, 1024, SWZ_128B), IDESC, (it > 0 || ks > 0) ? 1u : 0u);
+        mma_commit(bar);
+        mbar_wait(bar, 0, PROBE_TIMEOUT, err, abort_flag);
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (threadIdx.x < 32) tmem_dealloc(tmem, 256);
+}
+
+// Clusters of two: the even CTA issues M = 256 MMAs over both CTAs' operands (each: 128 x 128 A, 128 B columns).
+__global__ void __launch_bounds__(PROBE_THREADS, 1) mma_pair_probe_kernel(int iters, uint32_t* err) {
+    extern __shared__ uint8_t raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* a = smem;
+    uint8_t* b = smem + 16384;
+    uint64_t* bar = reinterpret_cast<uint64_t*>(smem + 16384 + 32768);
+    uint32_t* holder = reinterpret_cast<uint32_t*>(bar + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(holder + 1);
+    for (int i = threadIdx.x; i < (16384 + 32768) / 16; i += blockDim.x)
+        reinterpret_cast<uint4*>(smem)[i] = make_uint4(0, 0, 0, 0);
+    if (threadIdx.x == 0) {
+        mbar_init(bar, 1);
+        *abort_flag = 0;
+        fence_barrier_init();
+    }
+    fence_proxy_async_smem();
+    if (threadIdx.x < 32) {
+        tmem_alloc_pair(holder, 256);
+        tmem_relinquish_pair();
+    }
+    tc_fence_before();
+    cluster_sync_all();
+    tc_fence_after();
+    const uint32_t tmem = *holder;
+    if (threadIdx.x == 0 && cluster_ctarank() == 0) {
+        constexpr uint32_t IDESC = idesc_i8(256, 256, false, true);
+        const uint32_t ab = smem_u32(a), bb = smem_u32(b);
+        for (int it = 0; it < iters; ++it)
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks)
+                mma_i8_pair(tmem, smem_desc(ab + ks * 32, 16, 1024, SWZ_128B),
+                            smem_desc(bb + ks * 4 * 1024, 1024, 1024, SWZ_128B), IDESC, (it > 0 || ks > 0) ? 1u : 0u);
+        mma_commit_pair(bar, 0x1);
+        mbar_wait(bar, 0, PROBE_TIMEOUT, err, abort_flag);
+    }
+    tc_fence_before();
+    cluster_sync_all();
+    tc_fence_after();
+    if (threadIdx.x < 32) tmem_dealloc_pair(tmem, 256);
+}
+
+// One CTA per SM: `warps` warps each stream boxes of `box_bytes` (128-byte rows) through a ring of two slots.
+__global__ void __launch_bounds__(PROBE_THREADS, 1)
+tma_probe_kernel(const __grid_constant__ CUtensorMap tm, int boxes, int warps, int box_bytes, int row_blocks,
+                 uint32_t* err) {
+    extern __shared__ uint8_t raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* bar = reinterpret_cast<uint64_t*>(smem + 2 * warps * box_bytes);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(bar + 8);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < 8; ++s) mbar_init(&bar[s], 1);
+        *abort_flag = 0;
+        fence_barrier_init();
+        tma_prefetch_desc(&tm);
+    }
+    __syncthreads();
+    if (warp < warps && lane == 0) {
+        const int box_rows = box_bytes / 128, mine = boxes / warps;
+        for (int i = 0; i < mine + 2; ++i) {
+            const int slot = 2 * warp + (i & 1);
+            if (i >= 2 && !mbar_wait(&bar[slot], ((i - 2) >> 1) & 1, PROBE_TIMEOUT, err, abort_flag)) break;
+            if (i < mine) {
+                const int blk = static_cast<int>((blockIdx.x * 7919u + (i * warps + warp) * 104729u) % row_blocks);
+                mbar_arrive_expect_tx(&bar[slot], box_bytes);
+                tma_load_2d(smem + slot * box_bytes, &tm, &bar[slot], 0, blk * box_rows);
+            }
+        }
+    }
+    __syncthreads();
+}
+
+int sms_of_device() {
+    int dev = 0, n = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    return n;
+}
+
+}  // namespace
+}  // namespace p2cu
+
+extern "C" {
+
+// The int8 MMA rate (MACs per second, all SMs) over `iters` K = 128 steps per SM; pair != 0 on CTA pairs.
+int p2cu_probe_int8_mma(int pair, int iters, double* macs_per_s) {
+    using namespace p2cu;
+    if (!macs_per_s || iters < 1 || iters > (1 << 20)) return fail_fmt(P2CU_EINVAL, "p2cu_probe_int8_mma: arguments");
+    const int sms = sms_of_device();
+    const int smem = 1024 + 16384 + 32768 + 64;
+    cudaError_t e = cudaFuncSetAttribute(pair ? mma_pair_probe_kernel : mma_probe_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaEvent_t e0 = nullptr, e1 = nullptr;
+    if (e == cudaSuccess) e = cudaEventCreate(&e0);
+    if (e == cudaSuccess) e = cudaEventCreate(&e1);
+    float best = 0.f;
+    for (int rep = 0; e == cudaSuccess && rep < 3; ++rep) {
+        cudaEventRecord(e0);
+        if (pair) {
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3(sms / 2 * 2);
+            cfg.blockDim = dim3(PROBE_THREADS);
+            cfg.dynamicSmemBytes = smem;
+            cudaLaunchAttribute attr[1];
+            attr[0].id = cudaLaunchAttributeClusterDimension;
+            attr[0].val.clusterDim.x = 2;
+            attr[0].val.clusterDim.y = 1;
+            attr[0].val.clusterDim.z = 1;
+            cfg.attrs = attr;
+            cfg.numAttrs = 1;
+            e = cudaLaunchKernelEx(&cfg, mma_pair_probe_kernel, iters, device_error_word());
+        } else {
+            mma_probe_kernel<<<sms, PROBE_THREADS, smem>>>(iters, device_error_word());
+            e = cudaGetLastError();
+        }
+        cudaEventRecord(e1);
+        if (e == cudaSuccess) e = cudaEventSynchronize(e1);
+        float ms = 0.f;
+        if (e == cudaSuccess) cudaEventElapsedTime(&ms, e0, e1);
+        if (rep > 0 && (best == 0.f || ms < best)) best = ms;
+    }
+    if (e0) cudaEventDestroy(e0);
+    if (e1) cudaEventDestroy(e1);
+    if (e != cudaSuccess) return cuda_error(e, "p2cu_probe_int8_mma");
+    if (int rc = p2cu_check_device(nullptr)) return rc;
+    const double macs = (pair ? 256.0 : 128.0) * 256.0 * 128.0 * iters * (pair ? sms / 2 : sms);
+    *macs_per_s = macs / (best * 1e-3);
+    return P2CU_OK;
+}
+
+// Tiled TMA load throughput (bytes per second per SM) with `warps` issuing warps per CTA and boxes of `box_rows`
+// 128-byte rows (1-256), from an 8 MB matrix (L2-resident) with 128-byte swizzle.
+int p2cu_probe_tma_load(int warps, int box_rows, double* bytes_per_s_per_sm) {
+    using namespace p2cu;
+    if (!bytes_per_s_per_sm || warps < 1 || warps > 4 || box_rows < 8 || box_rows > 256 || (box_rows & 7) ||
+        2 * warps * 128 * box_rows > 196608)
+        return fail_fmt(P2CU_EINVAL, "p2cu_probe_tma_load: warps 1-4, box rows 8-256 (multiple of 8), "
+                        "2 x warps x box <= 192 KB");
+    const int rows = 8192, width = 128;   // an [8192][1024] matrix read as 128-byte columns of its first 128 bytes
+    const int stride = 1024;
+    uint8_t* buf = nullptr;
+    cudaError_t e = cudaMalloc(&buf, static_cast<size_t>(rows) * stride);
+    if (e != cudaSuccess) return cuda_error(e, "p2cu_probe_tma_load: cudaMalloc");
+    cudaMemset(buf, 1, static_cast<size_t>(rows) * stride);
+    CUtensorMap tm;
+    int rc = make_tile_map(&tm, buf, 1, width, rows, stride, 128, static_cast<uint32_t>(box_rows), 128,
+                           "p2cu_probe_tma_load");
+    const int sms = sms_of_device();
+    const int smem = 1024 + 196608 + 128;
+    const int boxes = 400;
+    float best = 0.f;
+    cudaEvent_t e0 = nullptr, e1 = nullptr;
+    if (rc == P2CU_OK) {
+        e = cudaFuncSetAttribute(tma_probe_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e == cudaSuccess) e = cudaEventCreate(&e0);
+        if (e == cudaSuccess) e = cudaEventCreate(&e1);
+        for (int rep = 0; e == cudaSuccess && rep < 3; ++rep) {
+            cudaEventRecord(e0);
+            tma_probe_kernel<<<sms, PROBE_THREADS, smem>>>(tm, boxes, warps, 128 * box_rows, rows / box_rows,
+                                                          device_error_word());
+            e = cudaGetLastError();
+            cudaEventRecord(e1);
+            if (e == cudaSuccess) e = cudaEventSynchronize(e1);
+            float ms = 0.f;
+            if (e == cudaSuccess) cudaEventElapsedTime(&ms, e0, e1);
+            if (rep > 0 && (best == 0.f || ms < best)) best = ms;
+        }
+        if (e != cudaSuccess) rc = cuda_error(e, "p2cu_probe_tma_load");
+    }
+    if (e0) cudaEventDestroy(e0);
+    if (e1) cudaEventDestroy(e1);
+    cudaFree(buf);
+    if (rc == P2CU_OK) rc = p2cu_check_device(nullptr);
+    if (rc == P2CU_OK) *bytes_per_s_per_sm = static_cast<double>(boxes / warps * warps) * 128 * box_rows /
+                                              (best * 1e-3);
+    return rc;
+}
+
+}  // extern "C"
