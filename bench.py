@@ -54,6 +54,16 @@ def gemm_bytes(M, K, N, beta, codes=False) -> int:
     return M * K + w + 8 * N + 4 * M * N + (4 * M * N if beta != 0.0 else 0)
 
 
+def block_traffic():
+    """DRAM bytes per step of the block GEMMs (int8w, planes) from the committed ncu capture, or None."""
+    import re
+    f = ROOT / "profiles" / "fv_gemm_block_T375_traffic.md"
+    if not f.exists():
+        return None
+    m = re.search(r"^traffic_bytes_per_step: (\d+)$", f.read_text(), re.M)
+    return int(m.group(1)) if m else None
+
+
 def load_peaks():
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -353,7 +363,12 @@ def run_ours(args, world, rank, local):
                            "l2": f"inputs rotate over {nsets} copies ({nsets * first.bytes() / 2**20:.0f} MiB > 2x L2)",
                            "parallelism": f"replicas x{world} (independent windows)"},
                 "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                             "frac": achieved / peak, "traffic": None, "peak_kind": peak_kind,
+                             "frac": achieved / peak,
+                             "traffic": block_traffic() if (args.mode == "int8w" and args.weights == "planes")
+                             else None,
+                             "traffic_source": "profiles/fv_gemm_block_T375_traffic.md: dram__bytes_read.sum + "
+                                               "dram__bytes_write.sum of the nine launches of one step (ncu), bytes",
+                             "peak_kind": peak_kind,
                              "kernel": f"fv_gemm_kernel ({args.weights}; nine launches of a step)",
                              "algo_bytes_per_step": algo_bytes, "gemm_us_per_step": gemm_ms * 1e3},
                 "gpu_launches": args.steps * 2 * len(gemms),
@@ -660,10 +675,13 @@ def run_gemm_sweep(args):
     torch.cuda.set_device(dev)
     s = torch.cuda.Stream()
     peak = measured_int8_peak(pkg)
-    for (M, K, N) in [(375, 1024, 4096), (1500, 1024, 4096), (4096, 1024, 4096), (8192, 1024, 4096),
-                      (24000, 1024, 4096), (8192, 4096, 1024)]:
+    shapes = [(375, 1024, 4096), (1500, 1024, 4096), (4096, 1024, 4096), (8192, 1024, 4096), (24000, 1024, 4096),
+              (8192, 4096, 1024)]
+    if args.gemm_shape:
+        shapes = [tuple(int(x) for x in args.gemm_shape.split(","))]
+    for (M, K, N) in shapes:
         w = synth.five_value(K, N, seed=1)
-        for codes in (False, True):
+        for codes in ((args.weights == "codes",) if args.gemm_shape else (False, True)):
             B = DeviceFiveValue(w, dev, codes=codes)
             A = torch.from_numpy(synth.activations(M, K, seed=2)).to(dev)
             q = torch.empty((M, K), dtype=torch.int8, device=dev)
@@ -780,6 +798,7 @@ def main():
     ap.add_argument("--encoder-config", choices=["long-audio", "window", "short"], default="long-audio",
                     help="--workload encoder: configs[3] (64 windows), [2] (one 30 s window) or [4] (3 s)")
     ap.add_argument("--windows", type=int, default=0, help="--workload encoder long-audio: only the first N windows")
+    ap.add_argument("--gemm-shape", default="", help="--workload gemm-sweep: only this M,K,N (with --weights)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     world, rank, local = dist_setup(args)
