@@ -380,8 +380,10 @@ def run_ours(args, world, rank, local):
             line["encoder"] = enc
     if not args.no_decoder:
         dec = decoder_ours(args, world, rank, local, torch, pkg)
+        mel = mel_ours(args, world, rank, local, torch, pkg)
         if rank == 0:
             line["decoder"] = dec
+            line["mel"] = mel
             line["transcribe"] = transcribe_ours(pkg, local)
     if rank == 0:
         if world == 1 and not args.no_cpu_baseline:
@@ -390,6 +392,7 @@ def run_ours(args, world, rank, local):
                 line["encoder"]["cpu_baseline"] = encoder_reference()
             if not args.no_decoder:
                 line["decoder"]["cpu_baseline"] = decoder_reference()
+                line["mel"]["cpu_baseline"] = mel_reference()
                 for cfg in line["transcribe"]:
                     cfg["cpu_baseline"] = transcribe_reference(cfg["mel_frames"])
         print(json.dumps(line))
@@ -572,6 +575,86 @@ def decoder_reference(seconds=10.0):
     return {"value": done * ENC_SECONDS_PER_FRAME / dt, "unit": "audio-s/s", "cores": orc.ref_threads(),
             "kind": "reference",
             "sample": f"phonon-2-c p2_greedy_decode on {n} window(s) of the decoder workload in {dt:.1f} s, "
+                      "P2_THREADS = all host cores"}
+
+
+def mel_ours(args, world, rank, local, torch, pkg, steps=5):
+    """The log-mel front end on this rank's share of the config-3 windows as 16 kHz audio (160 samples per mel frame):
+    device-timed p2cu_mel_run over the rank's windows (audio resident); then the whole path from audio - log-mel,
+    encoder, decoder - end to end through p2_b200_transcribe_audio_windows (host audio in, host tokens out)."""
+    from phonon2_b200 import model as M
+    frames, desc = encoder_workload("long-audio")
+    mine = shard_windows(frames, world)[rank]
+    ns = [frames[w] * 160 for w in mine]
+    audios = [M.audio(n, seed=w) for n, w in zip(ns, mine)]
+    stream = torch.cuda.Stream()
+    ms = 0.0
+    plan = None
+    if mine:
+        x = torch.from_numpy(np.concatenate(audios)).to(f"cuda:{local}")
+        out = torch.empty((sum(n // 160 for n in ns), 128), device=f"cuda:{local}")
+        plan = pkg.Mel(len(ns), sum(ns))
+        for _ in range(2):
+            plan.run(x.data_ptr(), ns, out.data_ptr(), stream)
+        stream.synchronize()
+    barrier(world)
+    if plan is not None:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            plan.run(x.data_ptr(), ns, out.data_ptr(), stream)
+        e1.record(stream)
+        e1.synchronize()
+        pkg.check_device(stream)
+        ms = e0.elapsed_time(e1) / steps
+    barrier(world)
+    ms_max = max_over_ranks(ms, world)
+    audio_s = sum(frames) * ENC_SECONDS_PER_FRAME
+    sm = M.SyntheticModel(seed=1)
+    e2e_ms = 0.0
+    n_tok = 0
+    if mine:
+        toks = pkg.host_transcribe_audio_windows(sm.struct, audios, devices=[local])   # plans outside the timing
+        n_tok = sum(len(t) for t in toks)
+        t0 = time.perf_counter()
+        for _ in range(2):
+            pkg.host_transcribe_audio_windows(sm.struct, audios, devices=[local])
+        e2e_ms = (time.perf_counter() - t0) / 2 * 1e3
+    barrier(world)
+    e2e_max = max_over_ranks(e2e_ms, world)
+    res = {"metric": "log-mel audio-sec/sec", "value": audio_s / (ms_max / 1e3), "unit": "audio-s/s",
+           "ms_per_step": ms_max, "steps": steps,
+           "workload": desc + "; as synthetic 16 kHz audio (seeded harmonics under a syllable envelope)",
+           "timing": "CUDA events around p2cu_mel_run over the rank's windows (audio resident), max over ranks",
+           "gpu_launches_per_step": 2,
+           "transcribe_audio": {"value": audio_s / (e2e_max / 1e3), "unit": "audio-s/s", "ms_per_step": e2e_max,
+                                "tokens_rank0": n_tok, "h2d_bytes_per_step": 4 * sum(ns),
+                                "d2h_bytes_per_step": 12 * n_tok,
+                                "api": "p2_b200_transcribe_audio_windows: log-mel, encoder and decoder on the device "
+                                       "(host audio in, host tokens out), wall clock, max over ranks"}}
+    if plan is not None:
+        plan.close()
+    return res
+
+
+def mel_reference(seconds=5.0):
+    """phonon-2-c's own p2_mel_spectrogram on the host cores over the config-3 windows for about `seconds`."""
+    orc = ge.load_oracle()
+    if not orc.ref_available():
+        return None
+    from phonon2_b200 import model as M
+    frames, _ = encoder_workload("long-audio")
+    done, dt, n = 0.0, 0.0, 0
+    while dt < seconds:
+        w = n % len(frames)
+        a = M.audio(frames[w] * 160, seed=w)
+        t1 = time.perf_counter()
+        orc.ref_mel_spectrogram(a)
+        dt += time.perf_counter() - t1
+        done += frames[w] * ENC_SECONDS_PER_FRAME
+        n += 1
+    return {"value": done / dt, "unit": "audio-s/s", "cores": orc.ref_threads(), "kind": "reference",
+            "sample": f"phonon-2-c p2_mel_spectrogram on {n} window(s) of the workload, {dt:.1f} s inside the calls, "
                       "P2_THREADS = all host cores"}
 
 

@@ -197,6 +197,19 @@ P2CU_API int p2cu_decoder_step(P2cuDecoder *d, int token_id, float *state, float
 /* The joint network (csrc/decoder.c:78-88) on device pointers: logits [8198]. Asynchronous on `stream`. */
 P2CU_API int p2cu_joint(P2cuDecoder *d, const float *enc_t, const float *dec_out, float *logits, void *stream);
 
+/* ---- The log-mel front end on the device (csrc/mel.c) ---------------------------------------------------------------
+ * p2cu_mel_create allocates the plan's tables for up to max_windows windows of max_samples samples together; runs
+ * allocate nothing. p2cu_mel_run computes, for each window of n_samples[w] samples (16 kHz, host array) stacked in
+ * `audio` (device), n_samples[w] / 160 frames of normalised log-mel features into `mel` (device, [sum frames][128],
+ * windows stacked) on `stream`; it waits for its small host-to-device table copies before returning. A window needs at
+ * least 320 samples (two frames), as in the reference. */
+typedef struct P2cuMel P2cuMel;
+P2CU_API int p2cu_mel_create(int max_windows, long long max_samples, P2cuMel **out);
+P2CU_API void p2cu_mel_destroy(P2cuMel *plan);
+P2CU_API int p2cu_mel_frames(long long n_samples);
+P2CU_API int p2cu_mel_run(P2cuMel *plan, const float *audio, const long long *n_samples, int n_windows, float *mel,
+                          void *stream);
+
 /* ---- Measurements of the hardware the kernels are built around (allocate their own buffers; a few launches) ----
  * p2cu_probe_int8_mma: the tcgen05 int8 MMA rate in MACs per second over all SMs, from shared-memory operands, one
  * CTA per SM (pair = 0, M = 128 per MMA) or on CTA pairs (pair != 0, M = 256); iters K = 128 steps per SM.

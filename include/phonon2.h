@@ -200,6 +200,19 @@ P2_API void p2_joint(const P2Model *m, const float *enc_t, const float *dec_out,
  * count returned, or -1 with a message on stderr. */
 P2_API int p2_greedy_decode(const P2Model *m, const float *enc_out, int T, P2Token **out_tokens);
 
+/* Log-mel features of 16 kHz audio (csrc/phonon2.h:391-392, csrc/mel.c): n_samples / 160 frames of 128 normalised
+ * log-mel values, computed on the calling thread's GPU; *out_mel is malloc'd (the caller frees it). Returns 0, or -1
+ * with a message on stderr (fewer than 320 samples: "audio too short", as the reference). */
+P2_API int p2_mel_spectrogram(const float *audio, int n_samples, float **out_mel, int *out_frames);
+
+/* The whole path from audio: log-mel, encoder and greedy decoder per window on the device, windows spread across GPUs
+ * as p2_b200_encode_windows spreads them. Window w has n_samples[w] samples (16 kHz), the windows one after another in
+ * `audio`; tokens / n_tokens as p2_b200_transcribe_windows. No counterpart in the reference, whose engine runs
+ * p2_mel_spectrogram, p2_encoder and p2_greedy_decode window after window (csrc/engine.c:256-292). */
+P2_API int p2_b200_transcribe_audio_windows(const P2Model *m, const float *audio, const long long *n_samples,
+                                            int n_windows, const int *devices, int n_devices, P2Token **tokens,
+                                            int *n_tokens);
+
 /* Encoder and greedy decoder over a batch of windows spread across GPUs, the encoder frames staying on the device. No
  * counterpart in the reference, whose engine runs p2_encoder then p2_greedy_decode window after window
  * (csrc/engine.c:100-125, 311-357). Windows, mel layout and GPU placement as p2_b200_encode_windows. tokens[w] receives

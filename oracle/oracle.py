@@ -285,6 +285,23 @@ def ref_joint(model_struct, enc_t: np.ndarray, dec_out: np.ndarray) -> np.ndarra
     return logits
 
 
+def ref_mel_spectrogram(audio: np.ndarray) -> np.ndarray:
+    """phonon-2-c's p2_mel_spectrogram (csrc/mel.c:158-217) on 16 kHz audio: [n // 160, 128] normalised log-mel."""
+    L = ref()
+    if not hasattr(L, "_mel_ready"):
+        L.p2_mel_spectrogram.argtypes = [_f32p, C.c_int, C.POINTER(C.c_void_p), C.POINTER(C.c_int)]
+        L.p2_mel_spectrogram.restype = C.c_int
+        L._mel_ready = True
+    audio = np.ascontiguousarray(audio, np.float32)
+    out, n = C.c_void_p(), C.c_int()
+    if L.p2_mel_spectrogram(audio, audio.shape[0], C.byref(out), C.byref(n)) != 0:
+        raise RuntimeError("reference p2_mel_spectrogram failed")
+    try:
+        return np.ctypeslib.as_array(C.cast(out, C.POINTER(C.c_float)), shape=(n.value, 128)).copy()
+    finally:
+        _libc.free(out)
+
+
 class _QuantA(C.Structure):   # csrc/phonon2.h:432-436
     _fields_ = [("q", C.c_void_p), ("scales", C.c_void_p), ("M", C.c_int), ("K", C.c_int)]
 

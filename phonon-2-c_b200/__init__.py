@@ -87,6 +87,10 @@ SIGNATURES = {
     "p2cu_decoder_offsets": (_vp, [_vp]),
     "p2cu_decoder_step": (_i, [_vp, _i, _vp, _vp, _vp]),
     "p2cu_joint": (_i, [_vp, _vp, _vp, _vp, _vp]),
+    "p2cu_mel_create": (_i, [_i, C.c_longlong, C.POINTER(_vp)]),
+    "p2cu_mel_destroy": (None, [_vp]),
+    "p2cu_mel_frames": (_i, [C.c_longlong]),
+    "p2cu_mel_run": (_i, [_vp, _vp, C.POINTER(C.c_longlong), _i, _vp, _vp]),
     "p2cu_probe_int8_mma": (_i, [_i, _i, C.POINTER(C.c_double)]),
     "p2cu_probe_tma_load": (_i, [_i, _i, C.POINTER(C.c_double)]),
     # include/phonon2.h: the reference's encoder and decoder entry points
@@ -98,6 +102,9 @@ SIGNATURES = {
     "p2_greedy_decode": (_i, [_vp, _vp, _i, C.POINTER(_vp)]),
     "p2_b200_transcribe_windows": (_i, [_vp, _vp, C.POINTER(_i), _i, C.POINTER(_i), _i, C.POINTER(_vp),
                                         C.POINTER(_i)]),
+    "p2_mel_spectrogram": (_i, [_vp, _i, C.POINTER(_vp), C.POINTER(_i)]),
+    "p2_b200_transcribe_audio_windows": (_i, [_vp, _vp, C.POINTER(C.c_longlong), _i, C.POINTER(_i), _i,
+                                              C.POINTER(_vp), C.POINTER(_i)]),
     # include/blas.h: the reference's host-pointer ABI
     "p2_sgemm": (None, [_i, _i, _i, _i, _i, _f, _vp, _i, _vp, _i, _f, _vp, _i]),
     "p2_sgemm_st": (None, [_i, _i, _i, _i, _i, _f, _vp, _i, _vp, _i, _f, _vp, _i]),
@@ -434,6 +441,72 @@ def host_transcribe_windows(model_struct, mels, devices=None):
     res = []
     libc = C.CDLL(None)
     for i in range(len(frames)):
+        res.append(_tokens_array(toks[i], counts[i]))
+        if toks[i]:
+            libc.free(C.c_void_p(toks[i]))
+    return res
+
+
+# ---- the log-mel front end (include/p2cuda.h device plan, include/phonon2.h host entry) -----------------------------
+
+class Mel:
+    """p2cu_mel_create: tables for up to max_windows windows of max_samples samples together."""
+
+    def __init__(self, max_windows: int, max_samples: int):
+        self.ptr = C.c_void_p()
+        check(lib().p2cu_mel_create(max_windows, max_samples, C.byref(self.ptr)))
+
+    def run(self, audio_ptr: int, n_samples, mel_ptr: int, stream=None) -> None:
+        ns = (C.c_longlong * len(n_samples))(*[int(n) for n in n_samples])
+        check(lib().p2cu_mel_run(self.ptr, audio_ptr, ns, len(n_samples), mel_ptr, stream_ptr(stream)))
+
+    def close(self) -> None:
+        if self.ptr:
+            lib().p2cu_mel_destroy(self.ptr)
+            self.ptr = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def mel_frames(n_samples: int) -> int:
+    return lib().p2cu_mel_frames(n_samples)
+
+
+def host_mel_spectrogram(audio):
+    """p2_mel_spectrogram on host audio (16 kHz float32): the [n // 160, 128] features as numpy."""
+    import numpy as _np
+    audio = _np.ascontiguousarray(audio, dtype=_np.float32)
+    out = C.c_void_p()
+    n = C.c_int()
+    rc = lib().p2_mel_spectrogram(audio.ctypes.data, audio.shape[0], C.byref(out), C.byref(n))
+    if rc != 0:
+        raise Error(rc, "p2_mel_spectrogram failed (see stderr)")
+    try:
+        return _np.ctypeslib.as_array(C.cast(out, C.POINTER(C.c_float)), shape=(n.value, 128)).copy()
+    finally:
+        C.CDLL(None).free(out)
+
+
+def host_transcribe_audio_windows(model_struct, audios, devices=None):
+    """p2_b200_transcribe_audio_windows: a list of host audio arrays (16 kHz) -> per-window int32 [k, 3] tokens."""
+    import numpy as _np
+    ns = [int(a.shape[0]) for a in audios]
+    stacked = _np.ascontiguousarray(_np.concatenate(audios), dtype=_np.float32)
+    na = (C.c_longlong * len(ns))(*ns)
+    devs = None if not devices else (C.c_int * len(devices))(*devices)
+    toks = (C.c_void_p * len(ns))()
+    counts = (C.c_int * len(ns))()
+    rc = lib().p2_b200_transcribe_audio_windows(C.addressof(model_struct), stacked.ctypes.data, na, len(ns), devs,
+                                                len(devices) if devices else 0, toks, counts)
+    if rc != 0:
+        raise Error(rc, "p2_b200_transcribe_audio_windows failed (see stderr)")
+    res = []
+    libc = C.CDLL(None)
+    for i in range(len(ns)):
         res.append(_tokens_array(toks[i], counts[i]))
         if toks[i]:
             libc.free(C.c_void_p(toks[i]))

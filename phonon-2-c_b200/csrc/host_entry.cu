@@ -14,6 +14,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <functional>
+#include <memory>
 #include <mutex>
 #include <numeric>
 #include <string>
@@ -99,6 +100,8 @@ struct ThreadCtx {
     int dec_frames = 0;
     float* io = nullptr;
     size_t io_floats = 0;
+    P2cuMel* mel = nullptr;   // p2_mel_spectrogram's one-window plan
+    long long mel_samples = 0;
 
     void drop_plan() {
         if (plan) p2cu_encoder_destroy(plan);
@@ -108,6 +111,9 @@ struct ThreadCtx {
         dec = nullptr;
         dec_model = nullptr;
         dec_frames = 0;
+        if (mel) p2cu_mel_destroy(mel);
+        mel = nullptr;
+        mel_samples = 0;
     }
     void drop_all() {
         if (device >= 0) cudaSetDevice(device);
@@ -278,6 +284,33 @@ struct DeviceSlot {
     P2cuDecoder* dec = nullptr;
     const P2cuModel* dec_model = nullptr;
     int dec_windows = 0, dec_frames = 0;
+    P2cuMel* mel = nullptr;          // the log-mel plan and the audio it reads (p2_b200_transcribe_audio_windows)
+    int mel_windows = 0;
+    long long mel_samples = 0;
+    float* audio = nullptr;
+
+    P2cuMel* mel_for(int windows, long long samples) {
+        if (mel && mel_windows >= windows && mel_samples >= samples) return mel;
+        drop_mel();
+        const int w = std::max(windows, 1);
+        const long long n = std::max(samples, static_cast<long long>(P2_N_MELS));
+        if (p2cu_mel_create(w, n, &mel) != P2CU_OK) return nullptr;
+        if (cudaMalloc(&audio, static_cast<size_t>(n) * sizeof(float)) != cudaSuccess) {
+            drop_mel();
+            return nullptr;
+        }
+        mel_windows = w;
+        mel_samples = n;
+        return mel;
+    }
+    void drop_mel() {
+        if (mel) p2cu_mel_destroy(mel);
+        if (audio) cudaFree(audio);
+        mel = nullptr;
+        audio = nullptr;
+        mel_windows = 0;
+        mel_samples = 0;
+    }
 
     P2cuEncoder* plan_for(const P2cuModel* dm, const std::vector<int>& frames, int mode, int chunk, int overlap) {
         for (Cached& c : plans)
@@ -317,12 +350,14 @@ DeviceSlot g_slots[64];
 // caller's window indices of the plan's windows in order.
 using AfterEncode = std::function<int(P2cuEncoder*, cudaStream_t, DeviceSlot&, const P2cuModel*,
                                       const std::vector<int>&, std::string*)>;
+// How a batched entry point fills an encoder plan's input (its mel frames, windows stacked) from the caller's data.
+using FeedEncoder = std::function<int(P2cuEncoder*, cudaStream_t, DeviceSlot&, const std::vector<int>&,
+                                      std::string*)>;
 
-// Encode `wins` (indices into the caller's windows) on `device` with one plan, then run `after` on its output; mel is
-// the caller's host array with per-window row offsets.
-int encode_on_device(const P2Model* m, int device, const std::vector<int>& wins, const float* mel,
-                     const std::vector<long long>& mel_off, const int* n_frames, int chunk, int overlap,
-                     const AfterEncode& after, std::string* err) {
+// Encode `wins` (indices into the caller's windows) on `device` with one plan, its input written by `feed`, then run
+// `after` on its output.
+int encode_on_device(const P2Model* m, int device, const std::vector<int>& wins, const int* n_frames, int chunk,
+                     int overlap, const FeedEncoder& feed, const AfterEncode& after, std::string* err) {
     if (wins.empty()) return 0;
     if (cudaSetDevice(device) != cudaSuccess) {
         *err = "cannot use GPU " + std::to_string(device);
@@ -346,29 +381,79 @@ int encode_on_device(const P2Model* m, int device, const std::vector<int>& wins,
         *err = p2cu_last_error();
         return -1;
     }
-    float* dmel = p2cu_encoder_mel(e);
-    cudaError_t ce = cudaSuccess;
-    size_t row = 0;
-    for (int w : wins) {
-        ce = cudaMemcpyAsync(dmel + row * P2_N_MELS, mel + mel_off[w] * P2_N_MELS,
-                             static_cast<size_t>(n_frames[w]) * P2_N_MELS * sizeof(float), cudaMemcpyHostToDevice,
-                             slot.stream);
-        if (ce != cudaSuccess) break;
-        row += n_frames[w];
-    }
-    const int rc = ce == cudaSuccess ? p2cu_encoder_run(e, slot.stream) : P2CU_ECUDA;
-    if (rc != P2CU_OK || ce != cudaSuccess) {
-        *err = ce != cudaSuccess ? cudaGetErrorString(ce) : p2cu_last_error();
+    if (feed(e, slot.stream, slot, wins, err) != 0) return -1;
+    if (p2cu_encoder_run(e, slot.stream) != P2CU_OK) {
+        *err = p2cu_last_error();
         return -1;
     }
     return after(e, slot.stream, slot, dm, wins, err);
 }
 
+// FeedEncoder from host mel frames ([sum n_frames][128], windows one after another).
+FeedEncoder feed_host_mel(const float* mel, const int* n_frames, int n_windows) {
+    auto off = std::make_shared<std::vector<long long>>(n_windows + 1, 0);
+    for (int w = 0; w < n_windows; ++w) (*off)[w + 1] = (*off)[w] + n_frames[w];
+    return [mel, n_frames, off](P2cuEncoder* e, cudaStream_t s, DeviceSlot&, const std::vector<int>& wins,
+                                std::string* err) {
+        float* dmel = p2cu_encoder_mel(e);
+        size_t row = 0;
+        for (int w : wins) {
+            const cudaError_t ce = cudaMemcpyAsync(dmel + row * P2_N_MELS, mel + (*off)[w] * P2_N_MELS,
+                                                   static_cast<size_t>(n_frames[w]) * P2_N_MELS * sizeof(float),
+                                                   cudaMemcpyHostToDevice, s);
+            if (ce != cudaSuccess) {
+                *err = cudaGetErrorString(ce);
+                return -1;
+            }
+            row += n_frames[w];
+        }
+        return 0;
+    };
+}
+
+// FeedEncoder from host audio ([sum n_samples] at 16 kHz): the windows' samples go up, the log-mel front end writes the
+// plan's input on the device.
+FeedEncoder feed_host_audio(const float* audio, const long long* n_samples, int n_windows) {
+    auto off = std::make_shared<std::vector<long long>>(n_windows + 1, 0);
+    for (int w = 0; w < n_windows; ++w) (*off)[w + 1] = (*off)[w] + n_samples[w];
+    return [audio, n_samples, off](P2cuEncoder* e, cudaStream_t s, DeviceSlot& slot, const std::vector<int>& wins,
+                                   std::string* err) {
+        long long total = 0;
+        std::vector<long long> ns;
+        for (int w : wins) {
+            ns.push_back(n_samples[w]);
+            total += n_samples[w];
+        }
+        P2cuMel* mp = slot.mel_for(static_cast<int>(wins.size()), total);
+        if (!mp) {
+            *err = std::string("log-mel plan: ") + p2cu_last_error();
+            return -1;
+        }
+        long long at = 0;
+        for (int w : wins) {
+            const cudaError_t ce = cudaMemcpyAsync(slot.audio + at, audio + (*off)[w],
+                                                   static_cast<size_t>(n_samples[w]) * sizeof(float),
+                                                   cudaMemcpyHostToDevice, s);
+            if (ce != cudaSuccess) {
+                *err = cudaGetErrorString(ce);
+                return -1;
+            }
+            at += n_samples[w];
+        }
+        if (p2cu_mel_run(mp, slot.audio, ns.data(), static_cast<int>(wins.size()), p2cu_encoder_mel(e), s) !=
+            P2CU_OK) {
+            *err = p2cu_last_error();
+            return -1;
+        }
+        return 0;
+    };
+}
+
 // The window checks, the sharding over GPUs and one host thread per GPU, shared by the batched entry points: `after`
 // runs on every plan's output. The reference's chunking rule applies per window (csrc/encoder.c:715-723): windows it
 // would chunk go in a plan of their own on the same GPU.
-int run_windows(const char* who, const P2Model* m, const float* mel, const int* n_frames, int n_windows,
-                const int* devices, int n_devices, const AfterEncode& after) {
+int run_windows(const char* who, const P2Model* m, const int* n_frames, int n_windows, const int* devices,
+                int n_devices, const FeedEncoder& feed, const AfterEncode& after) {
     std::vector<int> devs;
     if (n_devices == 0) {
         int n = 0;
@@ -385,14 +470,11 @@ int run_windows(const char* who, const P2Model* m, const float* mel, const int* 
             fprintf(stderr, "%s: device %d out of range\n", who, d);
             return -1;
         }
-    std::vector<long long> mel_off(n_windows + 1, 0);
-    for (int w = 0; w < n_windows; ++w) {
+    for (int w = 0; w < n_windows; ++w)
         if (n_frames[w] < 1) {
             fprintf(stderr, "%s: window %d has %d frames\n", who, w, n_frames[w]);
             return -1;
         }
-        mel_off[w + 1] = mel_off[w] + n_frames[w];
-    }
     const int chunk = env_int("P2_CHUNK_SIZE", 400), overlap = env_int("P2_CHUNK_OVERLAP", 8);
     int prev = 0;
     cudaGetDevice(&prev);
@@ -405,10 +487,9 @@ int run_windows(const char* who, const P2Model* m, const float* mel, const int* 
         threads.emplace_back([&, i] {
             std::vector<int> plain, chunked;
             for (int w : shards[i]) (should_chunk(conv3(n_frames[w])) ? chunked : plain).push_back(w);
-            rcs[i] = encode_on_device(m, devs[i], plain, mel, mel_off, n_frames, 0, 0, after, &errs[i]);
+            rcs[i] = encode_on_device(m, devs[i], plain, n_frames, 0, 0, feed, after, &errs[i]);
             if (rcs[i] == 0)
-                rcs[i] = encode_on_device(m, devs[i], chunked, mel, mel_off, n_frames, chunk, overlap, after,
-                                          &errs[i]);
+                rcs[i] = encode_on_device(m, devs[i], chunked, n_frames, chunk, overlap, feed, after, &errs[i]);
         });
     }
     for (auto& t : threads) t.join();
@@ -455,28 +536,19 @@ __attribute__((visibility("default"))) int p2_b200_encode_windows(const P2Model*
         }
         return 0;
     };
-    return run_windows("p2_b200_encode_windows", m, mel, n_frames, n_windows, devices, n_devices, copy_out);
+    return run_windows("p2_b200_encode_windows", m, n_frames, n_windows, devices, n_devices,
+                       feed_host_mel(mel, n_frames, n_windows), copy_out);
 }
 
-__attribute__((visibility("default"))) int p2_b200_transcribe_windows(const P2Model* m, const float* mel,
-                                                                      const int* n_frames, int n_windows,
-                                                                      const int* devices, int n_devices,
-                                                                      P2Token** tokens, int* n_tokens) {
-    if (!m || !mel || !n_frames || n_windows <= 0 || !tokens || !n_tokens || n_devices < 0 ||
-        (n_devices > 0 && !devices)) {
-        fprintf(stderr, "p2_b200_transcribe_windows: bad arguments\n");
-        return -1;
-    }
-    if (!m->dec.embed_w) {
-        fprintf(stderr, "p2_b200_transcribe_windows: the model has no decoder tables\n");
-        return -1;
-    }
-    for (int w = 0; w < n_windows; ++w) {
-        tokens[w] = nullptr;
-        n_tokens[w] = 0;
-    }
-    auto decode = [&](P2cuEncoder* e, cudaStream_t s, DeviceSlot& slot, const P2cuModel* dm,
-                      const std::vector<int>& wins, std::string* err) {
+}  // extern "C"
+
+namespace {
+
+// AfterEncode that decodes each plan's output on the device and hands every window's tokens to the caller (malloc'd
+// arrays in tokens[w], counts in n_tokens[w]).
+AfterEncode decode_after(P2Token** tokens, int* n_tokens) {
+    return [tokens, n_tokens](P2cuEncoder* e, cudaStream_t s, DeviceSlot& slot, const P2cuModel* dm,
+                              const std::vector<int>& wins, std::string* err) {
         const int nw = static_cast<int>(wins.size());
         std::vector<int> T(nw);
         for (int i = 0; i < nw; ++i) T[i] = p2cu_encoder_frames(e, i);
@@ -513,7 +585,20 @@ __attribute__((visibility("default"))) int p2_b200_transcribe_windows(const P2Mo
         }
         return 0;
     };
-    const int rc = run_windows("p2_b200_transcribe_windows", m, mel, n_frames, n_windows, devices, n_devices, decode);
+}
+
+// The shared part of the transcribe entry points: checks, token arrays reset, run, arrays freed on failure.
+int transcribe(const char* who, const P2Model* m, const int* n_frames, int n_windows, const int* devices,
+               int n_devices, const FeedEncoder& feed, P2Token** tokens, int* n_tokens) {
+    if (!m->dec.embed_w) {
+        fprintf(stderr, "%s: the model has no decoder tables\n", who);
+        return -1;
+    }
+    for (int w = 0; w < n_windows; ++w) {
+        tokens[w] = nullptr;
+        n_tokens[w] = 0;
+    }
+    const int rc = run_windows(who, m, n_frames, n_windows, devices, n_devices, feed, decode_after(tokens, n_tokens));
     if (rc != 0)
         for (int w = 0; w < n_windows; ++w) {
             free(tokens[w]);
@@ -521,6 +606,106 @@ __attribute__((visibility("default"))) int p2_b200_transcribe_windows(const P2Mo
             n_tokens[w] = 0;
         }
     return rc;
+}
+
+}  // namespace
+
+extern "C" {
+
+__attribute__((visibility("default"))) int p2_b200_transcribe_windows(const P2Model* m, const float* mel,
+                                                                      const int* n_frames, int n_windows,
+                                                                      const int* devices, int n_devices,
+                                                                      P2Token** tokens, int* n_tokens) {
+    if (!m || !mel || !n_frames || n_windows <= 0 || !tokens || !n_tokens || n_devices < 0 ||
+        (n_devices > 0 && !devices)) {
+        fprintf(stderr, "p2_b200_transcribe_windows: bad arguments\n");
+        return -1;
+    }
+    return transcribe("p2_b200_transcribe_windows", m, n_frames, n_windows, devices, n_devices,
+                      feed_host_mel(mel, n_frames, n_windows), tokens, n_tokens);
+}
+
+__attribute__((visibility("default"))) int p2_b200_transcribe_audio_windows(const P2Model* m, const float* audio,
+                                                                            const long long* n_samples,
+                                                                            int n_windows, const int* devices,
+                                                                            int n_devices, P2Token** tokens,
+                                                                            int* n_tokens) {
+    if (!m || !audio || !n_samples || n_windows <= 0 || !tokens || !n_tokens || n_devices < 0 ||
+        (n_devices > 0 && !devices)) {
+        fprintf(stderr, "p2_b200_transcribe_audio_windows: bad arguments\n");
+        return -1;
+    }
+    std::vector<int> frames(n_windows);
+    for (int w = 0; w < n_windows; ++w) {
+        frames[w] = p2cu_mel_frames(n_samples[w]);
+        if (frames[w] < 2) {
+            fprintf(stderr, "p2_b200_transcribe_audio_windows: window %d: audio too short: %lld samples\n", w,
+                    n_samples[w]);
+            return -1;
+        }
+    }
+    return transcribe("p2_b200_transcribe_audio_windows", m, frames.data(), n_windows, devices, n_devices,
+                      feed_host_audio(audio, n_samples, n_windows), tokens, n_tokens);
+}
+
+__attribute__((visibility("default"))) int p2_mel_spectrogram(const float* audio, int n_samples, float** out_mel,
+                                                              int* out_frames) {
+    if (!audio || !out_mel || !out_frames || n_samples < 0) {
+        fprintf(stderr, "p2_mel_spectrogram: bad arguments\n");
+        return -1;
+    }
+    const int nf = p2cu_mel_frames(n_samples);
+    if (nf < 2) {
+        fprintf(stderr, "audio too short: %d samples\n", n_samples);   // the reference's message
+        return -1;
+    }
+    ThreadCtx* cp = thread_ctx("p2_mel_spectrogram");
+    if (!cp) return -1;
+    ThreadCtx& c = *cp;
+    const size_t need = static_cast<size_t>(n_samples) + static_cast<size_t>(nf) * P2_N_MELS;
+    if (!c.mel || c.mel_samples < n_samples) {
+        if (c.mel) p2cu_mel_destroy(c.mel);
+        c.mel = nullptr;
+        const long long cap = std::max<long long>(n_samples, 2 * c.mel_samples);
+        if (p2cu_mel_create(1, cap, &c.mel) != P2CU_OK) {
+            fprintf(stderr, "p2_mel_spectrogram: %s\n", p2cu_last_error());
+            c.mel_samples = 0;
+            return -1;
+        }
+        c.mel_samples = cap;
+    }
+    if (c.io_floats < need) {
+        if (c.io) cudaFree(c.io);
+        c.io = nullptr;
+        c.io_floats = 0;
+        if (cudaMalloc(&c.io, need * sizeof(float)) != cudaSuccess) {
+            fprintf(stderr, "p2_mel_spectrogram: cannot allocate device memory\n");
+            return -1;
+        }
+        c.io_floats = need;
+    }
+    float* res = static_cast<float*>(malloc(static_cast<size_t>(nf) * P2_N_MELS * sizeof(float)));
+    if (!res) {
+        fprintf(stderr, "p2_mel_spectrogram: out of memory\n");
+        return -1;
+    }
+    const long long ns = n_samples;
+    float* dmel = c.io + n_samples;
+    cudaError_t ce = cudaMemcpyAsync(c.io, audio, static_cast<size_t>(n_samples) * sizeof(float),
+                                     cudaMemcpyHostToDevice, c.stream);
+    int rc = ce == cudaSuccess ? p2cu_mel_run(c.mel, c.io, &ns, 1, dmel, c.stream) : P2CU_ECUDA;
+    if (rc == P2CU_OK)
+        ce = cudaMemcpyAsync(res, dmel, static_cast<size_t>(nf) * P2_N_MELS * sizeof(float), cudaMemcpyDeviceToHost,
+                             c.stream);
+    if (rc == P2CU_OK && ce == cudaSuccess) rc = p2cu_check_device(c.stream);
+    if (rc != P2CU_OK || ce != cudaSuccess) {
+        fprintf(stderr, "p2_mel_spectrogram: %s\n", ce != cudaSuccess ? cudaGetErrorString(ce) : p2cu_last_error());
+        free(res);
+        return -1;
+    }
+    *out_mel = res;
+    *out_frames = nf;
+    return 0;
 }
 
 __attribute__((visibility("default"))) int p2_greedy_decode(const P2Model* m, const float* enc_out, int T,
@@ -629,7 +814,7 @@ void p2b_release_encoder_models(void) {
     for (int d = 0; d < 64; ++d) {
         DeviceSlot& slot = g_slots[d];
         std::lock_guard<std::mutex> lock(slot.mu);
-        if (slot.plans.empty() && !slot.dec) continue;
+        if (slot.plans.empty() && !slot.dec && !slot.mel) continue;
         cudaSetDevice(d);
         for (auto& c : slot.plans) p2cu_encoder_destroy(c.plan);
         slot.plans.clear();
@@ -637,6 +822,7 @@ void p2b_release_encoder_models(void) {
         slot.dec = nullptr;
         slot.dec_model = nullptr;
         slot.dec_windows = slot.dec_frames = 0;
+        slot.drop_mel();
     }
     std::lock_guard<std::mutex> lock(g_mu);
     int prev = 0;

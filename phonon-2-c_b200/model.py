@@ -222,6 +222,18 @@ def mel(n_frames: int, seed: int) -> np.ndarray:
     return np.random.default_rng(seed).standard_normal((n_frames, NMEL), dtype=np.float32)
 
 
+def audio(n_samples: int, seed: int) -> np.ndarray:
+    """Synthetic 16 kHz audio [n_samples]: a few gliding harmonics with a syllable-rate envelope over low noise,
+    seeded (speech-like spectra for the log-mel front end; no dataset is involved)."""
+    rng = np.random.default_rng(seed)
+    t = np.arange(n_samples) / 16000.0
+    f0 = 110.0 + 60.0 * np.sin(2 * np.pi * 0.7 * t + rng.uniform(0, 6.3))
+    phase = 2 * np.pi * np.cumsum(f0) / 16000.0
+    x = sum((0.3 / k) * np.sin(k * phase + rng.uniform(0, 6.3)) for k in range(1, 9))
+    env = 0.5 + 0.5 * np.sin(2 * np.pi * 4.0 * t + rng.uniform(0, 6.3))
+    return (x * env + 0.01 * rng.standard_normal(n_samples)).astype(np.float32)
+
+
 def long_audio_windows(seed: int = 0, n: int = 64, lo_s: float = 25.0, hi_s: float = 35.0) -> list[int]:
     """Mel frame counts of the long-audio batch: n windows of U(lo_s, hi_s) seconds of a
     synthetic stream, 100 mel frames per second."""
