@@ -1,0 +1,65 @@
+"""The drop-in, end to end: phonon-2-c's own command-line program (csrc/main.c over engine.c, segment.c, wav.c, ...)
+built twice by oracle/Makefile - on the reference's own sources (_ref/phonon2_cpu), and without blas.c, encoder.c,
+decoder.c and mel.c, linked against libphonon2_b200.so (_ref/phonon2_b200) - transcribes the same WAV files with the
+same synthetic model directory (oracle/weights_file.py). In exact mode (P2_GEMM=exact) the token ids must be identical:
+the engine's segmentation into windows, its dropout check and re-decodes, and the detokeniser run in the reference's C
+either way, while log-mel, encoder and decoder run on the GPU in the second program.
+"""
+import os
+import subprocess
+import time
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+ROOT = Path(__file__).resolve().parents[1]
+CPU_BIN = ROOT / "oracle" / "_ref" / "phonon2_cpu"
+B200_BIN = ROOT / "oracle" / "_ref" / "phonon2_b200"
+
+
+@pytest.fixture(scope="module")
+def model_dir(pkg, tmp_path_factory):
+    from oracle import weights_file as wf
+    from phonon2_b200 import model as M
+    d = tmp_path_factory.mktemp("model")
+    wf.write_model_dir(M.SyntheticModel(seed=1), d)
+    return d
+
+
+def _run(binary, model_dir, wav, env_extra):
+    env = dict(os.environ)
+    env.update(env_extra)
+    t = time.perf_counter()
+    r = subprocess.run([str(binary), "--quiet", "--tokens", str(model_dir), str(wav)], capture_output=True, text=True,
+                       env=env, timeout=900)
+    assert r.returncode == 0, r.stderr[-2000:]
+    return r.stdout.split(), time.perf_counter() - t
+
+
+@pytest.mark.skipif(not (CPU_BIN.exists() and B200_BIN.exists()), reason="oracle/_ref programs not built")
+@pytest.mark.parametrize("seconds", [3, 70])
+def test_reference_program_on_library_matches_reference(pkg, cuda, model_dir, tmp_path, seconds):
+    from oracle import weights_file as wf
+    from phonon2_b200 import model as M
+    wav = tmp_path / f"audio{seconds}.wav"
+    wf.write_wav16(wav, M.audio(16000 * seconds, seed=seconds))
+    want, t_cpu = _run(CPU_BIN, model_dir, wav, {})
+    got, t_gpu = _run(B200_BIN, model_dir, wav, {"P2_GEMM": "exact"})
+    print(f"{seconds} s: reference {t_cpu:.1f} s, reference program on the library {t_gpu:.1f} s (exact mode, "
+          f"including start-up and weight upload); {len(want)} tokens")
+    assert got == want
+
+
+@pytest.mark.skipif(not B200_BIN.exists(), reason="oracle/_ref programs not built")
+def test_reference_program_on_library_int8w(pkg, cuda, model_dir, tmp_path):
+    """The default int8w mode through the same program: it runs and yields a transcript (the int8 encoder differs from
+    the exact one by the quantisation, so no token equality is asked)."""
+    from oracle import weights_file as wf
+    from phonon2_b200 import model as M
+    wav = tmp_path / "audio.wav"
+    wf.write_wav16(wav, M.audio(16000 * 40, seed=4))
+    tokens, _ = _run(B200_BIN, model_dir, wav, {"P2_GEMM": "int8w"})
+    assert all(t.isdigit() for t in tokens)
