@@ -210,6 +210,29 @@ P2CU_API int p2cu_mel_frames(long long n_samples);
 P2CU_API int p2cu_mel_run(P2cuMel *plan, const float *audio, const long long *n_samples, int n_windows, float *mel,
                           void *stream);
 
+/* ---- The segmenter's energy measures (csrc/segment.c) --------------------------------------------------------------
+ * p2cu_block_rms: for each window w of device `audio` ([starts[w], starts[w] + lens[w]); host arrays), the RMS of
+ * its blocks of 50 ms aligned to its start, the last one zero-padded (csrc/segment.c:36-48), into `rms` (device), the
+ * windows' ceil(lens[w] / block) values one after another. Asynchronous on `stream`.
+ * The p2cu_seg_* functions are host code: the decisions csrc/segment.c and csrc/engine.c:213-251 take from block RMS
+ * values (`rms`, n_blocks of them, over n_samples samples), restated exactly. */
+P2CU_API int p2cu_block_rms(const float *audio, const long long *starts, const int *lens, int n_windows,
+                            int sample_rate, float *rms, void *stream);
+P2CU_API int p2cu_seg_block(int sample_rate);
+P2CU_API int p2cu_seg_blocks(int n_samples, int sample_rate);
+P2CU_API int p2cu_seg_window_max_samples(int sample_rate);
+/* p2_first_cut (csrc/segment.c:90-118): rms covers the first window-max samples. */
+P2CU_API int p2cu_seg_first_cut(const float *rms, int n_blocks, int n_samples, int sample_rate);
+/* p2_split_point (csrc/segment.c:142-151): rms covers the window. */
+P2CU_API int p2cu_seg_split_point(const float *rms, int n_blocks, int n_samples, int sample_rate);
+P2CU_API float p2cu_seg_speech_gate(const float *rms, int n_blocks);
+P2CU_API float p2cu_seg_speech_share(const float *rms, int n_blocks, int sample_rate, int from, int to, float gate);
+/* Whether a decoded window has a stretch of 2 s or more without a token (no RMS needed), and the full dropout test
+ * of csrc/engine.c:224-251 at 16 kHz (the first quiet stretch's samples and speech share to the optional outputs). */
+P2CU_API int p2cu_seg_long_gap(const P2Token *toks, int n_toks, int n_samples);
+P2CU_API int p2cu_seg_dropped_out(const float *rms, int n_blocks, int n_samples, const P2Token *toks, int n_toks,
+                                  int *gap_from, int *gap_to, float *speech);
+
 /* ---- Measurements of the hardware the kernels are built around (allocate their own buffers; a few launches) ----
  * p2cu_probe_int8_mma: the tcgen05 int8 MMA rate in MACs per second over all SMs, from shared-memory operands, one
  * CTA per SM (pair = 0, M = 128 per MMA) or on CTA pairs (pair != 0, M = 256); iters K = 128 steps per SM.

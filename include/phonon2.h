@@ -42,6 +42,11 @@ extern "C" {
 #define P2_N_DURATIONS  5
 #define P2_N_LOGITS     (P2_VOCAB + P2_N_DURATIONS)
 
+/* Audio front end (csrc/phonon2.h:99-105) */
+#define P2_SAMPLE_RATE  16000
+#define P2_HOP_LEN      160
+#define P2_FRAME_SECONDS ((float)(P2_SUB_FACTOR * P2_HOP_LEN) / (float)P2_SAMPLE_RATE)   /* 0.08 s per encoder frame */
+
 /* A GEMM weight op(B) = [K, N] in one of three storage kinds (csrc/phonon2.h:109-126). */
 typedef enum {
     P2_W_F32 = 0,   /* fp32 [K, N] */
@@ -220,6 +225,38 @@ P2_API int p2_b200_transcribe_audio_windows(const P2Model *m, const float *audio
  * Returns 0, or -1 with a message on stderr. */
 P2_API int p2_b200_transcribe_windows(const P2Model *m, const float *mel, const int *n_frames, int n_windows,
                                       const int *devices, int n_devices, P2Token **tokens, int *n_tokens);
+
+/* ---- Long audio (csrc/segment.c, csrc/engine.c:253-357) ----------------------------------------------------------- */
+
+/* A window of samples [start, end) of long audio (csrc/phonon2.h:359). */
+typedef struct { int start, end; } P2Window;
+
+/* p2_plan_windows (csrc/phonon2.h:360-366) with the block RMS computed on the calling thread's GPU: audio longer than
+ * the maximum window (35 s, or P2_WINDOW_MAX) cut at the longest pause of the 10 s before each maximum. 16 kHz audio
+ * only. Returns the number of windows in the malloc'd *out (freed by the caller), 0 for no audio or on failure. */
+P2_API int p2_b200_plan_windows(const float *audio, int n_samples, int sample_rate, P2Window **out);
+/* p2_split_point (csrc/phonon2.h:367-368) likewise: the middle of the longest pause in the middle third. */
+P2_API int p2_b200_split_point(const float *audio, int n_samples, int sample_rate);
+
+/* One decoded window of p2_b200_transcribe_long. */
+typedef struct {
+    int      start, end;      /* samples [start, end) of the audio given */
+    int      depth;           /* re-decode splits that made it: 0 for a planned window */
+    int      encoder_frames;  /* its encoder frames (80 ms each) */
+    P2Token *tokens;          /* its tokens, frames relative to `start` (malloc'd; NULL when n_tokens is 0) */
+    int      n_tokens;
+} P2B200Window;
+
+/* Long 16 kHz audio as p2_transcribe decodes it (csrc/engine.c:293-357) - pause-aligned windows over 35 s, a window
+ * that went quiet over speech re-decoded as two halves, at most two levels deep; P2_SEGMENT, P2_REDECODE and
+ * P2_WINDOW_MAX keep their meaning - with each split depth's windows decoded as one batch spread over the GPUs
+ * (`devices`, or all GPUs when n_devices is 0). Non-finite samples count as zeros. *out receives the final windows in
+ * the order the reference appends them as segments (by start), freed with p2_b200_windows_free; *encoder_frames (if
+ * not NULL) the encoder frames of every decode, split windows included (P2Result.encoder_frames). Returns 0, or -1
+ * with a message on stderr. */
+P2_API int p2_b200_transcribe_long(const P2Model *m, const float *audio, int n_samples, const int *devices,
+                                   int n_devices, P2B200Window **out, int *n_out, long long *encoder_frames);
+P2_API void p2_b200_windows_free(P2B200Window *windows, int n);
 
 #ifdef __cplusplus
 }

@@ -385,3 +385,160 @@ def cpu_cores() -> int:
         return len(os.sched_getaffinity(0))
     except AttributeError:
         return os.cpu_count() or 1
+
+
+# ---- the segmenter and the engine (csrc/segment.c, csrc/engine.c), for the long-audio scheduling ---------------------
+
+def _seg_ready(L):
+    if hasattr(L, "_seg_ready"):
+        return
+    L.p2_block_rms.argtypes = [C.c_void_p, C.c_int, C.c_int, C.POINTER(C.c_int)]
+    L.p2_block_rms.restype = C.c_void_p
+    L.p2_speech_gate.argtypes = [C.c_void_p, C.c_int]
+    L.p2_speech_gate.restype = C.c_float
+    L.p2_speech_share.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_float]
+    L.p2_speech_share.restype = C.c_float
+    L.p2_first_cut.argtypes = [C.c_void_p, C.c_int, C.c_int]
+    L.p2_first_cut.restype = C.c_int
+    L.p2_split_point.argtypes = [C.c_void_p, C.c_int, C.c_int]
+    L.p2_split_point.restype = C.c_int
+    L.p2_plan_windows.argtypes = [C.c_void_p, C.c_int, C.c_int, C.POINTER(C.c_void_p)]
+    L.p2_plan_windows.restype = C.c_int
+    L._seg_ready = True
+
+
+def ref_block_rms(audio: np.ndarray) -> np.ndarray:
+    """phonon-2-c's p2_block_rms (csrc/segment.c:158-162) on 16 kHz audio: 50 ms block RMS, float32."""
+    L = ref()
+    _seg_ready(L)
+    x = np.ascontiguousarray(audio, np.float32)
+    nb = C.c_int()
+    p = L.p2_block_rms(x.ctypes.data, x.shape[0], 16000, C.byref(nb))
+    if not p:
+        return np.zeros(0, np.float32)
+    try:
+        return np.ctypeslib.as_array(C.cast(p, C.POINTER(C.c_float)), shape=(nb.value,)).copy()
+    finally:
+        _libc.free(p)
+
+
+def ref_speech_gate(rms: np.ndarray) -> float:
+    """p2_speech_gate (csrc/segment.c:164-177)."""
+    L = ref()
+    _seg_ready(L)
+    r = np.ascontiguousarray(rms, np.float32)
+    return float(L.p2_speech_gate(r.ctypes.data, r.shape[0]))
+
+
+def ref_speech_share(rms: np.ndarray, frm: int, to: int, gate: float) -> float:
+    """p2_speech_share (csrc/segment.c:179-184) at 16 kHz."""
+    L = ref()
+    _seg_ready(L)
+    r = np.ascontiguousarray(rms, np.float32)
+    return float(L.p2_speech_share(r.ctypes.data, r.shape[0], 16000, frm, to, gate))
+
+
+def ref_first_cut(audio: np.ndarray) -> int:
+    """p2_first_cut (csrc/segment.c:90-118) at 16 kHz."""
+    L = ref()
+    _seg_ready(L)
+    x = np.ascontiguousarray(audio, np.float32)
+    return int(L.p2_first_cut(x.ctypes.data, x.shape[0], 16000))
+
+
+def ref_split_point(audio: np.ndarray) -> int:
+    """p2_split_point (csrc/segment.c:142-151) at 16 kHz."""
+    L = ref()
+    _seg_ready(L)
+    x = np.ascontiguousarray(audio, np.float32)
+    return int(L.p2_split_point(x.ctypes.data, x.shape[0], 16000))
+
+
+def ref_plan_windows(audio: np.ndarray) -> list[tuple[int, int]]:
+    """p2_plan_windows (csrc/segment.c:120-140) at 16 kHz: [(start, end), ...]."""
+    L = ref()
+    _seg_ready(L)
+    x = np.ascontiguousarray(audio, np.float32)
+    out = C.c_void_p()
+    n = L.p2_plan_windows(x.ctypes.data, x.shape[0], 16000, C.byref(out))
+    if n <= 0:
+        return []
+    try:
+        w = np.ctypeslib.as_array(C.cast(out, C.POINTER(C.c_int)), shape=(n, 2)).copy()
+    finally:
+        _libc.free(out)
+    return [(int(a), int(b)) for a, b in w]
+
+
+def ref_dropped_out(audio: np.ndarray, tokens: np.ndarray):
+    """The engine's dropout test (csrc/engine.c:224-251; a static function there, restated here over the reference's
+    own p2_block_rms / p2_speech_gate / p2_speech_share): (gap_from, gap_to, speech share) of the first stretch of
+    2 s or more without a token whose speech share lies in [0.40, 0.90], or None. tokens: int [k, 3] (id, frame,
+    duration) with frames relative to the window's start."""
+    frame, min_gap, n = 160 * 8, 32000, int(audio.shape[0])
+    rms, gate, prev = None, 0.0, 0
+    for i in range(len(tokens) + 1):
+        cur = int(tokens[i][1]) * frame if i < len(tokens) else n
+        cur = min(cur, n)
+        if cur - prev >= min_gap:
+            if rms is None:
+                rms = ref_block_rms(audio)
+                if rms.shape[0] == 0:
+                    return None
+                gate = ref_speech_gate(rms)
+            s = ref_speech_share(rms, prev, cur, gate)
+            if np.float32(0.40) <= np.float32(s) <= np.float32(0.90):
+                return prev, cur, s
+        if i < len(tokens):
+            d = int(tokens[i][2])
+            prev = cur + (d if d > 0 else 1) * frame
+    return None
+
+
+class _P2Token(C.Structure):
+    _fields_ = [("id", C.c_int), ("frame", C.c_int), ("duration", C.c_int)]
+
+
+class _P2Segment(C.Structure):   # csrc/phonon2.h:249-257
+    _fields_ = [("start", C.c_float), ("end", C.c_float), ("text", C.c_char_p), ("first_word", C.c_int),
+                ("n_words", C.c_int), ("first_token", C.c_int), ("n_tokens", C.c_int)]
+
+
+class _P2Result(C.Structure):   # csrc/phonon2.h:259-270
+    _fields_ = [("text", C.c_char_p), ("words", C.c_void_p), ("n_words", C.c_int),
+                ("tokens", C.POINTER(_P2Token)), ("n_tokens", C.c_int), ("segments", C.POINTER(_P2Segment)),
+                ("n_segments", C.c_int), ("encoder_frames", C.c_int), ("duration_seconds", C.c_float),
+                ("t_mel", C.c_double), ("t_encoder", C.c_double), ("t_decoder", C.c_double)]
+
+
+def ref_transcribe(model_dir, audio: np.ndarray, sample_rate: int = 16000) -> dict:
+    """phonon-2-c's engine end to end (p2_engine_open on a model directory, p2_transcribe; csrc/engine.c:293-357):
+    {"tokens": int [k, 3] (id, frame in the whole audio, duration), "segments": [(start_s, end_s, first_token,
+    n_tokens), ...], "encoder_frames": int}. The GEMM mode follows P2_GEMM (exact on x86)."""
+    L = ref()
+    if not hasattr(L, "_engine_ready"):
+        L.p2_engine_open.argtypes = [C.c_char_p]
+        L.p2_engine_open.restype = C.c_void_p
+        L.p2_engine_close.argtypes = [C.c_void_p]
+        L.p2_transcribe.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.POINTER(_P2Result)]
+        L.p2_transcribe.restype = C.c_int
+        L.p2_result_free.argtypes = [C.POINTER(_P2Result)]
+        L._engine_ready = True
+    C.c_int.in_dll(L, "p2_verbose").value = 0
+    e = L.p2_engine_open(str(model_dir).encode())
+    if not e:
+        raise RuntimeError(f"p2_engine_open({model_dir}) failed")
+    x = np.ascontiguousarray(audio, np.float32)
+    r = _P2Result()
+    try:
+        if L.p2_transcribe(e, x.ctypes.data, x.shape[0], sample_rate, C.byref(r)) != 0:
+            raise RuntimeError("reference p2_transcribe failed")
+        toks = np.array([(r.tokens[i].id, r.tokens[i].frame, r.tokens[i].duration) for i in range(r.n_tokens)],
+                        np.int32).reshape(-1, 3)
+        segs = [(r.segments[i].start, r.segments[i].end, r.segments[i].first_token, r.segments[i].n_tokens)
+                for i in range(r.n_segments)]
+        out = {"tokens": toks, "segments": segs, "encoder_frames": int(r.encoder_frames)}
+        L.p2_result_free(C.byref(r))
+        return out
+    finally:
+        L.p2_engine_close(e)

@@ -79,6 +79,28 @@ def write_model_dir(model, directory) -> Path:
     return d
 
 
+def as_loaded(model):
+    """`model` (a SyntheticModel) with its decoder tables replaced, in place, by what the reference's loader makes of
+    them from a directory written by write_model_dir: the int8 rows expanded as (float)q * scale
+    (csrc/weights.c:335-364). Returns the model."""
+    d = model.struct.dec
+    fields = {"decoder.embedding.weight": ("embed_w", None), "decoder.decoder_projector.weight": ("proj_w", None),
+              "joint.head.weight": ("head_w", None)}
+    for l in range(2):
+        fields[f"decoder.lstm.weight_ih_l{l}"] = ("lstm_w_ih", l)
+        fields[f"decoder.lstm.weight_hh_l{l}"] = ("lstm_w_hh", l)
+    for name, (field, idx) in fields.items():
+        a = model.arrays[name]
+        q, scale = _rows_int8(a.reshape(a.shape[0], -1).astype(np.float32))
+        w = np.ascontiguousarray((q.astype(np.float32) * scale[:, None]).astype(np.float32).reshape(a.shape))
+        addr = model._keep(name, w)
+        if idx is None:
+            setattr(d, field, addr)
+        else:
+            getattr(d, field)[idx] = addr
+    return model
+
+
 def write_wav16(path, audio: np.ndarray, rate: int = 16000) -> None:
     """Mono 16-bit PCM WAV of float audio in [-1, 1]."""
     import wave

@@ -91,6 +91,16 @@ SIGNATURES = {
     "p2cu_mel_destroy": (None, [_vp]),
     "p2cu_mel_frames": (_i, [C.c_longlong]),
     "p2cu_mel_run": (_i, [_vp, _vp, C.POINTER(C.c_longlong), _i, _vp, _vp]),
+    "p2cu_block_rms": (_i, [_vp, C.POINTER(C.c_longlong), C.POINTER(_i), _i, _i, _vp, _vp]),
+    "p2cu_seg_block": (_i, [_i]),
+    "p2cu_seg_blocks": (_i, [_i, _i]),
+    "p2cu_seg_window_max_samples": (_i, [_i]),
+    "p2cu_seg_first_cut": (_i, [_vp, _i, _i, _i]),
+    "p2cu_seg_split_point": (_i, [_vp, _i, _i, _i]),
+    "p2cu_seg_speech_gate": (_f, [_vp, _i]),
+    "p2cu_seg_speech_share": (_f, [_vp, _i, _i, _i, _i, _f]),
+    "p2cu_seg_long_gap": (_i, [_vp, _i, _i]),
+    "p2cu_seg_dropped_out": (_i, [_vp, _i, _i, _vp, _i, C.POINTER(_i), C.POINTER(_i), C.POINTER(_f)]),
     "p2cu_probe_int8_mma": (_i, [_i, _i, C.POINTER(C.c_double)]),
     "p2cu_probe_tma_load": (_i, [_i, _i, C.POINTER(C.c_double)]),
     # include/phonon2.h: the reference's encoder and decoder entry points
@@ -105,6 +115,11 @@ SIGNATURES = {
     "p2_mel_spectrogram": (_i, [_vp, _i, C.POINTER(_vp), C.POINTER(_i)]),
     "p2_b200_transcribe_audio_windows": (_i, [_vp, _vp, C.POINTER(C.c_longlong), _i, C.POINTER(_i), _i,
                                               C.POINTER(_vp), C.POINTER(_i)]),
+    "p2_b200_plan_windows": (_i, [_vp, _i, _i, C.POINTER(_vp)]),
+    "p2_b200_split_point": (_i, [_vp, _i, _i]),
+    "p2_b200_transcribe_long": (_i, [_vp, _vp, _i, C.POINTER(_i), _i, C.POINTER(_vp), C.POINTER(_i),
+                                     C.POINTER(C.c_longlong)]),
+    "p2_b200_windows_free": (None, [_vp, _i]),
     # include/blas.h: the reference's host-pointer ABI
     "p2_sgemm": (None, [_i, _i, _i, _i, _i, _f, _vp, _i, _vp, _i, _f, _vp, _i]),
     "p2_sgemm_st": (None, [_i, _i, _i, _i, _i, _f, _vp, _i, _vp, _i, _f, _vp, _i]),
@@ -511,3 +526,53 @@ def host_transcribe_audio_windows(model_struct, audios, devices=None):
         if toks[i]:
             libc.free(C.c_void_p(toks[i]))
     return res
+
+
+# ---- long audio: the segmenter's decisions and the batched re-decode scheduling ----------------------------------------
+
+class P2B200Window(C.Structure):   # include/phonon2.h
+    _fields_ = [("start", C.c_int), ("end", C.c_int), ("depth", C.c_int), ("encoder_frames", C.c_int),
+                ("tokens", C.c_void_p), ("n_tokens", C.c_int)]
+
+
+def host_plan_windows(audio):
+    """p2_b200_plan_windows on 16 kHz float32 audio: a list of (start, end) sample pairs."""
+    import numpy as _np
+    x = _np.ascontiguousarray(audio, dtype=_np.float32)
+    out = C.c_void_p()
+    n = lib().p2_b200_plan_windows(x.ctypes.data, int(x.shape[0]), 16000, C.byref(out))
+    if n <= 0:
+        return []
+    w = _np.ctypeslib.as_array(C.cast(out, C.POINTER(C.c_int)), shape=(n, 2)).copy()
+    C.CDLL(None).free(out)
+    return [(int(a), int(b)) for a, b in w]
+
+
+def host_split_point(audio) -> int:
+    """p2_b200_split_point on 16 kHz float32 audio."""
+    import numpy as _np
+    x = _np.ascontiguousarray(audio, dtype=_np.float32)
+    return int(lib().p2_b200_split_point(x.ctypes.data, int(x.shape[0]), 16000))
+
+
+def host_transcribe_long(model_struct, audio, devices=None):
+    """p2_b200_transcribe_long: 16 kHz audio -> (list of dicts with start, end, depth, encoder_frames and int32 [k, 3]
+    tokens (frames relative to the window's start), in the reference's segment order; total encoder frames)."""
+    import numpy as _np
+    x = _np.ascontiguousarray(audio, dtype=_np.float32)
+    devs = None if not devices else (C.c_int * len(devices))(*devices)
+    out = C.c_void_p()
+    n = C.c_int()
+    frames = C.c_longlong()
+    rc = lib().p2_b200_transcribe_long(C.addressof(model_struct), x.ctypes.data, int(x.shape[0]), devs,
+                                       len(devices) if devices else 0, C.byref(out), C.byref(n), C.byref(frames))
+    if rc != 0:
+        raise Error(rc, "p2_b200_transcribe_long failed (see stderr)")
+    res = []
+    if n.value > 0:
+        arr = C.cast(out, C.POINTER(P2B200Window * n.value)).contents
+        for w in arr:
+            res.append({"start": w.start, "end": w.end, "depth": w.depth, "encoder_frames": w.encoder_frames,
+                        "tokens": _tokens_array(w.tokens, w.n_tokens)})
+    lib().p2_b200_windows_free(out, n.value)
+    return res, frames.value

@@ -411,18 +411,18 @@ FeedEncoder feed_host_mel(const float* mel, const int* n_frames, int n_windows) 
     };
 }
 
-// FeedEncoder from host audio ([sum n_samples] at 16 kHz): the windows' samples go up, the log-mel front end writes the
-// plan's input on the device.
-FeedEncoder feed_host_audio(const float* audio, const long long* n_samples, int n_windows) {
-    auto off = std::make_shared<std::vector<long long>>(n_windows + 1, 0);
-    for (int w = 0; w < n_windows; ++w) (*off)[w + 1] = (*off)[w] + n_samples[w];
-    return [audio, n_samples, off](P2cuEncoder* e, cudaStream_t s, DeviceSlot& slot, const std::vector<int>& wins,
-                                   std::string* err) {
+// FeedEncoder from windows that are slices of host audio (16 kHz): window w is audio[starts[w], starts[w] + n[w]).
+// The windows' samples go up, the log-mel front end writes the plan's input on the device.
+FeedEncoder feed_host_slices(const float* audio, std::vector<long long> starts, std::vector<long long> n_samples) {
+    auto st = std::make_shared<std::vector<long long>>(std::move(starts));
+    auto ns_all = std::make_shared<std::vector<long long>>(std::move(n_samples));
+    return [audio, st, ns_all](P2cuEncoder* e, cudaStream_t s, DeviceSlot& slot, const std::vector<int>& wins,
+                               std::string* err) {
         long long total = 0;
         std::vector<long long> ns;
         for (int w : wins) {
-            ns.push_back(n_samples[w]);
-            total += n_samples[w];
+            ns.push_back((*ns_all)[w]);
+            total += (*ns_all)[w];
         }
         P2cuMel* mp = slot.mel_for(static_cast<int>(wins.size()), total);
         if (!mp) {
@@ -431,14 +431,14 @@ FeedEncoder feed_host_audio(const float* audio, const long long* n_samples, int 
         }
         long long at = 0;
         for (int w : wins) {
-            const cudaError_t ce = cudaMemcpyAsync(slot.audio + at, audio + (*off)[w],
-                                                   static_cast<size_t>(n_samples[w]) * sizeof(float),
+            const cudaError_t ce = cudaMemcpyAsync(slot.audio + at, audio + (*st)[w],
+                                                   static_cast<size_t>((*ns_all)[w]) * sizeof(float),
                                                    cudaMemcpyHostToDevice, s);
             if (ce != cudaSuccess) {
                 *err = cudaGetErrorString(ce);
                 return -1;
             }
-            at += n_samples[w];
+            at += (*ns_all)[w];
         }
         if (p2cu_mel_run(mp, slot.audio, ns.data(), static_cast<int>(wins.size()), p2cu_encoder_mel(e), s) !=
             P2CU_OK) {
@@ -447,6 +447,13 @@ FeedEncoder feed_host_audio(const float* audio, const long long* n_samples, int 
         }
         return 0;
     };
+}
+
+// FeedEncoder from host audio ([sum n_samples] at 16 kHz, the windows one after another).
+FeedEncoder feed_host_audio(const float* audio, const long long* n_samples, int n_windows) {
+    std::vector<long long> starts(n_windows, 0), ns(n_samples, n_samples + n_windows);
+    for (int w = 1; w < n_windows; ++w) starts[w] = starts[w - 1] + n_samples[w - 1];
+    return feed_host_slices(audio, std::move(starts), std::move(ns));
 }
 
 // The window checks, the sharding over GPUs and one host thread per GPU, shared by the batched entry points: `after`
@@ -545,13 +552,15 @@ __attribute__((visibility("default"))) int p2_b200_encode_windows(const P2Model*
 namespace {
 
 // AfterEncode that decodes each plan's output on the device and hands every window's tokens to the caller (malloc'd
-// arrays in tokens[w], counts in n_tokens[w]).
-AfterEncode decode_after(P2Token** tokens, int* n_tokens) {
-    return [tokens, n_tokens](P2cuEncoder* e, cudaStream_t s, DeviceSlot& slot, const P2cuModel* dm,
-                              const std::vector<int>& wins, std::string* err) {
+// arrays in tokens[w], counts in n_tokens[w], and the window's encoder frames in enc_frames[w] when it is given).
+AfterEncode decode_after(P2Token** tokens, int* n_tokens, int* enc_frames) {
+    return [tokens, n_tokens, enc_frames](P2cuEncoder* e, cudaStream_t s, DeviceSlot& slot, const P2cuModel* dm,
+                                          const std::vector<int>& wins, std::string* err) {
         const int nw = static_cast<int>(wins.size());
         std::vector<int> T(nw);
         for (int i = 0; i < nw; ++i) T[i] = p2cu_encoder_frames(e, i);
+        if (enc_frames)
+            for (int i = 0; i < nw; ++i) enc_frames[wins[i]] = T[i];
         // one decoder launch per group of at most kDecodeWindows windows
         constexpr int kDecodeWindows = 512;
         const float* enc = p2cu_encoder_out(e);
@@ -589,7 +598,7 @@ AfterEncode decode_after(P2Token** tokens, int* n_tokens) {
 
 // The shared part of the transcribe entry points: checks, token arrays reset, run, arrays freed on failure.
 int transcribe(const char* who, const P2Model* m, const int* n_frames, int n_windows, const int* devices,
-               int n_devices, const FeedEncoder& feed, P2Token** tokens, int* n_tokens) {
+               int n_devices, const FeedEncoder& feed, P2Token** tokens, int* n_tokens, int* enc_frames = nullptr) {
     if (!m->dec.embed_w) {
         fprintf(stderr, "%s: the model has no decoder tables\n", who);
         return -1;
@@ -598,7 +607,8 @@ int transcribe(const char* who, const P2Model* m, const int* n_frames, int n_win
         tokens[w] = nullptr;
         n_tokens[w] = 0;
     }
-    const int rc = run_windows(who, m, n_frames, n_windows, devices, n_devices, feed, decode_after(tokens, n_tokens));
+    const int rc = run_windows(who, m, n_frames, n_windows, devices, n_devices, feed,
+                               decode_after(tokens, n_tokens, enc_frames));
     if (rc != 0)
         for (int w = 0; w < n_windows; ++w) {
             free(tokens[w]);
@@ -646,6 +656,20 @@ __attribute__((visibility("default"))) int p2_b200_transcribe_audio_windows(cons
     }
     return transcribe("p2_b200_transcribe_audio_windows", m, frames.data(), n_windows, devices, n_devices,
                       feed_host_audio(audio, n_samples, n_windows), tokens, n_tokens);
+}
+
+// For long_audio.cu (not exported): windows that are slices of one host audio buffer, window w being
+// audio[starts[w], starts[w] + n_samples[w]) with at least 1280 samples; tokens and counts as
+// p2_b200_transcribe_audio_windows, each window's encoder frames in enc_frames[w].
+int p2b_transcribe_slices(const P2Model* m, const float* audio, const long long* starts, const long long* n_samples,
+                          int n_windows, const int* devices, int n_devices, P2Token** tokens, int* n_tokens,
+                          int* enc_frames) {
+    std::vector<int> frames(n_windows);
+    for (int w = 0; w < n_windows; ++w) frames[w] = p2cu_mel_frames(n_samples[w]);
+    return transcribe("p2_b200_transcribe_long", m, frames.data(), n_windows, devices, n_devices,
+                      feed_host_slices(audio, std::vector<long long>(starts, starts + n_windows),
+                                       std::vector<long long>(n_samples, n_samples + n_windows)),
+                      tokens, n_tokens, enc_frames);
 }
 
 __attribute__((visibility("default"))) int p2_mel_spectrogram(const float* audio, int n_samples, float** out_mel,

@@ -234,6 +234,20 @@ def audio(n_samples: int, seed: int) -> np.ndarray:
     return (x * env + 0.01 * rng.standard_normal(n_samples)).astype(np.float32)
 
 
+def audio_with_pauses(seconds: float, seed: int, pause_lo: float = 0.05, pause_hi: float = 1.4) -> np.ndarray:
+    """Synthetic long-form 16 kHz audio: bursts of audio() (1-6 s each, random level) separated by pauses of low noise
+    (pause_lo-pause_hi s), seeded - material for the segmenter, which cuts at pauses."""
+    rng = np.random.default_rng(seed)
+    parts, n, total = [], 0, int(seconds * 16000)
+    while n < total:
+        k = int(rng.uniform(1.0, 6.0) * 16000)
+        parts.append(audio(k, int(rng.integers(1 << 30))) * np.float32(rng.uniform(0.2, 1.0)))
+        p = int(rng.uniform(pause_lo, pause_hi) * 16000)
+        parts.append((rng.standard_normal(p) * rng.uniform(0.0002, 0.002)).astype(np.float32))
+        n += k + p
+    return np.concatenate(parts)[:total].astype(np.float32)
+
+
 def long_audio_windows(seed: int = 0, n: int = 64, lo_s: float = 25.0, hi_s: float = 35.0) -> list[int]:
     """Mel frame counts of the long-audio batch: n windows of U(lo_s, hi_s) seconds of a
     synthetic stream, 100 mel frames per second."""
