@@ -238,6 +238,12 @@ struct P2cuEncoder {
     cudaStream_t stream = nullptr;
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t exec = nullptr;
+    // A lazy plan runs its first pass eagerly on the caller's stream and is captured into a graph on its second run:
+    // window sets that are seen once (each split depth of long audio, each length of the reference engine's
+    // window-by-window calls) then cost one pass instead of an eager check pass, a capture and the run.
+    bool lazy = false;
+    bool capture_failed = false;
+    int eager_runs = 0;
 };
 
 namespace {
@@ -443,7 +449,7 @@ void destroy_plan(P2cuEncoder* e) {
 size_t al256(size_t x) { return (x + 255) & ~size_t(255); }
 
 int create_plan(const P2cuModel* m, const int* n_frames, int n_mel_win, int mode, int chunk, int overlap,
-                P2cuEncoder** out) {
+                P2cuEncoder** out, bool lazy) {
     if (!m || !n_frames || !out || n_mel_win <= 0) return fail_fmt(P2CU_EINVAL, "p2cu_encoder_create: bad arguments");
     if (chunk > 0 && overlap < 0) return fail_fmt(P2CU_EINVAL, "p2cu_encoder_create: overlap %d", overlap);
     if (mode != P2CU_INT8 && mode != P2CU_INT8W && mode != P2CU_EXACT)
@@ -698,6 +704,16 @@ int create_plan(const P2cuModel* m, const int* n_frames, int n_mel_win, int mode
         destroy_plan(e);
         return p2cu::cuda_error(ce, "p2cu_encoder_create: set-up");
     }
+    e->lazy = lazy;
+    if (lazy) {   // the first run is the eager pass; it must see the position table's quantised rows
+        ce = cudaStreamSynchronize(e->stream);
+        if (ce != cudaSuccess) {
+            destroy_plan(e);
+            return p2cu::cuda_error(ce, "p2cu_encoder_create: set-up");
+        }
+        *out = e;
+        return P2CU_OK;
+    }
     // One eager pass (checks every launch and loads every kernel), then the capture.
     int rc = forward(*e, e->stream);
     if (rc == P2CU_OK) rc = p2cu_check_device(e->stream);
@@ -738,7 +754,13 @@ size_t p2cu_model_bytes(const P2cuModel* m) { return m ? m->bytes : 0; }
 
 int p2cu_encoder_create(const P2cuModel* m, const int* n_frames, int n_windows, int mode, int chunk_frames,
                         int chunk_overlap, P2cuEncoder** out) {
-    return create_plan(m, n_frames, n_windows, mode, chunk_frames, chunk_overlap, out);
+    return create_plan(m, n_frames, n_windows, mode, chunk_frames, chunk_overlap, out, false);
+}
+
+// For the library's host entry points (not exported): a lazy plan (see P2cuEncoder::lazy).
+int p2cu_encoder_create_lazy(const P2cuModel* m, const int* n_frames, int n_windows, int mode, int chunk_frames,
+                             int chunk_overlap, P2cuEncoder** out) {
+    return create_plan(m, n_frames, n_windows, mode, chunk_frames, chunk_overlap, out, true);
 }
 
 void p2cu_encoder_destroy(P2cuEncoder* e) { destroy_plan(e); }
@@ -756,7 +778,30 @@ float* p2cu_encoder_out(P2cuEncoder* e) { return e ? e->out : nullptr; }
 int p2cu_encoder_run(P2cuEncoder* e, void* stream) {
     if (!e) return fail_fmt(P2CU_EINVAL, "p2cu_encoder_run: NULL plan");
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    if (!e->exec) return forward(*e, s);
+    const char* eager = getenv("P2CU_ENCODER_EAGER");
+    if (!e->exec && e->lazy && e->eager_runs > 0 && !e->capture_failed && !(eager && eager[0] == '1')) {
+        // second run of a lazy plan: capture it now (recorded on the plan's own stream, launched on the caller's)
+        cudaError_t ce = cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal);
+        if (ce == cudaSuccess) {
+            const int rc = forward(*e, e->stream);
+            ce = cudaStreamEndCapture(e->stream, &e->graph);
+            if (rc == P2CU_OK && ce == cudaSuccess) ce = cudaGraphInstantiate(&e->exec, e->graph, 0);
+            if (rc != P2CU_OK || ce != cudaSuccess) {
+                if (e->graph) cudaGraphDestroy(e->graph);
+                e->graph = nullptr;
+                e->exec = nullptr;
+                e->capture_failed = true;
+                cudaGetLastError();
+            }
+        } else {
+            e->capture_failed = true;
+            cudaGetLastError();
+        }
+    }
+    if (!e->exec) {
+        ++e->eager_runs;
+        return forward(*e, s);
+    }
     cudaError_t ce = cudaGraphLaunch(e->exec, s);
     return ce == cudaSuccess ? P2CU_OK : p2cu::cuda_error(ce, "p2cu_encoder_run");
 }

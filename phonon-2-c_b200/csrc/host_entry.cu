@@ -26,6 +26,8 @@
 extern "C" {
 int p2b_gemm_mode(void);       // blas_host.c
 int p2b_thread_device(void);   // blas_host.c
+int p2cu_encoder_create_lazy(const P2cuModel* m, const int* n_frames, int n_windows, int mode, int chunk_frames,
+                             int chunk_overlap, P2cuEncoder** out);   // encoder.cu
 }
 
 extern "C" {
@@ -183,7 +185,7 @@ int encode(const P2Model* m, const float* mel, int n_frames, bool force_chunk, f
         c.plan_overlap != overlap) {
         if (c.plan) p2cu_encoder_destroy(c.plan);
         c.plan = nullptr;
-        if (p2cu_encoder_create(dm, &n_frames, 1, mode, chunk, overlap, &c.plan) != P2CU_OK) {
+        if (p2cu_encoder_create_lazy(dm, &n_frames, 1, mode, chunk, overlap, &c.plan) != P2CU_OK) {
             fprintf(stderr, "p2_encoder: %s\n", p2cu_last_error());
             c.plan = nullptr;
             return -1;
@@ -317,7 +319,7 @@ struct DeviceSlot {
             if (c.model == dm && c.frames == frames && c.mode == mode && c.chunk == chunk && c.overlap == overlap)
                 return c.plan;
         P2cuEncoder* e = nullptr;
-        if (p2cu_encoder_create(dm, frames.data(), static_cast<int>(frames.size()), mode, chunk, overlap, &e) !=
+        if (p2cu_encoder_create_lazy(dm, frames.data(), static_cast<int>(frames.size()), mode, chunk, overlap, &e) !=
             P2CU_OK)
             return nullptr;
         if (plans.size() >= 2) {
