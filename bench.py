@@ -201,6 +201,7 @@ def cpu_baseline(seconds=12.0):
 def run_reference(args, world, rank):
     if rank != 0:
         return
+    ge.load_package()   # for the synthetic model and inputs (phonon2_b200.model); the library itself is not loaded
     orc = ge.load_oracle()
     if not orc.ref_available():
         print(json.dumps({"impl": "reference", "unavailable": "phonon-2-c library not built (oracle/_ref missing)"}))
@@ -232,6 +233,13 @@ def run_reference(args, world, rank):
                                "cpu_baseline": enc,
                                "e2e": {"value": enc["value"], "unit": "audio-s/s", "h2d_bytes_per_step": 0,
                                        "d2h_bytes_per_step": 0}}
+    if not args.no_decoder:
+        la = long_audio_reference()
+        if la is not None:
+            line["long_audio"] = {"metric": "long-form transcription audio-sec/sec", "value": la["value"],
+                                  "unit": "audio-s/s", "mode": "exact", "cpu_baseline": la,
+                                  "e2e": {"value": la["value"], "unit": "audio-s/s", "h2d_bytes_per_step": 0,
+                                          "d2h_bytes_per_step": 0}}
     print(json.dumps(line))
 
 
@@ -385,6 +393,9 @@ def run_ours(args, world, rank, local):
             line["decoder"] = dec
             line["mel"] = mel
             line["transcribe"] = transcribe_ours(pkg, local)
+        long_line = long_audio_ours(pkg, world, rank, local)
+        if rank == 0:
+            line["long_audio"] = long_line
     if rank == 0:
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline()
@@ -395,6 +406,7 @@ def run_ours(args, world, rank, local):
                 line["mel"]["cpu_baseline"] = mel_reference()
                 for cfg in line["transcribe"]:
                     cfg["cpu_baseline"] = transcribe_reference(cfg["mel_frames"])
+                line["long_audio"]["cpu_baseline"] = long_audio_reference()
         print(json.dumps(line))
 
 
@@ -693,6 +705,61 @@ def transcribe_reference(n_mel, reps=2):
     return {"value": ms, "unit": "ms", "cores": orc.ref_threads(), "kind": "reference",
             "sample": f"phonon-2-c p2_encoder (exact, AVX2) + p2_greedy_decode, {reps} runs, P2_THREADS = all host "
                       "cores"}
+
+
+LONG_SECONDS = 600.0
+
+
+def long_audio_ours(pkg, world, rank, local, steps=3):
+    """Long-form transcription (SURVEY's engine path): each rank transcribes its own 10-minute recording end to end
+    through p2_b200_transcribe_long - pause-aligned windows, dropout re-decodes scheduled as one batch per split depth,
+    log-mel, encoder and decoder on the device (host audio in, host tokens out). Weak scaling: every rank holds a
+    recording; value = all ranks' audio seconds / the slowest rank's wall time per recording."""
+    from phonon2_b200 import model as M
+    sm = M.SyntheticModel(seed=1)
+    x = M.audio_with_pauses(LONG_SECONDS, 7 + rank)
+    wins, frames = pkg.host_transcribe_long(sm.struct, x, devices=[local])   # weights and plans outside the timing
+    barrier(world)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        wins, frames = pkg.host_transcribe_long(sm.struct, x, devices=[local])
+    ms = (time.perf_counter() - t0) / steps * 1e3
+    barrier(world)
+    ms_max = max_over_ranks(ms, world)
+    depths = {}
+    for w in wins:
+        depths[str(w["depth"])] = depths.get(str(w["depth"]), 0) + 1
+    n_tok = sum(len(w["tokens"]) for w in wins)
+    return {"metric": "long-form transcription audio-sec/sec", "value": world * LONG_SECONDS / (ms_max / 1e3),
+            "unit": "audio-s/s", "ms_per_step": ms_max, "steps": steps, "scaling": "weak",
+            "workload": f"{LONG_SECONDS:.0f} s of synthetic long-form 16 kHz audio per rank (bursts of 1-6 s under a "
+                        "syllable envelope between pauses of 0.05-1.4 s, seeded); the synthetic model leaves most "
+                        "windows without tokens, so nearly every window is re-decoded twice",
+            "windows_by_depth_rank0": depths, "encoder_frames_rank0": frames, "tokens_rank0": n_tok,
+            "h2d_bytes_per_step": 4 * int(x.shape[0]), "d2h_bytes_per_step": 12 * n_tok,
+            "gpu_launches_per_step": "one mel + one encoder pass + one decoder launch per split depth and GPU, one "
+                                     "block-RMS launch per planned window and per split depth",
+            "api": "p2_b200_transcribe_long, wall clock (host audio -> host tokens per window), max over ranks"}
+
+
+def long_audio_reference(seconds=70.0):
+    """phonon-2-c's engine (p2_engine_open + p2_transcribe, exact: its x86 path) on the first `seconds` of the
+    long-form recording, on the host cores."""
+    orc = ge.load_oracle()
+    if not orc.ref_available():
+        return None
+    import tempfile
+    from phonon2_b200 import model as M
+    from oracle import weights_file as wf
+    x = M.audio_with_pauses(LONG_SECONDS, 7)[: int(seconds * 16000)]
+    with tempfile.TemporaryDirectory() as d:
+        wf.write_model_dir(M.SyntheticModel(seed=1), d)
+        t0 = time.perf_counter()
+        orc.ref_transcribe(d, x)
+        dt = time.perf_counter() - t0
+    return {"value": seconds / dt, "unit": "audio-s/s", "cores": orc.ref_threads(), "kind": "reference",
+            "sample": f"phonon-2-c p2_transcribe on the first {seconds:.0f} s of the recording ({dt:.1f} s; its "
+                      "windows and re-decodes one after another), exact mode, P2_THREADS = all host cores"}
 
 
 def run_encoder_only(args, world, rank, local):
