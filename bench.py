@@ -803,6 +803,14 @@ def run_probes(args):
                           "what": "tcgen05 kind::i8 MMAs from shared memory, M=%d N=256 K=32, all SMs" %
                                   (256 if pair else 128)}))
     v = C.c_double()
+    for mode, what in ((0, "issued without hand-back after the first round"),
+                       (1, "each stage handed back by the MMAs' commit, a producer arrive and the odd CTA's relay"),
+                       (2, "each stage handed back by the MMAs' commit and producer arrives, the odd CTA's on the "
+                           "even CTA's barrier")):
+        pkg.check(pkg.lib().p2cu_probe_int8_ring(mode, 4000, C.byref(v)))
+        print(json.dumps({"probe": "int8_mma_ring", "mode": mode, "value": v.value / 1e12, "unit": "TMAC/s",
+                          "what": "CTA-pair MMAs (M=256 N=256 K=128 per step) over a ring of six 32 KB stages, "
+                                  "zero operands, no copies: " + what}))
     for box_rows in (32, 128, 256):
         for warps in (1, 2, 4):
             if 2 * warps * 128 * box_rows > 196608:

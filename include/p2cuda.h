@@ -240,6 +240,10 @@ P2CU_API int p2cu_seg_dropped_out(const float *rms, int n_blocks, int n_samples,
  * rows (8-256) issued by `warps` warps (1-4) of each CTA, two boxes in flight per warp. */
 P2CU_API int p2cu_probe_int8_mma(int pair, int iters, double *macs_per_s);
 P2CU_API int p2cu_probe_tma_load(int warps, int box_rows, double *bytes_per_s_per_sm);
+/* p2cu_probe_int8_ring: the CTA-pair MMA stream (iters K = 128 steps per pair) over a ring of six 32 KB stages handed
+ * back through barriers as in the pair GEMM, without copies: mode 0 no hand-back after the first round, mode 1
+ * through a producer arrive and the odd CTA's relay, mode 2 with the odd CTA arriving on the even CTA's barrier. */
+P2CU_API int p2cu_probe_int8_ring(int mode, int iters, double *macs_per_s);
 
 #ifdef __cplusplus
 }

@@ -327,6 +327,12 @@ fv_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 if (G::ST) cc2[nl] = c2;   // in the int8w mode the expanders keep their clo table there
             }
         }
+        if (grp == 0 && !partial && !p.beta_zero) {   // C_old into L2 meanwhile: its TMA load after the wait hits L2
+            for (int i = rloc; i < BM * G::CHUNKS; i += 128) {
+                const int r = m0 + i / G::CHUNKS, c = n0 + 32 * (i % G::CHUNKS);
+                if (r < p.M && c < p.N) prefetch_l2(p.C + static_cast<size_t>(r) * p.ldc + c);
+            }
+        }
         griddep_wait();   // a_scales, C_old and C belong to the previous kernels until here
         const float as = live ? __fmul_rn(p.a_scales[row], p.alpha) : 0.f;
         named_barrier_sync(1, NEPI);   // constants visible; the expanders are done with the stage buffers

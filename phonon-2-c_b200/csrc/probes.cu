@@ -3,7 +3,13 @@
 //     instruction, one CTA per SM; or M = 256 on CTA pairs), i.e. the measured int8 dense peak;
 //   * p2cu_probe_tma_load: tiled TMA load throughput per SM from an L2-resident int8 matrix, with the loads issued
 //     by 1-4 warps of a CTA - one warp's loads complete one after another, which is why the GEMM kernels spread their
-//     K steps over several producer warps.
+//     K steps over several producer warps;
+//   * p2cu_probe_int8_ring: the CTA-pair MMA stream fed through the stage ring of the pair GEMM kernel without any
+//     copies - six stages of 32 KB per CTA, each released by the MMAs' commit to both CTAs' "empty" barriers and
+//     handed back by a producer thread's arrive, the odd CTA's stages relayed to the even one (mode 1) or arrived
+//     remotely on the even CTA's barrier (mode 2), against the same MMAs issued without waiting (mode 0). The gap is
+//     what the handshake alone costs: the MMAs of a step can start only after the MMAs six steps back have
+//     completed and their release has travelled round the ring.
 // Both allocate their own buffers, run a few launches, and report through out-parameters. Every wait is bounded.
 #include <cstdint>
 #include <cstdio>
@@ -105,6 +111,89 @@ __global__ void __launch_bounds__(PROBE_THREADS, 1) mma_pair_probe_kernel(int it
     if (threadIdx.x < 32) tmem_dealloc_pair(tmem, 256);
 }
 
+constexpr int RING_STAGES = 6;
+constexpr int RING_STAGE_BYTES = 32768;   // 16 KB of A, 16 KB of B per CTA, as a pair GEMM stage
+
+// Clusters of two over a six-stage ring of zero operands: mode 0 issues every step at once (the first round waits
+// like the others), mode 1 hands stages back through the even CTA's producer and the odd CTA's relay, mode 2 has the
+// odd CTA's producer arrive on the even CTA's barrier directly.
+__global__ void __launch_bounds__(PROBE_THREADS, 1) mma_ring_probe_kernel(int iters, int mode, uint32_t* err) {
+    extern __shared__ uint8_t raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + RING_STAGES * RING_STAGE_BYTES);
+    uint64_t* peer = full + RING_STAGES;
+    uint64_t* empty = peer + RING_STAGES;
+    uint64_t* done = empty + RING_STAGES;
+    uint32_t* holder = reinterpret_cast<uint32_t*>(done + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(holder + 1);
+    const uint32_t rank = cluster_ctarank();
+    for (int i = threadIdx.x; i < RING_STAGES * RING_STAGE_BYTES / 16; i += blockDim.x)
+        reinterpret_cast<uint4*>(smem)[i] = make_uint4(0, 0, 0, 0);
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < RING_STAGES; ++s) {
+            mbar_init(&full[s], mode == 2 && rank == 0 ? 2 : 1);
+            mbar_init(&peer[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(done, 1);
+        *abort_flag = 0;
+        fence_barrier_init();
+    }
+    fence_proxy_async_smem();
+    if (threadIdx.x < 32) {
+        tmem_alloc_pair(holder, 256);
+        tmem_relinquish_pair();
+    }
+    tc_fence_before();
+    cluster_sync_all();
+    tc_fence_after();
+    const uint32_t tmem = *holder;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int handed = mode == 0 ? RING_STAGES : iters;   // stages passed through the ring
+    if (warp == 1 && lane == 0) {
+        // producer of this CTA: a stage is refilled (here: handed back) once the pair's MMAs are done with it
+        const uint32_t full0 = cluster_map(&full[0], 0);
+        for (int g = 0; g < handed; ++g) {
+            const int s = g % RING_STAGES, r = g / RING_STAGES;
+            if (g >= RING_STAGES && !mbar_wait(&empty[s], (r & 1) ^ 1, PROBE_TIMEOUT, err, abort_flag)) break;
+            if (mode == 2 && rank == 1) mbar_arrive_remote_relaxed(full0 + static_cast<uint32_t>(s) * 8u);
+            else mbar_arrive(&full[s]);
+        }
+    } else if (warp == 0 && lane == 0 && rank == 1 && mode != 2) {
+        // relay of the odd CTA's stages to the even CTA
+        const uint32_t peer0 = cluster_map(&peer[0], 0);
+        for (int g = 0; g < handed; ++g) {
+            const int s = g % RING_STAGES, r = g / RING_STAGES;
+            if (!mbar_wait(&full[s], r & 1, PROBE_TIMEOUT, err, abort_flag)) break;
+            mbar_arrive_remote_relaxed(peer0 + static_cast<uint32_t>(s) * 8u);
+        }
+    } else if (warp == 0 && lane == 0 && rank == 0) {
+        constexpr uint32_t IDESC = idesc_i8(256, 256, false, true);
+        const uint32_t base = smem_u32(smem);
+        for (int g = 0; g < iters; ++g) {
+            const int s = g % RING_STAGES, r = g / RING_STAGES;
+            if (g < handed) {
+                if (!mbar_wait(&full[s], r & 1, PROBE_TIMEOUT, err, abort_flag)) break;
+                if (mode != 2 && !mbar_wait(&peer[s], r & 1, PROBE_TIMEOUT, err, abort_flag)) break;
+            }
+            tc_fence_after();
+            const uint32_t ab = base + s * RING_STAGE_BYTES, bb = ab + 16384;
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks)
+                mma_i8_pair(tmem, smem_desc(ab + ks * 32, 16, 1024, SWZ_128B),
+                            smem_desc(bb + ks * 4 * 1024, 1024, 1024, SWZ_128B), IDESC, (g > 0 || ks > 0) ? 1u : 0u);
+            mma_commit_pair(&empty[s], 0x3);
+        }
+        mma_commit_pair(done, 0x1);
+        mbar_wait(done, 0, PROBE_TIMEOUT, err, abort_flag);
+    }
+    __syncwarp();
+    tc_fence_before();
+    cluster_sync_all();
+    tc_fence_after();
+    if (threadIdx.x < 32) tmem_dealloc_pair(tmem, 256);
+}
+
 // One CTA per SM: `warps` warps each stream boxes of `box_bytes` (128-byte rows) through a ring of two slots.
 __global__ void __launch_bounds__(PROBE_THREADS, 1)
 tma_probe_kernel(const __grid_constant__ CUtensorMap tm, int boxes, int warps, int box_bytes, int row_blocks,
@@ -191,6 +280,45 @@ int p2cu_probe_int8_mma(int pair, int iters, double* macs_per_s) {
     if (int rc = p2cu_check_device(nullptr)) return rc;
     const double macs = (pair ? 256.0 : 128.0) * 256.0 * 128.0 * iters * (pair ? sms / 2 : sms);
     *macs_per_s = macs / (best * 1e-3);
+    return P2CU_OK;
+}
+
+int p2cu_probe_int8_ring(int mode, int iters, double* macs_per_s) {
+    using namespace p2cu;
+    if (!macs_per_s || mode < 0 || mode > 2 || iters < 1 || iters > (1 << 20))
+        return fail_fmt(P2CU_EINVAL, "p2cu_probe_int8_ring: arguments");
+    const int sms = sms_of_device();
+    const int smem = 1024 + RING_STAGES * RING_STAGE_BYTES + 256;
+    cudaError_t e = cudaFuncSetAttribute(mma_ring_probe_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaEvent_t e0 = nullptr, e1 = nullptr;
+    if (e == cudaSuccess) e = cudaEventCreate(&e0);
+    if (e == cudaSuccess) e = cudaEventCreate(&e1);
+    float best = 0.f;
+    for (int rep = 0; e == cudaSuccess && rep < 3; ++rep) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(sms / 2 * 2);
+        cfg.blockDim = dim3(PROBE_THREADS);
+        cfg.dynamicSmemBytes = smem;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        cudaEventRecord(e0);
+        e = cudaLaunchKernelEx(&cfg, mma_ring_probe_kernel, iters, mode, device_error_word());
+        cudaEventRecord(e1);
+        if (e == cudaSuccess) e = cudaEventSynchronize(e1);
+        float ms = 0.f;
+        if (e == cudaSuccess) cudaEventElapsedTime(&ms, e0, e1);
+        if (rep > 0 && (best == 0.f || ms < best)) best = ms;
+    }
+    if (e0) cudaEventDestroy(e0);
+    if (e1) cudaEventDestroy(e1);
+    if (e != cudaSuccess) return cuda_error(e, "p2cu_probe_int8_ring");
+    if (int rc = p2cu_check_device(nullptr)) return rc;
+    *macs_per_s = 256.0 * 256.0 * 128.0 * iters * (sms / 2) / (best * 1e-3);
     return P2CU_OK;
 }
 

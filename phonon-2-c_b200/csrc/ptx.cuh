@@ -75,6 +75,12 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, uint32
 
 // ---- TMA ---------------------------------------------------------------------------------------------------------
 
+// Prefetch the 128-byte line holding `p` into L2. L2 is where every SM's accesses meet, so a prefetch issued before a
+// dependency wait cannot hand out stale data: a later write by the kernel waited for updates the line there.
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+    asm volatile("prefetch.global.L2 [%0];" :: "l"(p) : "memory");
+}
+
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" :: "l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }

@@ -27,6 +27,10 @@ __device__ __forceinline__ float block_max(float v, float* red) {
 __global__ void __launch_bounds__(QT) quant_rows_kernel(const float* __restrict__ A, int M, int K, int lda,
                                                         int8_t* __restrict__ q, float* __restrict__ scales) {
     griddep_launch_dependents();
+    {   // the row into L2 while the previous kernel finishes (cold rows then cost no DRAM latency after the wait)
+        const char* rb = reinterpret_cast<const char*>(A + static_cast<size_t>(blockIdx.x) * lda);
+        for (int off = threadIdx.x * 128; off < K * 4; off += QT * 128) prefetch_l2(rb + off);
+    }
     griddep_wait();   // A may come from the previous kernel in the stream
     __shared__ float red[QT / 32];
     const int m = blockIdx.x;
