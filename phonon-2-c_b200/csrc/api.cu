@@ -337,10 +337,24 @@ const char* p2cu_last_error(void) { return g_msg; }
 
 int p2cu_check_device(void* stream) {
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    cudaError_t e = cudaStreamSynchronize(s);
-    if (e != cudaSuccess) return cuda_fail(e, "stream");
+    // The error word comes back on the stream itself, into a page-locked word of the calling thread, so that one
+    // synchronisation covers the work and the read (each host thread keeps its word for the process's life).
+    static thread_local uint32_t* word = nullptr;
+    if (!word && cudaMallocHost(&word, sizeof(uint32_t)) != cudaSuccess) {
+        cudaGetLastError();
+        word = nullptr;
+    }
+    cudaError_t e = cudaSuccess;
     uint32_t v = 0, zero = 0;
-    if ((e = cudaMemcpyFromSymbol(&v, g_dev_err, sizeof(v))) != cudaSuccess) return cuda_fail(e, "error word");
+    if (word) {
+        e = cudaMemcpyFromSymbolAsync(word, g_dev_err, sizeof(uint32_t), 0, cudaMemcpyDeviceToHost, s);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+        if (e != cudaSuccess) return cuda_fail(e, "stream");
+        v = *word;
+    } else {
+        if ((e = cudaStreamSynchronize(s)) != cudaSuccess) return cuda_fail(e, "stream");
+        if ((e = cudaMemcpyFromSymbol(&v, g_dev_err, sizeof(v))) != cudaSuccess) return cuda_fail(e, "error word");
+    }
     if (v) {
         cudaMemcpyToSymbol(g_dev_err, &zero, sizeof(zero));
         return fail(P2CU_EDEVICE, "a kernel stopped early and reported device error code %u", v);

@@ -194,18 +194,37 @@ __global__ void __launch_bounds__(NTHREADS, 3) attn_tc_kernel(const TcGroup* __r
         const bool ok = nk > 0 && warp_wait(accfull, 0, DEV_TIMEOUT_ACC, args.err, abort_flag);
         tc_fence_after();
         const int row = m0 + warp * 32 + lane;
+        const bool cvec = (g.ldc & 3) == 0 && (reinterpret_cast<uintptr_t>(C) & 15) == 0;
         if (ok) {
 #pragma unroll 1
             for (int c = 0; c < TN / 32; ++c) {
                 uint32_t v[32];
                 tmem_ld_32x32b_x32(tmem + (static_cast<uint32_t>(warp * 32) << 16) + 32 * c, v);
+                const int n = n0 + 32 * c;
+                float ob[32];
+#pragma unroll
+                for (int j = 0; j < 32; ++j) ob[j] = args.out_bias && n + j < g.N ? __ldg(args.out_bias + n + j) : 0.f;
                 tmem_wait_ld();
                 if (row < g.M) {
-                    float* crow = C + static_cast<size_t>(row) * g.ldc + n0 + 32 * c;
-                    const int nmax = g.N - (n0 + 32 * c);
+                    float x[32];
 #pragma unroll
-                    for (int j = 0; j < 32; ++j)
-                        if (j < nmax) crow[j] = __uint_as_float(v[j]);
+                    for (int j = 0; j < 32; ++j) {
+                        x[j] = __uint_as_float(v[j]);
+                        if (args.out_bias) x[j] = __fadd_rn(x[j], ob[j]);
+                        if (args.out_relu) x[j] = x[j] > 0.f ? x[j] : 0.f;
+                    }
+                    float* crow = C + static_cast<size_t>(row) * g.ldc + n;
+                    const int nmax = g.N - n;
+                    if (cvec && nmax >= 32) {   // the row's 32 columns as eight 16-byte stores
+#pragma unroll
+                        for (int j = 0; j < 8; ++j)
+                            reinterpret_cast<float4*>(crow)[j] = make_float4(x[4 * j], x[4 * j + 1], x[4 * j + 2],
+                                                                             x[4 * j + 3]);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j)
+                            if (j < nmax) crow[j] = x[j];
+                    }
                 }
             }
         }

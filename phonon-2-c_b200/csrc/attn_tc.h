@@ -25,6 +25,8 @@ struct TcArgs {
     const float* bias[2];   // per-K vectors added to A on load
     uint32_t* err;          // device error word for bounded waits
     TcGroup single;
+    const float* out_bias = nullptr;   // per-column vector added to every result (nullptr: none)
+    int out_relu = 0;                  // results below zero become zero (after the bias)
 };
 
 int tc_gemm_tiles(int M, int N);

@@ -273,6 +273,24 @@ int wmatmul_q8a(P2cuEncoder& e, int M, const DWeight& W, float* C, float alpha, 
 #define TRY(x) do { int rc_ = (x); if (rc_ != P2CU_OK) return rc_; } while (0)
 #define TRYC(x, what) do { cudaError_t ce_ = (x); if (ce_ != cudaSuccess) return p2cu::cuda_error(ce_, what); } while (0)
 
+// A 1x1 convolution over channel rows (csrc/encoder.c:192-196, 203-208): out[m] = relu(W in[m] + b), W [256 out][256
+// in], on the tensor cores with the split-tf32 products of the attention (fp32 accuracy; the reference's fp32 FMA
+// chain differs by an ulp or two).
+int conv1x1_tc(const float* in, int rows, const float* w, const float* b, float* out, cudaStream_t s,
+               const char* what) {
+    p2cu::TcArgs a{};
+    a.src[0] = in; a.src[1] = w;
+    a.dst[0] = out; a.dst[1] = out;
+    a.err = p2cu::device_error_word();
+    a.out_bias = b;
+    a.out_relu = 1;
+    p2cu::TcGroup& g = a.single;
+    g.M = rows; g.N = SUBC; g.K = SUBC; g.tile0 = 0;
+    g.a_src = 0; g.b_src = 1; g.c_dst = 0; g.lda = SUBC; g.ldb = SUBC; g.ldc = SUBC; g.bias_sel = -1;
+    TRYC(p2cu::attn_tc_launch(nullptr, 0, p2cu::tc_gemm_tiles(rows, SUBC), a, false, s), what);
+    return P2CU_OK;
+}
+
 // csrc/encoder.c:184-225: three stride-2 convolutions, flatten, linear 4096 -> 1024 + bias.
 int subsampling(P2cuEncoder& e, cudaStream_t s) {
     const P2cuModel& m = *e.m;
@@ -282,16 +300,10 @@ int subsampling(P2cuEncoder& e, cudaStream_t s) {
          "subsampling conv0");
     TRYC(p2cu::sub_dwconv_launch(e.s1, e.d_h1_off, e.d_h2_off, nw, m.c2w, m.c2b, e.s2dw, e.rows2, W1, SUBC, s),
          "subsampling conv2");
-    p2cu::Epilogue br;
-    br.relu = 1;
-    br.bias = m.c3b;
-    TRY(p2cu::gemm_exact(e.rows2 * W2, SUBC, SUBC, 1.f, e.s2dw, SUBC, 0, nullptr, nullptr, nullptr, m.c3w, SUBC, 1,
-                         0.f, e.s2, SUBC, &br, s, "subsampling conv3"));
+    TRY(conv1x1_tc(e.s2dw, e.rows2 * W2, m.c3w, m.c3b, e.s2, s, "subsampling conv3"));
     TRYC(p2cu::sub_dwconv_launch(e.s2, e.d_h2_off, e.d_sub_off, nw, m.c5w, m.c5b, e.s3dw, e.R_sub, W2, SUBC, s),
          "subsampling conv5");
-    br.bias = m.c6b;
-    TRY(p2cu::gemm_exact(e.R_sub * W3, SUBC, SUBC, 1.f, e.s3dw, SUBC, 0, nullptr, nullptr, nullptr, m.c6w, SUBC, 1,
-                         0.f, e.s3, SUBC, &br, s, "subsampling conv6"));
+    TRY(conv1x1_tc(e.s3dw, e.R_sub * W3, m.c6w, m.c6b, e.s3, s, "subsampling conv6"));
     TRYC(p2cu::sub_flatten_launch(e.s3, e.flat, e.R_sub, W3, SUBC, s), "subsampling flatten");
     TRY(wmatmul(e, e.flat, e.R_sub, m.lin, e.x_sub, 1.f, 0.f, nullptr, s, "subsampling linear"));
     TRYC(p2cu::bias_rows_launch(e.x_sub, m.lin_b, e.R_sub, D, s), "subsampling bias");

@@ -54,6 +54,28 @@ def test_strided_host_arrays(pkg, orc, synth, cuda):
     assert _bits_equal(out[:, N:], C_big[:, N:])   # columns beyond N untouched
 
 
+def _pinned(a):
+    """A page-locked copy of a float32 array (torch's pinned allocator), as a numpy view."""
+    import torch
+    t = torch.empty(a.shape, dtype=torch.float32, pin_memory=True)
+    t.numpy()[...] = a
+    return t, t.numpy()
+
+
+def test_page_locked_buffers(pkg, orc, synth, cuda):
+    """Page-locked A and C (as the bench's end-to-end leg passes them), ldc > N with the columns beyond N untouched."""
+    M, K, N = 520, 1024, 512
+    w = synth.five_value(K, N, seed=11)
+    A = synth.activations(M, K, seed=12)
+    C_big = np.random.default_rng(13).standard_normal((M, N + 32)).astype(np.float32)
+    ta, pa = _pinned(A)
+    tc, pc = _pinned(C_big)
+    pkg.host_sgemm_fvb(pa, w, pc[:, :N], beta=1.0)
+    want = orc.sgemm_i8(A, "int8w", np.ascontiguousarray(C_big[:, :N]).copy(), w=w, beta=1.0)
+    assert _bits_equal(np.ascontiguousarray(pc[:, :N]), want)
+    assert _bits_equal(pc[:, N:], C_big[:, N:])
+
+
 def test_quant_prepare_row_gemm(pkg, orc, synth, cuda):
     """p2_quant_prepare / p2_quant_row / p2_sgemm_fvb_q8a as csrc/encoder.c:330-348 drives them."""
     M, K, N = 375, 1024, 2048
