@@ -478,7 +478,8 @@ def encoder_ours(args, world, rank, local, torch, pkg, workload="long-audio", st
     # end to end through the public host API, on this rank's GPU
     e2e_ms = 0.0
     if mine:
-        pkg.host_encode_windows(sm.struct, mels, devices=[local])   # plan creation outside the timed region
+        for _ in range(2):   # plan creation and its graph capture (on a plan's second run) outside the timing
+            pkg.host_encode_windows(sm.struct, mels, devices=[local])
         t0 = time.perf_counter()
         for _ in range(steps):
             pkg.host_encode_windows(sm.struct, mels, devices=[local])
@@ -627,7 +628,8 @@ def mel_ours(args, world, rank, local, torch, pkg, steps=5):
     e2e_ms = 0.0
     n_tok = 0
     if mine:
-        toks = pkg.host_transcribe_audio_windows(sm.struct, audios, devices=[local])   # plans outside the timing
+        for _ in range(2):   # plans and their graph capture (on a plan's second run) outside the timing
+            toks = pkg.host_transcribe_audio_windows(sm.struct, audios, devices=[local])
         n_tok = sum(len(t) for t in toks)
         t0 = time.perf_counter()
         for _ in range(2):
@@ -679,7 +681,8 @@ def transcribe_ours(pkg, local, steps=5):
     out = []
     for name, n in (("window", 3000), ("short", 300)):
         mel = M.mel(n, seed=n)
-        toks = pkg.host_transcribe_windows(sm.struct, [mel], devices=[local])   # plans outside the timed region
+        for _ in range(2):   # plans and their graph capture (on a plan's second run) outside the timing
+            toks = pkg.host_transcribe_windows(sm.struct, [mel], devices=[local])
         t0 = time.perf_counter()
         for _ in range(steps):
             pkg.host_transcribe_windows(sm.struct, [mel], devices=[local])
