@@ -359,6 +359,10 @@ def run_ours(args, world, rank, local):
 
     # End to end: fp32 activations from pinned host memory, results back to pinned host memory, every step.
     e2e = run_e2e(pkg, torch, dev, stream, sets[0], mode, args, 1 + rank * 100)
+    e2e_ms = max_over_ranks(e2e["ms_per_step"], world)   # whole job: every rank's step over the slowest rank's time
+    e2e.update({"value": world * block_macs() / (e2e_ms / 1e3) / 1e12, "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": world * e2e["h2d_bytes_per_step"],
+                "d2h_bytes_per_step": world * e2e["d2h_bytes_per_step"]})
 
     line = None
     if rank == 0:
