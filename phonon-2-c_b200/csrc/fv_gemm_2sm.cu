@@ -16,8 +16,10 @@
 // TMA store (one thread's bulk copies complete in order, so spreading them over eight warps keeps the stores apace);
 // the column constants of a tile are read into shared memory once, C_old straight from global memory.
 // The even CTA's MMA completions are committed to the barriers of both CTAs at once (tcgen05.commit multicast); the
-// odd CTA's epilogue hands each drained accumulator back with a remote mbarrier arrive. No TMA load names another
-// CTA's barrier or uses cluster multicast: each CTA waits for its own copies, also on the way out after a timeout.
+// odd CTA's epilogue hands each drained accumulator back with a remote mbarrier arrive. With an int8 table (the code
+// cache) the odd CTA's TMA loads complete on the even CTA's stage barrier (the cta_group::2 form of the load, no
+// multicast), which expects both CTAs' bytes, so the MMA issuer waits on one barrier per stage and no relay hop lies
+// in the stage's round trip; with planes the odd CTA's expanders finish the stage, and its relay thread announces it.
 // Barriers that the other CTA completes (by a multicast commit or a remote arrive with release semantics at cluster
 // scope) are waited on like local ones, with the CTA-scope try_wait: a cluster-scope acquire there cost about 0.6 us
 // per K step on the critical path, and the operands the MMAs read are ordered by the tensor-core proxy's own commits
@@ -190,14 +192,16 @@ fv_gemm_2sm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
         const int pw = warp - G::PROD;
         if (lane == 0) {
             constexpr uint32_t FULL_TX = PLANES ? G::A_BYTES : G::A_BYTES + G::B_BYTES;
+            // table: both CTAs' copies of a stage complete on the even CTA's barrier, which expects them all
+            const uint32_t full_lead = cluster_map(&full[0], 0);
             auto load_b = [&](int s, int n0, int kx) {
                 if (PLANES) {
                     mbar_arrive_expect_tx(&pfull[s], G::SG_BYTES + G::FL_BYTES);
                     tma_load_2d(sg_tile(s), &tmB0, &pfull[s], (n0 + ncol) / 4, kx);
                     tma_load_2d(fl_tile(s), &tmB1, &pfull[s], (n0 + ncol) / 8, kx);
                 } else {
-                    mbar_arrive_expect_tx(&full[s], FULL_TX);   // the A load of the same stage follows
-                    tma_load_2d(b_tile(s), &tmB0, &full[s], n0 + ncol, kx);
+                    if (lead) mbar_arrive_expect_tx(&full[s], 2 * FULL_TX);   // the A loads of the stage follow
+                    tma_load_2d_pair(b_tile(s), &tmB0, full_lead + static_cast<uint32_t>(s) * 8u, n0 + ncol, kx);
                 }
             };
             // The first stages' weights before the dependency wait (they are constant), then everything else.
@@ -222,12 +226,27 @@ fv_gemm_2sm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                         }
                         load_b(s, d.n0, d.k_begin + kb * QBK);
                     }
-                    if (PLANES) mbar_arrive_expect_tx(&full[s], FULL_TX);
                     QTRACE(80 + g, g < 40);
-                    tma_load_2d(a_tile(s), &tmA, &full[s], d.k_begin + kb * QBK, d.m0 + mrow);
+                    if (PLANES) {
+                        mbar_arrive_expect_tx(&full[s], FULL_TX);
+                        tma_load_2d(a_tile(s), &tmA, &full[s], d.k_begin + kb * QBK, d.m0 + mrow);
+                    } else {
+                        tma_load_2d_pair(a_tile(s), &tmA, full_lead + static_cast<uint32_t>(s) * 8u,
+                                         d.k_begin + kb * QBK, d.m0 + mrow);
+                    }
                 }
             }
-            // No copy this warp issued may still be landing in this CTA's shared memory when it exits.
+            // No copy this warp issued may still be landing in this CTA's shared memory when it exits. With a table
+            // the even CTA's barrier counts both CTAs' copies: the even CTA waits for them, and the odd one, which
+            // cannot observe that barrier, leaves only after the even one (the cluster barrier at the end) and,
+            // after a timeout, after a bounded pause for copies still in flight.
+            if (!PLANES && !lead) {
+                if (*abort_flag) {
+                    const long long t0 = clock64();
+                    while (clock64() - t0 < 20000) {}
+                }
+                g = 0;
+            }
             for (int k = g - STAGES < 0 ? 0 : g - STAGES; k < g; ++k) {
                 if (k % G::NPROD != pw) continue;
                 const int s = k % STAGES, r = k / STAGES;
@@ -256,7 +275,7 @@ fv_gemm_2sm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                             break;
                         }
                         QTRACE(g, g < 40);
-                        if (!mbar_wait(&peer[s], r & 1, DEV_TIMEOUT_READY, p.err, abort_flag)) {
+                        if (PLANES && !mbar_wait(&peer[s], r & 1, DEV_TIMEOUT_READY, p.err, abort_flag)) {
                             ok = false;
                             break;
                         }
@@ -279,8 +298,8 @@ fv_gemm_2sm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                 mbar_wait(drain, 0, DEV_TIMEOUT_DRAIN, p.err, abort_flag);
             }
         } else {
-            // ---------------- relay: each of this CTA's stages, once landed (and expanded), to the even CTA --------
-            if (lane == 0) {
+            // ---------------- relay (planes): each of this CTA's stages, once expanded, to the even CTA --------
+            if (PLANES && lane == 0) {
                 const uint32_t peer0 = cluster_map(&peer[0], 0);
                 int g = 0;
                 bool ok = true;

@@ -85,6 +85,16 @@ __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" :: "l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
+// 2-D tiled load of one box into this CTA's shared memory whose completion is signalled on `bar_cluster`, an mbarrier
+// of either CTA of a CTA pair (a shared::cluster address, e.g. the even CTA's from cluster_map). No multicast.
+__device__ __forceinline__ void tma_load_2d_pair(void* smem_dst, const CUtensorMap* map, uint32_t bar_cluster,
+                                                 int32_t x, int32_t y) {
+    asm volatile("cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+                 " [%0], [%1, {%3, %4}], [%2];"
+                 :: "r"(smem_u32(smem_dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster),
+                    "r"(x), "r"(y) : "memory");
+}
+
 // 2-D tiled load of one box into shared memory, completing `bytes` of transaction on `bar`. No multicast.
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, uint64_t* bar,
                                             int32_t x, int32_t y) {
