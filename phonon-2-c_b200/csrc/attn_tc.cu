@@ -191,10 +191,12 @@ __global__ void __launch_bounds__(NTHREADS, 3) attn_tc_kernel(const TcGroup* __r
 
     if (warp < 4) {
         // ---------------- read-out: TMEM lane = tile row ----------------
+        // Each warp drains its 32 rows 32 columns at a time through a 4 KB block of the (now idle) stage buffers:
+        // thread = row on the way in, then four whole 128-byte rows per store instruction on the way out.
         const bool ok = nk > 0 && warp_wait(accfull, 0, DEV_TIMEOUT_ACC, args.err, abort_flag);
         tc_fence_after();
-        const int row = m0 + warp * 32 + lane;
         const bool cvec = (g.ldc & 3) == 0 && (reinterpret_cast<uintptr_t>(C) & 15) == 0;
+        uint8_t* blk = smem + warp * 4096;   // the MMAs are done with every stage once the accumulator is full
         if (ok) {
 #pragma unroll 1
             for (int c = 0; c < TN / 32; ++c) {
@@ -205,27 +207,38 @@ __global__ void __launch_bounds__(NTHREADS, 3) attn_tc_kernel(const TcGroup* __r
 #pragma unroll
                 for (int j = 0; j < 32; ++j) ob[j] = args.out_bias && n + j < g.N ? __ldg(args.out_bias + n + j) : 0.f;
                 tmem_wait_ld();
-                if (row < g.M) {
-                    float x[32];
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        x[j] = __uint_as_float(v[j]);
-                        if (args.out_bias) x[j] = __fadd_rn(x[j], ob[j]);
-                        if (args.out_relu) x[j] = x[j] > 0.f ? x[j] : 0.f;
+                for (int q = 0; q < 8; ++q) {   // row `lane`, columns 4q .. 4q + 3, at 16-byte slot q ^ (lane % 8)
+                    float x[4];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        x[e] = __uint_as_float(v[4 * q + e]);
+                        if (args.out_bias) x[e] = __fadd_rn(x[e], ob[4 * q + e]);
+                        if (args.out_relu) x[e] = x[e] > 0.f ? x[e] : 0.f;
                     }
-                    float* crow = C + static_cast<size_t>(row) * g.ldc + n;
-                    const int nmax = g.N - n;
-                    if (cvec && nmax >= 32) {   // the row's 32 columns as eight 16-byte stores
+                    *reinterpret_cast<float4*>(blk + lane * 128 + ((q ^ (lane & 7)) << 4)) =
+                        make_float4(x[0], x[1], x[2], x[3]);
+                }
+                __syncwarp();
+                const int q = lane & 7;
 #pragma unroll
-                        for (int j = 0; j < 8; ++j)
-                            reinterpret_cast<float4*>(crow)[j] = make_float4(x[4 * j], x[4 * j + 1], x[4 * j + 2],
-                                                                             x[4 * j + 3]);
-                    } else {
-#pragma unroll
-                        for (int j = 0; j < 32; ++j)
-                            if (j < nmax) crow[j] = x[j];
+                for (int it = 0; it < 8; ++it) {   // rows 4 it .. 4 it + 3, eight lanes per row
+                    const int r = 4 * it + (lane >> 3);
+                    const int row = m0 + warp * 32 + r, col = n + 4 * q;
+                    const float4 y = *reinterpret_cast<const float4*>(blk + r * 128 + ((q ^ (r & 7)) << 4));
+                    if (row < g.M) {
+                        float* dst = C + static_cast<size_t>(row) * g.ldc + col;
+                        if (cvec && col + 4 <= g.N) {
+                            *reinterpret_cast<float4*>(dst) = y;
+                        } else {
+                            if (col < g.N) dst[0] = y.x;
+                            if (col + 1 < g.N) dst[1] = y.y;
+                            if (col + 2 < g.N) dst[2] = y.z;
+                            if (col + 3 < g.N) dst[3] = y.w;
+                        }
                     }
                 }
+                __syncwarp();   // the block is read before the next chunk overwrites it
             }
         }
     }
