@@ -150,21 +150,68 @@ __global__ void __launch_bounds__(NTHREADS, 3) attn_tc_kernel(const TcGroup* __r
                 }
             }
         };
-        if (nk > 0) fetch(0);
-        for (int kb = 0; kb < nk; ++kb) {
-            const int s = kb % TSTAGES, r = kb / TSTAGES;
-            if (!warp_wait(&empty[s], (r & 1) ^ 1, DEV_TIMEOUT_EMPTY, args.err, abort_flag)) break;
-            uint8_t* st = smem + s * STAGE;
+        // The common case - 16-byte aligned rows of A, B [n][k] and the bias, K a multiple of 16 - loads without any
+        // branch: rows past the problem read row 0 instead and are zeroed when stored, and the bias is added then
+        // too, so nothing waits for a load before the stage it feeds is free.
+        const bool fast = !B_KN && avec && bvec && (g.K % TK) == 0 && (!bias || biasvec);
+        if (fast) {
+            float4 ba[PER];
+            uint32_t live = 0;   // bit i: A row of chunk i inside the problem; bit PER + i: B row
 #pragma unroll
             for (int i = 0; i < PER; ++i) {
-                const int e = t + 128 * i;
-                store_split(st, st + PART, kmaj_off(e >> 2, e & 3), ra[i]);
-                store_split(st + 2 * PART, st + 3 * PART, B_KN ? kmaj_off(e & 127, e >> 7) : kmaj_off(e >> 2, e & 3),
-                            rb[i]);
+                const int e = t + 128 * i, r = e >> 2;
+                live |= (m0 + r < g.M ? 1u : 0u) << i;
+                live |= (n0 + r < g.N ? 1u : 0u) << (PER + i);
             }
-            fence_proxy_async_smem();
-            mbar_arrive(&full[s]);
-            if (kb + 1 < nk) fetch(kb + 1);
+            auto fetch_fast = [&](int kb) {
+                const int k0 = kb * TK;
+#pragma unroll
+                for (int i = 0; i < PER; ++i) {
+                    const int e = t + 128 * i, r = e >> 2, c = e & 3, k = k0 + 4 * c;
+                    const int m = (live >> i) & 1 ? m0 + r : 0, n = (live >> (PER + i)) & 1 ? n0 + r : 0;
+                    ra[i] = __ldg(reinterpret_cast<const float4*>(A + static_cast<size_t>(m) * g.lda + k));
+                    rb[i] = __ldg(reinterpret_cast<const float4*>(B + static_cast<size_t>(n) * g.ldb + k));
+                    if (bias) ba[i] = __ldg(reinterpret_cast<const float4*>(bias + k));
+                }
+            };
+            if (nk > 0) fetch_fast(0);
+            for (int kb = 0; kb < nk; ++kb) {
+                const int s = kb % TSTAGES, r = kb / TSTAGES;
+                if (!warp_wait(&empty[s], (r & 1) ^ 1, DEV_TIMEOUT_EMPTY, args.err, abort_flag)) break;
+                uint8_t* st = smem + s * STAGE;
+#pragma unroll
+                for (int i = 0; i < PER; ++i) {
+                    const int e = t + 128 * i;
+                    float4 a = ra[i], b = rb[i];
+                    if (bias)
+                        a = make_float4(__fadd_rn(a.x, ba[i].x), __fadd_rn(a.y, ba[i].y), __fadd_rn(a.z, ba[i].z),
+                                        __fadd_rn(a.w, ba[i].w));
+                    if (!((live >> i) & 1)) a = make_float4(0.f, 0.f, 0.f, 0.f);
+                    if (!((live >> (PER + i)) & 1)) b = make_float4(0.f, 0.f, 0.f, 0.f);
+                    store_split(st, st + PART, kmaj_off(e >> 2, e & 3), a);
+                    store_split(st + 2 * PART, st + 3 * PART, kmaj_off(e >> 2, e & 3), b);
+                }
+                fence_proxy_async_smem();
+                mbar_arrive(&full[s]);
+                if (kb + 1 < nk) fetch_fast(kb + 1);
+            }
+        } else {
+            if (nk > 0) fetch(0);
+            for (int kb = 0; kb < nk; ++kb) {
+                const int s = kb % TSTAGES, r = kb / TSTAGES;
+                if (!warp_wait(&empty[s], (r & 1) ^ 1, DEV_TIMEOUT_EMPTY, args.err, abort_flag)) break;
+                uint8_t* st = smem + s * STAGE;
+#pragma unroll
+                for (int i = 0; i < PER; ++i) {
+                    const int e = t + 128 * i;
+                    store_split(st, st + PART, kmaj_off(e >> 2, e & 3), ra[i]);
+                    store_split(st + 2 * PART, st + 3 * PART,
+                                B_KN ? kmaj_off(e & 127, e >> 7) : kmaj_off(e >> 2, e & 3), rb[i]);
+                }
+                fence_proxy_async_smem();
+                mbar_arrive(&full[s]);
+                if (kb + 1 < nk) fetch(kb + 1);
+            }
         }
     } else if (lane == 0) {
         // ---------------- MMA issue ----------------
