@@ -150,10 +150,11 @@ __global__ void __launch_bounds__(NTHREADS, 3) attn_tc_kernel(const TcGroup* __r
                 }
             }
         };
-        // The common case - 16-byte aligned rows of A, B [n][k] and the bias, K a multiple of 16 - loads without any
+        // The common case - 16-byte aligned rows of A, B [n][k] and the bias - loads every whole K step without any
         // branch: rows past the problem read row 0 instead and are zeroed when stored, and the bias is added then
-        // too, so nothing waits for a load before the stage it feeds is free.
-        const bool fast = !B_KN && avec && bvec && (g.K % TK) == 0 && (!bias || biasvec);
+        // too, so nothing waits for a load before the stage it feeds is free. A last, partial K step takes the
+        // bounds-checked loads above (zeros past K, bias included).
+        const bool fast = !B_KN && avec && bvec && (!bias || biasvec);
         if (fast) {
             float4 ba[PER];
             uint32_t live = 0;   // bit i: A row of chunk i inside the problem; bit PER + i: B row
@@ -174,26 +175,33 @@ __global__ void __launch_bounds__(NTHREADS, 3) attn_tc_kernel(const TcGroup* __r
                     if (bias) ba[i] = __ldg(reinterpret_cast<const float4*>(bias + k));
                 }
             };
-            if (nk > 0) fetch_fast(0);
+            auto fetch_step = [&](int kb) {
+                if ((kb + 1) * TK <= g.K) fetch_fast(kb);
+                else fetch(kb);
+            };
+            if (nk > 0) fetch_step(0);
             for (int kb = 0; kb < nk; ++kb) {
                 const int s = kb % TSTAGES, r = kb / TSTAGES;
                 if (!warp_wait(&empty[s], (r & 1) ^ 1, DEV_TIMEOUT_EMPTY, args.err, abort_flag)) break;
                 uint8_t* st = smem + s * STAGE;
+                const bool whole = (kb + 1) * TK <= g.K;   // loaded by fetch_fast: bias and row masks still to apply
 #pragma unroll
                 for (int i = 0; i < PER; ++i) {
                     const int e = t + 128 * i;
                     float4 a = ra[i], b = rb[i];
-                    if (bias)
-                        a = make_float4(__fadd_rn(a.x, ba[i].x), __fadd_rn(a.y, ba[i].y), __fadd_rn(a.z, ba[i].z),
-                                        __fadd_rn(a.w, ba[i].w));
-                    if (!((live >> i) & 1)) a = make_float4(0.f, 0.f, 0.f, 0.f);
-                    if (!((live >> (PER + i)) & 1)) b = make_float4(0.f, 0.f, 0.f, 0.f);
+                    if (whole) {
+                        if (bias)
+                            a = make_float4(__fadd_rn(a.x, ba[i].x), __fadd_rn(a.y, ba[i].y), __fadd_rn(a.z, ba[i].z),
+                                            __fadd_rn(a.w, ba[i].w));
+                        if (!((live >> i) & 1)) a = make_float4(0.f, 0.f, 0.f, 0.f);
+                        if (!((live >> (PER + i)) & 1)) b = make_float4(0.f, 0.f, 0.f, 0.f);
+                    }
                     store_split(st, st + PART, kmaj_off(e >> 2, e & 3), a);
                     store_split(st + 2 * PART, st + 3 * PART, kmaj_off(e >> 2, e & 3), b);
                 }
                 fence_proxy_async_smem();
                 mbar_arrive(&full[s]);
-                if (kb + 1 < nk) fetch_fast(kb + 1);
+                if (kb + 1 < nk) fetch_step(kb + 1);
             }
         } else {
             if (nk > 0) fetch(0);

@@ -28,3 +28,26 @@ def test_sgemm_tf32x3_matches_float64(pkg, cuda, transB, M, N, K):
     err = np.abs(Cd.cpu().numpy() - ref) / scale
     assert np.isfinite(Cd.cpu().numpy()).all()
     assert err.max() <= TOL, err.max()
+
+
+@pytest.mark.parametrize("M,N,K,pad", [(375, 128, 375, 1), (200, 130, 100, 4), (129, 257, 48, 0), (64, 64, 17, 3)])
+def test_sgemm_tf32x3_padded_rows(pkg, cuda, M, N, K, pad):
+    """Row strides rounded up to 16 bytes (as the encoder's score and V^T rows are), K not a multiple of the 16-deep
+    K step: the branch-free path for whole steps and the bounds-checked one for the last, partial step."""
+    import torch
+    rng = np.random.default_rng(M + N + K)
+    ld = (K + pad + 3) & ~3
+    A = rng.standard_normal((M, ld)).astype(np.float32)
+    B = rng.standard_normal((N, ld)).astype(np.float32)
+    A[:, K:] = np.nan   # past K: must not be read into the products
+    B[:, K:] = np.nan
+    Ad, Bd = torch.from_numpy(A).to(cuda), torch.from_numpy(B).to(cuda)
+    Cd = torch.full((M, N), np.nan, dtype=torch.float32, device=cuda)
+    pkg.check(pkg.lib().p2cu_sgemm_tf32x3(1, M, N, K, Ad.data_ptr(), ld, Bd.data_ptr(), ld, Cd.data_ptr(), N, None))
+    pkg.check_device()
+    a, b = A[:, :K].astype(np.float64), B[:, :K].astype(np.float64)
+    ref = a @ b.T
+    scale = np.abs(a) @ np.abs(b).T
+    got = Cd.cpu().numpy()
+    assert np.isfinite(got).all()
+    assert (np.abs(got - ref) / scale).max() <= TOL
