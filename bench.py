@@ -754,8 +754,8 @@ LONG_SECONDS = 600.0
 
 
 def long_audio_ours(pkg, world, rank, local, steps=3):
-    """Long-form transcription (the engine's path for long audio): each rank transcribes its own 10-minute recording end to end
-    through p2_b200_transcribe_long - pause-aligned windows, dropout re-decodes scheduled as one batch per split depth,
+    """Long-form transcription (the engine's path for long audio): each rank transcribes its own 10-minute recording
+    end to end through p2_b200_transcribe_long - pause-aligned windows, dropout re-decodes as one batch per split depth,
     log-mel, encoder and decoder on the device (host audio in, host tokens out). Weak scaling: every rank holds a
     recording; value = all ranks' audio seconds / the slowest rank's wall time per recording."""
     from phonon2_b200 import model as M
