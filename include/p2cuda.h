@@ -104,8 +104,7 @@ P2CU_API int p2cu_fv_pack_codes(const P2cuFiveValue *B, signed char *codes, void
 #define P2CU_NOALLOC_SCRATCH_BYTES (16u << 20)
 
 /* p2cu_sgemm_fvb without a workspace argument, for callers that cannot allocate device memory: a real-time thread
- * (cudaMalloc may block and synchronise the device), a host that grants a fixed memory budget, code running while a
- * stream is captured into a CUDA graph. No counterpart in the reference (its GEMMs use per-thread host buffers).
+ * (cudaMalloc may block and synchronise the device) or a host that grants a fixed memory budget. No counterpart in the reference (its GEMMs use per-thread host buffers).
  * The scratch - quantised activations and, for K > 1024, the per-block partials; p2cu_gemm_workspace_bytes(M, N, K,
  * mode) bytes - lives in one fixed array of P2CU_NOALLOC_SCRATCH_BYTES per device; larger shapes are refused with
  * P2CU_EINVAL and a message. This function calls no cudaMalloc, cudaFree or other allocating routine. Its first call

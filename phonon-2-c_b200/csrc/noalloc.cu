@@ -2,14 +2,14 @@
 // device array that the library owns, for callers that cannot allocate device memory.
 //
 // Who needs it: a caller that must not call cudaMalloc, e.g. a real-time audio callback (cudaMalloc can block and
-// implicitly synchronise the device), a plugin host that only hands out a fixed memory budget, or code that runs
-// while a stream is being captured into a CUDA graph. p2cu_sgemm_fvb needs a workspace for the quantised
+// implicitly synchronise the device) or a plugin host that only hands out a fixed memory budget. p2cu_sgemm_fvb needs a workspace for the quantised
 // activations and, when K > 1024, for the per-1024-row-block partial results; here that workspace is the array below.
 //
 // The array is a file-scope __device__ variable: every GPU that loads this library holds its P2CU_NOALLOC_SCRATCH_BYTES
 // until the process exits. In host code the name g_noalloc_scratch is only a stand-in for the symbol, not a device
 // address, so it is never passed to a kernel; its device address is looked up once per device with
-// cudaGetSymbolAddress, with that device current, on the first call made on that device.
+// cudaGetSymbolAddress, with that device current, on the first call made on that device; make that first call before
+// any stream capture.
 #include <cstdint>
 #include <cstdio>
 #include <mutex>

@@ -1,8 +1,7 @@
 """p2cu_sgemm_fvb_noalloc: the five-value GEMM for callers that cannot allocate device memory.
 
-A real-time audio thread cannot risk cudaMalloc (it may block and synchronise the whole device), a host application
-may hand this library a fixed memory budget, and code running during CUDA-graph stream capture cannot allocate at
-all. For them the GEMM's scratch (the int8 activations and, for K > 1024, the per-block partial results) lives in a
+A real-time audio thread cannot risk cudaMalloc (it may block and synchronise the whole device), and a host
+application may hand this library a fixed memory budget. For them the GEMM's scratch (the int8 activations and, for K > 1024, the per-block partial results) lives in a
 fixed device array inside the library. These tests call the entry point through the C ABI and compare it with the
 workspace-taking entry point, p2cu_sgemm_fvb, bit for bit (the tolerance of every int8 GEMM test here), on two calls in
 a row that leave different contents in the shared array. The file is named to be collected last.
