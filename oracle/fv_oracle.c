@@ -31,9 +31,14 @@
 
 /* ---- quantisation ---------------------------------------------------------------------------------------- */
 
-/* Round half to even, as the NEON vcvtnq_s32_f32 the reference uses (blas.c:1124-1127). */
+/* Round half to even with saturation, as the NEON vcvtnq_s32_f32 (FCVTNS) the reference uses (blas.c:1124-1127):
+ * NaN gives 0 and values beyond the int32 range give its ends. Both occur when 1 / scale overflows to infinity (a row
+ * whose largest magnitude is below about 3.7e-37): x * inf is +-inf, and 0 * inf is NaN. */
 static int32_t round_even(float x)
 {
+    if (x != x) return 0;
+    if (x >= 2147483648.0f) return INT32_MAX;
+    if (x <= -2147483648.0f) return INT32_MIN;
     return (int32_t)nearbyintf(x);   /* default rounding mode is to-nearest-even */
 }
 
@@ -42,7 +47,10 @@ static int8_t sat8(int32_t v)         /* vqmovn_s32 then vqmovn_s16: saturate to
     return (int8_t)(v > 127 ? 127 : v < -128 ? -128 : v);
 }
 
-/* One row: amax over |x|, scale = amax / 127 (1 when the row is all zero), q = sat(rne(x * (1 / scale))). */
+/* One row: amax over |x|, scale = amax / 127 (1 when the row is all zero). The first K - K % 16 values take the
+ * reference's 16-wide loop, q = sat(rne(x * (1 / scale))) (blas.c:1122-1138); the last K % 16 its scalar tail,
+ * q = clamp(lrintf(x / scale), -127, 127) (blas.c:1139-1143): a division rather than the reciprocal, so a value can
+ * round to the other side of a half. */
 void orc_quant_row(const float *row, int K, int8_t *q, float *scale_out)
 {
     float amax = 0.0f;
@@ -52,7 +60,12 @@ void orc_quant_row(const float *row, int K, int8_t *q, float *scale_out)
     }
     float scale = amax > 0.0f ? amax / 127.0f : 1.0f;
     float inv = 1.0f / scale;
-    for (int k = 0; k < K; k++) q[k] = sat8(round_even(row[k] * inv));
+    const int k16 = K & ~15;
+    for (int k = 0; k < k16; k++) q[k] = sat8(round_even(row[k] * inv));
+    for (int k = k16; k < K; k++) {
+        int32_t v = round_even(row[k] / scale);
+        q[k] = (int8_t)(v > 127 ? 127 : v < -127 ? -127 : v);
+    }
     *scale_out = scale;
 }
 
@@ -161,8 +174,17 @@ void orc_acc_blocks(int M, int N, int K, const int8_t *q, int mode,
 
 /* ---- the int8 GEMM with the reference epilogue ----------------------------------------------------------- */
 
-/* C = alpha * A * B + beta * C on pre-quantised A (q row-major [M][K], one scale per row); beta must be 0 or 1
- * (other values are first applied by scale_c in the reference, blas.c:1435). Per K block b and element:
+/* scale_c (blas.c:60-70): C = beta * C, zeros for beta == 0, nothing for beta == 1. */
+static void scale_rows(float *C, int M, int N, int ldc, float beta)
+{
+    if (beta == 1.0f) return;
+    for (int m = 0; m < M; m++)
+        for (int n = 0; n < N; n++) C[(size_t)m * ldc + n] = beta == 0.0f ? 0.0f : C[(size_t)m * ldc + n] * beta;
+}
+
+/* C = alpha * A * B + beta * C on pre-quantised A (q row-major [M][K], one scale per row), as p2_sgemm_fvb_q8a and
+ * p2_sgemm_q8b_q8a run it (blas.c:1430-1446): alpha == 0 only scales C; other beta than 0 and 1 scale C first (scale_c,
+ * blas.c:60-70) and then accumulate. Per K block b and element:
  *   int8w: f = (float)acc * (hi * (1/127))            int8: f = fma((float)accT, hi - lo, (float)accS * lo)
  *   q8b:   f = (float)acc * scale[n]
  *   as = a_scale[m] * alpha;  C = (beta == 0 && b == 0) ? f * as : fma(f, as, C)      (blas.c:1316-1366) */
@@ -170,6 +192,8 @@ void orc_gemm_i8(int M, int N, int K, float alpha, const int8_t *q, const float 
                  const uint8_t *signs, const uint8_t *flags, const float *lo, const float *hi,
                  const int8_t *q8, const float *scales, int ldb, float beta, float *C, int ldc)
 {
+    if (alpha == 0.0f) { scale_rows(C, M, N, ldc, beta); return; }
+    if (beta != 0.0f && beta != 1.0f) { scale_rows(C, M, N, ldc, beta); beta = 1.0f; }
     int nblk = (K + ORC_KBLK - 1) / ORC_KBLK;
     size_t plane = (size_t)nblk * M * N;
     int32_t *accS = (int32_t *)malloc(plane * sizeof(int32_t));
@@ -199,14 +223,9 @@ void orc_gemm_i8(int M, int N, int K, float alpha, const int8_t *q, const float 
 
 /* ---- the exact path: one FMA chain per output ------------------------------------------------------------ */
 
-/* scale_c (blas.c:60-70), then for every output c = fma(alpha * a[m][k], w[k][n], c) over k = 0..K-1 in order: the
- * micro-kernels load C, run the chain over a KC block and store C, block after block (blas.c:155-181, 960-985). */
-static void scale_rows(float *C, int M, int N, int ldc, float beta)
-{
-    if (beta == 1.0f) return;
-    for (int m = 0; m < M; m++)
-        for (int n = 0; n < N; n++) C[(size_t)m * ldc + n] = beta == 0.0f ? 0.0f : C[(size_t)m * ldc + n] * beta;
-}
+/* The exact path: scale_c (blas.c:60-70), then for every output c = fma(alpha * a[m][k], w[k][n], c) over
+ * k = 0..K-1 in order: the micro-kernels load C, run the chain over a KC block and store C, block after block
+ * (blas.c:155-181, 960-985). */
 
 void orc_gemm_exact(int M, int N, int K, float alpha, const float *A, int lda,
                     const uint8_t *signs, const uint8_t *flags, const float *lo, const float *hi,

@@ -6,12 +6,18 @@ Three libraries, all built by oracle/Makefile (``__graft_entry__.build()`` runs 
   * ``_ref/libphonon2_ref_i8.so`` - the same, with its int8 GEMM entry points supplied by ref_int8_blas.c (the
     restatement), so that the reference's own encoder runs its int8 control flow on x86.
 
+  * ``_ref/libphonon2_ref_neon.so`` (IEEE arithmetic) and ``_ref/libphonon2_ref_neon_fm.so`` (the reference's own
+    -ffast-math flags) - phonon-2-c's blas.c compiled as for AArch64 with dot products, its NEON intrinsics modelled
+    in C by ``neon_emu/arm_neon.h``: the reference's own int8 and int8w GEMM code running on x86.
+
 Only tests/, ``__graft_entry__.smoke()`` and bench.py's CPU legs import this module; the product never does.
 """
 from __future__ import annotations
 
 import ctypes as C
 import os
+import shutil
+import tempfile
 from pathlib import Path
 
 import numpy as np
@@ -20,6 +26,8 @@ HERE = Path(__file__).resolve().parent
 ORACLE_SO = HERE / "liboracle.so"
 REF_SO = HERE / "_ref" / "libphonon2_ref.so"
 REF_I8_SO = HERE / "_ref" / "libphonon2_ref_i8.so"
+REF_NEON_SO = HERE / "_ref" / "libphonon2_ref_neon.so"
+REF_NEON_FM_SO = HERE / "_ref" / "libphonon2_ref_neon_fm.so"
 
 MODE_INT8, MODE_INT8W, MODE_Q8B = 0, 2, 8
 _MODES = {"int8": MODE_INT8, "int8w": MODE_INT8W}
@@ -188,6 +196,143 @@ def ref_sgemm(transA, transB, A, B, out, alpha=1.0, beta=0.0):
     ref().p2_sgemm(112 if transA else 111, 112 if transB else 111, M, N, K, alpha, np.ascontiguousarray(A), A.shape[1],
                    np.ascontiguousarray(B), B.shape[1], beta, out, N)
     return out
+
+
+# ---- the reference's AArch64 int8 GEMM code, compiled for x86 through the NEON model -------------------------------
+
+class QuantA(C.Structure):
+    """The reference's QuantA (csrc/phonon2.h:432-436)."""
+    _fields_ = [("q", C.c_void_p), ("scales", C.c_void_p), ("M", C.c_int), ("K", C.c_int)]
+
+
+_neon = {}
+
+
+def ref_neon_available() -> bool:
+    return REF_NEON_SO.exists() and REF_NEON_FM_SO.exists()
+
+
+def ref_neon(mode: str, fast_math: bool = False) -> C.CDLL:
+    """phonon-2-c's blas.c built as for AArch64 with dot products (oracle/Makefile, oracle/neon_emu/arm_neon.h), in GEMM
+    mode `mode` ('int8', 'int8w' or 'exact'); `fast_math` picks the build with the reference's own -ffast-math flags.
+
+    The reference reads P2_GEMM once per process (csrc/blas.c:1029-1053), so each mode gets its own copy of the library
+    file, loaded and initialised with P2_GEMM set to that mode (a second dlopen of one path would share its state)."""
+    key = (mode, fast_math)
+    if key in _neon:
+        return _neon[key]
+    src = REF_NEON_FM_SO if fast_math else REF_NEON_SO
+    if not src.exists():
+        raise RuntimeError(f"{src} is not built (needs the reference sources; run __graft_entry__.build())")
+    copy = Path(tempfile.mkdtemp(prefix="p2_ref_neon_")) / f"{src.stem}_{mode}.so"
+    shutil.copyfile(src, copy)
+    saved = {k: os.environ.get(k) for k in ("P2_GEMM", "P2_EXACT")}
+    os.environ["P2_GEMM"] = mode
+    os.environ.pop("P2_EXACT", None)
+    try:
+        L = C.CDLL(str(copy))
+        L.p2_gemm_mode.restype = C.c_char_p
+        L.p2_gemm_mode()                      # the mode is read now, under this P2_GEMM
+    finally:
+        for k, v in saved.items():
+            if v is None:
+                os.environ.pop(k, None)
+            else:
+                os.environ[k] = v
+    L.p2_sgemm_fvb.argtypes = [C.c_int, C.c_int, C.c_int, C.c_float, _f32p, C.c_int, C.POINTER(FiveValueB),
+                               C.c_float, _f32p, C.c_int]
+    L.p2_sgemm_q8b.argtypes = [C.c_int, C.c_int, C.c_int, C.c_float, _f32p, C.c_int, _i8p, _f32p, C.c_int,
+                               C.c_float, _f32p, C.c_int]
+    L.p2_sgemm.argtypes = [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_float, _f32p, C.c_int, _f32p,
+                           C.c_int, C.c_float, _f32p, C.c_int]
+    L.p2_quant_prepare.argtypes = [C.POINTER(QuantA), C.c_int, C.c_int]
+    L.p2_quant_prepare.restype = C.c_int
+    L.p2_quant_row.argtypes = [C.POINTER(QuantA), C.c_int, _f32p]
+    L.p2_sgemm_fvb_q8a.argtypes = [C.c_int, C.c_int, C.c_int, C.c_float, C.POINTER(QuantA), C.POINTER(FiveValueB),
+                                   C.c_float, _f32p, C.c_int]
+    L.p2_sgemm_q8b_q8a.argtypes = [C.c_int, C.c_int, C.c_int, C.c_float, C.POINTER(QuantA), _i8p, _f32p, C.c_int,
+                                   C.c_float, _f32p, C.c_int]
+    L.p2_fv_pack_codes.argtypes = [C.POINTER(FiveValueB), C.c_int, C.c_int]
+    L.p2_fv_pack_codes.restype = C.c_void_p
+    _neon[key] = L
+    return L
+
+
+def _fv_struct(w, codes=None):
+    return FiveValueB(_ptr(w["signs"]).value, _ptr(w["flags"]).value, _ptr(w["lo"]).value, _ptr(w["hi"]).value,
+                      None if codes is None else _ptr(codes).value)
+
+
+def neon_quant_rows(L, A: np.ndarray):
+    """The reference's own quantiser (p2_quant_prepare + p2_quant_row, csrc/blas.c:1114-1187) on the rows of A:
+    returns (q [M, K] int8 row-major, scales [M]), read out of its tile layout [Mp/4][K/4][4 rows][4 k]."""
+    A = np.ascontiguousarray(A, np.float32)
+    M, K = A.shape
+    qa = QuantA()
+    if L.p2_quant_prepare(C.byref(qa), M, K) != 0:
+        raise RuntimeError("p2_quant_prepare refused (exact mode, or K % 4 != 0)")
+    for m in range(M):
+        L.p2_quant_row(C.byref(qa), m, A[m])
+    Mp = (M + 3) // 4 * 4
+    tiles = np.ctypeslib.as_array(C.cast(qa.q, C.POINTER(C.c_int8)), shape=(Mp * K,))
+    q = tiles.reshape(Mp // 4, K // 4, 4, 4).transpose(0, 2, 1, 3).reshape(Mp, K)[:M].copy()
+    scales = np.ctypeslib.as_array(C.cast(qa.scales, C.POINTER(C.c_float)), shape=(M,)).copy()
+    return q, scales
+
+
+def neon_quanta(L, q: np.ndarray, scales: np.ndarray):
+    """A QuantA of the reference holding the given quantised rows (its own buffer from p2_quant_prepare, filled in
+    its tile layout), so that its GEMMs run on exactly these activations. Valid until the next prepare."""
+    M, K = q.shape
+    qa = QuantA()
+    if L.p2_quant_prepare(C.byref(qa), M, K) != 0:
+        raise RuntimeError("p2_quant_prepare refused (exact mode, or K % 4 != 0)")
+    Mp = (M + 3) // 4 * 4
+    qp = np.zeros((Mp, K), np.int8)
+    qp[:M] = q
+    tiles = np.ctypeslib.as_array(C.cast(qa.q, C.POINTER(C.c_int8)), shape=(Mp * K,))
+    tiles[:] = qp.reshape(Mp // 4, 4, K // 4, 4).transpose(0, 2, 1, 3).reshape(-1)
+    np.ctypeslib.as_array(C.cast(qa.scales, C.POINTER(C.c_float)), shape=(M,))[:] = scales
+    return qa
+
+
+def neon_sgemm_fvb(L, A, w, out, alpha=1.0, beta=0.0):
+    M, K = A.shape
+    b = _fv_struct(w)
+    L.p2_sgemm_fvb(M, out.shape[1], K, alpha, np.ascontiguousarray(A, np.float32), K, C.byref(b), beta, out,
+                   out.shape[1])
+    return out
+
+
+def neon_sgemm_fvb_q8a(L, q, scales, w, out, alpha=1.0, beta=0.0):
+    M, K = q.shape
+    qa = neon_quanta(L, q, scales)
+    b = _fv_struct(w)
+    L.p2_sgemm_fvb_q8a(M, out.shape[1], K, alpha, C.byref(qa), C.byref(b), beta, out, out.shape[1])
+    return out
+
+
+def neon_sgemm_q8b_q8a(L, q, scales, q8, out, alpha=1.0, beta=0.0):
+    M, K = q.shape
+    N = out.shape[1]
+    qa = neon_quanta(L, q, scales)
+    L.p2_sgemm_q8b_q8a(M, N, K, alpha, C.byref(qa), np.ascontiguousarray(q8["q8"]), q8["scales"], N, beta, out, N)
+    return out
+
+
+def neon_fv_pack_codes(L, w) -> np.ndarray:
+    """The reference's p2_fv_pack_codes (csrc/blas.c:1372-1400) as a row-major [K, N] int8 plane, read out of its
+    panel layout [N/16][K/4][16 columns][4 k]."""
+    K, N = w["K"], w["N"]
+    b = _fv_struct(w)
+    p = L.p2_fv_pack_codes(C.byref(b), K, N)
+    if not p:
+        raise RuntimeError("p2_fv_pack_codes returned NULL")
+    try:
+        raw = np.ctypeslib.as_array(C.cast(p, C.POINTER(C.c_int8)), shape=(K * N,)).copy()
+    finally:
+        C.CDLL(None).free(C.c_void_p(p))
+    return raw.reshape(N // 16, K // 4, 16, 4).transpose(1, 3, 0, 2).reshape(K, N)
 
 
 def _encoder_lib(path):

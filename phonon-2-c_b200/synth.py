@@ -45,6 +45,41 @@ def activations(M: int, K: int, seed: int) -> np.ndarray:
     return np.random.default_rng(seed).standard_normal((M, K), dtype=np.float32)
 
 
+def quantiser_edge_rows(K: int, seed: int) -> np.ndarray:
+    """fp32 rows [8, K] that reach the edges of the reference's per-row quantiser (csrc/blas.c:1114-1144).
+
+    Rows 0-3: the largest magnitude fixed at the first value, every other value placed where x * (1 / scale) and
+    x / scale round to different integers (near a half of the quantisation step), so the 16-wide loop (reciprocal)
+    and the scalar tail of the last K % 16 values (division) give visibly different codes. Row 4: all zeros
+    (scale 1). Row 5: a maximum of 2e-37, so that 1 / scale overflows to infinity (x * inf saturates to +127 or -128,
+    0 * inf is NaN and converts to 0). Row 6: one large value among small ones. Row 7: exact halves at scale 1
+    (ties to even)."""
+    rng = np.random.default_rng(seed)
+    f32 = np.float32
+    rows = np.zeros((8, K), f32)
+    for r in range(4):
+        amax = f32(rng.uniform(0.5, 8.0))
+        scale = f32(amax / f32(127))
+        inv = f32(f32(1) / scale)
+        picked = []
+        while len(picked) < K - 1:
+            n = rng.integers(-126, 126, 4096)
+            x = ((n + 0.5) * np.float64(scale)).astype(f32)
+            x = np.concatenate([x, np.nextafter(x, f32(np.inf)), np.nextafter(x, f32(-np.inf))]).astype(f32)
+            split = np.rint((x * inv).astype(f32)) != np.rint((x / scale).astype(f32))
+            picked.extend(x[split & (np.abs(x) < amax)].tolist())
+        rows[r, 0] = amax if r % 2 == 0 else -amax
+        rows[r, 1:] = np.asarray(picked[:K - 1], f32)
+    rows[5] = (rng.uniform(-2e-37, 2e-37, K)).astype(f32)
+    rows[5, 0] = f32(2e-37)
+    rows[5, 1:K:7] = 0.0
+    rows[6] = (rng.standard_normal(K) * 1e-3).astype(f32)
+    rows[6, K // 2] = f32(3.0e4)
+    rows[7] = ((np.arange(K) % 9) - 4).astype(f32) + f32(0.5)
+    rows[7, 0] = f32(127.0)
+    return rows
+
+
 def expand(w: dict) -> np.ndarray:
     """The exact fp32 weight [K, N], {0, +-lo, +-hi}, for reading results (not for the measured path)."""
     K, N = w["K"], w["N"]
