@@ -62,8 +62,9 @@ P2CU_API int p2cu_check_device(void *stream);
 /* Per-row int8 quantisation (csrc/blas.c:1114-1144): q [M][K] int8, scales [M]. */
 P2CU_API int p2cu_quant_rows(const float *A, int M, int K, int lda, signed char *q, float *scales, void *stream);
 
-/* C = alpha * A * B + beta * C on quantised A (csrc/blas.c:1430-1437). mode P2CU_INT8 or P2CU_INT8W.
- * N % 128 == 0, K % 16 == 0. beta: 0 stores, 1 accumulates, other values scale C first. When K > 1024 the GEMM
+/* C = alpha * A * B + beta * C on quantised A (csrc/blas.c:1430-1437). mode P2CU_INT8 or P2CU_INT8W. N % 16 == 0;
+ * the tcgen05 kernels take N % 128 == 0, K % 16 == 0 and C 16-byte aligned with ldc % 4 == 0, other shapes a SIMT
+ * kernel with the same arithmetic. beta: 0 stores, 1 accumulates, other values scale C first. When K > 1024 the GEMM
  * keeps one fp32 value per output and 1024-row block of K in `workspace` (p2cu_q8a_workspace_bytes; 0 otherwise)
  * and folds them into C in block order, as the reference's blockwise epilogue does. */
 P2CU_API int p2cu_sgemm_fvb_q8a(int M, int N, int K, float alpha, const signed char *q, const float *a_scales,
@@ -83,8 +84,8 @@ P2CU_API size_t p2cu_q8a_workspace_bytes(int M, int N, int K);
 P2CU_API size_t p2cu_gemm_workspace_bytes(int M, int N, int K, int mode);
 
 /* C = alpha * A * B + beta * C from fp32 A (csrc/blas.c:1481-1499 / 1462-1479): in the int8 modes A is quantised
- * into `workspace` first; in P2CU_EXACT the weights are expanded to fp32 and every output is the reference's FMA
- * chain, bit for bit. */
+ * into `workspace` first (K % 4 != 0 takes the exact path instead, as in the reference); in P2CU_EXACT the weights
+ * are expanded to fp32 and every output is the reference's FMA chain, bit for bit. */
 P2CU_API int p2cu_sgemm_fvb(int M, int N, int K, float alpha, const float *A, int lda, const P2cuFiveValue *B, int mode,
                    float beta, float *C, int ldc, void *workspace, size_t workspace_bytes, void *stream);
 P2CU_API int p2cu_sgemm_q8b(int M, int N, int K, float alpha, const float *A, int lda, const signed char *B,

@@ -159,10 +159,41 @@ int run_i8(int M, int N, int K, float alpha, const int8_t* q, const float* a_sca
     if (N % 16) return fail(P2CU_EINVAL, "%s: N = %d is not a multiple of 16", who, N);
     if (M == 0 || N == 0) return P2CU_OK;
     if (alpha == 0.f || K == 0) return scale_c(C, M, N, ldc, beta, s);   // no products: C = beta * C
-    if (N % 128) return fail(P2CU_EUNSUPPORTED, "%s: N = %d: the tensor-core path needs N %% 128 == 0", who, N);
-    if (K % 16) return fail(P2CU_EUNSUPPORTED, "%s: K = %d: the tensor-core path needs K %% 16 == 0", who, K);
     if (!q || !a_scales) return fail(P2CU_EINVAL, "%s: quantised A is NULL", who);
-    if (!aligned16(C) || ldc % 4) return fail(P2CU_EINVAL, "%s: C must be 16-byte aligned with ldc %% 4 == 0", who);
+    if (N % 128 || K % 16 || !aligned16(C) || ldc % 4) {
+        // shapes the tensor-core kernels do not take (the reference's int8 path takes any N % 16 == 0): the SIMT
+        // kernel, same sums and epilogue (fv_gemm_simt.cu)
+        p2cu::FvGemmParams p{};
+        p.M = M; p.N = N; p.K = K; p.alpha = alpha; p.a_scales = a_scales; p.C = C; p.ldc = ldc;
+        const int8_t* table = nullptr;
+        const uint8_t *signs = nullptr, *flags = nullptr;
+        int tld = 0;
+        if (B) {
+            if (!B->lo || !B->hi) return fail(P2CU_EINVAL, "%s: lo / hi are NULL", who);
+            if (B->K != K || B->N != N)
+                return fail(P2CU_EINVAL, "%s: weight is [%d, %d], GEMM wants [%d, %d]", who, B->K, B->N, K, N);
+            p.lo = B->lo; p.hi = B->hi;
+            p.cmode = mode == P2CU_INT8W ? p2cu::CM_INT8W : p2cu::CM_INT8;
+            if (mode == P2CU_INT8W && B->codes) {
+                table = B->codes; tld = N;
+            } else {
+                if (!B->signs || !B->flags) return fail(P2CU_EINVAL, "%s: planes are NULL", who);
+                signs = B->signs; flags = B->flags;
+            }
+        } else {
+            if (!q8 || !scales) return fail(P2CU_EINVAL, "%s: int8 table is NULL", who);
+            if (ldb < N) return fail(P2CU_EINVAL, "%s: ldb=%d < N=%d", who, ldb, N);
+            p.cmode = p2cu::CM_Q8B; p.scales = scales;
+            table = q8; tld = ldb;
+        }
+        if (beta != 0.f && beta != 1.f) {
+            if ((rc = scale_c(C, M, N, ldc, beta, s))) return rc;
+            beta = 1.f;
+        }
+        p.beta_zero = beta == 0.f;
+        cudaError_t e = p2cu::fv_gemm_simt_launch(q, signs, flags, table, tld, p, s);
+        return e == cudaSuccess ? P2CU_OK : cuda_fail(e, who);
+    }
     const int nblk = (K + 1023) / 1024;
     const size_t need = split_bytes(M, N, K);
     if (need && (!ws || ws_bytes < need || !aligned16(ws)))
@@ -423,6 +454,9 @@ int p2cu_sgemm_fvb(int M, int N, int K, float alpha, const float* A, int lda, co
         return run_exact(M, N, K, alpha, A, lda, 0, B, nullptr, nullptr, nullptr, 0, 0, beta, C, ldc, s,
                          "p2cu_sgemm_fvb");
     if (mode != P2CU_INT8 && mode != P2CU_INT8W) return fail(P2CU_EINVAL, "p2cu_sgemm_fvb: mode %d", mode);
+    if (K % 4)   // the reference quantises only rows of whole quads; other K take its exact path (csrc/blas.c:1490-1495)
+        return run_exact(M, N, K, alpha, A, lda, 0, B, nullptr, nullptr, nullptr, 0, 0, beta, C, ldc, s,
+                         "p2cu_sgemm_fvb");
     int rc = check_gemm_common(M, N, K, C, ldc, "p2cu_sgemm_fvb");
     if (rc) return rc;
     if (M == 0 || N == 0) return P2CU_OK;
@@ -442,7 +476,7 @@ int p2cu_sgemm_q8b(int M, int N, int K, float alpha, const float* A, int lda, co
                    const float* scales, int ldb, int mode, float beta, float* C, int ldc, void* workspace,
                    size_t workspace_bytes, void* stream) {
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    if (mode == P2CU_EXACT)
+    if (mode == P2CU_EXACT || K % 4)   // K % 4 != 0: the reference's exact path (csrc/blas.c:1470-1478)
         return run_exact(M, N, K, alpha, A, lda, 0, nullptr, reinterpret_cast<const int8_t*>(B), scales, nullptr, ldb,
                          0, beta, C, ldc, s, "p2cu_sgemm_q8b");
     int rc = check_gemm_common(M, N, K, C, ldc, "p2cu_sgemm_q8b");

@@ -149,7 +149,7 @@ __global__ void __launch_bounds__(256) ln_rows_kernel(const float* __restrict__ 
     const float scale = quant_scale(m);
     const float qinv = __fdiv_rn(1.0f, scale);
     int8_t* qrow = q + static_cast<size_t>(row) * D;
-    for (int i = threadIdx.x; i < D; i += 256) qrow[i] = quant_one(y(i), qinv);
+    for (int i = threadIdx.x; i < D; i += 256) qrow[i] = quant_at(y(i), qinv, scale, i, D);
     if (threadIdx.x == 0) qscale[row] = scale;
 }
 
@@ -182,7 +182,7 @@ __global__ void __launch_bounds__(256) swish_rows_kernel(const float* __restrict
     const float scale = quant_scale(amax);
     const float qinv = __fdiv_rn(1.0f, scale);
     int8_t* qrow = q + static_cast<size_t>(r) * len;
-    for (int i = threadIdx.x; i < len; i += 256) qrow[i] = quant_one(swish1(hr[i]), qinv);
+    for (int i = threadIdx.x; i < len; i += 256) qrow[i] = quant_at(swish1(hr[i]), qinv, scale, i, len);
     if (threadIdx.x == 0) qscale[r] = scale;
 }
 
@@ -340,7 +340,7 @@ __global__ void __launch_bounds__(256) dwconv_swish_kernel(const float* __restri
 #pragma unroll
     for (int u = 0; u < PER; ++u) {
         const int d = threadIdx.x + 256 * u;
-        if (d < D) q[static_cast<size_t>(r) * D + d] = quant_one(v[u], qinv);
+        if (d < D) q[static_cast<size_t>(r) * D + d] = quant_at(v[u], qinv, scale, d, D);
     }
     if (threadIdx.x == 0) qscale[r] = scale;
 }

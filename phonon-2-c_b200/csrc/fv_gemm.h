@@ -51,6 +51,12 @@ cudaError_t fv_gemm_2sm_launch(int kind, const CUtensorMap& a, const CUtensorMap
 int fv_gemm_2sm_tiles(int M, int N, int ksplit);
 int fv_gemm_p_min_tiles();   // the SM count: below it every tile has an SM of its own anyway
 
+// The same GEMM as a plain SIMT kernel (fv_gemm_simt.cu) for shapes the tensor-core kernels do not take (N % 128,
+// K % 16, unaligned C): B from the planes (signs [K, N/4], flags [K, N/8]) or from `table` [K, ldb] (an int8 table, or
+// the int8w code cache with ldb = N); no workspace, K blocks folded in registers.
+cudaError_t fv_gemm_simt_launch(const int8_t* q, const uint8_t* signs, const uint8_t* flags, const int8_t* table,
+                                int ldb, const FvGemmParams& p, cudaStream_t stream);
+
 // C = fold of the workspace slices (fp32 f per 1024-row block) in block order, with the row scales.
 cudaError_t fv_combine_launch(const float* f, int m_pad, int nblk, const float* a_scales, float alpha, int beta_zero,
                               float* C, int M, int N, int ldc, cudaStream_t stream);

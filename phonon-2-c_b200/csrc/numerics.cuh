@@ -6,10 +6,25 @@
 namespace p2cu {
 
 // One value of the reference's per-row int8 quantisation (csrc/blas.c:1123-1131): saturate(round_half_even(x * inv)).
+// The conversion saturates and maps NaN to 0, as the reference's FCVTNS does when 1 / scale overflows to infinity.
 __device__ __forceinline__ int8_t quant_one(float x, float inv) {
     int v = __float2int_rn(__fmul_rn(x, inv));
     v = v > 127 ? 127 : (v < -128 ? -128 : v);
     return static_cast<int8_t>(v);
+}
+
+// The reference quantises the first K - K % 16 values of a row in its 16-wide loop (quant_one) and the last K % 16
+// in a scalar tail, clamp(lrintf(x / scale), -127, 127) (csrc/blas.c:1139-1143): a division instead of the reciprocal,
+// so a value near a half can round the other way.
+__device__ __forceinline__ int8_t quant_tail(float x, float scale) {
+    int v = __float2int_rn(__fdiv_rn(x, scale));
+    v = v > 127 ? 127 : (v < -127 ? -127 : v);
+    return static_cast<int8_t>(v);
+}
+
+// Value k of a quantised row of K values.
+__device__ __forceinline__ int8_t quant_at(float x, float inv, float scale, int k, int K) {
+    return k < (K & ~15) ? quant_one(x, inv) : quant_tail(x, scale);
 }
 
 // The reference's scale for a row with maximum magnitude amax: amax / 127, or 1 for an all-zero row.

@@ -1,5 +1,6 @@
 // quant.cu - per-row symmetric int8 quantisation of fp32 activations (csrc/blas.c:1114-1144, quant_pack_row):
-//   amax = max |x|, scale = amax > 0 ? amax / 127 : 1, q = saturate_int8(round_half_even(x * (1 / scale))).
+//   amax = max |x|, scale = amax > 0 ? amax / 127 : 1, q = saturate_int8(round_half_even(x * (1 / scale))), and for
+//   the last K % 16 values of a row the reference's scalar tail, clamp(round_half_even(x / scale), -127, 127).
 // Division is IEEE (the C source as written; the reference's -ffast-math build may use a reciprocal, see the oracle).
 // Output is row-major int8 [M, K] plus one fp32 scale per row; the GEMM's TMA loads tile it.
 #include <cstdint>
@@ -53,10 +54,15 @@ __global__ void __launch_bounds__(QT) quant_rows_kernel(const float* __restrict_
 #pragma unroll
         for (int i = 0; i < QV; ++i) {
             const int k = 4 * (threadIdx.x + i * QT);
-            if (k < K) {
+            if (k < K) {   // k is a multiple of 4 and so is K & ~15: the four values are all in the tail or none
                 char4 o;
-                o.x = quant_one(v[i].x, inv); o.y = quant_one(v[i].y, inv);
-                o.z = quant_one(v[i].z, inv); o.w = quant_one(v[i].w, inv);
+                if (k < (K & ~15)) {
+                    o.x = quant_one(v[i].x, inv); o.y = quant_one(v[i].y, inv);
+                    o.z = quant_one(v[i].z, inv); o.w = quant_one(v[i].w, inv);
+                } else {
+                    o.x = quant_tail(v[i].x, scale); o.y = quant_tail(v[i].y, scale);
+                    o.z = quant_tail(v[i].z, scale); o.w = quant_tail(v[i].w, scale);
+                }
                 *reinterpret_cast<char4*>(qrow + k) = o;
             }
         }
@@ -68,7 +74,7 @@ __global__ void __launch_bounds__(QT) quant_rows_kernel(const float* __restrict_
     amax = block_max(amax, red);
     const float scale = amax > 0.f ? __fdiv_rn(amax, 127.0f) : 1.0f;
     const float inv = __fdiv_rn(1.0f, scale);
-    for (int k = threadIdx.x; k < K; k += QT) qrow[k] = quant_one(row[k], inv);
+    for (int k = threadIdx.x; k < K; k += QT) qrow[k] = quant_at(row[k], inv, scale, k, K);
     if (threadIdx.x == 0) scales[m] = scale;
 }
 

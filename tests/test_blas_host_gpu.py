@@ -40,6 +40,17 @@ def test_p2_sgemm_fvb_int8w(pkg, orc, synth, cuda, M, K, N, alpha, beta):
     assert _bits_equal(again, want)
 
 
+@pytest.mark.parametrize("M,K,N,alpha,beta", [(13, 1028, 48, 1.0, 0.0), (5, 100, 16, 0.5, 1.0)])
+def test_p2_sgemm_fvb_any_reference_shape(pkg, orc, synth, cuda, M, K, N, alpha, beta):
+    """Every shape the reference's int8 path takes (N % 16 == 0, K % 4 == 0), not only the tensor-core ones."""
+    w = synth.five_value(K, N, seed=K + N)
+    A = synth.activations(M, K, seed=M)
+    C0 = np.random.default_rng(1).standard_normal((M, N)).astype(np.float32)
+    got = pkg.host_sgemm_fvb(A, w, C0.copy(), alpha=alpha, beta=beta)
+    want = orc.sgemm_i8(A, "int8w", C0.copy(), w=w, alpha=alpha, beta=beta)
+    assert _bits_equal(got, want)
+
+
 def test_strided_host_arrays(pkg, orc, synth, cuda):
     """lda > K and ldc > N, as the reference's row-major contract allows (csrc/blas.h:24-29)."""
     M, K, N = 40, 1024, 256

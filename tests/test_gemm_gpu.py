@@ -157,6 +157,78 @@ def test_quantiser_bitwise(pkg, orc, cuda, M, K):
     assert _bits_equal(s_d.cpu().numpy(), s)
 
 
+@pytest.mark.parametrize("K", [20, 1000, 1002, 1024, 4100])
+def test_quantiser_edge_rows_bitwise(pkg, orc, synth, cuda, K):
+    """Rows at the quantiser's edges (synth.quantiser_edge_rows): values whose reciprocal and division roundings
+    differ, in the 16-wide body and in the K % 16 tail that the reference divides (csrc/blas.c:1139-1143); a row whose
+    1 / scale overflows (the conversion saturates, NaN gives 0); zeros; ties. The register path (K % 4 == 0,
+    K <= 4096) and the strided path (K = 1002, 4100)."""
+    import torch
+    A = np.concatenate([synth.quantiser_edge_rows(K, seed=K), synth.activations(9, K, seed=K + 1)])
+    M = A.shape[0]
+    A_d = torch.from_numpy(A).to(cuda)
+    q_d = torch.empty((M, K), dtype=torch.int8, device=cuda)
+    s_d = torch.empty(M, dtype=torch.float32, device=cuda)
+    pkg.quant_rows(A_d.data_ptr(), M, K, K, q_d.data_ptr(), s_d.data_ptr())
+    pkg.check_device()
+    q, s = orc.quant_rows(A)
+    assert np.array_equal(q_d.cpu().numpy(), q)
+    assert _bits_equal(s_d.cpu().numpy(), s)
+
+
+# Shapes the reference's int8 path takes but the tensor-core kernels do not (N % 128 != 0, K % 16 != 0): the SIMT
+# kernel, bit for bit.
+RAGGED = [(13, 1028, 48, 1.0, 0.0), (77, 2056, 144, 0.5, 1.0), (130, 1024, 80, 1.0, 0.5), (3, 100, 16, 1.0, 0.0),
+          (40, 1000, 256, 1.0, 1.0)]
+
+
+@pytest.mark.parametrize("mode", ["int8w", "int8"])
+@pytest.mark.parametrize("M,K,N,alpha,beta", RAGGED)
+def test_ragged_shapes_bitwise(pkg, orc, synth, cuda, mode, M, K, N, alpha, beta):
+    import torch
+    w = synth.five_value(K, N, seed=M + K + N)
+    A = np.concatenate([synth.quantiser_edge_rows(K, seed=K)[:M], synth.activations(max(M - 8, 0), K, seed=M)])[:M]
+    C0 = np.random.default_rng(9).standard_normal((M, N)).astype(np.float32)
+    got = _run_fvb(pkg, torch, cuda, w, A, pkg.MODES[mode], alpha, beta, C0)
+    want = orc.sgemm_i8(A, mode, C0.copy(), w=w, alpha=alpha, beta=beta)
+    assert _bits_equal(got, want), _report(got, want)
+    if mode == "int8w":   # from the code cache
+        got = _run_fvb(pkg, torch, cuda, w, A, pkg.INT8W, alpha, beta, C0, codes=True)
+        assert _bits_equal(got, want), _report(got, want)
+
+
+@pytest.mark.parametrize("M,K,N", [(13, 1028, 48), (33, 1000, 640)])
+def test_ragged_int8_table_bitwise(pkg, orc, synth, cuda, M, K, N):
+    import torch
+    t = synth.int8_table(K, N, seed=3)
+    A = synth.activations(M, K, seed=4)
+    A_d = torch.from_numpy(A).to(cuda)
+    B_d = torch.from_numpy(t["q8"]).to(cuda)
+    s_d = torch.from_numpy(t["scales"]).to(cuda)
+    C_d = torch.zeros((M, N), dtype=torch.float32, device=cuda)
+    nws = max(pkg.workspace_bytes(M, N, K, pkg.INT8), 16)
+    ws = torch.empty(nws, dtype=torch.uint8, device=cuda)
+    pkg.sgemm_q8b(M, N, K, 1.0, A_d.data_ptr(), K, B_d.data_ptr(), s_d.data_ptr(), N, pkg.INT8, 0.0, C_d.data_ptr(),
+                  N, ws.data_ptr(), nws)
+    pkg.check_device()
+    want = orc.sgemm_i8(A, "q8b", np.zeros((M, N), np.float32), q8=t)
+    assert _bits_equal(C_d.cpu().numpy(), want), _report(C_d.cpu().numpy(), want)
+
+
+@pytest.mark.parametrize("mode", ["int8w", "int8"])
+def test_k_not_whole_quads_takes_the_exact_path(pkg, orc, synth, cuda, mode):
+    """The reference quantises only rows of whole quads: with K % 4 != 0 its p2_sgemm_fvb runs the exact path
+    (csrc/blas.c:1490-1498), and so does this one."""
+    import torch
+    M, K, N = 21, 1022, 128
+    w = synth.five_value(K, N, seed=5)
+    A = synth.activations(M, K, seed=6)
+    C0 = np.random.default_rng(7).standard_normal((M, N)).astype(np.float32)
+    got = _run_fvb(pkg, torch, cuda, w, A, pkg.MODES[mode], 1.0, 0.5, C0)
+    want = orc.gemm_exact(A, C0.copy(), w=w, alpha=1.0, beta=0.5)
+    assert _bits_equal(got, want), _report(got, want)
+
+
 @pytest.mark.parametrize("tA,tB", [(0, 0), (0, 1), (1, 0), (1, 1)])
 @pytest.mark.parametrize("M,N,K", [(375, 375, 128), (48, 749, 128), (100, 128, 375), (5, 7, 3)])
 def test_fp32_sgemm(pkg, orc, cuda, tA, tB, M, N, K):
