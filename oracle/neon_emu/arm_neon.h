@@ -1,15 +1,16 @@
-/* arm_neon.h - a portable C model of the AArch64 Advanced SIMD intrinsics that phonon-2-c's csrc/blas.c uses.
- * TEST INFRASTRUCTURE ONLY: oracle/Makefile puts this directory first on the include path when it compiles the
- * reference's own blas.c for an x86 host with __aarch64__, __ARM_NEON and __ARM_FEATURE_DOTPROD defined, so that
- * the reference's NEON and int8 dot-product code paths (csrc/blas.c:76-149, 1068-1447), which only an AArch64
- * toolchain compiles, run here and can be compared with the C restatement (oracle/fv_oracle.c) and, through it, with
- * the GPU kernels.
+/* arm_neon.h - a portable C model of the AArch64 Advanced SIMD intrinsics that phonon-2-c's csrc/blas.c,
+ * csrc/tensor_ops.c and csrc/encoder.c use.
+ * TEST INFRASTRUCTURE ONLY: oracle/Makefile puts this directory first on the include path when it compiles those
+ * reference files for an x86 host with __aarch64__, __ARM_NEON and __ARM_FEATURE_DOTPROD defined, so that the
+ * reference's NEON and int8 dot-product code paths (csrc/blas.c:76-149, 1068-1447; the NEON branches of
+ * csrc/tensor_ops.c and csrc/encoder.c), which only an AArch64 toolchain compiles, run here and can be compared with
+ * the C restatement (oracle/fv_oracle.c) and, through it, with the GPU kernels.
  *
  * Each function computes what the Arm architecture manual defines for the instruction behind the intrinsic (the
  * instruction is named beside each one), element by element, in plain C: integer lanes wrap or saturate as the
  * instruction says, FCVTNS rounds to nearest with ties to even and saturates, FMLA is fused (fmaf), FADDP adds
- * neighbouring pairs. Only the intrinsics csrc/blas.c calls are modelled. The vector types are GCC vector types, so the
- * reference's brace-initialised constants (csrc/blas.c:1192-1195) compile unchanged.
+ * neighbouring pairs. Only the intrinsics those three files call are modelled. The vector types are GCC vector
+ * types, so the reference's brace-initialised constants (csrc/blas.c:1192-1195) compile unchanged.
  */
 #ifndef P2_ORACLE_NEON_EMU_ARM_NEON_H
 #define P2_ORACLE_NEON_EMU_ARM_NEON_H
@@ -66,6 +67,7 @@ P2_NEON_CAST(vreinterpretq_s8_u8, int8x16_t, uint8x16_t)
 P2_NEON_CAST(vreinterpretq_u8_u32, uint8x16_t, uint32x4_t)
 P2_NEON_CAST(vreinterpretq_u8_u16, uint8x16_t, uint16x8_t)
 P2_NEON_CAST(vreinterpretq_s32_s8, int32x4_t, int8x16_t)
+P2_NEON_CAST(vreinterpretq_f32_s32, float32x4_t, int32x4_t)
 #undef P2_NEON_CAST
 
 P2_NEON_EMU int8x8_t vget_low_s8(int8x16_t a) { int8x8_t r; memcpy(&r, &a, 8); return r; }
@@ -145,8 +147,52 @@ P2_NEON_EMU int32x4_t vcvtnq_s32_f32(float32x4_t a)
     for (int i = 0; i < 4; i++) r[i] = p2_neon_emu_fcvtns(a[i]);
     return r;
 }
+/* FCVTZS: toward zero; NaN gives 0; out of range saturates. */
+P2_NEON_EMU int32x4_t vcvtq_s32_f32(float32x4_t a)
+{
+    int32x4_t r;
+    for (int i = 0; i < 4; i++) {
+        const float x = a[i];
+        r[i] = x != x ? 0 : x >= 2147483648.0f ? INT32_MAX : x <= -2147483648.0f ? INT32_MIN : (int32_t)x;
+    }
+    return r;
+}
 
-/* ---- fp32 arithmetic (FMUL, FSUB, FMLA, FABS, FMAX, FMAXV, FADDP) ---------------------------------------------- */
+/* ---- fp32 arithmetic (FADD, FMUL, FSUB, FDIV, FNEG, FMLA, FABS, FMAX, FMIN, FMAXV, FADDP, FRINTN) --------------- */
+P2_NEON_EMU float32x4_t vaddq_f32(float32x4_t a, float32x4_t b)
+{
+    float32x4_t r;
+    for (int i = 0; i < 4; i++) r[i] = a[i] + b[i];
+    return r;
+}
+P2_NEON_EMU float32x4_t vdivq_f32(float32x4_t a, float32x4_t b)
+{
+    float32x4_t r;
+    for (int i = 0; i < 4; i++) r[i] = a[i] / b[i];
+    return r;
+}
+/* FNEG flips the sign bit. */
+P2_NEON_EMU float32x4_t vnegq_f32(float32x4_t a)
+{
+    uint32x4_t u; memcpy(&u, &a, 16);
+    for (int i = 0; i < 4; i++) u[i] ^= 0x80000000u;
+    float32x4_t r; memcpy(&r, &u, 16);
+    return r;
+}
+/* FMLA by a scalar: a + b · s with one rounding. */
+P2_NEON_EMU float32x4_t vfmaq_n_f32(float32x4_t a, float32x4_t b, float s)
+{
+    float32x4_t r;
+    for (int i = 0; i < 4; i++) r[i] = fmaf(b[i], s, a[i]);
+    return r;
+}
+/* FRINTN: to an integral float, ties to even (the default rounding mode; nearbyintf raises no inexact flag). */
+P2_NEON_EMU float32x4_t vrndnq_f32(float32x4_t a)
+{
+    float32x4_t r;
+    for (int i = 0; i < 4; i++) r[i] = nearbyintf(a[i]);
+    return r;
+}
 P2_NEON_EMU float32x4_t vmulq_f32(float32x4_t a, float32x4_t b)
 {
     float32x4_t r;
@@ -194,6 +240,20 @@ P2_NEON_EMU float32x4_t vmaxq_f32(float32x4_t a, float32x4_t b)
     for (int i = 0; i < 4; i++) r[i] = p2_neon_emu_fmax(a[i], b[i]);
     return r;
 }
+/* FMIN: a NaN operand gives NaN; min(+0, −0) = −0. */
+P2_NEON_EMU float p2_neon_emu_fmin(float a, float b)
+{
+    if (a != a) return a;
+    if (b != b) return b;
+    if (a == 0.0f && b == 0.0f) return signbit(a) ? a : b;
+    return a < b ? a : b;
+}
+P2_NEON_EMU float32x4_t vminq_f32(float32x4_t a, float32x4_t b)
+{
+    float32x4_t r;
+    for (int i = 0; i < 4; i++) r[i] = p2_neon_emu_fmin(a[i], b[i]);
+    return r;
+}
 /* FMAXV over four lanes: max(max(a0, a1), max(a2, a3)). */
 P2_NEON_EMU float vmaxvq_f32(float32x4_t a)
 {
@@ -206,7 +266,20 @@ P2_NEON_EMU float vaddvq_f32(float32x4_t a)
     return s01 + s23;
 }
 
-/* ---- integer lane arithmetic and bit ops (SUB, NEG, MUL, AND, CMTST, BSL, USHL, TBL, SDOT) --------------------- */
+/* ---- integer lane arithmetic and bit ops (ADD, SHL, SUB, NEG, MUL, AND, CMTST, BSL, USHL, TBL, SDOT) ------------ */
+P2_NEON_EMU int32x4_t vaddq_s32(int32x4_t a, int32x4_t b)
+{
+    int32x4_t r;
+    for (int i = 0; i < 4; i++) r[i] = (int32_t)((uint32_t)a[i] + (uint32_t)b[i]);
+    return r;
+}
+/* SHL by an immediate: the low bits shifted out, as an unsigned shift. */
+P2_NEON_EMU int32x4_t vshlq_n_s32(int32x4_t a, int n)
+{
+    int32x4_t r;
+    for (int i = 0; i < 4; i++) r[i] = (int32_t)((uint32_t)a[i] << n);
+    return r;
+}
 P2_NEON_EMU int8x16_t vsubq_s8(int8x16_t a, int8x16_t b)
 {
     int8x16_t r;

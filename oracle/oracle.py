@@ -335,6 +335,25 @@ def neon_fv_pack_codes(L, w) -> np.ndarray:
     return raw.reshape(N // 16, K // 4, 16, 4).transpose(1, 3, 0, 2).reshape(K, N)
 
 
+def ref_neon_encoder(model_struct, mel: np.ndarray, mode: str = "int8w") -> np.ndarray:
+    """phonon-2-c's p2_encoder as its AArch64 build runs it (the NEON branches of csrc/encoder.c and csrc/tensor_ops.c,
+    the int8 GEMMs of csrc/blas.c; compiled here through oracle/neon_emu), in GEMM mode `mode`: [T', 640]."""
+    L = ref_neon(mode)
+    if not hasattr(L, "_enc_ready"):
+        L.p2_encoder.argtypes = [C.c_void_p, _f32p, C.c_int, C.POINTER(C.c_void_p), C.POINTER(C.c_int)]
+        L.p2_encoder.restype = C.c_int
+        C.c_int.in_dll(L, "p2_verbose").value = 0
+        L._enc_ready = True
+    mel = np.ascontiguousarray(mel, np.float32)
+    out, n = C.c_void_p(), C.c_int()
+    if L.p2_encoder(C.addressof(model_struct), mel, mel.shape[0], C.byref(out), C.byref(n)) != 0:
+        raise RuntimeError("reference p2_encoder (AArch64 build) failed")
+    try:
+        return np.ctypeslib.as_array(C.cast(out, C.POINTER(C.c_float)), shape=(n.value, 640)).copy()
+    finally:
+        _libc.free(out)
+
+
 def _encoder_lib(path):
     L = C.CDLL(str(path))
     L.p2_encoder.argtypes = [C.c_void_p, _f32p, C.c_int, C.POINTER(C.c_void_p), C.POINTER(C.c_int)]

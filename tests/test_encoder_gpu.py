@@ -3,7 +3,8 @@
 Oracles: exact mode is phonon-2-c's p2_encoder compiled from its sources (oracle/_ref/libphonon2_ref.so, whose x86
 build is the exact path); the int8 modes are the same encoder sources with the int8 GEMM entry points restated
 (oracle/_ref/libphonon2_ref_i8.so), so the reference's int8 control flow - rows quantised as they are produced,
-residuals added in the GEMM epilogues - runs on x86.
+residuals added in the GEMM epilogues - runs on x86; and, where it is built, the reference's own AArch64 build of
+the encoder and its int8 GEMMs (oracle/_ref/libphonon2_ref_neon.so, through oracle/neon_emu).
 
 Tolerances. The five-value GEMMs are bit-exact (tests/test_gemm_gpu.py); the encoder as a whole cannot be, because the
 compiled reference's LayerNorm takes 1/sqrt from an approximate reciprocal square root refined by one Newton step and
@@ -168,6 +169,12 @@ def test_encoder_int8_matches_reference_control_flow(pkg, orc, cuda, model, dev_
     assert noise < 0.1
     assert _rel(got, ref) <= 2 * noise and _rel(got, exact) <= 2 * noise
     assert np.corrcoef(got.ravel(), ref.ravel())[0, 1] > 0.999
+    if orc.ref_neon_available():   # the reference's own AArch64 int8 encoder (oracle/neon_emu), within the same envelope
+        arm = orc.ref_neon_encoder(model.struct, mel, mode)
+        print(f"{mode}: device vs the reference's AArch64 build {_rel(got, arm):.3e}, "
+              f"corr {np.corrcoef(got.ravel(), arm.ravel())[0, 1]:.6f}")
+        assert _rel(got, arm) <= 2 * noise
+        assert np.corrcoef(got.ravel(), arm.ravel())[0, 1] > 0.999
 
 
 @pytest.mark.parametrize("mode", ["int8w", "exact"])

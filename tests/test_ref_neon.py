@@ -189,3 +189,45 @@ def test_exact_path_is_the_same_on_both_isas(neon, synth, M, K, N, alpha, beta):
     arm = neon.neon_sgemm_fvb(neon.ref_neon("exact"), A, w, C0.copy(), alpha=alpha, beta=beta)
     assert _bits_equal(arm, x86)
     assert _bits_equal(arm, neon.gemm_exact(A, C0.copy(), w=w, alpha=alpha, beta=beta))
+
+
+# ---- the encoder as the reference's AArch64 build runs it ----------------------------------------------------------
+
+@pytest.fixture(scope="module")
+def enc_model(pkg):
+    from phonon2_b200 import model as M
+    return M.SyntheticModel(seed=7)
+
+
+def _rel(a, b):
+    return float(np.abs(a - b).max() / np.abs(b).max())
+
+
+def test_aarch64_encoder_exact_mode_matches_x86_build(neon, enc_model):
+    """p2_encoder in exact mode through the reference's NEON branches (LayerNorm, softmax, the polynomial exp, SiLU,
+    the depthwise convolution; csrc/tensor_ops.c, csrc/encoder.c) against its x86 build, which the device encoder's
+    exact-mode tests use: within the same 1e-4 of the largest output."""
+    from phonon2_b200 import model as M
+    mel = M.mel(300, seed=11)
+    arm = neon.ref_neon_encoder(enc_model.struct, mel, "exact")
+    x86 = neon.ref_encoder(enc_model.struct, mel, "exact")
+    assert arm.shape == (38, 640)
+    assert _rel(arm, x86) <= 1e-4
+
+
+@pytest.mark.parametrize("mode", ["int8w", "int8"])
+def test_aarch64_int8_encoder_is_within_the_envelope_of_the_int8_oracle(neon, enc_model, mode):
+    """The device's int8 encoder is tested against the reference's encoder sources run with the restated int8 GEMMs
+    on their x86 branches (libphonon2_ref_i8.so): within twice that oracle's distance from exact mode, correlation
+    above 0.999. The reference's own AArch64 int8 encoder - its NEON branches and its int8 GEMMs - is a second valid
+    int8 encoder, and it meets the same criterion against that oracle (measured: 1.2-1.45 times the distance,
+    correlation 0.9993-0.9994): an ulp before a quantiser flips a code, and 24 blocks carry such flips."""
+    from phonon2_b200 import model as M
+    mel = M.mel(300, seed=11)
+    arm = neon.ref_neon_encoder(enc_model.struct, mel, mode)
+    oracle = neon.ref_encoder(enc_model.struct, mel, mode)
+    exact = neon.ref_encoder(enc_model.struct, mel, "exact")
+    noise = _rel(oracle, exact)
+    assert 1e-3 < noise < 0.1
+    assert _rel(arm, oracle) <= 2 * noise and _rel(arm, exact) <= 2 * noise
+    assert np.corrcoef(arm.ravel(), oracle.ravel())[0, 1] > 0.999
