@@ -80,7 +80,7 @@ P2CU_API int p2cu_sgemm_q8b_q8a(int M, int N, int K, float alpha, const signed c
 P2CU_API size_t p2cu_q8a_workspace_bytes(int M, int N, int K);
 
 /* Workspace bytes of p2cu_sgemm_fvb / p2cu_sgemm_q8b: the quantised activations plus the K-block slices
- * (0 in exact mode). */
+ * (0 in exact mode, and when K % 4 != 0, which runs the exact path). */
 P2CU_API size_t p2cu_gemm_workspace_bytes(int M, int N, int K, int mode);
 
 /* C = alpha * A * B + beta * C from fp32 A (csrc/blas.c:1481-1499 / 1462-1479): in the int8 modes A is quantised
@@ -244,6 +244,11 @@ P2CU_API int p2cu_probe_tma_load(int warps, int box_rows, double *bytes_per_s_pe
  * back through barriers as in the pair GEMM, without copies: mode 0 no hand-back after the first round, mode 1
  * through a producer arrive and the odd CTA's relay, mode 2 with the odd CTA arriving on the even CTA's barrier. */
 P2CU_API int p2cu_probe_int8_ring(int mode, int iters, double *macs_per_s);
+/* p2cu_probe_wait_timeout: the kernels' bounded-wait path, exercised without a fault - one warp waits on an mbarrier
+ * phase that nothing completes, gives up after `limit` polls (1 .. 2^20), records code 1 in the device error word and
+ * returns; `seconds` is the launch's duration. Returns what p2cu_check_device then returns: P2CU_EDEVICE (the word is
+ * cleared, the context stays usable). No counterpart in the reference (its CPU loops have no waits to bound). */
+P2CU_API int p2cu_probe_wait_timeout(unsigned limit, double *seconds);
 
 #ifdef __cplusplus
 }

@@ -104,6 +104,7 @@ SIGNATURES = {
     "p2cu_probe_int8_mma": (_i, [_i, _i, C.POINTER(C.c_double)]),
     "p2cu_probe_tma_load": (_i, [_i, _i, C.POINTER(C.c_double)]),
     "p2cu_probe_int8_ring": (_i, [_i, _i, C.POINTER(C.c_double)]),
+    "p2cu_probe_wait_timeout": (_i, [C.c_uint, C.POINTER(C.c_double)]),
     # include/phonon2.h: the reference's encoder and decoder entry points
     "p2_encoder": (_i, [_vp, _vp, _i, C.POINTER(_vp), C.POINTER(_i)]),
     "p2_encoder_chunked": (_i, [_vp, _vp, _i, C.POINTER(_vp), C.POINTER(_i)]),

@@ -425,7 +425,7 @@ size_t p2cu_q8a_workspace_bytes(int M, int N, int K) {
 }
 
 size_t p2cu_gemm_workspace_bytes(int M, int N, int K, int mode) {
-    if (mode == P2CU_EXACT || M <= 0 || K <= 0 || N <= 0) return 0;
+    if (mode == P2CU_EXACT || K % 4 || M <= 0 || K <= 0 || N <= 0) return 0;   // K % 4 != 0 runs the exact path
     return round256(static_cast<size_t>(M) * K) + round256(static_cast<size_t>(M) * sizeof(float)) +
            split_bytes(M, N, K);
 }

@@ -49,11 +49,11 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 }
 
 // Wait for the phase of `bar` with the given parity to complete. Returns false (after recording `code` in *err and
-// setting *abort) when the limit runs out or another role already aborted.
+// setting *abort) when `limit` polls run out or another role already aborted.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t code,
-                                          uint32_t* err, volatile int* abort_flag) {
+                                          uint32_t* err, volatile int* abort_flag, uint32_t limit = WAIT_LIMIT) {
     const uint32_t a = smem_u32(bar);
-    for (uint32_t i = 0; i < WAIT_LIMIT; ++i) {
+    for (uint32_t i = 0; i < limit; ++i) {
         if (mbar_try_wait(a, parity)) return true;
         if ((i & 1023u) == 1023u && *abort_flag) return false;
     }

@@ -43,6 +43,7 @@ GEMM_CASES = [
     ("int8_fvb_9x4096x64", "int8", 9, 4096, 64, 0.5, 1.0, 108, 208, False),
     ("int8_fvb_13x1028x48", "int8", 13, 1028, 48, 1.0, 0.25, 109, 209, True),
     ("int8_q8b_7x2048x128", "q8b", 7, 2048, 128, 1.0, 0.0, 110, 210, False),
+    ("int8w_fvb_5x1022x48", "int8w", 5, 1022, 48, 1.0, 0.5, 111, 211, False),   # K % 4 != 0: the exact path
 ]
 QUANT_K = (20, 1024, 1028)
 CODES = ((256, 128), (64, 48))

@@ -393,3 +393,23 @@ def test_persistent_kernel_bitwise(cuda, persist, tile, pair):
                          text=True, timeout=600)
     assert out.returncode == 0, out.stderr[-3000:]
     assert json.loads(out.stdout.strip().splitlines()[-1]) == [True] * 7
+
+
+def test_device_wait_timeout_is_reported_and_the_context_survives(pkg, orc, synth, cuda):
+    """Failure detection without a fault: a kernel waits, through the GEMM kernels' own bounded wait, on a barrier
+    that nothing completes; the wait gives up after 4096 polls, the kernel records code 1 (DEV_TIMEOUT_FULL) in the
+    device error word and returns; p2cu_check_device reports it as P2CU_EDEVICE and clears the word; the next GEMM on
+    the same context is still bit for bit the oracle's."""
+    import ctypes as C
+    import torch
+    secs = C.c_double()
+    rc = pkg.lib().p2cu_probe_wait_timeout(4096, C.byref(secs))
+    assert rc == pkg.P2CU_EDEVICE, pkg.last_error()
+    assert "device error code 1" in pkg.last_error()
+    assert 0.0 < secs.value < 2.0
+    pkg.check_device()   # cleared
+    M, K, N = 77, 1024, 256
+    w = synth.five_value(K, N, seed=1)
+    A = synth.activations(M, K, seed=2)
+    got = _run_fvb(pkg, torch, cuda, w, A, pkg.INT8W, 1.0, 0.0, np.zeros((M, N), np.float32))
+    assert _bits_equal(got, orc.sgemm_i8(A, "int8w", np.zeros((M, N), np.float32), w=w))

@@ -27,7 +27,7 @@ def test_gemm_restatement_matches_golden(orc, synth, golden, case):
     name, mode, M, K, N, alpha, beta, wseed, aseed, edge = case
     w, A, C0 = mg.gemm_inputs(synth, mode, M, K, N, wseed, aseed, edge)
     assert list(golden[f"{name}/sha"]) == [mg.weight_sha(w), mg.sha(A), mg.sha(C0)], "regenerated inputs drifted"
-    if mode == "exact":
+    if mode == "exact" or K % 4:   # the reference quantises only whole quads; other K run its exact path
         got = orc.gemm_exact(A, C0.copy(), w=w, alpha=alpha, beta=beta)
     elif mode == "q8b":
         got = orc.sgemm_i8(A, "q8b", C0.copy(), q8=w, alpha=alpha, beta=beta)
