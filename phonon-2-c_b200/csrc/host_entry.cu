@@ -461,6 +461,11 @@ FeedEncoder feed_host_audio(const float* audio, const long long* n_samples, int 
 // The window checks, the sharding over GPUs and one host thread per GPU, shared by the batched entry points: `after`
 // runs on every plan's output. The reference's chunking rule applies per window (csrc/encoder.c:715-723): windows it
 // would chunk go in a plan of their own on the same GPU.
+// A GPU whose share fails (a CUDA error, a kernel that reported a timeout, no memory) hands the share to a GPU whose
+// share succeeded, which runs it after its own; every window's result depends on the window alone, so the output is
+// the same. The call fails only when no GPU succeeded or the second attempt fails too. For tests, P2_B200_FAIL_SLOT=i
+// makes the share at position i of the device list report a failure before it runs anything (a host-side fault; no
+// GPU is disturbed).
 int run_windows(const char* who, const P2Model* m, const int* n_frames, int n_windows, const int* devices,
                 int n_devices, const FeedEncoder& feed, const AfterEncode& after) {
     std::vector<int> devs;
@@ -488,27 +493,55 @@ int run_windows(const char* who, const P2Model* m, const int* n_frames, int n_wi
     int prev = 0;
     cudaGetDevice(&prev);
     const auto shards = shard_windows(n_frames, n_windows, static_cast<int>(devs.size()));
+    int fail_slot = -1;
+    if (const char* fs = getenv("P2_B200_FAIL_SLOT")) {
+        char* end;
+        const long v = strtol(fs, &end, 10);
+        if (*fs && *end == '\0' && v >= 0 && v < 64) fail_slot = static_cast<int>(v);
+    }
+    auto run_share = [&](const std::vector<int>& share, int device, std::string* err) {
+        std::vector<int> plain, chunked;
+        for (int w : share) (should_chunk(conv3(n_frames[w])) ? chunked : plain).push_back(w);
+        int rc = encode_on_device(m, device, plain, n_frames, 0, 0, feed, after, err);
+        if (rc == 0) rc = encode_on_device(m, device, chunked, n_frames, chunk, overlap, feed, after, err);
+        return rc;
+    };
     // The same GPU may appear twice in `devices`: its shares then run one after the other (the slot's mutex).
     std::vector<std::string> errs(devs.size());
     std::vector<int> rcs(devs.size(), 0);
     std::vector<std::thread> threads;
     for (size_t i = 0; i < devs.size(); ++i) {
         threads.emplace_back([&, i] {
-            std::vector<int> plain, chunked;
-            for (int w : shards[i]) (should_chunk(conv3(n_frames[w])) ? chunked : plain).push_back(w);
-            rcs[i] = encode_on_device(m, devs[i], plain, n_frames, 0, 0, feed, after, &errs[i]);
-            if (rcs[i] == 0)
-                rcs[i] = encode_on_device(m, devs[i], chunked, n_frames, chunk, overlap, feed, after, &errs[i]);
+            if (static_cast<int>(i) == fail_slot && !shards[i].empty()) {
+                errs[i] = "failure injected by P2_B200_FAIL_SLOT";
+                rcs[i] = -1;
+                return;
+            }
+            rcs[i] = run_share(shards[i], devs[i], &errs[i]);
         });
     }
     for (auto& t : threads) t.join();
-    cudaSetDevice(prev);
+    std::vector<size_t> healthy;
     for (size_t i = 0; i < devs.size(); ++i)
-        if (rcs[i]) {
-            fprintf(stderr, "%s: GPU %d: %s\n", who, devs[i], errs[i].c_str());
-            return -1;
+        if (rcs[i] == 0) healthy.push_back(i);
+    int rc = 0;
+    for (size_t i = 0, k = 0; i < devs.size() && rc == 0; ++i) {
+        if (rcs[i] == 0) continue;
+        fprintf(stderr, "%s: GPU %d: %s\n", who, devs[i], errs[i].c_str());
+        if (healthy.empty()) {
+            rc = -1;
+            break;
         }
-    return 0;
+        const size_t j = healthy[k++ % healthy.size()];
+        fprintf(stderr, "%s: GPU %d's %zu window(s) re-run on GPU %d\n", who, devs[i], shards[i].size(), devs[j]);
+        std::string err;
+        if (run_share(shards[i], devs[j], &err) != 0) {
+            fprintf(stderr, "%s: GPU %d: %s\n", who, devs[j], err.c_str());
+            rc = -1;
+        }
+    }
+    cudaSetDevice(prev);
+    return rc;
 }
 
 }  // namespace
@@ -583,6 +616,8 @@ AfterEncode decode_after(P2Token** tokens, int* n_tokens, int* enc_frames) {
             }
             for (int i = 0; i < gn; ++i) {
                 const int n = offs[i + 1] - offs[i], w = wins[g0 + i];
+                free(tokens[w]);   // a share re-run after a failed attempt replaces what that attempt wrote
+                tokens[w] = nullptr;
                 n_tokens[w] = n;
                 if (n == 0) continue;
                 tokens[w] = static_cast<P2Token*>(malloc(static_cast<size_t>(n) * sizeof(P2Token)));

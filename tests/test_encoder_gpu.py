@@ -217,6 +217,25 @@ def test_encoder_argument_errors(pkg, cuda, dev_model):
         pkg.Encoder(dev_model, [300], 7)
 
 
+def test_failed_gpu_share_is_rerun_on_another(pkg, cuda, model, monkeypatch):
+    """Failure detection on the host, no GPU disturbed: P2_B200_FAIL_SLOT=0 makes the first GPU's share report a
+    failure before it runs anything; the batched entry points hand its windows to the other GPU of the list (GPU 0
+    named twice: two host threads), and every window's frames and tokens equal those of a run without the failure, bit
+    for bit. With one GPU listed, no GPU is left to take the share over and the call fails."""
+    from phonon2_b200 import model as M
+    mels = [M.mel(n, seed=n) for n in (300, 251, 333, 17)]
+    want = pkg.host_encode_windows(model.struct, mels, devices=[0, 0])
+    want_tok = pkg.host_transcribe_windows(model.struct, mels, devices=[0, 0])
+    monkeypatch.setenv("P2_B200_FAIL_SLOT", "0")
+    got = pkg.host_encode_windows(model.struct, mels, devices=[0, 0])
+    for g, w in zip(got, want):
+        assert np.array_equal(g.view(np.uint32), w.view(np.uint32))
+    got_tok = pkg.host_transcribe_windows(model.struct, mels, devices=[0, 0])
+    assert all(np.array_equal(g, w) for g, w in zip(got_tok, want_tok))
+    with pytest.raises(pkg.Error):
+        pkg.host_encode_windows(model.struct, mels, devices=[0])
+
+
 def test_encode_windows_spread_over_devices(pkg, cuda, model):
     """p2_b200_encode_windows gives every window exactly what p2_encoder gives it. The device list names GPU 0 twice,
     so the sharding, the per-GPU threads and the per-GPU plan cache run on a one-GPU box too."""
