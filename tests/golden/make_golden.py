@@ -16,6 +16,9 @@ stored beside the outputs so that a reader can tell regenerated inputs from drif
                   quantiser cases ``quant<K>/q``, ``/scales``; int8w code planes ``codes<K>x<N>``.
   * encoder.npz - p2_encoder's [T', 640] output on a 3 s synthetic log-mel (300 frames) with SyntheticModel(seed=7),
                   exact (x86 build) and int8w / int8 (AArch64 build).
+  * decoder.npz - with the same model: p2_joint's 8198 logits for two (encoder frame, decoder output) pairs, and
+                  p2_greedy_decode's tokens (id, frame, duration) over N(0, 1) frames of 38 and 375 rows.
+  * mel.npz     - p2_mel_spectrogram's [100, 128] features of 1 s of synthetic speech (model.audio).
 """
 from __future__ import annotations
 
@@ -48,6 +51,8 @@ GEMM_CASES = [
 QUANT_K = (20, 1024, 1028)
 CODES = ((256, 128), (64, 48))
 ENCODER_SEED, ENCODER_MEL_FRAMES, ENCODER_MEL_SEED = 7, 300, 11
+DECODE_T = (38, 375)
+MEL_SAMPLES = 16000
 
 
 def sha(*arrays) -> str:
@@ -75,6 +80,23 @@ def weight_sha(w) -> str:
 
 def quant_input(synth, K):
     return np.concatenate([synth.quantiser_edge_rows(K, seed=K), synth.activations(8, K, seed=K + 1)])
+
+
+def joint_inputs():
+    """Two (encoder frame, decoder output) pairs; the second's first 40 products cancel exactly."""
+    rng = np.random.default_rng(3)
+    pairs = []
+    for i in range(2):
+        enc = rng.standard_normal(640, dtype=np.float32)
+        dec = (rng.standard_normal(640) * 0.5).astype(np.float32)
+        if i == 1:
+            dec[:40] = -enc[:40]
+        pairs.append((enc, dec))
+    return pairs
+
+
+def decode_frames(T):
+    return np.random.default_rng(T).standard_normal((T, 640), dtype=np.float32)
 
 
 def main() -> None:
@@ -115,7 +137,18 @@ def main() -> None:
          "int8": orc.ref_neon_encoder(model.struct, mel, "int8"),
          "sha": np.array([sha(*(model.arrays[k] for k in sorted(model.arrays))), sha(mel)])}
     np.savez_compressed(HERE / "encoder.npz", **e)
-    print("wrote", HERE / "gemm.npz", HERE / "encoder.npz")
+
+    d = {"joint": np.stack([orc.ref_joint(model.struct, enc, dec) for enc, dec in joint_inputs()]),
+         "joint/sha": np.array([sha(*(a for pair in joint_inputs() for a in pair))])}
+    for T in DECODE_T:
+        frames = decode_frames(T)
+        d[f"tokens{T}"] = orc.ref_greedy_decode(model.struct, frames)
+        d[f"tokens{T}/sha"] = np.array([sha(frames)])
+    np.savez_compressed(HERE / "decoder.npz", **d)
+
+    audio = M.audio(MEL_SAMPLES, seed=MEL_SAMPLES)
+    np.savez_compressed(HERE / "mel.npz", mel=orc.ref_mel_spectrogram(audio), sha=np.array([sha(audio)]))
+    print("wrote", *(HERE / f for f in ("gemm.npz", "encoder.npz", "decoder.npz", "mel.npz")))
 
 
 if __name__ == "__main__":

@@ -63,3 +63,17 @@ def test_encoder_golden_inputs_regenerate(pkg):
     mel = M.mel(mg.ENCODER_MEL_FRAMES, seed=mg.ENCODER_MEL_SEED)
     assert stored == [mg.sha(*(model.arrays[k] for k in sorted(model.arrays))), mg.sha(mel)]
     assert shapes == [(M.frames_after_subsampling(mg.ENCODER_MEL_FRAMES), 640)] * 3
+
+
+def test_decoder_and_mel_golden_inputs_regenerate(pkg):
+    """The decoder and log-mel vectors' inputs regenerate from their seeds (tests/test_golden_gpu.py compares the
+    device's decoder and front end with them)."""
+    from phonon2_b200 import model as M
+    with np.load(GOLDEN / "decoder.npz") as z:
+        assert z["joint/sha"][0] == mg.sha(*(a for pair in mg.joint_inputs() for a in pair))
+        for T in mg.DECODE_T:
+            assert z[f"tokens{T}/sha"][0] == mg.sha(mg.decode_frames(T))
+            assert z[f"tokens{T}"].shape[1] == 3 and len(z[f"tokens{T}"]) > 0
+    with np.load(GOLDEN / "mel.npz") as z:
+        assert z["sha"][0] == mg.sha(M.audio(mg.MEL_SAMPLES, seed=mg.MEL_SAMPLES))
+        assert z["mel"].shape == (mg.MEL_SAMPLES // 160, 128)

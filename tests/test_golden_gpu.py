@@ -2,7 +2,8 @@
 from the reference's x86 build and its AArch64 int8 code), with no oracle in the loop: the GEMMs, the quantiser and
 the int8w code plane bit for bit; the encoder in exact mode within 1e-4 of the largest output, and in the int8 modes
 within the statistical envelope of the encoder tests (twice the reference's own int8-vs-exact distance, correlation
-above 0.999; see tests/test_encoder_gpu.py)."""
+above 0.999; see tests/test_encoder_gpu.py); the decoder's joint logits bit for bit and its greedy tokens equal; the
+log-mel features within 1e-4 absolute."""
 import sys
 from pathlib import Path
 
@@ -101,3 +102,38 @@ def test_device_encoder_matches_golden(pkg, cuda):
         assert 1e-3 < noise < 0.1
         assert _rel(out[mode], gold[mode]) <= 2 * noise
         assert np.corrcoef(out[mode].ravel(), gold[mode].ravel())[0, 1] > 0.999
+
+
+@pytest.fixture(scope="module")
+def model7(pkg):
+    from phonon2_b200 import model as M
+    return M.SyntheticModel(seed=mg.ENCODER_SEED)
+
+
+def test_device_joint_matches_golden(pkg, cuda, model7):
+    """p2_joint bit for bit: the dot products in the reference's order (csrc/tensor_ops.c:66-96)."""
+    with np.load(GOLDEN / "decoder.npz") as z:
+        want = z["joint"]
+    for i, (enc, dec) in enumerate(mg.joint_inputs()):
+        got = np.zeros(8198, np.float32)
+        pkg.host_joint(model7.struct, enc, dec, got)
+        assert _bits_equal(got, want[i])
+
+
+@pytest.mark.parametrize("T", mg.DECODE_T)
+def test_device_greedy_decode_matches_golden(pkg, cuda, model7, T):
+    """p2_greedy_decode: the same tokens (id, frame, duration) as the reference's."""
+    with np.load(GOLDEN / "decoder.npz") as z:
+        want = z[f"tokens{T}"]
+    assert np.array_equal(pkg.host_greedy_decode(model7.struct, mg.decode_frames(T)), want)
+
+
+def test_device_mel_matches_golden(pkg, cuda):
+    """p2_mel_spectrogram within 1e-4 (absolute, on features normalised to unit variance) of the reference's."""
+    from phonon2_b200 import model as M
+    with np.load(GOLDEN / "mel.npz") as z:
+        want = z["mel"]
+    got = pkg.host_mel_spectrogram(M.audio(mg.MEL_SAMPLES, seed=mg.MEL_SAMPLES))
+    err = np.abs(got - want)
+    print(f"mel: max |device - golden| {err.max():.2e}, median {np.median(err):.2e}")
+    assert got.shape == want.shape and err.max() <= 1e-4 and np.median(err) <= 2e-5
