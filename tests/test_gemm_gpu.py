@@ -252,18 +252,24 @@ def test_fp32_sgemm(pkg, orc, cuda, tA, tB, M, N, K):
         assert _bits_equal(got, want), _report(got, want)
 
 
-def test_contract_errors(pkg, synth, cuda):
+def test_contract_errors(pkg, orc, synth, cuda):
     import torch
     from phonon2_b200.device import DeviceFiveValue
     w = synth.five_value(256, 144, seed=1)                  # N % 16 == 0 but not % 128: no tensor-core tile
     B = DeviceFiveValue(w, cuda)
-    A_d = torch.zeros((8, 256), device=cuda)
+    A = synth.activations(8, 256, seed=2)
+    A_d = torch.from_numpy(A).to(cuda)
     C_d = torch.zeros((8, 144), device=cuda)
     ws = torch.empty(1 << 16, dtype=torch.uint8, device=cuda)
-    with pytest.raises(pkg.Error) as e:
-        pkg.sgemm_fvb(8, 144, 256, 1.0, A_d.data_ptr(), 256, B.struct, pkg.INT8W, 0.0, C_d.data_ptr(), 144,
+    # the reference takes this shape, and so does the SIMT kernel
+    pkg.sgemm_fvb(8, 144, 256, 1.0, A_d.data_ptr(), 256, B.struct, pkg.INT8W, 0.0, C_d.data_ptr(), 144,
+                  ws.data_ptr(), ws.numel())
+    pkg.check_device()
+    assert _bits_equal(C_d.cpu().numpy(), orc.sgemm_i8(A, "int8w", np.zeros((8, 144), np.float32), w=w))
+    with pytest.raises(pkg.Error) as e:                     # N not a multiple of 16, as the reference refuses it
+        pkg.sgemm_fvb(8, 136, 256, 1.0, A_d.data_ptr(), 256, B.struct, pkg.INT8W, 0.0, C_d.data_ptr(), 144,
                       ws.data_ptr(), ws.numel())
-    assert e.value.code == pkg.P2CU_EUNSUPPORTED
+    assert e.value.code == pkg.P2CU_EINVAL
     with pytest.raises(pkg.Error) as e:                     # workspace too small
         pkg.sgemm_fvb(8, 144, 256, 1.0, A_d.data_ptr(), 256, B.struct, pkg.INT8W, 0.0, C_d.data_ptr(), 144,
                       ws.data_ptr(), 10)
