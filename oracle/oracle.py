@@ -14,6 +14,7 @@ Only tests/, ``__graft_entry__.smoke()`` and bench.py's CPU legs import this mod
 """
 from __future__ import annotations
 
+import atexit
 import ctypes as C
 import os
 import shutil
@@ -224,7 +225,9 @@ def ref_neon(mode: str, fast_math: bool = False) -> C.CDLL:
     src = REF_NEON_FM_SO if fast_math else REF_NEON_SO
     if not src.exists():
         raise RuntimeError(f"{src} is not built (needs the reference sources; run __graft_entry__.build())")
-    copy = Path(tempfile.mkdtemp(prefix="p2_ref_neon_")) / f"{src.stem}_{mode}.so"
+    tmp = tempfile.mkdtemp(prefix="p2_ref_neon_")
+    atexit.register(shutil.rmtree, tmp, True)   # the mapping stays valid after the file is unlinked
+    copy = Path(tmp) / f"{src.stem}_{mode}.so"
     shutil.copyfile(src, copy)
     saved = {k: os.environ.get(k) for k in ("P2_GEMM", "P2_EXACT")}
     os.environ["P2_GEMM"] = mode
