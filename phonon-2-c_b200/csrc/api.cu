@@ -454,7 +454,7 @@ int p2cu_sgemm_fvb(int M, int N, int K, float alpha, const float* A, int lda, co
         return run_exact(M, N, K, alpha, A, lda, 0, B, nullptr, nullptr, nullptr, 0, 0, beta, C, ldc, s,
                          "p2cu_sgemm_fvb");
     if (mode != P2CU_INT8 && mode != P2CU_INT8W) return fail(P2CU_EINVAL, "p2cu_sgemm_fvb: mode %d", mode);
-    if (K % 4)   // the reference quantises only rows of whole quads; other K take its exact path (csrc/blas.c:1490-1495)
+    if (K % 4)   // the reference quantises only whole quads; other K take its exact path (csrc/blas.c:1490-1495)
         return run_exact(M, N, K, alpha, A, lda, 0, B, nullptr, nullptr, nullptr, 0, 0, beta, C, ldc, s,
                          "p2cu_sgemm_fvb");
     int rc = check_gemm_common(M, N, K, C, ldc, "p2cu_sgemm_fvb");

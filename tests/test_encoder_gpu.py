@@ -169,7 +169,7 @@ def test_encoder_int8_matches_reference_control_flow(pkg, orc, cuda, model, dev_
     assert noise < 0.1
     assert _rel(got, ref) <= 2 * noise and _rel(got, exact) <= 2 * noise
     assert np.corrcoef(got.ravel(), ref.ravel())[0, 1] > 0.999
-    if orc.ref_neon_available():   # the reference's own AArch64 int8 encoder (oracle/neon_emu), within the same envelope
+    if orc.ref_neon_available():   # the reference's own AArch64 int8 encoder (oracle/neon_emu), same envelope
         arm = orc.ref_neon_encoder(model.struct, mel, mode)
         print(f"{mode}: device vs the reference's AArch64 build {_rel(got, arm):.3e}, "
               f"corr {np.corrcoef(got.ravel(), arm.ravel())[0, 1]:.6f}")
