@@ -177,6 +177,27 @@ def test_encoder_int8_matches_reference_control_flow(pkg, orc, cuda, model, dev_
         assert np.corrcoef(got.ravel(), arm.ravel())[0, 1] > 0.999
 
 
+def test_encoder_int8w_config2_window(pkg, orc, cuda, model, dev_model):
+    """The same statistical parity at BASELINE config 2 (a 30 s window: 3000 mel frames, T' = 375), int8w, against
+    both int8 oracles: the restated-GEMM control flow and the reference's own AArch64 build."""
+    import torch
+    from phonon2_b200 import model as M
+    mel = M.mel(3000, seed=12)
+    got, = _run(pkg, torch, dev_model, [mel], pkg.INT8W)
+    exact = orc.ref_encoder(model.struct, mel, "exact")
+    refs = [orc.ref_encoder(model.struct, mel, "int8w")]
+    if orc.ref_neon_available():
+        refs.append(orc.ref_neon_encoder(model.struct, mel, "int8w"))
+    noise = _rel(refs[0], exact)
+    assert got.shape == (375, 640) and 1e-3 < noise < 0.1
+    assert _rel(got, exact) <= 2 * noise
+    for ref in refs:
+        print(f"T'=375 int8w: device vs reference {_rel(got, ref):.3e} (noise {noise:.3e}), "
+              f"corr {np.corrcoef(got.ravel(), ref.ravel())[0, 1]:.6f}")
+        assert _rel(got, ref) <= 2 * noise
+        assert np.corrcoef(got.ravel(), ref.ravel())[0, 1] > 0.999
+
+
 @pytest.mark.parametrize("mode", ["int8w", "exact"])
 def test_windows_batched_equal_windows_alone(pkg, cuda, dev_model, mode):
     import torch
