@@ -181,14 +181,19 @@ fv_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                         tma_load_2d(b_tile(s) + a * G::REGION, &tmB0, &full[s], n0 + a * G::ATOM_W, kx);
                 }
             };
+            // The stages are empty at the start (kb < pre). This warp's first stage's weights load before the
+            // dependency wait; those of its later first-round stages follow its first A tile, because a warp's TMA
+            // loads complete one after another and the first MMA must not queue behind weights it does not need.
             const int pre = nk < STAGES ? nk : STAGES;
-            for (int kb = pw; kb < pre; kb += G::NPROD) load_b(kb);   // the stages are empty at the start
+            if (pw < pre) load_b(pw);
             griddep_wait();
             int issued = 0;
             for (int kb = pw; kb < nk; kb += G::NPROD) {
                 const int s = kb % STAGES, r = kb / STAGES;
                 if (kb >= pre) {
                     if (!mbar_wait(&empty[s], (r & 1) ^ 1, DEV_TIMEOUT_EMPTY, p.err, abort_flag)) break;
+                    load_b(kb);
+                } else if (kb != pw) {
                     load_b(kb);
                 }
                 issued = kb + 1;
