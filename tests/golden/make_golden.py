@@ -2,7 +2,7 @@
 
 Run on a machine that has the reference sources and oracle/_ref built (``__graft_entry__.build()``):
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py [output directory, default tests/golden]
 
 Sources of the values (the libraries oracle/Makefile builds):
   * exact mode: ``_ref/libphonon2_ref.so``, the reference's x86 build (its only x86 GEMM path);
@@ -99,7 +99,8 @@ def decode_frames(T):
     return np.random.default_rng(T).standard_normal((T, 640), dtype=np.float32)
 
 
-def main() -> None:
+def main(out_dir: Path = HERE) -> None:
+    out_dir = Path(out_dir)
     ge.load_package()
     orc = ge.load_oracle()
     from phonon2_b200 import synth, model as M
@@ -128,7 +129,7 @@ def main() -> None:
         w = synth.five_value(k, n, seed=k + n)
         g[f"codes{k}x{n}"] = orc.neon_fv_pack_codes(orc.ref_neon("int8w"), w)
         g[f"codes{k}x{n}/sha"] = np.array([weight_sha(w)])
-    np.savez_compressed(HERE / "gemm.npz", **g)
+    np.savez_compressed(out_dir / "gemm.npz", **g)
 
     model = M.SyntheticModel(seed=ENCODER_SEED)
     mel = M.mel(ENCODER_MEL_FRAMES, seed=ENCODER_MEL_SEED)
@@ -136,7 +137,7 @@ def main() -> None:
          "int8w": orc.ref_neon_encoder(model.struct, mel, "int8w"),
          "int8": orc.ref_neon_encoder(model.struct, mel, "int8"),
          "sha": np.array([sha(*(model.arrays[k] for k in sorted(model.arrays))), sha(mel)])}
-    np.savez_compressed(HERE / "encoder.npz", **e)
+    np.savez_compressed(out_dir / "encoder.npz", **e)
 
     d = {"joint": np.stack([orc.ref_joint(model.struct, enc, dec) for enc, dec in joint_inputs()]),
          "joint/sha": np.array([sha(*(a for pair in joint_inputs() for a in pair))])}
@@ -144,12 +145,12 @@ def main() -> None:
         frames = decode_frames(T)
         d[f"tokens{T}"] = orc.ref_greedy_decode(model.struct, frames)
         d[f"tokens{T}/sha"] = np.array([sha(frames)])
-    np.savez_compressed(HERE / "decoder.npz", **d)
+    np.savez_compressed(out_dir / "decoder.npz", **d)
 
     audio = M.audio(MEL_SAMPLES, seed=MEL_SAMPLES)
-    np.savez_compressed(HERE / "mel.npz", mel=orc.ref_mel_spectrogram(audio), sha=np.array([sha(audio)]))
-    print("wrote", *(HERE / f for f in ("gemm.npz", "encoder.npz", "decoder.npz", "mel.npz")))
+    np.savez_compressed(out_dir / "mel.npz", mel=orc.ref_mel_spectrogram(audio), sha=np.array([sha(audio)]))
+    print("wrote", *(out_dir / f for f in ("gemm.npz", "encoder.npz", "decoder.npz", "mel.npz")))
 
 
 if __name__ == "__main__":
-    main()
+    main(Path(sys.argv[1]) if len(sys.argv) > 1 else HERE)

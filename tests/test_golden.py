@@ -77,3 +77,16 @@ def test_decoder_and_mel_golden_inputs_regenerate(pkg):
     with np.load(GOLDEN / "mel.npz") as z:
         assert z["sha"][0] == mg.sha(M.audio(mg.MEL_SAMPLES, seed=mg.MEL_SAMPLES))
         assert z["mel"].shape == (mg.MEL_SAMPLES // 160, 128)
+
+
+def test_golden_vectors_regenerate_from_the_reference(orc, tmp_path):
+    """Where the reference's builds are present, writing the vectors again gives the committed ones exactly: the
+    generator, the seeds and the reference's results have not drifted."""
+    if not (orc.ref_available() and orc.ref_neon_available()):
+        pytest.skip("the reference's builds are not present")
+    mg.main(tmp_path)
+    for name in ("gemm", "encoder", "decoder", "mel"):
+        with np.load(GOLDEN / f"{name}.npz") as want, np.load(tmp_path / f"{name}.npz") as got:
+            assert sorted(want.files) == sorted(got.files), name
+            for k in want.files:
+                assert np.array_equal(want[k], got[k]), f"{name}: {k}"
