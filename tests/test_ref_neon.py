@@ -231,3 +231,17 @@ def test_aarch64_int8_encoder_is_within_the_envelope_of_the_int8_oracle(neon, en
     assert 1e-3 < noise < 0.1
     assert _rel(arm, oracle) <= 2 * noise and _rel(arm, exact) <= 2 * noise
     assert np.corrcoef(arm.ravel(), oracle.ravel())[0, 1] > 0.999
+
+
+@pytest.mark.parametrize("beta", [0.0, 1.0, 0.5])
+def test_alpha_zero_only_scales_c(neon, synth, beta):
+    """alpha == 0: the reference's q8a entry points only apply beta to C (csrc/blas.c:1433, 1442): zeros for beta 0
+    (a memset, so +0 everywhere), C unchanged for 1, C * beta otherwise."""
+    M, K, N = 9, 1024, 64
+    q, s = neon.quant_rows(synth.activations(M, K, seed=1))
+    w = synth.five_value(K, N, seed=2)
+    C0 = np.random.default_rng(3).standard_normal((M, N)).astype(np.float32)
+    got = neon.neon_sgemm_fvb_q8a(neon.ref_neon("int8w"), q, s, w, C0.copy(), alpha=0.0, beta=beta)
+    want = neon.gemm_i8(q, s, "int8w", C0.copy(), w=w, alpha=0.0, beta=beta)
+    assert _bits_equal(got, want)
+    assert _bits_equal(want, np.zeros_like(C0) if beta == 0.0 else (C0 * np.float32(beta)).astype(np.float32))
