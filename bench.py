@@ -712,11 +712,18 @@ def mel_reference(seconds=5.0):
                       "P2_THREADS = all host cores"}
 
 
+def plane_bytes(sm) -> int:
+    """Bytes of every five-value weight's planes and magnitudes (signs, flags, lo, hi) in a SyntheticModel: what one
+    encoder pass reads from HBM at least once (230,031,360 for the 216 five-value tensors)."""
+    return sum(a.nbytes for k, a in sm.arrays.items() if k.endswith((".signs", ".flags", ".lo", ".hi")))
+
+
 def transcribe_ours(pkg, local, steps=5):
     """Configs 2 and 4 end to end: host mel in, host tokens out, through p2_b200_transcribe_windows (the encoder in
     the library's mode, then the decoder on the encoder's frames without leaving the device)."""
     from phonon2_b200 import model as M
     sm = M.SyntheticModel(seed=1)
+    planes = plane_bytes(sm)
     out = []
     for name, n in (("window", 3000), ("short", 300)):
         mel = M.mel(n, seed=n)
@@ -729,7 +736,11 @@ def transcribe_ours(pkg, local, steps=5):
         out.append({"config": name, "workload": encoder_workload(name)[1], "mel_frames": n,
                     "value": ms, "unit": "ms", "higher_is_better": False, "steps": steps,
                     "tokens": int(len(toks[0])), "h2d_bytes": mel.nbytes, "d2h_bytes": 12 * int(len(toks[0])),
-                    "api": "p2_b200_transcribe_windows, wall clock (mel host -> tokens host)"})
+                    "api": "p2_b200_transcribe_windows, wall clock (mel host -> tokens host)",
+                    # BASELINE configs[4] asks for the plane stream: every plane is read at least once per encoder
+                    # pass, so planes / end-to-end time bounds the rate from below
+                    "plane_stream": {"value": planes / (ms * 1e-3) / 1e9, "unit": "GB/s", "bytes": planes,
+                                     "bound": "lower: plane bytes / end-to-end time"}})
     return out
 
 

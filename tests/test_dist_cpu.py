@@ -76,3 +76,10 @@ def test_two_gloo_ranks(tmp_path):
     loads = [sum(frames[w] for w in r["mine"]) for r in res]
     assert all(r["slowest"] == max(loads) for r in res)   # every rank sees the slowest rank's value
     assert res[0]["all"] == res[1]["all"] == [r["mine"] for r in res]
+
+
+def test_plane_bytes_of_the_model(pkg):
+    """The plane stream figure's numerator: the 216 five-value tensors' planes and magnitudes, 229 MB."""
+    import bench
+    from phonon2_b200 import model as M
+    assert bench.plane_bytes(M.SyntheticModel(seed=1)) == 230_031_360
