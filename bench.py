@@ -248,20 +248,21 @@ def run_reference(args, world, rank):
 class GpuSet:
     """One independent copy of the workload on the device: weights, fp32 activations, outputs, workspace."""
 
-    def __init__(self, pkg, torch, dev, seed, mode, gemms, codes=False):
+    def __init__(self, pkg, torch, dev, seed, mode, gemms, codes=False, vindex=False):
         from phonon2_b200 import synth
         from phonon2_b200.device import DeviceFiveValue
         self.items = []
         for i, (name, M, K, N, alpha, beta) in enumerate(gemms):
             w = synth.five_value(K, N, seed=1000 * seed + i)
-            B = DeviceFiveValue(w, dev, codes=codes)
+            B = DeviceFiveValue(w, dev, codes=codes, vindex=vindex)
             A = torch.from_numpy(synth.activations(M, K, seed=2000 * seed + i)).to(dev)
             C = torch.zeros((M, N), dtype=torch.float32, device=dev)
             ws = torch.empty(max(pkg.workspace_bytes(M, N, K, mode), 256), dtype=torch.uint8, device=dev)
             self.items.append((M, K, N, alpha, beta, B, A, C, ws))
 
     def bytes(self):
-        return sum(B.plane_bytes + (B.codes.numel() if B.codes is not None else 0) + A.numel() * 4 + C.numel() * 4
+        return sum(B.plane_bytes + (B.codes.numel() if B.codes is not None else 0)
+                   + (4 * B.vindex.numel() if B.vindex is not None else 0) + A.numel() * 4 + C.numel() * 4
                    + ws.numel() for (_, _, _, _, _, B, A, C, ws) in self.items)
 
     def run(self, pkg, mode, stream):
@@ -295,9 +296,11 @@ def run_ours(args, world, rank, local):
 
     # Enough independent copies of the inputs that consecutive steps never find their operands in L2.
     codes = args.weights == "codes"
-    first = GpuSet(pkg, torch, dev, 1 + rank * 100, mode, gemms, codes)
+    vix = args.weights == "vindex"
+    first = GpuSet(pkg, torch, dev, 1 + rank * 100, mode, gemms, codes, vix)
     nsets = max(2, int(np.ceil(2 * L2_BYTES / first.bytes())))
-    sets = [first] + [GpuSet(pkg, torch, dev, 2 + i + rank * 100, mode, gemms, codes) for i in range(nsets - 1)]
+    sets = [first] + [GpuSet(pkg, torch, dev, 2 + i + rank * 100, mode, gemms, codes, vix)
+                      for i in range(nsets - 1)]
     torch.cuda.synchronize()
 
     with torch.cuda.stream(stream):
@@ -1008,7 +1011,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--mode", choices=["int8w", "int8", "exact"], default="int8w")
-    ap.add_argument("--weights", choices=["planes", "codes"], default="planes",
+    ap.add_argument("--weights", choices=["planes", "codes", "vindex"], default="planes",
                     help="planes: expand the sign/magnitude planes in every GEMM (the reference's default); codes: "
                          "the int8w code cache (the reference's P2_CACHE_CODES), int8w only")
     ap.add_argument("--no-cpu-baseline", action="store_true")

@@ -42,7 +42,9 @@ enum {
 enum { P2CU_INT8 = 0, P2CU_EXACT = 1, P2CU_INT8W = 2 };
 
 /* A five-value weight resident on the device. `codes` optionally points at the weight's int8w codes as a row-major
- * [K][N] int8 plane (p2cu_fv_pack_codes); with it the int8w GEMM streams the codes instead of expanding planes. */
+ * [K][N] int8 plane (p2cu_fv_pack_codes); with it the int8w GEMM streams the codes instead of expanding planes.
+ * `vindex` optionally points at the weight's value-index plane (p2cu_fv_pack_vindex, 4 bits per weight); with it
+ * int8w GEMMs of few rows (M up to about a thousand) expand the weights straight into tensor memory. */
 typedef struct {
     const unsigned char *signs;
     const unsigned char *flags;
@@ -50,6 +52,7 @@ typedef struct {
     const float         *hi;
     const signed char   *codes;
     int                  K, N;
+    const unsigned int  *vindex;
 } P2cuFiveValue;
 
 /* The message of the last failed call on this host thread ("" when none). */
@@ -99,6 +102,16 @@ P2CU_API int p2cu_sgemm(int transA, int transB, int M, int N, int K, float alpha
 
 /* The int8w codes of B as a row-major [K][N] int8 plane (csrc/blas.c:1391-1400 values): codes has K * N bytes. */
 P2CU_API int p2cu_fv_pack_codes(const P2cuFiveValue *B, signed char *codes, void *stream);
+
+/* The value-index plane of B, a device-side form of the reference's sign and magnitude planes (csrc/blas.h:38-45,
+ * written by convert_weights.py:114-125) for the small-M int8w GEMM: one 4-bit index per weight into the column's
+ * int8w codes (0: zero, 1: +clo, 2: -clo, 3: +127, 4: -127, 5 and 6: the unused 2-bit code 3 with flag 0 / 1, which
+ * the reference multiplies in as sign +2, csrc/blas.c:1197-1238), eight consecutive K rows per 32-bit word:
+ * vindex[r * N + n] holds rows 8 r .. 8 r + 7 of column n at bits 4 t .. 4 t + 3 (rows past K: 0). vindex has
+ * p2cu_fv_vindex_bytes(K, N) bytes, 16-byte aligned. Set B->vindex to it afterwards. No counterpart in the reference
+ * (its int8w path re-expands the planes per panel, csrc/blas.c:1224-1240, or keeps an 8-bit code cache). */
+P2CU_API size_t p2cu_fv_vindex_bytes(int K, int N);
+P2CU_API int p2cu_fv_pack_vindex(const P2cuFiveValue *B, unsigned int *vindex, void *stream);
 
 /* Bytes of the fixed device array behind p2cu_sgemm_fvb_noalloc (16 MiB), held on every device that loads the
  * library until the process exits. */

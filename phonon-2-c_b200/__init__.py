@@ -31,7 +31,7 @@ class Error(RuntimeError):
 class P2cuFiveValue(C.Structure):
     """include/p2cuda.h P2cuFiveValue: a five-value weight resident on the device."""
     _fields_ = [("signs", C.c_void_p), ("flags", C.c_void_p), ("lo", C.c_void_p), ("hi", C.c_void_p),
-                ("codes", C.c_void_p), ("K", C.c_int), ("N", C.c_int)]
+                ("codes", C.c_void_p), ("K", C.c_int), ("N", C.c_int), ("vindex", C.c_void_p)]
 
 
 class FiveValueB(C.Structure):
@@ -62,6 +62,8 @@ SIGNATURES = {
     "p2cu_sgemm_q8b": (_i, [_i, _i, _i, _f, _vp, _i, _vp, _vp, _i, _i, _f, _vp, _i, _vp, _sz, _vp]),
     "p2cu_sgemm": (_i, [_i, _i, _i, _i, _i, _f, _vp, _i, _vp, _i, _f, _vp, _i, _vp]),
     "p2cu_fv_pack_codes": (_i, [C.POINTER(P2cuFiveValue), _vp, _vp]),
+    "p2cu_fv_vindex_bytes": (_sz, [_i, _i]),
+    "p2cu_fv_pack_vindex": (_i, [C.POINTER(P2cuFiveValue), _vp, _vp]),
     "p2cu_sgemm_fvb_noalloc": (_i, [_i, _i, _i, _f, _vp, _i, C.POINTER(P2cuFiveValue), _i, _f, _vp, _i, _vp]),
     "p2cu_layer_norm_rows": (_i, [_vp, _vp, _vp, _vp, _i, _i, _vp]),
     "p2cu_layer_norm_quant_rows": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _vp]),
@@ -228,6 +230,15 @@ def sgemm(transA, transB, M, N, K, alpha, A, lda, B, ldb, beta, Cp, ldc, stream=
 
 def fv_pack_codes(B: P2cuFiveValue, codes: int, stream=None) -> None:
     check(lib().p2cu_fv_pack_codes(C.byref(B), codes, stream_ptr(stream)))
+
+
+def fv_vindex_bytes(K: int, N: int) -> int:
+    return int(lib().p2cu_fv_vindex_bytes(K, N))
+
+
+def fv_pack_vindex(B: P2cuFiveValue, vindex: int, stream=None) -> None:
+    """The weight's value-index plane (include/p2cuda.h p2cu_fv_pack_vindex), read by the tensor-memory GEMM."""
+    check(lib().p2cu_fv_pack_vindex(C.byref(B), vindex, stream_ptr(stream)))
 
 
 def check_device(stream=None) -> None:

@@ -99,6 +99,20 @@ int make_map(CUtensorMap* map, const void* base, int esize, uint64_t inner, uint
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
+// SMs of the current device (looked up once per device).
+int sm_count() {
+    static int counts[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return 148;
+    if (!counts[dev]) {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+        counts[dev] = n;
+    }
+    return counts[dev];
+}
+
 size_t round256(size_t x) { return (x + 255) & ~size_t(255); }
 
 __global__ void scale_c_kernel(float* C, int M, int N, int ldc, float beta) {
@@ -127,13 +141,19 @@ int check_gemm_common(int M, int N, int K, const void* C, int ldc, const char* w
 
 // Tile width for the tensor-core GEMM: the widest tile (128 for the two int8-mode planes, else 256) that still gives
 // about half the SMs a CTA, else 64. P2CU_TILE_N=64|128|256 forces one (where the operand kind allows it).
+// An on / off override from the environment: 1 forces, 0 forbids, -1 (unset or anything else) leaves the choice to
+// the shape. Read once per variable (callers keep the result in a function-local static, initialised thread-safely).
+int env_switch(const char* name) {
+    const char* e = getenv(name);
+    return e && e[0] == '1' ? 1 : e && e[0] == '0' ? 0 : -1;
+}
+
 int choose_bn(int M, int N, int nblk, int kind) {
-    static int forced = -1;
-    if (forced < 0) {
+    static const int forced = [] {
         const char* e = getenv("P2CU_TILE_N");
         const int v = e ? atoi(e) : 0;
-        forced = (v == 64 || v == 128 || v == 256) ? v : 0;
-    }
+        return (v == 64 || v == 128 || v == 256) ? v : 0;
+    }();
     const int widest = kind == p2cu::KIND_ST ? 128 : 256;
     if (forced) return forced > widest ? widest : forced;
     const long mt = (M + 127) / 128;
@@ -149,6 +169,49 @@ size_t split_bytes(int M, int N, int K) {
     return round256(static_cast<size_t>(nblk) * m_pad * N * sizeof(float));
 }
 
+// The int8w GEMM with the weights expanded into tensor memory (fv_gemm_t.cu) for few rows, when B carries the
+// value-index plane: N % 128 == 0, K % 16 == 0, M <= 1024 (P2CU_TGEMM=0 forbids it, 1 takes it up to M = 4096).
+// Returns RUN_T_DECLINED for shapes it does not take, so the caller picks another kernel.
+constexpr int RUN_T_DECLINED = 1;
+
+int run_t(int M, int N, int K, float alpha, const int8_t* q, const float* a_scales, const P2cuFiveValue* B,
+          float beta, float* C, int ldc, void* ws, size_t ws_bytes, cudaStream_t s, const char* who) {
+    static const int t_env = env_switch("P2CU_TGEMM");
+    if (t_env == 0 || N % 128 || K % 16 || M > (t_env == 1 ? 4096 : 1024)) return RUN_T_DECLINED;
+    if (!B->lo || !B->hi) return fail(P2CU_EINVAL, "%s: lo / hi are NULL", who);
+    if (B->K != K || B->N != N)
+        return fail(P2CU_EINVAL, "%s: weight is [%d, %d], GEMM wants [%d, %d]", who, B->K, B->N, K, N);
+    const int nblk = (K + 1023) / 1024;
+    const size_t need = split_bytes(M, N, K);
+    if (need && (!ws || ws_bytes < need || !aligned16(ws)))
+        return fail(P2CU_EINVAL, "%s: K = %d needs %zu bytes of 16-byte aligned workspace, %zu given", who, K, need,
+                    ws ? ws_bytes : 0);
+    int rc;
+    if (beta != 0.f && beta != 1.f) {
+        if ((rc = scale_c(C, M, N, ldc, beta, s))) return rc;
+        beta = 1.f;
+    }
+    p2cu::FvGemmTParams p{};
+    p.M = M; p.N = N; p.K = K; p.alpha = alpha; p.beta_zero = beta == 0.f;
+    p.a_scales = a_scales; p.lo = B->lo; p.hi = B->hi; p.C = C; p.ldc = ldc;
+    p.ws = static_cast<float*>(ws); p.ksplit = nblk; p.m_pad = (M + 127) / 128 * 128; p.err = dev_err_ptr();
+#ifdef P2CU_TRACE
+    static int t_launches = 0;
+    p.trace_slot = t_launches++;
+#endif
+    const int mt = p2cu::fv_gemm_t_rows(M, N, nblk, sm_count());
+    CUtensorMap ta, tvi;
+    if ((rc = make_map(&ta, q, 1, K, M, K, 128, mt, 128, "A"))) return rc;
+    if ((rc = make_map(&tvi, B->vindex, 4, N, static_cast<uint64_t>((K + 7) / 8), static_cast<uint64_t>(N) * 4, 128,
+                       16, 0, "value-index plane")))
+        return rc;
+    cudaError_t e = p2cu::fv_gemm_t_launch(mt, ta, tvi, p, s);
+    if (e == cudaSuccess && nblk > 1)
+        e = p2cu::fv_combine_launch(static_cast<const float*>(ws), p.m_pad, nblk, a_scales, alpha, p.beta_zero, C, M,
+                                    N, ldc, s);
+    return e == cudaSuccess ? P2CU_OK : cuda_fail(e, who);
+}
+
 // The tcgen05 GEMM on quantised rows. `B` five-value (planes or cached codes) or `q8`/`scales` an int8 table.
 // `ws` holds the per-block slices when K > 1024 (split_bytes).
 int run_i8(int M, int N, int K, float alpha, const int8_t* q, const float* a_scales, const P2cuFiveValue* B,
@@ -160,6 +223,10 @@ int run_i8(int M, int N, int K, float alpha, const int8_t* q, const float* a_sca
     if (M == 0 || N == 0) return P2CU_OK;
     if (alpha == 0.f || K == 0) return scale_c(C, M, N, ldc, beta, s);   // no products: C = beta * C
     if (!q || !a_scales) return fail(P2CU_EINVAL, "%s: quantised A is NULL", who);
+    if (B && mode == P2CU_INT8W && B->vindex) {
+        rc = run_t(M, N, K, alpha, q, a_scales, B, beta, C, ldc, ws, ws_bytes, s, who);
+        if (rc != RUN_T_DECLINED) return rc;
+    }
     if (N % 128 || K % 16 || !aligned16(C) || ldc % 4) {
         // shapes the tensor-core kernels do not take (the reference's int8 path takes any N % 16 == 0): the SIMT
         // kernel, same sums and epilogue (fv_gemm_simt.cu)
@@ -215,11 +282,7 @@ int run_i8(int M, int N, int K, float alpha, const int8_t* q, const float* a_sca
     const int kind = !planes ? p2cu::KIND_TABLE : mode == P2CU_INT8W ? p2cu::KIND_CODES : p2cu::KIND_ST;
     // CTA pairs (256 x 256 tiles, fv_gemm_2sm.cu) for int8w / int8-table products with at least as many pair tiles
     // as the GPU has SM pairs (large M: batched windows); P2CU_PAIR=1 forces them where they apply, 0 forbids them.
-    static int pair_env = -2;
-    if (pair_env == -2) {
-        const char* pe = getenv("P2CU_PAIR");
-        pair_env = pe && pe[0] == '1' ? 1 : pe && pe[0] == '0' ? 0 : -1;
-    }
+    static const int pair_env = env_switch("P2CU_PAIR");
     const bool vec_ok = aligned16(B ? B->lo : nullptr) && aligned16(B ? B->hi : nullptr) && aligned16(scales);
     const bool pair_ok = vec_ok && kind != p2cu::KIND_ST && N % 256 == 0;
     const bool use_pair = pair_ok && (pair_env == 1 ||
@@ -263,11 +326,7 @@ int run_i8(int M, int N, int K, float alpha, const int8_t* q, const float* a_sca
     // Many tiles (large M): the persistent kernel, where it measured faster - expanded planes, or more than one
     // 1024-row K block (with one K block from an int8 table or the code cache the one-tile-per-CTA kernel streams as
     // fast). P2CU_PERSIST=1 forces it, 0 forbids it. Its epilogue reads the per-column constants as 16-byte vectors.
-    static int persist_env = -2;
-    if (persist_env == -2) {
-        const char* pe = getenv("P2CU_PERSIST");
-        persist_env = pe && pe[0] == '1' ? 1 : pe && pe[0] == '0' ? 0 : -1;
-    }
+    static const int persist_env = env_switch("P2CU_PERSIST");
     const bool many = p2cu::fv_gemm_p_tiles(M, N, bn, nblk) > p2cu::fv_gemm_p_min_tiles();
     const bool persist = vec_ok && (persist_env == 1 ||
                                     (persist_env == -1 && many && (kind != p2cu::KIND_TABLE || nblk > 1)));
@@ -498,6 +557,20 @@ int p2cu_sgemm(int transA, int transB, int M, int N, int K, float alpha, const f
                int ldb, float beta, float* C, int ldc, void* stream) {
     return run_exact(M, N, K, alpha, A, lda, transA ? 1 : 0, nullptr, nullptr, nullptr, B, ldb, transB ? 1 : 0, beta,
                      C, ldc, static_cast<cudaStream_t>(stream), "p2cu_sgemm");
+}
+
+size_t p2cu_fv_vindex_bytes(int K, int N) {
+    if (K <= 0 || N <= 0) return 0;
+    return static_cast<size_t>((K + 7) / 8) * N * sizeof(uint32_t);
+}
+
+int p2cu_fv_pack_vindex(const P2cuFiveValue* B, unsigned int* vindex, void* stream) {
+    if (!B || !vindex || !B->signs || !B->flags) return fail(P2CU_EINVAL, "p2cu_fv_pack_vindex: NULL pointer");
+    if (B->K <= 0 || B->N <= 0 || B->N % 16)
+        return fail(P2CU_EINVAL, "p2cu_fv_pack_vindex: shape [%d, %d]", B->K, B->N);
+    if (!aligned16(vindex)) return fail(P2CU_EINVAL, "p2cu_fv_pack_vindex: output not 16-byte aligned");
+    cudaError_t e = p2cu::fv_vindex_launch(B->signs, B->flags, B->K, B->N, vindex, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? P2CU_OK : cuda_fail(e, "p2cu_fv_pack_vindex");
 }
 
 int p2cu_fv_pack_codes(const P2cuFiveValue* B, signed char* codes, void* stream) {

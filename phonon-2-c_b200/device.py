@@ -11,17 +11,20 @@ from . import P2cuFiveValue, five_value_struct
 class DeviceFiveValue:
     """A five-value weight (synth.five_value layout) copied to the device once, with its P2cuFiveValue view."""
 
-    def __init__(self, w: dict, device="cuda", codes: bool = False, stream=None):
+    def __init__(self, w: dict, device="cuda", codes: bool = False, stream=None, vindex: bool = False):
         self.K, self.N = int(w["K"]), int(w["N"])
         self.signs = torch.from_numpy(np.ascontiguousarray(w["signs"])).to(device)
         self.flags = torch.from_numpy(np.ascontiguousarray(w["flags"])).to(device)
         self.lo = torch.from_numpy(np.ascontiguousarray(w["lo"])).to(device)
         self.hi = torch.from_numpy(np.ascontiguousarray(w["hi"])).to(device)
         self.codes = None
+        self.vindex = None
         self.struct = five_value_struct(self.signs.data_ptr(), self.flags.data_ptr(), self.lo.data_ptr(),
                                         self.hi.data_ptr(), self.K, self.N)
         if codes:
             self.pack_codes(stream)
+        if vindex:
+            self.pack_vindex(stream)
 
     def pack_codes(self, stream=None) -> None:
         from . import fv_pack_codes
@@ -29,9 +32,22 @@ class DeviceFiveValue:
         fv_pack_codes(self.struct, self.codes.data_ptr(), stream)
         self.struct.codes = self.codes.data_ptr()
 
+    def pack_vindex(self, stream=None) -> None:
+        from . import fv_pack_vindex, fv_vindex_bytes
+        self.vindex = torch.empty(fv_vindex_bytes(self.K, self.N) // 4, dtype=torch.int32, device=self.signs.device)
+        fv_pack_vindex(self.struct, self.vindex.data_ptr(), stream)
+        self.struct.vindex = self.vindex.data_ptr()
+
     def without_codes(self) -> P2cuFiveValue:
         s = P2cuFiveValue.from_buffer_copy(self.struct)
         s.codes = None
+        return s
+
+    def variant(self, codes: bool = False, vindex: bool = False) -> P2cuFiveValue:
+        """A view of the weight with only the chosen optional layouts (the planes are always there)."""
+        s = P2cuFiveValue.from_buffer_copy(self.struct)
+        s.codes = s.codes if codes else None
+        s.vindex = s.vindex if vindex else None
         return s
 
     @property

@@ -6,10 +6,19 @@ way phonon-2-c's loader points a P2Model into its weights.bin mapping. Anything 
 take ``ctypes.byref(model.struct)``. The decoder tables are fp32 as the loader expands them (``decoder=False`` leaves
 them NULL: the encoder never reads them).
 
-Distributions (the BASELINE configs 2-4): five-value weights as ``synth.five_value`` (P(0) = 1/3, lo ~ U(0.005, 0.02),
-hi = lo * U(2, 4), fp16 values); fp32 norms and biases N(0, 0.02); LayerNorm gains ``1 + N(0, 0.02)`` by default
-(``gamma="unit"``) or plain N(0, 0.02) (``gamma="small"``); convolution weights N(0, 1 / fan_in); int8 tables with
-int6 values and per-column scales of about 1 / (18 sqrt K), so every layer keeps activations of order one.
+Distributions: five-value weights as ``synth.five_value`` (P(0) = 1/3, lo ~ U(0.005, 0.02), hi = lo * U(2, 4), fp16
+values: the weight statistics of phonon-2-c's five-value format, csrc/blas.h:38-45); fp32 norms and biases
+N(0, 0.02); LayerNorm gains ``1 + N(0, 0.02)`` by default (``gamma="unit"``) or plain N(0, 0.02) (``gamma="small"``);
+convolution weights N(0, 1 / fan_in); int8 tables with int6 values and per-column scales of about 1 / (18 sqrt K), so
+every layer keeps activations of order one.
+
+``attn_out_gain`` scales the magnitudes (lo, hi) of every block's attention output projection. With the same weight
+statistics everywhere (gain 1) the 24 blocks' relative-position attention averages the frames of a window into one
+common vector: the encoder output then varies across time by about 7 % of its spread across dimensions, and greedy TDT
+decoding (csrc/decoder.c:100-141) of it emits almost no tokens, so that end-to-end token comparisons would compare
+empty lists. ``SPEECH_ATTN_OUT_GAIN`` (0.1) keeps about 60 % of the spread across time; the decoder then emits about one
+token per encoder frame, dozens of distinct ids per 30 s window, with top-2 logit gaps that 1e-4 perturbations of the
+encoder output do not close. Every kernel runs the same operations on either model.
 """
 from __future__ import annotations
 
@@ -27,6 +36,7 @@ HID, EMB, VOCAB, BLANK, N_DUR = 640, 640, 8193, 8192, 5
 MAX_SYMBOLS = 10   # tokens at one frame before the decoder moves on (csrc/phonon2.h:92)
 LOGITS = VOCAB + N_DUR
 W_F32, W_I8, W_FV = 0, 8, 5
+SPEECH_ATTN_OUT_GAIN = 0.1   # the attention output gain of the model whose greedy decoding emits tokens
 
 
 class Weight(C.Structure):   # csrc/phonon2.h:116-126
@@ -87,10 +97,10 @@ def _seed(base: int, name: str) -> int:
 class SyntheticModel:
     """A seeded random encoder laid out as phonon-2-c's P2Model (``struct``), arrays kept alive by this object."""
 
-    def __init__(self, seed: int = 0, gamma: str = "unit", decoder: bool = True):
+    def __init__(self, seed: int = 0, gamma: str = "unit", decoder: bool = True, attn_out_gain: float = 1.0):
         if gamma not in ("unit", "small"):
             raise ValueError("gamma is 'unit' or 'small'")
-        self.seed, self.gamma = seed, gamma
+        self.seed, self.gamma, self.attn_out_gain = seed, gamma, float(attn_out_gain)
         self.arrays: dict[str, np.ndarray] = {}
         self.struct = P2Model()
         e = self.struct.enc
@@ -116,7 +126,7 @@ class SyntheticModel:
             b.norm_sa_w, b.norm_sa_b = self._norm(p + "norm_self_att")
             self._five(b.mha.qkv_w, p + "self_attn.qkv_proj.weight", D, 3 * D)
             self._five(b.mha.pos_w, p + "self_attn.relative_k_proj.weight", D, D)
-            self._five(b.mha.out_w, p + "self_attn.o_proj.weight", D, D)
+            self._five(b.mha.out_w, p + "self_attn.o_proj.weight", D, D, gain=self.attn_out_gain)
             b.mha.bias_u = self._normal(p + "self_attn.bias_u", D, 0.02)
             b.mha.bias_v = self._normal(p + "self_attn.bias_v", D, 0.02)
             b.norm_conv_w, b.norm_conv_b = self._norm(p + "norm_conv")
@@ -181,8 +191,11 @@ class SyntheticModel:
         gw = self._keep(prefix + ".weight", g.astype(np.float32))
         return gw, self._normal(prefix + ".bias", D, 0.02)
 
-    def _five(self, w: Weight, name: str, K: int, N: int) -> None:
+    def _five(self, w: Weight, name: str, K: int, N: int, gain: float = 1.0) -> None:
         fv = synth.five_value(K, N, _seed(self.seed, name))
+        if gain != 1.0:   # magnitudes stay fp16 values, as the format keeps them
+            fv["lo"] = (fv["lo"] * np.float32(gain)).astype(np.float16).astype(np.float32)
+            fv["hi"] = (fv["hi"] * np.float32(gain)).astype(np.float16).astype(np.float32)
         w.kind, w.K, w.N = W_FV, K, N
         w.signs = self._keep(name + ".signs", fv["signs"])
         w.flags = self._keep(name + ".flags", fv["flags"])
@@ -218,7 +231,8 @@ def frames_after_subsampling(n_mel: int) -> int:
 
 
 def mel(n_frames: int, seed: int) -> np.ndarray:
-    """Synthetic log-mel features [n_frames, 128], N(0, 1) per feature (the BASELINE configs 2-4)."""
+    """Synthetic log-mel features [n_frames, 128], N(0, 1) per feature (normalised features, as csrc/mel.c:200-215
+    leaves them)."""
     return np.random.default_rng(seed).standard_normal((n_frames, NMEL), dtype=np.float32)
 
 
@@ -249,7 +263,7 @@ def audio_with_pauses(seconds: float, seed: int, pause_lo: float = 0.05, pause_h
 
 
 def long_audio_windows(seed: int = 0, n: int = 64, lo_s: float = 25.0, hi_s: float = 35.0) -> list[int]:
-    """Mel frame counts of the long-audio batch: n windows of U(lo_s, hi_s) seconds of a
-    synthetic stream, 100 mel frames per second."""
+    """Mel frame counts of a long-audio batch: n windows of U(lo_s, hi_s) seconds of a synthetic stream (the 25-35 s
+    windows the reference's segmenter cuts, csrc/segment.c:52-87), 100 mel frames per second."""
     rng = np.random.default_rng(seed)
     return [int(round(s * 100)) for s in rng.uniform(lo_s, hi_s, n)]

@@ -5,8 +5,8 @@ The five-value operand follows the reference's on-disk planes (csrc/blas.h:38-45
 bit n % 8 set when |w| = hi[n], and fp32 ``lo``/``hi`` [N] that hold fp16 values (fermion_container.py:33-34; the
 exact-mode expansion relies on that, csrc/blas.c:838-840).
 
-Distribution (the BASELINE configs): P(0) = 1/3 and P(+-lo) = P(+-hi) = 1/6; lo ~ U(0.005, 0.02) and
-hi = lo * U(2, 4) per output column, both rounded to fp16.
+Distribution: P(0) = 1/3 and P(+-lo) = P(+-hi) = 1/6 (each sign equally likely); lo ~ U(0.005, 0.02) and
+hi = lo * U(2, 4) per output column, both rounded to fp16 (magnitudes of the size the reference's converter writes).
 """
 from __future__ import annotations
 
@@ -62,12 +62,20 @@ def quantiser_edge_rows(K: int, seed: int) -> np.ndarray:
         scale = f32(amax / f32(127))
         inv = f32(f32(1) / scale)
         picked = []
+        barren = 0
         while len(picked) < K - 1:
             n = rng.integers(-126, 126, 4096)
             x = ((n + 0.5) * np.float64(scale)).astype(f32)
             x = np.concatenate([x, np.nextafter(x, f32(np.inf)), np.nextafter(x, f32(-np.inf))]).astype(f32)
             split = np.rint((x * inv).astype(f32)) != np.rint((x / scale).astype(f32))
-            picked.extend(x[split & (np.abs(x) < amax)].tolist())
+            found = x[split & (np.abs(x) < amax)].tolist()
+            picked.extend(found)
+            barren = 0 if found else barren + 1
+            if barren == 16 and not picked:   # a scale whose reciprocal never rounds apart: draw another
+                amax = f32(rng.uniform(0.5, 8.0))
+                scale = f32(amax / f32(127))
+                inv = f32(f32(1) / scale)
+                barren = 0
         rows[r, 0] = amax if r % 2 == 0 else -amax
         rows[r, 1:] = np.asarray(picked[:K - 1], f32)
     rows[5] = (rng.uniform(-2e-37, 2e-37, K)).astype(f32)

@@ -178,7 +178,7 @@ def test_encoder_int8_matches_reference_control_flow(pkg, orc, cuda, model, dev_
 
 
 def test_encoder_int8w_config2_window(pkg, orc, cuda, model, dev_model):
-    """The same statistical parity at BASELINE config 2 (a 30 s window: 3000 mel frames, T' = 375), int8w, against
+    """The same statistical parity on one 30 s window (3000 mel frames, T' = 375), int8w, against
     both int8 oracles: the restated-GEMM control flow and the reference's own AArch64 build."""
     import torch
     from phonon2_b200 import model as M

@@ -1,9 +1,10 @@
 """The drop-in, end to end: phonon-2-c's own command-line program (csrc/main.c over engine.c, segment.c, wav.c, ...)
 built twice by oracle/Makefile - on the reference's own sources (_ref/phonon2_cpu), and without blas.c, encoder.c,
 decoder.c and mel.c, linked against libphonon2_b200.so (_ref/phonon2_b200) - transcribes the same WAV files with the
-same synthetic model directory (oracle/weights_file.py). In exact mode (P2_GEMM=exact) the token ids must be identical:
-the engine's segmentation into windows, its dropout check and re-decodes, and the detokeniser run in the reference's C
-either way, while log-mel, encoder and decoder run on the GPU in the second program.
+same synthetic model directory (oracle/weights_file.py; the speech-like model, model.SPEECH_ATTN_OUT_GAIN, on which
+greedy decoding emits tokens). In exact mode (P2_GEMM=exact) the token ids must be identical and at least one per four
+encoder frames: the engine's segmentation into windows, its dropout check and re-decodes, and the detokeniser run in
+the reference's C either way, while log-mel, encoder and decoder run on the GPU in the second program.
 """
 import os
 import subprocess
@@ -25,7 +26,7 @@ def model_dir(pkg, tmp_path_factory):
     from oracle import weights_file as wf
     from phonon2_b200 import model as M
     d = tmp_path_factory.mktemp("model")
-    wf.write_model_dir(M.SyntheticModel(seed=1), d)
+    wf.write_model_dir(M.SyntheticModel(seed=1, attn_out_gain=M.SPEECH_ATTN_OUT_GAIN), d)
     return d
 
 
@@ -50,6 +51,8 @@ def test_reference_program_on_library_matches_reference(pkg, cuda, model_dir, tm
     got, t_gpu = _run(B200_BIN, model_dir, wav, {"P2_GEMM": "exact"})
     print(f"{seconds} s: reference {t_cpu:.1f} s, reference program on the library {t_gpu:.1f} s (exact mode, "
           f"including start-up and weight upload); {len(want)} tokens")
+    encoder_frames = M.frames_after_subsampling(seconds * 100)
+    assert len(want) >= encoder_frames // 4, (len(want), encoder_frames)
     assert got == want
 
 

@@ -129,3 +129,22 @@ def test_codes_plane_matches_identity(orc, synth):
     flag = np.unpackbits(w["flags"], axis=1, bitorder="little").astype(bool)
     clo = np.array([orc.clo(l, h) for l, h in zip(w["lo"], w["hi"])], np.int32)
     assert np.array_equal(codes, S * np.where(flag, 127, clo[None, :]))
+
+
+@pytest.mark.parametrize("K,N", [(1024, 256), (100, 32), (4096, 128)])
+def test_vindex_restatement_decodes_to_the_codes(orc, synth, K, N):
+    """The value-index plane (include/p2cuda.h p2cu_fv_pack_vindex, restated by oracle.vindex) decodes through the
+    per-column palette to exactly the int8w codes (csrc/blas.c:1222-1240)."""
+    w = synth.five_value(K, N, seed=K + 3)
+    assert np.array_equal(orc.vindex_codes(orc.vindex(w), w), orc.fv_codes(w))
+
+
+def test_vindex_code3_matches_reference_pack(orc, synth):
+    """The unused 2-bit code 3 decodes as the reference's own code packer reads it (sign +2, product wrapping)."""
+    if not orc.ref_neon_available():
+        pytest.skip("the reference's AArch64 build is not built")
+    w = synth.five_value(64, 32, seed=5)
+    w["signs"] = w["signs"].copy()
+    w["signs"][::3, ::2] |= 0x03
+    ref = orc.neon_fv_pack_codes(orc.ref_neon("int8w"), w)
+    assert np.array_equal(orc.vindex_codes(orc.vindex(w), w), ref)
