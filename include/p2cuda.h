@@ -106,10 +106,11 @@ P2CU_API int p2cu_fv_pack_codes(const P2cuFiveValue *B, signed char *codes, void
 /* The value-index plane of B, a device-side form of the reference's sign and magnitude planes (csrc/blas.h:38-45,
  * written by convert_weights.py:114-125) for the small-M int8w GEMM: one 4-bit index per weight into the column's
  * int8w codes (0: zero, 1: +clo, 2: -clo, 3: +127, 4: -127, 5 and 6: the unused 2-bit code 3 with flag 0 / 1, which
- * the reference multiplies in as sign +2, csrc/blas.c:1197-1238), eight consecutive K rows per 32-bit word:
- * vindex[r * N + n] holds rows 8 r .. 8 r + 7 of column n at bits 4 t .. 4 t + 3 (rows past K: 0). vindex has
- * p2cu_fv_vindex_bytes(K, N) bytes, 16-byte aligned. Set B->vindex to it afterwards. No counterpart in the reference
- * (its int8w path re-expands the planes per panel, csrc/blas.c:1224-1240, or keeps an 8-bit code cache). */
+ * the reference multiplies in as sign +2, csrc/blas.c:1197-1238), 32 consecutive K rows of one column in 16 bytes:
+ * vindex[(kc * N + n) * 4 + v] holds rows 32 kc + 8 v + t of column n at bits 4 t .. 4 t + 3 (rows past K: 0).
+ * vindex has p2cu_fv_vindex_bytes(K, N) = 16 * ceil(K / 32) * N bytes, 16-byte aligned. Set B->vindex to it
+ * afterwards. No counterpart in the reference (its int8w path re-expands the planes per panel, csrc/blas.c:1224-1240,
+ * or keeps an 8-bit code cache). */
 P2CU_API size_t p2cu_fv_vindex_bytes(int K, int N);
 P2CU_API int p2cu_fv_pack_vindex(const P2cuFiveValue *B, unsigned int *vindex, void *stream);
 

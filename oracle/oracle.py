@@ -95,16 +95,18 @@ def fv_codes(w) -> np.ndarray:
 
 def vindex(w) -> np.ndarray:
     """The value-index plane p2cu_fv_pack_vindex writes (include/p2cuda.h), restated with numpy: uint32
-    [ceil(K / 8), N]; word [r, n] holds the 4-bit indices of K rows 8 r .. 8 r + 7 of column n at bits 4 t, from the
-    reference's 2-bit code and flag (csrc/blas.h:38-45): code 1 -> 0, code 2 -> 1 / 3, code 0 -> 2 / 4, code 3 -> 5 / 6
-    (flag 0 / 1); rows past K -> 0. A layout of this build, not of the reference; only the tests use this function."""
+    [ceil(K / 32), N, 4]; word [kc, n, v] holds the 4-bit indices of K rows 32 kc + 8 v .. + 7 of column n at bits 4 t,
+    from the reference's 2-bit code and flag (csrc/blas.h:38-45): code 1 -> 0, code 2 -> 1 / 3, code 0 -> 2 / 4,
+    code 3 -> 5 / 6 (flag 0 / 1); rows past K -> 0. A layout of this build, not of the reference; only the tests use
+    this function."""
     K, N = int(w["K"]), int(w["N"])
     codes = ((w["signs"][:, :, None] >> (2 * np.arange(4, dtype=np.uint8))) & 3).reshape(K, N).astype(np.uint32)
     flags = ((w["flags"][:, :, None] >> np.arange(8, dtype=np.uint8)) & 1).reshape(K, N).astype(np.uint32)
     idx = np.select([codes == 1, codes == 2, codes == 0], [np.zeros_like(flags), 1 + 2 * flags, 2 + 2 * flags], 5 + flags)
-    rows = (K + 7) // 8
-    idx = np.concatenate([idx, np.zeros((rows * 8 - K, N), np.uint32)]).astype(np.uint32).reshape(rows, 8, N)
-    return (idx << (4 * np.arange(8, dtype=np.uint32))[None, :, None]).sum(axis=1, dtype=np.uint64).astype(np.uint32)
+    kc = (K + 31) // 32
+    idx = np.concatenate([idx, np.zeros((kc * 32 - K, N), np.uint32)]).astype(np.uint32).reshape(kc, 4, 8, N)
+    words = (idx << (4 * np.arange(8, dtype=np.uint32))[None, None, :, None]).sum(axis=2, dtype=np.uint64)
+    return np.ascontiguousarray(words.astype(np.uint32).transpose(0, 2, 1))                # [kc, N, 4]
 
 
 def vindex_codes(vi: np.ndarray, w) -> np.ndarray:
@@ -117,7 +119,8 @@ def vindex_codes(vi: np.ndarray, w) -> np.ndarray:
     palette = np.stack([np.zeros(N, np.int64), clo_n, -clo_n, np.full(N, 127), np.full(N, -127), 2 * clo_n,
                         np.full(N, 254), np.zeros(N, np.int64)])                          # [8, N]
     palette = (palette & 0xFF).astype(np.uint8).view(np.int8)
-    idx = (vi[:, None, :] >> (4 * np.arange(8, dtype=np.uint32))[None, :, None]) & 0xF   # [rows, 8, N]
+    words = vi.reshape(-1, N, 4).transpose(0, 2, 1)                                     # [kc, 4, N]
+    idx = (words[:, :, None, :] >> (4 * np.arange(8, dtype=np.uint32))[None, None, :, None]) & 0xF
     idx = idx.reshape(-1, N)[:K].astype(np.int64)
     return np.take_along_axis(palette, idx & 7, axis=0)
 

@@ -194,18 +194,17 @@ int run_t(int M, int N, int K, float alpha, const int8_t* q, const float* a_scal
     p2cu::FvGemmTParams p{};
     p.M = M; p.N = N; p.K = K; p.alpha = alpha; p.beta_zero = beta == 0.f;
     p.a_scales = a_scales; p.lo = B->lo; p.hi = B->hi; p.C = C; p.ldc = ldc;
+    p.vindex = B->vindex; p.kchunks = (K + 31) / 32;
     p.ws = static_cast<float*>(ws); p.ksplit = nblk; p.m_pad = (M + 127) / 128 * 128; p.err = dev_err_ptr();
 #ifdef P2CU_TRACE
     static int t_launches = 0;
     p.trace_slot = t_launches++;
 #endif
     const int mt = p2cu::fv_gemm_t_rows(M, N, nblk, sm_count());
-    CUtensorMap ta, tvi;
+    if (!aligned16(B->vindex)) return fail(P2CU_EINVAL, "%s: value-index plane not 16-byte aligned", who);
+    CUtensorMap ta;
     if ((rc = make_map(&ta, q, 1, K, M, K, 128, mt, 128, "A"))) return rc;
-    if ((rc = make_map(&tvi, B->vindex, 4, N, static_cast<uint64_t>((K + 7) / 8), static_cast<uint64_t>(N) * 4, 128,
-                       16, 0, "value-index plane")))
-        return rc;
-    cudaError_t e = p2cu::fv_gemm_t_launch(mt, ta, tvi, p, s);
+    cudaError_t e = p2cu::fv_gemm_t_launch(mt, ta, p, s);
     if (e == cudaSuccess && nblk > 1)
         e = p2cu::fv_combine_launch(static_cast<const float*>(ws), p.m_pad, nblk, a_scales, alpha, p.beta_zero, C, M,
                                     N, ldc, s);
@@ -561,7 +560,7 @@ int p2cu_sgemm(int transA, int transB, int M, int N, int K, float alpha, const f
 
 size_t p2cu_fv_vindex_bytes(int K, int N) {
     if (K <= 0 || N <= 0) return 0;
-    return static_cast<size_t>((K + 7) / 8) * N * sizeof(uint32_t);
+    return static_cast<size_t>((K + 31) / 32) * N * 16;
 }
 
 int p2cu_fv_pack_vindex(const P2cuFiveValue* B, unsigned int* vindex, void* stream) {

@@ -59,9 +59,9 @@ cudaError_t fv_gemm_simt_launch(const int8_t* q, const uint8_t* signs, const uin
 
 // The int8w GEMM with the weights in tensor memory (fv_gemm_t.cu), for few rows: 128 output columns x MT rows per
 // CTA (MT = fv_gemm_t_rows(...), a multiple of 16 up to 128), one 1024-row K block per CTA. B comes as the value-index
-// plane of p2cu_fv_pack_vindex; a = int8 A [M, K] in 128 x MT boxes (128-byte swizzle), vi = the index plane as a
-// [ceil(K/8)][N] 32-bit tensor in 128 x 16 boxes. N % 128 == 0. ksplit > 1 writes f per block to ws slices
-// [ksplit][m_pad][N] for fv_combine_launch.
+// plane of p2cu_fv_pack_vindex (vindex, kchunks = ceil(K / 32) chunks of N x 16 bytes); a = int8 A [M, K] in
+// 128 x MT boxes (128-byte swizzle). N % 128 == 0. ksplit > 1 writes f per block to ws slices [ksplit][m_pad][N] for
+// fv_combine_launch.
 struct FvGemmTParams {
     int M, N, K;
     float alpha;
@@ -69,6 +69,8 @@ struct FvGemmTParams {
     const float* a_scales;
     const float* lo;
     const float* hi;
+    const uint32_t* vindex;
+    int kchunks;
     float* C;
     int ldc;
     float* ws;
@@ -79,9 +81,8 @@ struct FvGemmTParams {
 };
 // Rows per CTA for an M x N GEMM of ksplit K blocks on a GPU of `sms` SMs.
 int fv_gemm_t_rows(int M, int N, int ksplit, int sms);
-cudaError_t fv_gemm_t_launch(int mt, const CUtensorMap& a, const CUtensorMap& vi, const FvGemmTParams& p,
-                             cudaStream_t stream);
-// The value-index plane of a five-value weight (p2cu_fv_pack_vindex): [ceil(K/8)][N] 32-bit words.
+cudaError_t fv_gemm_t_launch(int mt, const CUtensorMap& a, const FvGemmTParams& p, cudaStream_t stream);
+// The value-index plane of a five-value weight (p2cu_fv_pack_vindex): [ceil(K/32)][N][4] 32-bit words.
 cudaError_t fv_vindex_launch(const uint8_t* signs, const uint8_t* flags, int K, int N, uint32_t* out,
                              cudaStream_t stream);
 

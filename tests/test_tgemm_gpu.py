@@ -73,7 +73,7 @@ def test_vindex_layout(pkg, orc, synth, cuda, K, N):
     w["signs"][::5, ::3] |= 0x03   # some 2-bit codes 3 (unused by the converter; the reference reads them as sign +2)
     B = _weight(pkg, torch, cuda, w)
     torch.cuda.synchronize()
-    got = B.vindex.cpu().numpy().view(np.uint32).reshape(-1, N)
+    got = B.vindex.cpu().numpy().view(np.uint32).reshape(-1, N, 4)
     assert np.array_equal(got, orc.vindex(w))
 
 
