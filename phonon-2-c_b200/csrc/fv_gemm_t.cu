@@ -124,6 +124,24 @@ fv_gemm_t_kernel(const __grid_constant__ CUtensorMap tmA, const FvGemmTParams p)
     const int nk = (k_len + TBK - 1) / TBK;
     const bool partial = p.ksplit > 1;
 
+    // The expanding threads' copies of their weight indices go out first of all (they need no barrier and no tensor
+    // memory, and their first bytes take about a microsecond to arrive): thread t of warps 0-15 copies, for stage kb,
+    // the 16 bytes of chunk k_begin / 32 + 4 kb + (t / 128) of column n0 + t % 128, one commit group per stage; rows
+    // past K read as zeros.
+    if (warp < EXP_WARPS) {
+        const int n = n0 + 32 * (warp & 3) + lane;
+        const uint4* vsrc = reinterpret_cast<const uint4*>(p.vindex) + n;
+        const int kc0 = k_begin / 32 + (warp >> 2);
+        uint4* vdst = reinterpret_cast<uint4*>(smem + G::VI_OFF) + threadIdx.x;
+#pragma unroll
+        for (int kb = 0; kb < TNK; ++kb) {
+            const int kc = kc0 + 4 * kb;
+            const bool valid = kb < nk && kc < p.kchunks;
+            cp_async16(vdst + kb * (EXP_WARPS * 32), valid ? vsrc + static_cast<size_t>(kc) * p.N : vsrc, valid);
+            cp_async_commit();
+        }
+    }
+
     if (threadIdx.x == 0) {
         TTRACE(0);
 #ifdef P2CU_TRACE
@@ -189,18 +207,24 @@ fv_gemm_t_kernel(const __grid_constant__ CUtensorMap tmA, const FvGemmTParams p)
     } else if (warp == MMA_WARP) {
         // ---------------- MMA issue: D[128 cols x MT rows] += W^T[tmem] * A^T[smem] ----------------
         if (lane == 0) {
-            for (int kb = 0; kb < nk; ++kb) {
-                if (!mbar_wait(&wfull[kb], 0, DEV_TIMEOUT_READY, p.err, abort_flag)) break;
+            // Stages come in pairs (the expanding warps release two at a time): one fence per pair.
+            for (int kb = 0; kb < nk; kb += 2) {
+                const int kn = kb + 1 < nk ? 2 : 1;
+                if (!mbar_wait(&wfull[kb + kn - 1], 0, DEV_TIMEOUT_READY, p.err, abort_flag)) break;
                 TTRACE(25 + kb);
                 if (!mbar_wait(&full_a[kb], 0, DEV_TIMEOUT_FULL, p.err, abort_flag)) break;
+                if (kn == 2 && !mbar_wait(&full_a[kb + 1], 0, DEV_TIMEOUT_FULL, p.err, abort_flag)) break;
                 tc_fence_after();
-                const uint32_t a_base = smem_u32(a_tiles + kb * G::A_BYTES);
+                for (int u = 0; u < kn; ++u) {
+                    const uint32_t a_base = smem_u32(a_tiles + (kb + u) * G::A_BYTES);
 #pragma unroll
-                for (int ks = 0; ks < TBK / 32; ++ks) {
-                    // A rows of 128 bytes (K-major), 8-row groups 1024 bytes apart; a K step of 32 moves 32 bytes
-                    // inside the swizzle atom. The weights of K step ks: TMEM columns W_COL + 32 kb + 8 ks.
-                    const uint64_t bdesc = smem_desc(a_base + ks * 32, 16, 1024, SWZ_128B);
-                    mma_i8_ts(tmem, tmem + W_COL + 32 * kb + 8 * ks, bdesc, G::IDESC, (kb > 0 || ks > 0) ? 1u : 0u);
+                    for (int ks = 0; ks < TBK / 32; ++ks) {
+                        // A rows of 128 bytes (K-major), 8-row groups 1024 bytes apart; a K step of 32 moves 32 bytes
+                        // inside the swizzle atom. The weights of K step ks: TMEM columns W_COL + 32 kb + 8 ks.
+                        const uint64_t bdesc = smem_desc(a_base + ks * 32, 16, 1024, SWZ_128B);
+                        mma_i8_ts(tmem, tmem + W_COL + 32 * (kb + u) + 8 * ks, bdesc, G::IDESC,
+                                  (kb + u > 0 || ks > 0) ? 1u : 0u);
+                    }
                 }
                 TTRACE(17 + kb);
             }
@@ -215,19 +239,7 @@ fv_gemm_t_kernel(const __grid_constant__ CUtensorMap tmA, const FvGemmTParams p)
         const int g = warp >> 2, q = warp & 3;
         const int nl = 32 * q + lane, n = n0 + nl;
         const uint32_t lane_base = static_cast<uint32_t>(32 * q) << 16;
-        // This thread's 16 bytes of weight indices for stage kb: chunk k_begin / 32 + 4 kb + g of column n. Every
-        // stage's copy goes out at once (the weights are constant: no dependency wait), one commit group per stage;
-        // rows past K read as zeros.
-        const uint4* vsrc = reinterpret_cast<const uint4*>(p.vindex) + n;
-        const int kc0 = k_begin / 32 + g;
-        uint4* vdst = reinterpret_cast<uint4*>(smem + G::VI_OFF) + threadIdx.x;
-#pragma unroll
-        for (int kb = 0; kb < TNK; ++kb) {
-            const int kc = kc0 + 4 * kb;
-            const bool valid = kb < nk && kc < p.kchunks;
-            cp_async16(vdst + kb * (EXP_WARPS * 32), valid ? vsrc + static_cast<size_t>(kc) * p.N : vsrc, valid);
-            cp_async_commit();
-        }
+        const uint4* vdst = reinterpret_cast<const uint4*>(smem + G::VI_OFF) + threadIdx.x;   // this thread's copies
         const uint32_t clo = static_cast<uint32_t>(clo_of(p.lo[n], p.hi[n]));
         const uint32_t pal_lo = (clo << 8) | (((0x100u - clo) & 0xFFu) << 16) | (0x7Fu << 24);
         const uint32_t pal_hi = 0x81u | (((2u * clo) & 0xFFu) << 8) | (0xFEu << 16);
