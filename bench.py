@@ -54,10 +54,16 @@ def gemm_bytes(M, K, N, beta, codes=False) -> int:
     return M * K + w + 8 * N + 4 * M * N + (4 * M * N if beta != 0.0 else 0)
 
 
-def block_traffic():
-    """DRAM bytes per step of the block GEMMs (int8w, planes) from the committed ncu capture, or None."""
+TRAFFIC_FILES = {"vindex": "fv_gemm_t_block_T375_traffic.md", "planes": "fv_gemm_block_T375_traffic.md"}
+
+
+def block_traffic(weights):
+    """DRAM bytes per step of the block GEMMs (int8w) from a committed ncu capture of the same kernels (a static
+    figure: ncu cannot run inside the bench), or None."""
     import re
-    f = ROOT / "profiles" / "fv_gemm_block_T375_traffic.md"
+    if weights not in TRAFFIC_FILES:
+        return None
+    f = ROOT / "profiles" / TRAFFIC_FILES[weights]
     if not f.exists():
         return None
     m = re.search(r"^traffic_bytes_per_step: (\d+)$", f.read_text(), re.M)
@@ -73,61 +79,58 @@ def load_peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons, sampled in the background during the timed region."""
-    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
-              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-              "clocks_event_reasons.sw_power_cap")
+    """SM clock and throttle reasons sampled through NVML by a background thread about every half millisecond; the
+    summary keeps the samples taken between mark_start() and mark_end() (the timed region), and says so."""
+    REASONS = (("hw_slowdown", 0x8), ("sw_thermal_slowdown", 0x20), ("hw_thermal_slowdown", 0x40),
+               ("sw_power_cap", 0x4))
 
     def __init__(self, device_index: int):
         self.dev = device_index
-        self.proc = None
-        self.lines = []
+        self.samples = []
         self.thread = None
+        self.stop = False
+        self.t0 = self.t1 = None
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.dev}", f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "50"],
-                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.thread = threading.Thread(target=self._read, daemon=True)
+            import pynvml
+            pynvml.nvmlInit()
+            h = pynvml.nvmlDeviceGetHandleByIndex(self.dev)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+            reasons = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                pynvml.nvmlDeviceGetCurrentClocksThrottleReasons
+
+            def loop():
+                while not self.stop:
+                    t = time.perf_counter()
+                    self.samples.append((t, pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM), reasons(h)))
+                    time.sleep(0.0005)
+
+            self.thread = threading.Thread(target=loop, daemon=True)
             self.thread.start()
-        except (OSError, FileNotFoundError):
-            self.proc = None
+        except Exception:   # no NVML: the summary says there were no samples
+            self.thread = None
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
+    def mark_start(self):
+        self.t0 = time.perf_counter()
+
+    def mark_end(self):
+        self.t1 = time.perf_counter()
 
     def __exit__(self, *exc):
-        if self.proc:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
+        self.stop = True
+        if self.thread:
             self.thread.join(timeout=2)
 
     def summary(self):
-        rows = []
-        for ln in self.lines:
-            parts = [x.strip() for x in ln.split(",")]
-            if len(parts) < 8:
-                continue
-            try:
-                rows.append((float(parts[0]), float(parts[1]), parts[3:]))
-            except ValueError:
-                continue
+        inside = [x for x in self.samples if self.t0 is not None and self.t1 is not None and self.t0 <= x[0] <= self.t1]
+        rows, where = (inside, "timed region") if inside else (self.samples, "around the timed region")
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"], "samples": 0}
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = set()
-        for _, _, r in rows:
-            for name, v in zip(names, r[1:5]):
-                if v.lower() == "active":
-                    reasons.add(name)
-        return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": max(r[1] for r in rows),
-                "reasons": sorted(reasons), "samples": len(rows)}
+        active = sorted({name for _, _, r in rows for name, bit in self.REASONS if r & bit})
+        return {"sm_mhz": statistics.median(r[1] for r in rows), "sm_max_mhz": self.max_mhz, "reasons": active,
+                "samples": len(rows), "sampled": f"NVML every 0.5 ms, {where}"}
 
 
 def dist_setup(args):
@@ -330,13 +333,16 @@ def run_ours(args, world, rank, local):
 
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
+        time.sleep(0.01)   # the sampler's first samples
         torch.cuda.synchronize()
+        clocks.mark_start()
         with torch.cuda.stream(stream):
             start.record(stream)
             for i in range(args.steps):
                 graphs[i % nsets].replay()
             end.record(stream)
         end.synchronize()
+        clocks.mark_end()
     torch.cuda.synchronize()
     barrier(world)
     ms = start.elapsed_time(end)
@@ -367,55 +373,224 @@ def run_ours(args, world, rank, local):
                 "h2d_bytes_per_step": world * e2e["h2d_bytes_per_step"],
                 "d2h_bytes_per_step": world * e2e["d2h_bytes_per_step"]})
 
+    n_split = sum(1 for (_, _, K, _, _, _) in gemms if K > 1024)
     line = None
     if rank == 0:
+        traffic = block_traffic(args.weights) if args.mode == "int8w" else None
         line = {"metric": METRIC, "value": value, "unit": "TMAC/s", "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
                 "scaling": "weak", "vs_baseline": None, "dtype": "int8" if mode != pkg.EXACT else "f32",
                 "data": "synthetic",
-                "config": {"workload": f"one FastConformer block's nine five-value GEMMs at T={T_FRAMES} "
-                                       "(BASELINE configs[1]): fp32 A quantised per row, then the tcgen05 GEMM",
+                "config": {"workload": f"BASELINE configs[1]: one block's nine five-value GEMMs at T={T_FRAMES}, fp32 "
+                                       "A quantised per row then the tcgen05 GEMM",
                            "mode": args.mode, "weights": args.weights, "T": T_FRAMES, "macs_per_step": macs,
                            "l2": f"inputs rotate over {nsets} copies ({nsets * first.bytes() / 2**20:.0f} MiB > 2x L2)",
-                           "parallelism": f"replicas x{world} (independent windows)"},
+                           "parallelism": f"replicas x{world}"},
                 "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                             "frac": achieved / peak,
-                             "traffic": block_traffic() if (args.mode == "int8w" and args.weights == "planes")
-                             else None,
-                             "traffic_source": "profiles/fv_gemm_block_T375_traffic.md: dram__bytes_read.sum + "
-                                               "dram__bytes_write.sum of the nine launches of one step (ncu), bytes",
-                             "peak_kind": peak_kind,
-                             "kernel": f"fv_gemm_kernel ({args.weights}; nine launches of a step)",
-                             "algo_bytes_per_step": algo_bytes, "gemm_us_per_step": gemm_ms * 1e3},
-                "gpu_launches": args.steps * 2 * len(gemms),
+                             "frac": achieved / peak, "traffic": traffic,
+                             "traffic_kind": "static ncu capture (profiles/" + TRAFFIC_FILES[args.weights] + ")"
+                             if traffic else None,
+                             "peak_kind": peak_kind, "algo_bytes_per_step": algo_bytes,
+                             "gemm_us_per_step": gemm_ms * 1e3,
+                             "kernel": "fv_gemm_t_kernel" if args.weights == "vindex" and args.mode == "int8w"
+                             else "fv_gemm_kernel"},
+                "gpu_launches": args.steps * (2 * len(gemms) + n_split),
                 "clocks": clocks.summary(),
                 "e2e": e2e}
+    extras = {}
     if not args.no_encoder:
-        enc = encoder_ours(args, world, rank, local, torch, pkg)
-        if rank == 0:
-            line["encoder"] = enc
+        extras["encoder"] = encoder_ours(args, world, rank, local, torch, pkg)
     if not args.no_decoder:
-        dec = decoder_ours(args, world, rank, local, torch, pkg)
-        mel = mel_ours(args, world, rank, local, torch, pkg)
-        if rank == 0:
-            line["decoder"] = dec
-            line["mel"] = mel
-            line["transcribe"] = transcribe_ours(pkg, local)
-        long_line = long_audio_ours(pkg, world, rank, local)
-        if rank == 0:
-            line["long_audio"] = long_line
+        extras["decoder"] = decoder_ours(args, world, rank, local, torch, pkg)
+        extras["mel"] = mel_ours(args, world, rank, local, torch, pkg)
+        extras["long_audio"] = long_audio_ours(pkg, world, rank, local)
+    cfg = None
+    if not args.no_configs and world == 1:   # the per-config objects are single-GPU measurements
+        cfg = configs_ours(args, world, rank, local, torch, pkg, value, gemm_ms, algo_bytes, peak)
     if rank == 0:
-        if world == 1 and not args.no_cpu_baseline:
+        cpu = world == 1 and not args.no_cpu_baseline
+        if cpu:
             line["cpu_baseline"] = cpu_baseline()
-            if not args.no_encoder:
-                line["encoder"]["cpu_baseline"] = encoder_reference()
-            if not args.no_decoder:
-                line["decoder"]["cpu_baseline"] = decoder_reference()
-                line["mel"]["cpu_baseline"] = mel_reference()
-                for cfg in line["transcribe"]:
-                    cfg["cpu_baseline"] = transcribe_reference(cfg["mel_frames"])
-                line["long_audio"]["cpu_baseline"] = long_audio_reference()
+        for name, obj in extras.items():
+            line[name] = compact(obj)
+        if cpu:
+            if "encoder" in line:
+                line["encoder"]["cpu"] = compact_cpu(encoder_reference())
+            if "decoder" in line:
+                line["decoder"]["cpu"] = compact_cpu(decoder_reference())
+                line["mel"]["cpu"] = compact_cpu(mel_reference())
+                line["long_audio"]["cpu"] = compact_cpu(long_audio_reference())
+        if cfg is not None:
+            if cpu:
+                for key, n_mel in (("c2", 3000), ("c4", 300)):
+                    cfg[key]["cpu_ms_exact"] = round(transcribe_reference(n_mel)["value"], 1)
+            line["configs"] = cfg
         print(json.dumps(line))
+
+
+def compact(obj):
+    """The headline-style fields of a sub-object (value, unit, time, e2e), without the long descriptions."""
+    keep = {k: obj[k] for k in ("value", "unit", "ms_per_step", "tokens_rank0", "windows", "mode", "weights")
+            if k in obj}
+    for k in ("e2e", "transcribe_audio"):
+        if k in obj:
+            keep[k] = {kk: obj[k][kk] for kk in ("value", "unit", "ms_per_step", "h2d_bytes_per_step",
+                                                 "d2h_bytes_per_step") if kk in obj[k]}
+    return keep
+
+
+def compact_cpu(c):
+    return None if c is None else {"value": c["value"], "unit": c["unit"], "cores": c["cores"], "kind": c["kind"]}
+
+
+def time_replays(torch, stream, graphs, steps):
+    """Milliseconds per replay over `steps` replays rotating over `graphs` (CUDA events on `stream`)."""
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        for i in range(3):
+            graphs[i % len(graphs)].replay()
+        e0.record(stream)
+        for i in range(steps):
+            graphs[i % len(graphs)].replay()
+        e1.record(stream)
+    e1.synchronize()
+    return e0.elapsed_time(e1) / steps
+
+
+def step_graphs(pkg, torch, dev, stream, mode, gemms, weights, seed, gemm_only=False):
+    """CUDA graphs of one step of `gemms` over enough input copies to exceed twice L2, as the headline's."""
+    codes, vix = weights == "codes", weights == "vindex"
+    first = GpuSet(pkg, torch, dev, seed, mode, gemms, codes, vix)
+    nsets = max(2, int(np.ceil(2 * L2_BYTES / first.bytes())))
+    sets = [first] + [GpuSet(pkg, torch, dev, seed + 1 + i, mode, gemms, codes, vix) for i in range(nsets - 1)]
+    graphs = []
+    with torch.cuda.stream(stream):
+        for st in sets:
+            st.run(pkg, mode, stream)
+            if gemm_only:
+                st.quantise(pkg, stream)
+        stream.synchronize()
+        for st in sets:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                (st.run_gemm_only if gemm_only else st.run)(pkg, mode, stream)
+            graphs.append(g)
+    torch.cuda.synchronize()
+    pkg.check_device(stream)
+    return graphs
+
+
+def int8_peak() -> tuple[float, str]:
+    """The int8 tcgen05 MMA rate the large-M fractions divide by: measured on this GPU by the probes library when it
+    is built, else the rate that probe measured on this pool's B200s (2284 TMAC/s, profiles/probes_tma_mma.md)."""
+    import ctypes as C
+    if (ROOT / "phonon-2-c_b200" / "libphonon2_probes.so").exists():
+        L = probes_lib()
+        v = C.c_double()
+        if L.p2cu_probe_int8_mma(0, 4000, C.byref(v)) == 0:
+            return v.value / 1e12, "measured in this run"
+    return 2284.0, "measured on this pool (profiles/probes_tma_mma.md)"
+
+
+def configs_ours(args, world, rank, local, torch, pkg, headline, gemm_ms, algo_bytes, hbm_peak):
+    """Every BASELINE config as a compact object (the headline is configs[1] int8w): c0 the single GEMM, c1 the block
+    in every mode and weight form, large_m the north star's M >= 4096 shape, c2 / c4 one window end to end in both
+    modes (the speech-like model, so that greedy decoding emits tokens), c3 is the `encoder` object."""
+    from phonon2_b200 import model as Mo
+    dev = torch.device("cuda", local)
+    stream = torch.cuda.Stream(device=dev)
+    gemms = block_gemms()
+    seed = 500 + rank * 100
+    out = {}
+    steps = max(10, min(args.steps, 100))
+    # c0: ff1 1024 -> 4096 at M = 375 alone: quantiser + GEMM, and the GEMM alone against its HBM bound
+    c0 = [g for g in gemms if g[0] == "ff1.linear1"]
+    _, M0, K0, N0, _, _ = c0[0]
+    t_step = time_replays(torch, stream, step_graphs(pkg, torch, dev, stream, pkg.INT8W, c0, args.weights, seed),
+                          steps)
+    t_gemm = time_replays(torch, stream, step_graphs(pkg, torch, dev, stream, pkg.INT8W, c0, args.weights, seed,
+                                                     gemm_only=True), steps)
+    b0 = gemm_bytes(M0, K0, N0, 0.0)
+    out["c0"] = {"tmacs": round(M0 * K0 * N0 / (t_step * 1e9), 1), "us": round(t_step * 1e3, 2),
+                 "gemm_us": round(t_gemm * 1e3, 2), "gemm_frac_hbm": round(b0 / (t_gemm * 1e-3) / 1e9 / hbm_peak, 3)}
+    # c1: the block in each mode / weight form (TMAC/s per step, the quantiser included)
+    c1 = {"int8w_" + args.weights: round(headline, 1)}
+    for mode, weights in (("int8", "planes"), ("exact", "planes"), ("int8w", "codes"), ("int8w", "planes")):
+        key = f"{mode}_{weights}"
+        if key in c1:
+            continue
+        t = time_replays(torch, stream, step_graphs(pkg, torch, dev, stream, pkg.MODES[mode], gemms, weights, seed),
+                         steps if mode != "exact" else 5)
+        c1[key] = round(block_macs() / (t * 1e9), 1)
+    c1["unit"] = "TMAC/s"
+    out["c1"] = c1
+    # large M (north star: >= 60 % of the int8 peak at K = 1024, N = 4096, M >= 4096), the GEMM alone
+    peak_i8, peak_kind = int8_peak()
+    lm = {"int8_peak_tmacs": round(peak_i8), "peak_kind": peak_kind}
+    for Mbig in (4096, 8192):
+        for weights in ("codes", "planes"):
+            t = time_replays(torch, stream, step_graphs(pkg, torch, dev, stream, pkg.INT8W,
+                                                        [("ff1.linear1", Mbig, 1024, 4096, 1.0, 0.0)], weights, seed,
+                                                        gemm_only=True), 20)
+            v = Mbig * 1024 * 4096 / (t * 1e9)
+            lm[f"M{Mbig}_{weights}"] = {"tmacs": round(v), "frac_int8": round(v / peak_i8, 3)}
+    out["large_m"] = lm
+    # c2 / c4: one window end to end, host mel in, host tokens out
+    sm = Mo.SyntheticModel(seed=1, attn_out_gain=Mo.SPEECH_ATTN_OUT_GAIN)
+    dm = pkg.DeviceModel(sm.struct)
+    for key, n_mel in (("c2", 3000), ("c4", 300)):
+        mel = Mo.mel(n_mel, seed=n_mel)
+        res = {"mel_frames": n_mel}
+        for _ in range(2):
+            toks = pkg.host_transcribe_windows(sm.struct, [mel], devices=[local])
+        t0 = time.perf_counter()
+        for _ in range(5):
+            toks = pkg.host_transcribe_windows(sm.struct, [mel], devices=[local])
+        res["ms_int8w"] = round((time.perf_counter() - t0) / 5 * 1e3, 2)
+        res["tokens_int8w"] = int(len(toks[0]))
+        res["ms_exact"], res["tokens_exact"] = plan_transcribe_ms(pkg, torch, dm, mel, pkg.EXACT, local)
+        res["api"] = "p2_b200_transcribe_windows (int8w); encoder + decoder plans with host copies (exact)"
+        out[key] = res
+    dm.close()
+    # the weight stream of config 4 (BASELINE: HBM GB/s on the planes): the bytes every pass reads at least once (the
+    # value-index planes the window-sized GEMMs read, plus lo / hi) over the end-to-end time - a lower bound
+    vi_bytes = sum(pkg.fv_vindex_bytes(K, N) + 8 * N for (_, K, N, _, _, _) in synth_block_shapes()) * 24
+    out["c4"]["weight_stream_gbs_lower_bound"] = round(vi_bytes / (out["c4"]["ms_int8w"] * 1e-3) / 1e9, 1)
+    return out if rank == 0 else None
+
+
+def synth_block_shapes():
+    from phonon2_b200 import synth
+    return synth.BLOCK_SHAPES
+
+
+def plan_transcribe_ms(pkg, torch, dm, mel, mode, local, steps=3):
+    """One window through the encoder plan and the decoder in `mode`, timed end to end by the wall clock: the mel
+    copied up from page-locked memory, the encoder's graph, the decoder launch, the tokens read back."""
+    from phonon2_b200.device import device_view
+    enc = pkg.Encoder(dm, [mel.shape[0]], mode)
+    dec = pkg.Decoder(dm, 1, enc.total_frames)
+    mel_h = torch.empty(mel.shape, dtype=torch.float32, pin_memory=True)
+    mel_h.numpy()[...] = mel
+    dst = device_view(enc.mel_ptr, mel.shape)
+    stream = torch.cuda.Stream(device=torch.device("cuda", local))
+
+    def once():
+        with torch.cuda.stream(stream):
+            dst.copy_(mel_h, non_blocking=True)
+        enc.run(stream)
+        dec.decode(enc.out_ptr, enc.frames, stream)
+        return dec.read(stream)
+
+    for _ in range(2):
+        toks = once()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        toks = once()
+    ms = (time.perf_counter() - t0) / steps * 1e3
+    dec.close()
+    enc.close()
+    return round(ms, 2), int(len(toks[0]))
 
 
 # ---- the encoder (BASELINE configs 2-4): audio seconds per second --------------------------------------------------
@@ -646,7 +821,7 @@ def mel_ours(args, world, rank, local, torch, pkg, steps=5):
     barrier(world)
     ms_max = max_over_ranks(ms, world)
     audio_s = sum(frames) * ENC_SECONDS_PER_FRAME
-    sm = M.SyntheticModel(seed=1)
+    sm = M.SyntheticModel(seed=1, attn_out_gain=M.SPEECH_ATTN_OUT_GAIN)
     e2e_ms = 0.0
     n_tok = 0
     if mine:
@@ -721,39 +896,14 @@ def plane_bytes(sm) -> int:
     return sum(a.nbytes for k, a in sm.arrays.items() if k.endswith((".signs", ".flags", ".lo", ".hi")))
 
 
-def transcribe_ours(pkg, local, steps=5):
-    """Configs 2 and 4 end to end: host mel in, host tokens out, through p2_b200_transcribe_windows (the encoder in
-    the library's mode, then the decoder on the encoder's frames without leaving the device)."""
-    from phonon2_b200 import model as M
-    sm = M.SyntheticModel(seed=1)
-    planes = plane_bytes(sm)
-    out = []
-    for name, n in (("window", 3000), ("short", 300)):
-        mel = M.mel(n, seed=n)
-        for _ in range(2):   # plans and their graph capture (on a plan's second run) outside the timing
-            toks = pkg.host_transcribe_windows(sm.struct, [mel], devices=[local])
-        t0 = time.perf_counter()
-        for _ in range(steps):
-            pkg.host_transcribe_windows(sm.struct, [mel], devices=[local])
-        ms = (time.perf_counter() - t0) / steps * 1e3
-        out.append({"config": name, "workload": encoder_workload(name)[1], "mel_frames": n,
-                    "value": ms, "unit": "ms", "higher_is_better": False, "steps": steps,
-                    "tokens": int(len(toks[0])), "h2d_bytes": mel.nbytes, "d2h_bytes": 12 * int(len(toks[0])),
-                    "api": "p2_b200_transcribe_windows, wall clock (mel host -> tokens host)",
-                    # BASELINE configs[4] asks for the plane stream: every plane is read at least once per encoder
-                    # pass, so planes / end-to-end time bounds the rate from below
-                    "plane_stream": {"value": planes / (ms * 1e-3) / 1e9, "unit": "GB/s", "bytes": planes,
-                                     "bound": "lower: plane bytes / end-to-end time"}})
-    return out
-
-
 def transcribe_reference(n_mel, reps=2):
-    """phonon-2-c's p2_encoder (exact) then p2_greedy_decode on the host cores for one window of n_mel frames."""
+    """phonon-2-c's p2_encoder (exact) then p2_greedy_decode on the host cores for one window of n_mel frames (the
+    speech-like synthetic model, as the configs' objects use)."""
     orc = ge.load_oracle()
     if not orc.ref_available():
         return None
     from phonon2_b200 import model as M
-    sm = M.SyntheticModel(seed=1)
+    sm = M.SyntheticModel(seed=1, attn_out_gain=M.SPEECH_ATTN_OUT_GAIN)
     mel = M.mel(n_mel, seed=n_mel)
     t0 = time.perf_counter()
     for _ in range(reps):
@@ -774,7 +924,7 @@ def long_audio_ours(pkg, world, rank, local, steps=3):
     recording; value = all ranks' audio seconds / the slowest rank's wall time per recording."""
     from phonon2_b200 import model as M
     import torch
-    sm = M.SyntheticModel(seed=1)
+    sm = M.SyntheticModel(seed=1, attn_out_gain=M.SPEECH_ATTN_OUT_GAIN)
     x_h = torch.empty(int(LONG_SECONDS * 16000), dtype=torch.float32, pin_memory=True)   # page-locked recording
     x = x_h.numpy()
     x[...] = M.audio_with_pauses(LONG_SECONDS, 7 + rank)
@@ -793,8 +943,7 @@ def long_audio_ours(pkg, world, rank, local, steps=3):
     return {"metric": "long-form transcription audio-sec/sec", "value": world * LONG_SECONDS / (ms_max / 1e3),
             "unit": "audio-s/s", "ms_per_step": ms_max, "steps": steps, "scaling": "weak",
             "workload": f"{LONG_SECONDS:.0f} s of synthetic long-form 16 kHz audio per rank (bursts of 1-6 s under a "
-                        "syllable envelope between pauses of 0.05-1.4 s, seeded); the synthetic model leaves most "
-                        "windows without tokens, so nearly every window is re-decoded twice",
+                        "syllable envelope between pauses of 0.05-1.4 s, seeded), the speech-like synthetic model",
             "windows_by_depth_rank0": depths, "encoder_frames_rank0": frames, "tokens_rank0": n_tok,
             "h2d_bytes_per_step": 4 * int(x.shape[0]), "d2h_bytes_per_step": 12 * n_tok,
             "gpu_launches_per_step": "one mel + one encoder pass + one decoder launch per split depth and GPU, one "
@@ -813,7 +962,7 @@ def long_audio_reference(seconds=70.0):
     from oracle import weights_file as wf
     x = M.audio_with_pauses(LONG_SECONDS, 7)[: int(seconds * 16000)]
     with tempfile.TemporaryDirectory() as d:
-        wf.write_model_dir(M.SyntheticModel(seed=1), d)
+        wf.write_model_dir(M.SyntheticModel(seed=1, attn_out_gain=M.SPEECH_ATTN_OUT_GAIN), d)
         t0 = time.perf_counter()
         orc.ref_transcribe(d, x)
         dt = time.perf_counter() - t0
@@ -846,11 +995,28 @@ def run_encoder_only(args, world, rank, local):
     print(json.dumps(line))
 
 
+def probes_lib():
+    """The hardware-rate probes (phonon-2-c_b200/libphonon2_probes.so, built beside the product library)."""
+    import ctypes as C
+    L = C.CDLL(str(ROOT / "phonon-2-c_b200" / "libphonon2_probes.so"))
+    for name in ("p2cu_probe_int8_mma", "p2cu_probe_int8_ring", "p2cu_probe_tma_load"):
+        getattr(L, name).argtypes = [C.c_int, C.c_int, C.POINTER(C.c_double)]
+        getattr(L, name).restype = C.c_int
+    L.p2cu_probes_last_error.restype = C.c_char_p
+    return L
+
+
+def probe_check(L, rc):
+    if rc != 0:
+        raise RuntimeError(f"probe failed ({rc}): {L.p2cu_probes_last_error().decode()}")
+
+
 def measured_int8_peak(pkg, pair=False) -> float:
     """The tcgen05 int8 MMA rate measured on this GPU (p2cu_probe_int8_mma), in TMAC/s."""
     import ctypes as C
+    L = probes_lib()
     v = C.c_double()
-    pkg.check(pkg.lib().p2cu_probe_int8_mma(1 if pair else 0, 4000, C.byref(v)))
+    probe_check(L, L.p2cu_probe_int8_mma(1 if pair else 0, 4000, C.byref(v)))
     return v.value / 1e12
 
 
@@ -871,7 +1037,7 @@ def run_probes(args):
                        (1, "each stage handed back by the MMAs' commit, a producer arrive and the odd CTA's relay"),
                        (2, "each stage handed back by the MMAs' commit and producer arrives, the odd CTA's on the "
                            "even CTA's barrier")):
-        pkg.check(pkg.lib().p2cu_probe_int8_ring(mode, 4000, C.byref(v)))
+        probe_check(probes_lib(), probes_lib().p2cu_probe_int8_ring(mode, 4000, C.byref(v)))
         print(json.dumps({"probe": "int8_mma_ring", "mode": mode, "value": v.value / 1e12, "unit": "TMAC/s",
                           "what": "CTA-pair MMAs (M=256 N=256 K=128 per step) over a ring of six 32 KB stages, "
                                   "zero operands, no copies: " + what}))
@@ -879,7 +1045,7 @@ def run_probes(args):
         for warps in (1, 2, 4):
             if 2 * warps * 128 * box_rows > 196608:
                 continue
-            pkg.check(pkg.lib().p2cu_probe_tma_load(warps, box_rows, C.byref(v)))
+            probe_check(probes_lib(), probes_lib().p2cu_probe_tma_load(warps, box_rows, C.byref(v)))
             print(json.dumps({"probe": "tma_load", "issuing_warps": warps, "box_bytes": 128 * box_rows,
                               "value": v.value / 1e9, "unit": "GB/s per SM",
                               "what": "tiled TMA loads of 128-byte rows from an L2-resident int8 matrix, two boxes "
@@ -903,8 +1069,9 @@ def run_gemm_sweep(args):
         shapes = [tuple(int(x) for x in args.gemm_shape.split(","))]
     for (M, K, N) in shapes:
         w = synth.five_value(K, N, seed=1)
-        for codes in ((args.weights == "codes",) if args.gemm_shape else (False, True)):
-            B = DeviceFiveValue(w, dev, codes=codes)
+        for form in ((args.weights,) if args.gemm_shape else ("planes", "codes", "vindex")):
+            codes = form == "codes"
+            B = DeviceFiveValue(w, dev, codes=codes, vindex=form == "vindex")
             A = torch.from_numpy(synth.activations(M, K, seed=2)).to(dev)
             q = torch.empty((M, K), dtype=torch.int8, device=dev)
             sc = torch.empty(M, dtype=torch.float32, device=dev)
@@ -938,7 +1105,7 @@ def run_gemm_sweep(args):
             us = e0.elapsed_time(e1) / (10 * reps) * 1e3
             tmacs = M * K * N / (us / 1e6) / 1e12
             print(json.dumps({"metric": "five-value int8 GEMM TMAC/s", "M": M, "K": K, "N": N, "mode": args.mode,
-                              "weights": "codes" if codes else "planes", "us": us, "value": tmacs, "unit": "TMAC/s",
+                              "weights": form, "us": us, "value": tmacs, "unit": "TMAC/s",
                               "frac_of_nominal_int8": tmacs / 2250.0, "measured_int8_peak": peak,
                               "frac_of_measured_int8": tmacs / peak,
                               "hbm_bound_us": (M * K + (K * N if codes else 3 * K * N // 8) + 4 * M * N) / 6534.8e3}))
@@ -1011,9 +1178,12 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--mode", choices=["int8w", "int8", "exact"], default="int8w")
-    ap.add_argument("--weights", choices=["planes", "codes", "vindex"], default="planes",
-                    help="planes: expand the sign/magnitude planes in every GEMM (the reference's default); codes: "
-                         "the int8w code cache (the reference's P2_CACHE_CODES), int8w only")
+    ap.add_argument("--weights", choices=["planes", "codes", "vindex"], default="vindex",
+                    help="vindex: the planes as the library uploads them (the reference's sign/magnitude planes plus "
+                         "the value-index plane packed from them once, which the int8w GEMMs of one window read); "
+                         "planes: the reference's planes alone, expanded in every GEMM; codes: the int8w code cache "
+                         "(the reference's P2_CACHE_CODES), int8w only")
+    ap.add_argument("--no-configs", action="store_true", help="skip the per-config objects at the end of the line")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-encoder", action="store_true", help="skip the encoder (config 3) part of the line")
     ap.add_argument("--no-decoder", action="store_true",

@@ -126,7 +126,8 @@ P2CU_API int p2cu_fv_pack_vindex(const P2cuFiveValue *B, unsigned int *vindex, v
  * on a device looks up the array's device address (cudaGetSymbolAddress, that device current): make that first call
  * before any stream capture. Every call on a device shares the array, so calls whose kernels overlap on the GPU (on
  * different streams, or from different threads) race on it and must be serialised by the caller; nothing in it
- * needs to start at zero. */
+ * needs to start at zero. The address looked up on the first call belongs to the device's context: after
+ * cudaDeviceReset on a device, this entry point must not be called on that device again in the process. */
 P2CU_API int p2cu_sgemm_fvb_noalloc(int M, int N, int K, float alpha, const float *A, int lda, const P2cuFiveValue *B,
                                     int mode, float beta, float *C, int ldc, void *stream);
 
@@ -247,17 +248,6 @@ P2CU_API int p2cu_seg_long_gap(const P2Token *toks, int n_toks, int n_samples);
 P2CU_API int p2cu_seg_dropped_out(const float *rms, int n_blocks, int n_samples, const P2Token *toks, int n_toks,
                                   int *gap_from, int *gap_to, float *speech);
 
-/* ---- Measurements of the hardware the kernels are built around (allocate their own buffers; a few launches) ----
- * p2cu_probe_int8_mma: the tcgen05 int8 MMA rate in MACs per second over all SMs, from shared-memory operands, one
- * CTA per SM (pair = 0, M = 128 per MMA) or on CTA pairs (pair != 0, M = 256); iters K = 128 steps per SM.
- * p2cu_probe_tma_load: tiled TMA load bytes per second per SM from an L2-resident matrix, boxes of box_rows 128-byte
- * rows (8-256) issued by `warps` warps (1-4) of each CTA, two boxes in flight per warp. */
-P2CU_API int p2cu_probe_int8_mma(int pair, int iters, double *macs_per_s);
-P2CU_API int p2cu_probe_tma_load(int warps, int box_rows, double *bytes_per_s_per_sm);
-/* p2cu_probe_int8_ring: the CTA-pair MMA stream (iters K = 128 steps per pair) over a ring of six 32 KB stages handed
- * back through barriers as in the pair GEMM, without copies: mode 0 no hand-back after the first round, mode 1
- * through a producer arrive and the odd CTA's relay, mode 2 with the odd CTA arriving on the even CTA's barrier. */
-P2CU_API int p2cu_probe_int8_ring(int mode, int iters, double *macs_per_s);
 /* p2cu_probe_wait_timeout: the kernels' bounded-wait path, exercised without a fault - one warp waits on an mbarrier
  * phase that nothing completes, gives up after `limit` polls (1 .. 2^20), records code 1 in the device error word and
  * returns; `seconds` is the launch's duration. Returns what p2cu_check_device then returns: P2CU_EDEVICE (the word is

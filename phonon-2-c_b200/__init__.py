@@ -103,9 +103,6 @@ SIGNATURES = {
     "p2cu_seg_speech_share": (_f, [_vp, _i, _i, _i, _i, _f]),
     "p2cu_seg_long_gap": (_i, [_vp, _i, _i]),
     "p2cu_seg_dropped_out": (_i, [_vp, _i, _i, _vp, _i, C.POINTER(_i), C.POINTER(_i), C.POINTER(_f)]),
-    "p2cu_probe_int8_mma": (_i, [_i, _i, C.POINTER(C.c_double)]),
-    "p2cu_probe_tma_load": (_i, [_i, _i, C.POINTER(C.c_double)]),
-    "p2cu_probe_int8_ring": (_i, [_i, _i, C.POINTER(C.c_double)]),
     "p2cu_probe_wait_timeout": (_i, [C.c_uint, C.POINTER(C.c_double)]),
     # include/phonon2.h: the reference's encoder and decoder entry points
     "p2_encoder": (_i, [_vp, _vp, _i, C.POINTER(_vp), C.POINTER(_i)]),

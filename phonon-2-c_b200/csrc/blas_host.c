@@ -236,7 +236,8 @@ static Entry *five_entry(const FiveValueB *b, int K, int N, Ctx *c, const char *
     Entry *e = reg_find(b->signs, W_FIVE, c->device, print);
     if (e) return e;
     size_t s_b = (size_t)K * N / 4, f_b = (size_t)K * N / 8, v_b = (size_t)N * sizeof(float);
-    size_t o_f = al256(s_b), o_lo = o_f + al256(f_b), o_hi = o_lo + al256(v_b), total = o_hi + al256(v_b);
+    size_t o_f = al256(s_b), o_lo = o_f + al256(f_b), o_hi = o_lo + al256(v_b), o_vi = o_hi + al256(v_b);
+    size_t total = o_vi + al256(p2cu_fv_vindex_bytes(K, N));
     e = (Entry *)calloc(1, sizeof(*e));
     if (!e) die(who, "out of memory");
     check_cuda(cudaMalloc(&e->block, total), who);
@@ -252,6 +253,10 @@ static Entry *five_entry(const FiveValueB *b, int K, int N, Ctx *c, const char *
     e->fv.hi = (const float *)(d + o_hi);
     e->fv.codes = NULL;
     e->fv.K = K; e->fv.N = N;
+    /* the value-index plane, read by the int8w GEMMs of few rows (include/p2cuda.h p2cu_fv_pack_vindex) */
+    check_p2(p2cu_fv_pack_vindex(&e->fv, (unsigned int *)(d + o_vi), c->stream), who);
+    check_cuda(cudaStreamSynchronize(c->stream), who);
+    e->fv.vindex = (const unsigned int *)(d + o_vi);
     reg_insert(e);
     return e;
 }

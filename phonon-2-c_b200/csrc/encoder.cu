@@ -24,6 +24,7 @@
 #include "encoder_ops.h"
 #include "attn_tc.h"
 #include "kernels.h"
+#include "fv_gemm.h"
 #include "model.h"
 
 namespace {
@@ -152,33 +153,42 @@ int upload_model(const P2Model* m, int codes, P2cuModel** out) {
         delete d;
         return fail_fmt(P2CU_EINVAL, "p2cu_model_upload: %s", u.what);
     }
-    // int8w code planes (the reference's P2_CACHE_CODES, csrc/weights.c:381-395): K x N bytes per five-value weight.
-    size_t codes_bytes = 0;
+    // Every five-value weight also gets its value-index plane (p2cu_fv_pack_vindex, 4 bits per weight: the int8w GEMMs
+    // of one window read it), and with `codes` the int8w code plane (the reference's P2_CACHE_CODES,
+    // csrc/weights.c:381-395: K x N bytes).
+    size_t codes_bytes = 0, vindex_bytes = 0;
     std::vector<DWeight*> fvs;
-    if (codes) {
-        for (int i = 0; i < NB; ++i) {
-            DBlock& o = d->blk[i];
-            for (DWeight* w : {&o.ff1a, &o.ff1b, &o.qkv, &o.pos, &o.out, &o.pw1, &o.pw2, &o.ff2a, &o.ff2b})
-                if (w->kind == P2_W_FV) {
-                    fvs.push_back(w);
-                    codes_bytes += (static_cast<size_t>(w->K) * w->N + 255) & ~size_t(255);
-                }
-        }
+    for (int i = 0; i < NB; ++i) {
+        DBlock& o = d->blk[i];
+        for (DWeight* w : {&o.ff1a, &o.ff1b, &o.qkv, &o.pos, &o.out, &o.pw1, &o.pw2, &o.ff2a, &o.ff2b})
+            if (w->kind == P2_W_FV) {
+                fvs.push_back(w);
+                vindex_bytes += (p2cu_fv_vindex_bytes(w->K, w->N) + 255) & ~size_t(255);
+                if (codes) codes_bytes += (static_cast<size_t>(w->K) * w->N + 255) & ~size_t(255);
+            }
     }
-    cudaError_t e = cudaMalloc(&d->arena, u.total + codes_bytes);
+    cudaError_t e = cudaMalloc(&d->arena, u.total + vindex_bytes + codes_bytes);
     if (e != cudaSuccess) {
         delete d;
         return p2cu::cuda_error(e, "p2cu_model_upload: cudaMalloc");
     }
-    d->bytes = u.total + codes_bytes;
+    d->bytes = u.total + vindex_bytes + codes_bytes;
     for (const auto& it : u.items) {
         e = cudaMemcpy(d->arena + it.off, it.host, it.bytes, cudaMemcpyHostToDevice);
         if (e != cudaSuccess) break;
         *it.slot = d->arena + it.off;
     }
-    if (e == cudaSuccess && codes) {
+    if (e == cudaSuccess) {
         size_t off = u.total;
         for (DWeight* w : fvs) {
+            uint32_t* vi = reinterpret_cast<uint32_t*>(d->arena + off);
+            e = p2cu::fv_vindex_launch(w->fv.signs, w->fv.flags, w->K, w->N, vi, 0);
+            if (e != cudaSuccess) break;
+            w->fv.vindex = vi;
+            off += (p2cu_fv_vindex_bytes(w->K, w->N) + 255) & ~size_t(255);
+        }
+        for (DWeight* w : fvs) {
+            if (!codes || e != cudaSuccess) break;
             int8_t* c = reinterpret_cast<int8_t*>(d->arena + off);
             e = p2cu::fv_codes_launch(w->fv.signs, w->fv.flags, w->fv.lo, w->fv.hi, w->K, w->N, c, 0);
             if (e != cudaSuccess) break;
@@ -186,7 +196,7 @@ int upload_model(const P2Model* m, int codes, P2cuModel** out) {
             off += (static_cast<size_t>(w->K) * w->N + 255) & ~size_t(255);
         }
         if (e == cudaSuccess) e = cudaDeviceSynchronize();
-        d->codes = 1;
+        d->codes = codes ? 1 : 0;
     }
     if (e != cudaSuccess) {
         cudaFree(d->arena);

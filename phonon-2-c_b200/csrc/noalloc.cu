@@ -9,7 +9,8 @@
 // until the process exits. In host code the name g_noalloc_scratch is only a stand-in for the symbol, not a device
 // address, so it is never passed to a kernel; its device address is looked up once per device with
 // cudaGetSymbolAddress, with that device current, on the first call made on that device; make that first call before
-// any stream capture.
+// any stream capture. The address is kept for the process's life: after cudaDeviceReset the module (and the array) of
+// the old context are gone, so the entry point must not be called on that device again.
 #include <cstdint>
 #include <cstdio>
 #include <mutex>

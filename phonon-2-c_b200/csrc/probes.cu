@@ -10,22 +10,73 @@
 //     remotely on the even CTA's barrier (mode 2), against the same MMAs issued without waiting (mode 0). The gap is
 //     what the handshake alone costs: the MMAs of a step can start only after the MMAs six steps back have
 //     completed and their release has travelled round the ring.
-//   * p2cu_probe_wait_timeout: the bounded-wait path itself - one warp waits, through the kernels' own mbar_wait, on
-//     an mbarrier phase that nothing completes, gives up after a given number of polls, records its code in the device
-//     error word and returns, and the host reads the error through p2cu_check_device with the context still usable.
-// Both allocate their own buffers, run a few launches, and report through out-parameters. Every wait is bounded.
+// Each allocates its own buffers, runs a few launches, and reports through out-parameters. Every wait is bounded.
+// Built as its own library (libphonon2_probes.so, declared in probes.h): the product library does not carry them.
 #include <cstdint>
 #include <cstdio>
 #include <cuda.h>
 #include <cuda_runtime.h>
-#include "p2cuda.h"
-#include "gemm.h"
+#include <cstdarg>
+#include "probes.h"
 #include "ptx.cuh"
-
-using p2cu::fail_fmt;
 
 namespace p2cu {
 namespace {
+
+// This library's own error text, device error word and tensor maps (it is built apart from libphonon2_b200.so).
+char g_probe_msg[256] = "";
+__device__ uint32_t g_probe_err;
+
+int fail_fmt(int code, const char* fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_probe_msg, sizeof(g_probe_msg), fmt, ap);
+    va_end(ap);
+    return code;
+}
+
+int cuda_error(cudaError_t e, const char* what) { return fail_fmt(-2, "%s: %s", what, cudaGetErrorString(e)); }
+
+uint32_t* device_error_word() {
+    void* p = nullptr;
+    return cudaGetSymbolAddress(&p, g_probe_err) == cudaSuccess ? static_cast<uint32_t*>(p) : nullptr;
+}
+
+// Synchronise and read (then clear) the error word: -3 when a probe's bounded wait ran out.
+int check_device() {
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return cuda_error(e, "probe");
+    uint32_t v = 0, zero = 0;
+    if ((e = cudaMemcpyFromSymbol(&v, g_probe_err, sizeof(v))) != cudaSuccess) return cuda_error(e, "error word");
+    if (v) {
+        cudaMemcpyToSymbol(g_probe_err, &zero, sizeof(zero));
+        return fail_fmt(-3, "a probe's wait ran out (device error code %u)", v);
+    }
+    return 0;
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// An int8 [outer][inner] tensor map, rows `stride` bytes apart, boxes box_in x box_out, 128-byte swizzle.
+int make_tile_map(CUtensorMap* map, const void* base, int, uint64_t inner, uint64_t outer, uint64_t stride,
+                  uint32_t box_in, uint32_t box_out, int, const char* what) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+        return fail_fmt(-2, "cuTensorMapEncodeTiled is not available");
+    const cuuint64_t dims[2] = {inner, outer};
+    const cuuint64_t strides[1] = {stride};
+    const cuuint32_t box[2] = {box_in, box_out};
+    const cuuint32_t estr[2] = {1, 1};
+    CUresult r = reinterpret_cast<EncodeTiledFn>(p)(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base),
+                                                    dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? 0 : fail_fmt(-2, "%s: cuTensorMapEncodeTiled failed (%d)", what, static_cast<int>(r));
+}
 
 constexpr int PROBE_THREADS = 128;
 constexpr uint32_t PROBE_TIMEOUT = 30;
@@ -235,57 +286,17 @@ int sms_of_device() {
     return n;
 }
 
-// One warp; its barrier expects one arrival and gets none, so phase 0 never completes and lane 0's wait runs out
-// after `limit` polls (DEV_TIMEOUT_FULL into the error word, the abort flag set).
-__global__ void __launch_bounds__(32) wait_timeout_kernel(uint32_t limit, uint32_t* err) {
-    __shared__ uint64_t bar;
-    __shared__ int abort_flag;
-    if (threadIdx.x == 0) {
-        mbar_init(&bar, 1);
-        abort_flag = 0;
-        fence_barrier_init();
-    }
-    __syncwarp();
-    int ok = 1;
-    if (threadIdx.x == 0) ok = mbar_wait(&bar, 0, DEV_TIMEOUT_FULL, err, &abort_flag, limit) ? 1 : 0;
-    ok = __shfl_sync(0xffffffffu, ok, 0);
-    if (ok && err) atomicCAS(err, DEV_OK, DEV_BAD_ARGS);   // a phase nobody completed cannot have completed
-}
-
 }  // namespace
 }  // namespace p2cu
 
 extern "C" {
 
-// The device timeout path: a wait on a barrier nothing completes gives up after `limit` polls (1 .. 2^20) and
-// reports it. Returns what p2cu_check_device returns afterwards: P2CU_EDEVICE with code 1 when the path works.
-int p2cu_probe_wait_timeout(unsigned limit, double* seconds) {
-    using namespace p2cu;
-    if (!seconds || limit < 1 || limit > (1u << 20)) return fail_fmt(P2CU_EINVAL, "p2cu_probe_wait_timeout: arguments");
-    if (int rc = p2cu_check_device(nullptr)) return rc;   // start from a clear error word
-    cudaEvent_t e0 = nullptr, e1 = nullptr;
-    cudaError_t e = cudaEventCreate(&e0);
-    if (e == cudaSuccess) e = cudaEventCreate(&e1);
-    if (e == cudaSuccess) e = cudaEventRecord(e0);
-    if (e == cudaSuccess) {
-        wait_timeout_kernel<<<1, 32>>>(limit, device_error_word());
-        e = cudaGetLastError();
-    }
-    if (e == cudaSuccess) e = cudaEventRecord(e1);
-    if (e == cudaSuccess) e = cudaEventSynchronize(e1);
-    float ms = 0.f;
-    if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, e0, e1);
-    if (e0) cudaEventDestroy(e0);
-    if (e1) cudaEventDestroy(e1);
-    if (e != cudaSuccess) return cuda_error(e, "p2cu_probe_wait_timeout");
-    *seconds = ms * 1e-3;
-    return p2cu_check_device(nullptr);
-}
+const char* p2cu_probes_last_error(void) { return p2cu::g_probe_msg; }
 
 // The int8 MMA rate (MACs per second, all SMs) over `iters` K = 128 steps per SM; pair != 0 on CTA pairs.
 int p2cu_probe_int8_mma(int pair, int iters, double* macs_per_s) {
     using namespace p2cu;
-    if (!macs_per_s || iters < 1 || iters > (1 << 20)) return fail_fmt(P2CU_EINVAL, "p2cu_probe_int8_mma: arguments");
+    if (!macs_per_s || iters < 1 || iters > (1 << 20)) return fail_fmt(-1, "p2cu_probe_int8_mma: arguments");
     const int sms = sms_of_device();
     const int smem = 1024 + 16384 + 32768 + 64;
     cudaError_t e = cudaFuncSetAttribute(pair ? mma_pair_probe_kernel : mma_probe_kernel,
@@ -322,16 +333,16 @@ int p2cu_probe_int8_mma(int pair, int iters, double* macs_per_s) {
     if (e0) cudaEventDestroy(e0);
     if (e1) cudaEventDestroy(e1);
     if (e != cudaSuccess) return cuda_error(e, "p2cu_probe_int8_mma");
-    if (int rc = p2cu_check_device(nullptr)) return rc;
+    if (int rc = check_device()) return rc;
     const double macs = (pair ? 256.0 : 128.0) * 256.0 * 128.0 * iters * (pair ? sms / 2 : sms);
     *macs_per_s = macs / (best * 1e-3);
-    return P2CU_OK;
+    return 0;
 }
 
 int p2cu_probe_int8_ring(int mode, int iters, double* macs_per_s) {
     using namespace p2cu;
     if (!macs_per_s || mode < 0 || mode > 2 || iters < 1 || iters > (1 << 20))
-        return fail_fmt(P2CU_EINVAL, "p2cu_probe_int8_ring: arguments");
+        return fail_fmt(-1, "p2cu_probe_int8_ring: arguments");
     const int sms = sms_of_device();
     const int smem = 1024 + RING_STAGES * RING_STAGE_BYTES + 256;
     cudaError_t e = cudaFuncSetAttribute(mma_ring_probe_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
@@ -362,9 +373,9 @@ int p2cu_probe_int8_ring(int mode, int iters, double* macs_per_s) {
     if (e0) cudaEventDestroy(e0);
     if (e1) cudaEventDestroy(e1);
     if (e != cudaSuccess) return cuda_error(e, "p2cu_probe_int8_ring");
-    if (int rc = p2cu_check_device(nullptr)) return rc;
+    if (int rc = check_device()) return rc;
     *macs_per_s = 256.0 * 256.0 * 128.0 * iters * (sms / 2) / (best * 1e-3);
-    return P2CU_OK;
+    return 0;
 }
 
 // Tiled TMA load throughput (bytes per second per SM) with `warps` issuing warps per CTA and boxes of `box_rows`
@@ -373,7 +384,7 @@ int p2cu_probe_tma_load(int warps, int box_rows, double* bytes_per_s_per_sm) {
     using namespace p2cu;
     if (!bytes_per_s_per_sm || warps < 1 || warps > 4 || box_rows < 8 || box_rows > 256 || (box_rows & 7) ||
         2 * warps * 128 * box_rows > 196608)
-        return fail_fmt(P2CU_EINVAL, "p2cu_probe_tma_load: warps 1-4, box rows 8-256 (multiple of 8), "
+        return fail_fmt(-1, "p2cu_probe_tma_load: warps 1-4, box rows 8-256 (multiple of 8), "
                         "2 x warps x box <= 192 KB");
     const int rows = 8192, width = 128;   // an [8192][1024] matrix read as 128-byte columns of its first 128 bytes
     const int stride = 1024;
@@ -389,7 +400,7 @@ int p2cu_probe_tma_load(int warps, int box_rows, double* bytes_per_s_per_sm) {
     const int boxes = 400;
     float best = 0.f;
     cudaEvent_t e0 = nullptr, e1 = nullptr;
-    if (rc == P2CU_OK) {
+    if (rc == 0) {
         e = cudaFuncSetAttribute(tma_probe_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e == cudaSuccess) e = cudaEventCreate(&e0);
         if (e == cudaSuccess) e = cudaEventCreate(&e1);
@@ -409,8 +420,8 @@ int p2cu_probe_tma_load(int warps, int box_rows, double* bytes_per_s_per_sm) {
     if (e0) cudaEventDestroy(e0);
     if (e1) cudaEventDestroy(e1);
     cudaFree(buf);
-    if (rc == P2CU_OK) rc = p2cu_check_device(nullptr);
-    if (rc == P2CU_OK) *bytes_per_s_per_sm = static_cast<double>(boxes / warps * warps) * 128 * box_rows /
+    if (rc == 0) rc = check_device();
+    if (rc == 0) *bytes_per_s_per_sm = static_cast<double>(boxes / warps * warps) * 128 * box_rows /
                                               (best * 1e-3);
     return rc;
 }

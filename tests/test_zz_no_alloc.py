@@ -31,11 +31,13 @@ def _noalloc_call(pkg, torch, dev, M, N, K, alpha, A_d, B, mode, beta, C0):
 def test_noalloc_matches_workspace_entry_on_two_calls_in_a_row(pkg, synth, cuda):
     import torch
     from phonon2_b200.device import DeviceFiveValue
-    cases = [(375, 4096, 1024, 0.5, 1.0),    # K > 1024: the per-block partials go through the fixed array
-             (375, 1024, 4096, 1.0, 0.0)]    # then a call that leaves other contents behind
-    for i, (M, K, N, alpha, beta) in enumerate(cases):
+    cases = [(375, 4096, 1024, 0.5, 1.0, False),   # K > 1024: the per-block partials go through the fixed array
+             (375, 1024, 4096, 1.0, 0.0, False),   # then a call that leaves other contents behind
+             (200, 3072, 384, 1.0, 1.0, False),    # K > 1024 again over the stale bytes, other M and N
+             (130, 2048, 512, 1.0, 0.0, True)]     # the tensor-memory kernel (value-index plane), K > 1024
+    for i, (M, K, N, alpha, beta, vindex) in enumerate(cases):
         w = synth.five_value(K, N, seed=50 + i)
-        B = DeviceFiveValue(w, cuda)
+        B = DeviceFiveValue(w, cuda, vindex=vindex)
         A_d = torch.from_numpy(synth.activations(M, K, seed=60 + i)).to(cuda)
         C0 = np.random.default_rng(70 + i).standard_normal((M, N)).astype(np.float32)
         want = _workspace_call(pkg, torch, cuda, M, N, K, alpha, A_d, B, pkg.INT8W, beta, C0)
@@ -55,3 +57,27 @@ def test_noalloc_refuses_shapes_beyond_its_array(pkg, synth, cuda):
         pkg.sgemm_fvb_noalloc(M, N, K, 1.0, A_d.data_ptr(), K, B.struct, pkg.INT8W, 0.0, C_d.data_ptr(), N)
     assert e.value.code == pkg.P2CU_EINVAL and "fixed array" in str(e.value)
     pkg.check_device()
+
+
+def test_noalloc_allocates_nothing(pkg, synth, cuda):
+    """The property the entry point exists for: after a first call on the device, further calls - the split-K path,
+    the tensor-memory kernel and the SIMT kernel (N % 128 != 0) - leave the device's free memory unchanged."""
+    import torch
+    from phonon2_b200.device import DeviceFiveValue
+    cases = []
+    for i, (M, K, N, vindex) in enumerate([(300, 4096, 1024, False), (375, 1024, 2048, True), (64, 1024, 144, False)]):
+        B = DeviceFiveValue(synth.five_value(K, N, seed=80 + i), cuda, vindex=vindex)
+        A_d = torch.from_numpy(synth.activations(M, K, seed=90 + i)).to(cuda)
+        C_d = torch.zeros((M, N), dtype=torch.float32, device=cuda)
+        cases.append((M, K, N, B, A_d, C_d))
+    for (M, K, N, B, A_d, C_d) in cases:   # first calls: the array's address is looked up, kernels get configured
+        pkg.sgemm_fvb_noalloc(M, N, K, 1.0, A_d.data_ptr(), K, B.struct, pkg.INT8W, 0.0, C_d.data_ptr(), N)
+    torch.cuda.synchronize()
+    free_before, _ = torch.cuda.mem_get_info()
+    for _ in range(3):
+        for (M, K, N, B, A_d, C_d) in cases:
+            pkg.sgemm_fvb_noalloc(M, N, K, 1.0, A_d.data_ptr(), K, B.struct, pkg.INT8W, 0.0, C_d.data_ptr(), N)
+    torch.cuda.synchronize()
+    free_after, _ = torch.cuda.mem_get_info()
+    pkg.check_device()
+    assert free_after == free_before, (free_before, free_after)
