@@ -1052,6 +1052,62 @@ def run_probes(args):
                                       "in flight per issuing warp"}))
 
 
+def run_transcribe(args, local):
+    """--workload transcribe: one window of --mel-frames mel frames (300 = configs[4], 3000 = configs[2]) from host
+    mel to host tokens in int8w, the synthetic speech-like model. Prints the end-to-end time of
+    p2_b200_transcribe_windows (wall clock) and its split measured with CUDA events on one stream through the plans it
+    is built from: mel copy up, the encoder's graph, the decoder launch, the token read-back."""
+    import torch
+    pkg = ge.load_package()
+    from phonon2_b200 import model as Mo
+    from phonon2_b200.device import device_view
+    torch.cuda.set_device(local)
+    n_mel = args.mel_frames
+    sm = Mo.SyntheticModel(seed=1, attn_out_gain=Mo.SPEECH_ATTN_OUT_GAIN)
+    mel = Mo.mel(n_mel, seed=n_mel)
+    steps = max(1, min(args.steps, 50))
+    for _ in range(args.warmup):
+        toks = pkg.host_transcribe_windows(sm.struct, [mel], devices=[local])
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        toks = pkg.host_transcribe_windows(sm.struct, [mel], devices=[local])
+    e2e_ms = (time.perf_counter() - t0) / steps * 1e3
+    dm = pkg.DeviceModel(sm.struct)
+    enc = pkg.Encoder(dm, [n_mel], pkg.INT8W)
+    dec = pkg.Decoder(dm, 1, enc.total_frames)
+    mel_h = torch.empty(mel.shape, dtype=torch.float32, pin_memory=True)
+    mel_h.numpy()[...] = mel
+    dst = device_view(enc.mel_ptr, mel.shape)
+    stream = torch.cuda.Stream()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    split = np.zeros(3)
+    for it in range(args.warmup + steps):
+        with torch.cuda.stream(stream):
+            ev[0].record(stream)
+            dst.copy_(mel_h, non_blocking=True)
+            ev[1].record(stream)
+        enc.run(stream)
+        with torch.cuda.stream(stream):
+            ev[2].record(stream)
+        dec.decode(enc.out_ptr, enc.frames, stream)
+        with torch.cuda.stream(stream):
+            ev[3].record(stream)
+        got = dec.read(stream)
+        if it >= args.warmup:
+            split += [ev[0].elapsed_time(ev[1]), ev[1].elapsed_time(ev[2]), ev[2].elapsed_time(ev[3])]
+    split /= steps
+    assert len(got) == len(toks) and all(np.array_equal(a, b) for a, b in zip(got, toks)), \
+        "plans and the host entry point disagree"
+    dec.close()
+    enc.close()
+    dm.close()
+    print(json.dumps({"workload": "transcribe", "mel_frames": n_mel, "encoder_frames": enc.frames[0],
+                      "tokens": int(len(toks[0])), "steps": steps, "e2e_ms": round(e2e_ms, 3),
+                      "split_ms": {"mel_up": round(split[0], 3), "encoder_graph": round(split[1], 3),
+                                   "decoder": round(split[2], 3)},
+                      "api": "p2_b200_transcribe_windows (wall clock); split by CUDA events through the plans"}))
+
+
 def run_gemm_sweep(args):
     """--workload gemm-sweep: the five-value GEMM alone (quantised A resident) at growing M, K = 1024, N = 4096 (the
     north star's large-M shape) and K = 4096, N = 1024; planes and the code cache. One JSON line per case."""
@@ -1188,13 +1244,15 @@ def main():
     ap.add_argument("--no-encoder", action="store_true", help="skip the encoder (config 3) part of the line")
     ap.add_argument("--no-decoder", action="store_true",
                     help="skip the decoder (config 3 windows) and transcription (configs 2, 4) parts of the line")
-    ap.add_argument("--workload", choices=["block-gemms", "encoder", "gemm-sweep", "probes"], default="block-gemms",
+    ap.add_argument("--workload", choices=["block-gemms", "encoder", "gemm-sweep", "probes", "transcribe"],
+                    default="block-gemms",
                     help="block-gemms: configs[1] with the encoder object (default); encoder: the encoder alone; "
                          "gemm-sweep: the GEMM alone at growing M (one line per case)")
     ap.add_argument("--encoder-config", choices=["long-audio", "window", "short"], default="long-audio",
                     help="--workload encoder: configs[3] (64 windows), [2] (one 30 s window) or [4] (3 s)")
     ap.add_argument("--windows", type=int, default=0, help="--workload encoder long-audio: only the first N windows")
     ap.add_argument("--gemm-shape", default="", help="--workload gemm-sweep: only this M,K,N (with --weights)")
+    ap.add_argument("--mel-frames", type=int, default=300, help="--workload transcribe: the window's mel frames")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     world, rank, local = dist_setup(args)
@@ -1209,6 +1267,9 @@ def main():
         elif args.workload == "probes":
             if rank == 0:
                 run_probes(args)
+        elif args.workload == "transcribe":
+            if rank == 0:
+                run_transcribe(args, local)
         else:
             run_ours(args, world, rank, local)
     finally:

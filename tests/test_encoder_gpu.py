@@ -56,6 +56,14 @@ def _rel(got, ref):
     return float(np.abs(got - ref).max() / np.abs(ref).max())
 
 
+def _elementwise_rel(got, ref):
+    """Percentiles (50, 99, 99.9, 100) of |got - ref| / |ref| over the outputs with |ref| >= 1 % of max |ref| (an
+    element-wise relative error is meaningless at values near zero), and the share of outputs that covers."""
+    big = np.abs(ref) >= 1e-2 * np.abs(ref).max()
+    r = np.abs(got - ref)[big] / np.abs(ref)[big]
+    return [float(np.percentile(r, q)) for q in (50, 99, 99.9, 100)], float(big.mean())
+
+
 # ---- the row ops against the reference's own functions -------------------------------------------------------------
 
 def test_layer_norm_rows(pkg, orc, cuda):
@@ -147,6 +155,9 @@ def test_encoder_exact_matches_reference(pkg, orc, cuda, model, dev_model, n_mel
     got, = _run(pkg, torch, dev_model, [mel], pkg.EXACT)
     ref = orc.ref_encoder(model.struct, mel, "exact")
     assert got.shape == ref.shape == (M.frames_after_subsampling(n_mel), 640)
+    pct, share = _elementwise_rel(got, ref)
+    print(f"exact T'={got.shape[0]}: normwise {_rel(got, ref):.2e}; element-wise relative p50 {pct[0]:.2e} "
+          f"p99 {pct[1]:.2e} p99.9 {pct[2]:.2e} max {pct[3]:.2e} over {100 * share:.1f} % of the outputs")
     assert _rel(got, ref) <= EXACT_TOL, _rel(got, ref)
 
 
