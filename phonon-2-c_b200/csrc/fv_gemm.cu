@@ -212,33 +212,35 @@ fv_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         }
     } else if (warp == G::MMAW) {
         // ---------------- MMA issue ----------------
-        if (lane == 0) {
-            for (int kb = 0; kb < nk; ++kb) {
-                const int s = kb % STAGES, r = kb / STAGES;
-                if (!mbar_wait(PLANES ? &bready[s] : &full[s], r & 1, DEV_TIMEOUT_READY, p.err, abort_flag)) break;
-                if (!mbar_wait(&afull[s], r & 1, DEV_TIMEOUT_READY, p.err, abort_flag)) break;
-                tc_fence_after();
-                TRACE(80 + kb);
-                const uint32_t a_base = smem_u32(a_tile(s));
-                const uint32_t b_base = smem_u32(b_tile(s));
+        // The whole warp runs the loop converged and waits with all lanes; one elected lane issues (issue from code
+        // one lane runs alone, branches inside it, was measured at about half the rate).
+        const uint32_t el = elect_one();
+        for (int kb = 0; kb < nk; ++kb) {
+            const int s = kb % STAGES, r = kb / STAGES;
+            if (!warp_wait_all(PLANES ? &bready[s] : &full[s], r & 1, DEV_TIMEOUT_READY, p.err, abort_flag)) break;
+            if (!warp_wait_all(&afull[s], r & 1, DEV_TIMEOUT_READY, p.err, abort_flag)) break;
+            tc_fence_after();
+            TRACE(80 + kb);
+            const uint32_t a_base = smem_u32(a_tile(s));
+            const uint32_t b_base = smem_u32(b_tile(s));
 #pragma unroll
-                for (int ks = 0; ks < BK / 32; ++ks) {
-                    // A: K-major 128-byte rows, 8-row groups 1024 bytes apart; a K step of 32 moves 32 bytes inside
-                    // the swizzle atom. B: MN-major atom columns ATOM_W bytes wide, REGION bytes apart (the leading
-                    // offset; with a single atom column it is never used and is set to SBO so that no reading of it
-                    // leaves the tile), 8-row K groups SBO bytes apart; a K step of 32 rows moves 4 groups.
-                    const uint64_t adesc = smem_desc(a_base + ks * 32, 16, 1024, SWZ_128B);
-                    const uint64_t bdesc = smem_desc(b_base + ks * 4 * G::SBO, G::N_ATOMS > 1 ? G::REGION : G::SBO,
-                                                     G::SBO, G::B_SWZ);
-                    mma_i8(tmem, adesc, bdesc, IDESC, (kb > 0 || ks > 0) ? 1u : 0u);
-                }
-                mma_commit(&empty[s]);
+            for (int ks = 0; ks < BK / 32; ++ks) {
+                // A: K-major 128-byte rows, 8-row groups 1024 bytes apart; a K step of 32 moves 32 bytes inside
+                // the swizzle atom. B: MN-major atom columns ATOM_W bytes wide, REGION bytes apart (the leading
+                // offset; with a single atom column it is never used and is set to SBO so that no reading of it
+                // leaves the tile), 8-row K groups SBO bytes apart; a K step of 32 rows moves 4 groups.
+                const uint64_t adesc = smem_desc(a_base + ks * 32, 16, 1024, SWZ_128B);
+                const uint64_t bdesc = smem_desc(b_base + ks * 4 * G::SBO, G::N_ATOMS > 1 ? G::REGION : G::SBO,
+                                                 G::SBO, G::B_SWZ);
+                mma_i8_lead(el, tmem, adesc, bdesc, IDESC, (kb > 0 || ks > 0) ? 1u : 0u);
             }
-            mma_commit(accfull);
-            // Every MMA issued has completed once `drain` flips (bounded: also on the abort path).
-            mma_commit(drain);
-            mbar_wait(drain, 0, DEV_TIMEOUT_DRAIN, p.err, abort_flag);
+            mma_commit_lead(el, &empty[s]);
         }
+        mma_commit_lead(el, accfull);
+        // Every MMA issued has completed once `drain` flips (bounded, and waited for on the abort path too).
+        mma_commit_lead(el, drain);
+        volatile int keep_waiting = 0;
+        warp_wait_all(drain, 0, DEV_TIMEOUT_DRAIN, p.err, &keep_waiting);
         __syncwarp();
     } else {
         if (PLANES && warp >= 4) {

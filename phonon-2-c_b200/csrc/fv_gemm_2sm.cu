@@ -258,45 +258,47 @@ fv_gemm_2sm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
     } else if (warp == G::MMAW) {
         if (lead) {
             // ---------------- MMA issue for the pair: tile i into accumulator i % 2 ----------------
-            if (lane == 0) {
-                int g = 0, it = 0;
-                bool ok = true;
-                for (int t = pair; ok && t < total; t += npairs, ++it) {
-                    const PairTile d = pair_tile(t, m_tiles, n_tiles, p.K);
-                    const int b = it & 1;
-                    if (!mbar_wait(&tempty[b], ((it >> 1) & 1) ^ 1, DEV_TIMEOUT_ACC, p.err, abort_flag)) break;
-                    tc_fence_after();
-                    const uint32_t acc = tmem + static_cast<uint32_t>(b * QBN);
-                    for (int kb = 0; kb < d.nk; ++kb, ++g) {
-                        const int s = g % STAGES, r = g / STAGES;
-                        if (!mbar_wait(&full[s], r & 1, DEV_TIMEOUT_READY, p.err, abort_flag) ||
-                            (PLANES && !mbar_wait(&bready[s], r & 1, DEV_TIMEOUT_READY, p.err, abort_flag))) {
-                            ok = false;
-                            break;
-                        }
-                        QTRACE(g, g < 40);
-                        if (PLANES && !mbar_wait(&peer[s], r & 1, DEV_TIMEOUT_READY, p.err, abort_flag)) {
-                            ok = false;
-                            break;
-                        }
-                        QTRACE(40 + g, g < 40);
-                        tc_fence_after();
-                        const uint32_t a_base = smem_u32(a_tile(s));
-                        const uint32_t b_base = smem_u32(b_tile(s));
-#pragma unroll
-                        for (int ks = 0; ks < QBK / 32; ++ks) {
-                            const uint64_t adesc = smem_desc(a_base + ks * 32, 16, 1024, SWZ_128B);
-                            const uint64_t bdesc = smem_desc(b_base + ks * 4 * G::SBO, G::SBO, G::SBO, SWZ_128B);
-                            mma_i8_pair(acc, adesc, bdesc, IDESC, (kb > 0 || ks > 0) ? 1u : 0u);
-                        }
-                        mma_commit_pair(&empty[s], 0x3);
+            // The whole warp runs the loop converged and waits with all lanes; one elected lane issues (issue from
+            // code one lane runs alone, branches inside it, was measured at about half the rate).
+            const uint32_t el = elect_one();
+            int g = 0, it = 0;
+            bool ok = true;
+            for (int t = pair; ok && t < total; t += npairs, ++it) {
+                const PairTile d = pair_tile(t, m_tiles, n_tiles, p.K);
+                const int b = it & 1;
+                if (!warp_wait_all(&tempty[b], ((it >> 1) & 1) ^ 1, DEV_TIMEOUT_ACC, p.err, abort_flag)) break;
+                tc_fence_after();
+                const uint32_t acc = tmem + static_cast<uint32_t>(b * QBN);
+                for (int kb = 0; kb < d.nk; ++kb, ++g) {
+                    const int s = g % STAGES, r = g / STAGES;
+                    if (!warp_wait_all(&full[s], r & 1, DEV_TIMEOUT_READY, p.err, abort_flag) ||
+                        (PLANES && !warp_wait_all(&bready[s], r & 1, DEV_TIMEOUT_READY, p.err, abort_flag))) {
+                        ok = false;
+                        break;
                     }
-                    if (ok) mma_commit_pair(&tfull[b], 0x3);
-                    QTRACE(176 + it, it < 8);
+                    QTRACE(g, g < 40 && el);
+                    if (PLANES && !warp_wait_all(&peer[s], r & 1, DEV_TIMEOUT_READY, p.err, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    QTRACE(40 + g, g < 40 && el);
+                    tc_fence_after();
+                    const uint32_t a_base = smem_u32(a_tile(s));
+                    const uint32_t b_base = smem_u32(b_tile(s));
+#pragma unroll
+                    for (int ks = 0; ks < QBK / 32; ++ks) {
+                        const uint64_t adesc = smem_desc(a_base + ks * 32, 16, 1024, SWZ_128B);
+                        const uint64_t bdesc = smem_desc(b_base + ks * 4 * G::SBO, G::SBO, G::SBO, SWZ_128B);
+                        mma_i8_pair_lead(el, acc, adesc, bdesc, IDESC, (kb > 0 || ks > 0) ? 1u : 0u);
+                    }
+                    mma_commit_pair_lead(el, &empty[s], 0x3);
                 }
-                mma_commit_pair(drain, 0x1);
-                mbar_wait(drain, 0, DEV_TIMEOUT_DRAIN, p.err, abort_flag);
+                if (ok) mma_commit_pair_lead(el, &tfull[b], 0x3);
+                QTRACE(176 + it, it < 8 && el);
             }
+            mma_commit_pair_lead(el, drain, 0x1);
+            volatile int keep_waiting = 0;   // tensor memory is freed only after the MMAs are done, on every path
+            warp_wait_all(drain, 0, DEV_TIMEOUT_DRAIN, p.err, &keep_waiting);
         } else {
             // ---------------- relay (planes): each of this CTA's stages, once expanded, to the even CTA --------
             if (PLANES && lane == 0) {

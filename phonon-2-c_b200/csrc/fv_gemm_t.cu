@@ -30,7 +30,7 @@
 // (no ring: each barrier completes once). Warps 0-15 expand (warp w: TMEM lanes 32 (w % 4).., K rows 32 (w / 4) .. of
 // every stage) and then run the epilogue; warps 16-23 issue the TMA loads of A (after griddepcontrol.wait), stage i from
 // warp 16 + i: one SM's TMA takes in about 57 GB/s from boxes one thread issues and about twice that from four or more
-// issuing warps; warp 24 owns TMEM and issues the MMAs.
+// issuing warps; warp 24 owns TMEM and issues the MMAs (converged, one elected lane issuing).
 // Every wait is bounded.
 #include <cstdint>
 #include <utility>
@@ -70,7 +70,8 @@ struct TCfg {
 // weight stage in registers, 3 expansion done, 4 dependency wait returned (producer), 5 last MMA issued,
 // 6 accumulator ready, 7 stores issued; slot 8 holds the SM id; 9 + kb: A stage kb landed (its producer warp);
 // 17 + kb: the MMAs of stage kb issued; 25 + kb: weight stage kb seen complete by the MMA issuer; 33 + w: expanding
-// warp w done; 49: %globaltimer at entry (reading it takes a fraction of a microsecond, so it is read once).
+// warp w done; 41: the epilogue's accumulator loads returned (warp 0); 42: the epilogue's dependency wait returned
+// (warp 0); 49: %globaltimer at entry (reading it takes a fraction of a microsecond, so it is read once).
 #ifdef P2CU_TRACE
 constexpr int TR_CTAS = 256, TR_EV = 50, TR_LAUNCHES = 16;
 __device__ unsigned long long g_t_trace[TR_LAUNCHES * TR_CTAS * TR_EV];
@@ -206,33 +207,39 @@ fv_gemm_t_kernel(const __grid_constant__ CUtensorMap tmA, const FvGemmTParams p)
         }
     } else if (warp == MMA_WARP) {
         // ---------------- MMA issue: D[128 cols x MT rows] += W^T[tmem] * A^T[smem] ----------------
-        if (lane == 0) {
-            // Stages come in pairs (the expanding warps release two at a time): one fence per pair.
-            for (int kb = 0; kb < nk; kb += 2) {
-                const int kn = kb + 1 < nk ? 2 : 1;
-                if (!mbar_wait(&wfull[kb + kn - 1], 0, DEV_TIMEOUT_READY, p.err, abort_flag)) break;
-                TTRACE(25 + kb);
-                if (!mbar_wait(&full_a[kb], 0, DEV_TIMEOUT_FULL, p.err, abort_flag)) break;
-                if (kn == 2 && !mbar_wait(&full_a[kb + 1], 0, DEV_TIMEOUT_FULL, p.err, abort_flag)) break;
-                tc_fence_after();
-                for (int u = 0; u < kn; ++u) {
-                    const uint32_t a_base = smem_u32(a_tiles + (kb + u) * G::A_BYTES);
+        // The whole warp runs this loop converged and waits with all lanes at once; one elected lane issues each MMA
+        // through a predicate. (Issued from code that lane 0 ran alone, with the waits' branches inside it, the same
+        // MMAs went out at ~65 ns each; converged, ~37 ns, against ~27 ns of tensor-core work at N = 96.)
+        const uint32_t lead = elect_one();
+        // A rows of 128 bytes (K-major), 8-row groups 1024 bytes apart; a K step of 32 moves 32 bytes inside the
+        // swizzle atom. The descriptor's start-address field holds the address >> 4 (14 bits; shared memory addresses
+        // stay below 256 KB), so the descriptor of stage s, K step ks is the first one plus (s * A_BYTES + 32 ks) >> 4.
+        // The weights of K step ks of stage s: TMEM columns W_COL + 32 s + 8 ks.
+        const uint64_t bdesc0 = smem_desc(smem_u32(a_tiles), 16, 1024, SWZ_128B);
+        const uint32_t wcol0 = tmem + W_COL;
+        // Stages come in pairs (the expanding warps release two at a time): one fence per pair.
+        for (int kb = 0; kb < nk; kb += 2) {
+            const int kn = kb + 1 < nk ? 2 : 1;
+            if (!warp_wait_all(&wfull[kb + kn - 1], 0, DEV_TIMEOUT_READY, p.err, abort_flag)) break;
+            TTRACE(25 + kb);
+            if (!warp_wait_all(&full_a[kb], 0, DEV_TIMEOUT_FULL, p.err, abort_flag)) break;
+            if (kn == 2 && !warp_wait_all(&full_a[kb + 1], 0, DEV_TIMEOUT_FULL, p.err, abort_flag)) break;
+            tc_fence_after();
+            for (int u = 0; u < kn; ++u) {
+                const int s = kb + u;
+                const uint64_t bd = bdesc0 + static_cast<uint64_t>(s * (G::A_BYTES >> 4));
+                const uint32_t wa = wcol0 + 32 * s;
+                mma_i8_ts_lead(lead, tmem, wa, bd, G::IDESC, s > 0 ? 1u : 0u);
 #pragma unroll
-                    for (int ks = 0; ks < TBK / 32; ++ks) {
-                        // A rows of 128 bytes (K-major), 8-row groups 1024 bytes apart; a K step of 32 moves 32 bytes
-                        // inside the swizzle atom. The weights of K step ks: TMEM columns W_COL + 32 kb + 8 ks.
-                        const uint64_t bdesc = smem_desc(a_base + ks * 32, 16, 1024, SWZ_128B);
-                        mma_i8_ts(tmem, tmem + W_COL + 32 * (kb + u) + 8 * ks, bdesc, G::IDESC,
-                                  (kb + u > 0 || ks > 0) ? 1u : 0u);
-                    }
-                }
-                TTRACE(17 + kb);
+                for (int ks = 1; ks < TBK / 32; ++ks) mma_i8_ts_lead(lead, tmem, wa + 8 * ks, bd + 2 * ks, G::IDESC, 1u);
             }
-            TTRACE(5);
-            mma_commit(accfull);
-            mma_commit(drain);   // every MMA issued has completed once this flips (also on the abort path)
-            mbar_wait(drain, 0, DEV_TIMEOUT_DRAIN, p.err, abort_flag);
+            TTRACE(17 + kb);
         }
+        TTRACE(5);
+        mma_commit_lead(lead, accfull);
+        mma_commit_lead(lead, drain);   // every MMA issued has completed once this flips (also on the abort path)
+        volatile int keep_waiting = 0;  // on the abort path too: tensor memory is freed only after the MMAs are done
+        warp_wait_all(drain, 0, DEV_TIMEOUT_DRAIN, p.err, &keep_waiting);
         __syncwarp();
     } else {
         // ---------------- expansion (warps 0-15), then the epilogue ----------------
@@ -285,6 +292,7 @@ fv_gemm_t_kernel(const __grid_constant__ CUtensorMap tmA, const FvGemmTParams p)
         float* out = partial ? p.ws + (static_cast<size_t>(z) * p.m_pad) * p.N + n : p.C + n;
         const size_t ld = partial ? static_cast<size_t>(p.N) : static_cast<size_t>(p.ldc);
         griddep_wait();   // C belongs to the previous kernels until here
+        if (warp == 0 && lane == 0) TTRACE(42);
         float old[ACC ? CPW : 1][8];
         if (ACC) {
 #pragma unroll
@@ -306,6 +314,7 @@ fv_gemm_t_kernel(const __grid_constant__ CUtensorMap tmA, const FvGemmTParams p)
             for (int j = 0; j < CPW; ++j)
                 if (g + 4 * j < MT / 8) tmem_ld_32x32b_x8(tmem + lane_base + 8 * (g + 4 * j), r[j]);
             tmem_wait_ld();
+            if (warp == 0 && lane == 0) TTRACE(41);
 #pragma unroll
             for (int j = 0; j < CPW; ++j) {
                 const int ch = g + 4 * j;

@@ -105,6 +105,30 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, uint32
     return ok != 0;
 }
 
+// The same wait for a converged warp whose lanes all poll at once (no lane waits alone, so no branch leaves the warp
+// diverged): every lane sees the same phase and returns the same result. For loops that one elected lane's issue
+// follows (the MMA issuers): issue from code that one lane runs alone, with branches inside it, was measured at about
+// half the rate of the same instructions in a converged warp.
+__device__ __forceinline__ bool warp_wait_all(uint64_t* bar, uint32_t parity, uint32_t code, uint32_t* err,
+                                              volatile int* abort_flag, uint32_t limit = WAIT_LIMIT) {
+    const uint32_t a = smem_u32(bar);
+    if (mbar_test_wait(a, parity)) return true;
+    for (uint32_t i = 0; i < limit; ++i) {
+        if (mbar_try_wait(a, parity)) return true;
+        if ((i & 1023u) == 1023u && *abort_flag) return false;
+    }
+    if (err && (threadIdx.x & 31) == 0) atomicCAS(err, DEV_OK, code);
+    *abort_flag = 1;
+    return false;
+}
+
+// One lane of a converged warp: 1 in the elected lane, 0 in the others.
+__device__ __forceinline__ uint32_t elect_one() {
+    uint32_t e;
+    asm volatile("{\n\t.reg .pred p;\n\telect.sync _|p, 0xffffffff;\n\tselp.u32 %0, 1, 0, p;\n\t}" : "=r"(e));
+    return e;
+}
+
 // ---- TMA ---------------------------------------------------------------------------------------------------------
 
 // Prefetch the 128-byte line holding `p` into L2. L2 is where every SM's accesses meet, so a prefetch issued before a
@@ -269,6 +293,31 @@ __device__ __forceinline__ void mma_i8_ts(uint32_t tmem_d, uint32_t tmem_a, uint
                  :: "r"(tmem_d), "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate) : "memory");
 }
 
+// The same MMA and commit issued by the lane whose `lead` is non-zero, the whole warp executing them (a predicate,
+// not a branch, selects the lane).
+__device__ __forceinline__ void mma_i8_ts_lead(uint32_t lead, uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc,
+                                               uint32_t idesc, uint32_t accumulate) {
+    asm volatile("{\n\t.reg .pred e, p;\n\t"
+                 "setp.ne.b32 e, %5, 0;\n\t"
+                 "setp.ne.b32 p, %4, 0;\n\t"
+                 "@e tcgen05.mma.cta_group::1.kind::i8 [%0], [%1], %2, %3, p;\n\t}"
+                 :: "r"(tmem_d), "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(lead) : "memory");
+}
+__device__ __forceinline__ void mma_i8_lead(uint32_t lead, uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                            uint32_t idesc, uint32_t accumulate) {
+    asm volatile("{\n\t.reg .pred e, p;\n\t"
+                 "setp.ne.b32 e, %5, 0;\n\t"
+                 "setp.ne.b32 p, %4, 0;\n\t"
+                 "@e tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}"
+                 :: "r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(lead) : "memory");
+}
+__device__ __forceinline__ void mma_commit_lead(uint32_t lead, uint64_t* bar) {
+    asm volatile("{\n\t.reg .pred e;\n\t"
+                 "setp.ne.b32 e, %1, 0;\n\t"
+                 "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}"
+                 :: "r"(smem_u32(bar)), "r"(lead) : "memory");
+}
+
 // ---- CTA pairs (clusters of two, tcgen05 cta_group::2) ------------------------------------------------------------
 
 __device__ __forceinline__ uint32_t cluster_ctarank() {
@@ -317,6 +366,22 @@ __device__ __forceinline__ void mma_i8_pair(uint32_t tmem_d, uint64_t adesc, uin
 __device__ __forceinline__ void mma_commit_pair(uint64_t* bar, uint16_t cta_mask) {
     asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;"
                  :: "r"(smem_u32(bar)), "h"(cta_mask) : "memory");
+}
+
+// The pair MMA and its commit from the lane whose `lead` is non-zero, the whole warp executing them.
+__device__ __forceinline__ void mma_i8_pair_lead(uint32_t lead, uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                                 uint32_t idesc, uint32_t accumulate) {
+    asm volatile("{\n\t.reg .pred e, p;\n\t"
+                 "setp.ne.b32 e, %5, 0;\n\t"
+                 "setp.ne.b32 p, %4, 0;\n\t"
+                 "@e tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t}"
+                 :: "r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(lead) : "memory");
+}
+__device__ __forceinline__ void mma_commit_pair_lead(uint32_t lead, uint64_t* bar, uint16_t cta_mask) {
+    asm volatile("{\n\t.reg .pred e;\n\t"
+                 "setp.ne.b32 e, %2, 0;\n\t"
+                 "@e tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;\n\t}"
+                 :: "r"(smem_u32(bar)), "h"(cta_mask), "r"(lead) : "memory");
 }
 
 // ---- descriptors ---------------------------------------------------------------------------------------------------
