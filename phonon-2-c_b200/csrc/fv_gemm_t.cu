@@ -28,7 +28,7 @@
 //
 // One CTA: a 128-column x MT-row output tile and one 1024-row K block in eight 128-row stages, all resident at once
 // (no ring: each barrier completes once). Warps 0-15 expand (warp w: TMEM lanes 32 (w % 4).., K rows 32 (w / 4) .. of
-// every stage) and then run the epilogue; warps 16-23 issue the TMA loads of A (after griddepcontrol.wait), stage i from
+// every stage; four stages per tcgen05.wait::st) and then run the epilogue; warps 16-23 issue the TMA loads of A (after griddepcontrol.wait), stage i from
 // warp 16 + i: one SM's TMA takes in about 57 GB/s from boxes one thread issues and about twice that from four or more
 // issuing warps; warp 24 owns TMEM and issues the MMAs (converged, one elected lane issuing).
 // Every wait is bounded.
@@ -217,7 +217,7 @@ fv_gemm_t_kernel(const __grid_constant__ CUtensorMap tmA, const FvGemmTParams p)
         // The weights of K step ks of stage s: TMEM columns W_COL + 32 s + 8 ks.
         const uint64_t bdesc0 = smem_desc(smem_u32(a_tiles), 16, 1024, SWZ_128B);
         const uint32_t wcol0 = tmem + W_COL;
-        // Stages come in pairs (the expanding warps release two at a time): one fence per pair.
+        // A pair of stages per wait and fence (the expanding warps release four at a time).
         for (int kb = 0; kb < nk; kb += 2) {
             const int kn = kb + 1 < nk ? 2 : 1;
             if (!warp_wait_all(&wfull[kb + kn - 1], 0, DEV_TIMEOUT_READY, p.err, abort_flag)) break;
@@ -251,17 +251,18 @@ fv_gemm_t_kernel(const __grid_constant__ CUtensorMap tmA, const FvGemmTParams p)
         const uint32_t pal_lo = (clo << 8) | (((0x100u - clo) & 0xFFu) << 16) | (0x7Fu << 24);
         const uint32_t pal_hi = 0x81u | (((2u * clo) & 0xFFu) << 8) | (0xFEu << 16);
         const float c1 = __fmul_rn(p.hi[n], 1.0f / 127.0f);
-        // Stages go to tensor memory two at a time: one wait for the stores of both (a store's completion is only
-        // observable through tcgen05.wait::st, a round trip of several hundred cycles), then both are released.
+        // Stages go to tensor memory EG at a time: one wait for the stores of the group (a store's completion is only
+        // observable through tcgen05.wait::st, a round trip of several hundred cycles, so the groups' waits are the
+        // expansion's serial chain), then the group's stages are released.
+        constexpr int EG = 4;
+        static_assert(TNK == 2 * EG, "two groups of stages");
 #pragma unroll
-        for (int kb = 0; kb < TNK; kb += 2) {
+        for (int kb = 0; kb < TNK; kb += EG) {
             if (kb >= nk) break;
-            if (kb == 0) cp_async_wait<TNK - 2>();   // groups 0 and 1 have landed (this thread's own copies)
-            else if (kb == 2) cp_async_wait<TNK - 4>();
-            else if (kb == 4) cp_async_wait<TNK - 6>();
+            if (kb == 0) cp_async_wait<TNK - EG>();   // the first group's commit groups have landed (own copies)
             else cp_async_wait<0>();
 #pragma unroll
-            for (int u = 0; u < 2; ++u) {
+            for (int u = 0; u < EG; ++u) {
                 if (kb + u < nk) {
                     const uint4 vv = vdst[(kb + u) * (EXP_WARPS * 32)];
                     const uint32_t x[4] = {vv.x, vv.y, vv.z, vv.w};
@@ -279,8 +280,9 @@ fv_gemm_t_kernel(const __grid_constant__ CUtensorMap tmA, const FvGemmTParams p)
             tc_fence_before();
             __syncwarp();
             if (lane == 0) {
-                mbar_arrive(&wfull[kb]);
-                if (kb + 1 < nk) mbar_arrive(&wfull[kb + 1]);
+#pragma unroll
+                for (int u = 0; u < EG; ++u)
+                    if (kb + u < nk) mbar_arrive(&wfull[kb + u]);
             }
         }
         cp_async_wait<0>();   // none of this thread's copies is still landing (the loop may have stopped early)
@@ -304,8 +306,8 @@ fv_gemm_t_kernel(const __grid_constant__ CUtensorMap tmA, const FvGemmTParams p)
                                                                              : 0.f;
             }
         }
-        const bool ok = warp_wait(accfull, 0, DEV_TIMEOUT_ACC, p.err, abort_flag, true) &&
-                        warp_wait(sready, 0, DEV_TIMEOUT_ACC, p.err, abort_flag, true);
+        const bool ok = warp_wait_all(accfull, 0, DEV_TIMEOUT_ACC, p.err, abort_flag) &&
+                        warp_wait_all(sready, 0, DEV_TIMEOUT_ACC, p.err, abort_flag);
         tc_fence_after();
         if (warp == 0 && lane == 0) TTRACE(6);
         if (ok) {
