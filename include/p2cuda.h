@@ -62,6 +62,17 @@ P2CU_API const char *p2cu_last_error(void);
  * ran out, P2CU_ECUDA on a CUDA error, else P2CU_OK. */
 P2CU_API int p2cu_check_device(void *stream);
 
+/* The quantisation rule of every int8 path (p2cu_quant_rows, the int8 GEMM entry points, the encoder's quantising
+ * row ops). 0 (the default): the reference's C source as written, IEEE division - scale = amax / 127,
+ * 1 / scale, and x / scale in the scalar tail (csrc/blas.c:1114-1144). 1: the arithmetic of the reference as its
+ * Makefile builds it (csrc/Makefile:2, -ffast-math), which that compiler derives from the same source:
+ * scale = amax * (1/127), the reciprocal 127 / amax, x times it in the tail (a non-finite product there gives 0).
+ * The environment variable P2CU_QUANT_FAST_MATH=1 selects 1 before the first call. Kernels follow the rule in force
+ * when they are launched (a captured graph: when it was captured). p2cu_set_quant_fast_math returns the previous
+ * rule. No counterpart in the reference, which has one rule per build. */
+P2CU_API int p2cu_set_quant_fast_math(int on);
+P2CU_API int p2cu_quant_fast_math(void);
+
 /* Per-row int8 quantisation (csrc/blas.c:1114-1144): q [M][K] int8, scales [M]. */
 P2CU_API int p2cu_quant_rows(const float *A, int M, int K, int lda, signed char *q, float *scales, void *stream);
 

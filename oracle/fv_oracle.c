@@ -75,6 +75,37 @@ void orc_quant_rows(const float *A, int M, int K, int lda, int8_t *q, float *sca
     for (int m = 0; m < M; m++) orc_quant_row(A + (size_t)m * lda, K, q + (size_t)m * K, scales + m);
 }
 
+/* The same row as the reference's Makefile builds it (-O3 -ffast-math, csrc/Makefile:2), which its compiler derives
+ * from the same source: amax / 127.0f becomes amax * (1/127) (the reciprocal rounded to fp32), 1 / scale folds into
+ * 127 / amax (one division), and the tail's x / scale becomes x times that reciprocal; the tail's lrintf of a product
+ * that is not finite (the reciprocal overflowed: a row whose largest magnitude is below about 1e-39) comes out of the
+ * int conversion as 0. Pinned against that build of the reference compiled here (tests/test_ref_neon.py). */
+void orc_quant_row_fast_math(const float *row, int K, int8_t *q, float *scale_out)
+{
+    float amax = 0.0f;
+    for (int k = 0; k < K; k++) {
+        float v = fabsf(row[k]);
+        if (v > amax) amax = v;
+    }
+    const float recip127 = 1.0f / 127.0f;
+    const float scale = amax > 0.0f ? amax * recip127 : 1.0f;
+    const float inv = amax > 0.0f ? 127.0f / amax : 1.0f;
+    const int k16 = K & ~15;
+    for (int k = 0; k < k16; k++) q[k] = sat8(round_even(row[k] * inv));
+    for (int k = k16; k < K; k++) {
+        const float t = row[k] * inv;
+        const int32_t v = isfinite(t) ? round_even(t) : 0;
+        q[k] = (int8_t)(v > 127 ? 127 : v < -127 ? -127 : v);
+    }
+    *scale_out = scale;
+}
+
+void orc_quant_rows_fast_math(const float *A, int M, int K, int lda, int8_t *q, float *scales)
+{
+    #pragma omp parallel for schedule(static)
+    for (int m = 0; m < M; m++) orc_quant_row_fast_math(A + (size_t)m * lda, K, q + (size_t)m * K, scales + m);
+}
+
 /* ---- five-value planes ----------------------------------------------------------------------------------- */
 
 /* sign of w[k][n] in {-1, 0, +1}: 2-bit code at bits 2*(n&3) of signs[k*N/4 + n/4], code - 1 (blas.h:38-45). */

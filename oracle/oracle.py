@@ -50,6 +50,7 @@ def lib() -> C.CDLL:
             raise RuntimeError(f"{ORACLE_SO} is not built (run __graft_entry__.build())")
         L = C.CDLL(str(ORACLE_SO))
         L.orc_quant_rows.argtypes = [_f32p, C.c_int, C.c_int, C.c_int, _i8p, _f32p]
+        L.orc_quant_rows_fast_math.argtypes = [_f32p, C.c_int, C.c_int, C.c_int, _i8p, _f32p]
         L.orc_clo.argtypes = [C.c_float, C.c_float]
         L.orc_clo.restype = C.c_int
         L.orc_fv_codes.argtypes = [_u8p, _u8p, _f32p, _f32p, C.c_int, C.c_int, _i8p]
@@ -74,11 +75,14 @@ def _fv_args(w):
     return [_ptr(w["signs"]), _ptr(w["flags"]), _ptr(w["lo"]), _ptr(w["hi"])]
 
 
-def quant_rows(A: np.ndarray):
+def quant_rows(A: np.ndarray, fast_math: bool = False):
+    """The reference's per-row quantiser restated (orc_quant_row), or with fast_math what its -ffast-math build
+    computes (orc_quant_row_fast_math): (q [M, K] int8, scales [M])."""
     M, K = A.shape
     q = np.empty((M, K), np.int8)
     s = np.empty(M, np.float32)
-    lib().orc_quant_rows(np.ascontiguousarray(A, np.float32), M, K, K, q, s)
+    fn = lib().orc_quant_rows_fast_math if fast_math else lib().orc_quant_rows
+    fn(np.ascontiguousarray(A, np.float32), M, K, K, q, s)
     return q, s
 
 

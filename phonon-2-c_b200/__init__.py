@@ -53,6 +53,8 @@ SIGNATURES = {
     "p2cu_last_error": (C.c_char_p, []),
     "p2cu_check_device": (_i, [_vp]),
     "p2cu_quant_rows": (_i, [_vp, _i, _i, _i, _vp, _vp, _vp]),
+    "p2cu_set_quant_fast_math": (_i, [_i]),
+    "p2cu_quant_fast_math": (_i, []),
     "p2cu_sgemm_fvb_q8a": (_i, [_i, _i, _i, _f, _vp, _vp, C.POINTER(P2cuFiveValue), _i, _f, _vp, _i, _vp, _sz,
                                 _vp]),
     "p2cu_sgemm_q8b_q8a": (_i, [_i, _i, _i, _f, _vp, _vp, _vp, _vp, _i, _f, _vp, _i, _vp, _sz, _vp]),
@@ -188,6 +190,12 @@ def stream_ptr(stream) -> int | None:
 
 def quant_rows(A: int, M: int, K: int, lda: int, q: int, scales: int, stream=None) -> None:
     check(lib().p2cu_quant_rows(A, M, K, lda, q, scales, stream_ptr(stream)))
+
+
+def set_quant_fast_math(on: bool) -> bool:
+    """p2cu_set_quant_fast_math: the quantisation rule of every int8 path from now on (False: the reference's C
+    source, IEEE; True: its -ffast-math build's arithmetic). Returns the previous rule."""
+    return bool(lib().p2cu_set_quant_fast_math(1 if on else 0))
 
 
 def sgemm_fvb(M, N, K, alpha, A, lda, B: P2cuFiveValue, mode, beta, Cp, ldc, workspace, ws_bytes, stream=None):

@@ -10,6 +10,7 @@
 #include "p2cuda.h"
 #include "fv_gemm.h"
 #include "kernels.h"
+#include "numerics.cuh"
 #include "gemm.h"
 
 namespace {
@@ -450,6 +451,14 @@ int p2cu_check_device(void* stream) {
     }
     return P2CU_OK;
 }
+
+int p2cu_set_quant_fast_math(int on) {
+    const int prev = p2cu::quant_fast_math();
+    p2cu::set_quant_fast_math(on);
+    return prev;
+}
+
+int p2cu_quant_fast_math(void) { return p2cu::quant_fast_math(); }
 
 int p2cu_quant_rows(const float* A, int M, int K, int lda, signed char* q, float* scales, void* stream) {
     if (M < 0 || K < 0 || lda < K) return fail(P2CU_EINVAL, "p2cu_quant_rows: bad shape M=%d K=%d lda=%d", M, K, lda);

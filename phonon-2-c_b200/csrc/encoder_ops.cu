@@ -56,7 +56,7 @@ template <int V, bool QUANT>
 __global__ void __launch_bounds__(256) ln_warp_kernel(const float* __restrict__ x, int ldx,
                                                       const float* __restrict__ gamma, const float* __restrict__ beta,
                                                       float* out, int ldo, int8_t* __restrict__ q,
-                                                      float* __restrict__ qscale, int rows) {
+                                                      float* __restrict__ qscale, int rows, int fm) {
     constexpr int D = 128 * V;
     const int lane = threadIdx.x & 31;
     const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
@@ -94,8 +94,8 @@ __global__ void __launch_bounds__(256) ln_warp_kernel(const float* __restrict__ 
         for (int i = 0; i < V; ++i) orow[lane + 32 * i] = v[i];
         return;
     }
-    const float scale = quant_scale(warp_max(amax));
-    const float qinv = __fdiv_rn(1.0f, scale);
+    const QuantRule qr = quant_rule(warp_max(amax), fm);
+    const float scale = qr.scale, qinv = qr.inv;
     char4* qrow = reinterpret_cast<char4*>(q + static_cast<size_t>(row) * D);
 #pragma unroll
     for (int i = 0; i < V; ++i) qrow[lane + 32 * i] = quant4(v[i], qinv);
@@ -107,7 +107,7 @@ template <bool QUANT>
 __global__ void __launch_bounds__(256) ln_rows_kernel(const float* __restrict__ x, int ldx,
                                                       const float* __restrict__ gamma, const float* __restrict__ beta,
                                                       float* out, int ldo, int8_t* __restrict__ q,
-                                                      float* __restrict__ qscale, int D) {
+                                                      float* __restrict__ qscale, int D, int fm) {
     __shared__ float red[8];
     const int row = blockIdx.x;
     const float* xr = x + static_cast<size_t>(row) * ldx;
@@ -146,10 +146,10 @@ __global__ void __launch_bounds__(256) ln_rows_kernel(const float* __restrict__ 
     float m = red[0];
 #pragma unroll
     for (int i = 1; i < 8; ++i) m = fmaxf(m, red[i]);
-    const float scale = quant_scale(m);
-    const float qinv = __fdiv_rn(1.0f, scale);
+    const QuantRule qr = quant_rule(m, fm);
+    const float scale = qr.scale;
     int8_t* qrow = q + static_cast<size_t>(row) * D;
-    for (int i = threadIdx.x; i < D; i += 256) qrow[i] = quant_at(y(i), qinv, scale, i, D);
+    for (int i = threadIdx.x; i < D; i += 256) qrow[i] = quant_at(y(i), qr, i, D, fm);
     if (threadIdx.x == 0) qscale[row] = scale;
 }
 
@@ -167,7 +167,8 @@ __device__ __forceinline__ float block_max256(float v, float* red) {
 
 template <bool QUANT>
 __global__ void __launch_bounds__(256) swish_rows_kernel(const float* __restrict__ h, int ldh, float* out, int ldo,
-                                                         int8_t* __restrict__ q, float* __restrict__ qscale, int len) {
+                                                         int8_t* __restrict__ q, float* __restrict__ qscale, int len,
+                                                         int fm) {
     __shared__ float red[8];
     const int r = blockIdx.x;
     const float* hr = h + static_cast<size_t>(r) * ldh;
@@ -179,17 +180,17 @@ __global__ void __launch_bounds__(256) swish_rows_kernel(const float* __restrict
     float amax = 0.f;
     for (int i = threadIdx.x; i < len; i += 256) amax = fmaxf(amax, fabsf(swish1(hr[i])));
     amax = block_max256(amax, red);
-    const float scale = quant_scale(amax);
-    const float qinv = __fdiv_rn(1.0f, scale);
+    const QuantRule qr = quant_rule(amax, fm);
+    const float scale = qr.scale;
     int8_t* qrow = q + static_cast<size_t>(r) * len;
-    for (int i = threadIdx.x; i < len; i += 256) qrow[i] = quant_at(swish1(hr[i]), qinv, scale, i, len);
+    for (int i = threadIdx.x; i < len; i += 256) qrow[i] = quant_at(swish1(hr[i]), qr, i, len, fm);
     if (threadIdx.x == 0) qscale[r] = scale;
 }
 
 // len = 1024 V, one 256-thread block per row, the row in registers.
 template <int V, bool QUANT>
 __global__ void __launch_bounds__(256) swish_vec_kernel(const float* __restrict__ h, int ldh, float* out, int ldo,
-                                                        int8_t* __restrict__ q, float* __restrict__ qscale) {
+                                                        int8_t* __restrict__ q, float* __restrict__ qscale, int fm) {
     __shared__ float red[8];
     constexpr int len = 1024 * V;
     const int r = blockIdx.x;
@@ -209,8 +210,8 @@ __global__ void __launch_bounds__(256) swish_vec_kernel(const float* __restrict_
         return;
     }
     amax = block_max256(amax, red);
-    const float scale = quant_scale(amax);
-    const float qinv = __fdiv_rn(1.0f, scale);
+    const QuantRule qr = quant_rule(amax, fm);
+    const float scale = qr.scale, qinv = qr.inv;
     char4* qrow = reinterpret_cast<char4*>(q + static_cast<size_t>(r) * len);
 #pragma unroll
     for (int i = 0; i < V; ++i) qrow[threadIdx.x + 256 * i] = quant4(v[i], qinv);
@@ -301,7 +302,7 @@ __global__ void __launch_bounds__(256) dwconv_swish_kernel(const float* __restri
                                                            const float* __restrict__ b,
                                                            const int* __restrict__ row_off, int n_win,
                                                            float* __restrict__ out, int8_t* __restrict__ q,
-                                                           float* __restrict__ qscale, int rows, int D) {
+                                                           float* __restrict__ qscale, int rows, int D, int fm) {
     __shared__ float red[8];
     constexpr int PER = 4;   // channels per thread (D <= 1024)
     const int r = blockIdx.x;
@@ -335,12 +336,12 @@ __global__ void __launch_bounds__(256) dwconv_swish_kernel(const float* __restri
         return;
     }
     amax = block_max256(amax, red);
-    const float scale = quant_scale(amax);
-    const float qinv = __fdiv_rn(1.0f, scale);
+    const QuantRule qr = quant_rule(amax, fm);
+    const float scale = qr.scale;
 #pragma unroll
     for (int u = 0; u < PER; ++u) {
         const int d = threadIdx.x + 256 * u;
-        if (d < D) q[static_cast<size_t>(r) * D + d] = quant_at(v[u], qinv, scale, d, D);
+        if (d < D) q[static_cast<size_t>(r) * D + d] = quant_at(v[u], qr, d, D, fm);
     }
     if (threadIdx.x == 0) qscale[r] = scale;
 }
@@ -739,13 +740,14 @@ static bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) =
 cudaError_t ln_rows_launch(const float* x, int ldx, const float* gamma, const float* beta, float* out, int ldo,
                            int8_t* q, float* qscale, int rows, int D, cudaStream_t s) {
     if (rows <= 0) return cudaSuccess;
+    const int fm = quant_fast_math();
     const bool vec = (D == 1024 || D == 512 || D == 256 || D == 128) && ldx % 4 == 0 && al16(x) && al16(gamma) &&
                      al16(beta) && (q ? al16(q) : (ldo % 4 == 0 && al16(out)));
     if (vec) {
         const unsigned grid = static_cast<unsigned>((rows + 7) / 8);
 #define P2CU_LN(V)                                                                                                   \
-        if (q) ln_warp_kernel<V, true><<<grid, 256, 0, s>>>(x, ldx, gamma, beta, out, ldo, q, qscale, rows);         \
-        else ln_warp_kernel<V, false><<<grid, 256, 0, s>>>(x, ldx, gamma, beta, out, ldo, q, qscale, rows);
+        if (q) ln_warp_kernel<V, true><<<grid, 256, 0, s>>>(x, ldx, gamma, beta, out, ldo, q, qscale, rows, fm);         \
+        else ln_warp_kernel<V, false><<<grid, 256, 0, s>>>(x, ldx, gamma, beta, out, ldo, q, qscale, rows, fm);
         switch (D) {
         case 1024: P2CU_LN(8) break;
         case 512: P2CU_LN(4) break;
@@ -755,20 +757,21 @@ cudaError_t ln_rows_launch(const float* x, int ldx, const float* gamma, const fl
 #undef P2CU_LN
         return cudaGetLastError();
     }
-    if (q) ln_rows_kernel<true><<<rows, 256, 0, s>>>(x, ldx, gamma, beta, out, ldo, q, qscale, D);
-    else ln_rows_kernel<false><<<rows, 256, 0, s>>>(x, ldx, gamma, beta, out, ldo, q, qscale, D);
+    if (q) ln_rows_kernel<true><<<rows, 256, 0, s>>>(x, ldx, gamma, beta, out, ldo, q, qscale, D, fm);
+    else ln_rows_kernel<false><<<rows, 256, 0, s>>>(x, ldx, gamma, beta, out, ldo, q, qscale, D, fm);
     return cudaGetLastError();
 }
 
 cudaError_t swish_rows_launch(const float* h, int ldh, float* out, int ldo, int8_t* q, float* qscale, int rows,
                               int len, cudaStream_t s) {
     if (rows <= 0) return cudaSuccess;
+    const int fm = quant_fast_math();
     const bool vec = (len == 4096 || len == 2048 || len == 1024) && ldh % 4 == 0 && al16(h) &&
                      (q ? al16(q) : (ldo % 4 == 0 && al16(out)));
     if (vec) {
 #define P2CU_SW(V)                                                                                                   \
-        if (q) swish_vec_kernel<V, true><<<rows, 256, 0, s>>>(h, ldh, out, ldo, q, qscale);                          \
-        else swish_vec_kernel<V, false><<<rows, 256, 0, s>>>(h, ldh, out, ldo, q, qscale);
+        if (q) swish_vec_kernel<V, true><<<rows, 256, 0, s>>>(h, ldh, out, ldo, q, qscale, fm);                          \
+        else swish_vec_kernel<V, false><<<rows, 256, 0, s>>>(h, ldh, out, ldo, q, qscale, fm);
         switch (len) {
         case 4096: P2CU_SW(4) break;
         case 2048: P2CU_SW(2) break;
@@ -777,8 +780,8 @@ cudaError_t swish_rows_launch(const float* h, int ldh, float* out, int ldo, int8
 #undef P2CU_SW
         return cudaGetLastError();
     }
-    if (q) swish_rows_kernel<true><<<rows, 256, 0, s>>>(h, ldh, out, ldo, q, qscale, len);
-    else swish_rows_kernel<false><<<rows, 256, 0, s>>>(h, ldh, out, ldo, q, qscale, len);
+    if (q) swish_rows_kernel<true><<<rows, 256, 0, s>>>(h, ldh, out, ldo, q, qscale, len, fm);
+    else swish_rows_kernel<false><<<rows, 256, 0, s>>>(h, ldh, out, ldo, q, qscale, len, fm);
     return cudaGetLastError();
 }
 
@@ -807,7 +810,7 @@ cudaError_t dwconv_swish_launch(const float* gated, const float* w, const float*
     if (D > 1024) return cudaErrorInvalidValue;
     auto* k = q ? (swish ? dwconv_swish_kernel<true, true> : dwconv_swish_kernel<true, false>)
                 : (swish ? dwconv_swish_kernel<false, true> : dwconv_swish_kernel<false, false>);
-    k<<<rows, 256, 0, s>>>(gated, w, b, row_off, n_win, out, q, qscale, rows, D);
+    k<<<rows, 256, 0, s>>>(gated, w, b, row_off, n_win, out, q, qscale, rows, D, quant_fast_math());
     return cudaGetLastError();
 }
 

@@ -13,22 +13,41 @@ __device__ __forceinline__ int8_t quant_one(float x, float inv) {
     return static_cast<int8_t>(v);
 }
 
+// The row's scale and the reciprocal the 16-wide loop multiplies by. fm = 0: the reference's C source as written
+// (csrc/blas.c:1120-1121, IEEE): scale = amax / 127, inv = 1 / scale. fm = 1: what its Makefile's build with
+// -ffast-math computes (csrc/Makefile:2, measured on that build compiled here): scale = amax * (1/127) (the reciprocal
+// of 127 rounded to fp32) and inv = 127 / amax (the compiler folds 1 / (amax / 127) into one division). Both are 1 for
+// an all-zero row.
+struct QuantRule { float scale, inv; };
+// Host side: the rule every quantising kernel launched from now on follows (0 IEEE, 1 the -ffast-math build's; from
+// P2CU_QUANT_FAST_MATH when first asked, p2cu_set_quant_fast_math after that). A captured graph keeps the rule its
+// launches were captured with.
+int quant_fast_math();
+void set_quant_fast_math(int on);
+__device__ __forceinline__ QuantRule quant_rule(float amax, int fm) {
+    if (!(amax > 0.f)) return {1.0f, 1.0f};
+    if (fm) return {__fmul_rn(amax, __int_as_float(0x3C010204)), __fdiv_rn(127.0f, amax)};
+    const float scale = __fdiv_rn(amax, 127.0f);
+    return {scale, __fdiv_rn(1.0f, scale)};
+}
+
 // The reference quantises the first K - K % 16 values of a row in its 16-wide loop (quant_one) and the last K % 16
 // in a scalar tail, clamp(lrintf(x / scale), -127, 127) (csrc/blas.c:1139-1143): a division instead of the reciprocal,
-// so a value near a half can round the other way.
-__device__ __forceinline__ int8_t quant_tail(float x, float scale) {
-    int v = __float2int_rn(__fdiv_rn(x, scale));
+// so a value near a half can round the other way. Its -ffast-math build (fm = 1) multiplies by inv there too, and a
+// product that is not finite (inv overflowed: a row whose maximum is below about 1e-39) comes out of its lrintf and
+// int conversion as 0.
+__device__ __forceinline__ int8_t quant_tail(float x, float scale, float inv, int fm) {
+    const float t = fm ? __fmul_rn(x, inv) : __fdiv_rn(x, scale);
+    if (fm && !isfinite(t)) return 0;
+    int v = __float2int_rn(t);
     v = v > 127 ? 127 : (v < -127 ? -127 : v);
     return static_cast<int8_t>(v);
 }
 
 // Value k of a quantised row of K values.
-__device__ __forceinline__ int8_t quant_at(float x, float inv, float scale, int k, int K) {
-    return k < (K & ~15) ? quant_one(x, inv) : quant_tail(x, scale);
+__device__ __forceinline__ int8_t quant_at(float x, const QuantRule& r, int k, int K, int fm) {
+    return k < (K & ~15) ? quant_one(x, r.inv) : quant_tail(x, r.scale, r.inv, fm);
 }
-
-// The reference's scale for a row with maximum magnitude amax: amax / 127, or 1 for an all-zero row.
-__device__ __forceinline__ float quant_scale(float amax) { return amax > 0.f ? __fdiv_rn(amax, 127.0f) : 1.0f; }
 
 // exp(x) as the reference's AVX2 path evaluates it (csrc/tensor_ops.c:154-172): clamp to [-87, 87], k = round(x *
 // log2 e), r = x - k * ln 2, a degree-5 Taylor polynomial in r by Horner's rule, times 2^k built in the exponent

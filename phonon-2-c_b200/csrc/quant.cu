@@ -1,9 +1,12 @@
 // quant.cu - per-row symmetric int8 quantisation of fp32 activations (csrc/blas.c:1114-1144, quant_pack_row):
 //   amax = max |x|, scale = amax > 0 ? amax / 127 : 1, q = saturate_int8(round_half_even(x * (1 / scale))), and for
 //   the last K % 16 values of a row the reference's scalar tail, clamp(round_half_even(x / scale), -127, 127).
-// Division is IEEE (the C source as written; the reference's -ffast-math build may use a reciprocal, see the oracle).
+// Division is IEEE (the C source as written); with the opt-in rule (p2cu_set_quant_fast_math, P2CU_QUANT_FAST_MATH)
+// the scale and reciprocal are those of the reference's -ffast-math build (numerics.cuh, quant_rule).
 // Output is row-major int8 [M, K] plus one fp32 scale per row; the GEMM's TMA loads tile it.
+#include <atomic>
 #include <cstdint>
+#include <cstdlib>
 #include <cuda_runtime.h>
 #include "kernels.h"
 #include "numerics.cuh"
@@ -26,7 +29,7 @@ __device__ __forceinline__ float block_max(float v, float* red) {
 }
 
 __global__ void __launch_bounds__(QT) quant_rows_kernel(const float* __restrict__ A, int M, int K, int lda,
-                                                        int8_t* __restrict__ q, float* __restrict__ scales) {
+                                                        int8_t* __restrict__ q, float* __restrict__ scales, int fm) {
     griddep_launch_dependents();
     {   // the row into L2 while the previous kernel finishes (cold rows then cost no DRAM latency after the wait)
         const char* rb = reinterpret_cast<const char*>(A + static_cast<size_t>(blockIdx.x) * lda);
@@ -49,8 +52,8 @@ __global__ void __launch_bounds__(QT) quant_rows_kernel(const float* __restrict_
             amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[i].x), fabsf(v[i].y)), fmaxf(fabsf(v[i].z), fabsf(v[i].w))));
         }
         amax = block_max(amax, red);
-        const float scale = amax > 0.f ? __fdiv_rn(amax, 127.0f) : 1.0f;
-        const float inv = __fdiv_rn(1.0f, scale);
+        const QuantRule qr = quant_rule(amax, fm);
+        const float scale = qr.scale, inv = qr.inv;
 #pragma unroll
         for (int i = 0; i < QV; ++i) {
             const int k = 4 * (threadIdx.x + i * QT);
@@ -60,8 +63,8 @@ __global__ void __launch_bounds__(QT) quant_rows_kernel(const float* __restrict_
                     o.x = quant_one(v[i].x, inv); o.y = quant_one(v[i].y, inv);
                     o.z = quant_one(v[i].z, inv); o.w = quant_one(v[i].w, inv);
                 } else {
-                    o.x = quant_tail(v[i].x, scale); o.y = quant_tail(v[i].y, scale);
-                    o.z = quant_tail(v[i].z, scale); o.w = quant_tail(v[i].w, scale);
+                    o.x = quant_tail(v[i].x, scale, inv, fm); o.y = quant_tail(v[i].y, scale, inv, fm);
+                    o.z = quant_tail(v[i].z, scale, inv, fm); o.w = quant_tail(v[i].w, scale, inv, fm);
                 }
                 *reinterpret_cast<char4*>(qrow + k) = o;
             }
@@ -72,11 +75,27 @@ __global__ void __launch_bounds__(QT) quant_rows_kernel(const float* __restrict_
     float amax = 0.f;
     for (int k = threadIdx.x; k < K; k += QT) amax = fmaxf(amax, fabsf(row[k]));
     amax = block_max(amax, red);
-    const float scale = amax > 0.f ? __fdiv_rn(amax, 127.0f) : 1.0f;
-    const float inv = __fdiv_rn(1.0f, scale);
-    for (int k = threadIdx.x; k < K; k += QT) qrow[k] = quant_at(row[k], inv, scale, k, K);
-    if (threadIdx.x == 0) scales[m] = scale;
+    const QuantRule qr = quant_rule(amax, fm);
+    for (int k = threadIdx.x; k < K; k += QT) qrow[k] = quant_at(row[k], qr, k, K, fm);
+    if (threadIdx.x == 0) scales[m] = qr.scale;
 }
+
+namespace {
+std::atomic<int> g_quant_fm{-1};   // -1: not read from the environment yet
+}
+
+int quant_fast_math() {
+    int v = g_quant_fm.load(std::memory_order_relaxed);
+    if (v < 0) {
+        const char* e = getenv("P2CU_QUANT_FAST_MATH");
+        int expected = -1;
+        g_quant_fm.compare_exchange_strong(expected, (e && *e && *e != '0') ? 1 : 0);
+        v = g_quant_fm.load(std::memory_order_relaxed);
+    }
+    return v;
+}
+
+void set_quant_fast_math(int on) { g_quant_fm.store(on ? 1 : 0, std::memory_order_relaxed); }
 
 cudaError_t quant_rows_launch(const float* A, int M, int K, int lda, int8_t* q, float* scales, cudaStream_t stream) {
     cudaLaunchConfig_t cfg = {};
@@ -88,7 +107,7 @@ cudaError_t quant_rows_launch(const float* A, int M, int K, int lda, int8_t* q, 
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, quant_rows_kernel, A, M, K, lda, q, scales);
+    return cudaLaunchKernelEx(&cfg, quant_rows_kernel, A, M, K, lda, q, scales, quant_fast_math());
 }
 
 // The int8w codes of a whole five-value weight as a row-major [K, N] int8 plane:

@@ -73,6 +73,23 @@ def test_quantiser_under_fast_math_takes_the_reciprocal_of_127(neon, synth):
     assert 0 < np.count_nonzero(s.view(np.uint32) != s_o.view(np.uint32)) < 0.1 * len(s)
 
 
+@pytest.mark.parametrize("K", [1024, 4096, 1000, 100, 36])
+def test_fast_math_quantiser_restatement_matches_reference_build(neon, synth, K):
+    """The opt-in rule (orc_quant_row_fast_math; on the device p2cu_set_quant_fast_math) against the reference's
+    -ffast-math build itself: every scale and every quantised value bit for bit, ragged tails and edge rows included
+    (the denormal row, whose reciprocal overflows, among them). The rule it pins: scale = amax * (1/127), the 16-wide
+    loop's reciprocal 127 / amax, the tail multiplied by it too."""
+    A = np.concatenate([synth.activations(3000, K, seed=K), _special_rows(K, seed=K + 1),
+                        synth.quantiser_edge_rows(K, seed=K)])
+    q, s = neon.neon_quant_rows(neon.ref_neon("int8w", fast_math=True), A)
+    q_o, s_o = neon.quant_rows(A, fast_math=True)
+    assert _bits_equal(s, s_o)
+    assert np.array_equal(q, q_o)
+    # and it is a different rule from the IEEE one: some rows' scales and values move
+    q_i, s_i = neon.quant_rows(A)
+    assert not _bits_equal(s_i, s_o)
+
+
 def _unit_quanta(M, K, seed):
     q = np.random.default_rng(seed).integers(-127, 128, size=(M, K)).astype(np.int8)
     return q, np.ones(M, np.float32)
