@@ -238,25 +238,9 @@ P2_API int p2_b200_plan_windows(const float *audio, int n_samples, int sample_ra
 /* p2_split_point (csrc/phonon2.h:367-368) likewise: the middle of the longest pause in the middle third. */
 P2_API int p2_b200_split_point(const float *audio, int n_samples, int sample_rate);
 
-/* One decoded window of p2_b200_transcribe_long. */
-typedef struct {
-    int      start, end;      /* samples [start, end) of the audio given */
-    int      depth;           /* re-decode splits that made it: 0 for a planned window */
-    int      encoder_frames;  /* its encoder frames (80 ms each) */
-    P2Token *tokens;          /* its tokens, frames relative to `start` (malloc'd; NULL when n_tokens is 0) */
-    int      n_tokens;
-} P2B200Window;
-
-/* Long 16 kHz audio as p2_transcribe decodes it (csrc/engine.c:293-357) - pause-aligned windows over 35 s, a window
- * that went quiet over speech re-decoded as two halves, at most two levels deep; P2_SEGMENT, P2_REDECODE and
- * P2_WINDOW_MAX keep their meaning - with each split depth's windows decoded as one batch spread over the GPUs
- * (`devices`, or all GPUs when n_devices is 0). Non-finite samples count as zeros. *out receives the final windows in
- * the order the reference appends them as segments (by start), freed with p2_b200_windows_free; *encoder_frames (if
- * not NULL) the encoder frames of every decode, split windows included (P2Result.encoder_frames). Returns 0, or -1
- * with a message on stderr. */
-P2_API int p2_b200_transcribe_long(const P2Model *m, const float *audio, int n_samples, const int *devices,
-                                   int n_devices, P2B200Window **out, int *n_out, long long *encoder_frames);
-P2_API void p2_b200_windows_free(P2B200Window *windows, int n);
+/* p2_b200_transcribe_long, p2_b200_windows_free: phonon2_b200.h (included here; an edited engine.c that keeps the
+ * reference's phonon2.h includes it after that header). */
+#include "phonon2_b200.h"
 
 #ifdef __cplusplus
 }

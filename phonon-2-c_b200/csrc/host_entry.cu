@@ -470,12 +470,31 @@ int run_windows(const char* who, const P2Model* m, const int* n_frames, int n_wi
                 int n_devices, const FeedEncoder& feed, const AfterEncode& after) {
     std::vector<int> devs;
     if (n_devices == 0) {
-        int n = 0;
-        if (cudaGetDeviceCount(&n) != cudaSuccess || n <= 0) {
-            fprintf(stderr, "%s: no CUDA device\n", who);
-            return -1;
+        // No list from the caller: P2_DEVICES (GPU indices separated by commas; an index may repeat, its shares then
+        // run one after the other), else every GPU.
+        const char* env = getenv("P2_DEVICES");
+        for (const char* c = env; c && *c;) {
+            char* end = nullptr;
+            const long v = strtol(c, &end, 10);
+            if (end == c || v < 0 || v >= 64) {
+                fprintf(stderr, "%s: P2_DEVICES=\"%s\" is not a list of GPU indices\n", who, env);
+                return -1;
+            }
+            devs.push_back(static_cast<int>(v));
+            c = *end == ',' ? end + 1 : end;
+            if (*end && *end != ',') {
+                fprintf(stderr, "%s: P2_DEVICES=\"%s\" is not a list of GPU indices\n", who, env);
+                return -1;
+            }
         }
-        for (int i = 0; i < n; ++i) devs.push_back(i);
+        if (devs.empty()) {
+            int n = 0;
+            if (cudaGetDeviceCount(&n) != cudaSuccess || n <= 0) {
+                fprintf(stderr, "%s: no CUDA device\n", who);
+                return -1;
+            }
+            for (int i = 0; i < n; ++i) devs.push_back(i);
+        }
     } else {
         devs.assign(devices, devices + n_devices);
     }
@@ -493,6 +512,11 @@ int run_windows(const char* who, const P2Model* m, const int* n_frames, int n_wi
     int prev = 0;
     cudaGetDevice(&prev);
     const auto shards = shard_windows(n_frames, n_windows, static_cast<int>(devs.size()));
+    if (p2_verbose && devs.size() > 1) {
+        size_t busy = 0;
+        for (const auto& sh : shards) busy += sh.empty() ? 0 : 1;
+        fprintf(stderr, "  %s: %d window(s) over %zu GPU slot(s) of %zu listed\n", who, n_windows, busy, devs.size());
+    }
     int fail_slot = -1;
     if (const char* fs = getenv("P2_B200_FAIL_SLOT")) {
         char* end;
