@@ -31,6 +31,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include "ptx.cuh"
+#include "launch.cuh"
 #include "fv_gemm.h"
 #include "fv_common.cuh"
 
@@ -474,21 +475,6 @@ __global__ void __launch_bounds__(256) fv_combine_kernel(const float* __restrict
     *reinterpret_cast<float4*>(C + static_cast<size_t>(m) * ldc + n) = c;
 }
 
-template <typename... KArgs, typename... Args>
-static cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
-                              Args&&... args) {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = grid;
-    cfg.blockDim = block;
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
-}
 
 template <int BN, int KIND>
 static cudaError_t launch(const CUtensorMap& a, const CUtensorMap& b0, const CUtensorMap& b1,
