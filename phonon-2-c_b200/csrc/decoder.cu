@@ -210,21 +210,31 @@ __device__ __forceinline__ float sigmoid_ref(float x) {   // csrc/phonon2.h:38-4
     return __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(x < -87.0f ? 87.0f : -x)));
 }
 
-// Grid barrier (generation counter) with a bounded wait. Returns false when it gave up.
-__device__ bool grid_sync(unsigned* count, volatile unsigned* gen, unsigned nblocks, uint32_t* err, int* s_ok) {
+// Grid barrier on an arrival count that only grows during a launch (the host zeroes it before): thread 0 of each CTA
+// adds one (acquire-release, so the CTA's writes before the barrier are published and, for the last arrival, everyone
+// else's acquired) and polls with acquire loads until the count reaches the next multiple of the grid size. One trip
+// through L2 per barrier, where a count reset by the last arrival and a generation word it then advances cost two.
+// The wait is bounded: a barrier that does not complete records an error and returns false.
+__device__ __forceinline__ unsigned atom_add_acq_rel(unsigned* p, unsigned v) {
+    unsigned old;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
+__device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ bool grid_sync(unsigned* count, unsigned nblocks, uint32_t* err, int* s_ok) {
     __syncthreads();
     if (threadIdx.x == 0) {
         int ok = 1;
-        const unsigned g = *gen;
-        __threadfence();
-        if (atomicAdd(count, 1u) == nblocks - 1) {
-            *count = 0;
-            __threadfence();
-            atomicAdd(const_cast<unsigned*>(gen), 1u);
-        } else {
+        const unsigned old = atom_add_acq_rel(count, 1u);
+        const unsigned target = (old / nblocks + 1) * nblocks;
+        if (old + 1 != target) {
             const unsigned long long t0 = global_ns();
             uint32_t i = 0;
-            while (*gen == g) {
+            while (static_cast<int>(ld_acquire(count) - target) < 0) {
                 if ((++i & 255u) == 0 && global_ns() - t0 > BARRIER_NS) {
                     ok = 0;
                     if (err) atomicCAS(err, DEV_OK, DEC_TIMEOUT_BARRIER);
@@ -232,7 +242,6 @@ __device__ bool grid_sync(unsigned* count, volatile unsigned* gen, unsigned nblo
                 }
             }
         }
-        __threadfence();
         *s_ok = ok;
     }
     __syncthreads();
@@ -447,9 +456,9 @@ __global__ void __launch_bounds__(THREADS, 1) tdt_decode_kernel(DecParams p) {
 
     // the first prediction-network step (from zero state for a decode, csrc/decoder.c:112)
     lstm_layer(0);
-    if (!grid_sync(p.bar_count, p.bar_gen, G, p.err, s_ok)) return;
+    if (!grid_sync(p.bar_count, G, p.err, s_ok)) return;
     lstm_layer(1);
-    if (!grid_sync(p.bar_count, p.bar_gen, G, p.err, s_ok)) return;
+    if (!grid_sync(p.bar_count, G, p.err, s_ok)) return;
     projector();
     if (p.mode == DEC_STEP) return;   // p2_decoder_step: the new h is on side 1, c in place, dec written
     if (warp == 0) {
@@ -457,7 +466,7 @@ __global__ void __launch_bounds__(THREADS, 1) tdt_decode_kernel(DecParams p) {
         for (int b0 = 0; b0 < B; b0 += 32) n = warp_append(b0 + lane < B && T_of(b0 + lane) > 0, b0 + lane, live, n);
         if (lane == 0) misc[2] = n;
     }
-    if (!grid_sync(p.bar_count, p.bar_gen, G, p.err, s_ok)) return;
+    if (!grid_sync(p.bar_count, G, p.err, s_ok)) return;
     DTRACE(TR_SETUP);
 
     int iter = 0;
@@ -525,7 +534,7 @@ __global__ void __launch_bounds__(THREADS, 1) tdt_decode_kernel(DecParams p) {
             }
         }
         DTRACE(TR_J);
-        if (!grid_sync(p.bar_count, p.bar_gen, G, p.err, s_ok)) return;
+        if (!grid_sync(p.bar_count, G, p.err, s_ok)) return;
         DTRACE(TR_JBAR);
         DCOUNT(TR_ITERS);
 
@@ -612,15 +621,15 @@ __global__ void __launch_bounds__(THREADS, 1) tdt_decode_kernel(DecParams p) {
             DCOUNT(TR_TOKITERS);
             lstm_layer(0);
             DTRACE(TR_L0);
-            if (!grid_sync(p.bar_count, p.bar_gen, G, p.err, s_ok)) return;
+            if (!grid_sync(p.bar_count, G, p.err, s_ok)) return;
             DTRACE(TR_L0BAR);
             lstm_layer(1);
             DTRACE(TR_L1);
-            if (!grid_sync(p.bar_count, p.bar_gen, G, p.err, s_ok)) return;
+            if (!grid_sync(p.bar_count, G, p.err, s_ok)) return;
             DTRACE(TR_L1BAR);
             projector();
             DTRACE(TR_P);
-            if (!grid_sync(p.bar_count, p.bar_gen, G, p.err, s_ok)) return;
+            if (!grid_sync(p.bar_count, G, p.err, s_ok)) return;
             DTRACE(TR_PBAR);
         }
     }

@@ -35,9 +35,8 @@ struct DecParams {
     int* tok_out;          // [sum of counts][3] id, frame, duration, window after window
     int* tok_off;          // [B + 1] prefix offsets into tok_out
     int* count;            // [B] tokens emitted
-    // grid barrier (bar_count zeroed by the host) and error word
+    // grid barrier's arrival count (zeroed by the host before each launch) and error word
     unsigned* bar_count;
-    unsigned* bar_gen;
     uint32_t* err;
 };
 

@@ -69,7 +69,6 @@ p2cu::DecParams params(const P2cuDecoder* d, int B) {
     p.count = d->count;
     p.logits = d->logits;
     p.bar_count = d->bar;
-    p.bar_gen = d->bar + 1;
     p.err = p2cu::device_error_word();
     return p;
 }
