@@ -12,8 +12,9 @@
 // expanders when the weights are five-value planes (its B half); 8 epilogue warps (its TMEM rows -> fp32 C); and one
 // warp that in the even CTA issues the pair's MMAs and in the odd CTA relays "this stage of mine has landed" to it.
 // The epilogue warps work independently: warp (h, q) drains TMEM lanes 32 q .. 32 q + 31 and accumulator columns
-// 128 h .. 128 h + 127, 32 at a time, through a 4 KB staging block of its own, each 32 x 32 block leaving by its own
-// TMA store (one thread's bulk copies complete in order, so spreading them over eight warps keeps the stores apace);
+// 128 h .. 128 h + 127, 32 at a time, through two 4 KB staging blocks of its own (one being written while the other's
+// store reads it), each 32 x 32 block leaving by its own TMA store (one thread's bulk copies complete in order, so
+// spreading them over eight warps keeps the stores apace);
 // the column constants of a tile are read into shared memory once, C_old straight from global memory.
 // The even CTA's MMA completions are committed to the barriers of both CTAs at once (tcgen05.commit multicast); the
 // odd CTA's epilogue hands each drained accumulator back with a remote mbarrier arrive. With an int8 table (the code
@@ -62,8 +63,8 @@ template <int KIND_> struct QCfg {
     static constexpr uint32_t FL_BYTES = QBK * FL_ROW;
     static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES + (PLANES ? SG_BYTES + FL_BYTES : 0);
     static constexpr uint32_t SBO = 8 * QHN;
-    static constexpr uint32_t WBUF = 32 * 32 * 4;               // one 32 x 32 fp32 output block per epilogue warp
-    static constexpr uint32_t STG_BYTES = NEPI * WBUF;
+    static constexpr uint32_t WBUF = 32 * 32 * 4;               // one 32 x 32 fp32 output block
+    static constexpr uint32_t STG_BYTES = NEPI * 2 * WBUF;      // two per epilogue warp: one written, one storing
     static constexpr uint32_t C1_BYTES = QBN * 4;               // the tile's column constants
     static constexpr uint32_t BAR_BYTES = 512;
     static constexpr uint32_t FIXED = 1024 + STG_BYTES + C1_BYTES + BAR_BYTES;
@@ -385,7 +386,8 @@ fv_gemm_2sm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
         const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
         const bool load_old = !partial && !p.beta_zero;
         const uint32_t tempty_lead = cluster_map(&tempty[0], 0);
-        uint8_t* buf = stg + ew * G::WBUF;
+        uint8_t* bufs = stg + ew * 2 * G::WBUF;
+        int nblk_done = 0;   // blocks this warp has handed to TMA stores (which of its two staging blocks is next)
         griddep_wait();   // a_scales, C_old and C belong to the previous kernels until here
         int it = 0;
         for (int t = pair; t < total; t += npairs, ++it) {
@@ -421,7 +423,8 @@ fv_gemm_2sm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
 #pragma unroll
                     for (int t4 = 0; t4 < 8; ++t4) old[t4] = row_ok ? src[t4] : make_float4(0.f, 0.f, 0.f, 0.f);
                 }
-                if (lane == 0) tma_store_wait_read();   // the store that last read this block has finished reading it
+                uint8_t* buf = bufs + (nblk_done & 1) * G::WBUF;
+                if (lane == 0) tma_store_wait_read_1();   // the store before last (this block's) has finished reading it
                 __syncwarp();
                 tmem_wait_ld();
 #pragma unroll
@@ -443,6 +446,7 @@ fv_gemm_2sm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                     tma_store_2d(&tmOut, buf, n, out_row);
                     tma_store_commit();
                 }
+                ++nblk_done;
             }
             QTRACE(168 + it, ew == 0 && lane == 0 && it < 8);
             // every TMEM read of accumulator b by this warp is complete: hand it back to the pair's MMA issuer
