@@ -921,13 +921,14 @@ def long_audio_ours(pkg, world, rank, local, steps=3):
     """Long-form transcription (the engine's path for long audio): each rank transcribes its own 10-minute recording
     end to end through p2_b200_transcribe_long - pause-aligned windows, dropout re-decodes as one batch per split depth,
     log-mel, encoder and decoder on the device (host audio in, host tokens out). Weak scaling: every rank holds a
-    recording; value = all ranks' audio seconds / the slowest rank's wall time per recording."""
+    recording (the same one, so that every rank has the same windows and re-decodes to do); value = all ranks' audio
+    seconds / the slowest rank's wall time per recording."""
     from phonon2_b200 import model as M
     import torch
     sm = M.SyntheticModel(seed=1, attn_out_gain=M.SPEECH_ATTN_OUT_GAIN)
     x_h = torch.empty(int(LONG_SECONDS * 16000), dtype=torch.float32, pin_memory=True)   # page-locked recording
     x = x_h.numpy()
-    x[...] = M.audio_with_pauses(LONG_SECONDS, 7 + rank)
+    x[...] = M.audio_with_pauses(LONG_SECONDS, 7)   # the same recording on every rank: the same work per rank
     wins, frames = pkg.host_transcribe_long(sm.struct, x, devices=[local])   # weights and plans outside the timing
     barrier(world)
     t0 = time.perf_counter()
@@ -942,7 +943,7 @@ def long_audio_ours(pkg, world, rank, local, steps=3):
     n_tok = sum(len(w["tokens"]) for w in wins)
     return {"metric": "long-form transcription audio-sec/sec", "value": world * LONG_SECONDS / (ms_max / 1e3),
             "unit": "audio-s/s", "ms_per_step": ms_max, "steps": steps, "scaling": "weak",
-            "workload": f"{LONG_SECONDS:.0f} s of synthetic long-form 16 kHz audio per rank (bursts of 1-6 s under a "
+            "workload": f"{LONG_SECONDS:.0f} s of synthetic long-form 16 kHz audio on each rank (bursts of 1-6 s under a "
                         "syllable envelope between pauses of 0.05-1.4 s, seeded), the speech-like synthetic model",
             "windows_by_depth_rank0": depths, "encoder_frames_rank0": frames, "tokens_rank0": n_tok,
             "h2d_bytes_per_step": 4 * int(x.shape[0]), "d2h_bytes_per_step": 12 * n_tok,
