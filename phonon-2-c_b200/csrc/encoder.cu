@@ -321,15 +321,24 @@ int subsampling(P2cuEncoder& e, cudaStream_t s) {
 }
 
 // csrc/encoder.c:319-348.
+// prev_w / prev_b: the previous block's closing norm (norm_out), applied to x first in the same launch, or null.
 int feed_forward(P2cuEncoder& e, const float* nw, const float* nb, const DWeight& w1, const DWeight& w2,
-                 cudaStream_t s) {
+                 cudaStream_t s, const float* prev_w = nullptr, const float* prev_b = nullptr) {
     if (e.mode != P2CU_EXACT) {
-        TRYC(p2cu::ln_rows_launch(e.x, D, nw, nb, nullptr, 0, e.q, e.qs, e.R, D, s), "ff layernorm");
+        if (prev_w)
+            TRYC(p2cu::ln2_rows_launch(e.x, D, prev_w, prev_b, nw, nb, nullptr, 0, e.q, e.qs, e.R, D, s),
+                 "norm_out + ff layernorm");
+        else
+            TRYC(p2cu::ln_rows_launch(e.x, D, nw, nb, nullptr, 0, e.q, e.qs, e.R, D, s), "ff layernorm");
         TRY(wmatmul_q8a(e, e.R, w1, e.big, 1.f, 0.f, s, "ff linear1"));
         TRYC(p2cu::swish_rows_launch(e.big, FF, nullptr, 0, e.q, e.qs, e.R, FF, s), "ff swish");
         return wmatmul_q8a(e, e.R, w2, e.x, 0.5f, 1.f, s, "ff linear2");   // x += ½ · ff(x)
     }
-    TRYC(p2cu::ln_rows_launch(e.x, D, nw, nb, e.lnbuf, D, nullptr, nullptr, e.R, D, s), "ff layernorm");
+    if (prev_w)
+        TRYC(p2cu::ln2_rows_launch(e.x, D, prev_w, prev_b, nw, nb, e.lnbuf, D, nullptr, nullptr, e.R, D, s),
+             "norm_out + ff layernorm");
+    else
+        TRYC(p2cu::ln_rows_launch(e.x, D, nw, nb, e.lnbuf, D, nullptr, nullptr, e.R, D, s), "ff layernorm");
     TRY(wmatmul(e, e.lnbuf, e.R, w1, e.big, 1.f, 0.f, nullptr, s, "ff linear1"));
     TRYC(p2cu::swish_rows_launch(e.big, FF, e.big, FF, nullptr, nullptr, e.R, FF, s), "ff swish");
     p2cu::Epilogue res;
@@ -424,11 +433,15 @@ int forward(P2cuEncoder& e, cudaStream_t s) {
         TRYC(p2cu::gather_rows_launch(e.x, e.x_sub, e.d_gather, e.R, D, s), "chunk gather");
     for (int i = 0; i < NB; ++i) {
         const DBlock& b = e.m->blk[i];
-        TRY(feed_forward(e, b.n_ff1_w, b.n_ff1_b, b.ff1a, b.ff1b, s));
+        // block i - 1's closing norm goes with this block's first LayerNorm (one launch, csrc/encoder.c:617-624)
+        const DBlock* pb = i > 0 ? &e.m->blk[i - 1] : nullptr;
+        TRY(feed_forward(e, b.n_ff1_w, b.n_ff1_b, b.ff1a, b.ff1b, s, pb ? pb->n_out_w : nullptr,
+                         pb ? pb->n_out_b : nullptr));
         TRY(self_attention(e, b, s));
         TRY(conv_module(e, b, s));
         TRY(feed_forward(e, b.n_ff2_w, b.n_ff2_b, b.ff2a, b.ff2b, s));
-        TRYC(p2cu::ln_rows_launch(e.x, D, b.n_out_w, b.n_out_b, e.x, D, nullptr, nullptr, e.R, D, s), "norm_out");
+        if (i == NB - 1)
+            TRYC(p2cu::ln_rows_launch(e.x, D, b.n_out_w, b.n_out_b, e.x, D, nullptr, nullptr, e.R, D, s), "norm_out");
     }
     const float* fin = e.x;
     if (e.chunked) {   // every frame from the chunk that owns it, without the overlap (csrc/encoder.c:704)

@@ -51,24 +51,15 @@ __device__ __forceinline__ char4 quant4(float4 v, float inv) {
     return c;
 }
 
-// D = 128 V; 8 rows per 256-thread block.
-template <int V, bool QUANT>
-__global__ void __launch_bounds__(256) ln_warp_kernel(const float* __restrict__ x, int ldx,
-                                                      const float* __restrict__ gamma, const float* __restrict__ beta,
-                                                      float* out, int ldo, int8_t* __restrict__ q,
-                                                      float* __restrict__ qscale, int rows, int fm) {
+// LayerNorm of one row of D = 128 V held by a warp in registers (lane l: float4s l, l + 32, ...), in place; returns
+// the row's largest magnitude after the norm.
+template <int V>
+__device__ __forceinline__ float ln_regs(float4 (&v)[V], const float* __restrict__ gamma,
+                                         const float* __restrict__ beta, int lane) {
     constexpr int D = 128 * V;
-    const int lane = threadIdx.x & 31;
-    const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
-    if (row >= rows) return;
-    const float4* xr = reinterpret_cast<const float4*>(x + static_cast<size_t>(row) * ldx);
-    float4 v[V];
     float s = 0.f;
 #pragma unroll
-    for (int i = 0; i < V; ++i) {
-        v[i] = xr[lane + 32 * i];
-        s = __fadd_rn(s, __fadd_rn(__fadd_rn(v[i].x, v[i].y), __fadd_rn(v[i].z, v[i].w)));
-    }
+    for (int i = 0; i < V; ++i) s = __fadd_rn(s, __fadd_rn(__fadd_rn(v[i].x, v[i].y), __fadd_rn(v[i].z, v[i].w)));
     const float mean = __fdiv_rn(warp_sum(s), static_cast<float>(D));
     float var = 0.f;
 #pragma unroll
@@ -88,18 +79,64 @@ __global__ void __launch_bounds__(256) ln_warp_kernel(const float* __restrict__ 
         v[i] = ln_apply(v[i], mean, inv, g4[lane + 32 * i], b4[lane + 32 * i]);
         amax = fmaxf(amax, amax4(v[i]));
     }
+    return warp_max(amax);
+}
+
+// The normed row out: fp32 to out, or (QUANT) quantised to q / qscale.
+template <int V, bool QUANT>
+__device__ __forceinline__ void ln_store(const float4 (&v)[V], float amax, float* out, int ldo, int8_t* q,
+                                         float* qscale, int row, int lane, int fm) {
+    constexpr int D = 128 * V;
     if (!QUANT) {
         float4* orow = reinterpret_cast<float4*>(out + static_cast<size_t>(row) * ldo);
 #pragma unroll
         for (int i = 0; i < V; ++i) orow[lane + 32 * i] = v[i];
         return;
     }
-    const QuantRule qr = quant_rule(warp_max(amax), fm);
-    const float scale = qr.scale, qinv = qr.inv;
+    const QuantRule qr = quant_rule(amax, fm);
     char4* qrow = reinterpret_cast<char4*>(q + static_cast<size_t>(row) * D);
 #pragma unroll
-    for (int i = 0; i < V; ++i) qrow[lane + 32 * i] = quant4(v[i], qinv);
-    if (lane == 0) qscale[row] = scale;
+    for (int i = 0; i < V; ++i) qrow[lane + 32 * i] = quant4(v[i], qr.inv);
+    if (lane == 0) qscale[row] = qr.scale;
+}
+
+// D = 128 V; 8 rows per 256-thread block.
+template <int V, bool QUANT>
+__global__ void __launch_bounds__(256) ln_warp_kernel(const float* __restrict__ x, int ldx,
+                                                      const float* __restrict__ gamma, const float* __restrict__ beta,
+                                                      float* out, int ldo, int8_t* __restrict__ q,
+                                                      float* __restrict__ qscale, int rows, int fm) {
+    const int lane = threadIdx.x & 31;
+    const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (row >= rows) return;
+    const float4* xr = reinterpret_cast<const float4*>(x + static_cast<size_t>(row) * ldx);
+    float4 v[V];
+#pragma unroll
+    for (int i = 0; i < V; ++i) v[i] = xr[lane + 32 * i];
+    const float amax = ln_regs<V>(v, gamma, beta, lane);
+    ln_store<V, QUANT>(v, amax, out, ldo, q, qscale, row, lane, fm);
+}
+
+// Two LayerNorms in a row (a block's closing norm, then the next block's first): x <- LN1(x) in place, then LN2 of
+// the new row to out2 or quantised - the values LN2 would read back, straight from registers.
+template <int V, bool QUANT>
+__global__ void __launch_bounds__(256) ln2_warp_kernel(float* x, int ldx, const float* __restrict__ g1,
+                                                       const float* __restrict__ b1, const float* __restrict__ g2,
+                                                       const float* __restrict__ b2, float* out2, int ldo,
+                                                       int8_t* __restrict__ q, float* __restrict__ qscale, int rows,
+                                                       int fm) {
+    const int lane = threadIdx.x & 31;
+    const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (row >= rows) return;
+    float4* xr = reinterpret_cast<float4*>(x + static_cast<size_t>(row) * ldx);
+    float4 v[V];
+#pragma unroll
+    for (int i = 0; i < V; ++i) v[i] = xr[lane + 32 * i];
+    ln_regs<V>(v, g1, b1, lane);
+#pragma unroll
+    for (int i = 0; i < V; ++i) xr[lane + 32 * i] = v[i];
+    const float amax = ln_regs<V>(v, g2, b2, lane);
+    ln_store<V, QUANT>(v, amax, out2, ldo, q, qscale, row, lane, fm);
 }
 
 // Any D and alignment: one 256-thread block per row, the row re-read from L1/L2 in each pass.
@@ -759,6 +796,22 @@ cudaError_t ln_rows_launch(const float* x, int ldx, const float* gamma, const fl
     }
     if (q) ln_rows_kernel<true><<<rows, 256, 0, s>>>(x, ldx, gamma, beta, out, ldo, q, qscale, D, fm);
     else ln_rows_kernel<false><<<rows, 256, 0, s>>>(x, ldx, gamma, beta, out, ldo, q, qscale, D, fm);
+    return cudaGetLastError();
+}
+
+cudaError_t ln2_rows_launch(float* x, int ldx, const float* g1, const float* b1, const float* g2, const float* b2,
+                            float* out2, int ldo, int8_t* q, float* qscale, int rows, int D, cudaStream_t s) {
+    if (rows <= 0) return cudaSuccess;
+    const bool vec = D == 1024 && ldx % 4 == 0 && al16(x) && al16(g1) && al16(b1) && al16(g2) && al16(b2) &&
+                     (q ? al16(q) : (ldo % 4 == 0 && al16(out2)));
+    if (!vec) {   // two passes
+        cudaError_t e = ln_rows_launch(x, ldx, g1, b1, x, ldx, nullptr, nullptr, rows, D, s);
+        return e != cudaSuccess ? e : ln_rows_launch(x, ldx, g2, b2, out2, ldo, q, qscale, rows, D, s);
+    }
+    const unsigned grid = static_cast<unsigned>((rows + 7) / 8);
+    const int fm = quant_fast_math();
+    if (q) ln2_warp_kernel<8, true><<<grid, 256, 0, s>>>(x, ldx, g1, b1, g2, b2, out2, ldo, q, qscale, rows, fm);
+    else ln2_warp_kernel<8, false><<<grid, 256, 0, s>>>(x, ldx, g1, b1, g2, b2, out2, ldo, q, qscale, rows, fm);
     return cudaGetLastError();
 }
 

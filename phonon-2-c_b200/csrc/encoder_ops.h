@@ -13,6 +13,10 @@ namespace p2cu {
 cudaError_t ln_rows_launch(const float* x, int ldx, const float* gamma, const float* beta, float* out, int ldo,
                            int8_t* q, float* qscale, int rows, int D, cudaStream_t s);
 
+// Two LayerNorms in a row: x <- LN(x; g1, b1) in place, then LN(x; g2, b2) into out2 or quantised into q / qscale.
+cudaError_t ln2_rows_launch(float* x, int ldx, const float* g1, const float* b1, const float* g2, const float* b2,
+                            float* out2, int ldo, int8_t* q, float* qscale, int rows, int D, cudaStream_t s);
+
 // SiLU of each row, into `out` (fp32, may alias h) or quantised into q / qscale.
 cudaError_t swish_rows_launch(const float* h, int ldh, float* out, int ldo, int8_t* q, float* qscale, int rows,
                               int len, cudaStream_t s);
