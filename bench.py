@@ -531,7 +531,7 @@ def configs_ours(args, world, rank, local, torch, pkg, headline, gemm_ms, algo_b
         for weights in ("codes", "planes"):
             t = time_replays(torch, stream, step_graphs(pkg, torch, dev, stream, pkg.INT8W,
                                                         [("ff1.linear1", Mbig, 1024, 4096, 1.0, 0.0)], weights, seed,
-                                                        gemm_only=True), 20)
+                                                        gemm_only=True), 100)
             v = Mbig * 1024 * 4096 / (t * 1e9)
             lm[f"M{Mbig}_{weights}"] = {"tmacs": round(v), "frac_int8": round(v / peak_i8, 3)}
     out["large_m"] = lm

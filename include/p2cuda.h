@@ -171,6 +171,20 @@ P2CU_API int p2cu_depthwise_conv1d_rows(const float *x, const float *w, const fl
 P2CU_API int p2cu_sgemm_tf32x3(int transB, int M, int N, int K, const float *A, int lda, const float *B, int ldb,
                                float *C, int ldc, void *stream);
 
+/* Relative-position self-attention of one encoder layer (self_attention's core, csrc/encoder.c:471-528) for n_win
+ * windows on device rows, as the encoder runs it: qkv [R][3072] holds each window's Q | K | V rows (window w's T[w]
+ * rows follow window w - 1's), P [2 Tmax - 1][1024] the projected positions of a window of Tmax frames (a window of
+ * T frames uses rows Tmax - T .. Tmax + T - 2), bias_u and bias_v [1024]. attn [R][1024] receives, per head h and
+ * window, softmax(((Q_h + bias_u) K_h^T + shift((Q_h + bias_v) P_h^T)) / sqrt(128)) V_h, the heads concatenated
+ * (csrc/encoder.c:425-447 for the shift). T: the windows' lengths in host memory, each <= Tmax <= 512. One kernel on
+ * the tensor cores, the products in the three-part tf32 split (fp32 accuracy, the summation order the tensor core's),
+ * the scores never in device memory. ws: device scratch of p2cu_rel_attention_ws_bytes(n_win, T) bytes, 16-byte
+ * aligned; every pointer 16-byte aligned. */
+P2CU_API size_t p2cu_rel_attention_ws_bytes(int n_win, const int *T);
+P2CU_API int p2cu_rel_attention(const float *qkv, const float *P, const float *bias_u, const float *bias_v,
+                                const int *T, int n_win, int Tmax, float *attn, void *ws, size_t ws_bytes,
+                                void *stream);
+
 /* ---- The encoder on the device (csrc/encoder.c) ------------------------------------------------------------------
  * Unlike the calls above these allocate device memory, once: p2cu_model_upload copies a model's weights to the
  * current device, p2cu_encoder_create makes a plan with every buffer of one batch of windows and captures its forward

@@ -74,6 +74,8 @@ SIGNATURES = {
     "p2cu_softmax_rows": (_i, [_vp, _i, _i, _vp]),
     "p2cu_depthwise_conv1d_rows": (_i, [_vp, _vp, _vp, _vp, _i, _i, _vp]),
     "p2cu_sgemm_tf32x3": (_i, [_i, _i, _i, _i, _vp, _i, _vp, _i, _vp, _i, _vp]),
+    "p2cu_rel_attention_ws_bytes": (_sz, [_i, C.POINTER(_i)]),
+    "p2cu_rel_attention": (_i, [_vp, _vp, _vp, _vp, C.POINTER(_i), _i, _i, _vp, _vp, _sz, _vp]),
     "p2cu_model_upload": (_i, [_vp, _i, C.POINTER(_vp)]),
     "p2cu_model_free": (None, [_vp]),
     "p2cu_model_bytes": (_sz, [_vp]),

@@ -18,6 +18,7 @@
 #include <cuda_runtime.h>
 #include "attn_tc.h"
 #include "ptx.cuh"
+#include "tf32_split.cuh"
 
 namespace p2cu {
 
@@ -32,18 +33,6 @@ constexpr uint32_t SMEM_BYTES = 1024 + TSTAGES * STAGE + 256;
 constexpr int NTHREADS = 160;               // warps 0-3 load / split / read out, warp 4 issues the MMAs
 constexpr int PER = TM * TK / 4 / 128;      // float4 per loader thread per operand and stage
 
-// x rounded to the tf32 grid (10 explicit mantissa bits, ties away from zero) and the exact remainder.
-__device__ __forceinline__ void split(float x, float& hi, float& lo) {
-    hi = __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u);
-    lo = __fsub_rn(x, hi);
-}
-
-// Byte offset of (row r, 16-byte chunk c) in a K-major tile of 64-byte rows with the 64-byte swizzle (8-row groups
-// of 512 bytes; chunk c of row r sits at chunk c ^ ((r >> 1) & 3)).
-__device__ __forceinline__ uint32_t kmaj_off(int r, int c) {
-    return static_cast<uint32_t>((r >> 3) * 512 + (r & 7) * 64 + ((c ^ ((r >> 1) & 3)) << 4));
-}
-
 __device__ __forceinline__ float4 load4(const float* row, int k, int K, bool vec) {   // row[k .. k+3], zero past K
     if (vec && k + 3 < K) return __ldg(reinterpret_cast<const float4*>(row + k));
     float4 v;
@@ -52,16 +41,6 @@ __device__ __forceinline__ float4 load4(const float* row, int k, int K, bool vec
     v.z = k + 2 < K ? __ldg(row + k + 2) : 0.f;
     v.w = k + 3 < K ? __ldg(row + k + 3) : 0.f;
     return v;
-}
-
-__device__ __forceinline__ void store_split(uint8_t* hi_tile, uint8_t* lo_tile, uint32_t off, float4 v) {
-    float4 h, l;
-    split(v.x, h.x, l.x);
-    split(v.y, h.y, l.y);
-    split(v.z, h.z, l.z);
-    split(v.w, h.w, l.w);
-    *reinterpret_cast<float4*>(hi_tile + off) = h;
-    *reinterpret_cast<float4*>(lo_tile + off) = l;
 }
 
 template <bool B_KN>

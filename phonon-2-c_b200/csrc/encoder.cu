@@ -239,8 +239,9 @@ struct P2cuEncoder {
     int ng = 0, t_ac = 0, t_bd = 0, t_av = 0;
     int2* att_tiles = nullptr;   // fused attention (every window <= ATT_MAXT frames): (window, first query) per tile
     int n_att_tiles = 0;
-    // Attention path: 0 = tensor cores (products as split-tf32 tcgen05 GEMMs, scores in HBM), 1 = SIMT grouped GEMMs,
-    // 2 = SIMT fused kernel (short windows). P2CU_ATTN=tc|simt|fused chooses; tc is the default.
+    // Attention path: 3 = one tensor-core kernel per layer, scores in TMEM (windows of at most ATT_MAXT frames; the
+    // default), 0 = tensor-core products as grouped split-tf32 GEMMs with the scores in HBM (the default for longer
+    // windows), 1 = SIMT grouped GEMMs, 2 = SIMT fused kernel (short windows). P2CU_ATTN=tc_fused|tc|simt|fused.
     int attn_path = 0;
     p2cu::TcGroup *tc_scores = nullptr, *tc_context = nullptr;
     int n_tc = 0, t_tc_scores = 0, t_tc_context = 0;
@@ -379,6 +380,9 @@ int self_attention(P2cuEncoder& e, const DBlock& b, cudaStream_t s) {
         c.dst[0] = e.attn; c.dst[1] = e.attn;
         c.err = a.err;
         TRYC(p2cu::attn_tc_launch(e.tc_context, e.n_tc, e.t_tc_context, c, false, s), "attention context");
+    } else if (e.attn_path == 3) {
+        TRY(p2cu::attn_rel_tc_launch(e.big, e.R, e.P, b.bias_u, b.bias_v, e.d_row_off, e.att_tiles, e.n_att_tiles,
+                                     e.Tmax, e.scale, e.attn, p2cu::device_error_word(), s));
     } else if (e.n_att_tiles) {
         TRYC(p2cu::attn_fused_launch(e.big, e.P, b.bias_u, b.bias_v, e.d_row_off, e.att_tiles, e.n_att_tiles, e.Tmax,
                                      e.scale, e.attn, s),
@@ -581,7 +585,11 @@ int create_plan(const P2cuModel* m, const int* n_frames, int n_mel_win, int mode
     e->srows = srow_off.back();
     {
         const char* ap = getenv("P2CU_ATTN");
-        e->attn_path = ap && strcmp(ap, "simt") == 0 ? 1 : ap && strcmp(ap, "fused") == 0 ? 2 : 0;
+        const bool fits = e->Tmax <= p2cu::ATT_MAXT;
+        if (ap && strcmp(ap, "simt") == 0) e->attn_path = 1;
+        else if (ap && strcmp(ap, "fused") == 0) e->attn_path = 2;
+        else if (ap && strcmp(ap, "tc") == 0) e->attn_path = 0;
+        else e->attn_path = fits ? 3 : 0;
     }
     // tensor-core groups: scores (AC then BD groups, one launch) and context (one launch)
     std::vector<p2cu::TcGroup> tcs, tcc;
@@ -626,11 +634,12 @@ int create_plan(const P2cuModel* m, const int* n_frames, int n_mel_win, int mode
         e->t_tc_scores = ts;
         e->t_tc_context = tc;
     }
-    const bool fused = e->attn_path == 2 && e->Tmax <= p2cu::ATT_MAXT;
+    const bool fused = (e->attn_path == 2 || e->attn_path == 3) && e->Tmax <= p2cu::ATT_MAXT;
     std::vector<int2> att_tiles;
-    if (fused) {
+    if (fused) {   // (window, first query) of every query tile: 32 queries (SIMT) or 128 (tensor cores)
+        const int step = e->attn_path == 3 ? p2cu::ATT_TC_QT : 32;
         for (int w = 0; w < n_win; ++w)
-            for (int q0 = 0; q0 < e->T[w]; q0 += 32) att_tiles.push_back(make_int2(w, q0));
+            for (int q0 = 0; q0 < e->T[w]; q0 += step) att_tiles.push_back(make_int2(w, q0));
         e->n_att_tiles = static_cast<int>(att_tiles.size());
         e->s_total = e->b_total = 0;   // no score matrices in HBM
     }

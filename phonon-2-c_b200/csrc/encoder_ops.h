@@ -93,4 +93,13 @@ cudaError_t attn_fused_launch(const float* qkv, const float* P, const float* bia
                               const int* row_off, const int2* tiles, int n_tiles, int Tmax, float scale, float* attn,
                               cudaStream_t s);
 
+// The same attention on the tensor cores (attn_rel_tc.cu): one CTA per (128-query tile, head), the products in the
+// three-part tf32 split, softmax in the kernel. qkv has `rows` rows (TMA reads past a window's rows, never past
+// these); tiles: (window, first query) of every ATT_TC_QT-query tile; err: the device error word of the bounded
+// waits. Returns a P2CU code.
+constexpr int ATT_TC_QT = 128;
+int attn_rel_tc_launch(const float* qkv, int rows, const float* P, const float* bias_u, const float* bias_v,
+                       const int* row_off, const int2* tiles, int n_tiles, int Tmax, float scale, float* attn,
+                       uint32_t* err, cudaStream_t s);
+
 }  // namespace p2cu

@@ -311,6 +311,24 @@ __device__ __forceinline__ void mma_i8_lead(uint32_t lead, uint32_t tmem_d, uint
                  "@e tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}"
                  :: "r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(lead) : "memory");
 }
+__device__ __forceinline__ void mma_tf32_lead(uint32_t lead, uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                              uint32_t idesc, uint32_t accumulate) {
+    asm volatile("{\n\t.reg .pred e, p;\n\t"
+                 "setp.ne.b32 e, %5, 0;\n\t"
+                 "setp.ne.b32 p, %4, 0;\n\t"
+                 "@e tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}"
+                 :: "r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(lead) : "memory");
+}
+// D[tmem] (+)= A[tmem] * B[smem], tf32 x tf32 -> fp32: A (M = 128 rows, one per TMEM lane, one tf32 K value per
+// 32-bit column) read from tensor memory at tmem_a.
+__device__ __forceinline__ void mma_tf32_ts_lead(uint32_t lead, uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc,
+                                                 uint32_t idesc, uint32_t accumulate) {
+    asm volatile("{\n\t.reg .pred e, p;\n\t"
+                 "setp.ne.b32 e, %5, 0;\n\t"
+                 "setp.ne.b32 p, %4, 0;\n\t"
+                 "@e tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}"
+                 :: "r"(tmem_d), "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(lead) : "memory");
+}
 __device__ __forceinline__ void mma_commit_lead(uint32_t lead, uint64_t* bar) {
     asm volatile("{\n\t.reg .pred e;\n\t"
                  "setp.ne.b32 e, %1, 0;\n\t"

@@ -281,10 +281,11 @@ def test_encode_windows_spread_over_devices(pkg, cuda, model):
         assert np.array_equal(a.view(np.uint32), one.view(np.uint32))
 
 
-@pytest.mark.parametrize("path", ["tc", "simt", "fused"])
+@pytest.mark.parametrize("path", ["tc_fused", "tc", "simt", "fused"])
 def test_attention_paths_match_reference(pkg, orc, cuda, model, dev_model, path, monkeypatch):
-    """Each attention implementation (tensor cores with split-tf32 operands, SIMT grouped GEMMs, the fused SIMT
-    kernel) gives the exact-mode encoder within 1e-4 of the reference (P2CU_ATTN chooses; the plan reads it)."""
+    """Each attention implementation (the fused tensor-core kernel, the tensor-core products with the scores in
+    device memory, SIMT grouped GEMMs, the fused SIMT kernel) gives the exact-mode encoder within 1e-4 of the
+    reference (P2CU_ATTN chooses; the plan reads it)."""
     import torch
     from phonon2_b200 import model as M
     monkeypatch.setenv("P2CU_ATTN", path)
