@@ -225,7 +225,8 @@ attn_rel_tc_kernel(const __grid_constant__ AttnMaps maps, const float* __restric
                 for (int i = 0; i < 2; ++i) {
                     const int e = t + 128 * i, row = e >> 2;
                     const uint32_t X = e * 16;
-                    const int dim = 16 * kk + 4 * ((e & 3) ^ ((row >> 1) & 3));   // the chunk's place before the swizzle
+                    // the 16-byte chunk's dimensions: its place in the row before the 64-byte swizzle
+                    const int dim = 16 * kk + 4 * ((e & 3) ^ ((row >> 1) & 3));
                     const float4 x1 = *reinterpret_cast<const float4*>(B + RAW_B1 + X);
                     const float4 x2 = *reinterpret_cast<const float4*>(B + RAW_B2 + X);
                     *reinterpret_cast<float4*>(B + LO_B1 + X) = lo4(x1);

@@ -307,10 +307,9 @@ int subsampling(P2cuEncoder& e, cudaStream_t s) {
     const P2cuModel& m = *e.m;
     const int W1 = conv_out(NMEL), W2 = conv_out(W1), W3 = conv_out(W2);
     const int nw = e.n_mel_win;
-    TRYC(p2cu::sub_conv0_launch(e.mel, e.d_mel_off, e.d_h1_off, nw, m.c0w, m.c0b, e.s1, e.rows1, NMEL, SUBC, s),
-         "subsampling conv0");
-    TRYC(p2cu::sub_dwconv_launch(e.s1, e.d_h1_off, e.d_h2_off, nw, m.c2w, m.c2b, e.s2dw, e.rows2, W1, SUBC, s),
-         "subsampling conv2");
+    TRYC(p2cu::sub_conv0_dw_launch(e.mel, e.d_mel_off, e.d_h1_off, e.d_h2_off, nw, m.c0w, m.c0b, m.c2w, m.c2b, e.s2dw,
+                                   e.rows2, NMEL, SUBC, s),
+         "subsampling conv0 + conv2");
     TRY(conv1x1_tc(e.s2dw, e.rows2 * W2, m.c3w, m.c3b, e.s2, s, "subsampling conv3"));
     TRYC(p2cu::sub_dwconv_launch(e.s2, e.d_h2_off, e.d_sub_off, nw, m.c5w, m.c5b, e.s3dw, e.R_sub, W2, SUBC, s),
          "subsampling conv5");
@@ -652,7 +651,8 @@ int create_plan(const P2cuModel* m, const int* n_frames, int n_mel_win, int mode
     const size_t f = sizeof(float);
     e->ws_bytes = p2cu::gemm_split_bytes(std::max(R, Rs), D, FF);
     struct Slot { void** p; size_t bytes; };
-    const size_t s1_bytes = std::max(static_cast<size_t>(e->rows1) * W1 * SUBC, static_cast<size_t>(Rs) * FF) * f;
+    const size_t s1_bytes = static_cast<size_t>(Rs) * FF * f;   // the flattened frames (the first convolution's
+                                                                // outputs are not stored)
     const size_t q_bytes = static_cast<size_t>(std::max(R, Rs)) * FF;
     std::vector<Slot> slots = {
         {reinterpret_cast<void**>(&e->mel), static_cast<size_t>(e->mel_rows) * NMEL * f},

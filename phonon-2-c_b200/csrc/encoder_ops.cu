@@ -332,105 +332,185 @@ __global__ void glu_rows_kernel(const float* __restrict__ pw1, float* __restrict
     gated[i] = __fdiv_rn(a, __fadd_rn(1.0f, expf(b < -87.0f ? 87.0f : -b)));
 }
 
-// One CTA per row (time step t of its window): for each channel, bias + the 9 taps over t - 4 .. t + 4 that fall
-// inside the window, as one FMA chain in tap order; then SiLU; then fp32 out or the row quantised.
+// DW_TR consecutive rows per CTA, 256 threads, four channels per thread: the DW_TR + 8 input rows the tile's taps
+// reach are loaded once into registers (a CTA reads each input row about twice instead of nine times). For each row
+// (time step t of its window) and channel: bias + the 9 taps over t - 4 .. t + 4 that fall inside the window, as one
+// FMA chain in tap order; then SiLU; then fp32 out or the row quantised.
+constexpr int DW_TR = 8;
+
 template <bool QUANT, bool SWISH>
 __global__ void __launch_bounds__(256) dwconv_swish_kernel(const float* __restrict__ gated, const float* __restrict__ w,
                                                            const float* __restrict__ b,
                                                            const int* __restrict__ row_off, int n_win,
                                                            float* __restrict__ out, int8_t* __restrict__ q,
                                                            float* __restrict__ qscale, int rows, int D, int fm) {
-    __shared__ float red[8];
+    __shared__ float red[8][DW_TR];
     constexpr int PER = 4;   // channels per thread (D <= 1024)
-    const int r = blockIdx.x;
-    // without a window table the rows are one window
-    const int win = row_off ? find_window(row_off, n_win, r) : 0;
-    const int r0 = row_off ? row_off[win] : 0, T = row_off ? row_off[win + 1] - r0 : rows, t = r - r0;
-    float v[PER];
-    float amax = 0.f;
+    const int g0 = blockIdx.x * DW_TR;   // the tile's first row
+    // the window bounds [lo, hi) of each of the tile's rows (without a window table the rows are one window)
+    int lo[DW_TR], hi[DW_TR];
+    {
+        int win = row_off ? find_window(row_off, n_win, g0) : 0;
+#pragma unroll
+        for (int i = 0; i < DW_TR; ++i) {
+            if (row_off) {
+                while (win + 1 < n_win && g0 + i >= row_off[win + 1]) ++win;
+                lo[i] = row_off[win];
+                hi[i] = row_off[win + 1];
+            } else {
+                lo[i] = 0;
+                hi[i] = rows;
+            }
+        }
+    }
+    float v[DW_TR][PER];
 #pragma unroll
     for (int u = 0; u < PER; ++u) {
         const int d = threadIdx.x + 256 * u;
-        v[u] = 0.f;
-        if (d < D) {
-            float acc = b ? b[d] : 0.f;
-            const float* wd = w + static_cast<size_t>(d) * 9;
+        if (d >= D) {
+#pragma unroll
+            for (int i = 0; i < DW_TR; ++i) v[i][u] = 0.f;
+            continue;
+        }
+        float x[DW_TR + 8];   // input rows g0 - 4 .. g0 + DW_TR + 3 of channel d
+#pragma unroll
+        for (int j = 0; j < DW_TR + 8; ++j) {
+            const int g = g0 - 4 + j;
+            x[j] = (g >= 0 && g < rows) ? __ldg(gated + static_cast<size_t>(g) * D + d) : 0.f;
+        }
+        float wk[9];
+#pragma unroll
+        for (int k = 0; k < 9; ++k) wk[k] = __ldg(w + static_cast<size_t>(d) * 9 + k);
+        const float bd = b ? __ldg(b + d) : 0.f;
+#pragma unroll
+        for (int i = 0; i < DW_TR; ++i) {
+            float acc = bd;
 #pragma unroll
             for (int k = 0; k < 9; ++k) {
-                const int src = t - 4 + k;
-                if (src >= 0 && src < T) acc = __fmaf_rn(gated[static_cast<size_t>(r0 + src) * D + d], wd[k], acc);
+                const int src = g0 + i - 4 + k;
+                if (src >= lo[i] && src < hi[i]) acc = __fmaf_rn(x[i + k], wk[k], acc);
             }
-            v[u] = SWISH ? swish1(acc) : acc;
-            amax = fmaxf(amax, fabsf(v[u]));
+            v[i][u] = SWISH ? swish1(acc) : acc;
         }
     }
-    if (!QUANT) {
+    if constexpr (!QUANT) {
 #pragma unroll
-        for (int u = 0; u < PER; ++u) {
-            const int d = threadIdx.x + 256 * u;
-            if (d < D) out[static_cast<size_t>(r) * D + d] = v[u];
+        for (int i = 0; i < DW_TR; ++i) {
+            if (g0 + i >= rows) break;
+#pragma unroll
+            for (int u = 0; u < PER; ++u) {
+                const int d = threadIdx.x + 256 * u;
+                if (d < D) out[static_cast<size_t>(g0 + i) * D + d] = v[i][u];
+            }
         }
         return;
     }
-    amax = block_max256(amax, red);
-    const QuantRule qr = quant_rule(amax, fm);
-    const float scale = qr.scale;
+    if constexpr (QUANT) {
+    // per row: the largest |value| over the 1024 channels (warp maxima in shared memory, then all eight)
 #pragma unroll
-    for (int u = 0; u < PER; ++u) {
-        const int d = threadIdx.x + 256 * u;
-        if (d < D) q[static_cast<size_t>(r) * D + d] = quant_at(v[u], qr, d, D, fm);
+    for (int i = 0; i < DW_TR; ++i) {
+        float a = 0.f;
+#pragma unroll
+        for (int u = 0; u < PER; ++u) a = fmaxf(a, fabsf(v[i][u]));
+        a = warp_max(a);
+        if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5][i] = a;
     }
-    if (threadIdx.x == 0) qscale[r] = scale;
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < DW_TR; ++i) {
+        const int r = g0 + i;
+        if (r >= rows) break;
+        float amax = red[0][i];
+#pragma unroll
+        for (int k = 1; k < 8; ++k) amax = fmaxf(amax, red[k][i]);
+        const QuantRule qr = quant_rule(amax, fm);
+#pragma unroll
+        for (int u = 0; u < PER; ++u) {
+            const int d = threadIdx.x + 256 * u;
+            if (d < D) q[static_cast<size_t>(r) * D + d] = quant_at(v[i][u], qr, d, D, fm);
+        }
+        if (threadIdx.x == 0) qscale[r] = qr.scale;
+    }
+    }
 }
 
 // ---- convolutional subsampling (csrc/encoder.c:98-225) ------------------------------------------------------------
 
 __device__ __forceinline__ int conv_out(int n) { return (n + 2 - 3) / 2 + 1; }
 
-// Conv2d(1 -> C, 3x3, stride 2, pad 1) + ReLU; out [rows1][W1][C], C fastest. One block per output row and 16
-// output columns, one thread per channel with its 9 taps in registers; the three input rows are staged in shared
-// memory. Per output: bias, then the in-range taps in (kh, kw) order as one FMA chain.
-constexpr int SUB_OW = 16;
-
-__global__ void __launch_bounds__(256) sub_conv0_kernel(const float* __restrict__ mel, const int* __restrict__ mel_off,
-                                                        const int* __restrict__ h1_off, int n_win,
-                                                        const float* __restrict__ w, const float* __restrict__ b,
-                                                        float* __restrict__ out, int W_in, int C) {
-    __shared__ float xs[3][2 * SUB_OW + 1];
-    const int W1 = conv_out(W_in);
-    const int r1 = blockIdx.x, ow0 = blockIdx.y * SUB_OW;
-    const int win = find_window(h1_off, n_win, r1);
-    const int oh = r1 - h1_off[win];
+// Conv2d(1 -> C, 3x3, stride 2, pad 1) + ReLU, then the depthwise Conv2d(C, 3x3, stride 2, pad 1) + bias that
+// follows it, per window: mel [frames][W_IN] -> [rows2][W2][C], C fastest. The first convolution's outputs are
+// computed where the second needs them instead of stored (each about twice; stored they are 6.3 GB at config 3):
+// one block per output row, one thread per channel, the 7 mel rows the row reaches in shared memory. Every
+// first-convolution output is bias, then its in-range taps in (kh, kw) order as one FMA chain, then ReLU; every
+// output is bias, then the in-range first-convolution outputs in (kh, kw) order as one FMA chain - the two layers'
+// own chains (csrc/encoder.c:103-153, 185-194), so the result is that of the two layers run one after the other.
+template <int W_IN>
+__global__ void __launch_bounds__(256) sub_conv0_dw_kernel(const float* __restrict__ mel,
+                                                           const int* __restrict__ mel_off,
+                                                           const int* __restrict__ h1_off,
+                                                           const int* __restrict__ h2_off, int n_win,
+                                                           const float* __restrict__ w0, const float* __restrict__ b0,
+                                                           const float* __restrict__ w2, const float* __restrict__ b2,
+                                                           float* __restrict__ out, int C) {
+    constexpr int W1 = (W_IN - 1) / 2 + 1, W2 = (W1 - 1) / 2 + 1;
+    __shared__ float xs[7][W_IN];   // mel rows 4 oh2 - 3 .. 4 oh2 + 3 of the window (zeros outside it)
+    const int r2 = blockIdx.x;
+    const int win = find_window(h2_off, n_win, r2);
+    const int oh2 = r2 - h2_off[win];
+    const int H1 = h1_off[win + 1] - h1_off[win];
     const int H = mel_off[win + 1] - mel_off[win];
-    const float* x = mel + static_cast<size_t>(mel_off[win]) * W_in;
-    const int iw0 = 2 * ow0 - 1;
-    for (int e = threadIdx.x; e < 3 * (2 * SUB_OW + 1); e += blockDim.x) {
-        const int kh = e / (2 * SUB_OW + 1), col = e % (2 * SUB_OW + 1);
-        const int ih = 2 * oh - 1 + kh, iw = iw0 + col;
-        xs[kh][col] = (ih >= 0 && ih < H && iw >= 0 && iw < W_in) ? x[static_cast<size_t>(ih) * W_in + iw] : 0.f;
+    const float* x = mel + static_cast<size_t>(mel_off[win]) * W_IN;
+    for (int e = threadIdx.x; e < 7 * W_IN; e += blockDim.x) {
+        const int j = e / W_IN, col = e % W_IN, ih = 4 * oh2 - 3 + j;
+        xs[j][col] = (ih >= 0 && ih < H) ? x[static_cast<size_t>(ih) * W_IN + col] : 0.f;
     }
     __syncthreads();
     for (int c = threadIdx.x; c < C; c += blockDim.x) {
-        float wc[9];
+        float w0c[9], w2c[9];
 #pragma unroll
-        for (int k = 0; k < 9; ++k) wc[k] = w[c * 9 + k];
-        const float bc = b[c];
-        for (int ow = ow0; ow < ow0 + SUB_OW && ow < W1; ++ow) {
-            float acc = bc;
+        for (int k = 0; k < 9; ++k) {
+            w0c[k] = w0[c * 9 + k];
+            w2c[k] = w2[c * 9 + k];
+        }
+        const float b0c = b0[c];
+        float acc[W2];
 #pragma unroll
-            for (int kh = 0; kh < 3; ++kh) {
-                const int ih = 2 * oh - 1 + kh;
-                if (ih < 0 || ih >= H) continue;
+        for (int ow = 0; ow < W2; ++ow) acc[ow] = b2[c];
+#pragma unroll
+        for (int kh = 0; kh < 3; ++kh) {   // the second convolution's row taps: first-convolution row ih1
+            const int ih1 = 2 * oh2 - 1 + kh;
+            if (ih1 < 0 || ih1 >= H1) continue;
+            float cv[W1];
+#pragma unroll
+            for (int iw1 = 0; iw1 < W1; ++iw1) {
+                float a = b0c;
+#pragma unroll
+                for (int kh0 = 0; kh0 < 3; ++kh0) {
+                    const int ih = 2 * ih1 - 1 + kh0;   // mel row 4 oh2 - 3 + 2 kh + kh0
+                    if (ih < 0 || ih >= H) continue;
+#pragma unroll
+                    for (int kw0 = 0; kw0 < 3; ++kw0) {
+                        const int iw = 2 * iw1 - 1 + kw0;
+                        if (iw >= 0 && iw < W_IN) a = __fmaf_rn(xs[2 * kh + kh0][iw], w0c[kh0 * 3 + kw0], a);
+                    }
+                }
+                cv[iw1] = a > 0.f ? a : 0.f;
+            }
+#pragma unroll
+            for (int ow = 0; ow < W2; ++ow)
 #pragma unroll
                 for (int kw = 0; kw < 3; ++kw) {
-                    const int iw = 2 * ow - 1 + kw;
-                    if (iw >= 0 && iw < W_in) acc = __fmaf_rn(xs[kh][iw - iw0], wc[kh * 3 + kw], acc);
+                    const int iw1 = 2 * ow - 1 + kw;
+                    if (iw1 >= 0 && iw1 < W1) acc[ow] = __fmaf_rn(cv[iw1], w2c[kh * 3 + kw], acc[ow]);
                 }
-            }
-            out[(static_cast<size_t>(r1) * W1 + ow) * C + c] = acc > 0.f ? acc : 0.f;
         }
+#pragma unroll
+        for (int ow = 0; ow < W2; ++ow) out[(static_cast<size_t>(r2) * W2 + ow) * C + c] = acc[ow];
     }
 }
+
+constexpr int SUB_OW = 16;   // output columns per block of the depthwise subsampling convolution
 
 // Depthwise Conv2d(C, 3x3, stride 2, pad 1) + bias (no activation), per window: [rows_in][W_in][C] ->
 // [rows_out][W_out][C]. One block per output row and 16 output columns, one thread per channel (loads coalesced
@@ -863,7 +943,8 @@ cudaError_t dwconv_swish_launch(const float* gated, const float* w, const float*
     if (D > 1024) return cudaErrorInvalidValue;
     auto* k = q ? (swish ? dwconv_swish_kernel<true, true> : dwconv_swish_kernel<true, false>)
                 : (swish ? dwconv_swish_kernel<false, true> : dwconv_swish_kernel<false, false>);
-    k<<<rows, 256, 0, s>>>(gated, w, b, row_off, n_win, out, q, qscale, rows, D, quant_fast_math());
+    k<<<(rows + DW_TR - 1) / DW_TR, 256, 0, s>>>(gated, w, b, row_off, n_win, out, q, qscale, rows, D,
+                                                 quant_fast_math());
     return cudaGetLastError();
 }
 
@@ -874,12 +955,12 @@ cudaError_t gather_rows_launch(float* dst, const float* src, const int* map, int
     return cudaGetLastError();
 }
 
-cudaError_t sub_conv0_launch(const float* mel, const int* mel_off, const int* h1_off, int n_win, const float* w,
-                             const float* b, float* out, int rows1, int W_in, int C, cudaStream_t s) {
-    const int W1 = (W_in - 1) / 2 + 1;
-    if (rows1 <= 0 || W1 <= 0) return cudaSuccess;
-    sub_conv0_kernel<<<dim3(rows1, (W1 + SUB_OW - 1) / SUB_OW), 256, 0, s>>>(mel, mel_off, h1_off, n_win, w, b, out,
-                                                                            W_in, C);
+cudaError_t sub_conv0_dw_launch(const float* mel, const int* mel_off, const int* h1_off, const int* h2_off, int n_win,
+                                const float* w0, const float* b0, const float* w2, const float* b2, float* out,
+                                int rows2, int W_in, int C, cudaStream_t s) {
+    if (rows2 <= 0) return cudaSuccess;
+    if (W_in != 128) return cudaErrorInvalidValue;   // the model's 128 mel bins
+    sub_conv0_dw_kernel<128><<<rows2, 256, 0, s>>>(mel, mel_off, h1_off, h2_off, n_win, w0, b0, w2, b2, out, C);
     return cudaGetLastError();
 }
 

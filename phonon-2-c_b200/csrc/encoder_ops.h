@@ -40,10 +40,12 @@ cudaError_t dwconv_swish_launch(const float* gated, const float* w, const float*
 // dst[r] = src[map[r]] for rows of `cols` floats.
 cudaError_t gather_rows_launch(float* dst, const float* src, const int* map, int rows, int cols, cudaStream_t s);
 
-// Subsampling, stage 1: Conv2d(1 -> C, 3x3, stride 2, pad 1) + ReLU over each window's [n_mel x 128] mel plane.
-// mel_off / h1_off: prefix offsets (mel rows, output rows) per window. Output [rows1][W1][C].
-cudaError_t sub_conv0_launch(const float* mel, const int* mel_off, const int* h1_off, int n_win, const float* w,
-                             const float* b, float* out, int rows1, int W_in, int C, cudaStream_t s);
+// Subsampling, Conv2d(1 -> C, 3x3, stride 2, pad 1) + ReLU and then depthwise Conv2d(C, 3x3, stride 2, pad 1) + bias
+// over each window, fused: mel [frames][W_in] -> [rows2][W2][C] (mel_off / h1_off / h2_off: the windows' row offsets
+// in the mel, after the first convolution and after the second). W_in is 128.
+cudaError_t sub_conv0_dw_launch(const float* mel, const int* mel_off, const int* h1_off, const int* h2_off, int n_win,
+                                const float* w0, const float* b0, const float* w2, const float* b2, float* out,
+                                int rows2, int W_in, int C, cudaStream_t s);
 
 // Subsampling, depthwise Conv2d(C, 3x3, stride 2, pad 1) + bias over each window: [rows_in][W_in][C] ->
 // [rows_out][W_out][C].
