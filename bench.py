@@ -1109,6 +1109,62 @@ def run_transcribe(args, local):
                       "api": "p2_b200_transcribe_windows (wall clock); split by CUDA events through the plans"}))
 
 
+def run_attention(args, local):
+    """--workload attention: the encoder's relative-position self-attention alone (p2cu_rel_attention, one launch of
+    attn_rel_tc_kernel) on the config-3 windows' encoder lengths (--windows N: the first N), synthetic N(0, 0.25)
+    Q | K | V rows and positions resident on the device, CUDA events around the timed calls. Reports the reference's
+    fp32 multiply-adds per call (AC, the full BD band of 2T - 1 positions, the context) and the tf32 products the
+    kernel executes (three per product, 64-key chunks and 64-position pieces, rows padded to the 128-query tile)."""
+    import ctypes as C
+    import torch
+    pkg = ge.load_package()
+    from phonon2_b200 import model as Mo
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    mel_frames = Mo.long_audio_windows(0)
+    if args.windows:
+        mel_frames = mel_frames[:args.windows]
+    Ts = [Mo.frames_after_subsampling(n) for n in mel_frames]
+    Tmax, R = max(Ts), sum(Ts)
+    g = torch.Generator(device=dev).manual_seed(5)
+    qkv = 0.5 * torch.randn(R, 3072, device=dev, generator=g)
+    P = 0.5 * torch.randn(2 * Tmax - 1, 1024, device=dev, generator=g)
+    bu = 0.1 * torch.randn(1024, device=dev, generator=g)
+    bv = 0.1 * torch.randn(1024, device=dev, generator=g)
+    out = torch.empty(R, 1024, device=dev)
+    L = pkg.lib()
+    Tarr = (C.c_int * len(Ts))(*Ts)
+    nws = L.p2cu_rel_attention_ws_bytes(len(Ts), Tarr)
+    ws = torch.empty(nws, dtype=torch.uint8, device=dev)
+
+    def call():
+        pkg.check(L.p2cu_rel_attention(qkv.data_ptr(), P.data_ptr(), bu.data_ptr(), bv.data_ptr(), Tarr, len(Ts), Tmax,
+                                       out.data_ptr(), ws.data_ptr(), nws, None))
+    steps = max(1, min(args.steps, 50))
+    for _ in range(args.warmup):
+        call()
+    torch.cuda.synchronize()
+    pkg.check_device()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        call()
+    e1.record()
+    e1.synchronize()
+    pkg.check_device()
+    ms = e0.elapsed_time(e1) / steps
+    fp32_macs = sum(8 * 128 * T * (T + (2 * T - 1) + T) for T in Ts)
+    tf32_macs = 0
+    for T in Ts:
+        nch = (T + 63) // 64
+        tf32_macs += ((T + 127) // 128) * 8 * 3 * (nch * (2 * 128 * 64 * 128 + 128 * 128 * 64) + 2 * 128 * 64 * 128)
+    print(json.dumps({"workload": "attention", "windows": len(Ts), "rows": R, "Tmax": Tmax,
+                      "ctas": 8 * sum((T + 127) // 128 for T in Ts), "steps": steps, "ms_per_call": round(ms, 4),
+                      "fp32_macs": fp32_macs, "tf32_macs_executed": tf32_macs,
+                      "tf32_tmacs_per_s": round(tf32_macs / ms / 1e9, 1),
+                      "api": "p2cu_rel_attention (include/p2cuda.h), device rows, CUDA events"}))
+
+
 def run_gemm_sweep(args):
     """--workload gemm-sweep: the five-value GEMM alone (quantised A resident) at growing M, K = 1024, N = 4096 (the
     north star's large-M shape) and K = 4096, N = 1024; planes and the code cache. One JSON line per case."""
@@ -1245,13 +1301,16 @@ def main():
     ap.add_argument("--no-encoder", action="store_true", help="skip the encoder (config 3) part of the line")
     ap.add_argument("--no-decoder", action="store_true",
                     help="skip the decoder (config 3 windows) and transcription (configs 2, 4) parts of the line")
-    ap.add_argument("--workload", choices=["block-gemms", "encoder", "gemm-sweep", "probes", "transcribe"],
+    ap.add_argument("--workload", choices=["block-gemms", "encoder", "gemm-sweep", "probes", "transcribe",
+                                           "attention"],
                     default="block-gemms",
                     help="block-gemms: configs[1] with the encoder object (default); encoder: the encoder alone; "
-                         "gemm-sweep: the GEMM alone at growing M (one line per case)")
+                         "gemm-sweep: the GEMM alone at growing M (one line per case); attention: the encoder's "
+                         "attention kernel alone on the config-3 windows")
     ap.add_argument("--encoder-config", choices=["long-audio", "window", "short"], default="long-audio",
                     help="--workload encoder: configs[3] (64 windows), [2] (one 30 s window) or [4] (3 s)")
-    ap.add_argument("--windows", type=int, default=0, help="--workload encoder long-audio: only the first N windows")
+    ap.add_argument("--windows", type=int, default=0,
+                    help="--workload encoder long-audio / attention: only the first N windows")
     ap.add_argument("--gemm-shape", default="", help="--workload gemm-sweep: only this M,K,N (with --weights)")
     ap.add_argument("--mel-frames", type=int, default=300, help="--workload transcribe: the window's mel frames")
     args = ap.parse_args()
@@ -1271,6 +1330,9 @@ def main():
         elif args.workload == "transcribe":
             if rank == 0:
                 run_transcribe(args, local)
+        elif args.workload == "attention":
+            if rank == 0:
+                run_attention(args, local)
         else:
             run_ours(args, world, rank, local)
     finally:
