@@ -73,16 +73,18 @@ def _pinned(a):
     return t, t.numpy()
 
 
-def test_page_locked_buffers(pkg, orc, synth, cuda):
-    """Page-locked A and C (as the bench's end-to-end leg passes them), ldc > N with the columns beyond N untouched."""
-    M, K, N = 520, 1024, 512
+@pytest.mark.parametrize("M,K,N,alpha,beta", [(520, 1024, 512, 1.0, 1.0), (375, 4096, 1024, 0.5, 1.0),
+                                              (375, 1024, 4096, 1.0, 0.0), (192, 1024, 256, 1.0, 0.0)])
+def test_page_locked_buffers(pkg, orc, synth, cuda, M, K, N, alpha, beta):
+    """Page-locked A and C (as the bench's end-to-end leg passes them), ldc > N with the columns beyond N untouched;
+    K > 1024 (the K-block workspace), alpha 1/2, beta 0 and 1."""
     w = synth.five_value(K, N, seed=11)
     A = synth.activations(M, K, seed=12)
     C_big = np.random.default_rng(13).standard_normal((M, N + 32)).astype(np.float32)
     ta, pa = _pinned(A)
     tc, pc = _pinned(C_big)
-    pkg.host_sgemm_fvb(pa, w, pc[:, :N], beta=1.0)
-    want = orc.sgemm_i8(A, "int8w", np.ascontiguousarray(C_big[:, :N]).copy(), w=w, beta=1.0)
+    pkg.host_sgemm_fvb(pa, w, pc[:, :N], alpha=alpha, beta=beta)
+    want = orc.sgemm_i8(A, "int8w", np.ascontiguousarray(C_big[:, :N]).copy(), w=w, alpha=alpha, beta=beta)
     assert _bits_equal(np.ascontiguousarray(pc[:, :N]), want)
     assert _bits_equal(pc[:, N:], C_big[:, N:])
 
