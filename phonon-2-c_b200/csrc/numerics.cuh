@@ -69,7 +69,7 @@ __device__ __forceinline__ float exp_poly(float x) {
 // SiLU as the reference's vector loop computes it (csrc/tensor_ops.c:450-458): v * (1 / (1 + exp(0 - v))).
 __device__ __forceinline__ float swish1(float v) {
     const float e = exp_poly(__fsub_rn(0.0f, v));
-    return __fmul_rn(v, __fdiv_rn(1.0f, __fadd_rn(1.0f, e)));
+    return __fmul_rn(v, __frcp_rn(__fadd_rn(1.0f, e)));
 }
 
 // Sum of the eight lanes of an 8-lane group in the order of the reference's AVX2 horizontal sum
