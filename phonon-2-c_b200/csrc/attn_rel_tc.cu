@@ -29,12 +29,17 @@
 //     more than 16, so that exp(s - m) stays below e^16. Softmax is invariant under the shift, so the result is the
 //     reference's up to rounding; the sum and the division by it close the row.
 //
+// A launch with few query tiles (a window or two) splits each tile's key chunks over up to four CTAs: each keeps its
+// own reference, sum and unnormalised context and writes them out; the last CTA of the tile to finish (an atomic count,
+// no waiting) merges them in split order, out = sum_s e^(m_s - M) O_s / sum_s e^(m_s - M) l_s with M = max_s m_s.
+//
 // Warps 0-3: softmax and read-out (TMEM lane = query row); warps 4-7: loader threads (lo parts, V transposed, bias
 // terms); warp 8: TMEM owner and MMA issue (converged, one elected lane issuing); warp 9: TMA issue (one lane). The
 // MMA order, one chunk of look-ahead:
 //     pieces 0, 1 | AC_0, piece 2, [scores 0] | AC_1, piece 3, [scores 1], context 0 | AC_2, piece 4, ... | context n-1
 // so the tensor pipe computes chunk c + 1's scores while the softmax threads work on chunk c. Every wait is bounded.
 #include <cstdint>
+#include <vector>
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include "encoder_ops.h"
@@ -115,8 +120,10 @@ __device__ __forceinline__ float dot4(float4 x, const float* b) {
 
 __global__ void __launch_bounds__(NTHREADS, 1)
 attn_rel_tc_kernel(const __grid_constant__ AttnMaps maps, const float* __restrict__ bias_u,
-                   const float* __restrict__ bias_v, const int* __restrict__ row_off, const int2* __restrict__ tiles,
-                   int Tmax, float scale, float* __restrict__ attn, uint32_t* err) {
+                   const float* __restrict__ bias_v, const int* __restrict__ row_off,
+                   const AttnTile* __restrict__ tiles, int Tmax, float scale, float* __restrict__ attn,
+                   float* __restrict__ part_o, float2* __restrict__ part_ml, int* __restrict__ counters,
+                   uint32_t* err) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* tfull = reinterpret_cast<uint64_t*>(smem + OFF_BAR);   // the stage's TMA bytes have landed
@@ -134,10 +141,11 @@ attn_rel_tc_kernel(const __grid_constant__ AttnMaps maps, const float* __restric
     float* cbuf = reinterpret_cast<float*>(smem + OFF_CB);
     float* dbuf = reinterpret_cast<float*>(smem + OFF_DB);
 
-    const int2 tile = tiles[blockIdx.x];
-    const int w = tile.x, q0 = tile.y, h = blockIdx.y;
+    const AttnTile tile = tiles[blockIdx.x];
+    const int w = tile.w, q0 = tile.q0, h = blockIdx.y;
     const int r0 = row_off[w], T = row_off[w + 1] - r0;
-    const int nch = (T + KC - 1) / KC;
+    // this CTA's key chunks c0 + u, u < nch (every chunk index below is relative to c0 but for the keys' places)
+    const int c0 = tile.c0, nch = tile.c1 - tile.c0;
     const int nstages = 8 + 12 * nch;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -169,7 +177,8 @@ attn_rel_tc_kernel(const __grid_constant__ AttnMaps maps, const float* __restric
     if (warp == 9) {
         // ---------------- TMA issue ----------------
         if (lane == 0) {
-            const int prow0 = Tmax - QT - q0;   // the row of P holding position 0 of piece 0 (may be < 0: zeros)
+            // the row of P holding position 0 of this CTA's piece 0 (may be < 0: zeros), and its first key's row
+            const int prow0 = Tmax - QT - q0 + KC * c0, krow0 = r0 + KC * c0;
             for (int st = 0; st < nstages; ++st) {
                 const int s = st % NST;
                 if (!mbar_wait(&empty[s], ((st / NST) & 1) ^ 1, DEV_TIMEOUT_EMPTY, err, abort_flag)) break;
@@ -178,7 +187,7 @@ attn_rel_tc_kernel(const __grid_constant__ AttnMaps maps, const float* __restric
                 uint8_t* B = smem + s * STAGE;
                 if (kind == ST_CTX) {
                     mbar_arrive_expect_tx(&tfull[s], CTX_TX);
-                    tma_load_2d(B + RAW_V, &maps.v, &tfull[s], 2 * DM + h * HD, r0 + KC * c + 16 * kk);
+                    tma_load_2d(B + RAW_V, &maps.v, &tfull[s], 2 * DM + h * HD, krow0 + KC * c + 16 * kk);
                 } else {
                     const int x = h * HD + 16 * kk;
                     mbar_arrive_expect_tx(&tfull[s], SCORE_TX);
@@ -187,7 +196,7 @@ attn_rel_tc_kernel(const __grid_constant__ AttnMaps maps, const float* __restric
                         tma_load_2d(B + RAW_B1, &maps.p, &tfull[s], x, prow0);
                         tma_load_2d(B + RAW_B2, &maps.p, &tfull[s], x, prow0 + KC);
                     } else {
-                        tma_load_2d(B + RAW_B1, &maps.k, &tfull[s], DM + x, r0 + KC * c);
+                        tma_load_2d(B + RAW_B1, &maps.k, &tfull[s], DM + x, krow0 + KC * c);
                         tma_load_2d(B + RAW_B2, &maps.p, &tfull[s], x, prow0 + KC * (c + 2));
                     }
                 }
@@ -354,7 +363,7 @@ attn_rel_tc_kernel(const __grid_constant__ AttnMaps maps, const float* __restric
                 const int o = 127 - r + jj;   // the band offset: piece c + o / 64, column o % 64
                 const float bd = __fadd_rn(shr[jj], dbuf[KC * ((c + (o >> 6)) & 3) + (o & 63)]);
                 const float ac = __fadd_rn(__uint_as_float(a[jj >> 5][jj & 31]), cb[jj]);
-                const float v = KC * c + jj < T ? __fmul_rn(__fadd_rn(ac, bd), scale) : -INFINITY;
+                const float v = KC * (c0 + c) + jj < T ? __fmul_rn(__fadd_rn(ac, bd), scale) : -INFINITY;
                 s[jj] = v;
                 mx = fmaxf(mx, v);
             }
@@ -408,34 +417,91 @@ attn_rel_tc_kernel(const __grid_constant__ AttnMaps maps, const float* __restric
             tc_fence_before();
             mbar_arrive(&pready[c & 1]);
         }
-        // ---------------- read-out: out = context / sum ----------------
+        // ---------------- read-out: out = context / sum, or this split's part and the merge ----------------
         if (ok && warp_wait(ofull, 0, DEV_TIMEOUT_ACC, err, abort_flag, true)) {
             tc_fence_after();
-            const float inv = __fdiv_rn(1.0f, l);
-            uint8_t* blk = smem + OFF_SH + warp * 32 * SROW * 4;   // this warp's band rows, free now
-            float* out0 = attn + static_cast<size_t>(r0 + q0) * DM + h * HD;
+            if (tile.nsplit == 1) {
+                const float inv = __fdiv_rn(1.0f, l);
+                uint8_t* blk = smem + OFF_SH + warp * 32 * SROW * 4;   // this warp's band rows, free now
+                float* out0 = attn + static_cast<size_t>(r0 + q0) * DM + h * HD;
 #pragma unroll 1
-            for (int q = 0; q < HD / 32; ++q) {
-                uint32_t v[32];
-                tmem_ld_32x32b_x32(lanes + COL_O + 32 * q, v);
-                tmem_wait_ld();
+                for (int q = 0; q < HD / 32; ++q) {
+                    uint32_t v[32];
+                    tmem_ld_32x32b_x32(lanes + COL_O + 32 * q, v);
+                    tmem_wait_ld();
 #pragma unroll
-                for (int c4 = 0; c4 < 8; ++c4)   // row `lane`, columns 4 c4 .. + 3, at 16-byte slot c4 ^ (lane % 8)
-                    *reinterpret_cast<float4*>(blk + lane * 128 + ((c4 ^ (lane & 7)) << 4)) =
-                        make_float4(__fmul_rn(__uint_as_float(v[4 * c4]), inv),
-                                    __fmul_rn(__uint_as_float(v[4 * c4 + 1]), inv),
-                                    __fmul_rn(__uint_as_float(v[4 * c4 + 2]), inv),
-                                    __fmul_rn(__uint_as_float(v[4 * c4 + 3]), inv));
-                __syncwarp();
-                const int c4 = lane & 7;
+                    for (int c4 = 0; c4 < 8; ++c4)   // row `lane`, columns 4 c4 .. + 3, at 16-byte slot c4 ^ (lane % 8)
+                        *reinterpret_cast<float4*>(blk + lane * 128 + ((c4 ^ (lane & 7)) << 4)) =
+                            make_float4(__fmul_rn(__uint_as_float(v[4 * c4]), inv),
+                                        __fmul_rn(__uint_as_float(v[4 * c4 + 1]), inv),
+                                        __fmul_rn(__uint_as_float(v[4 * c4 + 2]), inv),
+                                        __fmul_rn(__uint_as_float(v[4 * c4 + 3]), inv));
+                    __syncwarp();
+                    const int c4 = lane & 7;
 #pragma unroll
-                for (int it = 0; it < 8; ++it) {   // rows 4 it .. 4 it + 3, eight lanes (128 bytes) per row
-                    const int rr = 4 * it + (lane >> 3), row = warp * 32 + rr;
-                    const float4 y = *reinterpret_cast<const float4*>(blk + rr * 128 + ((c4 ^ (rr & 7)) << 4));
-                    if (q0 + row < T)
-                        *reinterpret_cast<float4*>(out0 + static_cast<size_t>(row) * DM + 32 * q + 4 * c4) = y;
+                    for (int it = 0; it < 8; ++it) {   // rows 4 it .. 4 it + 3, eight lanes (128 bytes) per row
+                        const int rr = 4 * it + (lane >> 3), row = warp * 32 + rr;
+                        const float4 y = *reinterpret_cast<const float4*>(blk + rr * 128 + ((c4 ^ (rr & 7)) << 4));
+                        if (q0 + row < T)
+                            *reinterpret_cast<float4*>(out0 + static_cast<size_t>(row) * DM + 32 * q + 4 * c4) = y;
+                    }
+                    __syncwarp();
                 }
-                __syncwarp();
+            } else {
+                // this split's row: reference, sum and unnormalised context
+                const size_t part = (static_cast<size_t>(blockIdx.x) * NHEAD + h) * QT + r;
+                float4* po = reinterpret_cast<float4*>(part_o + part * HD);
+#pragma unroll 1
+                for (int q = 0; q < HD / 32; ++q) {
+                    uint32_t v[32];
+                    tmem_ld_32x32b_x32(lanes + COL_O + 32 * q, v);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int c4 = 0; c4 < 8; ++c4)
+                        po[8 * q + c4] = make_float4(__uint_as_float(v[4 * c4]), __uint_as_float(v[4 * c4 + 1]),
+                                                     __uint_as_float(v[4 * c4 + 2]), __uint_as_float(v[4 * c4 + 3]));
+                }
+                part_ml[part] = make_float2(m, l);
+                __threadfence();
+                named_barrier_sync(2, 128);   // the four softmax warps' parts are out
+                int* last_s = reinterpret_cast<int*>(tmem_holder + 2);
+                if (r == 0) {
+                    int* cnt = counters + static_cast<size_t>(tile.group) * NHEAD + h;
+                    const int prev = atomicAdd(cnt, 1);
+                    *last_s = prev == tile.nsplit - 1;
+                    if (*last_s) *cnt = 0;   // ready for the next launch (the launches of a stream run in order)
+                }
+                named_barrier_sync(2, 128);
+                if (*last_s) {
+                    __threadfence();
+                    // every split's row r, in split order (the same result whichever CTA merges)
+                    const size_t stride = static_cast<size_t>(NHEAD) * QT;   // one tile's rows in the parts
+                    const size_t base = (static_cast<size_t>(tile.first) * NHEAD + h) * QT + r;
+                    float mm = -INFINITY;
+                    for (int sp = 0; sp < tile.nsplit; ++sp) mm = fmaxf(mm, __ldcg(&part_ml[base + sp * stride]).x);
+                    float ll = 0.f;
+                    for (int sp = 0; sp < tile.nsplit; ++sp) {
+                        const float2 ml = __ldcg(&part_ml[base + sp * stride]);
+                        ll = __fmaf_rn(exp_poly(__fsub_rn(ml.x, mm)), ml.y, ll);
+                    }
+                    const float inv = __fdiv_rn(1.0f, ll);
+                    float* orow = attn + static_cast<size_t>(r0 + q0 + r) * DM + h * HD;
+#pragma unroll 1
+                    for (int c4 = 0; c4 < HD / 4; ++c4) {
+                        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+                        for (int sp = 0; sp < tile.nsplit; ++sp) {
+                            const float a = exp_poly(__fsub_rn(__ldcg(&part_ml[base + sp * stride]).x, mm));
+                            const float4 o = __ldcg(reinterpret_cast<const float4*>(part_o + (base + sp * stride) *
+                                                                                    HD) + c4);
+                            acc = make_float4(__fmaf_rn(a, o.x, acc.x), __fmaf_rn(a, o.y, acc.y),
+                                              __fmaf_rn(a, o.z, acc.z), __fmaf_rn(a, o.w, acc.w));
+                        }
+                        if (q0 + r < T)
+                            *reinterpret_cast<float4*>(orow + 4 * c4) =
+                                make_float4(__fmul_rn(acc.x, inv), __fmul_rn(acc.y, inv), __fmul_rn(acc.z, inv),
+                                            __fmul_rn(acc.w, inv));
+                    }
+                }
             }
         }
     }
@@ -449,9 +515,36 @@ attn_rel_tc_kernel(const __grid_constant__ AttnMaps maps, const float* __restric
 
 }  // namespace
 
+int attn_rel_tc_plan(const int* T, int n_win, int sms, std::vector<AttnTile>& tiles, int* n_groups) {
+    int base = 0;
+    for (int w = 0; w < n_win; ++w) base += (T[w] + QT - 1) / QT;
+    // split the key chunks when the tiles alone give fewer than half the SMs a CTA
+    int want = base * NHEAD * 2 <= sms ? sms / (base * NHEAD) : 1;
+    if (want > 4) want = 4;
+    tiles.clear();
+    int g = 0;
+    for (int w = 0; w < n_win; ++w)
+        for (int q0 = 0; q0 < T[w]; q0 += QT, ++g) {
+            const int nch = (T[w] + KC - 1) / KC;
+            const int ns = want < nch ? want : nch;
+            const int first = static_cast<int>(tiles.size());
+            for (int sp = 0; sp < ns; ++sp) {
+                AttnTile t;
+                t.w = w; t.q0 = q0;
+                t.c0 = sp * nch / ns; t.c1 = (sp + 1) * nch / ns;
+                t.split = sp; t.nsplit = ns; t.group = g; t.first = first;
+                tiles.push_back(t);
+            }
+        }
+    *n_groups = g;
+    return static_cast<int>(tiles.size());
+}
+
+size_t attn_rel_tc_part_bytes(int n_tiles) { return static_cast<size_t>(n_tiles) * NHEAD * QT * (HD * 4 + 8); }
+
 int attn_rel_tc_launch(const float* qkv, int rows, const float* P, const float* bias_u, const float* bias_v,
-                       const int* row_off, const int2* tiles, int n_tiles, int Tmax, float scale, float* attn,
-                       uint32_t* err, cudaStream_t s) {
+                       const int* row_off, const AttnTile* tiles, int n_tiles, int Tmax, float scale, float* attn,
+                       void* parts, int* counters, uint32_t* err, cudaStream_t s) {
     if (n_tiles <= 0) return P2CU_OK;
     if (Tmax > ATT_MAXT || Tmax <= 0 || rows <= 0)
         return fail_fmt(P2CU_EINVAL, "attention: Tmax = %d, rows = %d", Tmax, rows);
@@ -465,8 +558,11 @@ int attn_rel_tc_launch(const float* qkv, int rows, const float* P, const float* 
     if (int rc = make_tile_map(&maps.p, P, 4, DM, 2 * Tmax - 1, pstride, 16, KC, 64, "attention P")) return rc;
     cudaError_t e = cudaFuncSetAttribute(attn_rel_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
     if (e != cudaSuccess) return cuda_error(e, "attention");
+    float* part_o = static_cast<float*>(parts);
+    float2* part_ml = parts ? reinterpret_cast<float2*>(part_o + static_cast<size_t>(n_tiles) * NHEAD * QT * HD)
+                            : nullptr;
     attn_rel_tc_kernel<<<dim3(n_tiles, NHEAD), NTHREADS, SMEM_BYTES, s>>>(maps, bias_u, bias_v, row_off, tiles, Tmax,
-                                                                         scale, attn, err);
+                                                                         scale, attn, part_o, part_ml, counters, err);
     e = cudaGetLastError();
     return e == cudaSuccess ? P2CU_OK : cuda_error(e, "attention");
 }

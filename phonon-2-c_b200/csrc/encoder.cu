@@ -237,8 +237,12 @@ struct P2cuEncoder {
     long long *d_s_off, *d_b_off, *d_vt_off;
     p2cu::GemmGroup *g_ac, *g_bd, *g_av;
     int ng = 0, t_ac = 0, t_bd = 0, t_av = 0;
-    int2* att_tiles = nullptr;   // fused attention (every window <= ATT_MAXT frames): (window, first query) per tile
+    int2* att_tiles = nullptr;   // fused SIMT attention (windows <= ATT_MAXT frames): (window, first query) per tile
     int n_att_tiles = 0;
+    p2cu::AttnTile* tc_tiles = nullptr;   // fused tensor-core attention: the launch's tiles (attn_rel_tc_plan)
+    int n_tc_tiles = 0;
+    void* att_parts = nullptr;            // its split parts and merge counters, when a tile's keys are split
+    int* att_counters = nullptr;
     // Attention path: 3 = one tensor-core kernel per layer, scores in TMEM (windows of at most ATT_MAXT frames; the
     // default), 0 = tensor-core products as grouped split-tf32 GEMMs with the scores in HBM (the default for longer
     // windows), 1 = SIMT grouped GEMMs, 2 = SIMT fused kernel (short windows). P2CU_ATTN=tc_fused|tc|simt|fused.
@@ -380,8 +384,9 @@ int self_attention(P2cuEncoder& e, const DBlock& b, cudaStream_t s) {
         c.err = a.err;
         TRYC(p2cu::attn_tc_launch(e.tc_context, e.n_tc, e.t_tc_context, c, false, s), "attention context");
     } else if (e.attn_path == 3) {
-        TRY(p2cu::attn_rel_tc_launch(e.big, e.R, e.P, b.bias_u, b.bias_v, e.d_row_off, e.att_tiles, e.n_att_tiles,
-                                     e.Tmax, e.scale, e.attn, p2cu::device_error_word(), s));
+        TRY(p2cu::attn_rel_tc_launch(e.big, e.R, e.P, b.bias_u, b.bias_v, e.d_row_off, e.tc_tiles, e.n_tc_tiles,
+                                     e.Tmax, e.scale, e.attn, e.att_parts, e.att_counters, p2cu::device_error_word(),
+                                     s));
     } else if (e.n_att_tiles) {
         TRYC(p2cu::attn_fused_launch(e.big, e.P, b.bias_u, b.bias_v, e.d_row_off, e.att_tiles, e.n_att_tiles, e.Tmax,
                                      e.scale, e.attn, s),
@@ -635,11 +640,22 @@ int create_plan(const P2cuModel* m, const int* n_frames, int n_mel_win, int mode
     }
     const bool fused = (e->attn_path == 2 || e->attn_path == 3) && e->Tmax <= p2cu::ATT_MAXT;
     std::vector<int2> att_tiles;
-    if (fused) {   // (window, first query) of every query tile: 32 queries (SIMT) or 128 (tensor cores)
-        const int step = e->attn_path == 3 ? p2cu::ATT_TC_QT : 32;
-        for (int w = 0; w < n_win; ++w)
-            for (int q0 = 0; q0 < e->T[w]; q0 += step) att_tiles.push_back(make_int2(w, q0));
-        e->n_att_tiles = static_cast<int>(att_tiles.size());
+    std::vector<p2cu::AttnTile> tc_tiles;
+    int tc_groups = 0;
+    bool tc_split = false;
+    if (fused) {
+        if (e->attn_path == 3) {   // 128-query tiles, the keys split over CTAs when there are few tiles
+            int dev = 0, sms = 148;
+            if (cudaGetDevice(&dev) != cudaSuccess ||
+                cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+                sms = 148;
+            e->n_tc_tiles = p2cu::attn_rel_tc_plan(e->T.data(), n_win, sms, tc_tiles, &tc_groups);
+            for (const p2cu::AttnTile& t : tc_tiles) tc_split = tc_split || t.nsplit > 1;
+        } else {                   // (window, first query) of every 32-query tile
+            for (int w = 0; w < n_win; ++w)
+                for (int q0 = 0; q0 < e->T[w]; q0 += 32) att_tiles.push_back(make_int2(w, q0));
+            e->n_att_tiles = static_cast<int>(att_tiles.size());
+        }
         e->s_total = e->b_total = 0;   // no score matrices in HBM
     }
     e->ng = static_cast<int>(gac.size());
@@ -694,6 +710,9 @@ int create_plan(const P2cuModel* m, const int* n_frames, int n_mel_win, int mode
         {reinterpret_cast<void**>(&e->g_bd), gbd.size() * sizeof(p2cu::GemmGroup)},
         {reinterpret_cast<void**>(&e->g_av), gav.size() * sizeof(p2cu::GemmGroup)},
         {reinterpret_cast<void**>(&e->att_tiles), att_tiles.size() * sizeof(int2)},
+        {reinterpret_cast<void**>(&e->tc_tiles), tc_tiles.size() * sizeof(p2cu::AttnTile)},
+        {&e->att_parts, tc_split ? p2cu::attn_rel_tc_part_bytes(e->n_tc_tiles) : 0},
+        {reinterpret_cast<void**>(&e->att_counters), tc_split ? static_cast<size_t>(tc_groups) * 8 * sizeof(int) : 0},
         {reinterpret_cast<void**>(&e->tc_scores), tcs.size() * sizeof(p2cu::TcGroup)},
         {reinterpret_cast<void**>(&e->tc_context), tcc.size() * sizeof(p2cu::TcGroup)},
     };
@@ -733,6 +752,7 @@ int create_plan(const P2cuModel* m, const int* n_frames, int n_mel_win, int mode
         {e->g_bd, gbd.data(), gbd.size() * sizeof(p2cu::GemmGroup)},
         {e->g_av, gav.data(), gav.size() * sizeof(p2cu::GemmGroup)},
         {e->att_tiles, att_tiles.data(), att_tiles.size() * sizeof(int2)},
+        {e->tc_tiles, tc_tiles.data(), tc_tiles.size() * sizeof(p2cu::AttnTile)},
         {e->tc_scores, tcs.data(), tcs.size() * sizeof(p2cu::TcGroup)},
         {e->tc_context, tcc.data(), tcc.size() * sizeof(p2cu::TcGroup)},
     };
@@ -741,6 +761,9 @@ int create_plan(const P2cuModel* m, const int* n_frames, int n_mel_win, int mode
     if (ce == cudaSuccess) ce = cudaMemset(e->mel, 0, static_cast<size_t>(e->mel_rows) * NMEL * f);
     if (ce == cudaSuccess && e->attn_path == 0)   // V^T's padding columns stay zero
         ce = cudaMemset(e->vt, 0, static_cast<size_t>(e->vt_total) * f);
+    if (ce == cudaSuccess && tc_split)   // the split attention's merge counters start at zero
+        ce = cudaMemset(e->att_counters, 0, static_cast<size_t>(tc_groups) * 8 * sizeof(int));
+    if (!tc_split) e->att_parts = nullptr, e->att_counters = nullptr;
     if (ce == cudaSuccess) ce = cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking);
     if (ce == cudaSuccess && mode != P2CU_EXACT)
         ce = p2cu::quant_rows_launch(e->pe, L, D, D, e->pe_q, e->pe_s, e->stream);

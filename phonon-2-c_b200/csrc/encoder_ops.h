@@ -4,6 +4,7 @@
 // of row offsets in device memory.
 #pragma once
 #include <cstdint>
+#include <vector>
 #include <cuda_runtime.h>
 
 namespace p2cu {
@@ -100,8 +101,20 @@ cudaError_t attn_fused_launch(const float* qkv, const float* P, const float* bia
 // these); tiles: (window, first query) of every ATT_TC_QT-query tile; err: the device error word of the bounded
 // waits. Returns a P2CU code.
 constexpr int ATT_TC_QT = 128;
+// One CTA's share of a launch (per head): window w, queries q0 .. q0 + 127, key chunks [c0, c1) of 64 keys; split
+// `split` of `nsplit` of query tile `group`, whose splits are tiles first .. first + nsplit - 1.
+struct AttnTile {
+    int w, q0, c0, c1, split, nsplit, group, first;
+};
+// The tiles of a launch over windows of T[0 .. n_win) frames on a GPU of `sms` SMs: the key chunks split over up to
+// four CTAs when the query tiles give fewer than half the SMs a CTA. Returns the tile count; *n_groups the query tiles.
+int attn_rel_tc_plan(const int* T, int n_win, int sms, std::vector<AttnTile>& tiles, int* n_groups);
+// Device bytes of the split parts of a launch of n_tiles tiles (used only when some tile has nsplit > 1), and the
+// launch: parts and counters (n_groups x 8 ints, zero before the first launch; the merging CTA zeroes its own) may be
+// null when no tile splits.
+size_t attn_rel_tc_part_bytes(int n_tiles);
 int attn_rel_tc_launch(const float* qkv, int rows, const float* P, const float* bias_u, const float* bias_v,
-                       const int* row_off, const int2* tiles, int n_tiles, int Tmax, float scale, float* attn,
-                       uint32_t* err, cudaStream_t s);
+                       const int* row_off, const AttnTile* tiles, int n_tiles, int Tmax, float scale, float* attn,
+                       void* parts, int* counters, uint32_t* err, cudaStream_t s);
 
 }  // namespace p2cu

@@ -1,6 +1,7 @@
 // ops_api.cu - the encoder's row ops on device rows (include/p2cuda.h), each one launch of an encoder_ops kernel.
 #include <cmath>
 #include <cstdint>
+#include <cstring>
 #include <vector>
 #include <cuda_runtime.h>
 #include "p2cuda.h"
@@ -93,17 +94,34 @@ int p2cu_sgemm_tf32x3(int transB, int M, int N, int K, const float* A, int lda, 
 
 namespace {
 
-// The scratch of p2cu_rel_attention: the windows' row offsets, then the (window, first query) of every query tile.
+// The scratch of p2cu_rel_attention: the windows' row offsets, the launch's tiles, then (when its keys are split) the
+// merge counters and the split parts.
 struct RelAttnLayout {
-    size_t tiles_off = 0, bytes = 0;
-    int n_tiles = 0;
+    std::vector<p2cu::AttnTile> tiles;
+    int n_groups = 0;
+    bool split = false;
+    size_t tiles_off = 0, counters_off = 0, parts_off = 0, bytes = 0;
 };
+
+int sm_count() {
+    int dev = 0, sms = 148;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) !=
+                                                  cudaSuccess) {
+        (void)cudaGetLastError();
+        return 148;
+    }
+    return sms;
+}
 
 RelAttnLayout rel_attention_layout(int n_win, const int* T) {
     RelAttnLayout l;
-    for (int w = 0; w < n_win; ++w) l.n_tiles += (T[w] + p2cu::ATT_TC_QT - 1) / p2cu::ATT_TC_QT;
-    l.tiles_off = (static_cast<size_t>(n_win + 1) * sizeof(int) + 15) & ~size_t(15);
-    l.bytes = l.tiles_off + static_cast<size_t>(l.n_tiles) * sizeof(int2);
+    const int n = p2cu::attn_rel_tc_plan(T, n_win, sm_count(), l.tiles, &l.n_groups);
+    for (const p2cu::AttnTile& t : l.tiles) l.split = l.split || t.nsplit > 1;
+    auto up = [](size_t x) { return (x + 255) & ~size_t(255); };
+    l.tiles_off = up(static_cast<size_t>(n_win + 1) * sizeof(int));
+    l.counters_off = up(l.tiles_off + static_cast<size_t>(n) * sizeof(p2cu::AttnTile));
+    l.parts_off = up(l.counters_off + (l.split ? static_cast<size_t>(l.n_groups) * 8 * sizeof(int) : 0));
+    l.bytes = l.parts_off + (l.split ? p2cu::attn_rel_tc_part_bytes(n) : 0);
     return l;
 }
 
@@ -121,33 +139,37 @@ int p2cu_rel_attention(const float* qkv, const float* P, const float* bias_u, co
     const char* who = "p2cu_rel_attention";
     if (n_win < 0) return p2cu::fail_fmt(P2CU_EINVAL, "%s: n_win = %d", who, n_win);
     if (n_win == 0) return P2CU_OK;
-    if (!qkv || !P || !bias_u || !bias_v || !T || !attn || !ws) return p2cu::fail_fmt(P2CU_EINVAL, "%s: NULL pointer", who);
+    if (!qkv || !P || !bias_u || !bias_v || !T || !attn || !ws)
+        return p2cu::fail_fmt(P2CU_EINVAL, "%s: NULL pointer", who);
     if (Tmax <= 0 || Tmax > p2cu::ATT_MAXT)
         return p2cu::fail_fmt(P2CU_EUNSUPPORTED, "%s: Tmax = %d (1 .. %d)", who, Tmax, p2cu::ATT_MAXT);
     for (int w = 0; w < n_win; ++w)
-        if (T[w] <= 0 || T[w] > Tmax) return p2cu::fail_fmt(P2CU_EINVAL, "%s: T[%d] = %d, Tmax = %d", who, w, T[w], Tmax);
+        if (T[w] <= 0 || T[w] > Tmax)
+            return p2cu::fail_fmt(P2CU_EINVAL, "%s: T[%d] = %d, Tmax = %d", who, w, T[w], Tmax);
     if ((reinterpret_cast<uintptr_t>(qkv) | reinterpret_cast<uintptr_t>(P) | reinterpret_cast<uintptr_t>(bias_u) |
-         reinterpret_cast<uintptr_t>(bias_v) | reinterpret_cast<uintptr_t>(attn) | reinterpret_cast<uintptr_t>(ws)) & 15)
+         reinterpret_cast<uintptr_t>(bias_v) | reinterpret_cast<uintptr_t>(attn) |
+         reinterpret_cast<uintptr_t>(ws)) & 15)
         return p2cu::fail_fmt(P2CU_EINVAL, "%s: pointers must be 16-byte aligned", who);
     const RelAttnLayout l = rel_attention_layout(n_win, T);
     if (ws_bytes < l.bytes) return p2cu::fail_fmt(P2CU_EINVAL, "%s: ws_bytes %zu < %zu", who, ws_bytes, l.bytes);
-    std::vector<uint8_t> host(l.bytes, 0);
+    std::vector<uint8_t> host(l.counters_off, 0);
     int* off = reinterpret_cast<int*>(host.data());
-    int2* tiles = reinterpret_cast<int2*>(host.data() + l.tiles_off);
     off[0] = 0;
-    int k = 0;
-    for (int w = 0; w < n_win; ++w) {
-        off[w + 1] = off[w] + T[w];
-        for (int q0 = 0; q0 < T[w]; q0 += p2cu::ATT_TC_QT) tiles[k++] = make_int2(w, q0);
-    }
+    for (int w = 0; w < n_win; ++w) off[w + 1] = off[w] + T[w];
+    std::memcpy(host.data() + l.tiles_off, l.tiles.data(), l.tiles.size() * sizeof(p2cu::AttnTile));
     const cudaStream_t s = static_cast<cudaStream_t>(stream);
     // from pageable memory: the call returns once the bytes are staged, so `host` may go out of scope
-    cudaError_t e = cudaMemcpyAsync(ws, host.data(), l.bytes, cudaMemcpyHostToDevice, s);
-    if (e != cudaSuccess) return p2cu::cuda_error(e, who);
+    cudaError_t e = cudaMemcpyAsync(ws, host.data(), host.size(), cudaMemcpyHostToDevice, s);
     uint8_t* wsb = static_cast<uint8_t*>(ws);
+    if (e == cudaSuccess && l.split)
+        e = cudaMemsetAsync(wsb + l.counters_off, 0, static_cast<size_t>(l.n_groups) * 8 * sizeof(int), s);
+    if (e != cudaSuccess) return p2cu::cuda_error(e, who);
     return p2cu::attn_rel_tc_launch(qkv, off[n_win], P, bias_u, bias_v, reinterpret_cast<const int*>(wsb),
-                                    reinterpret_cast<const int2*>(wsb + l.tiles_off), l.n_tiles, Tmax,
-                                    1.0f / sqrtf(128.0f), attn, p2cu::device_error_word(), s);
+                                    reinterpret_cast<const p2cu::AttnTile*>(wsb + l.tiles_off),
+                                    static_cast<int>(l.tiles.size()), Tmax, 1.0f / sqrtf(128.0f), attn,
+                                    l.split ? wsb + l.parts_off : nullptr,
+                                    l.split ? reinterpret_cast<int*>(wsb + l.counters_off) : nullptr,
+                                    p2cu::device_error_word(), s);
 }
 
 }  // extern "C"
