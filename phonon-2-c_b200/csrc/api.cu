@@ -175,8 +175,25 @@ size_t split_bytes(int M, int N, int K) {
 // Returns RUN_T_DECLINED for shapes it does not take, so the caller picks another kernel.
 constexpr int RUN_T_DECLINED = 1;
 
+// K > 1024: fold the per-block slices into C now, or (with `defer`, beta 1 and a dense C) describe them in *defer for
+// the caller's next kernel to fold.
+cudaError_t fold_or_defer(const void* ws, int m_pad, int nblk, const float* a_scales, float alpha, int beta_zero,
+                          float* C, int M, int N, int ldc, cudaStream_t s, p2cu::KFold* defer) {
+    if (defer && !beta_zero && ldc == N) {
+        defer->f = static_cast<const float*>(ws);
+        defer->m_pad = m_pad;
+        defer->nblk = nblk;
+        defer->a_scales = a_scales;
+        defer->alpha = alpha;
+        return cudaSuccess;
+    }
+    return p2cu::fv_combine_launch(static_cast<const float*>(ws), m_pad, nblk, a_scales, alpha, beta_zero, C, M, N,
+                                   ldc, s);
+}
+
 int run_t(int M, int N, int K, float alpha, const int8_t* q, const float* a_scales, const P2cuFiveValue* B,
-          float beta, float* C, int ldc, void* ws, size_t ws_bytes, cudaStream_t s, const char* who) {
+          float beta, float* C, int ldc, void* ws, size_t ws_bytes, cudaStream_t s, const char* who,
+          p2cu::KFold* defer) {
     static const int t_env = env_switch("P2CU_TGEMM");
     if (t_env == 0 || N % 128 || K % 16 || M > (t_env == 1 ? 4096 : 1024)) return RUN_T_DECLINED;
     if (!B->lo || !B->hi) return fail(P2CU_EINVAL, "%s: lo / hi are NULL", who);
@@ -207,8 +224,7 @@ int run_t(int M, int N, int K, float alpha, const int8_t* q, const float* a_scal
     if ((rc = make_map(&ta, q, 1, K, M, K, 128, mt, 128, "A"))) return rc;
     cudaError_t e = p2cu::fv_gemm_t_launch(mt, ta, p, s);
     if (e == cudaSuccess && nblk > 1)
-        e = p2cu::fv_combine_launch(static_cast<const float*>(ws), p.m_pad, nblk, a_scales, alpha, p.beta_zero, C, M,
-                                    N, ldc, s);
+        e = fold_or_defer(ws, p.m_pad, nblk, a_scales, alpha, p.beta_zero, C, M, N, ldc, s, defer);
     return e == cudaSuccess ? P2CU_OK : cuda_fail(e, who);
 }
 
@@ -216,7 +232,8 @@ int run_t(int M, int N, int K, float alpha, const int8_t* q, const float* a_scal
 // `ws` holds the per-block slices when K > 1024 (split_bytes).
 int run_i8(int M, int N, int K, float alpha, const int8_t* q, const float* a_scales, const P2cuFiveValue* B,
            const int8_t* q8, const float* scales, int ldb, int mode, float beta, float* C, int ldc, void* ws,
-           size_t ws_bytes, cudaStream_t s, const char* who) {
+           size_t ws_bytes, cudaStream_t s, const char* who, p2cu::KFold* defer = nullptr) {
+    if (defer) defer->nblk = 0;
     int rc = check_gemm_common(M, N, K, C, ldc, who);
     if (rc) return rc;
     if (N % 16) return fail(P2CU_EINVAL, "%s: N = %d is not a multiple of 16", who, N);
@@ -224,7 +241,7 @@ int run_i8(int M, int N, int K, float alpha, const int8_t* q, const float* a_sca
     if (alpha == 0.f || K == 0) return scale_c(C, M, N, ldc, beta, s);   // no products: C = beta * C
     if (!q || !a_scales) return fail(P2CU_EINVAL, "%s: quantised A is NULL", who);
     if (B && mode == P2CU_INT8W && B->vindex) {
-        rc = run_t(M, N, K, alpha, q, a_scales, B, beta, C, ldc, ws, ws_bytes, s, who);
+        rc = run_t(M, N, K, alpha, q, a_scales, B, beta, C, ldc, ws, ws_bytes, s, who, defer);
         if (rc != RUN_T_DECLINED) return rc;
     }
     if (N % 128 || K % 16 || !aligned16(C) || ldc % 4) {
@@ -334,8 +351,7 @@ int run_i8(int M, int N, int K, float alpha, const int8_t* q, const float* a_sca
                     : persist ? p2cu::fv_gemm_p_launch(bn, kind, ta, tb0, tb1, tout, p, s)
                               : p2cu::fv_gemm_launch(bn, kind, ta, tb0, tb1, tout, p, s);
     if (e == cudaSuccess && nblk > 1)
-        e = p2cu::fv_combine_launch(static_cast<const float*>(ws), p.m_pad, nblk, a_scales, alpha, p.beta_zero, C, M,
-                                    N, ldc, s);
+        e = fold_or_defer(ws, p.m_pad, nblk, a_scales, alpha, p.beta_zero, C, M, N, ldc, s, defer);
     return e == cudaSuccess ? P2CU_OK : cuda_fail(e, who);
 }
 
@@ -404,8 +420,8 @@ int make_tile_map(CUtensorMap* map, const void* base, int esize, uint64_t inner,
 
 int gemm_i8(int M, int N, int K, float alpha, const int8_t* q, const float* a_scales, const P2cuFiveValue* B,
             const int8_t* q8, const float* scales, int ldb, int mode, float beta, float* C, int ldc, void* ws,
-            size_t ws_bytes, cudaStream_t s, const char* who) {
-    return run_i8(M, N, K, alpha, q, a_scales, B, q8, scales, ldb, mode, beta, C, ldc, ws, ws_bytes, s, who);
+            size_t ws_bytes, cudaStream_t s, const char* who, KFold* defer) {
+    return run_i8(M, N, K, alpha, q, a_scales, B, q8, scales, ldb, mode, beta, C, ldc, ws, ws_bytes, s, who, defer);
 }
 
 int gemm_exact(int M, int N, int K, float alpha, const float* A, int lda, int transA, const P2cuFiveValue* B,

@@ -247,6 +247,9 @@ struct P2cuEncoder {
     // default), 0 = tensor-core products as grouped split-tf32 GEMMs with the scores in HBM (the default for longer
     // windows), 1 = SIMT grouped GEMMs, 2 = SIMT fused kernel (short windows). P2CU_ATTN=tc_fused|tc|simt|fused.
     int attn_path = 0;
+    // The K blocks of the last int8 GEMM into x still to be folded (its workspace slices): the LayerNorm that reads
+    // x next folds them in the same launch. No GEMM runs while one is pending (it would reuse the workspace).
+    p2cu::KFold pending;
     p2cu::TcGroup *tc_scores = nullptr, *tc_context = nullptr;
     int n_tc = 0, t_tc_scores = 0, t_tc_context = 0;
 
@@ -278,11 +281,21 @@ int wmatmul(P2cuEncoder& e, const float* A, int M, const DWeight& W, float* C, f
 }
 
 // p2_wmatmul_q8a (csrc/tensor_ops.c:48-63) on rows already quantised into e.q / e.qs.
+// defer: leave the K-block fold of a K > 1024 product into C (beta 1) to the next LayerNorm (e.pending).
 int wmatmul_q8a(P2cuEncoder& e, int M, const DWeight& W, float* C, float alpha, float beta, cudaStream_t s,
-                const char* who) {
+                const char* who, bool defer = false) {
     if (W.kind == P2_W_F32) return fail_fmt(P2CU_EINVAL, "%s: fp32 weight has no int8 path", who);
+    if (e.pending.nblk) return fail_fmt(P2CU_EINVAL, "%s: a K-block fold is still pending", who);
     return p2cu::gemm_i8(M, W.N, W.K, alpha, e.q, e.qs, W.kind == P2_W_FV ? &W.fv : nullptr, W.q8, W.scales, W.N,
-                         W.kind == P2_W_FV ? e.mode : P2CU_INT8, beta, C, W.N, e.ws, e.ws_bytes, s, who);
+                         W.kind == P2_W_FV ? e.mode : P2CU_INT8, beta, C, W.N, e.ws, e.ws_bytes, s, who,
+                         defer ? &e.pending : nullptr);
+}
+
+// The pending fold for the LayerNorm about to read x, and no fold pending after it.
+const p2cu::KFold* take_fold(P2cuEncoder& e, p2cu::KFold& hold) {
+    hold = e.pending;
+    e.pending.nblk = 0;
+    return &hold;
 }
 
 #define TRY(x) do { int rc_ = (x); if (rc_ != P2CU_OK) return rc_; } while (0)
@@ -329,14 +342,18 @@ int subsampling(P2cuEncoder& e, cudaStream_t s) {
 int feed_forward(P2cuEncoder& e, const float* nw, const float* nb, const DWeight& w1, const DWeight& w2,
                  cudaStream_t s, const float* prev_w = nullptr, const float* prev_b = nullptr) {
     if (e.mode != P2CU_EXACT) {
+        p2cu::KFold hold;
         if (prev_w)
-            TRYC(p2cu::ln2_rows_launch(e.x, D, prev_w, prev_b, nw, nb, nullptr, 0, e.q, e.qs, e.R, D, s),
+            TRYC(p2cu::ln2_rows_launch(e.x, D, prev_w, prev_b, nw, nb, nullptr, 0, e.q, e.qs, e.R, D, s,
+                                       take_fold(e, hold)),
                  "norm_out + ff layernorm");
         else
-            TRYC(p2cu::ln_rows_launch(e.x, D, nw, nb, nullptr, 0, e.q, e.qs, e.R, D, s), "ff layernorm");
+            TRYC(p2cu::ln_rows_launch(e.x, D, nw, nb, nullptr, 0, e.q, e.qs, e.R, D, s, take_fold(e, hold)),
+                 "ff layernorm");
         TRY(wmatmul_q8a(e, e.R, w1, e.big, 1.f, 0.f, s, "ff linear1"));
         TRYC(p2cu::swish_rows_launch(e.big, FF, nullptr, 0, e.q, e.qs, e.R, FF, s), "ff swish");
-        return wmatmul_q8a(e, e.R, w2, e.x, 0.5f, 1.f, s, "ff linear2");   // x += ½ · ff(x)
+        // x += ½ · ff(x); with K = 4096 the fold of its K blocks goes with the next LayerNorm
+        return wmatmul_q8a(e, e.R, w2, e.x, 0.5f, 1.f, s, "ff linear2", true);
     }
     if (prev_w)
         TRYC(p2cu::ln2_rows_launch(e.x, D, prev_w, prev_b, nw, nb, e.lnbuf, D, nullptr, nullptr, e.R, D, s),
@@ -355,7 +372,9 @@ int feed_forward(P2cuEncoder& e, const float* nw, const float* nb, const DWeight
 int self_attention(P2cuEncoder& e, const DBlock& b, cudaStream_t s) {
     const bool i8 = e.mode != P2CU_EXACT;
     if (i8) {
-        TRYC(p2cu::ln_rows_launch(e.x, D, b.n_sa_w, b.n_sa_b, nullptr, 0, e.q, e.qs, e.R, D, s), "mhsa layernorm");
+        p2cu::KFold hold;
+        TRYC(p2cu::ln_rows_launch(e.x, D, b.n_sa_w, b.n_sa_b, nullptr, 0, e.q, e.qs, e.R, D, s, take_fold(e, hold)),
+             "mhsa layernorm");
         TRY(wmatmul_q8a(e, e.R, b.qkv, e.big, 1.f, 0.f, s, "qkv"));
         // pe rows were quantised when the plan was made: the same rows every layer (csrc/encoder.c:500)
         TRY(p2cu::gemm_i8(e.L, D, D, 1.f, e.pe_q, e.pe_s, b.pos.kind == P2_W_FV ? &b.pos.fv : nullptr, b.pos.q8,
@@ -436,6 +455,7 @@ int conv_module(P2cuEncoder& e, const DBlock& b, cudaStream_t s) {
 
 // The whole forward pass on stream s (csrc/encoder.c:617-624, 725-751).
 int forward(P2cuEncoder& e, cudaStream_t s) {
+    e.pending.nblk = 0;   // a pass that failed part way leaves nothing for this one
     TRY(subsampling(e, s));
     if (e.chunked)   // each chunk's frames, with their overlap context, as a window of its own
         TRYC(p2cu::gather_rows_launch(e.x, e.x_sub, e.d_gather, e.R, D, s), "chunk gather");
@@ -448,8 +468,11 @@ int forward(P2cuEncoder& e, cudaStream_t s) {
         TRY(self_attention(e, b, s));
         TRY(conv_module(e, b, s));
         TRY(feed_forward(e, b.n_ff2_w, b.n_ff2_b, b.ff2a, b.ff2b, s));
+        p2cu::KFold hold;
         if (i == NB - 1)
-            TRYC(p2cu::ln_rows_launch(e.x, D, b.n_out_w, b.n_out_b, e.x, D, nullptr, nullptr, e.R, D, s), "norm_out");
+            TRYC(p2cu::ln_rows_launch(e.x, D, b.n_out_w, b.n_out_b, e.x, D, nullptr, nullptr, e.R, D, s,
+                                      take_fold(e, hold)),
+                 "norm_out");
     }
     const float* fin = e.x;
     if (e.chunked) {   // every frame from the chunk that owns it, without the overlap (csrc/encoder.c:704)

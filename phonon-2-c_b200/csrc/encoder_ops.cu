@@ -14,6 +14,7 @@
 #include <cstdint>
 #include <cuda_runtime.h>
 #include "encoder_ops.h"
+#include "fv_gemm.h"
 #include "numerics.cuh"
 
 namespace p2cu {
@@ -100,31 +101,28 @@ __device__ __forceinline__ void ln_store(const float4 (&v)[V], float amax, float
     if (lane == 0) qscale[row] = qr.scale;
 }
 
-// D = 128 V; 8 rows per 256-thread block.
-template <int V, bool QUANT>
-__global__ void __launch_bounds__(256) ln_warp_kernel(const float* __restrict__ x, int ldx,
-                                                      const float* __restrict__ gamma, const float* __restrict__ beta,
-                                                      float* out, int ldo, int8_t* __restrict__ q,
-                                                      float* __restrict__ qscale, int rows, int fm) {
-    const int lane = threadIdx.x & 31;
-    const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
-    if (row >= rows) return;
-    const float4* xr = reinterpret_cast<const float4*>(x + static_cast<size_t>(row) * ldx);
-    float4 v[V];
+// The row completed by the K blocks of the GEMM that wrote it: v = fma(f_b, a_scale * alpha, v) block after block,
+// the epilogue's fold (fv_combine_kernel with beta != 0) on the row in registers.
+template <int V>
+__device__ __forceinline__ void fold_regs(float4 (&v)[V], const KFold& fold, int row, int lane) {
+    const float as = __fmul_rn(fold.a_scales[row], fold.alpha);
+    for (int b = 0; b < fold.nblk; ++b) {
+        const float4* fr = reinterpret_cast<const float4*>(fold.f + (static_cast<size_t>(b) * fold.m_pad + row) * 128 * V);
 #pragma unroll
-    for (int i = 0; i < V; ++i) v[i] = xr[lane + 32 * i];
-    const float amax = ln_regs<V>(v, gamma, beta, lane);
-    ln_store<V, QUANT>(v, amax, out, ldo, q, qscale, row, lane, fm);
+        for (int i = 0; i < V; ++i) {
+            const float4 f = fr[lane + 32 * i];
+            v[i] = make_float4(__fmaf_rn(f.x, as, v[i].x), __fmaf_rn(f.y, as, v[i].y), __fmaf_rn(f.z, as, v[i].z),
+                               __fmaf_rn(f.w, as, v[i].w));
+        }
+    }
 }
 
-// Two LayerNorms in a row (a block's closing norm, then the next block's first): x <- LN1(x) in place, then LN2 of
-// the new row to out2 or quantised - the values LN2 would read back, straight from registers.
-template <int V, bool QUANT>
-__global__ void __launch_bounds__(256) ln2_warp_kernel(float* x, int ldx, const float* __restrict__ g1,
-                                                       const float* __restrict__ b1, const float* __restrict__ g2,
-                                                       const float* __restrict__ b2, float* out2, int ldo,
-                                                       int8_t* __restrict__ q, float* __restrict__ qscale, int rows,
-                                                       int fm) {
+// D = 128 V; 8 rows per 256-thread block. FOLD: the row is first completed by a GEMM's K blocks and stored back.
+template <int V, bool QUANT, bool FOLD>
+__global__ void __launch_bounds__(256) ln_warp_kernel(float* x, int ldx, const float* __restrict__ gamma,
+                                                      const float* __restrict__ beta, float* out, int ldo,
+                                                      int8_t* __restrict__ q, float* __restrict__ qscale, int rows,
+                                                      int fm, KFold fold) {
     const int lane = threadIdx.x & 31;
     const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
     if (row >= rows) return;
@@ -132,6 +130,31 @@ __global__ void __launch_bounds__(256) ln2_warp_kernel(float* x, int ldx, const 
     float4 v[V];
 #pragma unroll
     for (int i = 0; i < V; ++i) v[i] = xr[lane + 32 * i];
+    if (FOLD) {
+        fold_regs<V>(v, fold, row, lane);
+#pragma unroll
+        for (int i = 0; i < V; ++i) xr[lane + 32 * i] = v[i];
+    }
+    const float amax = ln_regs<V>(v, gamma, beta, lane);
+    ln_store<V, QUANT>(v, amax, out, ldo, q, qscale, row, lane, fm);
+}
+
+// Two LayerNorms in a row (a block's closing norm, then the next block's first): x <- LN1(x) in place, then LN2 of
+// the new row to out2 or quantised - the values LN2 would read back, straight from registers.
+template <int V, bool QUANT, bool FOLD>
+__global__ void __launch_bounds__(256) ln2_warp_kernel(float* x, int ldx, const float* __restrict__ g1,
+                                                       const float* __restrict__ b1, const float* __restrict__ g2,
+                                                       const float* __restrict__ b2, float* out2, int ldo,
+                                                       int8_t* __restrict__ q, float* __restrict__ qscale, int rows,
+                                                       int fm, KFold fold) {
+    const int lane = threadIdx.x & 31;
+    const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (row >= rows) return;
+    float4* xr = reinterpret_cast<float4*>(x + static_cast<size_t>(row) * ldx);
+    float4 v[V];
+#pragma unroll
+    for (int i = 0; i < V; ++i) v[i] = xr[lane + 32 * i];
+    if (FOLD) fold_regs<V>(v, fold, row, lane);
     ln_regs<V>(v, g1, b1, lane);
 #pragma unroll
     for (int i = 0; i < V; ++i) xr[lane + 32 * i] = v[i];
@@ -333,10 +356,11 @@ __global__ void glu_rows_kernel(const float* __restrict__ pw1, float* __restrict
 }
 
 // DW_TR consecutive rows per CTA, 256 threads, four channels per thread: the DW_TR + 8 input rows the tile's taps
-// reach are loaded once into registers (a CTA reads each input row about twice instead of nine times). For each row
-// (time step t of its window) and channel: bias + the 9 taps over t - 4 .. t + 4 that fall inside the window, as one
-// FMA chain in tap order; then SiLU; then fp32 out or the row quantised.
-constexpr int DW_TR = 8;
+// reach are loaded once into registers (a CTA reads each input row three times from L2 instead of nine; four rows
+// per CTA measured 9 % faster than eight, the smaller tiles' extra reads costing less than the CTAs they add). For
+// each row (time step t of its window) and channel: bias + the 9 taps over t - 4 .. t + 4 that fall inside the
+// window, as one FMA chain in tap order; then SiLU; then fp32 out or the row quantised.
+constexpr int DW_TR = 4;
 
 template <bool QUANT, bool SWISH>
 __global__ void __launch_bounds__(256) dwconv_swish_kernel(const float* __restrict__ gated, const float* __restrict__ w,
@@ -855,16 +879,33 @@ unsigned blocks_for(size_t n, int threads) { return static_cast<unsigned>((n + t
 static bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 cudaError_t ln_rows_launch(const float* x, int ldx, const float* gamma, const float* beta, float* out, int ldo,
-                           int8_t* q, float* qscale, int rows, int D, cudaStream_t s) {
+                           int8_t* q, float* qscale, int rows, int D, cudaStream_t s, const KFold* fold) {
     if (rows <= 0) return cudaSuccess;
     const int fm = quant_fast_math();
     const bool vec = (D == 1024 || D == 512 || D == 256 || D == 128) && ldx % 4 == 0 && al16(x) && al16(gamma) &&
                      al16(beta) && (q ? al16(q) : (ldo % 4 == 0 && al16(out)));
+    float* xw = const_cast<float*>(x);   // written only when folding, which the caller asks for on its own rows
+    if (fold && fold->nblk > 0) {
+        if (D == 1024 && ldx == D && vec) {
+            const unsigned grid = static_cast<unsigned>((rows + 7) / 8);
+            if (q) ln_warp_kernel<8, true, true><<<grid, 256, 0, s>>>(xw, ldx, gamma, beta, out, ldo, q, qscale, rows,
+                                                                     fm, *fold);
+            else ln_warp_kernel<8, false, true><<<grid, 256, 0, s>>>(xw, ldx, gamma, beta, out, ldo, q, qscale, rows,
+                                                                    fm, *fold);
+            return cudaGetLastError();
+        }
+        cudaError_t e = fv_combine_launch(fold->f, fold->m_pad, fold->nblk, fold->a_scales, fold->alpha, 0, xw, rows,
+                                          D, ldx, s);
+        if (e != cudaSuccess) return e;
+    }
+    const KFold none{};
     if (vec) {
         const unsigned grid = static_cast<unsigned>((rows + 7) / 8);
 #define P2CU_LN(V)                                                                                                   \
-        if (q) ln_warp_kernel<V, true><<<grid, 256, 0, s>>>(x, ldx, gamma, beta, out, ldo, q, qscale, rows, fm);         \
-        else ln_warp_kernel<V, false><<<grid, 256, 0, s>>>(x, ldx, gamma, beta, out, ldo, q, qscale, rows, fm);
+        if (q) ln_warp_kernel<V, true, false><<<grid, 256, 0, s>>>(xw, ldx, gamma, beta, out, ldo, q, qscale, rows,   \
+                                                                   fm, none);                                        \
+        else ln_warp_kernel<V, false, false><<<grid, 256, 0, s>>>(xw, ldx, gamma, beta, out, ldo, q, qscale, rows,    \
+                                                                  fm, none);
         switch (D) {
         case 1024: P2CU_LN(8) break;
         case 512: P2CU_LN(4) break;
@@ -880,18 +921,30 @@ cudaError_t ln_rows_launch(const float* x, int ldx, const float* gamma, const fl
 }
 
 cudaError_t ln2_rows_launch(float* x, int ldx, const float* g1, const float* b1, const float* g2, const float* b2,
-                            float* out2, int ldo, int8_t* q, float* qscale, int rows, int D, cudaStream_t s) {
+                            float* out2, int ldo, int8_t* q, float* qscale, int rows, int D, cudaStream_t s,
+                            const KFold* fold) {
     if (rows <= 0) return cudaSuccess;
     const bool vec = D == 1024 && ldx % 4 == 0 && al16(x) && al16(g1) && al16(b1) && al16(g2) && al16(b2) &&
                      (q ? al16(q) : (ldo % 4 == 0 && al16(out2)));
-    if (!vec) {   // two passes
-        cudaError_t e = ln_rows_launch(x, ldx, g1, b1, x, ldx, nullptr, nullptr, rows, D, s);
+    const bool folding = fold && fold->nblk > 0;
+    if (!vec || (folding && ldx != D)) {   // two passes (the first folds)
+        cudaError_t e = ln_rows_launch(x, ldx, g1, b1, x, ldx, nullptr, nullptr, rows, D, s, fold);
         return e != cudaSuccess ? e : ln_rows_launch(x, ldx, g2, b2, out2, ldo, q, qscale, rows, D, s);
     }
     const unsigned grid = static_cast<unsigned>((rows + 7) / 8);
     const int fm = quant_fast_math();
-    if (q) ln2_warp_kernel<8, true><<<grid, 256, 0, s>>>(x, ldx, g1, b1, g2, b2, out2, ldo, q, qscale, rows, fm);
-    else ln2_warp_kernel<8, false><<<grid, 256, 0, s>>>(x, ldx, g1, b1, g2, b2, out2, ldo, q, qscale, rows, fm);
+    const KFold f = folding ? *fold : KFold{};
+    if (folding) {
+        if (q) ln2_warp_kernel<8, true, true><<<grid, 256, 0, s>>>(x, ldx, g1, b1, g2, b2, out2, ldo, q, qscale, rows,
+                                                                  fm, f);
+        else ln2_warp_kernel<8, false, true><<<grid, 256, 0, s>>>(x, ldx, g1, b1, g2, b2, out2, ldo, q, qscale, rows,
+                                                                 fm, f);
+    } else {
+        if (q) ln2_warp_kernel<8, true, false><<<grid, 256, 0, s>>>(x, ldx, g1, b1, g2, b2, out2, ldo, q, qscale,
+                                                                   rows, fm, f);
+        else ln2_warp_kernel<8, false, false><<<grid, 256, 0, s>>>(x, ldx, g1, b1, g2, b2, out2, ldo, q, qscale,
+                                                                  rows, fm, f);
+    }
     return cudaGetLastError();
 }
 

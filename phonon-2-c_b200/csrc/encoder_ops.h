@@ -6,17 +6,21 @@
 #include <cstdint>
 #include <vector>
 #include <cuda_runtime.h>
+#include "gemm.h"
 
 namespace p2cu {
 
 // LayerNorm (eps 1e-5) of each row; into `out` (fp32, may alias x) or, with q != nullptr, quantised per row into
-// int8 q [rows][D] with one scale per row (the reference's quantiser).
+// int8 q [rows][D] with one scale per row (the reference's quantiser). With a fold (fold->nblk > 0), x is first
+// completed by the K blocks of the GEMM that wrote it (KFold) and stored back, then normed.
 cudaError_t ln_rows_launch(const float* x, int ldx, const float* gamma, const float* beta, float* out, int ldo,
-                           int8_t* q, float* qscale, int rows, int D, cudaStream_t s);
+                           int8_t* q, float* qscale, int rows, int D, cudaStream_t s, const KFold* fold = nullptr);
 
 // Two LayerNorms in a row: x <- LN(x; g1, b1) in place, then LN(x; g2, b2) into out2 or quantised into q / qscale.
+// With a fold, x is first completed by the K blocks of the GEMM that wrote it (KFold); only LN1 of it is stored.
 cudaError_t ln2_rows_launch(float* x, int ldx, const float* g1, const float* b1, const float* g2, const float* b2,
-                            float* out2, int ldo, int8_t* q, float* qscale, int rows, int D, cudaStream_t s);
+                            float* out2, int ldo, int8_t* q, float* qscale, int rows, int D, cudaStream_t s,
+                            const KFold* fold = nullptr);
 
 // SiLU of each row, into `out` (fp32, may alias h) or quantised into q / qscale.
 cudaError_t swish_rows_launch(const float* h, int ldh, float* out, int ldo, int8_t* q, float* qscale, int rows,
