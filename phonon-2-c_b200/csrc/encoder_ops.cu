@@ -465,7 +465,8 @@ __device__ __forceinline__ int conv_out(int n) { return (n + 2 - 3) / 2 + 1; }
 // Conv2d(1 -> C, 3x3, stride 2, pad 1) + ReLU, then the depthwise Conv2d(C, 3x3, stride 2, pad 1) + bias that
 // follows it, per window: mel [frames][W_IN] -> [rows2][W2][C], C fastest. The first convolution's outputs are
 // computed where the second needs them instead of stored (each about twice; stored they are 6.3 GB at config 3):
-// one block per output row, one thread per channel, the 7 mel rows the row reaches in shared memory. Every
+// one block per output row, the 7 mel rows the row reaches in shared memory, a thread per four channels and eight
+// output columns (each mel value read from shared memory feeds the four channels' FMAs). Every
 // first-convolution output is bias, then its in-range taps in (kh, kw) order as one FMA chain, then ReLU; every
 // output is bias, then the in-range first-convolution outputs in (kh, kw) order as one FMA chain - the two layers'
 // own chains (csrc/encoder.c:103-153, 185-194), so the result is that of the two layers run one after the other.
@@ -478,6 +479,9 @@ __global__ void __launch_bounds__(256) sub_conv0_dw_kernel(const float* __restri
                                                            const float* __restrict__ w2, const float* __restrict__ b2,
                                                            float* __restrict__ out, int C) {
     constexpr int W1 = (W_IN - 1) / 2 + 1, W2 = (W1 - 1) / 2 + 1;
+    constexpr int CPT = 4, OPT = 8;              // channels and output columns per thread
+    constexpr int NJ = 2 * OPT + 1;              // first-convolution columns the thread's outputs reach
+    static_assert(W2 % OPT == 0 && (W2 / OPT) * 64 == 256, "four column groups of 64 threads");
     __shared__ float xs[7][W_IN];   // mel rows 4 oh2 - 3 .. 4 oh2 + 3 of the window (zeros outside it)
     const int r2 = blockIdx.x;
     const int win = find_window(h2_off, n_win, r2);
@@ -486,51 +490,70 @@ __global__ void __launch_bounds__(256) sub_conv0_dw_kernel(const float* __restri
     const int H = mel_off[win + 1] - mel_off[win];
     const float* x = mel + static_cast<size_t>(mel_off[win]) * W_IN;
     for (int e = threadIdx.x; e < 7 * W_IN; e += blockDim.x) {
-        const int j = e / W_IN, col = e % W_IN, ih = 4 * oh2 - 3 + j;
-        xs[j][col] = (ih >= 0 && ih < H) ? x[static_cast<size_t>(ih) * W_IN + col] : 0.f;
+        const int jr = e / W_IN, col = e % W_IN, ih = 4 * oh2 - 3 + jr;
+        xs[jr][col] = (ih >= 0 && ih < H) ? x[static_cast<size_t>(ih) * W_IN + col] : 0.f;
     }
     __syncthreads();
-    for (int c = threadIdx.x; c < C; c += blockDim.x) {
-        float w0c[9], w2c[9];
+    const int cg = threadIdx.x & 63, wg = threadIdx.x >> 6;   // channels 4 cg .. + 3, outputs 8 wg .. 8 wg + 7
+    const int ow0 = OPT * wg, iw0 = 2 * ow0 - 1;              // the thread's first first-convolution column
+    for (int c0 = CPT * cg; c0 < C; c0 += CPT * 64) {
+        float w0c[CPT][9], w2c[CPT][9], b0c[CPT], acc[CPT][OPT];
 #pragma unroll
-        for (int k = 0; k < 9; ++k) {
-            w0c[k] = w0[c * 9 + k];
-            w2c[k] = w2[c * 9 + k];
+        for (int u = 0; u < CPT; ++u) {
+#pragma unroll
+            for (int k = 0; k < 9; ++k) {
+                w0c[u][k] = w0[(c0 + u) * 9 + k];
+                w2c[u][k] = w2[(c0 + u) * 9 + k];
+            }
+            b0c[u] = b0[c0 + u];
+#pragma unroll
+            for (int o = 0; o < OPT; ++o) acc[u][o] = b2[c0 + u];
         }
-        const float b0c = b0[c];
-        float acc[W2];
-#pragma unroll
-        for (int ow = 0; ow < W2; ++ow) acc[ow] = b2[c];
 #pragma unroll
         for (int kh = 0; kh < 3; ++kh) {   // the second convolution's row taps: first-convolution row ih1
             const int ih1 = 2 * oh2 - 1 + kh;
             if (ih1 < 0 || ih1 >= H1) continue;
-            float cv[W1];
+            float cv[CPT][NJ];   // first-convolution columns iw0 .. iw0 + 16 of row ih1, four channels
 #pragma unroll
-            for (int iw1 = 0; iw1 < W1; ++iw1) {
-                float a = b0c;
+            for (int u = 0; u < CPT; ++u)
 #pragma unroll
-                for (int kh0 = 0; kh0 < 3; ++kh0) {
-                    const int ih = 2 * ih1 - 1 + kh0;   // mel row 4 oh2 - 3 + 2 kh + kh0
-                    if (ih < 0 || ih >= H) continue;
+                for (int jc = 0; jc < NJ; ++jc) cv[u][jc] = b0c[u];
+#pragma unroll
+            for (int kh0 = 0; kh0 < 3; ++kh0) {   // each column's taps in (kh0, kw0) order, one mel value per 4 FMAs
+                const int ih = 2 * ih1 - 1 + kh0;   // mel row 4 oh2 - 3 + 2 kh + kh0
+                if (ih < 0 || ih >= H) continue;
+                const float* xr = xs[2 * kh + kh0];
+#pragma unroll
+                for (int jc = 0; jc < NJ; ++jc) {
 #pragma unroll
                     for (int kw0 = 0; kw0 < 3; ++kw0) {
-                        const int iw = 2 * iw1 - 1 + kw0;
-                        if (iw >= 0 && iw < W_IN) a = __fmaf_rn(xs[2 * kh + kh0][iw], w0c[kh0 * 3 + kw0], a);
+                        const int iw = 2 * (iw0 + jc) - 1 + kw0;
+                        if (iw >= 0 && iw < W_IN) {
+                            const float xv = xr[iw];
+#pragma unroll
+                            for (int u = 0; u < CPT; ++u) cv[u][jc] = __fmaf_rn(xv, w0c[u][kh0 * 3 + kw0], cv[u][jc]);
+                        }
                     }
                 }
-                cv[iw1] = a > 0.f ? a : 0.f;
             }
 #pragma unroll
-            for (int ow = 0; ow < W2; ++ow)
+            for (int o = 0; o < OPT; ++o)
 #pragma unroll
                 for (int kw = 0; kw < 3; ++kw) {
-                    const int iw1 = 2 * ow - 1 + kw;
-                    if (iw1 >= 0 && iw1 < W1) acc[ow] = __fmaf_rn(cv[iw1], w2c[kh * 3 + kw], acc[ow]);
+                    const int jc = 2 * o + kw, iw1 = iw0 + jc;
+                    if (iw1 >= 0 && iw1 < W1) {
+#pragma unroll
+                        for (int u = 0; u < CPT; ++u) {
+                            const float a = cv[u][jc] > 0.f ? cv[u][jc] : 0.f;   // ReLU of the first convolution
+                            acc[u][o] = __fmaf_rn(a, w2c[u][kh * 3 + kw], acc[u][o]);
+                        }
+                    }
                 }
         }
 #pragma unroll
-        for (int ow = 0; ow < W2; ++ow) out[(static_cast<size_t>(r2) * W2 + ow) * C + c] = acc[ow];
+        for (int o = 0; o < OPT; ++o)
+            *reinterpret_cast<float4*>(out + (static_cast<size_t>(r2) * W2 + ow0 + o) * C + c0) =
+                make_float4(acc[0][o], acc[1][o], acc[2][o], acc[3][o]);
     }
 }
 
@@ -1012,7 +1035,7 @@ cudaError_t sub_conv0_dw_launch(const float* mel, const int* mel_off, const int*
                                 const float* w0, const float* b0, const float* w2, const float* b2, float* out,
                                 int rows2, int W_in, int C, cudaStream_t s) {
     if (rows2 <= 0) return cudaSuccess;
-    if (W_in != 128) return cudaErrorInvalidValue;   // the model's 128 mel bins
+    if (W_in != 128 || C % 4) return cudaErrorInvalidValue;   // the model's 128 mel bins, channels in fours
     sub_conv0_dw_kernel<128><<<rows2, 256, 0, s>>>(mel, mel_off, h1_off, h2_off, n_win, w0, b0, w2, b2, out, C);
     return cudaGetLastError();
 }
