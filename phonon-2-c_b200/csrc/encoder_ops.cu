@@ -347,12 +347,28 @@ __global__ void __launch_bounds__(256) attn_softmax_kernel(float* s_ac, const fl
 // ---- conv module: GLU, depthwise conv, SiLU (csrc/encoder.c:543-552, csrc/tensor_ops.c:559-649) -----------------
 
 // gated = a / (1 + expneg(b)), expneg(b) = expf(b < -87 ? 87 : -b) (csrc/phonon2.h:38-41).
-__global__ void glu_rows_kernel(const float* __restrict__ pw1, float* __restrict__ gated, int rows, int D) {
+__device__ __forceinline__ float glu1(float a, float b) {
+    return __fdiv_rn(a, __fadd_rn(1.0f, expf(b < -87.0f ? 87.0f : -b)));
+}
+
+// One block per row, four channels per thread (D % 4 == 0): no index division, 16-byte loads and stores.
+__global__ void __launch_bounds__(256) glu_rows_kernel(const float* __restrict__ pw1, float* __restrict__ gated,
+                                                       int D) {
+    const float4* in = reinterpret_cast<const float4*>(pw1 + static_cast<size_t>(blockIdx.x) * 2 * D);
+    float4* out = reinterpret_cast<float4*>(gated + static_cast<size_t>(blockIdx.x) * D);
+    const int d4n = D / 4;
+    for (int d4 = threadIdx.x; d4 < d4n; d4 += blockDim.x) {
+        const float4 a = in[d4], b = in[d4n + d4];
+        out[d4] = make_float4(glu1(a.x, b.x), glu1(a.y, b.y), glu1(a.z, b.z), glu1(a.w, b.w));
+    }
+}
+
+// Any D: one thread per value.
+__global__ void glu_any_kernel(const float* __restrict__ pw1, float* __restrict__ gated, int rows, int D) {
     const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (i >= static_cast<size_t>(rows) * D) return;
     const size_t r = i / D, d = i % D;
-    const float a = pw1[r * 2 * D + d], b = pw1[r * 2 * D + D + d];
-    gated[i] = __fdiv_rn(a, __fadd_rn(1.0f, expf(b < -87.0f ? 87.0f : -b)));
+    gated[i] = glu1(pw1[r * 2 * D + d], pw1[r * 2 * D + D + d]);
 }
 
 // DW_TR consecutive rows per CTA, 256 threads, four channels per thread: the DW_TR + 8 input rows the tile's taps
@@ -1009,7 +1025,10 @@ cudaError_t softmax_rows_launch(float* x, int rows, int len, cudaStream_t s) {
 cudaError_t glu_rows_launch(const float* pw1, float* gated, int rows, int D, cudaStream_t s) {
     const size_t n = static_cast<size_t>(rows) * D;
     if (!n) return cudaSuccess;
-    glu_rows_kernel<<<blocks_for(n, 256), 256, 0, s>>>(pw1, gated, rows, D);
+    if (D % 4 == 0 && al16(pw1) && al16(gated))
+        glu_rows_kernel<<<rows, 256, 0, s>>>(pw1, gated, D);
+    else
+        glu_any_kernel<<<blocks_for(n, 256), 256, 0, s>>>(pw1, gated, rows, D);
     return cudaGetLastError();
 }
 
