@@ -611,6 +611,21 @@ __global__ void __launch_bounds__(256) sub_dwconv_kernel(const float* __restrict
     }
 }
 
+// One block per frame, W = 16 and C = 256: the frame's [16][256] values through shared memory, read along the channels
+// and written 16 consecutive values (one channel's W positions) per thread.
+__global__ void __launch_bounds__(256) sub_flatten16_kernel(const float* __restrict__ in, float* __restrict__ out) {
+    __shared__ float tile[16][256];
+    const float* src = in + static_cast<size_t>(blockIdx.x) * 16 * 256;
+#pragma unroll
+    for (int wv = 0; wv < 16; ++wv) tile[wv][threadIdx.x] = src[wv * 256 + threadIdx.x];
+    __syncthreads();
+    float4* dst = reinterpret_cast<float4*>(out + (static_cast<size_t>(blockIdx.x) * 256 + threadIdx.x) * 16);
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+        dst[q] = make_float4(tile[4 * q][threadIdx.x], tile[4 * q + 1][threadIdx.x], tile[4 * q + 2][threadIdx.x],
+                             tile[4 * q + 3][threadIdx.x]);
+}
+
 __global__ void sub_flatten_kernel(const float* __restrict__ in, float* __restrict__ out, int rows, int W, int C) {
     const size_t idx = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     const size_t per = static_cast<size_t>(W) * C;
@@ -652,6 +667,16 @@ __global__ void __launch_bounds__(256) v_transpose_kernel(const float* __restric
 __global__ void bias_rows_kernel(float* x, const float* __restrict__ b, size_t total, int N) {
     const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (i < total) x[i] = __fadd_rn(x[i], b[i % N]);
+}
+
+// One block per row, four values per thread (N % 4 == 0, 16-byte aligned rows).
+__global__ void __launch_bounds__(256) bias_rows4_kernel(float* x, const float* __restrict__ b, int N) {
+    float4* row = reinterpret_cast<float4*>(x + static_cast<size_t>(blockIdx.x) * N);
+    const float4* b4 = reinterpret_cast<const float4*>(b);
+    for (int i = threadIdx.x; i < N / 4; i += blockDim.x) {
+        const float4 v = row[i], c = b4[i];
+        row[i] = make_float4(__fadd_rn(v.x, c.x), __fadd_rn(v.y, c.y), __fadd_rn(v.z, c.z), __fadd_rn(v.w, c.w));
+    }
 }
 
 // ---- grouped SIMT fp32 GEMM (the attention products, csrc/encoder.c:282-316, 505-519) ---------------------------
@@ -1071,7 +1096,10 @@ cudaError_t sub_dwconv_launch(const float* in, const int* in_off, const int* out
 cudaError_t sub_flatten_launch(const float* in, float* out, int rows, int W, int C, cudaStream_t s) {
     const size_t n = static_cast<size_t>(rows) * W * C;
     if (!n) return cudaSuccess;
-    sub_flatten_kernel<<<blocks_for(n, 256), 256, 0, s>>>(in, out, rows, W, C);
+    if (W == 16 && C == 256 && al16(out))
+        sub_flatten16_kernel<<<rows, 256, 0, s>>>(in, out);
+    else
+        sub_flatten_kernel<<<blocks_for(n, 256), 256, 0, s>>>(in, out, rows, W, C);
     return cudaGetLastError();
 }
 
@@ -1085,7 +1113,10 @@ cudaError_t v_transpose_launch(const float* qkv, float* vt, const int* row_off, 
 cudaError_t bias_rows_launch(float* x, const float* b, int rows, int N, cudaStream_t s) {
     const size_t n = static_cast<size_t>(rows) * N;
     if (!n) return cudaSuccess;
-    bias_rows_kernel<<<blocks_for(n, 256), 256, 0, s>>>(x, b, n, N);
+    if (N % 4 == 0 && al16(x) && al16(b))
+        bias_rows4_kernel<<<rows, 256, 0, s>>>(x, b, N);
+    else
+        bias_rows_kernel<<<blocks_for(n, 256), 256, 0, s>>>(x, b, n, N);
     return cudaGetLastError();
 }
 
