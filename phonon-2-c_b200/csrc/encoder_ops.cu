@@ -46,9 +46,16 @@ __device__ __forceinline__ float amax4(float4 v) {
     return fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
 }
 
+// quant_one on four values: the conversions as there, then two saturating packs (PTX cvt.pack.sat.s8.s32.b32 puts
+// sat(b) in bits 0-7, sat(a) in bits 8-15 and c's low half above them), the clamp to [-128, 127] of quant_one.
 __device__ __forceinline__ char4 quant4(float4 v, float inv) {
+    const float2 t0 = f2_mul(make_float2(v.x, v.y), f2_splat(inv)), t1 = f2_mul(make_float2(v.z, v.w), f2_splat(inv));
+    const int x = __float2int_rn(t0.x), y = __float2int_rn(t0.y), z = __float2int_rn(t1.x), w = __float2int_rn(t1.y);
+    uint32_t zw, xyzw;
+    asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, 0;" : "=r"(zw) : "r"(w), "r"(z));
+    asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, %3;" : "=r"(xyzw) : "r"(y), "r"(x), "r"(zw));
     char4 c;
-    c.x = quant_one(v.x, inv); c.y = quant_one(v.y, inv); c.z = quant_one(v.z, inv); c.w = quant_one(v.w, inv);
+    *reinterpret_cast<uint32_t*>(&c) = xyzw;
     return c;
 }
 
@@ -260,7 +267,8 @@ __global__ void __launch_bounds__(256) swish_vec_kernel(const float* __restrict_
 #pragma unroll
     for (int i = 0; i < V; ++i) {
         const float4 a = hr[threadIdx.x + 256 * i];
-        v[i] = make_float4(swish1(a.x), swish1(a.y), swish1(a.z), swish1(a.w));
+        const float2 s0 = swish2(make_float2(a.x, a.y)), s1 = swish2(make_float2(a.z, a.w));
+        v[i] = make_float4(s0.x, s0.y, s1.x, s1.y);
         amax = fmaxf(amax, amax4(v[i]));
     }
     if (!QUANT) {
@@ -375,17 +383,57 @@ __global__ void glu_any_kernel(const float* __restrict__ pw1, float* __restrict_
 // reach are loaded once into registers (a CTA reads each input row three times from L2 instead of nine; four rows
 // per CTA measured 9 % faster than eight, the smaller tiles' extra reads costing less than the CTAs they add). For
 // each row (time step t of its window) and channel: bias + the 9 taps over t - 4 .. t + 4 that fall inside the
-// window, as one FMA chain in tap order; then SiLU; then fp32 out or the row quantised.
+// window, as one FMA chain in tap order; then SiLU; then fp32 out or the row quantised. A tile whose taps all lie
+// inside one window (every tile but those at a window's edges) skips the per-tap and per-row checks; DFIX = 1024
+// (the model's width) makes the row stride a constant.
 constexpr int DW_TR = 4;
 
-template <bool QUANT, bool SWISH>
-__global__ void __launch_bounds__(256) dwconv_swish_kernel(const float* __restrict__ gated, const float* __restrict__ w,
+template <bool SWISH, bool CHECK, int DFIX>
+__device__ __forceinline__ void dw_taps(const float* __restrict__ gated, const float* __restrict__ w,
+                                        const float* __restrict__ b, int g0, int rows, int D_, const int (&lo)[DW_TR],
+                                        const int (&hi)[DW_TR], float (&v)[DW_TR][4]) {
+    const int D = DFIX ? DFIX : D_;
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+        const int d = threadIdx.x + 256 * u;
+        if (!DFIX && d >= D) {
+#pragma unroll
+            for (int i = 0; i < DW_TR; ++i) v[i][u] = 0.f;
+            continue;
+        }
+        float x[DW_TR + 8];   // input rows g0 - 4 .. g0 + DW_TR + 3 of channel d
+        const float* col = gated + d;
+#pragma unroll
+        for (int j = 0; j < DW_TR + 8; ++j) {
+            const int g = g0 - 4 + j;
+            x[j] = (!CHECK || (g >= 0 && g < rows)) ? __ldg(col + static_cast<ptrdiff_t>(g) * D) : 0.f;
+        }
+        float wk[9];
+#pragma unroll
+        for (int k = 0; k < 9; ++k) wk[k] = __ldg(w + static_cast<size_t>(d) * 9 + k);
+        const float bd = b ? __ldg(b + d) : 0.f;
+#pragma unroll
+        for (int i = 0; i < DW_TR; ++i) {
+            float acc = bd;
+#pragma unroll
+            for (int k = 0; k < 9; ++k) {
+                const int src = g0 + i - 4 + k;
+                if (!CHECK || (src >= lo[i] && src < hi[i])) acc = __fmaf_rn(x[i + k], wk[k], acc);
+            }
+            v[i][u] = SWISH ? swish1(acc) : acc;
+        }
+    }
+}
+
+template <bool QUANT, bool SWISH, int DFIX>
+__global__ void __launch_bounds__(256, 4) dwconv_swish_kernel(const float* __restrict__ gated, const float* __restrict__ w,
                                                            const float* __restrict__ b,
                                                            const int* __restrict__ row_off, int n_win,
                                                            float* __restrict__ out, int8_t* __restrict__ q,
-                                                           float* __restrict__ qscale, int rows, int D, int fm) {
+                                                           float* __restrict__ qscale, int rows, int D_, int fm) {
     __shared__ float red[8][DW_TR];
     constexpr int PER = 4;   // channels per thread (D <= 1024)
+    const int D = DFIX ? DFIX : D_;
     const int g0 = blockIdx.x * DW_TR;   // the tile's first row
     // the window bounds [lo, hi) of each of the tile's rows (without a window table the rows are one window)
     int lo[DW_TR], hi[DW_TR];
@@ -403,36 +451,14 @@ __global__ void __launch_bounds__(256) dwconv_swish_kernel(const float* __restri
             }
         }
     }
+    // every tap of every row inside the first row's window (and so inside [0, rows))
+    const bool inner = lo[DW_TR - 1] == lo[0] && g0 - 4 >= lo[0] && g0 + DW_TR + 3 < hi[0] && g0 - 4 >= 0 &&
+                       g0 + DW_TR + 3 < rows;
     float v[DW_TR][PER];
-#pragma unroll
-    for (int u = 0; u < PER; ++u) {
-        const int d = threadIdx.x + 256 * u;
-        if (d >= D) {
-#pragma unroll
-            for (int i = 0; i < DW_TR; ++i) v[i][u] = 0.f;
-            continue;
-        }
-        float x[DW_TR + 8];   // input rows g0 - 4 .. g0 + DW_TR + 3 of channel d
-#pragma unroll
-        for (int j = 0; j < DW_TR + 8; ++j) {
-            const int g = g0 - 4 + j;
-            x[j] = (g >= 0 && g < rows) ? __ldg(gated + static_cast<size_t>(g) * D + d) : 0.f;
-        }
-        float wk[9];
-#pragma unroll
-        for (int k = 0; k < 9; ++k) wk[k] = __ldg(w + static_cast<size_t>(d) * 9 + k);
-        const float bd = b ? __ldg(b + d) : 0.f;
-#pragma unroll
-        for (int i = 0; i < DW_TR; ++i) {
-            float acc = bd;
-#pragma unroll
-            for (int k = 0; k < 9; ++k) {
-                const int src = g0 + i - 4 + k;
-                if (src >= lo[i] && src < hi[i]) acc = __fmaf_rn(x[i + k], wk[k], acc);
-            }
-            v[i][u] = SWISH ? swish1(acc) : acc;
-        }
-    }
+    if (inner)
+        dw_taps<SWISH, false, DFIX>(gated, w, b, g0, rows, D, lo, hi, v);
+    else
+        dw_taps<SWISH, true, DFIX>(gated, w, b, g0, rows, D, lo, hi, v);
     if constexpr (!QUANT) {
 #pragma unroll
         for (int i = 0; i < DW_TR; ++i) {
@@ -1061,8 +1087,11 @@ cudaError_t dwconv_swish_launch(const float* gated, const float* w, const float*
                                 float* out, int8_t* q, float* qscale, int rows, int D, cudaStream_t s, bool swish) {
     if (rows <= 0) return cudaSuccess;
     if (D > 1024) return cudaErrorInvalidValue;
-    auto* k = q ? (swish ? dwconv_swish_kernel<true, true> : dwconv_swish_kernel<true, false>)
-                : (swish ? dwconv_swish_kernel<false, true> : dwconv_swish_kernel<false, false>);
+    auto* k = D == 1024
+                  ? (q ? (swish ? dwconv_swish_kernel<true, true, 1024> : dwconv_swish_kernel<true, false, 1024>)
+                       : (swish ? dwconv_swish_kernel<false, true, 1024> : dwconv_swish_kernel<false, false, 1024>))
+                  : (q ? (swish ? dwconv_swish_kernel<true, true, 0> : dwconv_swish_kernel<true, false, 0>)
+                       : (swish ? dwconv_swish_kernel<false, true, 0> : dwconv_swish_kernel<false, false, 0>));
     k<<<(rows + DW_TR - 1) / DW_TR, 256, 0, s>>>(gated, w, b, row_off, n_win, out, q, qscale, rows, D,
                                                  quant_fast_math());
     return cudaGetLastError();

@@ -52,10 +52,16 @@ __device__ __forceinline__ int8_t quant_at(float x, const QuantRule& r, int k, i
 // exp(x) as the reference's AVX2 path evaluates it (csrc/tensor_ops.c:154-172): clamp to [-87, 87], k = round(x *
 // log2 e), r = x - k * ln 2, a degree-5 Taylor polynomial in r by Horner's rule, times 2^k built in the exponent
 // bits. The compiled reference fuses r into one fused multiply-subtract, as here.
+//
+// k is read off t + 1.5 * 2^23 (t = x log2 e, |t| <= 125.6): that sum lies in [2^23, 2^24), where the fp32 grid is
+// the integers, so the addition rounds t half to even, exactly as rintf does, and the sum's bits are 0x4B400000 + k
+// (checked for every fp32 |t| <= 126). It keeps the rounding and the conversion to an integer off the conversion
+// unit, which runs at a quarter of the FMA rate. 2^k's bits (k + 127) << 23 are then (bits + 127) << 23: 0x4B400000
+// shifted left by 23 leaves 32 bits.
 __device__ __forceinline__ float exp_poly(float x) {
     x = fminf(fmaxf(x, -87.0f), 87.0f);
-    const float kf = rintf(__fmul_rn(x, 1.44269504088896341f));
-    const int ki = static_cast<int>(kf);
+    const float sh = __fadd_rn(__fmul_rn(x, 1.44269504088896341f), 12582912.0f);
+    const float kf = __fsub_rn(sh, 12582912.0f);
     const float r = __fmaf_rn(-kf, 0.69314718055994529f, x);
     float y = 1.0f / 120.0f;
     y = __fmaf_rn(y, r, 1.0f / 24.0f);
@@ -63,13 +69,77 @@ __device__ __forceinline__ float exp_poly(float x) {
     y = __fmaf_rn(y, r, 0.5f);
     y = __fmaf_rn(y, r, 1.0f);
     y = __fmaf_rn(y, r, 1.0f);
-    return __fmul_rn(y, __int_as_float((ki + 127) << 23));
+    return __fmul_rn(y, __int_as_float(static_cast<int>((__float_as_uint(sh) + 127u) << 23)));
 }
 
 // SiLU as the reference's vector loop computes it (csrc/tensor_ops.c:450-458): v * (1 / (1 + exp(0 - v))).
 __device__ __forceinline__ float swish1(float v) {
     const float e = exp_poly(__fsub_rn(0.0f, v));
     return __fmul_rn(v, __frcp_rn(__fadd_rn(1.0f, e)));
+}
+
+// ---- two values per instruction: sm_100's packed fp32 arithmetic (PTX add / sub / mul / fma .rn.f32x2) ----------
+//
+// Each lane of a packed operation is the IEEE single-precision operation of its scalar form (round to nearest even,
+// no flush to zero), so a formula written with them gives the scalar formula's bits lane by lane at half the issue
+// slots for its adds, multiplies and FMAs - as long as no packed product whose rounding matters feeds a packed add
+// (see exp_poly2).
+__device__ __forceinline__ unsigned long long f2_pack(float2 v) {
+    return (static_cast<unsigned long long>(__float_as_uint(v.y)) << 32) | __float_as_uint(v.x);
+}
+__device__ __forceinline__ float2 f2_unpack(unsigned long long u) {
+    return make_float2(__uint_as_float(static_cast<unsigned>(u)), __uint_as_float(static_cast<unsigned>(u >> 32)));
+}
+__device__ __forceinline__ float2 f2_fma(float2 a, float2 b, float2 c) {
+    unsigned long long d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(f2_pack(a)), "l"(f2_pack(b)), "l"(f2_pack(c)));
+    return f2_unpack(d);
+}
+__device__ __forceinline__ float2 f2_add(float2 a, float2 b) {
+    unsigned long long d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(f2_pack(a)), "l"(f2_pack(b)));
+    return f2_unpack(d);
+}
+__device__ __forceinline__ float2 f2_sub(float2 a, float2 b) {
+    unsigned long long d;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(f2_pack(a)), "l"(f2_pack(b)));
+    return f2_unpack(d);
+}
+__device__ __forceinline__ float2 f2_mul(float2 a, float2 b) {
+    unsigned long long d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(f2_pack(a)), "l"(f2_pack(b)));
+    return f2_unpack(d);
+}
+__device__ __forceinline__ float2 f2_splat(float c) { return make_float2(c, c); }
+
+// exp_poly on two values: the same operations in the same order (r = x - k ln 2 as fma(k, -ln 2, x), the same
+// exactly rounded value as fma(-k, ln 2, x)). The products x log2 e stay scalar: a packed multiply whose result
+// feeds a packed add can be contracted into one packed FMA (the .rn of the packed forms does not forbid it as it does
+// for the scalar ones), which rounds x log2 e + 1.5 * 2^23 once and picks the other k wherever x log2 e lies within
+// an ulp of a half (measured: 122 of the 2^32 inputs). y 2^k below is exact (a power of two, normal results), so its
+// product may fuse into a following add without changing a bit.
+__device__ __forceinline__ float2 exp_poly2(float2 x) {
+    x.x = fminf(fmaxf(x.x, -87.0f), 87.0f);
+    x.y = fminf(fmaxf(x.y, -87.0f), 87.0f);
+    const float2 t = make_float2(__fmul_rn(x.x, 1.44269504088896341f), __fmul_rn(x.y, 1.44269504088896341f));
+    const float2 sh = f2_add(t, f2_splat(12582912.0f));
+    const float2 kf = f2_sub(sh, f2_splat(12582912.0f));
+    const float2 r = f2_fma(kf, f2_splat(-0.69314718055994529f), x);
+    float2 y = f2_splat(1.0f / 120.0f);
+    y = f2_fma(y, r, f2_splat(1.0f / 24.0f));
+    y = f2_fma(y, r, f2_splat(1.0f / 6.0f));
+    y = f2_fma(y, r, f2_splat(0.5f));
+    y = f2_fma(y, r, f2_splat(1.0f));
+    y = f2_fma(y, r, f2_splat(1.0f));
+    const float2 p2k = make_float2(__uint_as_float((__float_as_uint(sh.x) + 127u) << 23),
+                                   __uint_as_float((__float_as_uint(sh.y) + 127u) << 23));
+    return f2_mul(y, p2k);
+}
+
+// swish1 on two values.
+__device__ __forceinline__ float2 swish2(float2 v) {
+    const float2 d = f2_add(f2_splat(1.0f), exp_poly2(f2_sub(f2_splat(0.0f), v)));
+    return f2_mul(v, make_float2(__frcp_rn(d.x), __frcp_rn(d.y)));
 }
 
 // Sum of the eight lanes of an 8-lane group in the order of the reference's AVX2 horizontal sum
