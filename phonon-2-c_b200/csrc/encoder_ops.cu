@@ -420,8 +420,18 @@ __device__ __forceinline__ void dw_taps(const float* __restrict__ gated, const f
                 const int src = g0 + i - 4 + k;
                 if (!CHECK || (src >= lo[i] && src < hi[i])) acc = __fmaf_rn(x[i + k], wk[k], acc);
             }
-            v[i][u] = SWISH ? swish1(acc) : acc;
+            v[i][u] = acc;
         }
+    }
+    if (SWISH) {   // channels d, d + 256 in the two lanes of the packed SiLU
+#pragma unroll
+        for (int i = 0; i < DW_TR; ++i)
+#pragma unroll
+            for (int u = 0; u < 4; u += 2) {
+                const float2 r = swish2(make_float2(v[i][u], v[i][u + 1]));
+                v[i][u] = r.x;
+                v[i][u + 1] = r.y;
+            }
     }
 }
 

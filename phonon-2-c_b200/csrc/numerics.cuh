@@ -136,10 +136,26 @@ __device__ __forceinline__ float2 exp_poly2(float2 x) {
     return f2_mul(y, p2k);
 }
 
-// swish1 on two values.
+// 1 / d, correctly rounded, for d in [1, 2^126), two values at a time; nd = -d. From the hardware estimate
+// (rcp.approx, within an ulp) two steps of Markstein's correction y + y (1 - d y) (P. Markstein, "Computation of
+// elementary functions on the IBM RISC System/6000 processor", IBM J. Res. Dev. 34(1), 1990): once y is within an ulp
+// of 1 / d, 1 - d y is exact in one FMA and the last step rounds correctly. Checked against __frcp_rn for every fp32 d
+// in the range; results are normal there (above 2^-126), so the estimate's flush to zero never applies.
+__device__ __forceinline__ float2 rcp2_ge1(float2 d, float2 nd) {
+    float2 y;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y.x) : "f"(d.x));
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y.y) : "f"(d.y));
+    float2 e = f2_fma(nd, y, f2_splat(1.0f));
+    y = f2_fma(e, y, y);
+    e = f2_fma(nd, y, f2_splat(1.0f));
+    return f2_fma(e, y, y);
+}
+
+// swish1 on two values. 1 + e lies in [1, 2^126) (e <= exp_poly(87) = 0.71 * 2^126), the range of rcp2_ge1, and
+// -1 - e is exactly -(1 + e).
 __device__ __forceinline__ float2 swish2(float2 v) {
-    const float2 d = f2_add(f2_splat(1.0f), exp_poly2(f2_sub(f2_splat(0.0f), v)));
-    return f2_mul(v, make_float2(__frcp_rn(d.x), __frcp_rn(d.y)));
+    const float2 e = exp_poly2(f2_sub(f2_splat(0.0f), v));
+    return f2_mul(v, rcp2_ge1(f2_add(f2_splat(1.0f), e), f2_sub(f2_splat(-1.0f), e)));
 }
 
 // Sum of the eight lanes of an 8-lane group in the order of the reference's AVX2 horizontal sum
