@@ -419,7 +419,7 @@ int self_attention(P2cuEncoder& e, const DBlock& b, cudaStream_t s) {
         TRYC(p2cu::group_gemm_launch(e.g_av, e.ng, e.t_av, e.s_ac, e.big, e.attn, nullptr, 0, s), "attention av");
     }
     if (i8) {
-        TRYC(p2cu::quant_rows_launch(e.attn, e.R, D, D, e.q, e.qs, s), "attention quant");
+        TRYC(p2cu::quant_rows_dense_launch(e.attn, e.q, e.qs, e.R, D, s), "attention quant");
         return wmatmul_q8a(e, e.R, b.out, e.x, 1.f, 1.f, s, "out");   // x += attn @ W_o
     }
     p2cu::Epilogue res;

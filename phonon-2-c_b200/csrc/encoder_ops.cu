@@ -15,6 +15,7 @@
 #include <cuda_runtime.h>
 #include "encoder_ops.h"
 #include "fv_gemm.h"
+#include "kernels.h"
 #include "numerics.cuh"
 
 namespace p2cu {
@@ -144,6 +145,25 @@ __global__ void __launch_bounds__(256) ln_warp_kernel(float* x, int ldx, const f
     }
     const float amax = ln_regs<V>(v, gamma, beta, lane);
     ln_store<V, QUANT>(v, amax, out, ldo, q, qscale, row, lane, fm);
+}
+
+// The reference's per-row quantisation of rows of D = 128 V (D % 16 == 0, so no scalar tail), one warp per row held
+// in registers: quant_rows_kernel's arithmetic for these rows, without its block-wide reduction and barrier.
+template <int V>
+__global__ void __launch_bounds__(256) quant_warp_kernel(const float* __restrict__ x, int8_t* __restrict__ q,
+                                                         float* __restrict__ qscale, int rows, int fm) {
+    const int lane = threadIdx.x & 31;
+    const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (row >= rows) return;
+    const float4* xr = reinterpret_cast<const float4*>(x + static_cast<size_t>(row) * 128 * V);
+    float4 v[V];
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+        v[i] = xr[lane + 32 * i];
+        amax = fmaxf(amax, amax4(v[i]));
+    }
+    ln_store<V, true>(v, warp_max(amax), nullptr, 0, q, qscale, row, lane, fm);
 }
 
 // Two LayerNorms in a row (a block's closing norm, then the next block's first): x <- LN1(x) in place, then LN2 of
@@ -977,6 +997,13 @@ unsigned blocks_for(size_t n, int threads) { return static_cast<unsigned>((n + t
 }  // namespace
 
 static bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+cudaError_t quant_rows_dense_launch(const float* x, int8_t* q, float* qscale, int rows, int D, cudaStream_t s) {
+    if (rows <= 0) return cudaSuccess;
+    if (D != 1024 || !al16(x) || !al16(q)) return quant_rows_launch(x, rows, D, D, q, qscale, s);
+    quant_warp_kernel<8><<<static_cast<unsigned>((rows + 7) / 8), 256, 0, s>>>(x, q, qscale, rows, quant_fast_math());
+    return cudaGetLastError();
+}
 
 cudaError_t ln_rows_launch(const float* x, int ldx, const float* gamma, const float* beta, float* out, int ldo,
                            int8_t* q, float* qscale, int rows, int D, cudaStream_t s, const KFold* fold) {

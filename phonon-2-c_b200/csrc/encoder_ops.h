@@ -10,6 +10,10 @@
 
 namespace p2cu {
 
+// The reference's per-row int8 quantisation of dense rows [rows][D] (lda = D) into q / qscale, as quant_rows_launch;
+// D = 1024 with 16-byte aligned rows takes one warp per row.
+cudaError_t quant_rows_dense_launch(const float* x, int8_t* q, float* qscale, int rows, int D, cudaStream_t s);
+
 // LayerNorm (eps 1e-5) of each row; into `out` (fp32, may alias x) or, with q != nullptr, quantised per row into
 // int8 q [rows][D] with one scale per row (the reference's quantiser). With a fold (fold->nblk > 0), x is first
 // completed by the K blocks of the GEMM that wrote it (KFold) and stored back, then normed.

@@ -10,6 +10,8 @@
 //     remotely on the even CTA's barrier (mode 2), against the same MMAs issued without waiting (mode 0). The gap is
 //     what the handshake alone costs: the MMAs of a step can start only after the MMAs six steps back have
 //     completed and their release has travelled round the ring.
+//   * p2cu_probe_packed_math: the encoder's packed fp32x2 SiLU and exp (numerics.cuh) against their scalar forms,
+//     and the packed reciprocal against __frcp_rn, bit for bit over every input in their ranges.
 // Each allocates its own buffers, runs a few launches, and reports through out-parameters. Every wait is bounded.
 // Built as its own library (libphonon2_probes.so, declared in probes.h): the product library does not carry them.
 #include <cstdint>
@@ -19,6 +21,7 @@
 #include <cstdarg>
 #include "probes.h"
 #include "ptx.cuh"
+#include "numerics.cuh"
 
 namespace p2cu {
 namespace {
@@ -279,6 +282,64 @@ tma_probe_kernel(const __grid_constant__ CUtensorMap tm, int boxes, int warps, i
     __syncthreads();
 }
 
+// exp_poly as first written: k by rintf and an integer conversion (the reference's formula, step for step)
+__device__ __forceinline__ float exp_rint(float x) {
+    x = fminf(fmaxf(x, -87.0f), 87.0f);
+    const float kf = rintf(__fmul_rn(x, 1.44269504088896341f));
+    const int ki = static_cast<int>(kf);
+    const float r = __fmaf_rn(-kf, 0.69314718055994529f, x);
+    float y = 1.0f / 120.0f;
+    y = __fmaf_rn(y, r, 1.0f / 24.0f);
+    y = __fmaf_rn(y, r, 1.0f / 6.0f);
+    y = __fmaf_rn(y, r, 0.5f);
+    y = __fmaf_rn(y, r, 1.0f);
+    y = __fmaf_rn(y, r, 1.0f);
+    return __fmul_rn(y, __int_as_float((ki + 127) << 23));
+}
+
+__device__ __forceinline__ bool same_bits(float a, float b) {
+    return __float_as_uint(a) == __float_as_uint(b) || (a != a && b != b);
+}
+
+__device__ __forceinline__ uint32_t mix32(uint32_t x) {
+    x ^= x >> 16; x *= 0x7feb352du; x ^= x >> 15; x *= 0x846ca68bu; x ^= x >> 16;
+    return x;
+}
+
+// Over every 32-bit pattern u (x = the float with those bits, x' = -x): bad[0] exp_poly(x) != exp_rint(x); bad[1]
+// exp_poly2 on (x, x') != exp_poly on each; bad[2] swish2 on (x', x) != swish1 on each; bad[3] f2_fma != __fmaf_rn
+// on hashed operand triples (normal, subnormal and special values); bad[4] rcp2_ge1 != __frcp_rn over [1, 2^126).
+__global__ void packed_math_kernel(unsigned long long* bad) {
+    const uint64_t stride = static_cast<uint64_t>(gridDim.x) * blockDim.x;
+    unsigned long long b0 = 0, b1 = 0, b2 = 0, b3 = 0, b4 = 0;
+    for (uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; i < (1ull << 32); i += stride) {
+        const uint32_t u = static_cast<uint32_t>(i);
+        const float x = __uint_as_float(u), xn = __uint_as_float(u ^ 0x80000000u);
+        const float ex = exp_poly(x);
+        b0 += !same_bits(ex, exp_rint(x));
+        const float2 e2 = exp_poly2(make_float2(x, xn));
+        b1 += !same_bits(e2.x, ex) || !same_bits(e2.y, exp_poly(xn));
+        const float2 s2 = swish2(make_float2(xn, x));
+        b2 += !same_bits(s2.y, swish1(x)) || !same_bits(s2.x, swish1(xn));
+        const uint32_t h1 = mix32(u), h2 = mix32(u ^ 0x9e3779b9u), h3 = mix32(u + 0x632be5abu);
+        const float a = __uint_as_float(h1), bb = __uint_as_float(h2), c = __uint_as_float(h3);
+        const float as = __uint_as_float(h1 & 0x807fffffu), cs = __uint_as_float(h3 >> 9);
+        const float2 f = f2_fma(make_float2(a, as), make_float2(bb, bb), make_float2(c, cs));
+        b3 += !same_bits(f.x, __fmaf_rn(a, bb, c)) || !same_bits(f.y, __fmaf_rn(as, bb, cs));
+        if (u >= 0x3F800000u && u < 0x7E800000u && !(u & 1u)) {
+            const float2 d = make_float2(x, __uint_as_float(u + 1));
+            const float2 r = rcp2_ge1(d, make_float2(-d.x, -d.y));
+            b4 += (__float_as_uint(r.x) != __float_as_uint(__frcp_rn(d.x))) +
+                  (__float_as_uint(r.y) != __float_as_uint(__frcp_rn(d.y)));
+        }
+    }
+    if (b0) atomicAdd(&bad[0], b0);
+    if (b1) atomicAdd(&bad[1], b1);
+    if (b2) atomicAdd(&bad[2], b2);
+    if (b3) atomicAdd(&bad[3], b3);
+    if (b4) atomicAdd(&bad[4], b4);
+}
+
 int sms_of_device() {
     int dev = 0, n = 0;
     cudaGetDevice(&dev);
@@ -423,6 +484,25 @@ int p2cu_probe_tma_load(int warps, int box_rows, double* bytes_per_s_per_sm) {
     if (rc == 0) rc = check_device();
     if (rc == 0) *bytes_per_s_per_sm = static_cast<double>(boxes / warps * warps) * 128 * box_rows /
                                               (best * 1e-3);
+    return rc;
+}
+
+// The packed fp32x2 forms against the scalar ones (packed_math_kernel): mismatches[0..4] as listed there.
+int p2cu_probe_packed_math(unsigned long long* mismatches) {
+    using namespace p2cu;
+    if (!mismatches) return fail_fmt(-1, "p2cu_probe_packed_math: arguments");
+    unsigned long long* bad = nullptr;
+    cudaError_t e = cudaMalloc(&bad, 5 * sizeof(unsigned long long));
+    if (e != cudaSuccess) return cuda_error(e, "p2cu_probe_packed_math: buffer");
+    int rc = 0;
+    e = cudaMemset(bad, 0, 5 * sizeof(unsigned long long));
+    if (e == cudaSuccess) {
+        packed_math_kernel<<<sms_of_device() * 8, 256>>>(bad);
+        e = cudaGetLastError();
+    }
+    if (e == cudaSuccess) e = cudaMemcpy(mismatches, bad, 5 * sizeof(unsigned long long), cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) rc = cuda_error(e, "p2cu_probe_packed_math");
+    cudaFree(bad);
     return rc;
 }
 

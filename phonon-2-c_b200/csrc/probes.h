@@ -1,6 +1,7 @@
-/* probes.h - measurements of the B200 features the GEMM kernels are built around (libphonon2_probes.so, built beside
- * the product library and loaded only by the bench's probe workload and its large-M fractions). Each returns 0, or a
- * negative code with a message in p2cu_probes_last_error(). */
+/* probes.h - measurements of the B200 features the GEMM kernels are built around, and checks of the packed arithmetic
+ * the encoder's row kernels use (libphonon2_probes.so, built beside the product library and loaded only by the bench's
+ * probe workload, its large-M fractions and the tests). Each returns 0, or a negative code with a message in
+ * p2cu_probes_last_error(). */
 #ifndef P2_PROBES_H
 #define P2_PROBES_H
 
@@ -25,6 +26,10 @@ P2PROBE_API int p2cu_probe_tma_load(int warps, int box_rows, double *bytes_per_s
  * as in the pair GEMM, without copies: mode 0 no hand-back after the first round, mode 1 through a producer arrive and
  * the odd CTA's relay, mode 2 with the odd CTA arriving on the even CTA's barrier. */
 P2PROBE_API int p2cu_probe_int8_ring(int mode, int iters, double *macs_per_s);
+/* The encoder's packed fp32x2 arithmetic (numerics.cuh) against the scalar forms it replaces, bit for bit over every
+ * input: mismatches[0] exp_poly against the rintf form, [1] exp_poly2, [2] swish2, [3] the packed FMA on hashed
+ * operands, [4] rcp2_ge1 against __frcp_rn over [1, 2^126). All five are 0 on a correct build. */
+P2PROBE_API int p2cu_probe_packed_math(unsigned long long *mismatches);
 
 #ifdef __cplusplus
 }
