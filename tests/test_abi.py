@@ -41,3 +41,17 @@ def test_oracle_is_not_linked_by_the_product():
     """The product library must not depend on the test-side checkers."""
     so = (ROOT / "phonon-2-c_b200" / "libphonon2_b200.so").read_bytes()
     assert b"liboracle" not in so and b"orc_" not in so and b"libphonon2_ref" not in so
+
+
+def test_probes_library_exports_its_header_and_stays_out_of_the_product():
+    """The test-only probes library (hardware rates, the packed-arithmetic check) loads without a GPU, exports every
+    function probes.h declares, and none of them is in the product library."""
+    import ctypes
+    header = (ROOT / "phonon-2-c_b200" / "csrc" / "probes.h").read_text()
+    header = re.sub(r"/\*.*?\*/", "", header, flags=re.S)
+    names = set(re.findall(r"^\s*P2PROBE_API\s+[\w\s\*]*?\b(p2cu_\w+)\s*\(", header, re.M))
+    assert "p2cu_probe_packed_math" in names and "p2cu_probe_int8_mma" in names
+    probes = ctypes.CDLL(str(ROOT / "phonon-2-c_b200" / "libphonon2_probes.so"))
+    assert not [n for n in sorted(names) if not hasattr(probes, n)]
+    product = ctypes.CDLL(str(ROOT / "phonon-2-c_b200" / "libphonon2_b200.so"))
+    assert not [n for n in sorted(names) if hasattr(product, n)]
