@@ -411,8 +411,10 @@ def run_ours(args, world, rank, local):
         cpu = world == 1 and not args.no_cpu_baseline
         if cpu:
             line["cpu_baseline"] = cpu_baseline()
-        for name, obj in extras.items():
-            line[name] = compact(obj)
+        if cfg is not None and cpu:
+            for key, n_mel in (("c2", 3000), ("c4", 300)):
+                cfg[key]["cpu_ms_exact"] = round(transcribe_reference(n_mel)["value"], 1)
+        finish_line(line, extras, cfg)
         if cpu:
             if "encoder" in line:
                 line["encoder"]["cpu"] = compact_cpu(encoder_reference())
@@ -420,12 +422,19 @@ def run_ours(args, world, rank, local):
                 line["decoder"]["cpu"] = compact_cpu(decoder_reference())
                 line["mel"]["cpu"] = compact_cpu(mel_reference())
                 line["long_audio"]["cpu"] = compact_cpu(long_audio_reference())
-        if cfg is not None:
-            if cpu:
-                for key, n_mel in (("c2", 3000), ("c4", 300)):
-                    cfg[key]["cpu_ms_exact"] = round(transcribe_reference(n_mel)["value"], 1)
-            line["configs"] = cfg
         print(json.dumps(line))
+
+
+def finish_line(line, extras, cfg):
+    """The sub-objects after the headline keys: the per-config object first, then the decoder, log-mel and long-audio
+    objects, and the encoder (the metric's second half) last, at the end of the line, which is the part a record that
+    keeps only the tail of the output still holds."""
+    if cfg is not None:
+        line["configs"] = cfg
+    for name in ("decoder", "mel", "long_audio", "encoder"):
+        if name in extras:
+            line[name] = compact(extras[name])
+    return line
 
 
 def compact(obj):
