@@ -228,6 +228,14 @@ def run_reference(args, world, rank):
             "cpu_baseline": {"value": value, "unit": "TMAC/s", "cores": cores, "kind": "reference",
                              "sample": f"{args.steps} steps of the full workload"},
             "e2e": {"value": value, "unit": "TMAC/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    # the encoder object last, as on our arm's line: the end of the line is what a record of the output's tail keeps
+    if not args.no_decoder:
+        la = long_audio_reference()
+        if la is not None:
+            line["long_audio"] = {"metric": "long-form transcription audio-sec/sec", "value": la["value"],
+                                  "unit": "audio-s/s", "mode": "exact", "cpu_baseline": la,
+                                  "e2e": {"value": la["value"], "unit": "audio-s/s", "h2d_bytes_per_step": 0,
+                                          "d2h_bytes_per_step": 0}}
     if not args.no_encoder:
         enc = encoder_reference()
         if enc is not None:
@@ -236,13 +244,6 @@ def run_reference(args, world, rank):
                                "cpu_baseline": enc,
                                "e2e": {"value": enc["value"], "unit": "audio-s/s", "h2d_bytes_per_step": 0,
                                        "d2h_bytes_per_step": 0}}
-    if not args.no_decoder:
-        la = long_audio_reference()
-        if la is not None:
-            line["long_audio"] = {"metric": "long-form transcription audio-sec/sec", "value": la["value"],
-                                  "unit": "audio-s/s", "mode": "exact", "cpu_baseline": la,
-                                  "e2e": {"value": la["value"], "unit": "audio-s/s", "h2d_bytes_per_step": 0,
-                                          "d2h_bytes_per_step": 0}}
     print(json.dumps(line))
 
 
